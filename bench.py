@@ -1,0 +1,294 @@
+#!/usr/bin/env python
+"""Benchmark of the Mamba-3 SSD hot path on B200.
+
+Headline workload: KulaMamba layer forward in bf16 with fp32
+accumulation, x (16, 4096, 768) ~ N(0,1) seed 1, weights = the seed-0 default init
+cast to bf16 (d_state 128, headdim 64 -> 24 heads, mimo_rank 2).  One step = one
+layer forward over the batch.  Weak scaling under torchrun: every rank runs the
+full config-1 batch on its own GPU (batch sharding, no collective).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the reference algorithm on the host CPU (the numpy
+restatement in oracle/, all host cores) on a bounded sample of the same workload.
+Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG1 = dict(batch=16, seqlen=4096, d_model=768, d_state=128, headdim=64, mimo_rank=2, chunk_size=64, expand=2)
+METRIC = "KulaMamba layer forward tokens/s (config 1, bf16)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-sample-tokens", type=int, default=512)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (numpy restatement of the reference) on host cores
+# ---------------------------------------------------------------------------
+def cpu_baseline(sample_tokens: int, rows: int | None = None):
+    """Time the reference algorithm (oracle port, fp32) on `rows` rows x `sample_tokens` tokens of
+    config 1, one row per worker thread (numpy releases the GIL in its kernels)."""
+    import concurrent.futures as cf
+
+    import numpy as np
+    import torch
+
+    import oracle
+    from mamba3_b200.mamba3 import KulaMamba
+
+    cores = len(os.sched_getaffinity(0))
+    rows = rows or cores
+    torch.manual_seed(0)
+    m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2, chunk_size=64)
+    sd = {k: v.float().numpy() for k, v in m.state_dict().items()}
+    p = oracle.LayerParams.from_state_dict(sd, d_model=768, d_state=128, headdim=64, mimo_rank=2, chunk_size=64,
+                                           dtype=np.float32)
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(rows, sample_tokens, 768, generator=g).numpy()
+    oracle.layer_forward(p, x[:1, :64])  # warm the allocator / BLAS
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=cores) as ex:
+        list(ex.map(lambda r: oracle.layer_forward(p, x[r:r + 1]), range(rows)))
+    dt = time.perf_counter() - t0
+    return {"value": rows * sample_tokens / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{rows} rows x {sample_tokens} tokens of config 1, fp32 numpy oracle, one row per thread",
+            "seconds": round(dt, 2)}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    cpu_baseline(64, rows=1)  # warm-up: allocator, BLAS threads
+    per_step = max(64, min(512, 2048 // max(1, args.steps)))
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(per_step))
+    v = sum(b["value"] for b in vals) / len(vals)
+    cb = dict(vals[-1])
+    cb["value"] = v
+    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config 1: KulaMamba layer forward, x (16, 4096, 768)", "sampled": cb["sample"]},
+            "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def algorithmic_work(B, T, H=24, P=64, N=128, R=2, d_model=768, d_proj=3696):
+    """Per-launch algorithmic FLOPs / bytes of each kernel of one layer forward (bf16 I/O).
+
+    Tiles per (batch, chunk, head) with the kernels' chunk length L = 128 / R: rows (t,r) = 128,
+    columns (s,q) = 128.  FLOPs count the tensor-core contractions; bytes count compulsory HBM
+    traffic (each input read once, each output written once)."""
+    L = 128 // R
+    K = (T + L - 1) // L
+    chunks = B * K * H
+    tok = B * T
+    f_state = chunks * 2 * N * 128 * P                 # S'^T (N x P) over K = 128
+    f_out = chunks * (2 * 128 * 128 * N + 2 * 128 * P * 128 + 2 * 128 * P * N)  # S, P X, C H'
+    st_bytes = chunks * P * N * 2                      # one bf16 state tensor
+    tok_x = tok * H * P * 2                            # x (or z) columns of proj
+    tok_bc = tok * 2 * N * R * 2                       # B and C columns (shared by the heads)
+    tok_sc = tok * (2 * H + N // 2) * 2                # dt, lam, theta
+    return {
+        "chunk_out": {"flops": f_out, "bytes": 2 * tok_x + tok_bc + tok_sc + st_bytes + tok * H * P * 2},
+        "chunk_state": {"flops": f_state, "bytes": tok_x + tok_bc + tok_sc + st_bytes},
+        "scan": {"flops": 0, "bytes": 2 * st_bytes},
+        "prep": {"flops": 0, "bytes": tok_bc + tok_sc + tok * 8 + B * K * H * (N // 2) * 4},
+        "in_proj": {"flops": 2 * tok * d_model * d_proj, "bytes": tok * (d_model + d_proj) * 2},
+        "out_proj": {"flops": 2 * tok * H * P * d_model, "bytes": tok * (H * P + d_model) * 2},
+    }
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from mamba3_b200 import KulaMamba, _lib
+    from mamba3_b200.profiling import ClockSampler, stage_events
+
+    c = CFG1
+    B, T = c["batch"], c["seqlen"]
+    torch.manual_seed(0)
+    layer = KulaMamba(d_model=c["d_model"], d_state=c["d_state"], headdim=c["headdim"], mimo_rank=c["mimo_rank"],
+                      chunk_size=c["chunk_size"]).to(dev, torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(1 + rank)
+    x_host = torch.randn(B, T, c["d_model"], generator=g).to(torch.bfloat16).pin_memory()
+    x = x_host.to(dev)
+    nst = len(_lib.LAYER_FWD_STAGES) + 1
+
+    def mk():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    ev = [[mk() for _ in range(nst + 2)] for _ in range(args.steps)]
+    torch.cuda.synchronize()
+
+    def step(i=None):
+        if i is None:
+            return layer(x)
+        e = ev[i]
+        e[0].record()
+        proj = layer.in_proj(x)
+        with stage_events(e[1:1 + nst]):
+            y = layer.ssd_from_proj(proj)
+        out = layer.out_proj(y)
+        e[-1].record()
+        return out
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            t0.record()
+            for i in range(args.steps):
+                step(i)
+            t1.record()
+            torch.cuda.synchronize()
+        barrier()
+        ms = t0.elapsed_time(t1) / args.steps
+        if world > 1:
+            tt = torch.tensor([ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        # per-kernel durations (ms), averaged over the timed steps
+        names = ["in_proj", *_lib.LAYER_FWD_STAGES, "out_proj"]
+        per = {n: 0.0 for n in names}
+        for e in ev:
+            marks = [e[0], *e[1:1 + nst], e[-1]]
+            per["in_proj"] += e[0].elapsed_time(e[1])
+            for j, n in enumerate(_lib.LAYER_FWD_STAGES):
+                per[n] += e[1 + j].elapsed_time(e[2 + j])
+            per["out_proj"] += e[nst].elapsed_time(e[-1])
+            del marks
+        per = {k: v / args.steps for k, v in per.items()}
+
+        # end to end through the public API: pinned host x -> device -> layer -> pinned host y
+        y_host = torch.empty(B, T, c["d_model"], dtype=torch.bfloat16).pin_memory()
+        for _ in range(2):
+            y_host.copy_(layer(x_host.to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        ke = max(3, args.steps // 2)
+        e0.record()
+        for _ in range(ke):
+            y_host.copy_(layer(x_host.to(dev, non_blocking=True)), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_e2e = e0.elapsed_time(e1) / ke
+        if world > 1:
+            tt = torch.tensor([ms_e2e], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms_e2e = float(tt.item())
+
+    if rank == 0:
+        import math
+
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() \
+            else {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+        work = algorithmic_work(B, T)
+        ours = {k: per[k] for k in ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out")}
+        dom = max(ours, key=ours.get)
+        w = work.get(dom, {"flops": 0, "bytes": 0})
+        t_s = per[dom] / 1e3
+        t_tc = w["flops"] / (peaks["bf16_tflops"] * 1e12)
+        t_hbm = w["bytes"] / (peaks["hbm_gbs"] * 1e9)
+        if t_tc >= t_hbm:
+            roof = {"bound": "tensor", "achieved": w["flops"] / t_s / 1e12, "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s"}
+        else:
+            roof = {"bound": "hbm", "achieved": w["bytes"] / t_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+        roof["frac"] = roof["achieved"] / roof["peak"]
+        roof["kernel"] = dom
+        roof["traffic"] = None
+        roof["peak_source"] = "measured (MEASURED_PEAKS.json)" if not peaks.get("fallback") else "fallback"
+        kern = {}
+        for k, v in per.items():
+            wk = work.get(k)
+            d = {"ms": round(v, 4)}
+            if wk and v > 0:
+                if wk["flops"]:
+                    d["tflops"] = round(wk["flops"] / (v / 1e3) / 1e12, 1)
+                d["gbs"] = round(wk["bytes"] / (v / 1e3) / 1e9, 1)
+            kern[k] = d
+        tokens = world * B * T
+        line = {
+            "metric": METRIC, "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 1: KulaMamba layer forward (d_model 768, d_state 128, headdim 64, "
+                                   "mimo_rank 2), x (16, 4096, 768) per GPU", "global_batch": world * B,
+                       "seq_len": T, "parallelism": f"batch-sharded x{world}, no collective",
+                       "l2": "inputs larger than L2 (>1.5 GB touched per step)"},
+            "roofline": roof,
+            "kernels_ms": kern,
+            "gpu_launches": 5 * args.steps,
+            "e2e": {"value": tokens / (ms_e2e / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2,
+                    "ms_per_step": ms_e2e},
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_sample_tokens)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * mamba3_b200 -- C ABI of the B200 (sm_100a) Mamba-3 SSD kernels.
+ *
+ * Conventions (every entry point):
+ *  - Arguments are plain device pointers, element counts and dtype codes; no
+ *    framework types cross this boundary.  `stream` is a cudaStream_t.
+ *  - The caller owns every buffer, outputs and workspace included; the library
+ *    never allocates or frees device memory.
+ *  - Calls are asynchronous on `stream` and return M3B_OK or an m3b_status code;
+ *    they never abort the process.  m3b_last_error() gives a detail message for
+ *    the calling thread's last failure.
+ *  - Launches are reentrant and thread-safe for distinct streams; the only
+ *    process-wide state is a one-time kernel attribute setup per device.
+ *  - Optional `err` pointers name a device int that kernels set (first error
+ *    wins) when a bounded on-device wait expires; read it after synchronising.
+ *
+ * Shapes use the reference's layouts: activations (batch, seqlen, ...),
+ * states (batch, H, P, N), angles (batch, H, N/2).  H = heads, P = headdim,
+ * N = d_state, R = mimo_rank, G = ngroups.
+ */
+#ifndef MAMBA3_B200_H
+#define MAMBA3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define M3B_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define M3B_API __attribute__((visibility("default")))
+#else
+#define M3B_API
+#endif
+
+typedef enum m3b_dtype { M3B_F32 = 0, M3B_BF16 = 1, M3B_F16 = 2 } m3b_dtype;
+
+typedef enum m3b_status {
+  M3B_OK = 0,
+  M3B_ERR_INVALID_ARG = 1,  /* null pointer, bad shape or dtype */
+  M3B_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement */
+  M3B_ERR_CUDA = 3,         /* CUDA runtime / launch error */
+  M3B_ERR_ALIGNMENT = 4,    /* a pointer lacks the required 16-byte alignment */
+  M3B_ERR_TIMEOUT = 5,      /* a bounded device wait expired (reported via `err`) */
+  M3B_ERR_WORKSPACE = 6     /* workspace missing or too small */
+} m3b_status;
+
+/* Status code -> static string. */
+M3B_API const char* m3b_strerror(int status);
+/* Detail message of the calling thread's last failed call ("" if none). */
+M3B_API const char* m3b_last_error(void);
+/* M3B_ABI_VERSION of the loaded library. */
+M3B_API int m3b_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Inter-chunk scan.
+ * Replaces the reference's pybind entry `scan_forward(decay, h_chunk, h_init)`
+ * (mamba3/csrc/scan.cu:128-166; called from mamba3/scan.py:80 in SSDScanFn.forward,
+ * mamba3/scan.py:65-100).  h_states[:,0] = h_init (or 0);
+ * h_states[:,k+1] = decay[:,k] * h_states[:,k] + h_chunk[:,k], carried in fp32.
+ * Optionally also h_final = decay[:,K-1]*h_states[:,K-1] + h_chunk[:,K-1] (fp32),
+ * the value mamba3/ssd.py:235-242 derives from the scan.
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_scan_args {
+  const float* decay;     /* (B,K,H) */
+  const void* h_chunk;    /* (B,K,H,PN), `dtype` */
+  const float* h_init;    /* (B,H,PN) or NULL */
+  void* h_states;         /* (B,K,H,PN), `dtype` (may not alias h_chunk) */
+  float* h_final;         /* (B,H,PN) or NULL */
+  int64_t B, K, H, PN;
+  int32_t dtype;          /* M3B_F32 or M3B_BF16 */
+} m3b_scan_args;
+M3B_API int m3b_scan_fwd(const m3b_scan_args* a, void* stream);
+
+/* Parameters of one KulaMamba layer (names and shapes of mamba3/mamba3.py:95-111). */
+typedef struct m3b_layer_params {
+  int32_t H, P, N, R, G;
+  int32_t trapezoidal;    /* use_trapezoidal */
+  int32_t complex_ssm;    /* use_complex_ssm (data-dependent RoPE on B/C) */
+  int32_t param_dtype;    /* dtype of every pointer below */
+  float norm_eps;         /* B_norm / C_norm eps (1e-5 in the reference) */
+  const void* A_log;      /* (H) */
+  const void* D;          /* (H) */
+  const void* dt_bias;    /* (H) */
+  const void* B_norm_w;   /* (N*R) */
+  const void* C_norm_w;   /* (N*R) */
+  const void* B_bias;     /* (G,N,R) */
+  const void* C_bias;     /* (G,N,R) */
+  const void* mimo_x;     /* (H,P,R) */
+  const void* mimo_z;     /* (H,P,R) */
+  const void* mimo_down;  /* (H,P,R) */
+} m3b_layer_params;
+
+/* The input projection row of one token, as split by mamba3/mamba3.py:125-140:
+ * [ z (H*P) | x (H*P) | B (G*N*R) | C (G*N*R) | dt (H) | lam (H, if trapezoidal) |
+ *   theta (N/2, if complex_ssm) ], `proj_stride` elements between tokens. */
+
+/* ------------------------------------------------------------------------
+ * O(1) decode step.
+ * Replaces the SSM core of KulaMamba.step (mamba3/mamba3.py:278-316): everything
+ * between in_proj and out_proj -- softplus dt, decay, B/C RMSNorm + bias, RoPE
+ * advance of the angle state, MIMO x, the fp32 trapezoidal state update
+ * h = dA*h + gamma*B^x + beta*prev_BX, readout C^.h + D*x, gate and MIMO-down.
+ * State buffers may be updated in place (h_out == h, bx_out == prev_bx,
+ * angle_out == angle when angle is fp32).
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_step_args {
+  m3b_layer_params prm;
+  int64_t batch;
+  const void* proj;       /* (batch, proj_stride), act_dtype */
+  int64_t proj_stride;
+  int32_t act_dtype;
+  const void* dt_scale;   /* (batch, H) act_dtype, or NULL */
+  const float* h;         /* (batch,H,P,N) */
+  const float* prev_bx;   /* (batch,H,P,N) */
+  const void* angle;      /* (batch,H,N/2), angle_dtype */
+  int32_t angle_dtype;
+  float* h_out;           /* (batch,H,P,N) */
+  float* bx_out;          /* (batch,H,P,N): this token's B^x (next step's prev_BX) */
+  float* angle_out;       /* (batch,H,N/2) fp32 */
+  void* y;                /* (batch, H*P) act_dtype: gated MIMO-down output, input of out_proj */
+} m3b_step_args;
+M3B_API int m3b_step(const m3b_step_args* a, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Layer forward / prefill (parallel, chunked).
+ * Replaces KulaMamba._forward_impl between in_proj and out_proj
+ * (mamba3/mamba3.py:198-238) including chunked_ssd (mamba3/ssd.py:118-244) and,
+ * when requested, the prefill state of mamba3/mamba3.py:241-256.
+ * It may also continue from an inference state (h_init, angle_init, prev_bx_init),
+ * which the reference does not offer; with all three NULL it is the reference's
+ * computation from a zero state.
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_layer_fwd_args {
+  m3b_layer_params prm;
+  int64_t batch, seqlen;
+  const void* proj;          /* (batch, seqlen, proj_stride), act_dtype */
+  int64_t proj_stride;
+  int32_t act_dtype;         /* M3B_BF16 or M3B_F32 */
+  const void* dt_scale;      /* (batch, seqlen, H) act_dtype, or NULL */
+  const float* h_init;       /* (batch,H,P,N) or NULL */
+  const float* angle_init;   /* (batch,H,N/2) or NULL */
+  const float* prev_bx_init; /* (batch,H,P,N) or NULL */
+  void* y;                   /* (batch, seqlen, H*P) act_dtype */
+  float* h_final;            /* (batch,H,P,N) or NULL */
+  float* angle_final;        /* (batch,H,N/2) or NULL */
+  float* prev_bx_final;      /* (batch,H,P,N) or NULL */
+  int* err;                  /* device int or NULL */
+  /* NULL, or M3B_LAYER_FWD_STAGES + 1 cudaEvent_t: event i is recorded on `stream` before
+   * stage i (prep, angle prefix, chunk state, scan, chunk output, prefill prev_BX) and the
+   * last one after the final stage, so callers can time each kernel. */
+  void* const* stage_events;
+} m3b_layer_fwd_args;
+#define M3B_LAYER_FWD_STAGES 6
+/* Bytes of device workspace m3b_layer_fwd needs for these arguments. */
+M3B_API size_t m3b_layer_fwd_workspace(const m3b_layer_fwd_args* a);
+M3B_API int m3b_layer_fwd(const m3b_layer_fwd_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Tensor-core self-test (diagnostic; no counterpart in the reference).
+ * D (128 x 64, fp32) = A (128 x 128 bf16, row-major) x B (64 x 128 bf16, row-major)^T,
+ * staged through the same shared-memory layouts and UMMA descriptors as the chunk
+ * kernels: mode 0 reads A K-major, mode 1 stages A transposed and reads it MN-major.
+ * ------------------------------------------------------------------------ */
+M3B_API int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA3_B200_H */

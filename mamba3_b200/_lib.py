@@ -1,0 +1,193 @@
+"""ctypes binding of ``libmamba3_b200.so`` (the C ABI in ``include/mamba3_b200.h``).
+
+This module only marshals torch tensors into the C structs and calls the
+library on the tensors' device and current stream.  There is no fallback: if
+the library is missing or a tensor is not on a CUDA device the call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+import torch
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libmamba3_b200.so"
+
+F32, BF16, F16 = 0, 1, 2
+_DT = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class M3bError(RuntimeError):
+    """A failed call into libmamba3_b200 (status code + detail message)."""
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise M3bError(f"unsupported dtype {dt}") from None
+
+
+class ScanArgs(C.Structure):
+    _fields_ = [("decay", C.c_void_p), ("h_chunk", C.c_void_p), ("h_init", C.c_void_p), ("h_states", C.c_void_p),
+                ("h_final", C.c_void_p), ("B", C.c_int64), ("K", C.c_int64), ("H", C.c_int64), ("PN", C.c_int64),
+                ("dtype", C.c_int32)]
+
+
+class LayerParams(C.Structure):
+    _fields_ = [("H", C.c_int32), ("P", C.c_int32), ("N", C.c_int32), ("R", C.c_int32), ("G", C.c_int32),
+                ("trapezoidal", C.c_int32), ("complex_ssm", C.c_int32), ("param_dtype", C.c_int32),
+                ("norm_eps", C.c_float),
+                ("A_log", C.c_void_p), ("D", C.c_void_p), ("dt_bias", C.c_void_p), ("B_norm_w", C.c_void_p),
+                ("C_norm_w", C.c_void_p), ("B_bias", C.c_void_p), ("C_bias", C.c_void_p), ("mimo_x", C.c_void_p),
+                ("mimo_z", C.c_void_p), ("mimo_down", C.c_void_p)]
+
+
+class StepArgs(C.Structure):
+    _fields_ = [("prm", LayerParams), ("batch", C.c_int64), ("proj", C.c_void_p), ("proj_stride", C.c_int64),
+                ("act_dtype", C.c_int32), ("dt_scale", C.c_void_p), ("h", C.c_void_p), ("prev_bx", C.c_void_p),
+                ("angle", C.c_void_p), ("angle_dtype", C.c_int32), ("h_out", C.c_void_p), ("bx_out", C.c_void_p),
+                ("angle_out", C.c_void_p), ("y", C.c_void_p)]
+
+
+class LayerFwdArgs(C.Structure):
+    _fields_ = [("prm", LayerParams), ("batch", C.c_int64), ("seqlen", C.c_int64), ("proj", C.c_void_p),
+                ("proj_stride", C.c_int64), ("act_dtype", C.c_int32), ("dt_scale", C.c_void_p),
+                ("h_init", C.c_void_p), ("angle_init", C.c_void_p), ("prev_bx_init", C.c_void_p), ("y", C.c_void_p),
+                ("h_final", C.c_void_p), ("angle_final", C.c_void_p), ("prev_bx_final", C.c_void_p),
+                ("err", C.c_void_p), ("stage_events", C.POINTER(C.c_void_p))]
+
+
+LAYER_FWD_STAGES = ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out", "last_bx")
+
+
+# every symbol include/mamba3_b200.h declares, with its ctypes signature
+SIGNATURES = {
+    "m3b_strerror": (C.c_char_p, [C.c_int]),
+    "m3b_last_error": (C.c_char_p, []),
+    "m3b_abi_version": (C.c_int, []),
+    "m3b_scan_fwd": (C.c_int, [C.POINTER(ScanArgs), C.c_void_p]),
+    "m3b_step": (C.c_int, [C.POINTER(StepArgs), C.c_void_p]),
+    "m3b_layer_fwd_workspace": (C.c_size_t, [C.POINTER(LayerFwdArgs)]),
+    "m3b_layer_fwd": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_selftest_umma": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+}
+
+
+def lib():
+    """The loaded library (loaded once; raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise M3bError(f"{LIB_PATH.name} is not built; run `python -m mamba3_b200.build`")
+                h = C.CDLL(str(LIB_PATH))
+                for name, (res, args) in SIGNATURES.items():
+                    f = getattr(h, name)
+                    f.restype = res
+                    f.argtypes = args
+                _lib = h
+    return _lib
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        L = lib()
+        raise M3bError(f"{what}: {L.m3b_strerror(rc).decode()} ({L.m3b_last_error().decode()})")
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _cuda(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise M3bError("mamba3_b200 kernels need CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise M3bError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+def _stream(dev):
+    return C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def layer_params(H, P, N, R, G, trapezoidal, complex_ssm, norm_eps, A_log, D, dt_bias, B_norm_w, C_norm_w,
+                 B_bias, C_bias, mimo_x, mimo_z, mimo_down):
+    ps = [A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_z, mimo_down]
+    pdt = ps[0].dtype
+    for t in ps:
+        if t.dtype != pdt or not t.is_contiguous():
+            raise M3bError("layer parameters must be contiguous and share one dtype")
+    return LayerParams(H, P, N, R, G, int(bool(trapezoidal)), int(bool(complex_ssm)), dtype_code(pdt),
+                       float(norm_eps), *[_ptr(t) for t in ps])
+
+
+def scan_fwd(decay, h_chunk, h_init=None, h_states=None, h_final=None):
+    """Launch the inter-chunk scan; decay (B,K,H) fp32, h_chunk (B,K,H,PN) fp32/bf16."""
+    dev = _cuda(decay, h_chunk, h_init, h_states, h_final)
+    B, K, H, PN = h_chunk.shape
+    if h_states is None:
+        h_states = torch.empty_like(h_chunk)
+    a = ScanArgs(_ptr(decay), _ptr(h_chunk), _ptr(h_init), _ptr(h_states), _ptr(h_final), B, K, H, PN,
+                 dtype_code(h_chunk.dtype))
+    with torch.cuda.device(dev):
+        _check(lib().m3b_scan_fwd(C.byref(a), _stream(dev)), "m3b_scan_fwd")
+    return h_states
+
+
+def step(prm: LayerParams, proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y):
+    dev = _cuda(proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y)
+    a = StepArgs(prm, proj.shape[0], _ptr(proj), proj.stride(0), dtype_code(proj.dtype), _ptr(dt_scale), _ptr(h),
+                 _ptr(prev_bx), _ptr(angle), dtype_code(angle.dtype), _ptr(h_out), _ptr(bx_out), _ptr(angle_out),
+                 _ptr(y))
+    with torch.cuda.device(dev):
+        _check(lib().m3b_step(C.byref(a), _stream(dev)), "m3b_step")
+
+
+def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=None, prev_bx_init=None,
+              h_final=None, angle_final=None, prev_bx_final=None, err=None, workspace=None, stage_events=None):
+    """Launch the chunked layer forward; proj (B,T,d_proj) with unit stride in the last dim."""
+    dev = _cuda(proj, y, dt_scale, h_init, angle_init, prev_bx_init, h_final, angle_final, prev_bx_final, err)
+    Bt, T, _ = proj.shape
+    if proj.stride(2) != 1 or proj.stride(0) != T * proj.stride(1):
+        raise M3bError("proj must be row-contiguous (B,T,d_proj)")
+    a = LayerFwdArgs(prm, Bt, T, _ptr(proj), proj.stride(1), dtype_code(proj.dtype), _ptr(dt_scale), _ptr(h_init),
+                     _ptr(angle_init), _ptr(prev_bx_init), _ptr(y), _ptr(h_final), _ptr(angle_final),
+                     _ptr(prev_bx_final), _ptr(err))
+    if stage_events is not None:
+        if len(stage_events) != len(LAYER_FWD_STAGES) + 1:
+            raise M3bError("stage_events needs one event per stage plus one")
+        arr = (C.c_void_p * len(stage_events))(*[e.cuda_event for e in stage_events])
+        a.stage_events = C.cast(arr, C.POINTER(C.c_void_p))
+    L = lib()
+    need = L.m3b_layer_fwd_workspace(C.byref(a))
+    if need == 0:
+        _check(L.m3b_layer_fwd(C.byref(a), None, 0, None), "m3b_layer_fwd")  # reports the validation error
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(L.m3b_layer_fwd(C.byref(a), _ptr(workspace), need, _stream(dev)), "m3b_layer_fwd")
+    return workspace
+
+
+def selftest_umma(A, B, mode):
+    dev = _cuda(A, B)
+    D = torch.empty(128, 64, dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _check(lib().m3b_selftest_umma(_ptr(A), _ptr(B), _ptr(D), mode, _ptr(err), _stream(dev)), "selftest_umma")
+    return D, err

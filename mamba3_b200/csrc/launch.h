@@ -1,0 +1,37 @@
+// Host-side internals shared by the launchers (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mamba3_b200.h"
+
+namespace m3b {
+
+// Record a failure detail for m3b_last_error() and return `code`.
+int fail(int code, const char* fmt, ...);
+// cudaGetLastError() after a launch -> M3B_OK or M3B_ERR_CUDA (with detail).
+int check_launch(const char* what);
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct ScanLaunch {
+  const float* decay;
+  const void* h_chunk;
+  const float* h_init;
+  const float* init_bx;    // optional: h_states[0] += init_coef[b,h] * init_bx
+  const float* init_coef;  // (B,H)
+  void* h_states;
+  float* h_final;
+  int64_t B, K, H, PN;
+  int dtype;
+};
+int launch_scan(const ScanLaunch& s, cudaStream_t st);
+
+int launch_step(const m3b_step_args* a, cudaStream_t st);
+int layer_fwd(const m3b_layer_fwd_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t layer_fwd_workspace(const m3b_layer_fwd_args* a);
+
+}  // namespace m3b

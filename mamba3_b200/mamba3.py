@@ -1,0 +1,177 @@
+"""KulaMamba: the Mamba-3 SSD layer, drop-in for ``mamba3.mamba3`` of the reference.
+
+Same constructor, parameter names, shapes and default init as the reference
+(mamba3/mamba3.py:48-123), so a ``state_dict`` moves between the two in either
+direction and a seeded construction yields identical weights.  ``in_proj`` and
+``out_proj`` stay cuBLAS GEMMs; everything between them runs in the sm_100a
+kernels of ``libmamba3_b200`` (see ``ops.py``):
+
+* ``forward`` / ``prefill`` -> ``mamba3_b200::layer_ssd`` (chunked parallel form)
+* ``step``                  -> ``mamba3_b200::step_ssm`` (O(1) recurrent form)
+
+Deviation from the reference (documented): the ``angle`` entry of the inference
+state is kept in fp32 whatever the model dtype (the reference accumulates it in
+the model dtype, mamba3/mamba3.py:330, which drifts in bf16).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from . import ops
+
+
+class RMSNorm(nn.Module):
+    """RMSNorm with the reference's semantics (mamba3/mamba3.py:19-35)."""
+
+    def __init__(self, d: int, eps: float = 1e-5, dim: int = -1):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+        self.eps = eps
+        self.dim = dim
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        inv = torch.rsqrt(x.float().pow(2).mean(self.dim, keepdim=True) + self.eps).to(x.dtype)
+        shape = [1] * x.ndim
+        shape[self.dim] = -1
+        return x * inv * self.weight.view(*shape)
+
+
+class KulaMamba(nn.Module):
+    """Mamba-3 layer: trapezoidal discretisation, data-dependent RoPE on B/C, MIMO rank R."""
+
+    def __init__(
+        self,
+        d_model: int,
+        d_state: int = 128,
+        expand: int = 2,
+        headdim: int = 64,
+        ngroups: int | None = None,
+        mimo_rank: int = 2,
+        chunk_size: int = 64,
+        bias: bool = False,
+        dt_min: float = 0.001,
+        dt_max: float = 0.1,
+        use_trapezoidal: bool = True,
+        use_complex_ssm: bool = True,
+    ):
+        super().__init__()
+        self.d_model = d_model
+        self.d_state = d_state
+        self.expand = expand
+        self.headdim = headdim
+        self.mimo_rank = max(mimo_rank, 1)
+        # chunk_size is accepted for API compatibility; the kernels pick their own
+        # chunk length (128 / mimo_rank rounded up to a power of two), which changes
+        # no result beyond fp32 rounding.
+        self.chunk_size = chunk_size
+        self.use_trapezoidal = use_trapezoidal
+        self.use_complex_ssm = use_complex_ssm
+        self.d_inner = expand * d_model
+        if self.d_inner % headdim != 0:
+            raise ValueError("expand * d_model must be a multiple of headdim")
+        if d_state % 2 != 0:
+            raise ValueError("d_state must be even (RoPE pairing)")
+        self.nheads = self.d_inner // headdim
+        self.ngroups = ngroups if ngroups is not None else 1
+        if self.nheads % self.ngroups != 0:
+            raise ValueError("nheads must be a multiple of ngroups")
+        self.heads_per_group = self.nheads // self.ngroups
+        H, P, N, R, G = self.nheads, headdim, d_state, self.mimo_rank, self.ngroups
+
+        self._d_bc = G * N * R
+        self._d_x = self.d_inner
+        width = self.d_inner + self._d_x + 2 * self._d_bc + H
+        width += H if use_trapezoidal else 0
+        width += N // 2 if use_complex_ssm else 0
+        self.in_proj = nn.Linear(d_model, width, bias=bias)
+
+        self.A_log = nn.Parameter(torch.zeros(H))
+        self.D = nn.Parameter(torch.ones(H))
+        self.dt_bias = nn.Parameter(torch.zeros(H))
+        self.B_norm = RMSNorm(N * R)
+        self.C_norm = RMSNorm(N * R)
+        self.B_bias = nn.Parameter(torch.ones(G, N, R))
+        self.C_bias = nn.Parameter(torch.ones(G, N, R))
+        self.mimo_x = nn.Parameter(torch.ones(H, P, R))
+        self.mimo_z = nn.Parameter(torch.ones(H, P, R))
+        self.mimo_down = nn.Parameter(torch.full((H, P, R), 1.0 / R))
+        self.out_proj = nn.Linear(self.d_inner, d_model, bias=bias)
+        self._init_weights(dt_min, dt_max)
+
+    def _init_weights(self, dt_min: float, dt_max: float):
+        """Default init of the reference (mamba3/mamba3.py:114-123), same RNG draws in the same order."""
+        nn.init.kaiming_uniform_(self.in_proj.weight, a=math.sqrt(5))
+        with torch.no_grad():
+            u = torch.rand(self.nheads)
+            dt = torch.exp(u * (math.log(dt_max) - math.log(dt_min)) + math.log(dt_min))
+            # inverse softplus of dt
+            self.dt_bias.copy_(dt + torch.log(-torch.expm1(-dt)))
+            nn.init.uniform_(self.A_log, -4.0, -1.0)
+
+    # -- plumbing ------------------------------------------------------------
+    def _param_tensors(self):
+        return (self.A_log, self.D, self.dt_bias, self.B_norm.weight, self.C_norm.weight, self.B_bias,
+                self.C_bias, self.mimo_x, self.mimo_z, self.mimo_down)
+
+    def _dims(self):
+        return dict(H=self.nheads, P=self.headdim, N=self.d_state, R=self.mimo_rank, G=self.ngroups,
+                    trapezoidal=self.use_trapezoidal, complex_ssm=self.use_complex_ssm,
+                    norm_eps=float(self.B_norm.eps))
+
+    def ssd_from_proj(self, proj, dt_scale=None, return_state=False, state=None):
+        """Everything between in_proj and out_proj: proj (B,T,d_in_proj) -> y (B,T,d_inner) [+ state]."""
+        st = state or {}
+        y, h, angle, prev_bx = ops.layer_ssd(proj, *self._param_tensors(), dt_scale, st.get("h"), st.get("angle"),
+                                             st.get("prev_BX"), **self._dims(), return_state=return_state)
+        if not return_state:
+            return y
+        return y, {"h": h, "angle": angle, "prev_BX": prev_bx}
+
+    def _ssd(self, x, dt_scale, return_state, state=None):
+        if x.dim() != 3 or x.shape[1] <= 0:
+            raise ValueError(f"expected (batch, seqlen>0, d_model), got {tuple(x.shape)}")
+        proj = self.in_proj(x)
+        st = state or {}
+        y, h, angle, prev_bx = ops.layer_ssd(proj, *self._param_tensors(), dt_scale, st.get("h"), st.get("angle"),
+                                             st.get("prev_BX"), **self._dims(), return_state=return_state)
+        out = self.out_proj(y)
+        if not return_state:
+            return out, None
+        return out, {"h": h, "angle": angle, "prev_BX": prev_bx}
+
+    # -- reference API -------------------------------------------------------
+    def forward(self, x, dt_scale=None):
+        """(B, T, d_model) -> (B, T, d_model)   (mamba3/mamba3.py:260-262)."""
+        return self._ssd(x, dt_scale, False)[0]
+
+    def prefill(self, x, dt_scale=None):
+        """Forward plus the inference state after the last token (mamba3/mamba3.py:264-265)."""
+        return self._ssd(x, dt_scale, True)
+
+    def prefill_from(self, x, ssm_state, dt_scale=None):
+        """Continue a prefill from an inference state (chunked prefill; no reference counterpart)."""
+        return self._ssd(x, dt_scale, True, ssm_state)
+
+    def step(self, hidden_states, ssm_state, dt_scale=None):
+        """One token: (B, d_model) or (B, 1, d_model) -> same shape, new state (mamba3/mamba3.py:267-322)."""
+        squeeze = hidden_states.dim() == 2
+        x_in = hidden_states if squeeze else hidden_states.squeeze(1)
+        proj = self.in_proj(x_in)
+        y, h, bx, angle = ops.step_ssm(proj, *self._param_tensors(), ssm_state["h"], ssm_state["prev_BX"],
+                                       ssm_state["angle"], dt_scale, **self._dims())
+        out = self.out_proj(y)
+        if not squeeze:
+            out = out.unsqueeze(1)
+        return out, {"h": h, "angle": angle, "prev_BX": bx}
+
+    def allocate_inference_state(self, batch_size, dtype=None, device=None):
+        """Zero state {'h', 'angle', 'prev_BX'} (mamba3/mamba3.py:324-332); all fp32 (see module doc)."""
+        device = device or self.in_proj.weight.device
+        H, P, N = self.nheads, self.headdim, self.d_state
+        f32 = dict(dtype=torch.float32, device=device)
+        return {"h": torch.zeros(batch_size, H, P, N, **f32), "angle": torch.zeros(batch_size, H, N // 2, **f32),
+                "prev_BX": torch.zeros(batch_size, H, P, N, **f32)}

@@ -1,0 +1,127 @@
+"""torch.library custom ops over the C ABI.
+
+Each op allocates its outputs with torch (the library itself never allocates)
+and has a fake implementation so the modules trace under
+``torch.compile(fullgraph=True)`` as single opaque nodes.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .profiling import current_stage_events
+
+
+def _prm(H, P, N, R, G, trap, cplx, eps, A_log, D, dt_bias, Bw, Cw, Bb, Cb, mx, mz, md):
+    return _lib.layer_params(H, P, N, R, G, trap, cplx, eps, A_log, D, dt_bias, Bw, Cw, Bb, Cb, mx, mz, md)
+
+
+# ---------------------------------------------------------------------------
+# inter-chunk scan
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("mamba3_b200::scan_fwd", mutates_args=())
+def scan_fwd(decay: torch.Tensor, h_chunk: torch.Tensor, h_init: Optional[torch.Tensor]) -> torch.Tensor:
+    hc = h_chunk if h_chunk.dtype in (torch.float32, torch.bfloat16) else h_chunk.float()
+    hc = hc.contiguous()
+    d = decay.float().contiguous()
+    hi = None if h_init is None else h_init.float().contiguous()
+    out = _lib.scan_fwd(d, hc, hi)
+    return out if out.dtype == h_chunk.dtype else out.to(h_chunk.dtype)
+
+
+@scan_fwd.register_fake
+def _(decay, h_chunk, h_init):
+    return torch.empty_like(h_chunk)
+
+
+# ---------------------------------------------------------------------------
+# layer forward / prefill (everything between in_proj and out_proj)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("mamba3_b200::layer_ssd", mutates_args=())
+def layer_ssd(proj: torch.Tensor, A_log: torch.Tensor, D: torch.Tensor, dt_bias: torch.Tensor,
+              B_norm_w: torch.Tensor, C_norm_w: torch.Tensor, B_bias: torch.Tensor, C_bias: torch.Tensor,
+              mimo_x: torch.Tensor, mimo_z: torch.Tensor, mimo_down: torch.Tensor,
+              dt_scale: Optional[torch.Tensor], h_init: Optional[torch.Tensor], angle_init: Optional[torch.Tensor],
+              prev_bx_init: Optional[torch.Tensor],
+              H: int, P: int, N: int, R: int, G: int, trapezoidal: bool, complex_ssm: bool, norm_eps: float,
+              return_state: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    Bt, T, _ = proj.shape
+    proj = proj.contiguous()
+    dev = proj.device
+    prm = _prm(H, P, N, R, G, trapezoidal, complex_ssm, norm_eps, A_log, D, dt_bias, B_norm_w, C_norm_w,
+               B_bias, C_bias, mimo_x, mimo_z, mimo_down)
+    y = torch.empty(Bt, T, H * P, dtype=proj.dtype, device=dev)
+    f32 = dict(dtype=torch.float32, device=dev)
+    if return_state:
+        h_final = torch.empty(Bt, H, P, N, **f32)
+        angle = torch.empty(Bt, H, N // 2, **f32)
+        prev_bx = torch.empty(Bt, H, P, N, **f32)
+    else:
+        h_final = angle = prev_bx = None
+    ds = None if dt_scale is None else dt_scale.to(proj.dtype).expand(Bt, T, H).contiguous()
+    f = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
+    _lib.layer_fwd(prm, proj, y, dt_scale=ds, h_init=f(h_init), angle_init=f(angle_init),
+                   prev_bx_init=f(prev_bx_init), h_final=h_final, angle_final=angle, prev_bx_final=prev_bx,
+                   stage_events=current_stage_events())
+    if not return_state:
+        e = torch.empty(0, **f32)
+        return y, e, e.clone(), e.clone()
+    return y, h_final, angle, prev_bx
+
+
+@layer_ssd.register_fake
+def _(proj, A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_z, mimo_down, dt_scale, h_init,
+      angle_init, prev_bx_init, H, P, N, R, G, trapezoidal, complex_ssm, norm_eps, return_state):
+    Bt, T, _ = proj.shape
+    y = proj.new_empty(Bt, T, H * P)
+    f32 = dict(dtype=torch.float32, device=proj.device)
+    if return_state:
+        return (y, torch.empty(Bt, H, P, N, **f32), torch.empty(Bt, H, N // 2, **f32),
+                torch.empty(Bt, H, P, N, **f32))
+    e = torch.empty(0, **f32)
+    return y, e, e.clone(), e.clone()
+
+
+# ---------------------------------------------------------------------------
+# decode step (everything between in_proj and out_proj of KulaMamba.step)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("mamba3_b200::step_ssm", mutates_args=())
+def step_ssm(proj: torch.Tensor, A_log: torch.Tensor, D: torch.Tensor, dt_bias: torch.Tensor,
+             B_norm_w: torch.Tensor, C_norm_w: torch.Tensor, B_bias: torch.Tensor, C_bias: torch.Tensor,
+             mimo_x: torch.Tensor, mimo_z: torch.Tensor, mimo_down: torch.Tensor,
+             h: torch.Tensor, prev_bx: torch.Tensor, angle: torch.Tensor, dt_scale: Optional[torch.Tensor],
+             H: int, P: int, N: int, R: int, G: int, trapezoidal: bool, complex_ssm: bool,
+             norm_eps: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    Bt = proj.shape[0]
+    proj = proj.contiguous()
+    prm = _prm(H, P, N, R, G, trapezoidal, complex_ssm, norm_eps, A_log, D, dt_bias, B_norm_w, C_norm_w,
+               B_bias, C_bias, mimo_x, mimo_z, mimo_down)
+    h = h.float().contiguous()
+    prev_bx = prev_bx.float().contiguous()
+    angle = angle.contiguous()
+    h_out = torch.empty_like(h)
+    bx_out = torch.empty_like(prev_bx)
+    angle_out = torch.empty(angle.shape, dtype=torch.float32, device=proj.device)
+    y = torch.empty(Bt, H * P, dtype=proj.dtype, device=proj.device)
+    ds = None if dt_scale is None else dt_scale.to(proj.dtype).reshape(Bt, -1).expand(Bt, H).contiguous()
+    _lib.step(prm, proj, ds, h, prev_bx, angle, h_out, bx_out, angle_out, y)
+    return y, h_out, bx_out, angle_out
+
+
+@step_ssm.register_fake
+def _(proj, A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_z, mimo_down, h, prev_bx, angle,
+      dt_scale, H, P, N, R, G, trapezoidal, complex_ssm, norm_eps):
+    Bt = proj.shape[0]
+    return (proj.new_empty(Bt, H * P), torch.empty_like(h, dtype=torch.float32),
+            torch.empty_like(prev_bx, dtype=torch.float32), torch.empty(angle.shape, dtype=torch.float32,
+                                                                        device=proj.device))
+
+
+def step_ssm_(prm_tensors, dims, proj, h, prev_bx, angle, y, dt_scale=None):
+    """In-place decode step for CUDA-graph loops: updates h, prev_bx, angle (fp32) and writes y."""
+    H, P, N, R, G, trap, cplx, eps = dims
+    prm = _prm(H, P, N, R, G, trap, cplx, eps, *prm_tensors)
+    _lib.step(prm, proj, dt_scale, h, prev_bx, angle, h, prev_bx, angle, y)

@@ -1,0 +1,90 @@
+"""Instrumentation hooks: per-stage CUDA events inside the layer forward, clock sampling."""
+
+from __future__ import annotations
+
+import contextlib
+import statistics
+import threading
+import time
+
+_tls = threading.local()
+
+
+def current_stage_events():
+    return getattr(_tls, "events", None)
+
+
+@contextlib.contextmanager
+def stage_events(events):
+    """Record ``events`` (len = stages + 1) around the stages of the next layer forward on this thread."""
+    prev = getattr(_tls, "events", None)
+    _tls.events = events
+    try:
+        yield
+    finally:
+        _tls.events = prev
+
+
+# NVML clock-event reason bits
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+            0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x100: "display_clocks"}
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons of one GPU every `period` seconds (NVML)."""
+
+    def __init__(self, torch_device_index: int, period: float = 0.2):
+        import torch
+
+        self.period = period
+        self.samples = []
+        self._stop = threading.Event()
+        self._thr = None
+        self.handle = None
+        self.err = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(torch_device_index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            self.nv = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 -- reported in the JSON, not fatal
+            self.err = f"{type(e).__name__}: {e}"
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                pw = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((time.time(), sm, rs, pw))
+            except Exception as e:  # noqa: BLE001
+                self.err = f"{type(e).__name__}: {e}"
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self.handle is not None:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thr is not None:
+            self._thr.join()
+
+    def summary(self):
+        if self.handle is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": self.err}
+        sms = [s[1] for s in self.samples]
+        bits = 0
+        for s in self.samples:
+            bits |= int(s[2])
+        reasons = sorted(n for b, n in _REASONS.items() if bits & b and n != "gpu_idle")
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": self.max_sm, "reasons": reasons,
+                "samples": len(sms), "power_w_max": round(max(s[3] for s in self.samples), 1)}

@@ -262,14 +262,15 @@ def chunked_ssd(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, chunk_size=64, h_init=No
                 Bf = np.concatenate([Bg, Bb], axis=-1)
             else:                                                     # ssd.py:200-202
                 Bf = Bg
-            BX = np.einsum("hcpq,hcnq->hcpn", dtx, Bf, optimize=True)  # (H,CS,P,N)
+            BX = np.matmul(dtx, Bf.transpose(0, 1, 3, 2))             # (H,CS,P,N), bmm of ssd.py:198
             # _IntraChunkFn.forward, ssd.py:44-58
             enc = np.exp(-cum[k])[:, :, None, None]
             ec = exp_cum[k][:, :, None, None]
             scaled = BX * enc
             mid = ec * np.cumsum(scaled, axis=1)
-            Ck = C[b, sl].transpose(1, 3, 0, 2)                       # (H,R,CS,N)
-            y_intra[k] = np.einsum("hrcn,hcpn->hrcp", Ck, mid, optimize=True)
+            Ck = C[b, sl].transpose(1, 0, 3, 2)                       # (H,CS,R,N)
+            # bmm of ssd.py:49-56: per token (R x N) . (N x P)
+            y_intra[k] = np.matmul(Ck, mid.transpose(0, 1, 3, 2)).transpose(0, 2, 1, 3)
             # ssd.py:207-208
             h_chunk[k] = chunk_decay[k][:, None, None] * scaled.sum(axis=1)
         # ssd.py:210-213 -- inter-chunk scan
@@ -279,7 +280,7 @@ def chunked_ssd(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, chunk_size=64, h_init=No
             sl = slice(k * CS, (k + 1) * CS)
             Ck = C[b, sl].transpose(1, 3, 0, 2)                       # (H,R,CS,N)
             # ssd.py:215-222
-            y_inter = np.einsum("hrcn,hpn->hrcp", Ck, h_states[k], optimize=True) * exp_cum[k][:, None, :, None]
+            y_inter = np.matmul(Ck, h_states[k].transpose(0, 2, 1)[:, None]) * exp_cum[k][:, None, :, None]
             # ssd.py:224-233
             y_d = D[:, None, None, None] * x_raw[b, sl].transpose(1, 3, 0, 2)
             tot = y_intra[k] + y_inter + y_d                          # (H,R,CS,P)

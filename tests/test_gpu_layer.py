@@ -1,0 +1,121 @@
+"""Layer-level parity of the chunked tensor-core forward / prefill on the GPU.
+
+* fp32 models against the reference's golden outputs (the tensor-core operands are
+  bf16, so fp32 I/O is held to the bf16 tolerance 2e-2; fp32-accumulated states to 2e-2,
+  the angle -- pure fp32 arithmetic -- to 1e-4);
+* bf16 models against the fp64 oracle on the same bf16-rounded weights (2e-2);
+* properties at the benchmark sizes: causality (a prefix of the full-size output equals
+  the oracle on that prefix), chaining (prefill of a split sequence == prefill of the
+  whole), parallel == recurrent.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from goldens import LAYER_CASES, load, max_rel
+from helpers import oracle_params, ours_layer_from_golden, to_np
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 2e-2
+
+
+@pytest.mark.parametrize("case", LAYER_CASES)
+def test_forward_prefill_golden_fp32(case):
+    d = load(f"layer_{case}")
+    m = ours_layer_from_golden(d, torch.float32)
+    T = int(d["T"])
+    x = torch.from_numpy(d["x"][:, :T]).cuda()
+    with torch.no_grad():
+        y = m(x)
+        y2, st = m.prefill(x)
+    assert max_rel(to_np(y), d["y"]) < BF16_TOL
+    assert max_rel(to_np(y2), d["y"]) < BF16_TOL
+    assert max_rel(to_np(st["h"]), d["pf_h"]) < BF16_TOL
+    assert max_rel(to_np(st["angle"]), d["pf_angle"]) < 1e-4
+    assert max_rel(to_np(st["prev_BX"]), d["pf_prev_BX"]) < 1e-4
+
+
+@pytest.mark.parametrize("case", LAYER_CASES)
+def test_forward_bf16_vs_oracle(case):
+    d = load(f"layer_{case}")
+    m = ours_layer_from_golden(d, torch.bfloat16)
+    p = oracle_params(m)
+    T = int(d["T"])
+    x = torch.from_numpy(d["x"][:, :T]).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        y, st = m.prefill(x)
+    oy, ost = oracle.layer_prefill(p, to_np(x))
+    assert max_rel(to_np(y), oy) < BF16_TOL
+    assert max_rel(to_np(st["h"]), ost["h"]) < BF16_TOL
+    assert max_rel(to_np(st["prev_BX"]), ost["prev_BX"]) < BF16_TOL
+
+
+@pytest.mark.parametrize("case", ["default", "perturbed", "rank1", "rank4", "euler", "real", "ngroups2"])
+def test_parallel_equals_recurrent(case):
+    """Forward (chunked, tensor cores) vs the step kernel token by token (fp32 model)."""
+    d = load(f"layer_{case}")
+    m = ours_layer_from_golden(d, torch.float32)
+    x = torch.from_numpy(d["x"]).cuda()
+    B, T = x.shape[:2]
+    with torch.no_grad():
+        y_par = m(x)
+        st = m.allocate_inference_state(B)
+        ys = []
+        for t in range(T):
+            yt, st = m.step(x[:, t:t + 1], st)
+            ys.append(yt[:, 0])
+    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < BF16_TOL
+
+
+def test_chaining_prefill_from_state():
+    """prefill(x[:, :T1]) then prefill_from(x[:, T1:]) == prefill(x) (sequence-split property)."""
+    d = load("layer_n128p64")
+    m = ours_layer_from_golden(d, torch.bfloat16)
+    x = torch.from_numpy(d["x"]).cuda().to(torch.bfloat16)
+    T1 = 70
+    with torch.no_grad():
+        y, st = m.prefill(x)
+        y1, st1 = m.prefill(x[:, :T1])
+        y2, st2 = m.prefill_from(x[:, T1:], st1)
+    assert max_rel(to_np(torch.cat([y1, y2], 1)), to_np(y)) < BF16_TOL
+    for k in ("h", "angle", "prev_BX"):
+        assert max_rel(to_np(st2[k]), to_np(st[k])) < BF16_TOL
+
+
+def test_extreme_decay_finite():
+    """A_log = 0, dt_bias = 3 (mamba3 tests :410-423): segsum form stays finite."""
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(0)
+    m = KulaMamba(d_model=64, d_state=16, headdim=16, mimo_rank=2, chunk_size=8).cuda().eval()
+    with torch.no_grad():
+        m.A_log.fill_(0.0)
+        m.dt_bias.fill_(3.0)
+        x = torch.randn(1, 300, 64, device="cuda")
+        y = m(x)
+    assert torch.isfinite(y).all() and y.abs().max() > 0
+    p = oracle_params(m)
+    oy, _ = oracle.layer_forward(p, to_np(x))
+    assert max_rel(to_np(y), oy) < BF16_TOL
+
+
+@pytest.mark.parametrize("B,T,seed", [(16, 4096, 1)])
+def test_cfg1_full_size_prefix_parity(B, T, seed):
+    """Config 1 at full size: rows 0 and B-1, first 256 tokens vs the oracle (causal prefix)."""
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(0)
+    m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2, chunk_size=64).cuda().to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, T, 768, generator=g).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        y, st = m.prefill(x)
+    assert torch.isfinite(y).all() and torch.isfinite(st["h"]).all()
+    p = oracle_params(m)
+    Tp = 256
+    for b in (0, B - 1):
+        oy, _ = oracle.layer_forward(p, to_np(x[b:b + 1, :Tp]))
+        assert max_rel(to_np(y[b:b + 1, :Tp]), oy) < BF16_TOL

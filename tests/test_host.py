@@ -1,0 +1,118 @@
+"""CPU-only checks of the boundary and the host logic (no kernel launches)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from goldens import LAYER_CASES, layer_cfg, load, state_dict
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        names |= set(re.findall(r"M3B_API\s+[\w\s\*]+?\b(m3b_\w+)\s*\(", h.read_text()))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol():
+    from mamba3_b200 import _lib
+
+    names = declared_symbols()
+    assert len(names) >= 8
+    h = ctypes.CDLL(str(_lib.LIB_PATH))
+    for n in names:
+        assert hasattr(h, n), n
+    assert set(names) == set(_lib.SIGNATURES), "ctypes binding must cover exactly the header"
+    L = _lib.lib()
+    assert L.m3b_abi_version() == 1
+    assert L.m3b_strerror(0) == b"ok"
+
+
+def test_library_rejects_bad_args_without_gpu():
+    """Argument validation runs on the host and reports status codes, never aborts."""
+    from mamba3_b200 import _lib
+
+    L = _lib.lib()
+    a = _lib.ScanArgs()
+    assert L.m3b_scan_fwd(ctypes.byref(a), None) == 1  # M3B_ERR_INVALID_ARG: null pointers
+    assert b"null" in L.m3b_last_error()
+    s = _lib.StepArgs()
+    assert L.m3b_step(ctypes.byref(s), None) == 1
+    f = _lib.LayerFwdArgs()
+    assert L.m3b_layer_fwd_workspace(ctypes.byref(f)) == 0
+    assert L.m3b_layer_fwd(ctypes.byref(f), None, 0, None) == 1
+
+
+@pytest.mark.parametrize("case", ["default", "rank1", "ngroups2", "euler", "real"])
+def test_seeded_init_matches_reference(case):
+    """Same constructor, names, shapes and RNG draws as the reference: identical weights under a seed."""
+    from mamba3_b200 import KulaMamba
+
+    d = load(f"layer_{case}")
+    if int(d["perturb"]):
+        pytest.skip("perturbed fixture")
+    torch.manual_seed(int(d["seed"]))
+    m = KulaMamba(**layer_cfg(d))
+    ref = state_dict(d)
+    sd = m.state_dict()
+    assert set(sd) == set(ref)
+    for k, v in sd.items():
+        np.testing.assert_array_equal(v.numpy(), ref[k], err_msg=k)
+
+
+def test_seeded_init_matches_reference_big():
+    """Config-0 dims: weight checksums of the reference's seed-0 init."""
+    import hashlib
+
+    from mamba3_b200 import KulaMamba
+
+    d = load("biglayer_cfg0dims")
+    torch.manual_seed(int(d["seed"]))
+    m = KulaMamba(d_model=768, d_state=128, expand=2, headdim=64, mimo_rank=2, chunk_size=64)
+    for k, v in m.state_dict().items():
+        assert abs(float(v.double().sum()) - float(d[f"wsum.{k}"])) < 1e-9 * max(1.0, abs(float(d[f"wsum.{k}"])))
+    w = m.in_proj.weight.detach().contiguous().numpy()
+    assert hashlib.sha1(w.tobytes()).hexdigest().encode() == bytes(d["in_proj_sha1"])
+
+
+def test_lm_structure_matches_reference():
+    from mamba3_b200 import KulaMambaLM
+
+    d = load("lm_small")
+    cfg = {k[4:]: d[k].item() for k in d if k.startswith("cfg.")}
+    torch.manual_seed(int(d["seed"]))
+    lm = KulaMambaLM(**cfg)
+    ref = state_dict(d)
+    sd = lm.state_dict()
+    assert set(sd) == set(ref)
+    for k, v in sd.items():
+        np.testing.assert_array_equal(v.numpy(), ref[k], err_msg=k)
+
+
+def test_cpu_tensors_raise_no_fallback():
+    from mamba3_b200 import KulaMamba, ssd_scan
+    from mamba3_b200._lib import M3bError
+
+    m = KulaMamba(d_model=64, d_state=16, headdim=16, chunk_size=8)
+    with pytest.raises(M3bError):
+        m(torch.randn(1, 8, 64))
+    with pytest.raises(M3bError):
+        m.step(torch.randn(1, 64), m.allocate_inference_state(1))
+    with pytest.raises(M3bError):
+        ssd_scan(torch.rand(1, 2, 1), torch.randn(1, 2, 1, 4))
+
+
+def test_state_shapes_and_dtypes():
+    from mamba3_b200 import KulaMamba
+
+    m = KulaMamba(d_model=64, d_state=16, headdim=16, chunk_size=8)
+    st = m.allocate_inference_state(2, dtype=torch.bfloat16, device="cpu")
+    assert st["h"].shape == (2, 8, 16, 16) and st["prev_BX"].shape == (2, 8, 16, 16)
+    assert st["angle"].shape == (2, 8, 8)
+    assert all(v.dtype == torch.float32 for v in st.values())
