@@ -160,6 +160,37 @@ M3B_API size_t m3b_layer_fwd_workspace(const m3b_layer_fwd_args* a);
 M3B_API int m3b_layer_fwd(const m3b_layer_fwd_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * chunked_ssd on pre-processed tensors.
+ * Replaces the reference's chunked_ssd(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw,
+ * chunk_size, h_init, return_final_state) (mamba3/ssd.py:118-244): the input of token s
+ * is dt_s * sum_q [x_g|x_b][s,:,q] [B_g|B_b][s,:,q]^T (x_b / B_b may be NULL: Euler),
+ * y = intra-chunk + inter-chunk readout + D * x_raw, h_final in fp32.  All tensors are
+ * contiguous; the per-chunk length is the library's own (results do not depend on it).
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_ssd_args {
+  int64_t batch, seqlen;
+  int32_t H, P, N, R;
+  int32_t dtype;             /* of x_g, x_b, B_g, B_b, C, x_raw and y: M3B_BF16 or M3B_F32 */
+  const void* x_g;           /* (batch,seqlen,H,P,R) */
+  const void* x_b;           /* (batch,seqlen,H,P,R) or NULL */
+  const void* B_g;           /* (batch,seqlen,H,N,R) */
+  const void* B_b;           /* (batch,seqlen,H,N,R) or NULL (NULL iff x_b is NULL) */
+  const void* C;             /* (batch,seqlen,H,N,R) */
+  const void* x_raw;         /* (batch,seqlen,H,P,R) */
+  const void* dt;            /* (batch,seqlen,H), dt_dtype */
+  int32_t dt_dtype;
+  const void* A;             /* (H), ad_dtype (A = -exp(A_log), negative) */
+  const void* D;             /* (H), ad_dtype */
+  int32_t ad_dtype;
+  const float* h_init;       /* (batch,H,P,N) or NULL */
+  void* y;                   /* (batch,seqlen,H,P,R), dtype */
+  float* h_final;            /* (batch,H,P,N) or NULL */
+  int* err;                  /* device int or NULL */
+} m3b_ssd_args;
+M3B_API size_t m3b_chunked_ssd_workspace(const m3b_ssd_args* a);
+M3B_API int m3b_chunked_ssd(const m3b_ssd_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Tensor-core self-test (diagnostic; no counterpart in the reference).
  * D (128 x 64, fp32) = A (128 x 128 bf16, row-major) x B (64 x 128 bf16, row-major)^T,
  * staged through the same shared-memory layouts and UMMA descriptors as the chunk

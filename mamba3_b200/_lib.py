@@ -64,6 +64,15 @@ class LayerFwdArgs(C.Structure):
                 ("err", C.c_void_p), ("stage_events", C.POINTER(C.c_void_p))]
 
 
+class SsdArgs(C.Structure):
+    _fields_ = [("batch", C.c_int64), ("seqlen", C.c_int64), ("H", C.c_int32), ("P", C.c_int32), ("N", C.c_int32),
+                ("R", C.c_int32), ("dtype", C.c_int32), ("x_g", C.c_void_p), ("x_b", C.c_void_p),
+                ("B_g", C.c_void_p), ("B_b", C.c_void_p), ("C", C.c_void_p), ("x_raw", C.c_void_p),
+                ("dt", C.c_void_p), ("dt_dtype", C.c_int32), ("A", C.c_void_p), ("D", C.c_void_p),
+                ("ad_dtype", C.c_int32), ("h_init", C.c_void_p), ("y", C.c_void_p), ("h_final", C.c_void_p),
+                ("err", C.c_void_p)]
+
+
 LAYER_FWD_STAGES = ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out", "last_bx")
 
 
@@ -76,6 +85,8 @@ SIGNATURES = {
     "m3b_step": (C.c_int, [C.POINTER(StepArgs), C.c_void_p]),
     "m3b_layer_fwd_workspace": (C.c_size_t, [C.POINTER(LayerFwdArgs)]),
     "m3b_layer_fwd": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_chunked_ssd_workspace": (C.c_size_t, [C.POINTER(SsdArgs)]),
+    "m3b_chunked_ssd": (C.c_int, [C.POINTER(SsdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_selftest_umma": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
 }
 
@@ -182,6 +193,23 @@ def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=
     with torch.cuda.device(dev):
         _check(L.m3b_layer_fwd(C.byref(a), _ptr(workspace), need, _stream(dev)), "m3b_layer_fwd")
     return workspace
+
+
+def chunked_ssd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, y, h_init=None, h_final=None, err=None):
+    """Launch the general chunked SSD; all activations contiguous and of one dtype."""
+    dev = _cuda(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, y, h_init, h_final, err)
+    Bt, T, H, P, R = x_g.shape
+    N = B_g.shape[3]
+    a = SsdArgs(Bt, T, H, P, N, R, dtype_code(x_g.dtype), _ptr(x_g), _ptr(x_b), _ptr(B_g), _ptr(B_b), _ptr(Cm),
+                _ptr(x_raw), _ptr(dt), dtype_code(dt.dtype), _ptr(A), _ptr(D), dtype_code(A.dtype), _ptr(h_init),
+                _ptr(y), _ptr(h_final), _ptr(err))
+    L = lib()
+    need = L.m3b_chunked_ssd_workspace(C.byref(a))
+    if need == 0:
+        _check(L.m3b_chunked_ssd(C.byref(a), None, 0, None), "m3b_chunked_ssd")
+    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(L.m3b_chunked_ssd(C.byref(a), _ptr(ws), need, _stream(dev)), "m3b_chunked_ssd")
 
 
 def selftest_umma(A, B, mode):

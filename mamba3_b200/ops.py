@@ -86,6 +86,37 @@ def _(proj, A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_
 
 
 # ---------------------------------------------------------------------------
+# chunked SSD on pre-processed tensors (the reference's chunked_ssd)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("mamba3_b200::chunked_ssd", mutates_args=())
+def chunked_ssd(x_g: torch.Tensor, x_b: Optional[torch.Tensor], B_g: torch.Tensor, B_b: Optional[torch.Tensor],
+                C: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, D: torch.Tensor, x_raw: torch.Tensor,
+                h_init: Optional[torch.Tensor], return_final_state: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    wd = x_g.dtype if x_g.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    c = lambda t: None if t is None else t.to(wd).contiguous()  # noqa: E731
+    xg, xb, Bg, Bb, Cc, xr = map(c, (x_g, x_b, B_g, B_b, C, x_raw))
+    Bt, T, H, P, R = xg.shape
+    N = Bg.shape[3]
+    y = torch.empty(Bt, T, H, P, R, dtype=wd, device=xg.device)
+    hf = torch.empty(Bt, H, P, N, dtype=torch.float32, device=xg.device) if return_final_state else None
+    A32 = A.float().contiguous()
+    D32 = D.to(A32.dtype).contiguous()
+    hi = None if h_init is None else h_init.float().contiguous()
+    _lib.chunked_ssd(xg, xb, Bg, Bb, Cc, dt.float().contiguous(), A32, D32, xr, y, h_init=hi, h_final=hf)
+    y = y if y.dtype == x_g.dtype else y.to(x_g.dtype)
+    return y, (hf if hf is not None else torch.empty(0, dtype=torch.float32, device=xg.device))
+
+
+@chunked_ssd.register_fake
+def _(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, h_init, return_final_state):
+    Bt, T, H, P, R = x_g.shape
+    N = B_g.shape[3]
+    hf = (torch.empty(Bt, H, P, N, dtype=torch.float32, device=x_g.device) if return_final_state
+          else torch.empty(0, dtype=torch.float32, device=x_g.device))
+    return torch.empty_like(x_g), hf
+
+
+# ---------------------------------------------------------------------------
 # decode step (everything between in_proj and out_proj of KulaMamba.step)
 # ---------------------------------------------------------------------------
 @torch.library.custom_op("mamba3_b200::step_ssm", mutates_args=())

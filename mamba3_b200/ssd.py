@@ -10,6 +10,8 @@ from dataclasses import dataclass
 
 import torch
 
+from . import ops
+
 
 @dataclass
 class SSDOutput:
@@ -20,4 +22,12 @@ class SSDOutput:
 
 
 def chunked_ssd(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, chunk_size=64, h_init=None, return_final_state=False):
-    raise NotImplementedError("mamba3_b200.chunked_ssd: general (pre-processed input) kernel not built yet")
+    """Chunked SSD forward on pre-processed inputs (mamba3/ssd.py:118-244).
+
+    x_g, x_b, x_raw: (B,T,H,P,R); B_g, B_b, C: (B,T,H,N,R); dt: (B,T,H); A, D: (H,);
+    h_init: (B,H,P,N) or None.  ``x_b``/``B_b`` None selects the Euler form.  ``chunk_size``
+    is accepted for API compatibility; the kernels use their own chunk length, which does
+    not change the result beyond fp32 rounding.  Returns SSDOutput(y in x_g.dtype, h_final fp32).
+    """
+    y, hf = ops.chunked_ssd(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, h_init, return_final_state)
+    return SSDOutput(y=y, h_final=hf if return_final_state else None)
