@@ -162,6 +162,8 @@ __device__ void chunk_scalars(const FwdParams& a, uint8_t* sm, int b, int k, int
 }
 
 // phi[s][i] = omega_k[i] - sum_{s'<=s} dt_s' theta_s'[i]   (mamba3/mamba3.py:160-162)
+// All (s, i) products are loaded in one coalesced pass, then each i is scanned in
+// nseg segments in parallel (segment totals combined in shared memory).
 template <typename TA, int RP>
 __device__ void chunk_angles(const FwdParams& a, uint8_t* sm, int b, int k, int h) {
   using PL = Plan<RP>;
@@ -170,21 +172,47 @@ __device__ void chunk_angles(const FwdParams& a, uint8_t* sm, int b, int k, int 
   const int nh2 = p.N / 2;
   const float* dtv = reinterpret_cast<const float*>(sm + PL::dtv);
   float* phi = reinterpret_cast<float*>(sm + PL::phi);
+  // segment totals (<= kCT floats); the H'-tile region is not in use during the prologue
+  float* segtot = reinterpret_cast<float*>(sm + PL::tileH);
   const int64_t t0 = (int64_t)k * L;
   const int offTh = 2 * p.H * p.P + 2 * p.G * p.N * p.R + p.H + (p.trapezoidal ? p.H : 0);
   const TA* base = reinterpret_cast<const TA*>(a.proj) + (int64_t)b * a.T * a.proj_stride + offTh;
-  const int i = threadIdx.x;
-  if (i < nh2) {
-    const float om = a.omega[(((int64_t)b * (a.K + 1) + k) * p.H + h) * nh2 + i];
-    float acc = 0.f;
-    const int nt = (int)((a.T - t0) < L ? (a.T - t0) : L);
-#pragma unroll 8
-    for (int s = 0; s < L; ++s) {
-      const float th = s < nt ? io<TA>::ld(base + (t0 + s) * a.proj_stride + i) : 0.f;
-      acc = fmaf(dtv[s], th, acc);
-      phi[s * 64 + i] = om - acc;
-    }
+  const int nt = (int)((a.T - t0) < L ? (a.T - t0) : L);
+  for (int e = threadIdx.x; e < L * nh2; e += kCT) {
+    const int s = e / nh2, i = e - s * nh2;
+    phi[s * 64 + i] = s < nt ? dtv[s] * io<TA>::ld(base + (t0 + s) * a.proj_stride + i) : 0.f;
   }
+  __syncthreads();
+  int nseg = 1;
+  while (nseg * 2 * nh2 <= kCT && nseg * 2 <= L && nseg * 2 <= 32) nseg *= 2;
+  const int seglen = L / nseg;
+  const int i = threadIdx.x % nh2, seg = threadIdx.x / nh2;
+  const bool act = seg < nseg;
+  float run = 0.f;
+  if (act) {
+    for (int s = seg * seglen; s < (seg + 1) * seglen; ++s) {
+      run += phi[s * 64 + i];
+      phi[s * 64 + i] = run;
+    }
+    segtot[seg * nh2 + i] = run;
+  }
+  __syncthreads();
+  if (act) {
+    const float om = a.omega[(((int64_t)b * (a.K + 1) + k) * p.H + h) * nh2 + i];
+    float off = 0.f;
+    for (int q = 0; q < seg; ++q) off += segtot[q * nh2 + i];
+    for (int s = seg * seglen; s < (seg + 1) * seglen; ++s) phi[s * 64 + i] = om - (off + phi[s * 64 + i]);
+  }
+  __syncthreads();
+}
+
+// sin/cos of an unbounded angle: Cody-Waite reduction by 2*pi (2*pi split into its fp32
+// value and the fp32 remainder), then the hardware approximations on [-pi, pi].
+__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+  const float kq = rintf(x * 0.15915494309189535f);
+  float r = fmaf(-kq, 6.28318548202514648f, x);
+  r = fmaf(-kq, -1.7484555314695172e-7f, r);
+  __sincosf(r, s, c);
 }
 
 // Layer parameters used by the producers / epilogue, staged in fp32.
@@ -313,7 +341,7 @@ __device__ void chunk_produce_bc(const FwdParams& a, uint8_t* sm, int b, int k, 
 #pragma unroll
         for (int pr = 0; pr < 4; ++pr) {
           float sn, cs;
-          sincosf(phi[s * 64 + c * 4 + pr], &sn, &cs);
+          sincos_reduced(phi[s * 64 + c * 4 + pr], &sn, &cs);
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             const int e0 = (2 * pr) * R + r, e1 = (2 * pr + 1) * R + r;
