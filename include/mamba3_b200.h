@@ -155,6 +155,21 @@ typedef struct m3b_layer_fwd_args {
   void* const* stage_events;
 } m3b_layer_fwd_args;
 #define M3B_LAYER_FWD_STAGES 6
+
+/* ------------------------------------------------------------------------
+ * Allocation-free layer forward (no counterpart in the reference).
+ * For callers that cannot allocate device memory where they run the layer --
+ * e.g. a plugin hosted by another runtime that owns the allocator and hands it
+ * only input and output buffers.  Same arguments and results as m3b_layer_fwd,
+ * but the workspace is a static device array of M3B_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading the library holds until exit; larger problems fail with
+ * M3B_ERR_WORKSPACE.  All calls share that array: calls that overlap on the GPU
+ * race and must be serialised by the caller.  The first call on a device looks
+ * the array's address up; make it before any stream capture.  Calls no
+ * allocating routine.
+ * ------------------------------------------------------------------------ */
+#define M3B_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+M3B_API int m3b_layer_fwd_noalloc(const m3b_layer_fwd_args* a, void* stream);
 /* Bytes of device workspace m3b_layer_fwd needs for these arguments. */
 M3B_API size_t m3b_layer_fwd_workspace(const m3b_layer_fwd_args* a);
 M3B_API int m3b_layer_fwd(const m3b_layer_fwd_args* a, void* workspace, size_t workspace_bytes, void* stream);

@@ -85,6 +85,7 @@ SIGNATURES = {
     "m3b_step": (C.c_int, [C.POINTER(StepArgs), C.c_void_p]),
     "m3b_layer_fwd_workspace": (C.c_size_t, [C.POINTER(LayerFwdArgs)]),
     "m3b_layer_fwd": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_layer_fwd_noalloc": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p]),
     "m3b_chunked_ssd_workspace": (C.c_size_t, [C.POINTER(SsdArgs)]),
     "m3b_chunked_ssd": (C.c_int, [C.POINTER(SsdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_selftest_umma": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
