@@ -153,6 +153,10 @@ typedef struct m3b_layer_fwd_args {
    * stage i (prep, angle prefix, chunk state, scan, chunk output, prefill prev_BX) and the
    * last one after the final stage, so callers can time each kernel. */
   void* const* stage_events;
+  /* 0: automatic; 1: fused sequential kernel (one persistent CTA per SM walks whole
+   * (batch, head) sequences, state kept on chip); 2: chunk-parallel kernels (chunk
+   * states in HBM + scan). Same results up to fp32 rounding. */
+  int32_t algo;
 } m3b_layer_fwd_args;
 #define M3B_LAYER_FWD_STAGES 6
 
@@ -209,7 +213,8 @@ M3B_API int m3b_chunked_ssd(const m3b_ssd_args* a, void* workspace, size_t works
  * Tensor-core self-test (diagnostic; no counterpart in the reference).
  * D (128 x 64, fp32) = A (128 x 128 bf16, row-major) x B (64 x 128 bf16, row-major)^T,
  * staged through the same shared-memory layouts and UMMA descriptors as the chunk
- * kernels: mode 0 reads A K-major, mode 1 stages A transposed and reads it MN-major.
+ * kernels: mode 0 reads A K-major, mode 1 stages A transposed and reads it MN-major,
+ * mode 2 stages B transposed and reads it MN-major.
  * ------------------------------------------------------------------------ */
 M3B_API int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream);
 

@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kCT) prep_kernel(FwdParams a) {
       o[1] = rsqrtf(sc / (float)NR + p.norm_eps);
     }
   }
-  if (!p.complex_ssm) return;
+  if (!p.complex_ssm || !a.asum) return;
   const int nh2 = p.N / 2;
   const int offTh = offC + G * NR + H + (p.trapezoidal ? H : 0);
   for (int e = threadIdx.x; e < nt * nh2; e += kCT) {
@@ -401,7 +401,7 @@ __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
 // prefill prev_BX = sum_r B^_{T-1}[n,r] x_r[T-1,p,r]  (mamba3/mamba3.py:248-250), fp32.
 // ---------------------------------------------------------------------------
 template <typename TA>
-__global__ void __launch_bounds__(kCT) last_bx_kernel(FwdParams a, float* prev_bx) {
+__global__ void __launch_bounds__(kCT) last_bx_kernel(FwdParams a, const float* angle_last, float* prev_bx) {
   __shared__ float sB[kNS * 8];
   __shared__ float sX[kPP * 8];
   const m3b_layer_params& p = a.prm;
@@ -417,7 +417,7 @@ __global__ void __launch_bounds__(kCT) last_bx_kernel(FwdParams a, float* prev_b
     sX[e] = io<TA>::ld(row + H * P + h * P + e / R) * ldf(p.mimo_x, (int64_t)h * P * R + e, pd);
   __syncthreads();
   if (p.complex_ssm) {
-    const float* ang = a.omega + (((int64_t)b * (a.K + 1) + a.K) * H + h) * (N / 2);
+    const float* ang = angle_last + ((int64_t)b * H + h) * (N / 2);
     for (int i = threadIdx.x; i < N / 2; i += kCT) {
       float sn, cs;
       sincosf(ang[i], &sn, &cs);
@@ -444,19 +444,31 @@ __global__ void __launch_bounds__(kCT) last_bx_kernel(FwdParams a, float* prev_b
 namespace {
 
 struct WsLayout {
-  size_t rms, asum, omega, sstate, hstate, decay, coef0, total;
+  size_t rms, asum, omega, sstate, hstate, decay, coef0, angle_last, total;
+  bool fused;
 };
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool use_fused(const m3b_layer_fwd_args* a) {
+  if (a->algo == 2) return false;
+  return fused_supported(a->prm);
+}
 
 WsLayout ws_layout(const m3b_layer_fwd_args* a, int L) {
   const m3b_layer_params& p = a->prm;
   const int64_t B = a->batch, T = a->seqlen, K = (T + L - 1) / L;
   const size_t ssz = (a->act_dtype == M3B_BF16) ? 2 : 4;
   const bool cx = p.complex_ssm != 0;
-  WsLayout w;
+  WsLayout w{};
   size_t o = 0;
+  w.fused = use_fused(a);
   w.rms = o; o += up256((size_t)B * T * p.G * 2 * 4);
+  w.angle_last = o; o += up256((size_t)B * p.H * (p.N / 2) * 4);
+  if (w.fused) {
+    w.total = o;
+    return w;
+  }
   w.asum = o; o += cx ? up256((size_t)B * K * p.H * (p.N / 2) * 4) : 0;
   w.omega = o; o += cx ? up256((size_t)B * (K + 1) * p.H * (p.N / 2) * 4) : 0;
   w.sstate = o; o += up256((size_t)B * K * p.H * p.P * p.N * ssz);
@@ -539,7 +551,7 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
   fp.asum = reinterpret_cast<float*>(ws + w.asum);
   fp.omega = reinterpret_cast<float*>(ws + w.omega);
   fp.angle_init = a->angle_init;
-  fp.angle_final = a->angle_final;
+  fp.angle_final = reinterpret_cast<float*>(ws + w.angle_last);
   fp.sstate = ws + w.sstate;
   fp.hstate = ws + w.hstate;
   fp.decay = reinterpret_cast<float*>(ws + w.decay);
@@ -550,13 +562,56 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
   auto mark = [&](int i) {
     if (a->stage_events) cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), st);
   };
+  float* angle_last = reinterpret_cast<float*>(ws + w.angle_last);
   mark(0);
+  if (w.fused) fp.asum = nullptr;
   prep_kernel<TA><<<dim3((unsigned)fp.K, (unsigned)fp.B), kCT, 0, st>>>(fp);
   if ((rc = check_launch("prep")) != M3B_OK) return rc;
+  if (w.fused) {
+    mark(1);
+    mark(2);
+    mark(3);
+    mark(4);
+    FusedParams f{};
+    f.prm = p;
+    f.proj = a->proj;
+    f.proj_stride = a->proj_stride;
+    f.dt_scale = a->dt_scale;
+    f.B = fp.B;
+    f.T = fp.T;
+    f.K = fp.K;
+    f.L = fp.L;
+    f.rms = fp.rms;
+    f.h_init = a->h_init;
+    f.angle_init = a->angle_init;
+    f.prev_bx_init = a->prev_bx_init;
+    f.y = a->y;
+    f.h_final = a->h_final;
+    f.angle_last = angle_last;
+    f.err = a->err;
+    if ((rc = launch_fused(f, st, a->act_dtype == M3B_BF16)) != M3B_OK) return rc;
+    if (a->angle_final) {
+      const cudaError_t e = cudaMemcpyAsync(a->angle_final, angle_last, (size_t)fp.B * p.H * (p.N / 2) * 4,
+                                            cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "angle_final: %s", cudaGetErrorString(e));
+    }
+    mark(5);
+    if (a->prev_bx_final) {
+      last_bx_kernel<TA><<<(unsigned)(fp.B * p.H), kCT, 0, st>>>(fp, angle_last, a->prev_bx_final);
+      if ((rc = check_launch("last_bx")) != M3B_OK) return rc;
+    }
+    mark(6);
+    return M3B_OK;
+  }
   mark(1);
   if (p.complex_ssm) {
     angle_prefix_kernel<<<(unsigned)(fp.B * p.H), kCT, 0, st>>>(fp);
     if ((rc = check_launch("angle_prefix")) != M3B_OK) return rc;
+    if (a->angle_final) {
+      const cudaError_t e = cudaMemcpyAsync(a->angle_final, angle_last, (size_t)fp.B * p.H * (p.N / 2) * 4,
+                                            cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "angle_final: %s", cudaGetErrorString(e));
+    }
   } else if (a->angle_final) {
     const size_t bytes = (size_t)fp.B * p.H * (p.N / 2) * 4;
     const cudaError_t e = a->angle_init
@@ -567,7 +622,7 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
   if ((rc = run_rank<TA, TS>(fp, a, st, mark)) != M3B_OK) return rc;
   mark(5);
   if (a->prev_bx_final) {
-    last_bx_kernel<TA><<<(unsigned)(fp.B * p.H), kCT, 0, st>>>(fp, a->prev_bx_final);
+    last_bx_kernel<TA><<<(unsigned)(fp.B * p.H), kCT, 0, st>>>(fp, angle_last, a->prev_bx_final);
     if ((rc = check_launch("last_bx")) != M3B_OK) return rc;
   }
   mark(6);

@@ -54,6 +54,27 @@ struct FwdParams {
   int* err;
 };
 
+struct FusedParams {
+  m3b_layer_params prm;
+  const void* proj;
+  int64_t proj_stride;
+  const void* dt_scale;
+  int64_t B, T;
+  int K, L;
+  const float* rms;
+  const float* h_init;
+  const float* angle_init;
+  const float* prev_bx_init;
+  void* y;
+  float* h_final;
+  float* angle_last;  // (B,H,N/2): angle after the last token (always written)
+  int* err;
+};
+
+// Fused sequential path (fused.cu): supported shapes and launcher.
+bool fused_supported(const m3b_layer_params& p);
+int launch_fused(const FusedParams& fp, cudaStream_t st, bool bf16);
+
 __host__ __device__ constexpr int rp_of(int R) { return R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8; }
 
 // dt of token row `row`, head h: softplus(dt_raw + dt_bias) * dt_scale (mamba3/mamba3.py:200-202).

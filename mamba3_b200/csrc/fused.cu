@@ -1,0 +1,724 @@
+// Fused sequential SSD layer kernel: one persistent CTA per SM walks whole (batch, head)
+// sequences chunk by chunk, so the inter-chunk state never leaves the SM.
+//
+// Roles (416 threads):
+//   warps 0-3  epilogue: decay mask S -> P, running-state bookkeeping (TMEM <-> SMEM),
+//              output y = P X + e^cum C^ H'^T + D x, gate, MIMO down, h_final
+//   warps 4-11 producers: per chunk, token scalars, angle prefix + RoPE on B/C, MIMO x tiles,
+//              into one of two shared-memory stages
+//   warp 12    tcgen05 issue (one thread) + TMEM allocation
+// Per chunk g (stage s = g % 2), with the running state H (fp32, TMEM lanes n x cols p):
+//   MMA:  S  = C^ B^T                         (TMEM [0,128))
+//         Yi = C^ H'_g^T   (H' bf16 tile)     (TMEM [256 + 64 (g%2), ...))
+//         H += B^^T (w X)  (H already scaled by the chunk decay)   (TMEM [384,448))
+//         Y  = P X         (P = mask(S))      (TMEM [128 + 64 (g%2), ...))
+//   epilogue: mask(g); state(g+1): H'_{g+1} = H -> bf16 tile, H *= d_{g+1}; output(g)
+// The algebra (weights W, w, the first-token beta term carried by H') is in chunk.cuh.
+// Every wait is bounded; on a timeout one leader thread per role raises a shared abort flag
+// that its role reads after a named barrier, so every role leaves its loop uniformly.
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "chunk.cuh"
+
+namespace m3b {
+
+constexpr int kFusedThreads = 13 * 32;
+constexpr int kEpiThreads = 128;
+constexpr int kProdThreads = 256;
+constexpr int kMmaWarp = 12;
+constexpr uint32_t kColS = 0, kColY = 128, kColYi = 256, kColH = 384;
+constexpr int kBarProd = 1, kBarEpi = 2;
+
+template <int RP>
+struct FPlan {
+  static constexpr int L = 128 / RP;
+  static constexpr int kStage = 98304;
+  static constexpr int tC = 0, tB = 32768, tX = 65536, tW = 81920;  // offsets inside a stage
+  static constexpr int tileH = 2 * kStage;                           // 128 rows (n) x 64 cols (p)
+  static constexpr int NA = L + 1;
+  static constexpr int scalStride = ((8 * NA * 4) + 15) & ~15;       // cum2 dtv gam bpr wst gb rmsB rmsC
+  static constexpr int scal = tileH + 16384;
+  static constexpr int omega = scal + 2 * scalStride;                // 2 x 64 doubles (by chunk parity)
+  static constexpr int segt = omega + 128 * 8;                       // 256 floats
+  static constexpr int bars = segt + 256 * 4;                        // 8 mbarriers
+  static constexpr int misc = bars + 64;                             // taddr, abort
+  static constexpr int bytes = misc + 16 + 1024;
+  static_assert(bytes <= 227 * 1024, "fused CTA shared memory exceeds 227 KB");
+};
+
+enum { BAR_FULL0 = 0, BAR_FULL1 = 1, BAR_EMPTY0 = 2, BAR_EMPTY1 = 3, BAR_SMMA = 4, BAR_YMMA = 5, BAR_HREADY = 6,
+       BAR_PREADY = 7 };
+
+// CTA c walks sequences (batch, head) = c, c + stride, c + 2 stride, ... of nseq_total,
+// each chunk by chunk; g numbers the chunks of all its sequences.
+struct Sched {
+  int K, H, nseq_total, stride;
+  __device__ int count() const { return (nseq_total - (int)blockIdx.x + stride - 1) / stride; }
+  __device__ void at(int g, int& seq, int& b, int& h, int& k) const {
+    const int j = g / K;
+    k = g - j * K;
+    seq = (int)blockIdx.x + j * stride;
+    b = seq / H;
+    h = seq - b * H;
+  }
+};
+
+// One leader waits on the mbarrier; the role's named barrier then releases the others.
+// Returns false (for every thread of the role) once any wait of this CTA has timed out.
+__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, bool leader, int bar_id, int nthreads,
+                                          volatile int* abort_flag, int* err) {
+  if (leader && !*abort_flag) {
+    if (!mbar_wait(bar, parity)) {
+      *abort_flag = 1;
+      record_error(err, M3B_ERR_TIMEOUT);
+    }
+  }
+  named_bar(bar_id, nthreads);
+  return *abort_flag == 0;
+}
+
+// 2R consecutive activations (the (2i, 2i+1) x R block of a B or C row) as floats.
+template <typename TA, int R>
+__device__ __forceinline__ void load_pair_block(const TA* p, float (&v)[2 * R]) {
+  if constexpr (sizeof(TA) == 2) {
+    if constexpr (R == 1) {
+      const uint32_t u = __ldg(reinterpret_cast<const unsigned int*>(p));
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+      v[0] = f.x;
+      v[1] = f.y;
+    } else if constexpr (R == 2) {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float2 f = __bfloat1622float2(hh[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+      }
+    } else if constexpr (R == 4) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(hh[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < R; ++e) {
+        const uint32_t u = __ldg(reinterpret_cast<const unsigned int*>(p) + e);
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 2 * R; ++e) v[e] = __ldg(reinterpret_cast<const float*>(p) + e);
+  }
+}
+
+template <typename TA, int R>
+__global__ void __maxnreg__(152) ssd_fused_kernel(FusedParams a, Sched sc) {
+  constexpr int RP = rp_of(R);
+  using PL = FPlan<RP>;
+  constexpr int L = PL::L;
+  constexpr int NA = PL::NA;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const m3b_layer_params& p = a.prm;
+  const int H = p.H, P = p.P, N = p.N, NR = N * R;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + PL::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + PL::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + PL::misc + 4);
+  double* omega = reinterpret_cast<double*>(sm + PL::omega);
+  float* segt = reinterpret_cast<float*>(sm + PL::segt);
+  const int G = sc.count() * sc.K;
+
+  if (warp == kMmaWarp) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bars[BAR_FULL0], 1);
+    mbar_init(&bars[BAR_FULL1], 1);
+    mbar_init(&bars[BAR_EMPTY0], kEpiThreads);
+    mbar_init(&bars[BAR_EMPTY1], kEpiThreads);
+    mbar_init(&bars[BAR_SMMA], 1);
+    mbar_init(&bars[BAR_YMMA], 1);
+    mbar_init(&bars[BAR_HREADY], 1);
+    mbar_init(&bars[BAR_PREADY], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  // columns n >= N of the operand tiles stay zero for the whole kernel (only tileC keeps them;
+  // tileB is rewritten by P each chunk, so producers zero them per chunk when N < 128)
+  for (int e = tid; e < (2 * PL::kStage + 16384) / 16; e += kFusedThreads)
+    reinterpret_cast<uint4*>(sm)[e] = make_uint4(0, 0, 0, 0);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  const TA* proj = reinterpret_cast<const TA*>(a.proj);
+  const int HP = H * P;
+  const int offB = 2 * HP, offC = offB + p.G * NR, offDt = offC + p.G * NR;
+  const int offLam = offDt + H, offTh = offLam + (p.trapezoidal ? H : 0);
+
+  if (warp >= 4 && warp < 12) {
+    // =============================== producers ===============================
+    const int ptid = tid - 128;
+    const int nh2 = N / 2;
+    int nseg = 1;
+    while (nseg * 2 * nh2 <= kProdThreads && nseg * 2 <= L) nseg *= 2;
+    const int seglen = L / nseg;
+    const bool bc_act = ptid < nh2 * nseg;
+    const int pi = ptid % nh2, seg = ptid / nh2;
+    const int pc = ptid & 7;  // x-tile p-chunk
+    float wB[2][R], bB[2][R], wC[2][R], bC[2][R];
+    float mx[8][RP];
+    for (int g = 0; g < G; ++g) {
+      const int s = g & 1;
+      int seq, b, h, k;
+      sc.at(g, seq, b, h, k);
+      const int grp = h / (H / p.G);
+      const int64_t t0 = (int64_t)k * L;
+      const TA* rowbase = proj + (int64_t)b * a.T * a.proj_stride;
+      if (k == 0) {
+        const int pd = p.param_dtype;
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int idx = (2 * pi + e) * R + r;
+            const bool okn = bc_act && (2 * pi + e) < N;
+            wB[e][r] = okn ? ldf(p.B_norm_w, idx, pd) : 0.f;
+            wC[e][r] = okn ? ldf(p.C_norm_w, idx, pd) : 0.f;
+            bB[e][r] = okn ? ldf(p.B_bias, (int64_t)grp * NR + idx, pd) : 0.f;
+            bC[e][r] = okn ? ldf(p.C_bias, (int64_t)grp * NR + idx, pd) : 0.f;
+          }
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+          for (int q = 0; q < RP; ++q) {
+            const int pp = pc * 8 + e;
+            mx[e][q] = (pp < P && q < R) ? ldf(p.mimo_x, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
+          }
+        if (ptid < nh2)
+          omega[(g & 1) * 64 + ptid] = a.angle_init ? (double)a.angle_init[((int64_t)b * H + h) * nh2 + ptid] : 0.0;
+      }
+      if (g >= 2 && !role_wait(&bars[BAR_EMPTY0 + s], ((g >> 1) - 1) & 1, ptid == 0, kBarProd, kProdThreads,
+                               abort_flag, a.err))
+        break;
+      uint8_t* st = sm + s * PL::kStage;
+      float* scal = reinterpret_cast<float*>(sm + PL::scal + s * PL::scalStride);
+      float* cum2 = scal;
+      float* dtv = scal + NA;
+      float* gam = scal + 2 * NA;
+      float* bpr = scal + 3 * NA;
+      float* wst = scal + 4 * NA;
+      float* gbw = scal + 5 * NA;
+      float* rmsB = scal + 6 * NA;
+      float* rmsC = scal + 7 * NA;
+      // (1) token scalars (token L is the next chunk's first token)
+      if (ptid <= L) {
+        const int64_t t = t0 + ptid;
+        float dt = 0.f, gmm = 0.f, bp = 0.f, rb = 0.f, rc = 0.f;
+        if (t < a.T) {
+          const TA* row = rowbase + t * a.proj_stride;
+          dt = softplus_f(io<TA>::ld(row + offDt + h) + ldf(p.dt_bias, h, p.param_dtype));
+          if (a.dt_scale) dt *= io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + ((int64_t)b * a.T + t) * H + h);
+          if (p.trapezoidal) {
+            const float lam = sigmoid_f(io<TA>::ld(row + offLam + h));
+            gmm = lam * dt;
+            bp = (1.f - lam) * dt;
+          } else {
+            gmm = dt;
+          }
+          if (ptid < L) {
+            const float* rr = a.rms + (((int64_t)b * a.T + t) * p.G + grp) * 2;
+            rb = rr[0];
+            rc = rr[1];
+          }
+        }
+        dtv[ptid] = dt;
+        gam[ptid] = gmm;
+        bpr[ptid] = bp;
+        if (ptid < L) {
+          rmsB[ptid] = rb;
+          rmsC[ptid] = rc;
+        }
+      }
+      named_bar(kBarProd, kProdThreads);
+      if (ptid < 32) {
+        constexpr int PER = L / 32;
+        const float A = -expf(ldf(p.A_log, h, p.param_dtype));
+        float v[PER];
+        float run = 0.f;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          run += A * dtv[ptid * PER + e];
+          v[e] = run;
+        }
+        float incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float nb = __shfl_up_sync(0xffffffffu, incl, o);
+          if (ptid >= o) incl += nb;
+        }
+        const float excl = incl - run;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) cum2[ptid * PER + e] = (v[e] + excl) * kLog2e;
+      }
+      named_bar(kBarProd, kProdThreads);
+      if (ptid < L) {
+        const float gw = gam[ptid] + bpr[ptid + 1];
+        gbw[ptid] = gw;
+        wst[ptid] = exp2f(cum2[L - 1] - cum2[ptid]) * gw;
+      }
+      // (2) angles and the rotated, normalised B^ / C^ rows (pair i of tokens [seg*seglen, +seglen))
+      const TA* thp = rowbase + offTh + pi;
+      float segsum = 0.f;
+      if (bc_act && p.complex_ssm) {
+        for (int j = seg * seglen; j < (seg + 1) * seglen; ++j) {
+          const int64_t t = t0 + j;
+          segsum = fmaf(dtv[j], t < a.T ? io<TA>::ld(thp + t * a.proj_stride) : 0.f, segsum);
+        }
+        segt[seg * nh2 + pi] = segsum;
+      }
+      named_bar(kBarProd, kProdThreads);
+      if (bc_act) {
+        float off = 0.f;
+        if (p.complex_ssm) {
+          for (int q = 0; q < seg; ++q) off += segt[q * nh2 + pi];
+        }
+        const double om = omega[(g & 1) * 64 + pi];
+        float run = off;
+        const TA* pB = rowbase + offB + grp * NR + 2 * pi * R;
+        const TA* pC = rowbase + offC + grp * NR + 2 * pi * R;
+        constexpr int TB = R >= 4 ? 2 : 4;  // tokens per load batch
+        for (int j0 = seg * seglen; j0 < (seg + 1) * seglen; j0 += TB) {
+          float vb[TB][2 * R], vc[TB][2 * R], th[TB];
+#pragma unroll
+          for (int u = 0; u < TB; ++u) {
+            const int j = j0 + u;
+            const int64_t t = t0 + j;
+            if (j < (seg + 1) * seglen && t < a.T) {
+              load_pair_block<TA, R>(pB + t * a.proj_stride, vb[u]);
+              load_pair_block<TA, R>(pC + t * a.proj_stride, vc[u]);
+              th[u] = p.complex_ssm ? io<TA>::ld(thp + t * a.proj_stride) : 0.f;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 2 * R; ++e) vb[u][e] = vc[u][e] = 0.f;
+              th[u] = 0.f;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < TB; ++u) {
+            const int j = j0 + u;
+            if (j >= (seg + 1) * seglen) break;
+            const bool valid = t0 + j < a.T;
+            float cs = 1.f, sn = 0.f;
+            if (p.complex_ssm) {
+              run = fmaf(dtv[j], th[u], run);
+              sincos_reduced((float)(om - (double)run), &sn, &cs);
+            }
+            const float rb = rmsB[j], rc = rmsC[j];
+#pragma unroll
+            for (int r = 0; r < RP; ++r) {
+              uint32_t ob = 0, oc = 0;
+              if (r < R && valid) {
+                const float b0 = fmaf(vb[u][r] * rb, wB[0][r], bB[0][r]);
+                const float b1 = fmaf(vb[u][R + r] * rb, wB[1][r], bB[1][r]);
+                const float c0 = fmaf(vc[u][r] * rc, wC[0][r], bC[0][r]);
+                const float c1 = fmaf(vc[u][R + r] * rc, wC[1][r], bC[1][r]);
+                ob = pack_bf16x2(b0 * cs - b1 * sn, b0 * sn + b1 * cs);
+                oc = pack_bf16x2(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
+              }
+              const uint32_t o = sw128_offset(j * RP + r, 2 * pi, 128);
+              *reinterpret_cast<uint32_t*>(st + PL::tB + o) = ob;
+              *reinterpret_cast<uint32_t*>(st + PL::tC + o) = oc;
+            }
+          }
+        }
+        if (seg == nseg - 1) {
+          // angle after this chunk = before - (off + own segment sum); the next chunk reads the other slot
+          const double nom = p.complex_ssm ? om - (double)(off + segsum) : om;
+          omega[((g + 1) & 1) * 64 + pi] = nom;
+          if (k == sc.K - 1) a.angle_last[((int64_t)b * H + h) * nh2 + pi] = (float)nom;
+        }
+      }
+      if (N < kNS) {  // zero columns [N, 128) of the B tile (P of an earlier chunk lives there)
+        const int c0 = N / 8;
+        const int ncz = kNS / 8 - c0;
+        for (int u = ptid; u < 128 * ncz; u += kProdThreads)
+          sw128_store_chunk(st + PL::tB, u / ncz, c0 + u % ncz, 128, make_uint4(0, 0, 0, 0));
+      }
+      named_bar(kBarProd, kProdThreads);  // wst ready
+      // (3) X and w X tiles: row (s*RP + q), column p
+      for (int u = ptid; u < L * 8; u += kProdThreads) {
+        const int j = u >> 3;
+        const int64_t t = t0 + j;
+        float xv[8];
+        if (t < a.T && pc * 8 < P) {
+          load8<TA>(rowbase + t * a.proj_stride + HP + h * P + pc * 8, xv);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) xv[e] = 0.f;
+        }
+        const float w = wst[j];
+#pragma unroll
+        for (int q = 0; q < RP; ++q) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = xv[e] * mx[e][q];
+          uint4 o1, o2;
+          o1.x = pack_bf16x2(v[0], v[1]);
+          o1.y = pack_bf16x2(v[2], v[3]);
+          o1.z = pack_bf16x2(v[4], v[5]);
+          o1.w = pack_bf16x2(v[6], v[7]);
+          o2.x = pack_bf16x2(v[0] * w, v[1] * w);
+          o2.y = pack_bf16x2(v[2] * w, v[3] * w);
+          o2.z = pack_bf16x2(v[4] * w, v[5] * w);
+          o2.w = pack_bf16x2(v[6] * w, v[7] * w);
+          sw128_store_chunk(st + PL::tX, j * RP + q, pc, 128, o1);
+          sw128_store_chunk(st + PL::tW, j * RP + q, pc, 128, o2);
+        }
+      }
+      fence_async_smem();
+      named_bar(kBarProd, kProdThreads);
+      if (ptid == 0) mbar_arrive(&bars[BAR_FULL0 + s]);
+    }
+  } else if (warp == kMmaWarp) {
+    // =============================== MMA issue ===============================
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idYi = idesc_bf16(128, kPP, false, true);
+      constexpr uint32_t idH = idesc_bf16(128, kPP, true, true);
+      constexpr uint32_t idY = idesc_bf16(128, kPP, false, true);
+      uint8_t* tileH = sm + PL::tileH;
+      for (int g = 0; g < G; ++g) {
+        const int s = g & 1;
+        uint8_t* st = sm + s * PL::kStage;
+        if (*abort_flag) break;
+        if (!mbar_wait(&bars[BAR_FULL0 + s], (g >> 1) & 1)) {
+          *abort_flag = 1;
+          record_error(a.err, M3B_ERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tbase + kColS, kmajor_desc(st + PL::tC, 128, kk * 16), kmajor_desc(st + PL::tB, 128, kk * 16),
+                    idS, kk > 0 ? 1u : 0u);
+        if (!mbar_wait(&bars[BAR_HREADY], g & 1)) {
+          *abort_flag = 1;
+          record_error(a.err, M3B_ERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t cyi = kColYi + 64 * (g & 1);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tbase + cyi, kmajor_desc(st + PL::tC, 128, kk * 16), mnmajor_desc(tileH, 128, kk * 16), idYi,
+                    kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tbase + kColH, mnmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(st + PL::tW, 128, kk * 16),
+                    idH, 1u);
+        umma_commit(&bars[BAR_SMMA]);
+        if (!mbar_wait(&bars[BAR_PREADY], g & 1)) {
+          *abort_flag = 1;
+          record_error(a.err, M3B_ERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t cy = kColY + 64 * (g & 1);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tbase + cy, kmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(st + PL::tX, 128, kk * 16), idY,
+                    kk > 0 ? 1u : 0u);
+        umma_commit(&bars[BAR_YMMA]);
+      }
+    }
+  } else if (warp < 4) {
+    // =============================== epilogue ===============================
+    const int m = tid;  // TMEM lane
+    const int t = m / RP, r = m % RP;
+    const uint32_t trow = tbase + ((uint32_t)(32 * warp) << 16);
+    uint8_t* tileH = sm + PL::tileH;
+    const bool lead = m == 0;
+    // H'_0 of the sequence starting at chunk gs -> bf16 tile row n = m, and H = d * H'_0 in TMEM
+    auto state_init = [&](int gs) -> bool {
+      int seq, b, h, k;
+      sc.at(gs, seq, b, h, k);
+      const int s2 = gs & 1;
+      if (!role_wait(&bars[BAR_FULL0 + s2], (gs >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))
+        return false;
+      const float* scal = reinterpret_cast<const float*>(sm + PL::scal + s2 * PL::scalStride);
+      const float d = exp2f(scal[L - 1]);
+      const float c0 = scal[3 * NA];  // (1-lam_0) dt_0
+      const int64_t base = ((int64_t)b * H + h) * (int64_t)P * N;
+      float hv[64];
+#pragma unroll
+      for (int pp = 0; pp < 64; ++pp) {
+        float v = 0.f;
+        if (m < N && pp < P) {
+          if (a.h_init) v = a.h_init[base + (int64_t)pp * N + m];
+          if (a.prev_bx_init) v = fmaf(c0, a.prev_bx_init[base + (int64_t)pp * N + m], v);
+        }
+        hv[pp] = v;
+      }
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        uint4 o;
+        o.x = pack_bf16x2(hv[8 * c8 + 0], hv[8 * c8 + 1]);
+        o.y = pack_bf16x2(hv[8 * c8 + 2], hv[8 * c8 + 3]);
+        o.z = pack_bf16x2(hv[8 * c8 + 4], hv[8 * c8 + 5]);
+        o.w = pack_bf16x2(hv[8 * c8 + 6], hv[8 * c8 + 7]);
+        sw128_store_chunk(tileH, m, c8, 128, o);
+      }
+      float v32[32];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v32[e] = d * hv[32 * hf + e];
+        tmem_st32(trow + kColH + 32 * hf, v32);
+      }
+      return true;
+    };
+    auto write_h_final = [&](int glast) {
+      if (!a.h_final) return;
+      int seq, b, h, k;
+      sc.at(glast, seq, b, h, k);
+      const int64_t base = ((int64_t)b * H + h) * (int64_t)P * N;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float v[32];
+        tmem_ld32(trow + kColH + 32 * hf, v);
+        if (m < N) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int pp = 32 * hf + e;
+            if (pp < P) a.h_final[base + (int64_t)pp * N + m] = v[e];
+          }
+        }
+      }
+    };
+    bool ok = G > 0 && state_init(0);
+    if (ok) {
+      fence_async_smem();
+      tc_fence_before();
+      named_bar(kBarEpi, kEpiThreads);
+      if (lead) mbar_arrive(&bars[BAR_HREADY]);
+    }
+    for (int g = 0; ok && g < G; ++g) {
+      const int s = g & 1;
+      int seq, b, h, k;
+      sc.at(g, seq, b, h, k);
+      uint8_t* st = sm + s * PL::kStage;
+      const float* scal = reinterpret_cast<const float*>(sm + PL::scal + s * PL::scalStride);
+      const float* cum2 = scal;
+      const float* gam = scal + 2 * NA;
+      const float* gbw = scal + 5 * NA;
+      if (!(ok = role_wait(&bars[BAR_SMMA], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
+      tc_fence_after();
+      // ---- mask: P[m, (s,q)] = S * exp(cum_t - cum_s) * (s<t ? gamma_s + (1-lam_{s+1})dt_{s+1} : gamma_s)
+      {
+        const float ct = cum2[t];
+#pragma unroll
+        for (int c32 = 0; c32 < 4; ++c32) {
+          float v[32];
+          tmem_ld32(trow + kColS + 32 * c32, v);
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += RP) {
+            const int sj = (32 * c32 + jj) / RP;
+            const float w = sj <= t ? exp2f(ct - cum2[sj]) * (sj < t ? gbw[sj] : gam[sj]) : 0.f;
+#pragma unroll
+            for (int q = 0; q < RP; ++q) v[jj + q] *= w;
+          }
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint4 o;
+            o.x = pack_bf16x2(v[8 * cc + 0], v[8 * cc + 1]);
+            o.y = pack_bf16x2(v[8 * cc + 2], v[8 * cc + 3]);
+            o.z = pack_bf16x2(v[8 * cc + 4], v[8 * cc + 5]);
+            o.w = pack_bf16x2(v[8 * cc + 6], v[8 * cc + 7]);
+            sw128_store_chunk(st + PL::tB, m, 4 * c32 + cc, 128, o);
+          }
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      named_bar(kBarEpi, kEpiThreads);
+      if (lead) mbar_arrive(&bars[BAR_PREADY]);
+      // ---- state for chunk g+1
+      if (g + 1 < G) {
+        int seq1, b1, h1, k1;
+        sc.at(g + 1, seq1, b1, h1, k1);
+        if (k1 == 0) {
+          write_h_final(g);
+          if (!(ok = state_init(g + 1))) break;
+        } else {
+          const int s1 = (g + 1) & 1;
+          if (!(ok = role_wait(&bars[BAR_FULL0 + s1], ((g + 1) >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag,
+                               a.err)))
+            break;
+          const float* scal1 = reinterpret_cast<const float*>(sm + PL::scal + s1 * PL::scalStride);
+          const float d = exp2f(scal1[L - 1]);
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            float v[32];
+            tmem_ld32(trow + kColH + 32 * hf, v);
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+              uint4 o;
+              o.x = pack_bf16x2(v[8 * c8 + 0], v[8 * c8 + 1]);
+              o.y = pack_bf16x2(v[8 * c8 + 2], v[8 * c8 + 3]);
+              o.z = pack_bf16x2(v[8 * c8 + 4], v[8 * c8 + 5]);
+              o.w = pack_bf16x2(v[8 * c8 + 6], v[8 * c8 + 7]);
+              sw128_store_chunk(tileH, m, 4 * hf + c8, 128, o);
+            }
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= d;
+            tmem_st32(trow + kColH + 32 * hf, v);
+          }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_bar(kBarEpi, kEpiThreads);
+        if (lead) mbar_arrive(&bars[BAR_HREADY]);
+      } else {
+        write_h_final(g);
+      }
+      // ---- output of chunk g
+      if (!(ok = role_wait(&bars[BAR_YMMA], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
+      tc_fence_after();
+      {
+        const int64_t tok = (int64_t)k * L + t;
+        const float ec = exp2f(cum2[t]);
+        const float Dh = ldf(p.D, h, p.param_dtype);
+        const TA* row = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride;
+        TA* yo = reinterpret_cast<TA*>(a.y) + ((int64_t)b * a.T + tok) * HP + (int64_t)h * P;
+        const uint32_t cy = kColY + 64 * (g & 1), cyi = kColYi + 64 * (g & 1);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float Y[32], Yi[32];
+          tmem_ld32(trow + cy + 32 * hf, Y);
+          tmem_ld32(trow + cyi + 32 * hf, Yi);
+          float acc[32];
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            const int p0 = 32 * hf + 8 * c8;
+            float xv[8], zv[8];
+            if (tok < a.T && p0 < P && r < R) {
+              load8<TA>(row + HP + h * P + p0, xv);
+              load8<TA>(row + h * P + p0, zv);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) xv[e] = zv[e] = 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int pp = p0 + e;
+              float o = 0.f;
+              if (pp < P && r < R) {
+                const int64_t q = ((int64_t)h * P + pp) * R + r;
+                const float xr = xv[e] * ldf(p.mimo_x, q, p.param_dtype);
+                const float zz = zv[e] * ldf(p.mimo_z, q, p.param_dtype);
+                o = (Y[8 * c8 + e] + ec * Yi[8 * c8 + e] + Dh * xr) * silu_f(zz) * ldf(p.mimo_down, q, p.param_dtype);
+              }
+              acc[8 * c8 + e] = o;
+            }
+          }
+#pragma unroll
+          for (int o = 1; o < RP; o <<= 1) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+          }
+          if (tok < a.T) {
+            constexpr int W = 32 / RP;
+#pragma unroll
+            for (int rr = 0; rr < RP; ++rr) {
+              if (rr != r) continue;
+#pragma unroll
+              for (int c8 = 0; c8 < W / 8; ++c8) {
+                const int p0 = 32 * hf + rr * W + c8 * 8;
+                if (p0 + 8 <= P) {
+                  float o8[8];
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) o8[e] = acc[rr * W + c8 * 8 + e];
+                  store8<TA>(yo + p0, o8);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e)
+                    if (p0 + e < P) io<TA>::st(yo + p0 + e, acc[rr * W + c8 * 8 + e]);
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars[BAR_EMPTY0 + s]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+int ensure_smem_f(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({kernel, dev})) return M3B_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  done.insert({kernel, dev});
+  return M3B_OK;
+}
+
+template <typename TA, int R>
+int launch_fused_t(const FusedParams& fp, cudaStream_t st) {
+  constexpr int RP = rp_of(R);
+  using PL = FPlan<RP>;
+  const int nseq_total = (int)(fp.B * fp.prm.H);
+  const int nsm = num_sms();
+  const int grid = nseq_total < nsm ? nseq_total : nsm;
+  int rc;
+  if ((rc = ensure_smem_f((const void*)ssd_fused_kernel<TA, R>, PL::bytes)) != M3B_OK) return rc;
+  const Sched sc{fp.K, fp.prm.H, nseq_total, grid};
+  ssd_fused_kernel<TA, R><<<grid, kFusedThreads, PL::bytes, st>>>(fp, sc);
+  return check_launch("ssd_fused");
+}
+}  // namespace
+
+bool fused_supported(const m3b_layer_params& p) {
+  const int nh2 = p.N / 2;
+  return p.N <= kNS && p.P <= kPP && (nh2 & (nh2 - 1)) == 0 && nh2 >= 1 && (p.R == 1 || p.R == 2 || p.R == 4);
+}
+
+int launch_fused(const FusedParams& fp, cudaStream_t st, bool bf16) {
+  switch (fp.prm.R) {
+    case 1: return bf16 ? launch_fused_t<__nv_bfloat16, 1>(fp, st) : launch_fused_t<float, 1>(fp, st);
+    case 2: return bf16 ? launch_fused_t<__nv_bfloat16, 2>(fp, st) : launch_fused_t<float, 2>(fp, st);
+    case 4: return bf16 ? launch_fused_t<__nv_bfloat16, 4>(fp, st) : launch_fused_t<float, 4>(fp, st);
+    default: return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: mimo_rank %d", fp.prm.R);
+  }
+}
+
+}  // namespace m3b

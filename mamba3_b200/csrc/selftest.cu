@@ -9,13 +9,14 @@ namespace m3b {
 
 // D[m][n] = sum_k A[m][k] * B[n][k];  A (128 x 128), B (64 x 128), row-major bf16 in global memory.
 // mode 0: A staged K-major (tile row = m).  mode 1: A staged as A^T (tile row = k) and read MN-major.
+// mode 2: A K-major, B staged as B^T (tile row = k, 64 columns n) and read MN-major.
 __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(const __nv_bfloat16* __restrict__ A,
                                                                const __nv_bfloat16* __restrict__ B,
                                                                float* __restrict__ D, int mode, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tA = sm;              // 32 KB
-  uint8_t* tB = sm + 32768;      // 16 KB
+  uint8_t* tB = sm + 32768;      // 16 KB (64 rows x 128, or 128 rows x 64 in mode 2)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 49152);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 49152 + 16);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -30,7 +31,7 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(const __nv_bfloat
   for (int u = threadIdx.x; u < 128 * 16; u += blockDim.x) {
     const int row = u / 16, c = u % 16;
     uint4 v;
-    if (mode == 0) {
+    if (mode != 1) {
       v = *reinterpret_cast<const uint4*>(A + row * 128 + c * 8);
     } else {  // tile row = k, columns = m
       uint32_t w[4];
@@ -44,9 +45,23 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(const __nv_bfloat
     }
     sw128_store_chunk(tA, row, c, 128, v);
   }
-  for (int u = threadIdx.x; u < 64 * 16; u += blockDim.x) {
-    const int row = u / 16, c = u % 16;
-    sw128_store_chunk(tB, row, c, 64, *reinterpret_cast<const uint4*>(B + row * 128 + c * 8));
+  if (mode != 2) {
+    for (int u = threadIdx.x; u < 64 * 16; u += blockDim.x) {
+      const int row = u / 16, c = u % 16;
+      sw128_store_chunk(tB, row, c, 64, *reinterpret_cast<const uint4*>(B + row * 128 + c * 8));
+    }
+  } else {  // tile row = k (128 rows), 8 chunks of 8 n
+    for (int u = threadIdx.x; u < 128 * 8; u += blockDim.x) {
+      const int row = u / 8, c = u % 8;
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat16 lo = B[(c * 8 + 2 * e) * 128 + row];
+        const __nv_bfloat16 hi = B[(c * 8 + 2 * e + 1) * 128 + row];
+        w[e] = (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+      }
+      sw128_store_chunk(tB, row, c, 128, make_uint4(w[0], w[1], w[2], w[3]));
+    }
   }
   fence_async_smem();
   tc_fence_before();
@@ -54,10 +69,11 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(const __nv_bfloat
   tc_fence_after();
   const uint32_t tbase = *tslot;
   if (threadIdx.x == 0) {
-    const uint32_t idesc = idesc_bf16(128, 64, mode == 1, false);
+    const uint32_t idesc = idesc_bf16(128, 64, mode == 1, mode == 2);
     for (int kk = 0; kk < 8; ++kk) {
-      const uint64_t ad = mode == 0 ? kmajor_desc(tA, 128, kk * 16) : mnmajor_desc(tA, 128, kk * 16);
-      umma_bf16(tbase, ad, kmajor_desc(tB, 64, kk * 16), idesc, kk > 0 ? 1u : 0u);
+      const uint64_t ad = mode == 1 ? mnmajor_desc(tA, 128, kk * 16) : kmajor_desc(tA, 128, kk * 16);
+      const uint64_t bd = mode == 2 ? mnmajor_desc(tB, 128, kk * 16) : kmajor_desc(tB, 64, kk * 16);
+      umma_bf16(tbase, ad, bd, idesc, kk > 0 ? 1u : 0u);
     }
     umma_commit(bar);
   }
@@ -87,7 +103,7 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(const __nv_bfloat
 }  // namespace m3b
 
 extern "C" int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream) {
-  if (!A || !B || !D || (mode != 0 && mode != 1)) return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_umma: bad args");
+  if (!A || !B || !D || mode < 0 || mode > 2) return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_umma: bad args");
   if (!m3b::aligned16(A) || !m3b::aligned16(B)) return m3b::fail(M3B_ERR_ALIGNMENT, "selftest_umma: alignment");
   const int bytes = 49152 + 64 + 1024;
   cudaError_t e = cudaFuncSetAttribute(m3b::umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

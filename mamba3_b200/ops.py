@@ -14,6 +14,16 @@ import torch
 from . import _lib
 from .profiling import current_stage_events
 
+# Which layer-forward algorithm m3b_layer_fwd runs: 0 automatic, 1 fused sequential,
+# 2 chunk-parallel.  Both compute the same result; tests and benches pin one.
+_LAYER_ALGO = 0
+
+
+def set_layer_algo(algo: int) -> int:
+    global _LAYER_ALGO
+    prev, _LAYER_ALGO = _LAYER_ALGO, int(algo)
+    return prev
+
 
 def _prm(H, P, N, R, G, trap, cplx, eps, A_log, D, dt_bias, Bw, Cw, Bb, Cb, mx, mz, md):
     return _lib.layer_params(H, P, N, R, G, trap, cplx, eps, A_log, D, dt_bias, Bw, Cw, Bb, Cb, mx, mz, md)
@@ -65,7 +75,7 @@ def layer_ssd(proj: torch.Tensor, A_log: torch.Tensor, D: torch.Tensor, dt_bias:
     f = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
     _lib.layer_fwd(prm, proj, y, dt_scale=ds, h_init=f(h_init), angle_init=f(angle_init),
                    prev_bx_init=f(prev_bx_init), h_final=h_final, angle_final=angle, prev_bx_final=prev_bx,
-                   stage_events=current_stage_events())
+                   stage_events=current_stage_events(), algo=_LAYER_ALGO)
     if not return_state:
         e = torch.empty(0, **f32)
         return y, e, e.clone(), e.clone()

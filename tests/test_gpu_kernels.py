@@ -15,7 +15,7 @@ from helpers import ours_layer_from_golden, to_np
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 def test_umma_selftest(mode):
     from mamba3_b200 import _lib
 

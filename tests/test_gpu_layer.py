@@ -22,6 +22,16 @@ pytestmark = pytest.mark.gpu
 BF16_TOL = 2e-2
 
 
+@pytest.fixture(params=[1, 2], ids=["fused", "chunked"], autouse=True)
+def layer_algo(request):
+    """Run every layer test on both layer-forward algorithms."""
+    from mamba3_b200 import ops
+
+    prev = ops.set_layer_algo(request.param)
+    yield request.param
+    ops.set_layer_algo(prev)
+
+
 @pytest.mark.parametrize("case", LAYER_CASES)
 def test_forward_prefill_golden_fp32(case):
     d = load(f"layer_{case}")
