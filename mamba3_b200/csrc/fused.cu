@@ -122,7 +122,7 @@ __device__ __forceinline__ void load_pair_block(const TA* p, float (&v)[2 * R]) 
 }
 
 template <typename TA, int R>
-__global__ void __maxnreg__(152) ssd_fused_kernel(FusedParams a, Sched sc) {
+__global__ void __maxnreg__(144) ssd_fused_kernel(FusedParams a, Sched sc) {
   constexpr int RP = rp_of(R);
   using PL = FPlan<RP>;
   constexpr int L = PL::L;
@@ -701,6 +701,11 @@ int launch_fused_t(const FusedParams& fp, cudaStream_t st) {
   const int grid = nseq_total < nsm ? nseq_total : nsm;
   int rc;
   if ((rc = ensure_smem_f((const void*)ssd_fused_kernel<TA, R>, PL::bytes)) != M3B_OK) return rc;
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, (const void*)ssd_fused_kernel<TA, R>) == cudaSuccess &&
+      fa.maxThreadsPerBlock < kFusedThreads)
+    return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: %d registers/thread allow only %d threads per block (need %d)",
+                fa.numRegs, fa.maxThreadsPerBlock, kFusedThreads);
   const Sched sc{fp.K, fp.prm.H, nseq_total, grid};
   ssd_fused_kernel<TA, R><<<grid, kFusedThreads, PL::bytes, st>>>(fp, sc);
   return check_launch("ssd_fused");
