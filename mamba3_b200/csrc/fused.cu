@@ -42,7 +42,9 @@ struct FPlan {
   static constexpr int scal = tileH + 16384;
   static constexpr int omega = scal + 2 * scalStride;                // 2 x 64 doubles (by chunk parity)
   static constexpr int segt = omega + 128 * 8;                       // 256 floats
-  static constexpr int bars = segt + 256 * 4;                        // 8 mbarriers
+  static constexpr int nrm = segt + 256 * 4;                         // B/C norm weight, bias: 4 x N*R fp32
+  static constexpr int mxs = nrm + 4 * kNS * RP * 4;                 // mimo_x: kPP x RP fp32
+  static constexpr int bars = mxs + kPP * RP * 4;                    // 8 mbarriers
   static constexpr int misc = bars + 64;                             // taddr, abort
   static constexpr int bytes = misc + 16 + 1024;
   static_assert(bytes <= 227 * 1024, "fused CTA shared memory exceeds 227 KB");
@@ -122,7 +124,7 @@ __device__ __forceinline__ void load_pair_block(const TA* p, float (&v)[2 * R]) 
 }
 
 template <typename TA, int R>
-__global__ void __maxnreg__(144) ssd_fused_kernel(FusedParams a, Sched sc) {
+__global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams a, Sched sc) {
   constexpr int RP = rp_of(R);
   using PL = FPlan<RP>;
   constexpr int L = PL::L;
@@ -179,8 +181,11 @@ __global__ void __maxnreg__(144) ssd_fused_kernel(FusedParams a, Sched sc) {
     const bool bc_act = ptid < nh2 * nseg;
     const int pi = ptid % nh2, seg = ptid / nh2;
     const int pc = ptid & 7;  // x-tile p-chunk
-    float wB[2][R], bB[2][R], wC[2][R], bC[2][R];
-    float mx[8][RP];
+    float* nwB = reinterpret_cast<float*>(sm + PL::nrm);
+    float* nwC = nwB + kNS * RP;
+    float* nbB = nwC + kNS * RP;
+    float* nbC = nbB + kNS * RP;
+    float* mxs = reinterpret_cast<float*>(sm + PL::mxs);
     for (int g = 0; g < G; ++g) {
       const int s = g & 1;
       int seq, b, h, k;
@@ -188,26 +193,18 @@ __global__ void __maxnreg__(144) ssd_fused_kernel(FusedParams a, Sched sc) {
       const int grp = h / (H / p.G);
       const int64_t t0 = (int64_t)k * L;
       const TA* rowbase = proj + (int64_t)b * a.T * a.proj_stride;
-      if (k == 0) {
+      if (k == 0) {  // per-sequence parameters (every producer passed the last barrier of chunk g-1)
         const int pd = p.param_dtype;
-#pragma unroll
-        for (int e = 0; e < 2; ++e)
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            const int idx = (2 * pi + e) * R + r;
-            const bool okn = bc_act && (2 * pi + e) < N;
-            wB[e][r] = okn ? ldf(p.B_norm_w, idx, pd) : 0.f;
-            wC[e][r] = okn ? ldf(p.C_norm_w, idx, pd) : 0.f;
-            bB[e][r] = okn ? ldf(p.B_bias, (int64_t)grp * NR + idx, pd) : 0.f;
-            bC[e][r] = okn ? ldf(p.C_bias, (int64_t)grp * NR + idx, pd) : 0.f;
-          }
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-#pragma unroll
-          for (int q = 0; q < RP; ++q) {
-            const int pp = pc * 8 + e;
-            mx[e][q] = (pp < P && q < R) ? ldf(p.mimo_x, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
-          }
+        for (int e = ptid; e < NR; e += kProdThreads) {
+          nwB[e] = ldf(p.B_norm_w, e, pd);
+          nwC[e] = ldf(p.C_norm_w, e, pd);
+          nbB[e] = ldf(p.B_bias, (int64_t)grp * NR + e, pd);
+          nbC[e] = ldf(p.C_bias, (int64_t)grp * NR + e, pd);
+        }
+        for (int e = ptid; e < kPP * RP; e += kProdThreads) {
+          const int pp = e / RP, q = e % RP;
+          mxs[e] = (pp < P && q < R) ? ldf(p.mimo_x, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
+        }
         if (ptid < nh2)
           omega[(g & 1) * 64 + ptid] = a.angle_init ? (double)a.angle_init[((int64_t)b * H + h) * nh2 + ptid] : 0.0;
       }
@@ -332,10 +329,11 @@ __global__ void __maxnreg__(144) ssd_fused_kernel(FusedParams a, Sched sc) {
             for (int r = 0; r < RP; ++r) {
               uint32_t ob = 0, oc = 0;
               if (r < R && valid) {
-                const float b0 = fmaf(vb[u][r] * rb, wB[0][r], bB[0][r]);
-                const float b1 = fmaf(vb[u][R + r] * rb, wB[1][r], bB[1][r]);
-                const float c0 = fmaf(vc[u][r] * rc, wC[0][r], bC[0][r]);
-                const float c1 = fmaf(vc[u][R + r] * rc, wC[1][r], bC[1][r]);
+                const int i0 = 2 * pi * R + r, i1 = i0 + R;  // flat (n, r) index of n = 2i, 2i+1
+                const float b0 = fmaf(vb[u][r] * rb, nwB[i0], nbB[i0]);
+                const float b1 = fmaf(vb[u][R + r] * rb, nwB[i1], nbB[i1]);
+                const float c0 = fmaf(vc[u][r] * rc, nwC[i0], nbC[i0]);
+                const float c1 = fmaf(vc[u][R + r] * rc, nwC[i1], nbC[i1]);
                 ob = pack_bf16x2(b0 * cs - b1 * sn, b0 * sn + b1 * cs);
                 oc = pack_bf16x2(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
               }
@@ -375,7 +373,7 @@ __global__ void __maxnreg__(144) ssd_fused_kernel(FusedParams a, Sched sc) {
         for (int q = 0; q < RP; ++q) {
           float v[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = xv[e] * mx[e][q];
+          for (int e = 0; e < 8; ++e) v[e] = xv[e] * mxs[(pc * 8 + e) * RP + q];
           uint4 o1, o2;
           o1.x = pack_bf16x2(v[0], v[1]);
           o1.y = pack_bf16x2(v[2], v[3]);
