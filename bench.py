@@ -38,6 +38,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample-tokens", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None, help="override config-1 batch (profiling captures)")
+    ap.add_argument("--seqlen", type=int, default=None, help="override config-1 seqlen (profiling captures)")
+    ap.add_argument("--algo", type=int, default=0, help="layer algorithm: 0 auto, 1 fused, 2 chunk-parallel")
     return ap.parse_args()
 
 
@@ -145,8 +148,15 @@ def run_ours(args):
     from mamba3_b200 import KulaMamba, _lib
     from mamba3_b200.profiling import ClockSampler, stage_events
 
-    c = CFG1
+    c = dict(CFG1)
+    if args.batch:
+        c["batch"] = args.batch
+    if args.seqlen:
+        c["seqlen"] = args.seqlen
     B, T = c["batch"], c["seqlen"]
+    from mamba3_b200 import ops as _ops
+
+    _ops.set_layer_algo(args.algo)
     torch.manual_seed(0)
     layer = KulaMamba(d_model=c["d_model"], d_state=c["d_state"], headdim=c["headdim"], mimo_rank=c["mimo_rank"],
                       chunk_size=c["chunk_size"]).to(dev, torch.bfloat16).eval()

@@ -77,10 +77,12 @@ def test_noalloc_rejects_problem_larger_than_scratch():
 
     m = _layer()
     L = _lib.lib()
-    # 16 x 4096 tokens needs far more than the static scratch; refused on the host, nothing launched
+    # the chunk-parallel algorithm keeps every chunk state in scratch: 16 x 4096 tokens need far
+    # more than the static array; refused on the host, nothing launched
     proj = torch.empty(16, 4096, m.in_proj.out_features, dtype=torch.bfloat16, device="cuda")
     out = _outputs(proj, m.nheads, m.headdim, m.d_state)
     a = _args(m, proj, *out)
+    a.algo = 2
     assert L.m3b_layer_fwd_workspace(C.byref(a)) > (32 << 20)
     rc = L.m3b_layer_fwd_noalloc(C.byref(a), C.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 6  # M3B_ERR_WORKSPACE
