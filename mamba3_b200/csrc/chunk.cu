@@ -187,6 +187,7 @@ __global__ void __launch_bounds__(kCT, 1) chunk_state_kernel(FwdParams a) {
     umma_commit(&bar[0]);
   }
   bool ok = mbar_wait(&bar[0], 0);
+  __syncwarp();
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
     umma_commit(&bar[0]);
   }
   bool ok = mbar_wait(&bar[0], 0);
+  __syncwarp();
   ok = __syncthreads_and(ok);
   tc_fence_after();
   const int lq = warp & 3, half = warp >> 2;
@@ -337,6 +339,7 @@ __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
   if (ok) {
     ok = mbar_wait(&bar[1], 0);
   }
+  __syncwarp();
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {

@@ -44,7 +44,8 @@ struct FPlan {
   static constexpr int segt = omega + 128 * 8;                       // 256 floats
   static constexpr int nrm = segt + 256 * 4;                         // B/C norm weight, bias: 4 x N*R fp32
   static constexpr int mxs = nrm + 4 * kNS * RP * 4;                 // mimo_x: kPP x RP fp32
-  static constexpr int bars = mxs + kPP * RP * 4;                    // 8 mbarriers
+  static constexpr int epar = mxs + kPP * RP * 4;                    // mimo_z, mimo_down (epilogue)
+  static constexpr int bars = epar + 2 * kPP * RP * 4;               // 8 mbarriers
   static constexpr int misc = bars + 64;                             // taddr, abort
   static constexpr int bytes = misc + 16 + 1024;
   static_assert(bytes <= 227 * 1024, "fused CTA shared memory exceeds 227 KB");
@@ -77,51 +78,77 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, bool l
       record_error(err, M3B_ERR_TIMEOUT);
     }
   }
+  __syncwarp();  // the leader's lanes reconverge before the aligned barrier
   named_bar(bar_id, nthreads);
   return *abort_flag == 0;
 }
 
-// 2R consecutive activations (the (2i, 2i+1) x R block of a B or C row) as floats.
+// 2R consecutive activations (the (2i, 2i+1) x R block of a B or C row), kept packed in
+// registers between the load and its use so a whole batch of loads can be in flight.
 template <typename TA, int R>
-__device__ __forceinline__ void load_pair_block(const TA* p, float (&v)[2 * R]) {
-  if constexpr (sizeof(TA) == 2) {
-    if constexpr (R == 1) {
-      const uint32_t u = __ldg(reinterpret_cast<const unsigned int*>(p));
-      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
-      v[0] = f.x;
-      v[1] = f.y;
-    } else if constexpr (R == 2) {
-      const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float2 f = __bfloat1622float2(hh[e]);
-        v[2 * e] = f.x;
-        v[2 * e + 1] = f.y;
-      }
-    } else if constexpr (R == 4) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(hh[e]);
-        v[2 * e] = f.x;
-        v[2 * e + 1] = f.y;
-      }
+struct PairRaw {
+  static constexpr int W = sizeof(TA) == 2 ? R : 2 * R;  // 32-bit words
+  uint32_t w[W];
+  __device__ __forceinline__ void load(const TA* p) {
+    if constexpr (W == 1) {
+      w[0] = __ldg(reinterpret_cast<const unsigned int*>(p));
+    } else if constexpr (W == 2) {
+      const uint2 t = __ldg(reinterpret_cast<const uint2*>(p));
+      w[0] = t.x;
+      w[1] = t.y;
     } else {
 #pragma unroll
-      for (int e = 0; e < R; ++e) {
-        const uint32_t u = __ldg(reinterpret_cast<const unsigned int*>(p) + e);
-        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
-        v[2 * e] = f.x;
-        v[2 * e + 1] = f.y;
+      for (int i = 0; i < W / 4; ++i) {
+        const uint4 t = __ldg(reinterpret_cast<const uint4*>(p) + i);
+        w[4 * i] = t.x;
+        w[4 * i + 1] = t.y;
+        w[4 * i + 2] = t.z;
+        w[4 * i + 3] = t.w;
       }
     }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 2 * R; ++e) v[e] = __ldg(reinterpret_cast<const float*>(p) + e);
   }
-}
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < W; ++i) w[i] = 0u;
+  }
+  __device__ __forceinline__ float get(int e) const {  // element e of the 2R
+    if constexpr (sizeof(TA) == 2) {
+      const uint32_t x = w[e >> 1];
+      return __uint_as_float((e & 1) ? (x & 0xffff0000u) : (x << 16));
+    } else {
+      return __uint_as_float(w[e]);
+    }
+  }
+};
+
+// 8 consecutive activations, packed (16 B for 16-bit types, 32 B for fp32).
+template <typename TA>
+struct Raw8 {
+  static constexpr int W = sizeof(TA) == 2 ? 4 : 8;
+  uint32_t w[W];
+  __device__ __forceinline__ void load(const TA* p) {
+#pragma unroll
+    for (int i = 0; i < W / 4; ++i) {
+      const uint4 t = __ldg(reinterpret_cast<const uint4*>(p) + i);
+      w[4 * i] = t.x;
+      w[4 * i + 1] = t.y;
+      w[4 * i + 2] = t.z;
+      w[4 * i + 3] = t.w;
+    }
+  }
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < W; ++i) w[i] = 0u;
+  }
+  __device__ __forceinline__ float get(int e) const {
+    if constexpr (sizeof(TA) == 2) {
+      const uint32_t x = w[e >> 1];
+      return __uint_as_float((e & 1) ? (x & 0xffff0000u) : (x << 16));
+    } else {
+      return __uint_as_float(w[e]);
+    }
+  }
+};
 
 template <typename TA, int R>
 __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams a, Sched sc) {
@@ -129,6 +156,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
   using PL = FPlan<RP>;
   constexpr int L = PL::L;
   constexpr int NA = PL::NA;
+  constexpr int SEGMAX = L / 4;          // longest token segment of one producer thread (N/2 <= 64)
+  constexpr int TB = R >= 4 ? 8 : 16;    // tokens per B/C load batch
+  constexpr int XU = L / 32;             // x-tile units per producer thread (L * 8 / 256)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const m3b_layer_params& p = a.prm;
@@ -157,8 +187,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
     *abort_flag = 0;
     fence_mbar_init();
   }
-  // columns n >= N of the operand tiles stay zero for the whole kernel (only tileC keeps them;
-  // tileB is rewritten by P each chunk, so producers zero them per chunk when N < 128)
+  // the operand tiles start zeroed: columns n >= N of tileC stay zero for the whole kernel
+  // (tileB is rewritten by P every chunk, so the producers zero those columns per chunk)
   for (int e = tid; e < (2 * PL::kStage + 16384) / 16; e += kFusedThreads)
     reinterpret_cast<uint4*>(sm)[e] = make_uint4(0, 0, 0, 0);
   tc_fence_before();
@@ -177,7 +207,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
     const int nh2 = N / 2;
     int nseg = 1;
     while (nseg * 2 * nh2 <= kProdThreads && nseg * 2 <= L) nseg *= 2;
-    const int seglen = L / nseg;
+    const int seglen = L / nseg;  // <= SEGMAX
     const bool bc_act = ptid < nh2 * nseg;
     const int pi = ptid % nh2, seg = ptid / nh2;
     const int pc = ptid & 7;  // x-tile p-chunk
@@ -221,25 +251,47 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       float* gbw = scal + 5 * NA;
       float* rmsB = scal + 6 * NA;
       float* rmsC = scal + 7 * NA;
+      // (0) every load that does not depend on this chunk's scalars, issued together
+      Raw8<TA> xr[XU];
+#pragma unroll
+      for (int jj = 0; jj < XU; ++jj) {
+        const int j = (ptid + kProdThreads * jj) >> 3;
+        const int64_t t = t0 + j;
+        if (t < a.T && pc * 8 < P) xr[jj].load(rowbase + t * a.proj_stride + HP + h * P + pc * 8);
+        else xr[jj].zero();
+      }
+      const TA* thp = rowbase + offTh + pi;
+      float th[SEGMAX];
+#pragma unroll
+      for (int jj = 0; jj < SEGMAX; ++jj) {
+        const int64_t t = t0 + seg * seglen + jj;
+        th[jj] = (bc_act && p.complex_ssm && jj < seglen && t < a.T) ? io<TA>::ld(thp + t * a.proj_stride) : 0.f;
+      }
+      float dt_raw = 0.f, lam_raw = 0.f, rb = 0.f, rc = 0.f;
+      const bool tok_act = ptid <= L && t0 + ptid < a.T;
+      if (tok_act) {
+        const TA* row = rowbase + (t0 + ptid) * a.proj_stride;
+        dt_raw = io<TA>::ld(row + offDt + h);
+        if (p.trapezoidal) lam_raw = io<TA>::ld(row + offLam + h);
+        if (ptid < L) {
+          const float* rr = a.rms + (((int64_t)b * a.T + t0 + ptid) * p.G + grp) * 2;
+          rb = rr[0];
+          rc = rr[1];
+        }
+      }
       // (1) token scalars (token L is the next chunk's first token)
       if (ptid <= L) {
-        const int64_t t = t0 + ptid;
-        float dt = 0.f, gmm = 0.f, bp = 0.f, rb = 0.f, rc = 0.f;
-        if (t < a.T) {
-          const TA* row = rowbase + t * a.proj_stride;
-          dt = softplus_f(io<TA>::ld(row + offDt + h) + ldf(p.dt_bias, h, p.param_dtype));
-          if (a.dt_scale) dt *= io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + ((int64_t)b * a.T + t) * H + h);
+        float dt = 0.f, gmm = 0.f, bp = 0.f;
+        if (tok_act) {
+          dt = softplus_f(dt_raw + ldf(p.dt_bias, h, p.param_dtype));
+          if (a.dt_scale)
+            dt *= io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + ((int64_t)b * a.T + t0 + ptid) * H + h);
           if (p.trapezoidal) {
-            const float lam = sigmoid_f(io<TA>::ld(row + offLam + h));
+            const float lam = sigmoid_f(lam_raw);
             gmm = lam * dt;
             bp = (1.f - lam) * dt;
           } else {
             gmm = dt;
-          }
-          if (ptid < L) {
-            const float* rr = a.rms + (((int64_t)b * a.T + t) * p.G + grp) * 2;
-            rb = rr[0];
-            rc = rr[1];
           }
         }
         dtv[ptid] = dt;
@@ -271,69 +323,75 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
 #pragma unroll
         for (int e = 0; e < PER; ++e) cum2[ptid * PER + e] = (v[e] + excl) * kLog2e;
       }
+      // (2a) sum of dt * theta over my segment (dtv is visible: barrier above)
+      float segsum = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < SEGMAX; ++jj)
+        if (jj < seglen) segsum = fmaf(dtv[seg * seglen + jj], th[jj], segsum);
+      if (bc_act) segt[seg * nh2 + pi] = segsum;
       named_bar(kBarProd, kProdThreads);
       if (ptid < L) {
         const float gw = gam[ptid] + bpr[ptid + 1];
         gbw[ptid] = gw;
         wst[ptid] = exp2f(cum2[L - 1] - cum2[ptid]) * gw;
       }
-      // (2) angles and the rotated, normalised B^ / C^ rows (pair i of tokens [seg*seglen, +seglen))
-      const TA* thp = rowbase + offTh + pi;
-      float segsum = 0.f;
-      if (bc_act && p.complex_ssm) {
-        for (int j = seg * seglen; j < (seg + 1) * seglen; ++j) {
-          const int64_t t = t0 + j;
-          segsum = fmaf(dtv[j], t < a.T ? io<TA>::ld(thp + t * a.proj_stride) : 0.f, segsum);
-        }
-        segt[seg * nh2 + pi] = segsum;
-      }
-      named_bar(kBarProd, kProdThreads);
+      // (2b) rotated, normalised B^ / C^ entries of pair i for the tokens of my segment
       if (bc_act) {
         float off = 0.f;
-        if (p.complex_ssm) {
-          for (int q = 0; q < seg; ++q) off += segt[q * nh2 + pi];
-        }
+        for (int q = 0; q < seg; ++q) off += segt[q * nh2 + pi];
         const double om = omega[(g & 1) * 64 + pi];
         float run = off;
         const TA* pB = rowbase + offB + grp * NR + 2 * pi * R;
         const TA* pC = rowbase + offC + grp * NR + 2 * pi * R;
-        constexpr int TB = R >= 4 ? 2 : 4;  // tokens per load batch
-        for (int j0 = seg * seglen; j0 < (seg + 1) * seglen; j0 += TB) {
-          float vb[TB][2 * R], vc[TB][2 * R], th[TB];
+        float wb0[RP], wb1[RP], bb0[RP], bb1[RP], wc0[RP], wc1[RP], bc0[RP], bc1[RP];
+#pragma unroll
+        for (int r = 0; r < RP; ++r) {
+          const int i0 = 2 * pi * R + (r < R ? r : 0), i1 = i0 + R;  // flat (n, r) of n = 2i, 2i+1
+          wb0[r] = nwB[i0];
+          wb1[r] = nwB[i1];
+          bb0[r] = nbB[i0];
+          bb1[r] = nbB[i1];
+          wc0[r] = nwC[i0];
+          wc1[r] = nwC[i1];
+          bc0[r] = nbC[i0];
+          bc1[r] = nbC[i1];
+        }
+#pragma unroll
+        for (int j0 = 0; j0 < SEGMAX; j0 += TB) {
+          if (j0 >= seglen) break;
+          PairRaw<TA, R> vb[TB], vc[TB];
 #pragma unroll
           for (int u = 0; u < TB; ++u) {
-            const int j = j0 + u;
-            const int64_t t = t0 + j;
-            if (j < (seg + 1) * seglen && t < a.T) {
-              load_pair_block<TA, R>(pB + t * a.proj_stride, vb[u]);
-              load_pair_block<TA, R>(pC + t * a.proj_stride, vc[u]);
-              th[u] = p.complex_ssm ? io<TA>::ld(thp + t * a.proj_stride) : 0.f;
+            const int jj = j0 + u;
+            const int64_t t = t0 + seg * seglen + jj;
+            if (jj < seglen && t < a.T) {
+              vb[u].load(pB + t * a.proj_stride);
+              vc[u].load(pC + t * a.proj_stride);
             } else {
-#pragma unroll
-              for (int e = 0; e < 2 * R; ++e) vb[u][e] = vc[u][e] = 0.f;
-              th[u] = 0.f;
+              vb[u].zero();
+              vc[u].zero();
             }
           }
 #pragma unroll
           for (int u = 0; u < TB; ++u) {
-            const int j = j0 + u;
-            if (j >= (seg + 1) * seglen) break;
+            const int jj = j0 + u;
+            if (jj >= seglen) break;
+            const int j = seg * seglen + jj;
             const bool valid = t0 + j < a.T;
             float cs = 1.f, sn = 0.f;
             if (p.complex_ssm) {
-              run = fmaf(dtv[j], th[u], run);
+              run = fmaf(dtv[j], th[jj], run);
               sincos_reduced((float)(om - (double)run), &sn, &cs);
             }
-            const float rb = rmsB[j], rc = rmsC[j];
+            const float rbj = rmsB[j], rcj = rmsC[j];
 #pragma unroll
             for (int r = 0; r < RP; ++r) {
               uint32_t ob = 0, oc = 0;
               if (r < R && valid) {
-                const int i0 = 2 * pi * R + r, i1 = i0 + R;  // flat (n, r) index of n = 2i, 2i+1
-                const float b0 = fmaf(vb[u][r] * rb, nwB[i0], nbB[i0]);
-                const float b1 = fmaf(vb[u][R + r] * rb, nwB[i1], nbB[i1]);
-                const float c0 = fmaf(vc[u][r] * rc, nwC[i0], nbC[i0]);
-                const float c1 = fmaf(vc[u][R + r] * rc, nwC[i1], nbC[i1]);
+                const float b0 = fmaf(vb[u].get(r) * rbj, wb0[r], bb0[r]);
+                const float b1 = fmaf(vb[u].get(R + r) * rbj, wb1[r], bb1[r]);
+                const float c0 = fmaf(vc[u].get(r) * rcj, wc0[r], bc0[r]);
+                const float c1 = fmaf(vc[u].get(R + r) * rcj, wc1[r], bc1[r]);
                 ob = pack_bf16x2(b0 * cs - b1 * sn, b0 * sn + b1 * cs);
                 oc = pack_bf16x2(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
               }
@@ -357,23 +415,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           sw128_store_chunk(st + PL::tB, u / ncz, c0 + u % ncz, 128, make_uint4(0, 0, 0, 0));
       }
       named_bar(kBarProd, kProdThreads);  // wst ready
-      // (3) X and w X tiles: row (s*RP + q), column p
-      for (int u = ptid; u < L * 8; u += kProdThreads) {
-        const int j = u >> 3;
-        const int64_t t = t0 + j;
-        float xv[8];
-        if (t < a.T && pc * 8 < P) {
-          load8<TA>(rowbase + t * a.proj_stride + HP + h * P + pc * 8, xv);
-        } else {
+      // (3) X and w X tiles from the prefetched x rows: row (s*RP + q), column p
 #pragma unroll
-          for (int e = 0; e < 8; ++e) xv[e] = 0.f;
-        }
+      for (int jj = 0; jj < XU; ++jj) {
+        const int j = (ptid + kProdThreads * jj) >> 3;
         const float w = wst[j];
 #pragma unroll
         for (int q = 0; q < RP; ++q) {
           float v[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = xv[e] * mxs[(pc * 8 + e) * RP + q];
+          for (int e = 0; e < 8; ++e) v[e] = xr[jj].get(e) * mxs[(pc * 8 + e) * RP + q];
           uint4 o1, o2;
           o1.x = pack_bf16x2(v[0], v[1]);
           o1.y = pack_bf16x2(v[2], v[3]);
@@ -443,12 +494,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         umma_commit(&bars[BAR_YMMA]);
       }
     }
+    __syncwarp();  // reconverge before the CTA-wide barrier below
   } else if (warp < 4) {
     // =============================== epilogue ===============================
-    const int m = tid;  // TMEM lane
+    const int m = tid;  // TMEM lane = tile row (t, r)
     const int t = m / RP, r = m % RP;
     const uint32_t trow = tbase + ((uint32_t)(32 * warp) << 16);
     uint8_t* tileH = sm + PL::tileH;
+    float* emz = reinterpret_cast<float*>(sm + PL::epar);  // mimo_z, mimo_down of the current sequence
+    float* emd = emz + kPP * RP;
     const bool lead = m == 0;
     // H'_0 of the sequence starting at chunk gs -> bf16 tile row n = m, and H = d * H'_0 in TMEM
     auto state_init = [&](int gs) -> bool {
@@ -461,31 +515,39 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       const float d = exp2f(scal[L - 1]);
       const float c0 = scal[3 * NA];  // (1-lam_0) dt_0
       const int64_t base = ((int64_t)b * H + h) * (int64_t)P * N;
-      float hv[64];
-#pragma unroll
-      for (int pp = 0; pp < 64; ++pp) {
-        float v = 0.f;
-        if (m < N && pp < P) {
-          if (a.h_init) v = a.h_init[base + (int64_t)pp * N + m];
-          if (a.prev_bx_init) v = fmaf(c0, a.prev_bx_init[base + (int64_t)pp * N + m], v);
-        }
-        hv[pp] = v;
-      }
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        uint4 o;
-        o.x = pack_bf16x2(hv[8 * c8 + 0], hv[8 * c8 + 1]);
-        o.y = pack_bf16x2(hv[8 * c8 + 2], hv[8 * c8 + 3]);
-        o.z = pack_bf16x2(hv[8 * c8 + 4], hv[8 * c8 + 5]);
-        o.w = pack_bf16x2(hv[8 * c8 + 6], hv[8 * c8 + 7]);
-        sw128_store_chunk(tileH, m, c8, 128, o);
-      }
-      float v32[32];
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
+        float hv[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v32[e] = d * hv[32 * hf + e];
-        tmem_st32(trow + kColH + 32 * hf, v32);
+        for (int e = 0; e < 32; ++e) {
+          const int pp = 32 * hf + e;
+          float v = 0.f;
+          if (m < N && pp < P) {
+            if (a.h_init) v = a.h_init[base + (int64_t)pp * N + m];
+            if (a.prev_bx_init) v = fmaf(c0, a.prev_bx_init[base + (int64_t)pp * N + m], v);
+          }
+          hv[e] = v;
+        }
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint4 o;
+          o.x = pack_bf16x2(hv[8 * c8 + 0], hv[8 * c8 + 1]);
+          o.y = pack_bf16x2(hv[8 * c8 + 2], hv[8 * c8 + 3]);
+          o.z = pack_bf16x2(hv[8 * c8 + 4], hv[8 * c8 + 5]);
+          o.w = pack_bf16x2(hv[8 * c8 + 6], hv[8 * c8 + 7]);
+          sw128_store_chunk(tileH, m, 4 * hf + c8, 128, o);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) hv[e] *= d;
+        tmem_st32(trow + kColH + 32 * hf, hv);
+      }
+      // this sequence's gate parameters (the previous sequence's last output is complete)
+      const int pd = p.param_dtype;
+      for (int e = m; e < kPP * RP; e += kEpiThreads) {
+        const int pp = e / RP, q = e % RP;
+        const bool okp = pp < P && q < R;
+        emz[e] = okp ? ldf(p.mimo_z, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
+        emd[e] = okp ? ldf(p.mimo_down, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
       }
       return true;
     };
@@ -593,70 +655,78 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       } else {
         write_h_final(g);
       }
-      // ---- output of chunk g
+      // ---- output of chunk g: z is prefetched before waiting for P X; x_r is read from the X tile
+      const int64_t tok = (int64_t)k * L + t;
+      const bool row_ok = tok < a.T && r < R;
+      Raw8<TA> zr[8];
+      {
+        const TA* zrow = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride + (int64_t)h * P;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          if (row_ok && c8 * 8 < P) zr[c8].load(zrow + c8 * 8);
+          else zr[c8].zero();
+        }
+      }
       if (!(ok = role_wait(&bars[BAR_YMMA], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
       tc_fence_after();
       {
-        const int64_t tok = (int64_t)k * L + t;
         const float ec = exp2f(cum2[t]);
         const float Dh = ldf(p.D, h, p.param_dtype);
-        const TA* row = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride;
         TA* yo = reinterpret_cast<TA*>(a.y) + ((int64_t)b * a.T + tok) * HP + (int64_t)h * P;
         const uint32_t cy = kColY + 64 * (g & 1), cyi = kColYi + 64 * (g & 1);
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          float Y[32], Yi[32];
-          tmem_ld32(trow + cy + 32 * hf, Y);
-          tmem_ld32(trow + cyi + 32 * hf, Yi);
-          float acc[32];
+        for (int qq = 0; qq < 4; ++qq) {
+          float Y[16], Yi[16];
+          tmem_ld16(trow + cy + 16 * qq, Y);
+          tmem_ld16(trow + cyi + 16 * qq, Yi);
+          float acc[16];
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            const int p0 = 32 * hf + 8 * c8;
-            float xv[8], zv[8];
-            if (tok < a.T && p0 < P && r < R) {
-              load8<TA>(row + HP + h * P + p0, xv);
-              load8<TA>(row + h * P + p0, zv);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) xv[e] = zv[e] = 0.f;
-            }
+          for (int hc = 0; hc < 2; ++hc) {
+            const int c8 = 2 * qq + hc;
+            const uint4 xq = *reinterpret_cast<const uint4*>(st + PL::tX + sw128_offset(m, c8 * 8, 128));
+            const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const int pp = p0 + e;
-              float o = 0.f;
-              if (pp < P && r < R) {
-                const int64_t q = ((int64_t)h * P + pp) * R + r;
-                const float xr = xv[e] * ldf(p.mimo_x, q, p.param_dtype);
-                const float zz = zv[e] * ldf(p.mimo_z, q, p.param_dtype);
-                o = (Y[8 * c8 + e] + ec * Yi[8 * c8 + e] + Dh * xr) * silu_f(zz) * ldf(p.mimo_down, q, p.param_dtype);
-              }
-              acc[8 * c8 + e] = o;
+              const int pp = c8 * 8 + e;
+              const float xr = __uint_as_float((e & 1) ? (xw[e >> 1] & 0xffff0000u) : (xw[e >> 1] << 16));
+              const float zz = zr[c8].get(e) * emz[pp * RP + r];
+              acc[8 * hc + e] = (Y[8 * hc + e] + ec * Yi[8 * hc + e] + Dh * xr) * silu_fast(zz) * emd[pp * RP + r];
             }
           }
 #pragma unroll
           for (int o = 1; o < RP; o <<= 1) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+            for (int e = 0; e < 16; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
           }
           if (tok < a.T) {
-            constexpr int W = 32 / RP;
+            constexpr int W = 16 / RP;  // outputs written by each of the RP lanes of a token
 #pragma unroll
             for (int rr = 0; rr < RP; ++rr) {
               if (rr != r) continue;
+              const int p0 = 16 * qq + rr * W;
+              if constexpr (W == 16) {
+                if (p0 + 16 <= P) {
+                  float o8[8];
 #pragma unroll
-              for (int c8 = 0; c8 < W / 8; ++c8) {
-                const int p0 = 32 * hf + rr * W + c8 * 8;
+                  for (int e = 0; e < 8; ++e) o8[e] = acc[e];
+                  store8<TA>(yo + p0, o8);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) o8[e] = acc[8 + e];
+                  store8<TA>(yo + p0 + 8, o8);
+                  continue;
+                }
+              } else if constexpr (W == 8) {
                 if (p0 + 8 <= P) {
                   float o8[8];
 #pragma unroll
-                  for (int e = 0; e < 8; ++e) o8[e] = acc[rr * W + c8 * 8 + e];
+                  for (int e = 0; e < 8; ++e) o8[e] = acc[rr * W + e];
                   store8<TA>(yo + p0, o8);
-                } else {
-#pragma unroll
-                  for (int e = 0; e < 8; ++e)
-                    if (p0 + e < P) io<TA>::st(yo + p0 + e, acc[rr * W + c8 * 8 + e]);
+                  continue;
                 }
               }
+#pragma unroll
+              for (int e = 0; e < W; ++e)
+                if (p0 + e < P) io<TA>::st(yo + p0 + e, acc[rr * W + e]);
             }
           }
         }

@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(const __nv_bfloat
     umma_commit(bar);
   }
   bool ok = mbar_wait(bar, 0);
+  __syncwarp();
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {

@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(kCT, 1) gen_state_kernel(SsdParams a) {
     umma_commit(&bar[0]);
   }
   bool ok = mbar_wait(&bar[0], 0);
+  __syncwarp();
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {
@@ -294,6 +295,7 @@ __global__ void __launch_bounds__(kCT, 1) gen_out_kernel(SsdParams a) {
     umma_commit(&bar[0]);
   }
   bool ok = mbar_wait(&bar[0], 0);
+  __syncwarp();
   ok = __syncthreads_and(ok);
   tc_fence_after();
   const int lq = warp & 3, half = warp >> 2;
@@ -339,6 +341,7 @@ __global__ void __launch_bounds__(kCT, 1) gen_out_kernel(SsdParams a) {
     umma_commit(&bar[1]);
   }
   if (ok) ok = mbar_wait(&bar[1], 0);
+  __syncwarp();
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {
