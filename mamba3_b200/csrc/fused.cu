@@ -31,6 +31,20 @@ constexpr int kMmaWarp = 12;
 constexpr uint32_t kColS = 0, kColY = 128, kColYi = 256, kColH = 384;
 constexpr int kBarProd = 1, kBarEpi = 2;
 
+// Optional per-phase timestamps of CTA 0 for pipeline analysis: build with -DM3B_TIMELINE and
+// read them with m3b_timeline_read(); compiled out otherwise.
+#ifdef M3B_TIMELINE
+__device__ unsigned long long g_m3b_timeline[64 * 16];
+#define M3B_TL(g, slot)                                                              \
+  do {                                                                               \
+    if (blockIdx.x == 0 && (g) < 64) g_m3b_timeline[(g)*16 + (slot)] = globaltimer_ns(); \
+  } while (0)
+#else
+#define M3B_TL(g, slot) \
+  do {                  \
+  } while (0)
+#endif
+
 template <int RP>
 struct FPlan {
   static constexpr int L = 128 / RP;
@@ -238,9 +252,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         if (ptid < nh2)
           omega[(g & 1) * 64 + ptid] = a.angle_init ? (double)a.angle_init[((int64_t)b * H + h) * nh2 + ptid] : 0.0;
       }
+      if (ptid == 0) M3B_TL(g, 0);
       if (g >= 2 && !role_wait(&bars[BAR_EMPTY0 + s], ((g >> 1) - 1) & 1, ptid == 0, kBarProd, kProdThreads,
                                abort_flag, a.err))
         break;
+      if (ptid == 0) M3B_TL(g, 1);
       uint8_t* st = sm + s * PL::kStage;
       float* scal = reinterpret_cast<float*>(sm + PL::scal + s * PL::scalStride);
       float* cum2 = scal;
@@ -303,6 +319,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         }
       }
       named_bar(kBarProd, kProdThreads);
+      if (ptid == 0) M3B_TL(g, 2);
       if (ptid < 32) {
         constexpr int PER = L / 32;
         const float A = -expf(ldf(p.A_log, h, p.param_dtype));
@@ -414,6 +431,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         for (int u = ptid; u < 128 * ncz; u += kProdThreads)
           sw128_store_chunk(st + PL::tB, u / ncz, c0 + u % ncz, 128, make_uint4(0, 0, 0, 0));
       }
+      if (ptid == 0) M3B_TL(g, 3);
       named_bar(kBarProd, kProdThreads);  // wst ready
       // (3) X and w X tiles from the prefetched x rows: row (s*RP + q), column p
 #pragma unroll
@@ -441,6 +459,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       fence_async_smem();
       named_bar(kBarProd, kProdThreads);
       if (ptid == 0) mbar_arrive(&bars[BAR_FULL0 + s]);
+      if (ptid == 0) M3B_TL(g, 4);
     }
   } else if (warp == kMmaWarp) {
     // =============================== MMA issue ===============================
@@ -460,6 +479,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           break;
         }
         tc_fence_after();
+        M3B_TL(g, 5);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_bf16(tbase + kColS, kmajor_desc(st + PL::tC, 128, kk * 16), kmajor_desc(st + PL::tB, 128, kk * 16),
@@ -470,6 +490,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           break;
         }
         tc_fence_after();
+        M3B_TL(g, 6);
         const uint32_t cyi = kColYi + 64 * (g & 1);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -486,6 +507,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           break;
         }
         tc_fence_after();
+        M3B_TL(g, 7);
         const uint32_t cy = kColY + 64 * (g & 1);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -585,8 +607,21 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       const float* cum2 = scal;
       const float* gam = scal + 2 * NA;
       const float* gbw = scal + 5 * NA;
+      // z of this chunk's row (t, r), prefetched while the tensor core works
+      const int64_t tok = (int64_t)k * L + t;
+      const bool row_ok = tok < a.T && r < R;
+      Raw8<TA> zr[8];
+      {
+        const TA* zrow = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride + (int64_t)h * P;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          if (row_ok && c8 * 8 < P) zr[c8].load(zrow + c8 * 8);
+          else zr[c8].zero();
+        }
+      }
       if (!(ok = role_wait(&bars[BAR_SMMA], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
       tc_fence_after();
+      if (lead) M3B_TL(g, 8);
       // ---- mask: P[m, (s,q)] = S * exp(cum_t - cum_s) * (s<t ? gamma_s + (1-lam_{s+1})dt_{s+1} : gamma_s)
       {
         const float ct = cum2[t];
@@ -616,59 +651,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       tc_fence_before();
       named_bar(kBarEpi, kEpiThreads);
       if (lead) mbar_arrive(&bars[BAR_PREADY]);
-      // ---- state for chunk g+1
-      if (g + 1 < G) {
-        int seq1, b1, h1, k1;
-        sc.at(g + 1, seq1, b1, h1, k1);
-        if (k1 == 0) {
-          write_h_final(g);
-          if (!(ok = state_init(g + 1))) break;
-        } else {
-          const int s1 = (g + 1) & 1;
-          if (!(ok = role_wait(&bars[BAR_FULL0 + s1], ((g + 1) >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag,
-                               a.err)))
-            break;
-          const float* scal1 = reinterpret_cast<const float*>(sm + PL::scal + s1 * PL::scalStride);
-          const float d = exp2f(scal1[L - 1]);
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            float v[32];
-            tmem_ld32(trow + kColH + 32 * hf, v);
-#pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-              uint4 o;
-              o.x = pack_bf16x2(v[8 * c8 + 0], v[8 * c8 + 1]);
-              o.y = pack_bf16x2(v[8 * c8 + 2], v[8 * c8 + 3]);
-              o.z = pack_bf16x2(v[8 * c8 + 4], v[8 * c8 + 5]);
-              o.w = pack_bf16x2(v[8 * c8 + 6], v[8 * c8 + 7]);
-              sw128_store_chunk(tileH, m, 4 * hf + c8, 128, o);
-            }
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] *= d;
-            tmem_st32(trow + kColH + 32 * hf, v);
-          }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        named_bar(kBarEpi, kEpiThreads);
-        if (lead) mbar_arrive(&bars[BAR_HREADY]);
-      } else {
-        write_h_final(g);
-      }
-      // ---- output of chunk g: z is prefetched before waiting for P X; x_r is read from the X tile
-      const int64_t tok = (int64_t)k * L + t;
-      const bool row_ok = tok < a.T && r < R;
-      Raw8<TA> zr[8];
-      {
-        const TA* zrow = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride + (int64_t)h * P;
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          if (row_ok && c8 * 8 < P) zr[c8].load(zrow + c8 * 8);
-          else zr[c8].zero();
-        }
-      }
+      if (lead) M3B_TL(g, 9);
+      // ---- output of chunk g (x_r comes from the X tile of this stage)
       if (!(ok = role_wait(&bars[BAR_YMMA], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
       tc_fence_after();
+      if (lead) M3B_TL(g, 10);
       {
         const float ec = exp2f(cum2[t]);
         const float Dh = ldf(p.D, h, p.param_dtype);
@@ -733,6 +720,47 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       }
       tc_fence_before();
       mbar_arrive(&bars[BAR_EMPTY0 + s]);
+      if (lead) M3B_TL(g, 11);
+      // ---- state for chunk g+1: H'_{g+1} -> bf16 tile, H *= d_{g+1}
+      if (g + 1 < G) {
+        int seq1, b1, h1, k1;
+        sc.at(g + 1, seq1, b1, h1, k1);
+        if (k1 == 0) {
+          write_h_final(g);
+          if (!(ok = state_init(g + 1))) break;
+        } else {
+          const int s1 = (g + 1) & 1;
+          if (!(ok = role_wait(&bars[BAR_FULL0 + s1], ((g + 1) >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag,
+                               a.err)))
+            break;
+          const float* scal1 = reinterpret_cast<const float*>(sm + PL::scal + s1 * PL::scalStride);
+          const float d = exp2f(scal1[L - 1]);
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            float v[32];
+            tmem_ld32(trow + kColH + 32 * hf, v);
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+              uint4 o;
+              o.x = pack_bf16x2(v[8 * c8 + 0], v[8 * c8 + 1]);
+              o.y = pack_bf16x2(v[8 * c8 + 2], v[8 * c8 + 3]);
+              o.z = pack_bf16x2(v[8 * c8 + 4], v[8 * c8 + 5]);
+              o.w = pack_bf16x2(v[8 * c8 + 6], v[8 * c8 + 7]);
+              sw128_store_chunk(tileH, m, 4 * hf + c8, 128, o);
+            }
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= d;
+            tmem_st32(trow + kColH + 32 * hf, v);
+          }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_bar(kBarEpi, kEpiThreads);
+        if (lead) mbar_arrive(&bars[BAR_HREADY]);
+        if (lead) M3B_TL(g, 12);
+      } else {
+        write_h_final(g);
+      }
     }
   }
   tc_fence_before();
@@ -779,6 +807,15 @@ int launch_fused_t(const FusedParams& fp, cudaStream_t st) {
   return check_launch("ssd_fused");
 }
 }  // namespace
+
+#ifdef M3B_TIMELINE
+extern "C" M3B_API int m3b_timeline_read(unsigned long long* host, int n) {
+  return cudaMemcpyFromSymbol(host, g_m3b_timeline, sizeof(unsigned long long) * (n < 1024 ? n : 1024)) ==
+                 cudaSuccess
+             ? 0
+             : 3;
+}
+#endif
 
 bool fused_supported(const m3b_layer_params& p) {
   const int nh2 = p.N / 2;
