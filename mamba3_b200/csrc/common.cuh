@@ -325,6 +325,18 @@ __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+// 2^x with the hardware approximation (flushes denormals; exact 0 for very negative x).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Bring [p, p + bytes) into L2 ahead of use (16-byte aligned address and size).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // silu(v) = v * sigmoid(v) = 0.5 v (1 + tanh(v / 2)), with the hardware tanh approximation.
 __device__ __forceinline__ float silu_fast(float v) {
   float th;

@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
   constexpr int L = PL::L;
   constexpr int NA = PL::NA;
   constexpr int SEGMAX = L / 4;          // longest token segment of one producer thread (N/2 <= 64)
-  constexpr int TB = R >= 4 ? 8 : 16;    // tokens per B/C load batch
+  constexpr int TB = R >= 2 ? 8 : 16;    // tokens per B/C load batch
   constexpr int XU = L / 32;             // x-tile units per producer thread (L * 8 / 256)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
@@ -267,6 +267,25 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       float* gbw = scal + 5 * NA;
       float* rmsB = scal + 6 * NA;
       float* rmsC = scal + 7 * NA;
+      // L2 prefetch of the projection rows the next chunk reads (B|C, x, z, dt|lam|theta)
+      if (g + 1 < G && ptid < 4 * L) {
+        int seqn, bn, hn, kn;
+        sc.at(g + 1, seqn, bn, hn, kn);
+        const int64_t tn = (int64_t)kn * L + (ptid >> 2);
+        if (tn < a.T) {
+          const TA* row = proj + ((int64_t)bn * a.T + tn) * a.proj_stride;
+          const int part = ptid & 3;
+          const int esz = (int)sizeof(TA);
+          if (part == 0) prefetch_l2(row + offB, (uint32_t)(2 * p.G * NR * esz) & ~15u);
+          else if (part == 1) prefetch_l2(row + HP + hn * P, (uint32_t)(P * esz) & ~15u);
+          else if (part == 2) prefetch_l2(row + hn * P, (uint32_t)(P * esz) & ~15u);
+          else {
+            const int64_t span = (int64_t)a.proj_stride - offDt;  // dt | lam | theta to the row end
+            const uint32_t bytes = (uint32_t)((span * esz) & ~int64_t(15));
+            if (bytes > 0 && ((offDt * esz) & 15) == 0) prefetch_l2(row + offDt, bytes < 4096u ? bytes : 4096u);
+          }
+        }
+      }
       // (0) every load that does not depend on this chunk's scalars, issued together
       Raw8<TA> xr[XU];
 #pragma unroll
@@ -632,7 +651,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
 #pragma unroll
           for (int jj = 0; jj < 32; jj += RP) {
             const int sj = (32 * c32 + jj) / RP;
-            const float w = sj <= t ? exp2f(ct - cum2[sj]) * (sj < t ? gbw[sj] : gam[sj]) : 0.f;
+            const float e = ex2_fast(fminf(ct - cum2[sj], 0.f));
+            const float w = sj < t ? e * gbw[sj] : (sj == t ? gam[sj] : 0.f);
 #pragma unroll
             for (int q = 0; q < RP; ++q) v[jj + q] *= w;
           }
