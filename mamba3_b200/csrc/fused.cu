@@ -58,7 +58,8 @@ struct FPlan {
   static constexpr int segt = omega + 128 * 8;                       // 256 floats
   static constexpr int nrm = segt + 256 * 4;                         // B/C norm weight, bias: 4 x N*R fp32
   static constexpr int mxs = nrm + 4 * kNS * RP * 4;                 // mimo_x: kPP x RP fp32
-  static constexpr int epar = mxs + kPP * RP * 4;                    // mimo_z, mimo_down (epilogue)
+  static constexpr int seqp = mxs + kPP * RP * 4;                    // A, dt_bias of the producers' sequence
+  static constexpr int epar = seqp + 16;                             // mimo_z, mimo_down (epilogue)
   static constexpr int bars = epar + 2 * kPP * RP * 4;               // 8 mbarriers
   static constexpr int misc = bars + 64;                             // taddr, abort
   static constexpr int bytes = misc + 16 + 1024;
@@ -171,7 +172,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
   constexpr int L = PL::L;
   constexpr int NA = PL::NA;
   constexpr int SEGMAX = L / 4;          // longest token segment of one producer thread (N/2 <= 64)
-  constexpr int TB = R >= 2 ? 8 : 16;    // tokens per B/C load batch
   constexpr int XU = L / 32;             // x-tile units per producer thread (L * 8 / 256)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
@@ -286,7 +286,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           }
         }
       }
-      // (0) every load that does not depend on this chunk's scalars, issued together
+      // (0) every global load of this chunk, issued together: x rows, theta and the B/C rows of
+      // my segment, the token scalars.  One round trip covers the scalar and prefix phases.
       Raw8<TA> xr[XU];
 #pragma unroll
       for (int jj = 0; jj < XU; ++jj) {
@@ -301,6 +302,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       for (int jj = 0; jj < SEGMAX; ++jj) {
         const int64_t t = t0 + seg * seglen + jj;
         th[jj] = (bc_act && p.complex_ssm && jj < seglen && t < a.T) ? io<TA>::ld(thp + t * a.proj_stride) : 0.f;
+      }
+      const TA* pB = rowbase + offB + grp * NR + 2 * pi * R;
+      const TA* pC = rowbase + offC + grp * NR + 2 * pi * R;
+      PairRaw<TA, R> vb[SEGMAX], vc[SEGMAX];
+#pragma unroll
+      for (int jj = 0; jj < SEGMAX; ++jj) {
+        const int64_t t = t0 + seg * seglen + jj;
+        if (bc_act && jj < seglen && t < a.T) {
+          vb[jj].load(pB + t * a.proj_stride);
+          vc[jj].load(pC + t * a.proj_stride);
+        } else {
+          vb[jj].zero();
+          vc[jj].zero();
+        }
       }
       float dt_raw = 0.f, lam_raw = 0.f, rb = 0.f, rc = 0.f;
       const bool tok_act = ptid <= L && t0 + ptid < a.T;
@@ -318,7 +333,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       if (ptid <= L) {
         float dt = 0.f, gmm = 0.f, bp = 0.f;
         if (tok_act) {
-          dt = softplus_f(dt_raw + ldf(p.dt_bias, h, p.param_dtype));
+          dt = softplus_f(dt_raw + reinterpret_cast<const float*>(sm + PL::seqp)[1]);
           if (a.dt_scale)
             dt *= io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + ((int64_t)b * a.T + t0 + ptid) * H + h);
           if (p.trapezoidal) {
@@ -341,7 +356,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       if (ptid == 0) M3B_TL(g, 2);
       if (ptid < 32) {
         constexpr int PER = L / 32;
-        const float A = -expf(ldf(p.A_log, h, p.param_dtype));
+        const float A = reinterpret_cast<const float*>(sm + PL::seqp)[0];
         float v[PER];
         float run = 0.f;
 #pragma unroll
@@ -377,8 +392,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         for (int q = 0; q < seg; ++q) off += segt[q * nh2 + pi];
         const double om = omega[(g & 1) * 64 + pi];
         float run = off;
-        const TA* pB = rowbase + offB + grp * NR + 2 * pi * R;
-        const TA* pC = rowbase + offC + grp * NR + 2 * pi * R;
         float wb0[RP], wb1[RP], bb0[RP], bb1[RP], wc0[RP], wc1[RP], bc0[RP], bc1[RP];
 #pragma unroll
         for (int r = 0; r < RP; ++r) {
@@ -393,48 +406,30 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           bc1[r] = nbC[i1];
         }
 #pragma unroll
-        for (int j0 = 0; j0 < SEGMAX; j0 += TB) {
-          if (j0 >= seglen) break;
-          PairRaw<TA, R> vb[TB], vc[TB];
-#pragma unroll
-          for (int u = 0; u < TB; ++u) {
-            const int jj = j0 + u;
-            const int64_t t = t0 + seg * seglen + jj;
-            if (jj < seglen && t < a.T) {
-              vb[u].load(pB + t * a.proj_stride);
-              vc[u].load(pC + t * a.proj_stride);
-            } else {
-              vb[u].zero();
-              vc[u].zero();
-            }
+        for (int jj = 0; jj < SEGMAX; ++jj) {
+          if (jj >= seglen) break;
+          const int j = seg * seglen + jj;
+          const bool valid = t0 + j < a.T;
+          float cs = 1.f, sn = 0.f;
+          if (p.complex_ssm) {
+            run = fmaf(dtv[j], th[jj], run);
+            sincos_reduced((float)(om - (double)run), &sn, &cs);
           }
+          const float rbj = rmsB[j], rcj = rmsC[j];
 #pragma unroll
-          for (int u = 0; u < TB; ++u) {
-            const int jj = j0 + u;
-            if (jj >= seglen) break;
-            const int j = seg * seglen + jj;
-            const bool valid = t0 + j < a.T;
-            float cs = 1.f, sn = 0.f;
-            if (p.complex_ssm) {
-              run = fmaf(dtv[j], th[jj], run);
-              sincos_reduced((float)(om - (double)run), &sn, &cs);
+          for (int r = 0; r < RP; ++r) {
+            uint32_t ob = 0, oc = 0;
+            if (r < R && valid) {
+              const float b0 = fmaf(vb[jj].get(r) * rbj, wb0[r], bb0[r]);
+              const float b1 = fmaf(vb[jj].get(R + r) * rbj, wb1[r], bb1[r]);
+              const float c0 = fmaf(vc[jj].get(r) * rcj, wc0[r], bc0[r]);
+              const float c1 = fmaf(vc[jj].get(R + r) * rcj, wc1[r], bc1[r]);
+              ob = pack_bf16x2(b0 * cs - b1 * sn, b0 * sn + b1 * cs);
+              oc = pack_bf16x2(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
             }
-            const float rbj = rmsB[j], rcj = rmsC[j];
-#pragma unroll
-            for (int r = 0; r < RP; ++r) {
-              uint32_t ob = 0, oc = 0;
-              if (r < R && valid) {
-                const float b0 = fmaf(vb[u].get(r) * rbj, wb0[r], bb0[r]);
-                const float b1 = fmaf(vb[u].get(R + r) * rbj, wb1[r], bb1[r]);
-                const float c0 = fmaf(vc[u].get(r) * rcj, wc0[r], bc0[r]);
-                const float c1 = fmaf(vc[u].get(R + r) * rcj, wc1[r], bc1[r]);
-                ob = pack_bf16x2(b0 * cs - b1 * sn, b0 * sn + b1 * cs);
-                oc = pack_bf16x2(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
-              }
-              const uint32_t o = sw128_offset(j * RP + r, 2 * pi, 128);
-              *reinterpret_cast<uint32_t*>(st + PL::tB + o) = ob;
-              *reinterpret_cast<uint32_t*>(st + PL::tC + o) = oc;
-            }
+            const uint32_t o = sw128_offset(j * RP + r, 2 * pi, 128);
+            *reinterpret_cast<uint32_t*>(st + PL::tB + o) = ob;
+            *reinterpret_cast<uint32_t*>(st + PL::tC + o) = oc;
           }
         }
         if (seg == nseg - 1) {
