@@ -416,6 +416,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
             sincos_reduced((float)(om - (double)run), &sn, &cs);
           }
           const float rbj = rmsB[j], rcj = rmsC[j];
+          if (ptid == 0 && jj == 4) M3B_TL(g, 15);
 #pragma unroll
           for (int r = 0; r < RP; ++r) {
             uint32_t ob = 0, oc = 0;
@@ -643,6 +644,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         for (int c32 = 0; c32 < 4; ++c32) {
           float v[32];
           tmem_ld32(trow + kColS + 32 * c32, v);
+          if (lead && c32 == 0) M3B_TL(g, 13);
 #pragma unroll
           for (int jj = 0; jj < 32; jj += RP) {
             const int sj = (32 * c32 + jj) / RP;
@@ -660,6 +662,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
             o.w = pack_bf16x2(v[8 * cc + 6], v[8 * cc + 7]);
             sw128_store_chunk(st + PL::tB, m, 4 * c32 + cc, 128, o);
           }
+          if (lead && c32 == 0) M3B_TL(g, 14);
         }
       }
       fence_async_smem();
