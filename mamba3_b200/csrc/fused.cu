@@ -251,6 +251,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         }
         if (ptid < nh2)
           omega[(g & 1) * 64 + ptid] = a.angle_init ? (double)a.angle_init[((int64_t)b * H + h) * nh2 + ptid] : 0.0;
+        if (ptid == 0) {
+          float* sp = reinterpret_cast<float*>(sm + PL::seqp);
+          sp[0] = -expf(ldf(p.A_log, h, pd));
+          sp[1] = ldf(p.dt_bias, h, pd);
+        }
+        named_bar(kBarProd, kProdThreads);  // the sequence's parameters are read below
       }
       if (ptid == 0) M3B_TL(g, 0);
       if (g >= 2 && !role_wait(&bars[BAR_EMPTY0 + s], ((g >> 1) - 1) & 1, ptid == 0, kBarProd, kProdThreads,
