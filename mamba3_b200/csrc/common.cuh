@@ -164,12 +164,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// As mbar_try_wait, but the thread may sleep in the barrier for up to `hint_ns` before the test
+// fails (it wakes as soon as the phase completes), so long waits issue few instructions.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete; false if the wait limit expired.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
 }
@@ -320,6 +334,34 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Arrive on `bar` and add `bytes` to the transaction count its current phase waits for.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Tensor-memory-accelerator load of one 3-D box (coordinates in elements, innermost first)
+// into this CTA's shared memory; completion is signalled on `bar` as transaction bytes.
+// No cluster multicast: every CTA fetches its own boxes.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Bring one 3-D box of a tensor map into L2 (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_3d(const void* tmap, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(tmap), "r"(c0), "r"(c1),
+               "r"(c2)
+               : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
 // Barrier among `n` threads (multiple of 32) of the CTA on hardware barrier `id` (1..15).
 __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -337,11 +379,42 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Packed fp32 pairs (Blackwell f32x2 FMA / MUL): one instruction for two lanes of work.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2,%3};\n\tmov.b64 rb, {%4,%5};\n\tmov.b64 rc, {%6,%7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0,%1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2,%3};\n\tmov.b64 rb, {%4,%5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0,%1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// bf16x2 word -> two floats (low half first)
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 // silu(v) = v * sigmoid(v) = 0.5 v (1 + tanh(v / 2)), with the hardware tanh approximation.
 __device__ __forceinline__ float silu_fast(float v) {
   float th;
   asm("tanh.approx.f32 %0, %1;" : "=f"(th) : "f"(0.5f * v));
   return 0.5f * v * (1.f + th);
+}
+
+// silu of a pair: h (1 + tanh h) with h = v / 2, on packed fp32 pairs
+__device__ __forceinline__ float2 silu_fast2(float2 v) {
+  const float2 hv = mul2(v, make_float2(0.5f, 0.5f));
+  float2 th;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th.x) : "f"(hv.x));
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th.y) : "f"(hv.y));
+  return fma2(hv, th, hv);
 }
 
 }  // namespace m3b

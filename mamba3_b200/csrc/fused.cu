@@ -1,21 +1,27 @@
 // Fused sequential SSD layer kernel: one persistent CTA per SM walks whole (batch, head)
 // sequences chunk by chunk, so the inter-chunk state never leaves the SM.
 //
-// Roles (416 threads):
-//   warps 0-3  epilogue: decay mask S -> P, running-state bookkeeping (TMEM <-> SMEM),
-//              output y = P X + e^cum C^ H'^T + D x, gate, MIMO down, h_final
-//   warps 4-11 producers: per chunk, token scalars, angle prefix + RoPE on B/C, MIMO x tiles,
-//              into one of two shared-memory stages
-//   warp 12    tcgen05 issue (one thread) + TMEM allocation
-// Per chunk g (stage s = g % 2), with the running state H (fp32, TMEM lanes n x cols p):
-//   MMA:  S  = C^ B^T                         (TMEM [0,128))
-//         Yi = C^ H'_g^T   (H' bf16 tile)     (TMEM [256 + 64 (g%2), ...))
-//         H += B^^T (w X)  (H already scaled by the chunk decay)   (TMEM [384,448))
-//         Y  = P X         (P = mask(S))      (TMEM [128 + 64 (g%2), ...))
-//   epilogue: mask(g); state(g+1): H'_{g+1} = H -> bf16 tile, H *= d_{g+1}; output(g)
+// Roles (512 threads, 128 registers each):
+//   warps 0-7   epilogue (TMEM lane quadrant = warp % 4, column half = warp / 4):
+//               decay mask S -> P, output y = P X + e^cum C^ H'^T + D x with gate and MIMO down,
+//               running-state bookkeeping (TMEM <-> bf16 tile), MIMO x tiles X and W, h_final.
+//               Its leader issues the GEMMs that depend on the running state and on P, and
+//               hands each shared-memory stage back to the producers (with the TMA copies of
+//               the chunk two ahead) once the output that read it is written.
+//   warps 8-15  producers: per chunk, token scalars, angle prefix + RoPE + norm of B/C into one
+//               of two shared-memory stages; their leader issues S = C^ B^T.
+// Per chunk g (stage s = g % 2), with the running state H (fp32, TMEM lanes n x columns p):
+//   producer leader:  S_g = C^ B^T                            -> TMEM S[g%2] (128 columns)
+//   epilogue leader:  Yi_g = C^ H'_g^T, H += B^^T W           -> Yi[g%2], H    (after state(g))
+//                     Y_g = P X                               -> first 64 columns of S[g%2]
+//   epilogue:         mask(g), output(g), state(g+1): H'_{g+1} = H -> bf16 tile, H *= d_{g+1},
+//                     X and W tiles of chunk g+1
 // The algebra (weights W, w, the first-token beta term carried by H') is in chunk.cuh.
-// Every wait is bounded; on a timeout one leader thread per role raises a shared abort flag
-// that its role reads after a named barrier, so every role leaves its loop uniformly.
+// Every wait is bounded.  On a timeout a role's leader raises that role's own abort flag, which
+// the role reads after its named barrier, so all its threads leave the loop together; the other
+// role then times out on the barrier this role no longer arrives on, and leaves too.
+#include <cuda.h>
+
 #include <mutex>
 #include <set>
 #include <utility>
@@ -24,19 +30,18 @@
 
 namespace m3b {
 
-constexpr int kFusedThreads = 13 * 32;
-constexpr int kEpiThreads = 128;
+constexpr int kFusedThreads = 16 * 32;
+constexpr int kEpiThreads = 256;
 constexpr int kProdThreads = 256;
-constexpr int kMmaWarp = 12;
-constexpr uint32_t kColS = 0, kColY = 128, kColYi = 256, kColH = 384;
+constexpr uint32_t kColS = 0, kColYi = 256, kColH = 384;  // S[g%2] at 128 (g%2); Yi at 256 + 64 (g%2)
 constexpr int kBarProd = 1, kBarEpi = 2;
 
 // Optional per-phase timestamps of CTA 0 for pipeline analysis: build with -DM3B_TIMELINE and
 // read them with m3b_timeline_read(); compiled out otherwise.
 #ifdef M3B_TIMELINE
 __device__ unsigned long long g_m3b_timeline[64 * 16];
-#define M3B_TL(g, slot)                                                              \
-  do {                                                                               \
+#define M3B_TL(g, slot)                                                                   \
+  do {                                                                                    \
     if (blockIdx.x == 0 && (g) < 64) g_m3b_timeline[(g)*16 + (slot)] = globaltimer_ns(); \
   } while (0)
 #else
@@ -57,17 +62,17 @@ struct FPlan {
   static constexpr int omega = scal + 2 * scalStride;                // 2 x 64 doubles (by chunk parity)
   static constexpr int segt = omega + 128 * 8;                       // 256 floats
   static constexpr int nrm = segt + 256 * 4;                         // B/C norm weight, bias: 4 x N*R fp32
-  static constexpr int mxs = nrm + 4 * kNS * RP * 4;                 // mimo_x: kPP x RP fp32
+  static constexpr int mxs = nrm + 4 * kNS * RP * 4;                 // mimo_x (epilogue): kPP x RP fp32
   static constexpr int seqp = mxs + kPP * RP * 4;                    // A, dt_bias of the producers' sequence
   static constexpr int epar = seqp + 16;                             // mimo_z, mimo_down (epilogue)
-  static constexpr int bars = epar + 2 * kPP * RP * 4;               // 8 mbarriers
-  static constexpr int misc = bars + 64;                             // taddr, abort
+  static constexpr int bars = epar + 2 * kPP * RP * 4;               // 9 mbarriers
+  static constexpr int misc = bars + 128;                            // taddr, abort flags
   static constexpr int bytes = misc + 16 + 1024;
   static_assert(bytes <= 227 * 1024, "fused CTA shared memory exceeds 227 KB");
 };
 
-enum { BAR_FULL0 = 0, BAR_FULL1 = 1, BAR_EMPTY0 = 2, BAR_EMPTY1 = 3, BAR_SMMA = 4, BAR_YMMA = 5, BAR_HREADY = 6,
-       BAR_PREADY = 7 };
+enum { BAR_FULL0 = 0, BAR_FULL1 = 1, BAR_EMPTY0 = 2, BAR_EMPTY1 = 3, BAR_SDONE0 = 4, BAR_SDONE1 = 5,
+       BAR_HDONE = 6, BAR_YDONE = 7, BAR_STAGE0 = 8, BAR_STAGE1 = 9 };
 
 // CTA c walks sequences (batch, head) = c, c + stride, c + 2 stride, ... of nseq_total,
 // each chunk by chunk; g numbers the chunks of all its sequences.
@@ -122,17 +127,32 @@ struct PairRaw {
       }
     }
   }
+  __device__ __forceinline__ void load_shared(const uint8_t* p) {
+    if constexpr (W == 1) {
+      w[0] = *reinterpret_cast<const uint32_t*>(p);
+    } else if constexpr (W == 2) {
+      const uint2 t = *reinterpret_cast<const uint2*>(p);
+      w[0] = t.x;
+      w[1] = t.y;
+    } else {
+#pragma unroll
+      for (int i = 0; i < W / 4; ++i) {
+        const uint4 t = reinterpret_cast<const uint4*>(p)[i];
+        w[4 * i] = t.x;
+        w[4 * i + 1] = t.y;
+        w[4 * i + 2] = t.z;
+        w[4 * i + 3] = t.w;
+      }
+    }
+  }
   __device__ __forceinline__ void zero() {
 #pragma unroll
     for (int i = 0; i < W; ++i) w[i] = 0u;
   }
-  __device__ __forceinline__ float get(int e) const {  // element e of the 2R
-    if constexpr (sizeof(TA) == 2) {
-      const uint32_t x = w[e >> 1];
-      return __uint_as_float((e & 1) ? (x & 0xffff0000u) : (x << 16));
-    } else {
-      return __uint_as_float(w[e]);
-    }
+  // elements (e, e+1) of the 2R as a float pair (e even)
+  __device__ __forceinline__ float2 pair(int e) const {
+    if constexpr (sizeof(TA) == 2) return bf2_to_f2(w[e >> 1]);
+    else return make_float2(__uint_as_float(w[e]), __uint_as_float(w[e + 1]));
   }
 };
 
@@ -163,16 +183,38 @@ struct Raw8 {
       return __uint_as_float(w[e]);
     }
   }
+  // elements (e, e+1) as a float pair (e even)
+  __device__ __forceinline__ float2 pair(int e) const {
+    if constexpr (sizeof(TA) == 2) return bf2_to_f2(w[e >> 1]);
+    else return make_float2(__uint_as_float(w[e]), __uint_as_float(w[e + 1]));
+  }
 };
 
-template <typename TA, int R>
-__global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams a, Sched sc) {
+__device__ __forceinline__ void st_pack_chunk(uint8_t* tile, int row, int c8, const float (&v)[8]) {
+  uint4 o;
+  o.x = pack_bf16x2(v[0], v[1]);
+  o.y = pack_bf16x2(v[2], v[3]);
+  o.z = pack_bf16x2(v[4], v[5]);
+  o.w = pack_bf16x2(v[6], v[7]);
+  sw128_store_chunk(tile, row, c8, 128, o);
+}
+
+// TMA: bf16 activations, N = 128 and 16-byte aligned projection rows.  The raw B / C rows and
+// theta of a chunk then arrive by tensor-memory-accelerator copies straight into the stage's
+// B / C / W tiles, and each producer warp rewrites its tokens in place; otherwise every
+// producer thread loads its raw values from global memory into registers.
+template <typename TA, int R, bool TMA>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    ssd_fused_kernel(FusedParams a, Sched sc, const __grid_constant__ CUtensorMap tm_bc,
+                     const __grid_constant__ CUtensorMap tm_th) {
+  static_assert(!TMA || sizeof(TA) == 2, "the TMA producer path stages bf16 rows");
+  constexpr bool N128 = TMA;
   constexpr int RP = rp_of(R);
   using PL = FPlan<RP>;
   constexpr int L = PL::L;
   constexpr int NA = PL::NA;
-  constexpr int SEGMAX = L / 4;          // longest token segment of one producer thread (N/2 <= 64)
-  constexpr int XU = L / 32;             // x-tile units per producer thread (L * 8 / 256)
+  constexpr int SEGMAX = L / 4;  // longest token segment of one producer thread (N/2 <= 64)
+  constexpr int XU = L / 32;     // X / W tile units (8 columns of one token) per epilogue thread
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const m3b_layer_params& p = a.prm;
@@ -180,25 +222,29 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + PL::bars);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + PL::misc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + PL::misc + 4);
+  volatile int* prod_abort = reinterpret_cast<volatile int*>(sm + PL::misc + 4);
+  volatile int* epi_abort = reinterpret_cast<volatile int*>(sm + PL::misc + 8);
   double* omega = reinterpret_cast<double*>(sm + PL::omega);
   float* segt = reinterpret_cast<float*>(sm + PL::segt);
   const int G = sc.count() * sc.K;
 
-  if (warp == kMmaWarp) {
+  if (warp == 0) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
-  if (tid == 0) {
+  if (tid == 32) {
     mbar_init(&bars[BAR_FULL0], 1);
     mbar_init(&bars[BAR_FULL1], 1);
     mbar_init(&bars[BAR_EMPTY0], kEpiThreads);
     mbar_init(&bars[BAR_EMPTY1], kEpiThreads);
-    mbar_init(&bars[BAR_SMMA], 1);
-    mbar_init(&bars[BAR_YMMA], 1);
-    mbar_init(&bars[BAR_HREADY], 1);
-    mbar_init(&bars[BAR_PREADY], 1);
-    *abort_flag = 0;
+    mbar_init(&bars[BAR_SDONE0], 1);
+    mbar_init(&bars[BAR_SDONE1], 1);
+    mbar_init(&bars[BAR_HDONE], 1);
+    mbar_init(&bars[BAR_YDONE], 1);
+    mbar_init(&bars[BAR_STAGE0], 1);
+    mbar_init(&bars[BAR_STAGE1], 1);
+    *prod_abort = 0;
+    *epi_abort = 0;
     fence_mbar_init();
   }
   // the operand tiles start zeroed: columns n >= N of tileC stay zero for the whole kernel
@@ -215,21 +261,80 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
   const int offB = 2 * HP, offC = offB + p.G * NR, offDt = offC + p.G * NR;
   const int offLam = offDt + H, offTh = offLam + (p.trapezoidal ? H : 0);
 
-  if (warp >= 4 && warp < 12) {
+  // Stage gg % 2 is handed to the producers for chunk gg through STAGE[gg % 2].  On the TMA path
+  // the hand-over also starts the copies of the chunk's raw B / C halves (n < 64 | n >= 64 ->
+  // tile blocks 0 | 1; token j's half lands on the bytes of tile rows j*RP .. j*RP+RP-1) and of
+  // theta (-> the W tile, built only after theta has been consumed), counted as transaction
+  // bytes of the same phase.  The producers hand chunks 0 and 1 to themselves; the epilogue
+  // leader hands chunk g + 2 over once every epilogue thread has written the output of chunk g.
+  auto issue_stage = [&](int gg) {
+    uint64_t* bar = &bars[BAR_STAGE0 + (gg & 1)];
+    if constexpr (TMA) {
+      int sq, bb, hh, kk;
+      sc.at(gg, sq, bb, hh, kk);
+      const int gr = hh / (H / p.G);
+      uint8_t* stg = sm + (gg & 1) * PL::kStage;
+      constexpr uint32_t kHalf = 16384;
+      mbar_arrive_expect_tx(bar, 4 * kHalf + (p.complex_ssm ? (uint32_t)L * 128u : 0u));
+      const int xb = offB + gr * NR, xc = offC + gr * NR, ti = kk * L;
+      tma_load_3d(stg + PL::tB, &tm_bc, xb, ti, bb, bar);
+      tma_load_3d(stg + PL::tB + kHalf, &tm_bc, xb + NR / 2, ti, bb, bar);
+      tma_load_3d(stg + PL::tC, &tm_bc, xc, ti, bb, bar);
+      tma_load_3d(stg + PL::tC + kHalf, &tm_bc, xc + NR / 2, ti, bb, bar);
+      if (p.complex_ssm) tma_load_3d(stg + PL::tW, &tm_th, offTh, ti, bb, bar);
+    } else {
+      mbar_arrive(bar);
+    }
+  };
+
+  if (warp >= 8) {
     // =============================== producers ===============================
-    const int ptid = tid - 128;
+    volatile int* abort_flag = prod_abort;
+    const int ptid = tid - kEpiThreads;
     const int nh2 = N / 2;
     int nseg = 1;
     while (nseg * 2 * nh2 <= kProdThreads && nseg * 2 <= L) nseg *= 2;
-    const int seglen = L / nseg;  // <= SEGMAX
+    const int seglen = N128 ? SEGMAX : L / nseg;  // N = 128: nseg = 4
     const bool bc_act = ptid < nh2 * nseg;
     const int pi = ptid % nh2, seg = ptid / nh2;
-    const int pc = ptid & 7;  // x-tile p-chunk
     float* nwB = reinterpret_cast<float*>(sm + PL::nrm);
     float* nwC = nwB + kNS * RP;
     float* nbB = nwC + kNS * RP;
     float* nbC = nbB + kNS * RP;
-    float* mxs = reinterpret_cast<float*>(sm + PL::mxs);
+    const float* sp = reinterpret_cast<const float*>(sm + PL::seqp);
+    constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
+    if (ptid == 0) {
+      if (G > 0) issue_stage(0);
+      if (G > 1) issue_stage(1);
+    }
+    // raw token scalars of chunk gg for token ptid (0..L; token L is the next chunk's first),
+    // loaded one chunk ahead of their use
+    struct TokRaw {
+      float dt, lam, rb, rc, dts;
+      bool ok;
+    };
+    auto load_tok = [&](int gg, TokRaw& tr) {
+      int sq, bb, hh, kk;
+      sc.at(gg, sq, bb, hh, kk);
+      const int gr = hh / (H / p.G);
+      const int64_t tt = (int64_t)kk * L + ptid;
+      tr.dt = tr.lam = tr.rb = tr.rc = 0.f;
+      tr.dts = 1.f;
+      tr.ok = ptid <= L && tt < a.T;
+      if (tr.ok) {
+        const TA* row = proj + ((int64_t)bb * a.T + tt) * a.proj_stride;
+        tr.dt = io<TA>::ld(row + offDt + hh);
+        if (p.trapezoidal) tr.lam = io<TA>::ld(row + offLam + hh);
+        if (a.dt_scale) tr.dts = io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + ((int64_t)bb * a.T + tt) * H + hh);
+        if (ptid < L) {
+          const float2 rr = *reinterpret_cast<const float2*>(a.rms + (((int64_t)bb * a.T + tt) * p.G + gr) * 2);
+          tr.rb = rr.x;
+          tr.rc = rr.y;
+        }
+      }
+    };
+    TokRaw nxt;
+    if (G > 0) load_tok(0, nxt);
     for (int g = 0; g < G; ++g) {
       const int s = g & 1;
       int seq, b, h, k;
@@ -245,25 +350,23 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           nbB[e] = ldf(p.B_bias, (int64_t)grp * NR + e, pd);
           nbC[e] = ldf(p.C_bias, (int64_t)grp * NR + e, pd);
         }
-        for (int e = ptid; e < kPP * RP; e += kProdThreads) {
-          const int pp = e / RP, q = e % RP;
-          mxs[e] = (pp < P && q < R) ? ldf(p.mimo_x, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
-        }
         if (ptid < nh2)
           omega[(g & 1) * 64 + ptid] = a.angle_init ? (double)a.angle_init[((int64_t)b * H + h) * nh2 + ptid] : 0.0;
         if (ptid == 0) {
-          float* sp = reinterpret_cast<float*>(sm + PL::seqp);
-          sp[0] = -expf(ldf(p.A_log, h, pd));
-          sp[1] = ldf(p.dt_bias, h, pd);
+          float* spw = reinterpret_cast<float*>(sm + PL::seqp);
+          spw[0] = -expf(ldf(p.A_log, h, pd));
+          spw[1] = ldf(p.dt_bias, h, pd);
         }
         named_bar(kBarProd, kProdThreads);  // the sequence's parameters are read below
       }
       if (ptid == 0) M3B_TL(g, 0);
-      if (g >= 2 && !role_wait(&bars[BAR_EMPTY0 + s], ((g >> 1) - 1) & 1, ptid == 0, kBarProd, kProdThreads,
-                               abort_flag, a.err))
+      // the stage is free (and on the TMA path its raw rows have landed)
+      if (!role_wait(&bars[BAR_STAGE0 + s], (g >> 1) & 1, ptid == 0, kBarProd, kProdThreads, abort_flag, a.err))
         break;
       if (ptid == 0) M3B_TL(g, 1);
       uint8_t* st = sm + s * PL::kStage;
+      const TokRaw cur = nxt;
+      if (g + 1 < G) load_tok(g + 1, nxt);
       float* scal = reinterpret_cast<float*>(sm + PL::scal + s * PL::scalStride);
       float* cum2 = scal;
       float* dtv = scal + NA;
@@ -273,8 +376,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       float* gbw = scal + 5 * NA;
       float* rmsB = scal + 6 * NA;
       float* rmsC = scal + 7 * NA;
-      // L2 prefetch of the projection rows the next chunk reads (B|C, x, z, dt|lam|theta)
-      if (g + 1 < G && ptid < 4 * L) {
+      // register path: L2 prefetch of the projection rows the next chunk reads (the TMA path
+      // starts its copies a chunk ahead, and the epilogue loads x and z ahead of use)
+      if (!TMA && g + 1 < G && ptid < 4 * L) {
         int seqn, bn, hn, kn;
         sc.at(g + 1, seqn, bn, hn, kn);
         const int64_t tn = (int64_t)kn * L + (ptid >> 2);
@@ -292,58 +396,45 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           }
         }
       }
-      // (0) every global load of this chunk, issued together: x rows, theta and the B/C rows of
-      // my segment, the token scalars.  One round trip covers the scalar and prefix phases.
-      Raw8<TA> xr[XU];
+      // (0) register path: the raw theta, B and C values of my segment, issued together
+      constexpr int SEGR = TMA ? 1 : SEGMAX;  // register-staged tokens (the TMA path reads shared memory)
+      float th[SEGR];
+      PairRaw<TA, R> vb[SEGR], vc[SEGR];
+      if constexpr (!TMA) {
+        const TA* thp = rowbase + offTh + pi;
 #pragma unroll
-      for (int jj = 0; jj < XU; ++jj) {
-        const int j = (ptid + kProdThreads * jj) >> 3;
-        const int64_t t = t0 + j;
-        if (t < a.T && pc * 8 < P) xr[jj].load(rowbase + t * a.proj_stride + HP + h * P + pc * 8);
-        else xr[jj].zero();
-      }
-      const TA* thp = rowbase + offTh + pi;
-      float th[SEGMAX];
+        for (int jj = 0; jj < SEGMAX; ++jj) {
+          const int64_t t = t0 + seg * seglen + jj;
+          th[jj] = (bc_act && p.complex_ssm && jj < seglen && t < a.T) ? io<TA>::ld(thp + t * a.proj_stride) : 0.f;
+        }
+        const TA* pB = rowbase + offB + grp * NR + 2 * pi * R;
+        const TA* pC = rowbase + offC + grp * NR + 2 * pi * R;
 #pragma unroll
-      for (int jj = 0; jj < SEGMAX; ++jj) {
-        const int64_t t = t0 + seg * seglen + jj;
-        th[jj] = (bc_act && p.complex_ssm && jj < seglen && t < a.T) ? io<TA>::ld(thp + t * a.proj_stride) : 0.f;
-      }
-      const TA* pB = rowbase + offB + grp * NR + 2 * pi * R;
-      const TA* pC = rowbase + offC + grp * NR + 2 * pi * R;
-      PairRaw<TA, R> vb[SEGMAX], vc[SEGMAX];
-#pragma unroll
-      for (int jj = 0; jj < SEGMAX; ++jj) {
-        const int64_t t = t0 + seg * seglen + jj;
-        if (bc_act && jj < seglen && t < a.T) {
-          vb[jj].load(pB + t * a.proj_stride);
-          vc[jj].load(pC + t * a.proj_stride);
-        } else {
-          vb[jj].zero();
-          vc[jj].zero();
+        for (int jj = 0; jj < SEGMAX; ++jj) {
+          const int64_t t = t0 + seg * seglen + jj;
+          if (bc_act && jj < seglen && t < a.T) {
+            vb[jj].load(pB + t * a.proj_stride);
+            vc[jj].load(pC + t * a.proj_stride);
+          } else {
+            vb[jj].zero();
+            vc[jj].zero();
+          }
         }
       }
-      float dt_raw = 0.f, lam_raw = 0.f, rb = 0.f, rc = 0.f;
-      const bool tok_act = ptid <= L && t0 + ptid < a.T;
-      if (tok_act) {
-        const TA* row = rowbase + (t0 + ptid) * a.proj_stride;
-        dt_raw = io<TA>::ld(row + offDt + h);
-        if (p.trapezoidal) lam_raw = io<TA>::ld(row + offLam + h);
-        if (ptid < L) {
-          const float* rr = a.rms + (((int64_t)b * a.T + t0 + ptid) * p.G + grp) * 2;
-          rb = rr[0];
-          rc = rr[1];
-        }
-      }
+      // theta of (token j of the chunk, my pair) from the TMA-staged W tile
+      const __nv_bfloat16* ths = reinterpret_cast<const __nv_bfloat16*>(st + PL::tW) + pi;
+      auto theta = [&](int jj) -> float {
+        if constexpr (TMA) return p.complex_ssm ? __bfloat162float(ths[(seg * SEGMAX + jj) * 64]) : 0.f;
+        else return th[jj];
+      };
+      if (ptid == 0) M3B_TL(g, 5);
       // (1) token scalars (token L is the next chunk's first token)
       if (ptid <= L) {
         float dt = 0.f, gmm = 0.f, bp = 0.f;
-        if (tok_act) {
-          dt = softplus_f(dt_raw + reinterpret_cast<const float*>(sm + PL::seqp)[1]);
-          if (a.dt_scale)
-            dt *= io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + ((int64_t)b * a.T + t0 + ptid) * H + h);
+        if (cur.ok) {
+          dt = softplus_f(cur.dt + sp[1]) * cur.dts;
           if (p.trapezoidal) {
-            const float lam = sigmoid_f(lam_raw);
+            const float lam = sigmoid_f(cur.lam);
             gmm = lam * dt;
             bp = (1.f - lam) * dt;
           } else {
@@ -354,15 +445,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         gam[ptid] = gmm;
         bpr[ptid] = bp;
         if (ptid < L) {
-          rmsB[ptid] = rb;
-          rmsC[ptid] = rc;
+          rmsB[ptid] = cur.rb;
+          rmsC[ptid] = cur.rc;
         }
       }
-      named_bar(kBarProd, kProdThreads);
+      if (ptid == 0) M3B_TL(g, 6);
+      named_bar(kBarProd, kProdThreads);  // scalars written
       if (ptid == 0) M3B_TL(g, 2);
       if (ptid < 32) {
         constexpr int PER = L / 32;
-        const float A = reinterpret_cast<const float*>(sm + PL::seqp)[0];
+        const float A = sp[0];
         float v[PER];
         float run = 0.f;
 #pragma unroll
@@ -384,9 +476,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       float segsum = 0.f;
 #pragma unroll
       for (int jj = 0; jj < SEGMAX; ++jj)
-        if (jj < seglen) segsum = fmaf(dtv[seg * seglen + jj], th[jj], segsum);
+        if (N128 || jj < seglen) segsum = fmaf(dtv[seg * seglen + jj], theta(jj), segsum);
       if (bc_act) segt[seg * nh2 + pi] = segsum;
       named_bar(kBarProd, kProdThreads);
+      if (ptid == 0) M3B_TL(g, 7);
       if (ptid < L) {
         const float gw = gam[ptid] + bpr[ptid + 1];
         gbw[ptid] = gw;
@@ -397,46 +490,95 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
         float off = 0.f;
         for (int q = 0; q < seg; ++q) off += segt[q * nh2 + pi];
         const double om = omega[(g & 1) * 64 + pi];
+        const float omf = (float)om;
         float run = off;
-        float wb0[RP], wb1[RP], bb0[RP], bb1[RP], wc0[RP], wc1[RP], bc0[RP], bc1[RP];
+        // norm weight / bias of (n = 2i + e, r) as r-pairs (R even) or n-pairs (R = 1)
+        float2 wB0[RP / 2 + 1], wB1[RP / 2 + 1], bB0[RP / 2 + 1], bB1[RP / 2 + 1];
+        float2 wC0[RP / 2 + 1], wC1[RP / 2 + 1], bC0[RP / 2 + 1], bC1[RP / 2 + 1];
+        if constexpr (R % 2 == 0) {
 #pragma unroll
-        for (int r = 0; r < RP; ++r) {
-          const int i0 = 2 * pi * R + (r < R ? r : 0), i1 = i0 + R;  // flat (n, r) of n = 2i, 2i+1
-          wb0[r] = nwB[i0];
-          wb1[r] = nwB[i1];
-          bb0[r] = nbB[i0];
-          bb1[r] = nbB[i1];
-          wc0[r] = nwC[i0];
-          wc1[r] = nwC[i1];
-          bc0[r] = nbC[i0];
-          bc1[r] = nbC[i1];
+          for (int rp = 0; rp < R / 2; ++rp) {
+            const int i0 = 2 * pi * R + 2 * rp, i1 = i0 + R;
+            wB0[rp] = make_float2(nwB[i0], nwB[i0 + 1]);
+            wB1[rp] = make_float2(nwB[i1], nwB[i1 + 1]);
+            bB0[rp] = make_float2(nbB[i0], nbB[i0 + 1]);
+            bB1[rp] = make_float2(nbB[i1], nbB[i1 + 1]);
+            wC0[rp] = make_float2(nwC[i0], nwC[i0 + 1]);
+            wC1[rp] = make_float2(nwC[i1], nwC[i1 + 1]);
+            bC0[rp] = make_float2(nbC[i0], nbC[i0 + 1]);
+            bC1[rp] = make_float2(nbC[i1], nbC[i1 + 1]);
+          }
+        } else {
+          wB0[0] = make_float2(nwB[2 * pi], nwB[2 * pi + 1]);
+          bB0[0] = make_float2(nbB[2 * pi], nbB[2 * pi + 1]);
+          wC0[0] = make_float2(nwC[2 * pi], nwC[2 * pi + 1]);
+          bC0[0] = make_float2(nbC[2 * pi], nbC[2 * pi + 1]);
         }
+        // raw (2i, 2i+1) x R blocks: registers, or shared memory (TMA path), where the whole warp
+        // reads a group of TG tokens before any lane overwrites them with tile entries
+        constexpr int TG = TMA ? 4 : 1;
+        PairRaw<TA, R> grb[TG], grc[TG];
 #pragma unroll
         for (int jj = 0; jj < SEGMAX; ++jj) {
-          if (jj >= seglen) break;
+          if (!N128 && jj >= seglen) break;
           const int j = seg * seglen + jj;
           const bool valid = t0 + j < a.T;
+          if constexpr (TMA) {
+            if (jj % TG == 0) {
+#pragma unroll
+              for (int u = 0; u < TG; ++u) {
+                const uint8_t* src = st + (pi >> 5) * 16384 + (j + u) * (RP * 128) + (pi & 31) * (R * 4);
+                grb[u].load_shared(src + PL::tB);
+                grc[u].load_shared(src + PL::tC);
+              }
+              __syncwarp();
+            }
+          }
+          const PairRaw<TA, R>& rawb = TMA ? grb[jj % TG] : vb[jj];
+          const PairRaw<TA, R>& rawc = TMA ? grc[jj % TG] : vc[jj];
           float cs = 1.f, sn = 0.f;
           if (p.complex_ssm) {
-            run = fmaf(dtv[j], th[jj], run);
-            sincos_reduced((float)(om - (double)run), &sn, &cs);
+            run = fmaf(dtv[j], theta(jj), run);
+            sincos_reduced(omf - run, &sn, &cs);
           }
-          const float rbj = rmsB[j], rcj = rmsC[j];
-          if (ptid == 0 && jj == 4) M3B_TL(g, 15);
+          const float2 rbj = make_float2(rmsB[j], rmsB[j]), rcj = make_float2(rmsC[j], rmsC[j]);
+          uint32_t ob[RP], oc[RP];
+          if constexpr (R % 2 == 0) {
+            const float2 c2 = make_float2(cs, cs), s2 = make_float2(sn, sn), ns2 = make_float2(-sn, -sn);
+#pragma unroll
+            for (int rp = 0; rp < R / 2; ++rp) {
+              // x0 = element n = 2i, x1 = n = 2i+1, both for ranks (2 rp, 2 rp + 1)
+              const float2 b0 = fma2(rawb.pair(2 * rp), mul2(rbj, wB0[rp]), bB0[rp]);
+              const float2 b1 = fma2(rawb.pair(R + 2 * rp), mul2(rbj, wB1[rp]), bB1[rp]);
+              const float2 c0 = fma2(rawc.pair(2 * rp), mul2(rcj, wC0[rp]), bC0[rp]);
+              const float2 c1 = fma2(rawc.pair(R + 2 * rp), mul2(rcj, wC1[rp]), bC1[rp]);
+              const float2 be = fma2(b1, ns2, mul2(b0, c2)), bo = fma2(b1, c2, mul2(b0, s2));
+              const float2 ce = fma2(c1, ns2, mul2(c0, c2)), co = fma2(c1, c2, mul2(c0, s2));
+              ob[2 * rp] = valid ? pack_bf16x2(be.x, bo.x) : 0u;
+              ob[2 * rp + 1] = valid ? pack_bf16x2(be.y, bo.y) : 0u;
+              oc[2 * rp] = valid ? pack_bf16x2(ce.x, co.x) : 0u;
+              oc[2 * rp + 1] = valid ? pack_bf16x2(ce.y, co.y) : 0u;
+            }
+#pragma unroll
+            for (int r = R; r < RP; ++r) ob[r] = oc[r] = 0u;
+          } else {
+            // R = 1: the pair (n = 2i, 2i+1) is one float2
+            const float2 bv = fma2(rawb.pair(0), mul2(rbj, wB0[0]), bB0[0]);
+            const float2 cv = fma2(rawc.pair(0), mul2(rcj, wC0[0]), bC0[0]);
+            // (x0 c - x1 s, x0 s + x1 c) = x1 * (-s, c) + x0 * (c, s)
+            const float2 ncs = make_float2(-sn, cs), csn = make_float2(cs, sn);
+            const float2 be = fma2(make_float2(bv.y, bv.y), ncs, mul2(make_float2(bv.x, bv.x), csn));
+            const float2 ce = fma2(make_float2(cv.y, cv.y), ncs, mul2(make_float2(cv.x, cv.x), csn));
+            ob[0] = valid ? pack_bf16x2(be.x, be.y) : 0u;
+            oc[0] = valid ? pack_bf16x2(ce.x, ce.y) : 0u;
+#pragma unroll
+            for (int r = 1; r < RP; ++r) ob[r] = oc[r] = 0u;
+          }
 #pragma unroll
           for (int r = 0; r < RP; ++r) {
-            uint32_t ob = 0, oc = 0;
-            if (r < R && valid) {
-              const float b0 = fmaf(vb[jj].get(r) * rbj, wb0[r], bb0[r]);
-              const float b1 = fmaf(vb[jj].get(R + r) * rbj, wb1[r], bb1[r]);
-              const float c0 = fmaf(vc[jj].get(r) * rcj, wc0[r], bc0[r]);
-              const float c1 = fmaf(vc[jj].get(R + r) * rcj, wc1[r], bc1[r]);
-              ob = pack_bf16x2(b0 * cs - b1 * sn, b0 * sn + b1 * cs);
-              oc = pack_bf16x2(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
-            }
             const uint32_t o = sw128_offset(j * RP + r, 2 * pi, 128);
-            *reinterpret_cast<uint32_t*>(st + PL::tB + o) = ob;
-            *reinterpret_cast<uint32_t*>(st + PL::tC + o) = oc;
+            *reinterpret_cast<uint32_t*>(st + PL::tB + o) = ob[r];
+            *reinterpret_cast<uint32_t*>(st + PL::tC + o) = oc[r];
           }
         }
         if (seg == nseg - 1) {
@@ -453,100 +595,95 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
           sw128_store_chunk(st + PL::tB, u / ncz, c0 + u % ncz, 128, make_uint4(0, 0, 0, 0));
       }
       if (ptid == 0) M3B_TL(g, 3);
-      named_bar(kBarProd, kProdThreads);  // wst ready
-      // (3) X and w X tiles from the prefetched x rows: row (s*RP + q), column p
+      fence_async_smem();
+      named_bar(kBarProd, kProdThreads);  // B^, C^ tiles and the token scalars (wst, gbw) complete
+      if (ptid == 0) {
+        mbar_arrive(&bars[BAR_FULL0 + s]);
+        // S_g = C^ B^T into S[g%2] (free: the epilogue released this stage before handing it over)
+        tc_fence_after();
+        const uint32_t cs0 = kColS + 128 * s;
 #pragma unroll
-      for (int jj = 0; jj < XU; ++jj) {
-        const int j = (ptid + kProdThreads * jj) >> 3;
-        const float w = wst[j];
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tbase + cs0, kmajor_desc(st + PL::tC, 128, kk * 16), kmajor_desc(st + PL::tB, 128, kk * 16),
+                    idS, kk > 0 ? 1u : 0u);
+        umma_commit(&bars[BAR_SDONE0 + s]);
+        M3B_TL(g, 4);
+      }
+    }
+  } else {
+    // =============================== epilogue ===============================
+    volatile int* abort_flag = epi_abort;
+    const int lq = warp & 3, ch = warp >> 2;  // TMEM lane quadrant, column half
+    const int m = 32 * lq + lane;             // TMEM lane = tile row (t, r)
+    const int t = m / RP, r = m % RP;
+    const uint32_t trow = tbase + ((uint32_t)(32 * lq) << 16);
+    uint8_t* tileH = sm + PL::tileH;
+    // mimo_z, mimo_down, mimo_x of the current sequence, rank-major: [q][p]
+    float* emz = reinterpret_cast<float*>(sm + PL::epar);
+    float* emd = emz + kPP * RP;
+    float* emx = reinterpret_cast<float*>(sm + PL::mxs);
+    const bool lead = tid == 0;
+    const int xpc = tid & 7;  // X / W tiles: this thread's 8-column chunk of p
+    // x of chunk gg, rows j = (tid + 256 u) / 8 (loaded a chunk ahead of the X / W tiles)
+    auto load_x = [&](int gg, Raw8<TA> (&xr)[XU]) {
+      int sq, bb, hh, kk;
+      sc.at(gg, sq, bb, hh, kk);
+      const TA* xb = proj + (int64_t)bb * a.T * a.proj_stride + HP + (int64_t)hh * P + xpc * 8;
+#pragma unroll
+      for (int u = 0; u < XU; ++u) {
+        const int64_t tt = (int64_t)kk * L + ((tid + kEpiThreads * u) >> 3);
+        if (tt < a.T && xpc * 8 < P) xr[u].load(xb + tt * a.proj_stride);
+        else xr[u].zero();
+      }
+    };
+    // X (rows (s, q) = x_s * mimo_x[:, q]) and W = wst_s X tiles of chunk gg; its token scalars
+    // are in place (FULL of gg has completed) and mimo_x is the current sequence's
+    auto build_xw = [&](int gg, const Raw8<TA> (&xr)[XU]) {
+      uint8_t* stg = sm + (gg & 1) * PL::kStage;
+      const float* wsg = reinterpret_cast<const float*>(sm + PL::scal + (gg & 1) * PL::scalStride) + 4 * NA;
+#pragma unroll
+      for (int u = 0; u < XU; ++u) {
+        const int j = (tid + kEpiThreads * u) >> 3;
+        const float2 w2 = make_float2(wsg[j], wsg[j]);
 #pragma unroll
         for (int q = 0; q < RP; ++q) {
-          float v[8];
+          const float4* mx4 = reinterpret_cast<const float4*>(emx + q * kPP + xpc * 8);
+          const float4 ma = mx4[0], mb = mx4[1];
+          const float2 mxp[4] = {make_float2(ma.x, ma.y), make_float2(ma.z, ma.w), make_float2(mb.x, mb.y),
+                                 make_float2(mb.z, mb.w)};
+          uint4 ox, ow;
+          uint32_t* oxw = reinterpret_cast<uint32_t*>(&ox);
+          uint32_t* oww = reinterpret_cast<uint32_t*>(&ow);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = xr[jj].get(e) * mxs[(pc * 8 + e) * RP + q];
-          uint4 o1, o2;
-          o1.x = pack_bf16x2(v[0], v[1]);
-          o1.y = pack_bf16x2(v[2], v[3]);
-          o1.z = pack_bf16x2(v[4], v[5]);
-          o1.w = pack_bf16x2(v[6], v[7]);
-          o2.x = pack_bf16x2(v[0] * w, v[1] * w);
-          o2.y = pack_bf16x2(v[2] * w, v[3] * w);
-          o2.z = pack_bf16x2(v[4] * w, v[5] * w);
-          o2.w = pack_bf16x2(v[6] * w, v[7] * w);
-          sw128_store_chunk(st + PL::tX, j * RP + q, pc, 128, o1);
-          sw128_store_chunk(st + PL::tW, j * RP + q, pc, 128, o2);
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const float2 v = mul2(xr[u].pair(2 * e2), mxp[e2]);
+            const float2 vw = mul2(v, w2);
+            oxw[e2] = pack_bf16x2(v.x, v.y);
+            oww[e2] = pack_bf16x2(vw.x, vw.y);
+          }
+          sw128_store_chunk(stg + PL::tX, j * RP + q, xpc, 128, ox);
+          sw128_store_chunk(stg + PL::tW, j * RP + q, xpc, 128, ow);
         }
       }
-      fence_async_smem();
-      named_bar(kBarProd, kProdThreads);
-      if (ptid == 0) mbar_arrive(&bars[BAR_FULL0 + s]);
-      if (ptid == 0) M3B_TL(g, 4);
-    }
-  } else if (warp == kMmaWarp) {
-    // =============================== MMA issue ===============================
-    if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
-      constexpr uint32_t idYi = idesc_bf16(128, kPP, false, true);
-      constexpr uint32_t idH = idesc_bf16(128, kPP, true, true);
-      constexpr uint32_t idY = idesc_bf16(128, kPP, false, true);
-      uint8_t* tileH = sm + PL::tileH;
-      for (int g = 0; g < G; ++g) {
-        const int s = g & 1;
-        uint8_t* st = sm + s * PL::kStage;
-        if (*abort_flag) break;
-        if (!mbar_wait(&bars[BAR_FULL0 + s], (g >> 1) & 1)) {
-          *abort_flag = 1;
-          record_error(a.err, M3B_ERR_TIMEOUT);
-          break;
-        }
-        tc_fence_after();
-        M3B_TL(g, 5);
+    };
+    constexpr uint32_t idO = idesc_bf16(128, kPP, false, true);  // Yi and Y: B operand MN-major
+    constexpr uint32_t idH = idesc_bf16(128, kPP, true, true);   // H: A and B MN-major
+    // leader: Yi_g = C^ H'^T and H += B^^T (w X) for chunk g, then commit HDONE
+    auto issue_state_mma = [&](int g) {
+      const int s = g & 1;
+      uint8_t* st = sm + s * PL::kStage;
+      tc_fence_after();
+      const uint32_t cyi = kColYi + 64 * s;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tbase + kColS, kmajor_desc(st + PL::tC, 128, kk * 16), kmajor_desc(st + PL::tB, 128, kk * 16),
-                    idS, kk > 0 ? 1u : 0u);
-        if (!mbar_wait(&bars[BAR_HREADY], g & 1)) {
-          *abort_flag = 1;
-          record_error(a.err, M3B_ERR_TIMEOUT);
-          break;
-        }
-        tc_fence_after();
-        M3B_TL(g, 6);
-        const uint32_t cyi = kColYi + 64 * (g & 1);
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tbase + cyi, kmajor_desc(st + PL::tC, 128, kk * 16), mnmajor_desc(tileH, 128, kk * 16), idO,
+                  kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tbase + cyi, kmajor_desc(st + PL::tC, 128, kk * 16), mnmajor_desc(tileH, 128, kk * 16), idYi,
-                    kk > 0 ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tbase + kColH, mnmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(st + PL::tW, 128, kk * 16),
-                    idH, 1u);
-        umma_commit(&bars[BAR_SMMA]);
-        if (!mbar_wait(&bars[BAR_PREADY], g & 1)) {
-          *abort_flag = 1;
-          record_error(a.err, M3B_ERR_TIMEOUT);
-          break;
-        }
-        tc_fence_after();
-        M3B_TL(g, 7);
-        const uint32_t cy = kColY + 64 * (g & 1);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tbase + cy, kmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(st + PL::tX, 128, kk * 16), idY,
-                    kk > 0 ? 1u : 0u);
-        umma_commit(&bars[BAR_YMMA]);
-      }
-    }
-    __syncwarp();  // reconverge before the CTA-wide barrier below
-  } else if (warp < 4) {
-    // =============================== epilogue ===============================
-    const int m = tid;  // TMEM lane = tile row (t, r)
-    const int t = m / RP, r = m % RP;
-    const uint32_t trow = tbase + ((uint32_t)(32 * warp) << 16);
-    uint8_t* tileH = sm + PL::tileH;
-    float* emz = reinterpret_cast<float*>(sm + PL::epar);  // mimo_z, mimo_down of the current sequence
-    float* emd = emz + kPP * RP;
-    const bool lead = m == 0;
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tbase + kColH, mnmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(st + PL::tW, 128, kk * 16),
+                  idH, 1u);
+      umma_commit(&bars[BAR_HDONE]);
+    };
     // H'_0 of the sequence starting at chunk gs -> bf16 tile row n = m, and H = d * H'_0 in TMEM
     auto state_init = [&](int gs) -> bool {
       int seq, b, h, k;
@@ -558,40 +695,37 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       const float d = exp2f(scal[L - 1]);
       const float c0 = scal[3 * NA];  // (1-lam_0) dt_0
       const int64_t base = ((int64_t)b * H + h) * (int64_t)P * N;
+      float hv[32];
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        float hv[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int pp = 32 * hf + e;
-          float v = 0.f;
-          if (m < N && pp < P) {
-            if (a.h_init) v = a.h_init[base + (int64_t)pp * N + m];
-            if (a.prev_bx_init) v = fmaf(c0, a.prev_bx_init[base + (int64_t)pp * N + m], v);
-          }
-          hv[e] = v;
+      for (int e = 0; e < 32; ++e) {
+        const int pp = 32 * ch + e;
+        float v = 0.f;
+        if (m < N && pp < P) {
+          if (a.h_init) v = a.h_init[base + (int64_t)pp * N + m];
+          if (a.prev_bx_init) v = fmaf(c0, a.prev_bx_init[base + (int64_t)pp * N + m], v);
         }
-#pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          uint4 o;
-          o.x = pack_bf16x2(hv[8 * c8 + 0], hv[8 * c8 + 1]);
-          o.y = pack_bf16x2(hv[8 * c8 + 2], hv[8 * c8 + 3]);
-          o.z = pack_bf16x2(hv[8 * c8 + 4], hv[8 * c8 + 5]);
-          o.w = pack_bf16x2(hv[8 * c8 + 6], hv[8 * c8 + 7]);
-          sw128_store_chunk(tileH, m, 4 * hf + c8, 128, o);
-        }
-#pragma unroll
-        for (int e = 0; e < 32; ++e) hv[e] *= d;
-        tmem_st32(trow + kColH + 32 * hf, hv);
+        hv[e] = v;
       }
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        float v8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v8[e] = hv[8 * c8 + e];
+        st_pack_chunk(tileH, m, 4 * ch + c8, v8);
+      }
+#pragma unroll
+      for (int e = 0; e < 32; ++e) hv[e] *= d;
+      tmem_st32(trow + kColH + 32 * ch, hv);
       // this sequence's gate parameters (the previous sequence's last output is complete)
       const int pd = p.param_dtype;
-      for (int e = m; e < kPP * RP; e += kEpiThreads) {
+      for (int e = tid; e < kPP * RP; e += kEpiThreads) {
         const int pp = e / RP, q = e % RP;
         const bool okp = pp < P && q < R;
-        emz[e] = okp ? ldf(p.mimo_z, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
-        emd[e] = okp ? ldf(p.mimo_down, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
+        emz[q * kPP + pp] = okp ? ldf(p.mimo_z, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
+        emd[q * kPP + pp] = okp ? ldf(p.mimo_down, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
+        emx[q * kPP + pp] = okp ? ldf(p.mimo_x, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
       }
+      named_bar(kBarEpi, kEpiThreads);  // mimo_x is read by the X / W tiles below
       return true;
     };
     auto write_h_final = [&](int glast) {
@@ -599,25 +733,25 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       int seq, b, h, k;
       sc.at(glast, seq, b, h, k);
       const int64_t base = ((int64_t)b * H + h) * (int64_t)P * N;
+      float v[32];
+      tmem_ld32(trow + kColH + 32 * ch, v);
+      if (m < N) {
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        float v[32];
-        tmem_ld32(trow + kColH + 32 * hf, v);
-        if (m < N) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int pp = 32 * hf + e;
-            if (pp < P) a.h_final[base + (int64_t)pp * N + m] = v[e];
-          }
+        for (int e = 0; e < 32; ++e) {
+          const int pp = 32 * ch + e;
+          if (pp < P) a.h_final[base + (int64_t)pp * N + m] = v[e];
         }
       }
     };
+    Raw8<TA> xn[XU];  // x of the next chunk
+    if (G > 0) load_x(0, xn);
     bool ok = G > 0 && state_init(0);
     if (ok) {
+      build_xw(0, xn);
       fence_async_smem();
       tc_fence_before();
       named_bar(kBarEpi, kEpiThreads);
-      if (lead) mbar_arrive(&bars[BAR_HREADY]);
+      if (lead) issue_state_mma(0);
     }
     for (int g = 0; ok && g < G; ++g) {
       const int s = g & 1;
@@ -628,45 +762,93 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       const float* cum2 = scal;
       const float* gam = scal + 2 * NA;
       const float* gbw = scal + 5 * NA;
-      // z of this chunk's row (t, r), prefetched while the tensor core works
+      const uint32_t cs0 = kColS + 128 * s;
+      if (g + 1 < G) load_x(g + 1, xn);
+      // z of this thread's row (t, r) and column half, prefetched while the tensor core works
       const int64_t tok = (int64_t)k * L + t;
       const bool row_ok = tok < a.T && r < R;
-      Raw8<TA> zr[8];
+      Raw8<TA> zr[4];
       {
-        const TA* zrow = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride + (int64_t)h * P;
+        const TA* zrow = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride + (int64_t)h * P + 32 * ch;
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          if (row_ok && c8 * 8 < P) zr[c8].load(zrow + c8 * 8);
+        for (int c8 = 0; c8 < 4; ++c8) {
+          if (row_ok && 32 * ch + c8 * 8 < P) zr[c8].load(zrow + c8 * 8);
           else zr[c8].zero();
         }
       }
-      if (!(ok = role_wait(&bars[BAR_SMMA], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
+      // S_g (producer) and Yi_g / H update (this role) must be complete before P overwrites B^
+      if (lead && !*abort_flag) {
+        if (!mbar_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1) || !mbar_wait(&bars[BAR_HDONE], g & 1)) {
+          *abort_flag = 1;
+          record_error(a.err, M3B_ERR_TIMEOUT);
+        }
+      }
+      __syncwarp();
+      named_bar(kBarEpi, kEpiThreads);
+      if (*abort_flag) break;
       tc_fence_after();
       if (lead) M3B_TL(g, 8);
-      // ---- mask: P[m, (s,q)] = S * exp(cum_t - cum_s) * (s<t ? gamma_s + (1-lam_{s+1})dt_{s+1} : gamma_s)
+      // ---- mask.  The intra-chunk weight of (token t, source s <= t) is
+      //   w(t, s) = 2^(cum_t - cum_s) * (s < t ? gamma_s + (1-lam_{s+1}) dt_{s+1} : gamma_s).
+      // Separable form (the chunk's decay range cum_0 - cum_{L-1} <= kSepRange): for s < t,
+      // w = e_t * wst_s with e_t = 2^(cum_t - cum_{L-1}) and wst_s the state-update weight, so
+      // Y = diag(e) * P' * W with P' = S masked (s < t: S; s = t: S gamma_t / gbw_t; s > t: 0)
+      // and W the chunk-state tile: no per-element exponentials.  Otherwise P = S * w, Y = P X.
+      // Column block blk (32 columns) of warp quadrant lq lies below (blk < lq), on (blk == lq)
+      // or above (blk > lq) the block diagonal, for every lane alike.
+      constexpr float kSepRange = 64.f;
+      const float c_last = cum2[L - 1];
+      const bool sep = cum2[0] - c_last <= kSepRange;
       {
         const float ct = cum2[t];
+        const float gwt = gbw[t];
+        const float rat = gwt > 0.f ? gam[t] / gwt : 0.f;
 #pragma unroll
-        for (int c32 = 0; c32 < 4; ++c32) {
+        for (int c32 = 0; c32 < 2; ++c32) {
+          const int blk = 2 * ch + c32;
+          const int c0 = 32 * blk;
           float v[32];
-          tmem_ld32(trow + kColS + 32 * c32, v);
-          if (lead && c32 == 0) M3B_TL(g, 13);
+          if (blk > lq) {
 #pragma unroll
-          for (int jj = 0; jj < 32; jj += RP) {
-            const int sj = (32 * c32 + jj) / RP;
-            const float e = ex2_fast(fminf(ct - cum2[sj], 0.f));
-            const float w = sj < t ? e * gbw[sj] : (sj == t ? gam[sj] : 0.f);
+            for (int e = 0; e < 32; ++e) v[e] = 0.f;
+          } else {
+            tmem_ld32(trow + cs0 + c0, v);
+            if (lead && c32 == 0) M3B_TL(g, 13);
+            if (sep) {
+              if (blk == lq) {
 #pragma unroll
-            for (int q = 0; q < RP; ++q) v[jj + q] *= w;
+                for (int jj = 0; jj < 32; jj += RP) {
+                  const int sj = (c0 + jj) / RP;
+                  const float f = sj < t ? 1.f : (sj == t ? rat : 0.f);
+#pragma unroll
+                  for (int q = 0; q < RP; ++q) v[jj + q] *= f;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 32; jj += RP) {
+                const int sj = (c0 + jj) / RP;
+                const float e = ex2_fast(fminf(ct - cum2[sj], 0.f));
+                const float w = sj < t ? e * gbw[sj] : (sj == t ? gam[sj] : 0.f);
+                if constexpr (RP >= 2) {
+#pragma unroll
+                  for (int q = 0; q < RP; q += 2) {
+                    const float2 pr = mul2(make_float2(v[jj + q], v[jj + q + 1]), make_float2(w, w));
+                    v[jj + q] = pr.x;
+                    v[jj + q + 1] = pr.y;
+                  }
+                } else {
+                  v[jj] *= w;
+                }
+              }
+            }
           }
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
-            uint4 o;
-            o.x = pack_bf16x2(v[8 * cc + 0], v[8 * cc + 1]);
-            o.y = pack_bf16x2(v[8 * cc + 2], v[8 * cc + 3]);
-            o.z = pack_bf16x2(v[8 * cc + 4], v[8 * cc + 5]);
-            o.w = pack_bf16x2(v[8 * cc + 6], v[8 * cc + 7]);
-            sw128_store_chunk(st + PL::tB, m, 4 * c32 + cc, 128, o);
+            float v8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v8[e] = v[8 * cc + e];
+            st_pack_chunk(st + PL::tB, m, c0 / 8 + cc, v8);
           }
           if (lead && c32 == 0) M3B_TL(g, 14);
         }
@@ -674,34 +856,56 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       fence_async_smem();
       tc_fence_before();
       named_bar(kBarEpi, kEpiThreads);
-      if (lead) mbar_arrive(&bars[BAR_PREADY]);
-      if (lead) M3B_TL(g, 9);
+      if (lead) {
+        // Y_g = P' W (separable) or P X into the first 64 columns of S[g%2] (the mask has consumed S_g)
+        tc_fence_after();
+        const uint8_t* yb = st + (sep ? PL::tW : PL::tX);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tbase + cs0, kmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(yb, 128, kk * 16), idO,
+                    kk > 0 ? 1u : 0u);
+        umma_commit(&bars[BAR_YDONE]);
+        M3B_TL(g, 9);
+      }
       // ---- output of chunk g (x_r comes from the X tile of this stage)
-      if (!(ok = role_wait(&bars[BAR_YMMA], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
+      if (!(ok = role_wait(&bars[BAR_YDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
       tc_fence_after();
       if (lead) M3B_TL(g, 10);
       {
         const float ec = exp2f(cum2[t]);
+        const float et = sep ? exp2f(cum2[t] - c_last) : 1.f;
         const float Dh = ldf(p.D, h, p.param_dtype);
+        const float2 et2 = make_float2(et, et), ec2 = make_float2(ec, ec), D2 = make_float2(Dh, Dh);
         TA* yo = reinterpret_cast<TA*>(a.y) + ((int64_t)b * a.T + tok) * HP + (int64_t)h * P;
-        const uint32_t cy = kColY + 64 * (g & 1), cyi = kColYi + 64 * (g & 1);
+        const uint32_t cyi = kColYi + 64 * s;
 #pragma unroll
-        for (int qq = 0; qq < 4; ++qq) {
+        for (int qq = 0; qq < 2; ++qq) {
           float Y[16], Yi[16];
-          tmem_ld16(trow + cy + 16 * qq, Y);
-          tmem_ld16(trow + cyi + 16 * qq, Yi);
+          tmem_ld16(trow + cs0 + 32 * ch + 16 * qq, Y);
+          tmem_ld16(trow + cyi + 32 * ch + 16 * qq, Yi);
           float acc[16];
 #pragma unroll
           for (int hc = 0; hc < 2; ++hc) {
-            const int c8 = 2 * qq + hc;
-            const uint4 xq = *reinterpret_cast<const uint4*>(st + PL::tX + sw128_offset(m, c8 * 8, 128));
+            const int c8 = 2 * qq + hc;  // chunk within this column half
+            const int p8 = 32 * ch + c8 * 8;
+            const uint4 xq = *reinterpret_cast<const uint4*>(st + PL::tX + sw128_offset(m, p8, 128));
             const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
+            const float4* mz4 = reinterpret_cast<const float4*>(emz + r * kPP + p8);
+            const float4* md4 = reinterpret_cast<const float4*>(emd + r * kPP + p8);
+            const float4 za = mz4[0], zb = mz4[1], da = md4[0], db = md4[1];
+            const float2 mzp[4] = {make_float2(za.x, za.y), make_float2(za.z, za.w), make_float2(zb.x, zb.y),
+                                   make_float2(zb.z, zb.w)};
+            const float2 mdp[4] = {make_float2(da.x, da.y), make_float2(da.z, da.w), make_float2(db.x, db.y),
+                                   make_float2(db.z, db.w)};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int pp = c8 * 8 + e;
-              const float xr = __uint_as_float((e & 1) ? (xw[e >> 1] & 0xffff0000u) : (xw[e >> 1] << 16));
-              const float zz = zr[c8].get(e) * emz[pp * RP + r];
-              acc[8 * hc + e] = (Y[8 * hc + e] + ec * Yi[8 * hc + e] + Dh * xr) * silu_fast(zz) * emd[pp * RP + r];
+            for (int e2 = 0; e2 < 4; ++e2) {
+              const int i = 8 * hc + 2 * e2;
+              const float2 yv = fma2(et2, make_float2(Y[i], Y[i + 1]),
+                                     fma2(ec2, make_float2(Yi[i], Yi[i + 1]), mul2(D2, bf2_to_f2(xw[e2]))));
+              const float2 gz = silu_fast2(mul2(zr[c8].pair(2 * e2), mzp[e2]));
+              const float2 o = mul2(mul2(yv, gz), mdp[e2]);
+              acc[i] = o.x;
+              acc[i + 1] = o.y;
             }
           }
 #pragma unroll
@@ -714,7 +918,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
 #pragma unroll
             for (int rr = 0; rr < RP; ++rr) {
               if (rr != r) continue;
-              const int p0 = 16 * qq + rr * W;
+              const int p0 = 32 * ch + 16 * qq + rr * W;
               if constexpr (W == 16) {
                 if (p0 + 16 <= P) {
                   float o8[8];
@@ -745,7 +949,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
       tc_fence_before();
       mbar_arrive(&bars[BAR_EMPTY0 + s]);
       if (lead) M3B_TL(g, 11);
-      // ---- state for chunk g+1: H'_{g+1} -> bf16 tile, H *= d_{g+1}
+      // every epilogue thread is done with stage s for chunk g: hand it over for chunk g + 2
+      if (lead && g + 2 < G && !*abort_flag) {
+        if (mbar_wait(&bars[BAR_EMPTY0 + s], (g >> 1) & 1)) {
+          issue_stage(g + 2);
+        } else {
+          *abort_flag = 1;
+          record_error(a.err, M3B_ERR_TIMEOUT);
+        }
+      }
+      // ---- state for chunk g+1: H'_{g+1} -> bf16 tile, H *= d_{g+1}; then Yi_{g+1}, H += ...
       if (g + 1 < G) {
         int seq1, b1, h1, k1;
         sc.at(g + 1, seq1, b1, h1, k1);
@@ -759,29 +972,27 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
             break;
           const float* scal1 = reinterpret_cast<const float*>(sm + PL::scal + s1 * PL::scalStride);
           const float d = exp2f(scal1[L - 1]);
+          float v[32];
+          tmem_ld32(trow + kColH + 32 * ch, v);
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            float v[32];
-            tmem_ld32(trow + kColH + 32 * hf, v);
+          for (int c8 = 0; c8 < 4; ++c8) {
+            float v8[8];
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-              uint4 o;
-              o.x = pack_bf16x2(v[8 * c8 + 0], v[8 * c8 + 1]);
-              o.y = pack_bf16x2(v[8 * c8 + 2], v[8 * c8 + 3]);
-              o.z = pack_bf16x2(v[8 * c8 + 4], v[8 * c8 + 5]);
-              o.w = pack_bf16x2(v[8 * c8 + 6], v[8 * c8 + 7]);
-              sw128_store_chunk(tileH, m, 4 * hf + c8, 128, o);
-            }
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] *= d;
-            tmem_st32(trow + kColH + 32 * hf, v);
+            for (int e = 0; e < 8; ++e) v8[e] = v[8 * c8 + e];
+            st_pack_chunk(tileH, m, 4 * ch + c8, v8);
           }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] *= d;
+          tmem_st32(trow + kColH + 32 * ch, v);
         }
+        build_xw(g + 1, xn);
         fence_async_smem();
         tc_fence_before();
         named_bar(kBarEpi, kEpiThreads);
-        if (lead) mbar_arrive(&bars[BAR_HREADY]);
-        if (lead) M3B_TL(g, 12);
+        if (lead) {
+          issue_state_mma(g + 1);
+          M3B_TL(g, 12);
+        }
       } else {
         write_h_final(g);
       }
@@ -789,7 +1000,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ssd_fused_kernel(FusedParams
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tbase, 512);
   }
@@ -812,23 +1023,74 @@ int ensure_smem_f(const void* kernel, int bytes) {
   return M3B_OK;
 }
 
-template <typename TA, int R>
-int launch_fused_t(const FusedParams& fp, cudaStream_t st) {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver the runtime is bound to (no link-time libcuda dependency).
+EncodeTiledFn encode_tiled() {
+  static const EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// 3-D bf16 map over the projection (columns, tokens, batch rows) with box (box0, box1, 1); tokens
+// past T read as zeros.  False when the driver refuses the encoding.
+bool make_proj_map(CUtensorMap* m, const FusedParams& fp, uint32_t box0, uint32_t box1) {
+  const EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)fp.proj_stride, (cuuint64_t)fp.T, (cuuint64_t)fp.B};
+  const cuuint64_t strides[2] = {(cuuint64_t)fp.proj_stride * 2, (cuuint64_t)fp.proj_stride * 2 * (cuuint64_t)fp.T};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(fp.proj), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The TMA producer path needs N = 128 and 16-byte aligned rows and column offsets of B, C and theta.
+bool tma_layout_ok(const FusedParams& fp) {
+  const m3b_layer_params& p = fp.prm;
+  const int64_t HP = (int64_t)p.H * p.P, NR = (int64_t)p.N * p.R;
+  const int64_t offB = 2 * HP, offTh = offB + 2 * p.G * NR + p.H + (p.trapezoidal ? p.H : 0);
+  return p.N == 128 && (reinterpret_cast<uintptr_t>(fp.proj) & 15) == 0 && fp.proj_stride % 8 == 0 &&
+         offB % 8 == 0 && (!p.complex_ssm || offTh % 8 == 0) && fp.T < (int64_t(1) << 31);
+}
+
+template <typename TA, int R, bool TMA>
+int launch_fused_t(const FusedParams& fp, cudaStream_t st, const CUtensorMap& tm_bc, const CUtensorMap& tm_th) {
   constexpr int RP = rp_of(R);
   using PL = FPlan<RP>;
   const int nseq_total = (int)(fp.B * fp.prm.H);
   const int nsm = num_sms();
   const int grid = nseq_total < nsm ? nseq_total : nsm;
+  const void* fn = (const void*)ssd_fused_kernel<TA, R, TMA>;
   int rc;
-  if ((rc = ensure_smem_f((const void*)ssd_fused_kernel<TA, R>, PL::bytes)) != M3B_OK) return rc;
+  if ((rc = ensure_smem_f(fn, PL::bytes)) != M3B_OK) return rc;
   cudaFuncAttributes fa{};
-  if (cudaFuncGetAttributes(&fa, (const void*)ssd_fused_kernel<TA, R>) == cudaSuccess &&
-      fa.maxThreadsPerBlock < kFusedThreads)
+  if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess && fa.maxThreadsPerBlock < kFusedThreads)
     return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: %d registers/thread allow only %d threads per block (need %d)",
                 fa.numRegs, fa.maxThreadsPerBlock, kFusedThreads);
   const Sched sc{fp.K, fp.prm.H, nseq_total, grid};
-  ssd_fused_kernel<TA, R><<<grid, kFusedThreads, PL::bytes, st>>>(fp, sc);
+  ssd_fused_kernel<TA, R, TMA><<<grid, kFusedThreads, PL::bytes, st>>>(fp, sc, tm_bc, tm_th);
   return check_launch("ssd_fused");
+}
+
+template <typename TA, int R>
+int launch_fused_r(const FusedParams& fp, cudaStream_t st) {
+  CUtensorMap tm_bc{}, tm_th{};
+  if constexpr (sizeof(TA) == 2) {
+    constexpr int L = 128 / rp_of(R);
+    if (tma_layout_ok(fp) && make_proj_map(&tm_bc, fp, 64 * R, L) && make_proj_map(&tm_th, fp, 64, L))
+      return launch_fused_t<TA, R, true>(fp, st, tm_bc, tm_th);
+  }
+  return launch_fused_t<TA, R, false>(fp, st, tm_bc, tm_th);
 }
 }  // namespace
 
@@ -848,9 +1110,9 @@ bool fused_supported(const m3b_layer_params& p) {
 
 int launch_fused(const FusedParams& fp, cudaStream_t st, bool bf16) {
   switch (fp.prm.R) {
-    case 1: return bf16 ? launch_fused_t<__nv_bfloat16, 1>(fp, st) : launch_fused_t<float, 1>(fp, st);
-    case 2: return bf16 ? launch_fused_t<__nv_bfloat16, 2>(fp, st) : launch_fused_t<float, 2>(fp, st);
-    case 4: return bf16 ? launch_fused_t<__nv_bfloat16, 4>(fp, st) : launch_fused_t<float, 4>(fp, st);
+    case 1: return bf16 ? launch_fused_r<__nv_bfloat16, 1>(fp, st) : launch_fused_r<float, 1>(fp, st);
+    case 2: return bf16 ? launch_fused_r<__nv_bfloat16, 2>(fp, st) : launch_fused_r<float, 2>(fp, st);
+    case 4: return bf16 ? launch_fused_r<__nv_bfloat16, 4>(fp, st) : launch_fused_r<float, 4>(fp, st);
     default: return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: mimo_rank %d", fp.prm.R);
   }
 }
