@@ -56,7 +56,7 @@ struct FPlan {
   static constexpr int kStage = 98304;
   static constexpr int tC = 0, tB = 32768, tX = 65536, tW = 81920;  // offsets inside a stage
   static constexpr int tileH = 2 * kStage;                           // 128 rows (n) x 64 cols (p)
-  static constexpr int NA = L + 1;
+  static constexpr int NA = (L + 1 + 3) & ~3;  // per-token scalar arrays: L + 1 entries, 16-byte rows
   static constexpr int scalStride = ((8 * NA * 4) + 15) & ~15;       // cum2 dtv gam bpr wst gb rmsB rmsC
   static constexpr int scal = tileH + 16384;
   static constexpr int omega = scal + 2 * scalStride;                // 2 x 64 doubles (by chunk parity)
@@ -74,17 +74,38 @@ struct FPlan {
 enum { BAR_FULL0 = 0, BAR_FULL1 = 1, BAR_EMPTY0 = 2, BAR_EMPTY1 = 3, BAR_SDONE0 = 4, BAR_SDONE1 = 5,
        BAR_HDONE = 6, BAR_YDONE = 7, BAR_STAGE0 = 8, BAR_STAGE1 = 9 };
 
+// Position of one chunk: sequence index, batch row, head, chunk within the sequence, group.
+struct ChunkPos {
+  int seq, b, h, k, grp;
+};
+
 // CTA c walks sequences (batch, head) = c, c + stride, c + 2 stride, ... of nseq_total,
-// each chunk by chunk; g numbers the chunks of all its sequences.
+// each chunk by chunk; g numbers the chunks of all its sequences.  The roles step a ChunkPos
+// cursor along g (a division only when a new sequence starts).
 struct Sched {
-  int K, H, nseq_total, stride;
+  int K, H, nseq_total, stride, heads_per_group;
   __device__ int count() const { return (nseq_total - (int)blockIdx.x + stride - 1) / stride; }
-  __device__ void at(int g, int& seq, int& b, int& h, int& k) const {
-    const int j = g / K;
-    k = g - j * K;
-    seq = (int)blockIdx.x + j * stride;
-    b = seq / H;
-    h = seq - b * H;
+  __device__ void set_seq(ChunkPos& c, int seq) const {
+    c.seq = seq;
+    c.b = seq / H;
+    c.h = seq - c.b * H;
+    c.grp = c.h / heads_per_group;
+  }
+  __device__ ChunkPos first() const {
+    ChunkPos c;
+    set_seq(c, (int)blockIdx.x);
+    c.k = 0;
+    return c;
+  }
+  __device__ void advance(ChunkPos& c) const {
+    if (++c.k == K) {
+      c.k = 0;
+      set_seq(c, c.seq + stride);
+    }
+  }
+  __device__ ChunkPos ahead(ChunkPos c, int n) const {
+    for (int i = 0; i < n; ++i) advance(c);
+    return c;
   }
 };
 
@@ -267,21 +288,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   // theta (-> the W tile, built only after theta has been consumed), counted as transaction
   // bytes of the same phase.  The producers hand chunks 0 and 1 to themselves; the epilogue
   // leader hands chunk g + 2 over once every epilogue thread has written the output of chunk g.
-  auto issue_stage = [&](int gg) {
+  auto issue_stage = [&](const ChunkPos& c, int gg) {
     uint64_t* bar = &bars[BAR_STAGE0 + (gg & 1)];
     if constexpr (TMA) {
-      int sq, bb, hh, kk;
-      sc.at(gg, sq, bb, hh, kk);
-      const int gr = hh / (H / p.G);
       uint8_t* stg = sm + (gg & 1) * PL::kStage;
       constexpr uint32_t kHalf = 16384;
       mbar_arrive_expect_tx(bar, 4 * kHalf + (p.complex_ssm ? (uint32_t)L * 128u : 0u));
-      const int xb = offB + gr * NR, xc = offC + gr * NR, ti = kk * L;
-      tma_load_3d(stg + PL::tB, &tm_bc, xb, ti, bb, bar);
-      tma_load_3d(stg + PL::tB + kHalf, &tm_bc, xb + NR / 2, ti, bb, bar);
-      tma_load_3d(stg + PL::tC, &tm_bc, xc, ti, bb, bar);
-      tma_load_3d(stg + PL::tC + kHalf, &tm_bc, xc + NR / 2, ti, bb, bar);
-      if (p.complex_ssm) tma_load_3d(stg + PL::tW, &tm_th, offTh, ti, bb, bar);
+      const int xb = offB + c.grp * NR, xc = offC + c.grp * NR, ti = c.k * L;
+      tma_load_3d(stg + PL::tB, &tm_bc, xb, ti, c.b, bar);
+      tma_load_3d(stg + PL::tB + kHalf, &tm_bc, xb + NR / 2, ti, c.b, bar);
+      tma_load_3d(stg + PL::tC, &tm_bc, xc, ti, c.b, bar);
+      tma_load_3d(stg + PL::tC + kHalf, &tm_bc, xc + NR / 2, ti, c.b, bar);
+      if (p.complex_ssm) tma_load_3d(stg + PL::tW, &tm_th, offTh, ti, c.b, bar);
     } else {
       mbar_arrive(bar);
     }
@@ -303,9 +321,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     float* nbC = nbB + kNS * RP;
     const float* sp = reinterpret_cast<const float*>(sm + PL::seqp);
     constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
+    ChunkPos pos = sc.first();
     if (ptid == 0) {
-      if (G > 0) issue_stage(0);
-      if (G > 1) issue_stage(1);
+      if (G > 0) issue_stage(pos, 0);
+      if (G > 1) issue_stage(sc.ahead(pos, 1), 1);
     }
     // raw token scalars of chunk gg for token ptid (0..L; token L is the next chunk's first),
     // loaded one chunk ahead of their use
@@ -313,11 +332,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       float dt, lam, rb, rc, dts;
       bool ok;
     };
-    auto load_tok = [&](int gg, TokRaw& tr) {
-      int sq, bb, hh, kk;
-      sc.at(gg, sq, bb, hh, kk);
-      const int gr = hh / (H / p.G);
-      const int64_t tt = (int64_t)kk * L + ptid;
+    auto load_tok = [&](const ChunkPos& c, TokRaw& tr) {
+      const int bb = c.b, hh = c.h, gr = c.grp;
+      const int64_t tt = (int64_t)c.k * L + ptid;
       tr.dt = tr.lam = tr.rb = tr.rc = 0.f;
       tr.dts = 1.f;
       tr.ok = ptid <= L && tt < a.T;
@@ -334,12 +351,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
     };
     TokRaw nxt;
-    if (G > 0) load_tok(0, nxt);
-    for (int g = 0; g < G; ++g) {
+    if (G > 0) load_tok(pos, nxt);
+    for (int g = 0; g < G; ++g, sc.advance(pos)) {
       const int s = g & 1;
-      int seq, b, h, k;
-      sc.at(g, seq, b, h, k);
-      const int grp = h / (H / p.G);
+      const int b = pos.b, h = pos.h, k = pos.k, grp = pos.grp;
+      const ChunkPos pnext = sc.ahead(pos, 1);
       const int64_t t0 = (int64_t)k * L;
       const TA* rowbase = proj + (int64_t)b * a.T * a.proj_stride;
       if (k == 0) {  // per-sequence parameters (every producer passed the last barrier of chunk g-1)
@@ -366,7 +382,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if (ptid == 0) M3B_TL(g, 1);
       uint8_t* st = sm + s * PL::kStage;
       const TokRaw cur = nxt;
-      if (g + 1 < G) load_tok(g + 1, nxt);
+      if (g + 1 < G) load_tok(pnext, nxt);
       float* scal = reinterpret_cast<float*>(sm + PL::scal + s * PL::scalStride);
       float* cum2 = scal;
       float* dtv = scal + NA;
@@ -379,8 +395,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       // register path: L2 prefetch of the projection rows the next chunk reads (the TMA path
       // starts its copies a chunk ahead, and the epilogue loads x and z ahead of use)
       if (!TMA && g + 1 < G && ptid < 4 * L) {
-        int seqn, bn, hn, kn;
-        sc.at(g + 1, seqn, bn, hn, kn);
+        const int bn = pnext.b, hn = pnext.h, kn = pnext.k;
         const int64_t tn = (int64_t)kn * L + (ptid >> 2);
         if (tn < a.T) {
           const TA* row = proj + ((int64_t)bn * a.T + tn) * a.proj_stride;
@@ -432,9 +447,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if (ptid <= L) {
         float dt = 0.f, gmm = 0.f, bp = 0.f;
         if (cur.ok) {
-          dt = softplus_f(cur.dt + sp[1]) * cur.dts;
+          dt = softplus_fast(cur.dt + sp[1]) * cur.dts;
           if (p.trapezoidal) {
-            const float lam = sigmoid_f(cur.lam);
+            const float lam = sigmoid_fast(cur.lam);
             gmm = lam * dt;
             bp = (1.f - lam) * dt;
           } else {
@@ -517,13 +532,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         // raw (2i, 2i+1) x R blocks: registers, or shared memory (TMA path), where the whole warp
         // reads a group of TG tokens before any lane overwrites them with tile entries
         constexpr int TG = TMA ? 4 : 1;
+        // Rows of tokens past T come out as the rotated bias: harmless, since their C^ rows only
+        // reach outputs that are not stored, their S columns are masked for every stored row,
+        // and their X / W rows are zero.
         PairRaw<TA, R> grb[TG], grc[TG];
+        float4 dt4, rb4, rc4;  // the group's dt and rms of B / C (TMA path)
 #pragma unroll
         for (int jj = 0; jj < SEGMAX; ++jj) {
           if (!N128 && jj >= seglen) break;
           const int j = seg * seglen + jj;
-          const bool valid = t0 + j < a.T;
           if constexpr (TMA) {
+            static_assert(TG == 4, "the TMA path reads the group's token scalars as float4");
             if (jj % TG == 0) {
 #pragma unroll
               for (int u = 0; u < TG; ++u) {
@@ -531,17 +550,30 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                 grb[u].load_shared(src + PL::tB);
                 grc[u].load_shared(src + PL::tC);
               }
+              dt4 = *reinterpret_cast<const float4*>(dtv + j);
+              rb4 = *reinterpret_cast<const float4*>(rmsB + j);
+              rc4 = *reinterpret_cast<const float4*>(rmsC + j);
               __syncwarp();
             }
           }
-          const PairRaw<TA, R>& rawb = TMA ? grb[jj % TG] : vb[jj];
-          const PairRaw<TA, R>& rawc = TMA ? grc[jj % TG] : vc[jj];
+          auto comp = [](const float4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; };
+          const float dtj = TMA ? comp(dt4, jj % 4) : dtv[j];
+          const float rbv = TMA ? comp(rb4, jj % 4) : rmsB[j];
+          const float rcv = TMA ? comp(rc4, jj % 4) : rmsC[j];
+          const PairRaw<TA, R>& rawb = [&]() -> const PairRaw<TA, R>& {
+            if constexpr (TMA) return grb[jj % TG];
+            else return vb[jj];
+          }();
+          const PairRaw<TA, R>& rawc = [&]() -> const PairRaw<TA, R>& {
+            if constexpr (TMA) return grc[jj % TG];
+            else return vc[jj];
+          }();
           float cs = 1.f, sn = 0.f;
           if (p.complex_ssm) {
-            run = fmaf(dtv[j], theta(jj), run);
+            run = fmaf(dtj, theta(jj), run);
             sincos_reduced(omf - run, &sn, &cs);
           }
-          const float2 rbj = make_float2(rmsB[j], rmsB[j]), rcj = make_float2(rmsC[j], rmsC[j]);
+          const float2 rbj = make_float2(rbv, rbv), rcj = make_float2(rcv, rcv);
           uint32_t ob[RP], oc[RP];
           if constexpr (R % 2 == 0) {
             const float2 c2 = make_float2(cs, cs), s2 = make_float2(sn, sn), ns2 = make_float2(-sn, -sn);
@@ -554,10 +586,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
               const float2 c1 = fma2(rawc.pair(R + 2 * rp), mul2(rcj, wC1[rp]), bC1[rp]);
               const float2 be = fma2(b1, ns2, mul2(b0, c2)), bo = fma2(b1, c2, mul2(b0, s2));
               const float2 ce = fma2(c1, ns2, mul2(c0, c2)), co = fma2(c1, c2, mul2(c0, s2));
-              ob[2 * rp] = valid ? pack_bf16x2(be.x, bo.x) : 0u;
-              ob[2 * rp + 1] = valid ? pack_bf16x2(be.y, bo.y) : 0u;
-              oc[2 * rp] = valid ? pack_bf16x2(ce.x, co.x) : 0u;
-              oc[2 * rp + 1] = valid ? pack_bf16x2(ce.y, co.y) : 0u;
+              ob[2 * rp] = pack_bf16x2(be.x, bo.x);
+              ob[2 * rp + 1] = pack_bf16x2(be.y, bo.y);
+              oc[2 * rp] = pack_bf16x2(ce.x, co.x);
+              oc[2 * rp + 1] = pack_bf16x2(ce.y, co.y);
             }
 #pragma unroll
             for (int r = R; r < RP; ++r) ob[r] = oc[r] = 0u;
@@ -569,8 +601,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             const float2 ncs = make_float2(-sn, cs), csn = make_float2(cs, sn);
             const float2 be = fma2(make_float2(bv.y, bv.y), ncs, mul2(make_float2(bv.x, bv.x), csn));
             const float2 ce = fma2(make_float2(cv.y, cv.y), ncs, mul2(make_float2(cv.x, cv.x), csn));
-            ob[0] = valid ? pack_bf16x2(be.x, be.y) : 0u;
-            oc[0] = valid ? pack_bf16x2(ce.x, ce.y) : 0u;
+            ob[0] = pack_bf16x2(be.x, be.y);
+            oc[0] = pack_bf16x2(ce.x, ce.y);
 #pragma unroll
             for (int r = 1; r < RP; ++r) ob[r] = oc[r] = 0u;
           }
@@ -625,13 +657,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const bool lead = tid == 0;
     const int xpc = tid & 7;  // X / W tiles: this thread's 8-column chunk of p
     // x of chunk gg, rows j = (tid + 256 u) / 8 (loaded a chunk ahead of the X / W tiles)
-    auto load_x = [&](int gg, Raw8<TA> (&xr)[XU]) {
-      int sq, bb, hh, kk;
-      sc.at(gg, sq, bb, hh, kk);
-      const TA* xb = proj + (int64_t)bb * a.T * a.proj_stride + HP + (int64_t)hh * P + xpc * 8;
+    auto load_x = [&](const ChunkPos& c, Raw8<TA> (&xr)[XU]) {
+      const TA* xb = proj + (int64_t)c.b * a.T * a.proj_stride + HP + (int64_t)c.h * P + xpc * 8;
 #pragma unroll
       for (int u = 0; u < XU; ++u) {
-        const int64_t tt = (int64_t)kk * L + ((tid + kEpiThreads * u) >> 3);
+        const int64_t tt = (int64_t)c.k * L + ((tid + kEpiThreads * u) >> 3);
         if (tt < a.T && xpc * 8 < P) xr[u].load(xb + tt * a.proj_stride);
         else xr[u].zero();
       }
@@ -685,9 +715,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       umma_commit(&bars[BAR_HDONE]);
     };
     // H'_0 of the sequence starting at chunk gs -> bf16 tile row n = m, and H = d * H'_0 in TMEM
-    auto state_init = [&](int gs) -> bool {
-      int seq, b, h, k;
-      sc.at(gs, seq, b, h, k);
+    auto state_init = [&](const ChunkPos& c, int gs) -> bool {
+      const int b = c.b, h = c.h;
       const int s2 = gs & 1;
       if (!role_wait(&bars[BAR_FULL0 + s2], (gs >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))
         return false;
@@ -728,11 +757,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       named_bar(kBarEpi, kEpiThreads);  // mimo_x is read by the X / W tiles below
       return true;
     };
-    auto write_h_final = [&](int glast) {
+    auto write_h_final = [&](const ChunkPos& c) {
       if (!a.h_final) return;
-      int seq, b, h, k;
-      sc.at(glast, seq, b, h, k);
-      const int64_t base = ((int64_t)b * H + h) * (int64_t)P * N;
+      const int64_t base = ((int64_t)c.b * H + c.h) * (int64_t)P * N;
       float v[32];
       tmem_ld32(trow + kColH + 32 * ch, v);
       if (m < N) {
@@ -744,8 +771,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
     };
     Raw8<TA> xn[XU];  // x of the next chunk
-    if (G > 0) load_x(0, xn);
-    bool ok = G > 0 && state_init(0);
+    ChunkPos pos = sc.first();
+    if (G > 0) load_x(pos, xn);
+    bool ok = G > 0 && state_init(pos, 0);
     if (ok) {
       build_xw(0, xn);
       fence_async_smem();
@@ -753,17 +781,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       named_bar(kBarEpi, kEpiThreads);
       if (lead) issue_state_mma(0);
     }
-    for (int g = 0; ok && g < G; ++g) {
+    for (int g = 0; ok && g < G; ++g, sc.advance(pos)) {
       const int s = g & 1;
-      int seq, b, h, k;
-      sc.at(g, seq, b, h, k);
+      const int b = pos.b, h = pos.h, k = pos.k;
+      const ChunkPos pnext = sc.ahead(pos, 1);
       uint8_t* st = sm + s * PL::kStage;
       const float* scal = reinterpret_cast<const float*>(sm + PL::scal + s * PL::scalStride);
       const float* cum2 = scal;
       const float* gam = scal + 2 * NA;
       const float* gbw = scal + 5 * NA;
       const uint32_t cs0 = kColS + 128 * s;
-      if (g + 1 < G) load_x(g + 1, xn);
+      if (g + 1 < G) load_x(pnext, xn);
       // z of this thread's row (t, r) and column half, prefetched while the tensor core works
       const int64_t tok = (int64_t)k * L + t;
       const bool row_ok = tok < a.T && r < R;
@@ -952,7 +980,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       // every epilogue thread is done with stage s for chunk g: hand it over for chunk g + 2
       if (lead && g + 2 < G && !*abort_flag) {
         if (mbar_wait(&bars[BAR_EMPTY0 + s], (g >> 1) & 1)) {
-          issue_stage(g + 2);
+          issue_stage(sc.ahead(pnext, 1), g + 2);
         } else {
           *abort_flag = 1;
           record_error(a.err, M3B_ERR_TIMEOUT);
@@ -960,11 +988,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
       // ---- state for chunk g+1: H'_{g+1} -> bf16 tile, H *= d_{g+1}; then Yi_{g+1}, H += ...
       if (g + 1 < G) {
-        int seq1, b1, h1, k1;
-        sc.at(g + 1, seq1, b1, h1, k1);
-        if (k1 == 0) {
-          write_h_final(g);
-          if (!(ok = state_init(g + 1))) break;
+        if (pnext.k == 0) {
+          write_h_final(pos);
+          if (!(ok = state_init(pnext, g + 1))) break;
         } else {
           const int s1 = (g + 1) & 1;
           if (!(ok = role_wait(&bars[BAR_FULL0 + s1], ((g + 1) >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag,
@@ -994,7 +1020,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           M3B_TL(g, 12);
         }
       } else {
-        write_h_final(g);
+        write_h_final(pos);
       }
     }
   }
@@ -1077,7 +1103,7 @@ int launch_fused_t(const FusedParams& fp, cudaStream_t st, const CUtensorMap& tm
   if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess && fa.maxThreadsPerBlock < kFusedThreads)
     return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: %d registers/thread allow only %d threads per block (need %d)",
                 fa.numRegs, fa.maxThreadsPerBlock, kFusedThreads);
-  const Sched sc{fp.K, fp.prm.H, nseq_total, grid};
+  const Sched sc{fp.K, fp.prm.H, nseq_total, grid, fp.prm.H / fp.prm.G};
   ssd_fused_kernel<TA, R, TMA><<<grid, kFusedThreads, PL::bytes, st>>>(fp, sc, tm_bc, tm_th);
   return check_launch("ssd_fused");
 }
