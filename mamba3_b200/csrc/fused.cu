@@ -792,6 +792,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const float* gbw = scal + 5 * NA;
       const uint32_t cs0 = kColS + 128 * s;
       if (g + 1 < G) load_x(pnext, xn);
+      if constexpr (TMA) {  // z of the next chunk into L2 (its loads below are a chunk later)
+        if (lead && g + 1 < G) tma_prefetch_3d(&tm_th, pnext.h * P, pnext.k * L, pnext.b);
+      }
       // z of this thread's row (t, r) and column half, prefetched while the tensor core works
       const int64_t tok = (int64_t)k * L + t;
       const bool row_ok = tok < a.T && r < R;
@@ -908,9 +911,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         const uint32_t cyi = kColYi + 64 * s;
 #pragma unroll
         for (int qq = 0; qq < 2; ++qq) {
-          float Y[16], Yi[16];
-          tmem_ld16(trow + cs0 + 32 * ch + 16 * qq, Y);
-          tmem_ld16(trow + cyi + 32 * ch + 16 * qq, Yi);
+          // 16 columns of Y and of Yi in flight at once, combined right away
+          uint32_t yraw[16], yiraw[16];
+          tmem_ld16_async(trow + cs0 + 32 * ch + 16 * qq, yraw);
+          tmem_ld16_async(trow + cyi + 32 * ch + 16 * qq, yiraw);
+          tmem_wait_ld(yraw, yiraw);
+          float ysum[16];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const float2 v = fma2(et2, make_float2(__uint_as_float(yraw[i]), __uint_as_float(yraw[i + 1])),
+                                  mul2(ec2, make_float2(__uint_as_float(yiraw[i]), __uint_as_float(yiraw[i + 1]))));
+            ysum[i] = v.x;
+            ysum[i + 1] = v.y;
+          }
           float acc[16];
 #pragma unroll
           for (int hc = 0; hc < 2; ++hc) {
@@ -928,8 +941,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 #pragma unroll
             for (int e2 = 0; e2 < 4; ++e2) {
               const int i = 8 * hc + 2 * e2;
-              const float2 yv = fma2(et2, make_float2(Y[i], Y[i + 1]),
-                                     fma2(ec2, make_float2(Yi[i], Yi[i + 1]), mul2(D2, bf2_to_f2(xw[e2]))));
+              const float2 yv = fma2(D2, bf2_to_f2(xw[e2]), make_float2(ysum[i], ysum[i + 1]));
               const float2 gz = silu_fast2(mul2(zr[c8].pair(2 * e2), mzp[e2]));
               const float2 o = mul2(mul2(yv, gz), mdp[e2]);
               acc[i] = o.x;
