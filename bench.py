@@ -33,7 +33,7 @@ METRIC = "KulaMamba layer forward tokens/s (config 1, bf16)"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample-tokens", type=int, default=512)
@@ -41,6 +41,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="override config-1 batch (profiling captures)")
     ap.add_argument("--seqlen", type=int, default=None, help="override config-1 seqlen (profiling captures)")
     ap.add_argument("--algo", type=int, default=0, help="layer algorithm: 0 auto, 1 fused, 2 chunk-parallel")
+    ap.add_argument("--e2e-pieces", type=int, default=8,
+                    help="token ranges forward_host streams the host batch in (copy/compute overlap)")
     return ap.parse_args()
 
 
@@ -111,6 +113,12 @@ def algorithmic_work(B, T, H=24, P=64, N=128, R=2, d_model=768, d_proj=3696):
     K = (T + L - 1) // L
     chunks = B * K * H
     tok = B * T
+    # the reference's algorithmic work per (batch, 64-token chunk, head), dense chunk tiles:
+    # C B~^T 2(CS R)(CS 2R)N + mask X~ 2(CS R)(CS 2R)P + state 2P(CS 2R)N + out 2(CS R)NP
+    CS = 64
+    ref_chunks = B * ((T + CS - 1) // CS) * H
+    f_ref = ref_chunks * (2 * (CS * R) * (CS * 2 * R) * N + 2 * (CS * R) * (CS * 2 * R) * P
+                          + 2 * P * (CS * 2 * R) * N + 2 * (CS * R) * N * P)
     f_state = chunks * 2 * N * 128 * P                 # S'^T (N x P) over K = 128
     f_out = chunks * (2 * 128 * 128 * N + 2 * 128 * P * 128 + 2 * 128 * P * N)  # S, P X, C H'
     st_bytes = chunks * P * N * 2                      # one bf16 state tensor
@@ -118,6 +126,7 @@ def algorithmic_work(B, T, H=24, P=64, N=128, R=2, d_model=768, d_proj=3696):
     tok_bc = tok * 2 * N * R * 2                       # B and C columns (shared by the heads)
     tok_sc = tok * (2 * H + N // 2) * 2                # dt, lam, theta
     return {
+        "ssd_fused": {"flops": f_ref, "bytes": 2 * tok_x + tok_bc + tok_sc + tok * H * P * 2},
         "chunk_out": {"flops": f_out, "bytes": 2 * tok_x + tok_bc + tok_sc + st_bytes + tok * H * P * 2},
         "chunk_state": {"flops": f_state, "bytes": tok_x + tok_bc + tok_sc + st_bytes},
         "scan": {"flops": 0, "bytes": 2 * st_bytes},
@@ -125,6 +134,26 @@ def algorithmic_work(B, T, H=24, P=64, N=128, R=2, d_model=768, d_proj=3696):
         "in_proj": {"flops": 2 * tok * d_model * d_proj, "bytes": tok * (d_model + d_proj) * 2},
         "out_proj": {"flops": 2 * tok * H * P * d_model, "bytes": tok * (H * P + d_model) * 2},
     }
+
+
+def profiled_traffic(kernel, B, T):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu summary
+    profiles/<kernel>_cfg1.txt (line 'dram_bytes_per_launch: N' measured at B0 x T0 tokens,
+    scaled by tokens), or None."""
+    f = ROOT / "profiles" / f"{kernel}_cfg1.txt"
+    if not f.exists():
+        return None
+    vals = {}
+    for ln in f.read_text().splitlines():
+        if ":" in ln:
+            k, _, v = ln.partition(":")
+            vals[k.strip()] = v.strip()
+    try:
+        b = float(vals["dram_bytes_per_launch"])
+        tok = float(vals.get("tokens", B * T))
+    except (KeyError, ValueError):
+        return None
+    return b * (B * T) / tok
 
 
 def run_ours(args):
@@ -216,11 +245,20 @@ def run_ours(args):
             per["out_proj"] += e[nst].elapsed_time(e[-1])
             del marks
         per = {k: v / args.steps for k, v in per.items()}
+        # the fused path leaves the angle / chunk-state / scan stages empty and times its single
+        # kernel in the chunk_out slot
+        fused = per["angle_prefix"] + per["chunk_state"] + per["scan"] < 0.02
+        if fused:
+            per["ssd_fused"] = per.pop("chunk_out")
+            for k in ("angle_prefix", "chunk_state", "scan"):
+                per.pop(k)
+        launches_per_step = 2 if fused else 5  # prep + ssd_fused | prep, angle, state, scan, out
 
-        # end to end through the public API: pinned host x -> device -> layer -> pinned host y
+        # end to end through the public API: pinned host x -> layer -> pinned host y, streamed by
+        # forward_host in token ranges so the copies in, the layer and the copies out overlap
         y_host = torch.empty(B, T, c["d_model"], dtype=torch.bfloat16).pin_memory()
         for _ in range(2):
-            y_host.copy_(layer(x_host.to(dev, non_blocking=True)), non_blocking=True)
+            layer.forward_host(x_host, y_host, pieces=args.e2e_pieces)
         torch.cuda.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -228,7 +266,7 @@ def run_ours(args):
         ke = max(3, args.steps // 2)
         e0.record()
         for _ in range(ke):
-            y_host.copy_(layer(x_host.to(dev, non_blocking=True)), non_blocking=True)
+            layer.forward_host(x_host, y_host, pieces=args.e2e_pieces)
         e1.record()
         torch.cuda.synchronize()
         ms_e2e = e0.elapsed_time(e1) / ke
@@ -243,7 +281,7 @@ def run_ours(args):
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() \
             else {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
         work = algorithmic_work(B, T)
-        ours = {k: per[k] for k in ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out")}
+        ours = {k: v for k, v in per.items() if k not in ("in_proj", "out_proj", "last_bx")}
         dom = max(ours, key=ours.get)
         w = work.get(dom, {"flops": 0, "bytes": 0})
         t_s = per[dom] / 1e3
@@ -256,7 +294,7 @@ def run_ours(args):
             roof = {"bound": "hbm", "achieved": w["bytes"] / t_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
         roof["frac"] = roof["achieved"] / roof["peak"]
         roof["kernel"] = dom
-        roof["traffic"] = None
+        roof["traffic"] = profiled_traffic(dom, B, T)
         roof["peak_source"] = "measured (MEASURED_PEAKS.json)" if not peaks.get("fallback") else "fallback"
         kern = {}
         for k, v in per.items():
@@ -278,10 +316,10 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (>1.5 GB touched per step)"},
             "roofline": roof,
             "kernels_ms": kern,
-            "gpu_launches": 5 * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "e2e": {"value": tokens / (ms_e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2,
-                    "ms_per_step": ms_e2e},
+                    "ms_per_step": ms_e2e, "api": f"KulaMamba.forward_host(pieces={args.e2e_pieces})"},
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline:

@@ -174,6 +174,17 @@ typedef struct m3b_layer_fwd_args {
  * ------------------------------------------------------------------------ */
 #define M3B_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
 M3B_API int m3b_layer_fwd_noalloc(const m3b_layer_fwd_args* a, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Strided copy of `rows` rows of `row_bytes` bytes between host and device
+ * memory (either direction, or device to device) on `stream`, one call per
+ * block of rows: the piece-wise host streaming of KulaMamba.forward_host
+ * (no reference counterpart) moves a (batch, token range) slab of a
+ * (batch, seqlen, d_model) host tensor with it.  Pitches are in bytes; host
+ * memory should be pinned for the copy to be asynchronous.
+ * ------------------------------------------------------------------------ */
+M3B_API int m3b_copy_rows_async(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t row_bytes,
+                                size_t rows, void* stream);
 /* Bytes of device workspace m3b_layer_fwd needs for these arguments. */
 M3B_API size_t m3b_layer_fwd_workspace(const m3b_layer_fwd_args* a);
 M3B_API int m3b_layer_fwd(const m3b_layer_fwd_args* a, void* workspace, size_t workspace_bytes, void* stream);

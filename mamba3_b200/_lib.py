@@ -86,6 +86,8 @@ SIGNATURES = {
     "m3b_layer_fwd_workspace": (C.c_size_t, [C.POINTER(LayerFwdArgs)]),
     "m3b_layer_fwd": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_layer_fwd_noalloc": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p]),
+    "m3b_copy_rows_async": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                      C.c_void_p]),
     "m3b_chunked_ssd_workspace": (C.c_size_t, [C.POINTER(SsdArgs)]),
     "m3b_chunked_ssd": (C.c_int, [C.POINTER(SsdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_selftest_umma": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
@@ -222,3 +224,22 @@ def selftest_umma(A, B, mode):
     with torch.cuda.device(dev):
         _check(lib().m3b_selftest_umma(_ptr(A), _ptr(B), _ptr(D), mode, _ptr(err), _stream(dev)), "selftest_umma")
     return D, err
+
+
+def copy_token_range(dst, dst_t0, src, src_t0, ntok, stream):
+    """dst[:, dst_t0:dst_t0+ntok] = src[:, src_t0:src_t0+ntok] for (batch, seqlen, d) tensors with
+    contiguous last two dims, host or device on either side, asynchronously on `stream` (one
+    strided copy for the whole batch)."""
+    if dst.dim() != 3 or src.dim() != 3 or dst.shape[0] != src.shape[0] or dst.shape[2] != src.shape[2]:
+        raise M3bError("copy_token_range: (batch, seqlen, d) tensors with equal batch and d expected")
+    if dst.dtype != src.dtype:
+        raise M3bError("copy_token_range: dtypes differ")
+    for t in (dst, src):
+        if t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+            raise M3bError("copy_token_range: the (seqlen, d) dims must be contiguous")
+    es = src.element_size()
+    row = ntok * src.shape[2] * es
+    d_ptr = C.c_void_p(dst.data_ptr() + dst_t0 * dst.stride(1) * es)
+    s_ptr = C.c_void_p(src.data_ptr() + src_t0 * src.stride(1) * es)
+    _check(lib().m3b_copy_rows_async(d_ptr, dst.stride(0) * es, s_ptr, src.stride(0) * es, row, src.shape[0],
+                                     C.c_void_p(stream.cuda_stream)), "m3b_copy_rows_async")

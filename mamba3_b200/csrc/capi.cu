@@ -57,6 +57,17 @@ const char* m3b_last_error(void) { return m3b::g_last_error; }
 
 int m3b_abi_version(void) { return M3B_ABI_VERSION; }
 
+int m3b_copy_rows_async(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t row_bytes,
+                        size_t rows, void* stream) {
+  if (!dst || !src || row_bytes > dst_pitch || row_bytes > src_pitch)
+    return m3b::fail(M3B_ERR_INVALID_ARG, "copy_rows: null pointer or row wider than its pitch");
+  if (rows == 0 || row_bytes == 0) return M3B_OK;
+  const cudaError_t e = cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, row_bytes, rows, cudaMemcpyDefault,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return m3b::fail(M3B_ERR_CUDA, "copy_rows: %s", cudaGetErrorString(e));
+  return M3B_OK;
+}
+
 int m3b_scan_fwd(const m3b_scan_args* a, void* stream) {
   m3b::g_last_error[0] = 0;
   if (!a || !a->decay || !a->h_chunk || !a->h_states)

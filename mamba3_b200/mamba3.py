@@ -156,6 +156,49 @@ class KulaMamba(nn.Module):
         """Continue a prefill from an inference state (chunked prefill; no reference counterpart)."""
         return self._ssd(x, dt_scale, True, ssm_state)
 
+    def forward_host(self, x_host, out=None, pieces=4):
+        """forward() of a batch held in pinned host memory, streamed through the GPU in `pieces`
+        token ranges (no reference counterpart): the host->device copy of range i+1, the layer on
+        range i and the device->host copy of range i-1 run on three streams and overlap, the
+        state crossing range boundaries as in prefill_from.  Returns `out` (pinned host memory,
+        allocated when None).  The caller's current stream is ordered after the last copy."""
+        from . import _lib
+
+        if x_host.is_cuda or x_host.dim() != 3 or not x_host.is_pinned():
+            raise ValueError("forward_host expects a pinned host tensor (batch, seqlen, d_model)")
+        dev = self.in_proj.weight.device
+        B, T, D = x_host.shape
+        if out is None:
+            out = torch.empty(B, T, D, dtype=x_host.dtype, pin_memory=True)
+        n = max(1, min(int(pieces), T))
+        edges = [T * i // n for i in range(n + 1)]
+        span = max(edges[i + 1] - edges[i] for i in range(n))
+        cmp = torch.cuda.current_stream(dev)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        s_in.wait_stream(cmp)
+        s_out.wait_stream(cmp)
+        xb = [torch.empty(B, span, D, dtype=x_host.dtype, device=dev) for _ in range(2)]
+        ev_in = [torch.cuda.Event() for _ in range(n)]
+        ev_cmp = [torch.cuda.Event() for _ in range(n)]
+        ev_out = [torch.cuda.Event() for _ in range(n)]
+        state = None
+        for i in range(n):
+            t0, nt, k = edges[i], edges[i + 1] - edges[i], i % 2
+            if i >= 2:
+                s_in.wait_event(ev_cmp[i - 2])  # range i-2 has been read out of xb[k]
+            _lib.copy_token_range(xb[k], 0, x_host, t0, nt, s_in)
+            ev_in[i].record(s_in)
+            cmp.wait_event(ev_in[i])
+            y, state = self._ssd(xb[k][:, :nt], None, i + 1 < n, state)
+            ev_cmp[i].record(cmp)
+            s_out.wait_event(ev_cmp[i])
+            _lib.copy_token_range(out, t0, y, 0, nt, s_out)
+            y.record_stream(s_out)  # its memory is not reused before this copy has run
+            ev_out[i].record(s_out)
+        cmp.wait_event(ev_out[n - 1])
+        cmp.wait_stream(s_in)
+        return out
+
     def step(self, hidden_states, ssm_state, dt_scale=None):
         """One token: (B, d_model) or (B, 1, d_model) -> same shape, new state (mamba3/mamba3.py:267-322)."""
         squeeze = hidden_states.dim() == 2

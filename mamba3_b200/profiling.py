@@ -32,9 +32,10 @@ _REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks", 0x4: "sw_power_cap", 0x
 
 
 class ClockSampler:
-    """Samples SM clock, power and clock-event reasons of one GPU every `period` seconds (NVML)."""
+    """Samples SM clock, power and clock-event reasons of one GPU every `period` seconds (NVML),
+    fine enough to put several samples inside a timed region of a few tens of milliseconds."""
 
-    def __init__(self, torch_device_index: int, period: float = 0.2):
+    def __init__(self, torch_device_index: int, period: float = 0.005):
         import torch
 
         self.period = period

@@ -138,6 +138,23 @@ def test_mixed_decay_heads_n128():
     assert max_rel(to_np(st["h"]), ost["h"]) < BF16_TOL
 
 
+@pytest.mark.parametrize("pieces", [1, 3, 8])
+def test_forward_host_streaming_equals_forward(pieces):
+    """forward_host (pinned host input streamed through the GPU in token ranges) == forward."""
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(6)
+    m = KulaMamba(d_model=256, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 333, 256, generator=g).to(torch.bfloat16).pin_memory()
+    with torch.no_grad():
+        ref = m(x.cuda())
+        out = m.forward_host(x, pieces=pieces)
+    torch.cuda.synchronize()
+    assert not out.is_cuda and out.is_pinned()
+    assert max_rel(to_np(out), to_np(ref)) < BF16_TOL
+
+
 @pytest.mark.parametrize("B,T,seed", [(16, 4096, 1)])
 def test_cfg1_full_size_prefix_parity(B, T, seed):
     """Config 1 at full size: rows 0 and B-1, first 256 tokens vs the oracle (causal prefix)."""
