@@ -41,6 +41,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="override config-1 batch (profiling captures)")
     ap.add_argument("--seqlen", type=int, default=None, help="override config-1 seqlen (profiling captures)")
     ap.add_argument("--algo", type=int, default=0, help="layer algorithm: 0 auto, 1 fused, 2 chunk-parallel")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-4 decode measurement")
     ap.add_argument("--e2e-pieces", type=int, default=8,
                     help="token ranges forward_host streams the host batch in (copy/compute overlap)")
     return ap.parse_args()
@@ -134,6 +135,72 @@ def algorithmic_work(B, T, H=24, P=64, N=128, R=2, d_model=768, d_proj=3696):
         "in_proj": {"flops": 2 * tok * d_model * d_proj, "bytes": tok * (d_model + d_proj) * 2},
         "out_proj": {"flops": 2 * tok * H * P * d_model, "bytes": tok * (H * P + d_model) * 2},
     }
+
+
+def run_decode(dev, world, rank, barrier):
+    """Config 4: the 24-layer config-2 LM prefills (256 / world, 512) prompt tokens per rank and
+    decodes greedily with the CUDA-graph decoder.  Also times the step kernel of one layer alone
+    against its state bytes (h read + write, prev_BX read + write: 4 P N fp32 per (batch, head))."""
+    import torch
+    import torch.distributed as dist
+
+    from mamba3_b200 import KulaMambaLM, ops
+    from mamba3_b200.decode import GraphDecoder
+
+    Bg, Tp, new = 256, 512, 256
+    B = max(1, Bg // world)
+    torch.manual_seed(2)
+    lm = KulaMambaLM(vocab_size=32000, d_model=768, n_layers=24, d_state=128, headdim=64, mimo_rank=2,
+                     residual_scale="depth").to(dev, torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, 32000, (Bg, Tp), generator=g)[rank * B:(rank + 1) * B].to(dev)
+    dec = GraphDecoder(lm, batch_size=B, max_new_tokens=new)
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with torch.no_grad():
+        dec.prefill(ids)
+        dec.decode(4)  # capture + warm-up
+        ms_prefill = timed(lambda: dec.prefill(ids))
+        steps = new - 1
+        ms_dec = timed(lambda: dec.decode(steps))
+        # the step kernel of layer 0 alone, in place on its state
+        ssm = lm.layers[0].ssm
+        st = dec.states[0]
+        proj = ssm.in_proj(torch.randn(B, 768, device=dev, dtype=torch.bfloat16))
+        y = torch.empty(B, ssm.nheads * ssm.headdim, device=dev, dtype=torch.bfloat16)
+        dims = GraphDecoder._dims(ssm)
+        prm = ssm._param_tensors()
+        for _ in range(3):
+            ops.step_ssm_(prm, dims, proj, st["h"], st["prev_BX"], st["angle"], y)
+        reps = 50
+        ms_k = timed(lambda: [ops.step_ssm_(prm, dims, proj, st["h"], st["prev_BX"], st["angle"], y)
+                              for _ in range(reps)]) / reps
+    H, P, N = ssm.nheads, ssm.headdim, ssm.d_state
+    state_bytes = 4 * P * N * 4 * B * H
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() \
+        else {"hbm_gbs": 6650.0}
+    gbs = state_bytes / (ms_k / 1e3) / 1e9
+    return {"workload": f"config 4: 24-layer LM, prompt ({Bg}, {Tp}) + {new} greedy tokens, batch {B} per GPU, "
+                        "CUDA-graph decode (GraphDecoder)",
+            "decode_tokens_per_s": world * B * steps / (ms_dec / 1e3), "ms_per_token": ms_dec / steps,
+            "prefill_tokens_per_s": world * B * Tp / (ms_prefill / 1e3),
+            "step_kernel": {"ms": ms_k, "state_bytes": state_bytes, "achieved_gbs": gbs,
+                            "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
+                            "batch": B, "heads": H}}
 
 
 def profiled_traffic(kernel, B, T):
@@ -275,6 +342,8 @@ def run_ours(args):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ms_e2e = float(tt.item())
 
+    decode = None if args.no_decode else run_decode(dev, world, rank, barrier)
+
     if rank == 0:
         import math
 
@@ -322,6 +391,8 @@ def run_ours(args):
                     "ms_per_step": ms_e2e, "api": f"KulaMamba.forward_host(pieces={args.e2e_pieces})"},
             "clocks": clk.summary(),
         }
+        if decode is not None:
+            line["decode"] = decode
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_sample_tokens)
         print(json.dumps(line), flush=True)

@@ -11,6 +11,7 @@ from .mamba3 import KulaMamba, RMSNorm  # noqa: E402
 from .block import KulaMambaBlock, KulaMambaLM, SwiGLU  # noqa: E402
 from .ssd import SSDOutput, chunked_ssd  # noqa: E402
 from .scan import ssd_scan  # noqa: E402
+from .decode import GraphDecoder  # noqa: E402  (extension: CUDA-graph decode loop)
 
 __all__ = [
     "KulaMamba",
@@ -21,4 +22,5 @@ __all__ = [
     "SSDOutput",
     "chunked_ssd",
     "ssd_scan",
+    "GraphDecoder",
 ]
