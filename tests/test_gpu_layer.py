@@ -80,6 +80,25 @@ def test_parallel_equals_recurrent(case):
     assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < BF16_TOL
 
 
+@pytest.mark.parametrize("R", [1, 2, 3, 4])
+def test_parallel_equals_recurrent_n128(R):
+    """d_state 128 (the step kernel's one-warp-per-state-row path for R = 1, 2, 4; the generic
+    path for R = 3): forward vs token-by-token steps, fp32 model."""
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(12 + R)
+    m = KulaMamba(d_model=128, d_state=128, headdim=64, mimo_rank=R).cuda().eval()
+    x = torch.randn(2, 40, 128, generator=torch.Generator().manual_seed(R)).cuda()
+    with torch.no_grad():
+        y_par = m(x)
+        st = m.allocate_inference_state(2)
+        ys = []
+        for t in range(x.shape[1]):
+            yt, st = m.step(x[:, t:t + 1], st)
+            ys.append(yt[:, 0])
+    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < BF16_TOL
+
+
 def test_chaining_prefill_from_state():
     """prefill(x[:, :T1]) then prefill_from(x[:, T1:]) == prefill(x) (sequence-split property)."""
     d = load("layer_n128p64")
