@@ -42,6 +42,7 @@ def parse():
     ap.add_argument("--seqlen", type=int, default=None, help="override config-1 seqlen (profiling captures)")
     ap.add_argument("--algo", type=int, default=0, help="layer algorithm: 0 auto, 1 fused, 2 chunk-parallel")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-4 decode measurement")
+    ap.add_argument("--no-seqpar", action="store_true", help="skip the config-3 sequence-sharded measurement")
     ap.add_argument("--e2e-pieces", type=int, default=8,
                     help="token ranges forward_host streams the host batch in (copy/compute overlap)")
     return ap.parse_args()
@@ -203,6 +204,50 @@ def run_decode(dev, world, rank, barrier):
                             "batch": B, "heads": H}}
 
 
+def run_seqpar(dev, world, rank, barrier):
+    """Config 3: one d_model 2048 / 64-head / mimo_rank 4 layer over x (2, 131072, 2048),
+    sequence-sharded: rank r holds tokens [r T/G, (r+1) T/G) of both rows and runs
+    seqpar.prefill_sharded (local pass, one all_gather of shard summaries, exact second pass).
+    On one GPU it is the plain prefill."""
+    import torch
+    import torch.distributed as dist
+
+    from mamba3_b200 import KulaMamba, seqpar
+
+    B, T, D = 2, 131072, 2048
+    torch.manual_seed(0)
+    layer = KulaMamba(d_model=D, d_state=128, headdim=64, mimo_rank=4).to(dev, torch.bfloat16).eval()
+    Ts = T // world
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(B, T, D, generator=g, device=dev)[:, rank * Ts:(rank + 1) * Ts].to(torch.bfloat16).contiguous()
+
+    def run():
+        if world == 1:
+            return layer.prefill(x)
+        return seqpar.prefill_sharded(layer, x, return_state=True)
+
+    with torch.no_grad():
+        run()
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        a.record()
+        for _ in range(reps):
+            run()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+    return {"workload": f"config 3: layer d_model {D}, 64 heads, mimo_rank 4, x ({B}, {T}, {D}) bf16, "
+                        f"sequence-sharded over {world} GPU(s), {Ts} tokens per GPU",
+            "tokens_per_s": B * T / (ms / 1e3), "ms_per_step": ms, "scaling": "strong",
+            "exchange": "one all_gather of (S, PB, Om, Lam, c0) per layer" if world > 1 else "none"}
+
+
 def profiled_traffic(kernel, B, T):
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu summary
     profiles/<kernel>_cfg1.txt (line 'dram_bytes_per_launch: N' measured at B0 x T0 tokens,
@@ -343,6 +388,7 @@ def run_ours(args):
             ms_e2e = float(tt.item())
 
     decode = None if args.no_decode else run_decode(dev, world, rank, barrier)
+    seqp = None if args.no_seqpar else run_seqpar(dev, world, rank, barrier)
 
     if rank == 0:
         import math
@@ -393,6 +439,8 @@ def run_ours(args):
         }
         if decode is not None:
             line["decode"] = decode
+        if seqp is not None:
+            line["seqpar"] = seqp
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_sample_tokens)
         print(json.dumps(line), flush=True)
