@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3B_ABI_VERSION 1
+#define M3B_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define M3B_API __attribute__((visibility("default")))
@@ -157,6 +157,9 @@ typedef struct m3b_layer_fwd_args {
    * (batch, head) sequences, state kept on chip); 2: chunk-parallel kernels (chunk
    * states in HBM + scan). Same results up to fp32 rounding. */
   int32_t algo;
+  /* 1: the caller needs only h_final / angle_final / prev_bx_final; y must still be a valid
+   * buffer, but the fused path may leave it unwritten and skips the output work. */
+  int32_t state_only;
 } m3b_layer_fwd_args;
 #define M3B_LAYER_FWD_STAGES 6
 

@@ -61,7 +61,8 @@ class LayerFwdArgs(C.Structure):
                 ("proj_stride", C.c_int64), ("act_dtype", C.c_int32), ("dt_scale", C.c_void_p),
                 ("h_init", C.c_void_p), ("angle_init", C.c_void_p), ("prev_bx_init", C.c_void_p), ("y", C.c_void_p),
                 ("h_final", C.c_void_p), ("angle_final", C.c_void_p), ("prev_bx_final", C.c_void_p),
-                ("err", C.c_void_p), ("stage_events", C.POINTER(C.c_void_p)), ("algo", C.c_int32)]
+                ("err", C.c_void_p), ("stage_events", C.POINTER(C.c_void_p)), ("algo", C.c_int32),
+                ("state_only", C.c_int32)]
 
 
 class SsdArgs(C.Structure):
@@ -174,7 +175,7 @@ def step(prm: LayerParams, proj, dt_scale, h, prev_bx, angle, h_out, bx_out, ang
 
 def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=None, prev_bx_init=None,
               h_final=None, angle_final=None, prev_bx_final=None, err=None, workspace=None, stage_events=None,
-              algo=0):
+              algo=0, state_only=False):
     """Launch the chunked layer forward; proj (B,T,d_proj) with unit stride in the last dim."""
     dev = _cuda(proj, y, dt_scale, h_init, angle_init, prev_bx_init, h_final, angle_final, prev_bx_final, err)
     Bt, T, _ = proj.shape
@@ -184,6 +185,7 @@ def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=
                      _ptr(angle_init), _ptr(prev_bx_init), _ptr(y), _ptr(h_final), _ptr(angle_final),
                      _ptr(prev_bx_final), _ptr(err))
     a.algo = int(algo)
+    a.state_only = int(bool(state_only))
     if stage_events is not None:
         if len(stage_events) != len(LAYER_FWD_STAGES) + 1:
             raise M3bError("stage_events needs one event per stage plus one")

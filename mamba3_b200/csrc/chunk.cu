@@ -592,6 +592,7 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
     f.h_final = a->h_final;
     f.angle_last = angle_last;
     f.err = a->err;
+    f.state_only = a->state_only != 0;
     if ((rc = launch_fused(f, st, a->act_dtype == M3B_BF16)) != M3B_OK) return rc;
     if (a->angle_final) {
       const cudaError_t e = cudaMemcpyAsync(a->angle_final, angle_last, (size_t)fp.B * p.H * (p.N / 2) * 4,

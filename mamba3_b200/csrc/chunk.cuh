@@ -69,6 +69,7 @@ struct FusedParams {
   float* h_final;
   float* angle_last;  // (B,H,N/2): angle after the last token (always written)
   int* err;
+  bool state_only;    // y not needed: the kernel may skip the outputs (TMA path)
 };
 
 // Fused sequential path (fused.cu): supported shapes and launcher.

@@ -224,11 +224,14 @@ __device__ __forceinline__ void st_pack_chunk(uint8_t* tile, int row, int c8, co
 // theta of a chunk then arrive by tensor-memory-accelerator copies straight into the stage's
 // B / C / W tiles, and each producer warp rewrites its tokens in place; otherwise every
 // producer thread loads its raw values from global memory into registers.
-template <typename TA, int R, bool TMA>
+// SO (state only, TMA path): the caller needs the final state but not y, so C^, S, the mask,
+// P'W, C^H'^T and the output are skipped; what remains is B^, W and H += B^^T W per chunk.
+template <typename TA, int R, bool TMA, bool SO>
 __global__ void __launch_bounds__(kFusedThreads, 1)
     ssd_fused_kernel(FusedParams a, Sched sc, const __grid_constant__ CUtensorMap tm_bc,
                      const __grid_constant__ CUtensorMap tm_th) {
   static_assert(!TMA || sizeof(TA) == 2, "the TMA producer path stages bf16 rows");
+  static_assert(!SO || TMA, "the state-only variant is built on the TMA path");
   constexpr bool N128 = TMA;
   constexpr int RP = rp_of(R);
   using PL = FPlan<RP>;
@@ -293,12 +296,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     if constexpr (TMA) {
       uint8_t* stg = sm + (gg & 1) * PL::kStage;
       constexpr uint32_t kHalf = 16384;
-      mbar_arrive_expect_tx(bar, 4 * kHalf + (p.complex_ssm ? (uint32_t)L * 128u : 0u));
+      mbar_arrive_expect_tx(bar, (SO ? 2 : 4) * kHalf + (p.complex_ssm ? (uint32_t)L * 128u : 0u));
       const int xb = offB + c.grp * NR, xc = offC + c.grp * NR, ti = c.k * L;
       tma_load_3d(stg + PL::tB, &tm_bc, xb, ti, c.b, bar);
       tma_load_3d(stg + PL::tB + kHalf, &tm_bc, xb + NR / 2, ti, c.b, bar);
-      tma_load_3d(stg + PL::tC, &tm_bc, xc, ti, c.b, bar);
-      tma_load_3d(stg + PL::tC + kHalf, &tm_bc, xc + NR / 2, ti, c.b, bar);
+      if constexpr (!SO) {
+        tma_load_3d(stg + PL::tC, &tm_bc, xc, ti, c.b, bar);
+        tma_load_3d(stg + PL::tC + kHalf, &tm_bc, xc + NR / 2, ti, c.b, bar);
+      }
       if (p.complex_ssm) tma_load_3d(stg + PL::tW, &tm_th, offTh, ti, c.b, bar);
     } else {
       mbar_arrive(bar);
@@ -610,7 +615,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           for (int r = 0; r < RP; ++r) {
             const uint32_t o = sw128_offset(j * RP + r, 2 * pi, 128);
             *reinterpret_cast<uint32_t*>(st + PL::tB + o) = ob[r];
-            *reinterpret_cast<uint32_t*>(st + PL::tC + o) = oc[r];
+            if constexpr (!SO) *reinterpret_cast<uint32_t*>(st + PL::tC + o) = oc[r];
           }
         }
         if (seg == nseg - 1) {
@@ -631,14 +636,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       named_bar(kBarProd, kProdThreads);  // B^, C^ tiles and the token scalars (wst, gbw) complete
       if (ptid == 0) {
         mbar_arrive(&bars[BAR_FULL0 + s]);
-        // S_g = C^ B^T into S[g%2] (free: the epilogue released this stage before handing it over)
-        tc_fence_after();
-        const uint32_t cs0 = kColS + 128 * s;
+        if constexpr (!SO) {
+          // S_g = C^ B^T into S[g%2] (free: the epilogue released this stage before handing it over)
+          tc_fence_after();
+          const uint32_t cs0 = kColS + 128 * s;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tbase + cs0, kmajor_desc(st + PL::tC, 128, kk * 16), kmajor_desc(st + PL::tB, 128, kk * 16),
-                    idS, kk > 0 ? 1u : 0u);
-        umma_commit(&bars[BAR_SDONE0 + s]);
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tbase + cs0, kmajor_desc(st + PL::tC, 128, kk * 16), kmajor_desc(st + PL::tB, 128, kk * 16),
+                      idS, kk > 0 ? 1u : 0u);
+          umma_commit(&bars[BAR_SDONE0 + s]);
+        }
         M3B_TL(g, 4);
       }
     }
@@ -691,7 +698,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             oxw[e2] = pack_bf16x2(v.x, v.y);
             oww[e2] = pack_bf16x2(vw.x, vw.y);
           }
-          sw128_store_chunk(stg + PL::tX, j * RP + q, xpc, 128, ox);
+          if constexpr (!SO) sw128_store_chunk(stg + PL::tX, j * RP + q, xpc, 128, ox);
           sw128_store_chunk(stg + PL::tW, j * RP + q, xpc, 128, ow);
         }
       }
@@ -704,10 +711,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       uint8_t* st = sm + s * PL::kStage;
       tc_fence_after();
       const uint32_t cyi = kColYi + 64 * s;
+      if constexpr (!SO) {
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma_bf16(tbase + cyi, kmajor_desc(st + PL::tC, 128, kk * 16), mnmajor_desc(tileH, 128, kk * 16), idO,
-                  kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tbase + cyi, kmajor_desc(st + PL::tC, 128, kk * 16), mnmajor_desc(tileH, 128, kk * 16), idO,
+                    kk > 0 ? 1u : 0u);
+      }
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
         umma_bf16(tbase + kColH, mnmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(st + PL::tW, 128, kk * 16),
@@ -792,196 +801,203 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const float* gbw = scal + 5 * NA;
       const uint32_t cs0 = kColS + 128 * s;
       if (g + 1 < G) load_x(pnext, xn);
-      if constexpr (TMA) {  // z of the next chunk into L2 (its loads below are a chunk later)
+      if constexpr (TMA && !SO) {  // z of the next chunk into L2 (its loads below are a chunk later)
         if (lead && g + 1 < G) tma_prefetch_3d(&tm_th, pnext.h * P, pnext.k * L, pnext.b);
       }
-      // z of this thread's row (t, r) and column half, prefetched while the tensor core works
-      const int64_t tok = (int64_t)k * L + t;
-      const bool row_ok = tok < a.T && r < R;
-      Raw8<TA> zr[4];
-      {
-        const TA* zrow = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride + (int64_t)h * P + 32 * ch;
+      if constexpr (SO) {
+        // state only: the H update of chunk g must be complete before the stage is handed
+        // over and before state(g+1) reads H
+        if (!(ok = role_wait(&bars[BAR_HDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
+        tc_fence_after();
+      } else {
+        // z of this thread's row (t, r) and column half, prefetched while the tensor core works
+        const int64_t tok = (int64_t)k * L + t;
+        const bool row_ok = tok < a.T && r < R;
+        Raw8<TA> zr[4];
+        {
+          const TA* zrow = proj + ((int64_t)b * a.T + (tok < a.T ? tok : 0)) * a.proj_stride + (int64_t)h * P + 32 * ch;
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          if (row_ok && 32 * ch + c8 * 8 < P) zr[c8].load(zrow + c8 * 8);
-          else zr[c8].zero();
+          for (int c8 = 0; c8 < 4; ++c8) {
+            if (row_ok && 32 * ch + c8 * 8 < P) zr[c8].load(zrow + c8 * 8);
+            else zr[c8].zero();
+          }
         }
-      }
-      // S_g (producer) and Yi_g / H update (this role) must be complete before P overwrites B^
-      if (lead && !*abort_flag) {
-        if (!mbar_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1) || !mbar_wait(&bars[BAR_HDONE], g & 1)) {
-          *abort_flag = 1;
-          record_error(a.err, M3B_ERR_TIMEOUT);
+        // S_g (producer) and Yi_g / H update (this role) must be complete before P overwrites B^
+        if (lead && !*abort_flag) {
+          if (!mbar_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1) || !mbar_wait(&bars[BAR_HDONE], g & 1)) {
+            *abort_flag = 1;
+            record_error(a.err, M3B_ERR_TIMEOUT);
+          }
         }
-      }
-      __syncwarp();
-      named_bar(kBarEpi, kEpiThreads);
-      if (*abort_flag) break;
-      tc_fence_after();
-      if (lead) M3B_TL(g, 8);
-      // ---- mask.  The intra-chunk weight of (token t, source s <= t) is
-      //   w(t, s) = 2^(cum_t - cum_s) * (s < t ? gamma_s + (1-lam_{s+1}) dt_{s+1} : gamma_s).
-      // Separable form (the chunk's decay range cum_0 - cum_{L-1} <= kSepRange): for s < t,
-      // w = e_t * wst_s with e_t = 2^(cum_t - cum_{L-1}) and wst_s the state-update weight, so
-      // Y = diag(e) * P' * W with P' = S masked (s < t: S; s = t: S gamma_t / gbw_t; s > t: 0)
-      // and W the chunk-state tile: no per-element exponentials.  Otherwise P = S * w, Y = P X.
-      // Column block blk (32 columns) of warp quadrant lq lies below (blk < lq), on (blk == lq)
-      // or above (blk > lq) the block diagonal, for every lane alike.
-      constexpr float kSepRange = 64.f;
-      const float c_last = cum2[L - 1];
-      const bool sep = cum2[0] - c_last <= kSepRange;
-      {
-        const float ct = cum2[t];
-        const float gwt = gbw[t];
-        const float rat = gwt > 0.f ? gam[t] / gwt : 0.f;
+        __syncwarp();
+        named_bar(kBarEpi, kEpiThreads);
+        if (*abort_flag) break;
+        tc_fence_after();
+        if (lead) M3B_TL(g, 8);
+        // ---- mask.  The intra-chunk weight of (token t, source s <= t) is
+        //   w(t, s) = 2^(cum_t - cum_s) * (s < t ? gamma_s + (1-lam_{s+1}) dt_{s+1} : gamma_s).
+        // Separable form (the chunk's decay range cum_0 - cum_{L-1} <= kSepRange): for s < t,
+        // w = e_t * wst_s with e_t = 2^(cum_t - cum_{L-1}) and wst_s the state-update weight, so
+        // Y = diag(e) * P' * W with P' = S masked (s < t: S; s = t: S gamma_t / gbw_t; s > t: 0)
+        // and W the chunk-state tile: no per-element exponentials.  Otherwise P = S * w, Y = P X.
+        // Column block blk (32 columns) of warp quadrant lq lies below (blk < lq), on (blk == lq)
+        // or above (blk > lq) the block diagonal, for every lane alike.
+        constexpr float kSepRange = 64.f;
+        const float c_last = cum2[L - 1];
+        const bool sep = cum2[0] - c_last <= kSepRange;
+        {
+          const float ct = cum2[t];
+          const float gwt = gbw[t];
+          const float rat = gwt > 0.f ? gam[t] / gwt : 0.f;
 #pragma unroll
-        for (int c32 = 0; c32 < 2; ++c32) {
-          const int blk = 2 * ch + c32;
-          const int c0 = 32 * blk;
-          float v[32];
-          if (blk > lq) {
+          for (int c32 = 0; c32 < 2; ++c32) {
+            const int blk = 2 * ch + c32;
+            const int c0 = 32 * blk;
+            float v[32];
+            if (blk > lq) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = 0.f;
-          } else {
-            tmem_ld32(trow + cs0 + c0, v);
-            if (lead && c32 == 0) M3B_TL(g, 13);
-            if (sep) {
-              if (blk == lq) {
+              for (int e = 0; e < 32; ++e) v[e] = 0.f;
+            } else {
+              tmem_ld32(trow + cs0 + c0, v);
+              if (lead && c32 == 0) M3B_TL(g, 13);
+              if (sep) {
+                if (blk == lq) {
+#pragma unroll
+                  for (int jj = 0; jj < 32; jj += RP) {
+                    const int sj = (c0 + jj) / RP;
+                    const float f = sj < t ? 1.f : (sj == t ? rat : 0.f);
+#pragma unroll
+                    for (int q = 0; q < RP; ++q) v[jj + q] *= f;
+                  }
+                }
+              } else {
 #pragma unroll
                 for (int jj = 0; jj < 32; jj += RP) {
                   const int sj = (c0 + jj) / RP;
-                  const float f = sj < t ? 1.f : (sj == t ? rat : 0.f);
+                  const float e = ex2_fast(fminf(ct - cum2[sj], 0.f));
+                  const float w = sj < t ? e * gbw[sj] : (sj == t ? gam[sj] : 0.f);
+                  if constexpr (RP >= 2) {
 #pragma unroll
-                  for (int q = 0; q < RP; ++q) v[jj + q] *= f;
-                }
-              }
-            } else {
-#pragma unroll
-              for (int jj = 0; jj < 32; jj += RP) {
-                const int sj = (c0 + jj) / RP;
-                const float e = ex2_fast(fminf(ct - cum2[sj], 0.f));
-                const float w = sj < t ? e * gbw[sj] : (sj == t ? gam[sj] : 0.f);
-                if constexpr (RP >= 2) {
-#pragma unroll
-                  for (int q = 0; q < RP; q += 2) {
-                    const float2 pr = mul2(make_float2(v[jj + q], v[jj + q + 1]), make_float2(w, w));
-                    v[jj + q] = pr.x;
-                    v[jj + q + 1] = pr.y;
+                    for (int q = 0; q < RP; q += 2) {
+                      const float2 pr = mul2(make_float2(v[jj + q], v[jj + q + 1]), make_float2(w, w));
+                      v[jj + q] = pr.x;
+                      v[jj + q + 1] = pr.y;
+                    }
+                  } else {
+                    v[jj] *= w;
                   }
-                } else {
-                  v[jj] *= w;
                 }
               }
             }
-          }
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            float v8[8];
+            for (int cc = 0; cc < 4; ++cc) {
+              float v8[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v8[e] = v[8 * cc + e];
-            st_pack_chunk(st + PL::tB, m, c0 / 8 + cc, v8);
+              for (int e = 0; e < 8; ++e) v8[e] = v[8 * cc + e];
+              st_pack_chunk(st + PL::tB, m, c0 / 8 + cc, v8);
+            }
+            if (lead && c32 == 0) M3B_TL(g, 14);
           }
-          if (lead && c32 == 0) M3B_TL(g, 14);
         }
-      }
-      fence_async_smem();
-      tc_fence_before();
-      named_bar(kBarEpi, kEpiThreads);
-      if (lead) {
-        // Y_g = P' W (separable) or P X into the first 64 columns of S[g%2] (the mask has consumed S_g)
+        fence_async_smem();
+        tc_fence_before();
+        named_bar(kBarEpi, kEpiThreads);
+        if (lead) {
+          // Y_g = P' W (separable) or P X into the first 64 columns of S[g%2] (the mask has consumed S_g)
+          tc_fence_after();
+          const uint8_t* yb = st + (sep ? PL::tW : PL::tX);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tbase + cs0, kmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(yb, 128, kk * 16), idO,
+                      kk > 0 ? 1u : 0u);
+          umma_commit(&bars[BAR_YDONE]);
+          M3B_TL(g, 9);
+        }
+        // ---- output of chunk g (x_r comes from the X tile of this stage)
+        if (!(ok = role_wait(&bars[BAR_YDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
         tc_fence_after();
-        const uint8_t* yb = st + (sep ? PL::tW : PL::tX);
+        if (lead) M3B_TL(g, 10);
+        {
+          const float ec = exp2f(cum2[t]);
+          const float et = sep ? exp2f(cum2[t] - c_last) : 1.f;
+          const float Dh = ldf(p.D, h, p.param_dtype);
+          const float2 et2 = make_float2(et, et), ec2 = make_float2(ec, ec), D2 = make_float2(Dh, Dh);
+          TA* yo = reinterpret_cast<TA*>(a.y) + ((int64_t)b * a.T + tok) * HP + (int64_t)h * P;
+          const uint32_t cyi = kColYi + 64 * s;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tbase + cs0, kmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(yb, 128, kk * 16), idO,
-                    kk > 0 ? 1u : 0u);
-        umma_commit(&bars[BAR_YDONE]);
-        M3B_TL(g, 9);
-      }
-      // ---- output of chunk g (x_r comes from the X tile of this stage)
-      if (!(ok = role_wait(&bars[BAR_YDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
-      tc_fence_after();
-      if (lead) M3B_TL(g, 10);
-      {
-        const float ec = exp2f(cum2[t]);
-        const float et = sep ? exp2f(cum2[t] - c_last) : 1.f;
-        const float Dh = ldf(p.D, h, p.param_dtype);
-        const float2 et2 = make_float2(et, et), ec2 = make_float2(ec, ec), D2 = make_float2(Dh, Dh);
-        TA* yo = reinterpret_cast<TA*>(a.y) + ((int64_t)b * a.T + tok) * HP + (int64_t)h * P;
-        const uint32_t cyi = kColYi + 64 * s;
+          for (int qq = 0; qq < 2; ++qq) {
+            // 16 columns of Y and of Yi in flight at once, combined right away
+            uint32_t yraw[16], yiraw[16];
+            tmem_ld16_async(trow + cs0 + 32 * ch + 16 * qq, yraw);
+            tmem_ld16_async(trow + cyi + 32 * ch + 16 * qq, yiraw);
+            tmem_wait_ld(yraw, yiraw);
+            float ysum[16];
 #pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-          // 16 columns of Y and of Yi in flight at once, combined right away
-          uint32_t yraw[16], yiraw[16];
-          tmem_ld16_async(trow + cs0 + 32 * ch + 16 * qq, yraw);
-          tmem_ld16_async(trow + cyi + 32 * ch + 16 * qq, yiraw);
-          tmem_wait_ld(yraw, yiraw);
-          float ysum[16];
-#pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            const float2 v = fma2(et2, make_float2(__uint_as_float(yraw[i]), __uint_as_float(yraw[i + 1])),
-                                  mul2(ec2, make_float2(__uint_as_float(yiraw[i]), __uint_as_float(yiraw[i + 1]))));
-            ysum[i] = v.x;
-            ysum[i + 1] = v.y;
-          }
-          float acc[16];
-#pragma unroll
-          for (int hc = 0; hc < 2; ++hc) {
-            const int c8 = 2 * qq + hc;  // chunk within this column half
-            const int p8 = 32 * ch + c8 * 8;
-            const uint4 xq = *reinterpret_cast<const uint4*>(st + PL::tX + sw128_offset(m, p8, 128));
-            const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
-            const float4* mz4 = reinterpret_cast<const float4*>(emz + r * kPP + p8);
-            const float4* md4 = reinterpret_cast<const float4*>(emd + r * kPP + p8);
-            const float4 za = mz4[0], zb = mz4[1], da = md4[0], db = md4[1];
-            const float2 mzp[4] = {make_float2(za.x, za.y), make_float2(za.z, za.w), make_float2(zb.x, zb.y),
-                                   make_float2(zb.z, zb.w)};
-            const float2 mdp[4] = {make_float2(da.x, da.y), make_float2(da.z, da.w), make_float2(db.x, db.y),
-                                   make_float2(db.z, db.w)};
-#pragma unroll
-            for (int e2 = 0; e2 < 4; ++e2) {
-              const int i = 8 * hc + 2 * e2;
-              const float2 yv = fma2(D2, bf2_to_f2(xw[e2]), make_float2(ysum[i], ysum[i + 1]));
-              const float2 gz = silu_fast2(mul2(zr[c8].pair(2 * e2), mzp[e2]));
-              const float2 o = mul2(mul2(yv, gz), mdp[e2]);
-              acc[i] = o.x;
-              acc[i + 1] = o.y;
+            for (int i = 0; i < 16; i += 2) {
+              const float2 v = fma2(et2, make_float2(__uint_as_float(yraw[i]), __uint_as_float(yraw[i + 1])),
+                                    mul2(ec2, make_float2(__uint_as_float(yiraw[i]), __uint_as_float(yiraw[i + 1]))));
+              ysum[i] = v.x;
+              ysum[i + 1] = v.y;
             }
-          }
+            float acc[16];
 #pragma unroll
-          for (int o = 1; o < RP; o <<= 1) {
+            for (int hc = 0; hc < 2; ++hc) {
+              const int c8 = 2 * qq + hc;  // chunk within this column half
+              const int p8 = 32 * ch + c8 * 8;
+              const uint4 xq = *reinterpret_cast<const uint4*>(st + PL::tX + sw128_offset(m, p8, 128));
+              const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
+              const float4* mz4 = reinterpret_cast<const float4*>(emz + r * kPP + p8);
+              const float4* md4 = reinterpret_cast<const float4*>(emd + r * kPP + p8);
+              const float4 za = mz4[0], zb = mz4[1], da = md4[0], db = md4[1];
+              const float2 mzp[4] = {make_float2(za.x, za.y), make_float2(za.z, za.w), make_float2(zb.x, zb.y),
+                                     make_float2(zb.z, zb.w)};
+              const float2 mdp[4] = {make_float2(da.x, da.y), make_float2(da.z, da.w), make_float2(db.x, db.y),
+                                     make_float2(db.z, db.w)};
 #pragma unroll
-            for (int e = 0; e < 16; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
-          }
-          if (tok < a.T) {
-            constexpr int W = 16 / RP;  // outputs written by each of the RP lanes of a token
-#pragma unroll
-            for (int rr = 0; rr < RP; ++rr) {
-              if (rr != r) continue;
-              const int p0 = 32 * ch + 16 * qq + rr * W;
-              if constexpr (W == 16) {
-                if (p0 + 16 <= P) {
-                  float o8[8];
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) o8[e] = acc[e];
-                  store8<TA>(yo + p0, o8);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) o8[e] = acc[8 + e];
-                  store8<TA>(yo + p0 + 8, o8);
-                  continue;
-                }
-              } else if constexpr (W == 8) {
-                if (p0 + 8 <= P) {
-                  float o8[8];
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) o8[e] = acc[rr * W + e];
-                  store8<TA>(yo + p0, o8);
-                  continue;
-                }
+              for (int e2 = 0; e2 < 4; ++e2) {
+                const int i = 8 * hc + 2 * e2;
+                const float2 yv = fma2(D2, bf2_to_f2(xw[e2]), make_float2(ysum[i], ysum[i + 1]));
+                const float2 gz = silu_fast2(mul2(zr[c8].pair(2 * e2), mzp[e2]));
+                const float2 o = mul2(mul2(yv, gz), mdp[e2]);
+                acc[i] = o.x;
+                acc[i + 1] = o.y;
               }
+            }
 #pragma unroll
-              for (int e = 0; e < W; ++e)
-                if (p0 + e < P) io<TA>::st(yo + p0 + e, acc[rr * W + e]);
+            for (int o = 1; o < RP; o <<= 1) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+            }
+            if (tok < a.T) {
+              constexpr int W = 16 / RP;  // outputs written by each of the RP lanes of a token
+#pragma unroll
+              for (int rr = 0; rr < RP; ++rr) {
+                if (rr != r) continue;
+                const int p0 = 32 * ch + 16 * qq + rr * W;
+                if constexpr (W == 16) {
+                  if (p0 + 16 <= P) {
+                    float o8[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o8[e] = acc[e];
+                    store8<TA>(yo + p0, o8);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o8[e] = acc[8 + e];
+                    store8<TA>(yo + p0 + 8, o8);
+                    continue;
+                  }
+                } else if constexpr (W == 8) {
+                  if (p0 + 8 <= P) {
+                    float o8[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o8[e] = acc[rr * W + e];
+                    store8<TA>(yo + p0, o8);
+                    continue;
+                  }
+                }
+#pragma unroll
+                for (int e = 0; e < W; ++e)
+                  if (p0 + e < P) io<TA>::st(yo + p0 + e, acc[rr * W + e]);
+              }
             }
           }
         }
@@ -1012,12 +1028,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           const float d = exp2f(scal1[L - 1]);
           float v[32];
           tmem_ld32(trow + kColH + 32 * ch, v);
+          if constexpr (!SO) {  // H' for C^H'^T (not issued in state-only mode)
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            float v8[8];
+            for (int c8 = 0; c8 < 4; ++c8) {
+              float v8[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v8[e] = v[8 * c8 + e];
-            st_pack_chunk(tileH, m, 4 * ch + c8, v8);
+              for (int e = 0; e < 8; ++e) v8[e] = v[8 * c8 + e];
+              st_pack_chunk(tileH, m, 4 * ch + c8, v8);
+            }
           }
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] *= d;
@@ -1101,14 +1119,14 @@ bool tma_layout_ok(const FusedParams& fp) {
          offB % 8 == 0 && (!p.complex_ssm || offTh % 8 == 0) && fp.T < (int64_t(1) << 31);
 }
 
-template <typename TA, int R, bool TMA>
+template <typename TA, int R, bool TMA, bool SO>
 int launch_fused_t(const FusedParams& fp, cudaStream_t st, const CUtensorMap& tm_bc, const CUtensorMap& tm_th) {
   constexpr int RP = rp_of(R);
   using PL = FPlan<RP>;
   const int nseq_total = (int)(fp.B * fp.prm.H);
   const int nsm = num_sms();
   const int grid = nseq_total < nsm ? nseq_total : nsm;
-  const void* fn = (const void*)ssd_fused_kernel<TA, R, TMA>;
+  const void* fn = (const void*)ssd_fused_kernel<TA, R, TMA, SO>;
   int rc;
   if ((rc = ensure_smem_f(fn, PL::bytes)) != M3B_OK) return rc;
   cudaFuncAttributes fa{};
@@ -1116,7 +1134,7 @@ int launch_fused_t(const FusedParams& fp, cudaStream_t st, const CUtensorMap& tm
     return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: %d registers/thread allow only %d threads per block (need %d)",
                 fa.numRegs, fa.maxThreadsPerBlock, kFusedThreads);
   const Sched sc{fp.K, fp.prm.H, nseq_total, grid, fp.prm.H / fp.prm.G};
-  ssd_fused_kernel<TA, R, TMA><<<grid, kFusedThreads, PL::bytes, st>>>(fp, sc, tm_bc, tm_th);
+  ssd_fused_kernel<TA, R, TMA, SO><<<grid, kFusedThreads, PL::bytes, st>>>(fp, sc, tm_bc, tm_th);
   return check_launch("ssd_fused");
 }
 
@@ -1126,9 +1144,10 @@ int launch_fused_r(const FusedParams& fp, cudaStream_t st) {
   if constexpr (sizeof(TA) == 2) {
     constexpr int L = 128 / rp_of(R);
     if (tma_layout_ok(fp) && make_proj_map(&tm_bc, fp, 64 * R, L) && make_proj_map(&tm_th, fp, 64, L))
-      return launch_fused_t<TA, R, true>(fp, st, tm_bc, tm_th);
+      return fp.state_only ? launch_fused_t<TA, R, true, true>(fp, st, tm_bc, tm_th)
+                           : launch_fused_t<TA, R, true, false>(fp, st, tm_bc, tm_th);
   }
-  return launch_fused_t<TA, R, false>(fp, st, tm_bc, tm_th);
+  return launch_fused_t<TA, R, false, false>(fp, st, tm_bc, tm_th);
 }
 }  // namespace
 

@@ -18,8 +18,8 @@ depend on a).  So:
 3. rank r folds the tuples of ranks 0 .. r-1 into its exact initial state;
 4. rank r runs the layer on its shard again from that state (prefill_from).
 
-The exchange is the only collective.  Step 1 costs a second pass over the shard, so the
-speed-up over one GPU is about G / 2 for large G; the exchange is tiny.
+The exchange is the only collective.  Step 1 asks only for the state (no C^, no intra-chunk
+products, no y), which costs a fraction of a full pass; the exchange is tiny.
 """
 
 from __future__ import annotations
@@ -102,9 +102,30 @@ def exchange(aff: dict, group=None) -> list:
     return [unpack(b, aff) for b in bufs]
 
 
+def layer_state_only(layer, proj: torch.Tensor) -> dict:
+    """The layer's state after `proj`'s tokens from the zero state, without the outputs: the
+    kernels skip C, the intra-chunk products and y where they can (m3b_layer_fwd state_only)."""
+    from . import _lib, ops
+
+    d = layer._dims()
+    H, P, N = d["H"], d["P"], d["N"]
+    prm = ops._prm(H, P, N, d["R"], d["G"], d["trapezoidal"], d["complex_ssm"], d["norm_eps"],
+                   *layer._param_tensors())
+    proj = proj.contiguous()
+    Bt, T, _ = proj.shape
+    dev = proj.device
+    y = torch.empty(Bt, T, H * P, dtype=proj.dtype, device=dev)  # required buffer; may stay unwritten
+    f32 = dict(dtype=torch.float32, device=dev)
+    st = {"h": torch.empty(Bt, H, P, N, **f32), "angle": torch.empty(Bt, H, N // 2, **f32),
+          "prev_BX": torch.empty(Bt, H, P, N, **f32)}
+    _lib.layer_fwd(prm, proj, y, h_final=st["h"], angle_final=st["angle"], prev_bx_final=st["prev_BX"],
+                   algo=ops._LAYER_ALGO, state_only=True)
+    return st
+
+
 def layer_summary(layer, proj: torch.Tensor) -> dict:
     """Step 1 on this rank's shard: the layer from the zero state, kept as an affine summary."""
-    _, st = layer.ssd_from_proj(proj, return_state=True)
+    st = layer_state_only(layer, proj)
     d = layer._dims()
     lam_sum, c0 = shard_scalars(proj, layer.A_log, layer.dt_bias, d["H"], d["P"], d["N"], d["R"], d["G"],
                                 d["trapezoidal"])

@@ -138,3 +138,21 @@ def test_sharded_prefill_on_one_gpu(shards):
     assert max_rel(torch.cat(ys, 1).float().cpu().numpy(), y_ref.float().cpu().numpy()) < 2e-2
     for k in ("h", "angle", "prev_BX"):
         assert max_rel(st[k].float().cpu().numpy(), st_ref[k].float().cpu().numpy()) < 2e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,dtype", [(1, torch.bfloat16), (2, torch.bfloat16), (4, torch.bfloat16),
+                                     (2, torch.float32)])
+def test_state_only_pass_matches_prefill_state(R, dtype):
+    """The state-only first pass (skips C^, the intra-chunk products and y on the TMA path;
+    fp32 rows take the full path) gives prefill's state."""
+    from mamba3_b200 import KulaMamba, seqpar
+
+    torch.manual_seed(20 + R)
+    m = KulaMamba(d_model=128, d_state=128, headdim=64, mimo_rank=R).cuda().to(dtype).eval()
+    x = torch.randn(2, 300, 128, generator=torch.Generator().manual_seed(R)).cuda().to(dtype)
+    with torch.no_grad():
+        _, ref = m.prefill(x)
+        st = seqpar.layer_state_only(m, m.in_proj(x))
+    for k in ("h", "angle", "prev_BX"):
+        assert max_rel(st[k].cpu().numpy(), ref[k].cpu().numpy()) < 1e-5, k
