@@ -43,6 +43,7 @@ def parse():
     ap.add_argument("--algo", type=int, default=0, help="layer algorithm: 0 auto, 1 fused, 2 chunk-parallel")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-4 decode measurement")
     ap.add_argument("--no-seqpar", action="store_true", help="skip the config-3 sequence-sharded measurement")
+    ap.add_argument("--no-lm", action="store_true", help="skip the config-2 LM forward measurement")
     ap.add_argument("--e2e-pieces", type=int, default=8,
                     help="token ranges forward_host streams the host batch in (copy/compute overlap)")
     return ap.parse_args()
@@ -202,6 +203,44 @@ def run_decode(dev, world, rank, barrier):
             "step_kernel": {"ms": ms_k, "state_bytes": state_bytes, "achieved_gbs": gbs,
                             "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
                             "batch": B, "heads": H}}
+
+
+def run_lm(dev, world, rank, barrier):
+    """Config 2: KulaMambaLM forward (vocab 32000, d_model 768, 24 layers, bf16, weights seed 2)
+    on input_ids (64, 2048) U[0, 32000), batch-sharded: 64 / G rows per rank, no collective."""
+    import torch
+    import torch.distributed as dist
+
+    from mamba3_b200 import KulaMambaLM
+
+    Bg, T = 64, 2048
+    B = max(1, Bg // world)
+    torch.manual_seed(2)
+    lm = KulaMambaLM(vocab_size=32000, d_model=768, n_layers=24, d_state=128, headdim=64, mimo_rank=2,
+                     residual_scale="depth").to(dev, torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(2)
+    ids = torch.randint(0, 32000, (Bg, T), generator=g)[rank * B:(rank + 1) * B].to(dev)
+    with torch.no_grad():
+        lm(ids)
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        a.record()
+        for _ in range(reps):
+            lm(ids)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+    del lm
+    torch.cuda.empty_cache()
+    return {"workload": f"config 2: KulaMambaLM forward, 24 layers, vocab 32000, ids ({Bg}, {T}), "
+                        f"{B} rows per GPU", "tokens_per_s": world * B * T / (ms / 1e3), "ms_per_step": ms,
+            "scaling": "strong (global batch 64 split over the GPUs)"}
 
 
 def run_seqpar(dev, world, rank, barrier):
@@ -389,6 +428,7 @@ def run_ours(args):
 
     decode = None if args.no_decode else run_decode(dev, world, rank, barrier)
     seqp = None if args.no_seqpar else run_seqpar(dev, world, rank, barrier)
+    lmf = None if args.no_lm else run_lm(dev, world, rank, barrier)
 
     if rank == 0:
         import math
@@ -441,6 +481,8 @@ def run_ours(args):
             line["decode"] = decode
         if seqp is not None:
             line["seqpar"] = seqp
+        if lmf is not None:
+            line["lm_forward"] = lmf
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_sample_tokens)
         print(json.dumps(line), flush=True)
