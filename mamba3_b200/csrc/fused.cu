@@ -494,9 +494,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
       // (2a) sum of dt * theta over my segment (dtv is visible: barrier above)
       float segsum = 0.f;
+      float pre[SEGMAX];  // running dt * theta sum of my segment, per token
 #pragma unroll
-      for (int jj = 0; jj < SEGMAX; ++jj)
+      for (int jj = 0; jj < SEGMAX; ++jj) {
         if (N128 || jj < seglen) segsum = fmaf(dtv[seg * seglen + jj], theta(jj), segsum);
+        pre[jj] = segsum;
+      }
       if (bc_act) segt[seg * nh2 + pi] = segsum;
       named_bar(kBarProd, kProdThreads);
       if (ptid == 0) M3B_TL(g, 7);
@@ -533,6 +536,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           bB0[0] = make_float2(nbB[2 * pi], nbB[2 * pi + 1]);
           wC0[0] = make_float2(nwC[2 * pi], nwC[2 * pi + 1]);
           bC0[0] = make_float2(nbC[2 * pi], nbC[2 * pi + 1]);
+        }
+        // TMA path (bf16 rows): norm and rotation in packed bf16 arithmetic straight on the raw
+        // bf16 pairs, as the reference computes them for a bf16 model; weights / biases as pairs
+        __nv_bfloat162 hwB0[RP / 2 + 1], hwB1[RP / 2 + 1], hbB0[RP / 2 + 1], hbB1[RP / 2 + 1];
+        __nv_bfloat162 hwC0[RP / 2 + 1], hwC1[RP / 2 + 1], hbC0[RP / 2 + 1], hbC1[RP / 2 + 1];
+        if constexpr (TMA) {
+          const int nrp = R % 2 == 0 ? R / 2 : 1;
+#pragma unroll
+          for (int rp = 0; rp < nrp; ++rp) {
+            hwB0[rp] = __floats2bfloat162_rn(wB0[rp].x, wB0[rp].y);
+            hbB0[rp] = __floats2bfloat162_rn(bB0[rp].x, bB0[rp].y);
+            hwC0[rp] = __floats2bfloat162_rn(wC0[rp].x, wC0[rp].y);
+            hbC0[rp] = __floats2bfloat162_rn(bC0[rp].x, bC0[rp].y);
+            if constexpr (R % 2 == 0) {
+              hwB1[rp] = __floats2bfloat162_rn(wB1[rp].x, wB1[rp].y);
+              hbB1[rp] = __floats2bfloat162_rn(bB1[rp].x, bB1[rp].y);
+              hwC1[rp] = __floats2bfloat162_rn(wC1[rp].x, wC1[rp].y);
+              hbC1[rp] = __floats2bfloat162_rn(bC1[rp].x, bC1[rp].y);
+            }
+          }
         }
         // raw (2i, 2i+1) x R blocks: registers, or shared memory (TMA path), where the whole warp
         // reads a group of TG tokens before any lane overwrites them with tile entries
@@ -575,12 +598,44 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }();
           float cs = 1.f, sn = 0.f;
           if (p.complex_ssm) {
-            run = fmaf(dtj, theta(jj), run);
+            run = off + pre[jj];
             sincos_reduced(omf - run, &sn, &cs);
           }
           const float2 rbj = make_float2(rbv, rbv), rcj = make_float2(rcv, rcv);
           uint32_t ob[RP], oc[RP];
-          if constexpr (R % 2 == 0) {
+          auto as_h2 = [](uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); };
+          auto as_u = [](__nv_bfloat162 v) { return *reinterpret_cast<const uint32_t*>(&v); };
+          if constexpr (TMA && R % 2 == 0) {
+            const __nv_bfloat162 rb2 = __float2bfloat162_rn(rbv), rc2 = __float2bfloat162_rn(rcv);
+            const __nv_bfloat162 c2 = __float2bfloat162_rn(cs), s2 = __float2bfloat162_rn(sn);
+            const __nv_bfloat162 ns2 = __hneg2(s2);
+#pragma unroll
+            for (int rp = 0; rp < R / 2; ++rp) {
+              // words: n = 2i (ranks 2rp, 2rp+1) and n = 2i+1 (same ranks)
+              const __nv_bfloat162 b0 = __hfma2(__hmul2(as_h2(rawb.w[rp]), hwB0[rp]), rb2, hbB0[rp]);
+              const __nv_bfloat162 b1 = __hfma2(__hmul2(as_h2(rawb.w[R / 2 + rp]), hwB1[rp]), rb2, hbB1[rp]);
+              const __nv_bfloat162 be = __hfma2(b1, ns2, __hmul2(b0, c2)), bo = __hfma2(b1, c2, __hmul2(b0, s2));
+              ob[2 * rp] = as_u(__lows2bfloat162(be, bo));
+              ob[2 * rp + 1] = as_u(__highs2bfloat162(be, bo));
+              if constexpr (!SO) {
+                const __nv_bfloat162 c0 = __hfma2(__hmul2(as_h2(rawc.w[rp]), hwC0[rp]), rc2, hbC0[rp]);
+                const __nv_bfloat162 c1 = __hfma2(__hmul2(as_h2(rawc.w[R / 2 + rp]), hwC1[rp]), rc2, hbC1[rp]);
+                const __nv_bfloat162 ce = __hfma2(c1, ns2, __hmul2(c0, c2)), co = __hfma2(c1, c2, __hmul2(c0, s2));
+                oc[2 * rp] = as_u(__lows2bfloat162(ce, co));
+                oc[2 * rp + 1] = as_u(__highs2bfloat162(ce, co));
+              } else {
+                oc[2 * rp] = oc[2 * rp + 1] = 0u;
+              }
+            }
+          } else if constexpr (TMA) {
+            // R = 1: the word is (n = 2i, 2i+1); (x0 c - x1 s, x0 s + x1 c) = x1 (-s, c) + x0 (c, s)
+            const __nv_bfloat162 rb2 = __float2bfloat162_rn(rbv), rc2 = __float2bfloat162_rn(rcv);
+            const __nv_bfloat162 ncs = __floats2bfloat162_rn(-sn, cs), csn = __floats2bfloat162_rn(cs, sn);
+            const __nv_bfloat162 bv = __hfma2(__hmul2(as_h2(rawb.w[0]), hwB0[0]), rb2, hbB0[0]);
+            ob[0] = as_u(__hfma2(__high2bfloat162(bv), ncs, __hmul2(__low2bfloat162(bv), csn)));
+            const __nv_bfloat162 cv = __hfma2(__hmul2(as_h2(rawc.w[0]), hwC0[0]), rc2, hbC0[0]);
+            oc[0] = as_u(__hfma2(__high2bfloat162(cv), ncs, __hmul2(__low2bfloat162(cv), csn)));
+          } else if constexpr (R % 2 == 0) {
             const float2 c2 = make_float2(cs, cs), s2 = make_float2(sn, sn), ns2 = make_float2(-sn, -sn);
 #pragma unroll
             for (int rp = 0; rp < R / 2; ++rp) {
