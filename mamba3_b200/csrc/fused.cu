@@ -1019,39 +1019,43 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
               }
             }
 #pragma unroll
-            for (int o = 1; o < RP; o <<= 1) {
+            // sum over the RP lanes (t, r) of a token, reduce-scatter style: each halving step
+            // keeps the half picked by one bit of r, so lane r ends with columns [r W, r W + W)
+            constexpr int W = 16 / RP;  // outputs written by each of the RP lanes of a token
 #pragma unroll
-              for (int e = 0; e < 16; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+            for (int o = RP / 2, w = 8; o >= 1; o >>= 1, w >>= 1) {
+              const bool up = (r & o) != 0;
+#pragma unroll
+              for (int e = 0; e < w; ++e) {
+                const float send = up ? acc[e] : acc[e + w];
+                const float keep = up ? acc[e + w] : acc[e];
+                acc[e] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+              }
             }
             if (tok < a.T) {
-              constexpr int W = 16 / RP;  // outputs written by each of the RP lanes of a token
+              const int p0 = 32 * ch + 16 * qq + r * W;
+              if (p0 + W <= P) {
+                if constexpr (W >= 8) {
 #pragma unroll
-              for (int rr = 0; rr < RP; ++rr) {
-                if (rr != r) continue;
-                const int p0 = 32 * ch + 16 * qq + rr * W;
-                if constexpr (W == 16) {
-                  if (p0 + 16 <= P) {
+                  for (int h8 = 0; h8 < W / 8; ++h8) {
                     float o8[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) o8[e] = acc[e];
-                    store8<TA>(yo + p0, o8);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) o8[e] = acc[8 + e];
-                    store8<TA>(yo + p0 + 8, o8);
-                    continue;
+                    for (int e = 0; e < 8; ++e) o8[e] = acc[8 * h8 + e];
+                    store8<TA>(yo + p0 + 8 * h8, o8);
                   }
-                } else if constexpr (W == 8) {
-                  if (p0 + 8 <= P) {
-                    float o8[8];
+                } else if constexpr (W == 4 && sizeof(TA) == 2) {
+                  uint2 o4;
+                  o4.x = pack_bf16x2(acc[0], acc[1]);
+                  o4.y = pack_bf16x2(acc[2], acc[3]);
+                  *reinterpret_cast<uint2*>(yo + p0) = o4;
+                } else {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) o8[e] = acc[rr * W + e];
-                    store8<TA>(yo + p0, o8);
-                    continue;
-                  }
+                  for (int e = 0; e < W; ++e) io<TA>::st(yo + p0 + e, acc[e]);
                 }
+              } else {
 #pragma unroll
                 for (int e = 0; e < W; ++e)
-                  if (p0 + e < P) io<TA>::st(yo + p0 + e, acc[rr * W + e]);
+                  if (p0 + e < P) io<TA>::st(yo + p0 + e, acc[e]);
               }
             }
           }
