@@ -141,8 +141,10 @@ def algorithmic_work(B, T, H=24, P=64, N=128, R=2, d_model=768, d_proj=3696):
 
 def run_decode(dev, world, rank, barrier):
     """Config 4: the 24-layer config-2 LM prefills (256 / world, 512) prompt tokens per rank and
-    decodes greedily with the CUDA-graph decoder.  Also times the step kernel of one layer alone
-    against its state bytes (h read + write, prev_BX read + write: 4 P N fp32 per (batch, head))."""
+    decodes greedily with the CUDA-graph decoder (compact previous-token state).  Also times the
+    step kernel of one layer alone against its state bytes: compact (h read + write, the previous
+    token's B^ and x_r read + write) and the reference's layout (h, prev_BX: 4 P N fp32 per
+    (batch, head))."""
     import torch
     import torch.distributed as dist
 
@@ -179,30 +181,39 @@ def run_decode(dev, world, rank, barrier):
         ms_prefill = timed(lambda: dec.prefill(ids))
         steps = new - 1
         ms_dec = timed(lambda: dec.decode(steps))
-        # the step kernel of layer 0 alone, in place on its state
+        # the step kernel of layer 0 alone, in place on a state: the compact form the decoder
+        # uses (h + the previous token's B^ and x_r) and the reference's prev_BX form
         ssm = lm.layers[0].ssm
         st = dec.states[0]
+        full = ssm.allocate_inference_state(B, device=dev)
         proj = ssm.in_proj(torch.randn(B, 768, device=dev, dtype=torch.bfloat16))
         y = torch.empty(B, ssm.nheads * ssm.headdim, device=dev, dtype=torch.bfloat16)
         dims = GraphDecoder._dims(ssm)
         prm = ssm._param_tensors()
+        run_c = lambda: ops.step_ssm_compact_(prm, dims, proj, st["h"], st["prev_B"], st["prev_x"], st["angle"], y)  # noqa: E731
+        run_f = lambda: ops.step_ssm_(prm, dims, proj, full["h"], full["prev_BX"], full["angle"], y)  # noqa: E731
         for _ in range(3):
-            ops.step_ssm_(prm, dims, proj, st["h"], st["prev_BX"], st["angle"], y)
+            run_c()
+            run_f()
         reps = 50
-        ms_k = timed(lambda: [ops.step_ssm_(prm, dims, proj, st["h"], st["prev_BX"], st["angle"], y)
-                              for _ in range(reps)]) / reps
-    H, P, N = ssm.nheads, ssm.headdim, ssm.d_state
-    state_bytes = 4 * P * N * 4 * B * H
+        ms_k = timed(lambda: [run_c() for _ in range(reps)]) / reps
+        ms_f = timed(lambda: [run_f() for _ in range(reps)]) / reps
+    H, P, N, R = ssm.nheads, ssm.headdim, ssm.d_state, ssm.mimo_rank
+    state_bytes = (2 * P * N + 2 * (N + P) * R) * 4 * B * H  # h read + write, B^ / x_r read + write
+    full_bytes = 4 * P * N * 4 * B * H
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() \
         else {"hbm_gbs": 6650.0}
     gbs = state_bytes / (ms_k / 1e3) / 1e9
+    gbs_f = full_bytes / (ms_f / 1e3) / 1e9
     return {"workload": f"config 4: 24-layer LM, prompt ({Bg}, {Tp}) + {new} greedy tokens, batch {B} per GPU, "
                         "CUDA-graph decode (GraphDecoder)",
             "decode_tokens_per_s": world * B * steps / (ms_dec / 1e3), "ms_per_token": ms_dec / steps,
             "prefill_tokens_per_s": world * B * Tp / (ms_prefill / 1e3),
-            "step_kernel": {"ms": ms_k, "state_bytes": state_bytes, "achieved_gbs": gbs,
-                            "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
-                            "batch": B, "heads": H}}
+            "step_kernel": {"ms": ms_k, "state": "compact (h + previous B^, x_r)", "state_bytes": state_bytes,
+                            "achieved_gbs": gbs, "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
+                            "batch": B, "heads": H},
+            "step_kernel_prev_bx": {"ms": ms_f, "state_bytes": full_bytes, "achieved_gbs": gbs_f,
+                                    "frac": gbs_f / peaks["hbm_gbs"]}}
 
 
 def run_lm(dev, world, rank, barrier):

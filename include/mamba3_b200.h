@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3B_ABI_VERSION 2
+#define M3B_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define M3B_API __attribute__((visibility("default")))
@@ -122,6 +122,15 @@ typedef struct m3b_step_args {
   float* bx_out;          /* (batch,H,P,N): this token's B^x (next step's prev_BX) */
   float* angle_out;       /* (batch,H,N/2) fp32 */
   void* y;                /* (batch, H*P) act_dtype: gated MIMO-down output, input of out_proj */
+  /* Compact previous-token state (no reference counterpart; opt-in): when prev_b is not NULL
+   * the previous token is given as its rotated B^ (batch,H,N,R) and MIMO x (batch,H,P,R) fp32,
+   * prev_BX = sum_r prev_b[n,r] prev_x[p,r] is rebuilt inside the kernel, prev_bx / bx_out
+   * are not used, and this token's B^ / x_r are written to prev_b_out / prev_x_out (may alias
+   * prev_b / prev_x): half the state bytes per step. */
+  const float* prev_b;
+  const float* prev_x;
+  float* prev_b_out;
+  float* prev_x_out;
 } m3b_step_args;
 M3B_API int m3b_step(const m3b_step_args* a, void* stream);
 
@@ -160,6 +169,10 @@ typedef struct m3b_layer_fwd_args {
   /* 1: the caller needs only h_final / angle_final / prev_bx_final; y must still be a valid
    * buffer, but the fused path may leave it unwritten and skips the output work. */
   int32_t state_only;
+  /* Optional compact final previous-token state (see m3b_step_args.prev_b): the last token's
+   * rotated B^ (batch,H,N,R) and MIMO x (batch,H,P,R), fp32. */
+  float* prev_b_final;
+  float* prev_x_final;
 } m3b_layer_fwd_args;
 #define M3B_LAYER_FWD_STAGES 6
 

@@ -53,7 +53,8 @@ class StepArgs(C.Structure):
     _fields_ = [("prm", LayerParams), ("batch", C.c_int64), ("proj", C.c_void_p), ("proj_stride", C.c_int64),
                 ("act_dtype", C.c_int32), ("dt_scale", C.c_void_p), ("h", C.c_void_p), ("prev_bx", C.c_void_p),
                 ("angle", C.c_void_p), ("angle_dtype", C.c_int32), ("h_out", C.c_void_p), ("bx_out", C.c_void_p),
-                ("angle_out", C.c_void_p), ("y", C.c_void_p)]
+                ("angle_out", C.c_void_p), ("y", C.c_void_p), ("prev_b", C.c_void_p), ("prev_x", C.c_void_p),
+                ("prev_b_out", C.c_void_p), ("prev_x_out", C.c_void_p)]
 
 
 class LayerFwdArgs(C.Structure):
@@ -62,7 +63,7 @@ class LayerFwdArgs(C.Structure):
                 ("h_init", C.c_void_p), ("angle_init", C.c_void_p), ("prev_bx_init", C.c_void_p), ("y", C.c_void_p),
                 ("h_final", C.c_void_p), ("angle_final", C.c_void_p), ("prev_bx_final", C.c_void_p),
                 ("err", C.c_void_p), ("stage_events", C.POINTER(C.c_void_p)), ("algo", C.c_int32),
-                ("state_only", C.c_int32)]
+                ("state_only", C.c_int32), ("prev_b_final", C.c_void_p), ("prev_x_final", C.c_void_p)]
 
 
 class SsdArgs(C.Structure):
@@ -164,18 +165,22 @@ def scan_fwd(decay, h_chunk, h_init=None, h_states=None, h_final=None):
     return h_states
 
 
-def step(prm: LayerParams, proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y):
-    dev = _cuda(proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y)
+def step(prm: LayerParams, proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y, prev_b=None,
+         prev_x=None, prev_b_out=None, prev_x_out=None):
+    """One decode step.  Either prev_bx / bx_out (the reference's (P, N) previous-token state) or
+    the compact prev_b / prev_x / prev_b_out / prev_x_out ((N, R) and (P, R)) are given."""
+    dev = _cuda(proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y, prev_b, prev_x, prev_b_out,
+                prev_x_out)
     a = StepArgs(prm, proj.shape[0], _ptr(proj), proj.stride(0), dtype_code(proj.dtype), _ptr(dt_scale), _ptr(h),
                  _ptr(prev_bx), _ptr(angle), dtype_code(angle.dtype), _ptr(h_out), _ptr(bx_out), _ptr(angle_out),
-                 _ptr(y))
+                 _ptr(y), _ptr(prev_b), _ptr(prev_x), _ptr(prev_b_out), _ptr(prev_x_out))
     with torch.cuda.device(dev):
         _check(lib().m3b_step(C.byref(a), _stream(dev)), "m3b_step")
 
 
 def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=None, prev_bx_init=None,
               h_final=None, angle_final=None, prev_bx_final=None, err=None, workspace=None, stage_events=None,
-              algo=0, state_only=False):
+              algo=0, state_only=False, prev_b_final=None, prev_x_final=None):
     """Launch the chunked layer forward; proj (B,T,d_proj) with unit stride in the last dim."""
     dev = _cuda(proj, y, dt_scale, h_init, angle_init, prev_bx_init, h_final, angle_final, prev_bx_final, err)
     Bt, T, _ = proj.shape
@@ -186,6 +191,8 @@ def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=
                      _ptr(prev_bx_final), _ptr(err))
     a.algo = int(algo)
     a.state_only = int(bool(state_only))
+    a.prev_b_final = _ptr(prev_b_final)
+    a.prev_x_final = _ptr(prev_x_final)
     if stage_events is not None:
         if len(stage_events) != len(LAYER_FWD_STAGES) + 1:
             raise M3bError("stage_events needs one event per stage plus one")

@@ -86,8 +86,8 @@ class KulaMambaBlock(nn.Module):
         h, new_state = self.ssm.step(self.ssm_norm(x), ssm_state)
         return self._mlp_residual(x + h * self.residual_scale), new_state
 
-    def prefill(self, x):
-        h, state = self.ssm.prefill(self.ssm_norm(x))
+    def prefill(self, x, compact_state=False):
+        h, state = self.ssm.prefill(self.ssm_norm(x), compact_state=compact_state)
         return self._mlp_residual(x + h * self.residual_scale), state
 
 

@@ -404,7 +404,8 @@ __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
 // prefill prev_BX = sum_r B^_{T-1}[n,r] x_r[T-1,p,r]  (mamba3/mamba3.py:248-250), fp32.
 // ---------------------------------------------------------------------------
 template <typename TA>
-__global__ void __launch_bounds__(kCT) last_bx_kernel(FwdParams a, const float* angle_last, float* prev_bx) {
+__global__ void __launch_bounds__(kCT) last_bx_kernel(FwdParams a, const float* angle_last, float* prev_bx,
+                                                       float* prev_b, float* prev_x) {
   __shared__ float sB[kNS * 8];
   __shared__ float sX[kPP * 8];
   const m3b_layer_params& p = a.prm;
@@ -432,6 +433,12 @@ __global__ void __launch_bounds__(kCT) last_bx_kernel(FwdParams a, const float* 
     }
     __syncthreads();
   }
+  if (prev_b) {  // compact form: the last token's B^ (N, R) and x_r (P, R)
+    const int64_t bh = (int64_t)b * H + h;
+    for (int e = threadIdx.x; e < NR; e += kCT) prev_b[bh * NR + e] = sB[e];
+    for (int e = threadIdx.x; e < P * R; e += kCT) prev_x[bh * P * R + e] = sX[e];
+  }
+  if (!prev_bx) return;
   float* out = prev_bx + ((int64_t)b * H + h) * (int64_t)P * N;
   for (int e = threadIdx.x; e < P * N; e += kCT) {
     const int pp = e / N, n = e % N;
@@ -600,8 +607,9 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
       if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "angle_final: %s", cudaGetErrorString(e));
     }
     mark(5);
-    if (a->prev_bx_final) {
-      last_bx_kernel<TA><<<(unsigned)(fp.B * p.H), kCT, 0, st>>>(fp, angle_last, a->prev_bx_final);
+    if (a->prev_bx_final || a->prev_b_final) {
+      last_bx_kernel<TA><<<(unsigned)(fp.B * p.H), kCT, 0, st>>>(fp, angle_last, a->prev_bx_final, a->prev_b_final,
+                                                                 a->prev_x_final);
       if ((rc = check_launch("last_bx")) != M3B_OK) return rc;
     }
     mark(6);
@@ -625,8 +633,9 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
   }
   if ((rc = run_rank<TA, TS>(fp, a, st, mark)) != M3B_OK) return rc;
   mark(5);
-  if (a->prev_bx_final) {
-    last_bx_kernel<TA><<<(unsigned)(fp.B * p.H), kCT, 0, st>>>(fp, angle_last, a->prev_bx_final);
+  if (a->prev_bx_final || a->prev_b_final) {
+    last_bx_kernel<TA><<<(unsigned)(fp.B * p.H), kCT, 0, st>>>(fp, angle_last, a->prev_bx_final, a->prev_b_final,
+                                                               a->prev_x_final);
     if ((rc = check_launch("last_bx")) != M3B_OK) return rc;
   }
   mark(6);

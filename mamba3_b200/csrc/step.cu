@@ -24,7 +24,9 @@ constexpr int kStepMaxP = 256;
 
 // ROW32: N = 128, so the 32 float4 of one state row are the 32 lanes of one warp (R a power of
 // two, so that the readout's reduce-scatter halves evenly).
-template <typename TA, int R, bool ROW32>
+// COMPACT: the previous token is kept as its rotated B^ (N, R) and MIMO x (P, R) instead of the
+// (P, N) product prev_BX, which the state loop rebuilds on the fly: half the state traffic.
+template <typename TA, int R, bool ROW32, bool COMPACT>
 __global__ void __launch_bounds__(kStepThreads) step_kernel(m3b_step_args a) {
   const m3b_layer_params& prm = a.prm;
   const int H = prm.H, P = prm.P, N = prm.N, G = prm.G;
@@ -43,26 +45,37 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(m3b_step_args a) {
   __shared__ float sY[kStepMaxP * R];
   __shared__ float sRed[2][kStepThreads / 32];
   __shared__ float sScal[4];  // dA, gamma, beta, dt
+  // COMPACT: previous token's B^ (rank-major) and x_r
+  __shared__ __align__(16) float sPB[COMPACT ? kStepMaxN * R : 4];
+  __shared__ float sPX[COMPACT ? kStepMaxP * R : 4];
 
   // The first batch of the (P, N) state is requested before anything else: its HBM latency
   // then overlaps the per-token operand preparation below.
   const int64_t sbase = ((int64_t)b * H + h) * (int64_t)P * N;
   const float4* h4 = reinterpret_cast<const float4*>(a.h + sbase);
-  const float4* p4 = reinterpret_cast<const float4*>(a.prev_bx + sbase);
+  const float4* p4 = COMPACT ? nullptr : reinterpret_cast<const float4*>(a.prev_bx + sbase);
   const int nvec = P * N / 4;
   constexpr int BATCH = 8;
-  float4 hv[BATCH], pv[BATCH];
+  float4 hv[BATCH], pv[COMPACT ? 1 : BATCH];
   auto load_batch = [&](int f0) {
 #pragma unroll
     for (int u = 0; u < BATCH; ++u) {
       const int f = f0 + u * kStepThreads + tid;
       if (f < nvec) {
         hv[u] = __ldcs(h4 + f);
-        pv[u] = __ldcs(p4 + f);
+        if constexpr (!COMPACT) pv[u] = __ldcs(p4 + f);
       }
     }
   };
   load_batch(0);
+  if constexpr (COMPACT) {
+    const int64_t bh = (int64_t)b * H + h;
+    for (int e = tid; e < N * R; e += kStepThreads) {  // (n, r), r fastest
+      const int n = e / R, r = e - (e / R) * R;
+      sPB[r * N + n] = a.prev_b[bh * N * R + e];
+    }
+    for (int e = tid; e < P * R; e += kStepThreads) sPX[e] = a.prev_x[bh * P * R + e];
+  }
 
   const TA* row = reinterpret_cast<const TA*>(a.proj) + (int64_t)b * a.proj_stride;
   const int HP = H * P;
@@ -204,7 +217,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(m3b_step_args a) {
   // --- stream the state: float4 f covers (p, n0..n0+3)
   const float dA = sScal[0], gamma = sScal[1], beta = sScal[2];
   float4* ho4 = reinterpret_cast<float4*>(a.h_out + sbase);
-  float4* bo4 = reinterpret_cast<float4*>(a.bx_out + sbase);
+  float4* bo4 = COMPACT ? nullptr : reinterpret_cast<float4*>(a.bx_out + sbase);
   const int gsz = N / 4;                                     // lanes per state row
   const bool pow2 = (gsz & (gsz - 1)) == 0;
   const int lane = tid & 31, wid = tid >> 5;
@@ -222,7 +235,22 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(m3b_step_args a) {
       for (int r = 0; r < R; ++r) yr[r] = 0.f;
       if (ok) {
         const float hin[4] = {hv[u].x, hv[u].y, hv[u].z, hv[u].w};
-        const float pin[4] = {pv[u].x, pv[u].y, pv[u].z, pv[u].w};
+        float pin[4];
+        if constexpr (COMPACT) {  // prev_BX[p, n] = sum_r prev_B[n, r] prev_x[p, r]
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) pin[jj] = 0.f;
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const float4 q4 = *reinterpret_cast<const float4*>(sPB + r * N + n0);
+            const float px = sPX[p * R + r];
+            pin[0] = fmaf(q4.x, px, pin[0]);
+            pin[1] = fmaf(q4.y, px, pin[1]);
+            pin[2] = fmaf(q4.z, px, pin[2]);
+            pin[3] = fmaf(q4.w, px, pin[3]);
+          }
+        } else {
+          pin[0] = pv[u].x, pin[1] = pv[u].y, pin[2] = pv[u].z, pin[3] = pv[u].w;
+        }
         float hn[4], bx[4];
         float bq[R][4], cq[R][4], xq[R];
 #pragma unroll
@@ -244,7 +272,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(m3b_step_args a) {
           for (int r = 0; r < R; ++r) yr[r] = fmaf(cq[r][jj], hn[jj], yr[r]);
         }
         __stcs(ho4 + f, make_float4(hn[0], hn[1], hn[2], hn[3]));
-        __stcs(bo4 + f, make_float4(bx[0], bx[1], bx[2], bx[3]));
+        if constexpr (!COMPACT) __stcs(bo4 + f, make_float4(bx[0], bx[1], bx[2], bx[3]));
       }
       if constexpr (ROW32) {
 #pragma unroll
@@ -304,6 +332,14 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(m3b_step_args a) {
     }
   }
   __syncthreads();
+  if constexpr (COMPACT) {  // this token's B^ and x_r are the next step's previous token
+    const int64_t bh = (int64_t)b * H + h;
+    for (int e = tid; e < N * R; e += kStepThreads) {
+      const int n = e / R, r = e - (e / R) * R;
+      a.prev_b_out[bh * N * R + e] = sB[r * N + n];
+    }
+    for (int e = tid; e < P * R; e += kStepThreads) a.prev_x_out[bh * P * R + e] = sXr[e];
+  }
   // --- readout + D, gate, MIMO down
   TA* yo = reinterpret_cast<TA*>(a.y) + (int64_t)b * HP + (int64_t)h * P;
   for (int p = tid; p < P; p += kStepThreads) {
@@ -318,10 +354,14 @@ template <typename TA>
 static int launch_step_t(const m3b_step_args* a, cudaStream_t st) {
   const unsigned grid = (unsigned)(a->batch * a->prm.H);
   const bool row32 = a->prm.N == 128;
-#define M3B_STEP_CASE(RR)                                                                   \
-  case RR:                                                                                  \
-    if (row32 && (RR & (RR - 1)) == 0) step_kernel<TA, RR, (RR & (RR - 1)) == 0><<<grid, kStepThreads, 0, st>>>(*a); \
-    else step_kernel<TA, RR, false><<<grid, kStepThreads, 0, st>>>(*a);                     \
+  const bool compact = a->prev_b != nullptr;
+#define M3B_STEP_ROW(RR, CP)                                                                            \
+  if (row32 && (RR & (RR - 1)) == 0) step_kernel<TA, RR, (RR & (RR - 1)) == 0, CP><<<grid, kStepThreads, 0, st>>>(*a); \
+  else step_kernel<TA, RR, false, CP><<<grid, kStepThreads, 0, st>>>(*a);
+#define M3B_STEP_CASE(RR)                   \
+  case RR:                                  \
+    if (compact) { M3B_STEP_ROW(RR, true) } \
+    else { M3B_STEP_ROW(RR, false) }        \
     break;
   switch (a->prm.R) {
     M3B_STEP_CASE(1)
@@ -331,18 +371,23 @@ static int launch_step_t(const m3b_step_args* a, cudaStream_t st) {
     default: return fail(M3B_ERR_UNSUPPORTED, "step: mimo_rank %d not built (1..4)", a->prm.R);
   }
 #undef M3B_STEP_CASE
+#undef M3B_STEP_ROW
   return check_launch("step");
 }
 
 int launch_step(const m3b_step_args* a, cudaStream_t st) {
   const m3b_layer_params& p = a->prm;
-  if (!a->proj || !a->h || !a->prev_bx || !a->angle || !a->h_out || !a->bx_out || !a->angle_out || !a->y)
+  const bool compact = a->prev_b != nullptr;
+  if (!a->proj || !a->h || !a->angle || !a->h_out || !a->angle_out || !a->y)
     return fail(M3B_ERR_INVALID_ARG, "step: null pointer");
+  if (compact ? (!a->prev_x || !a->prev_b_out || !a->prev_x_out) : (!a->prev_bx || !a->bx_out))
+    return fail(M3B_ERR_INVALID_ARG, "step: null previous-token state (%s form)", compact ? "compact" : "prev_BX");
   if (p.H <= 0 || p.P <= 0 || p.N <= 0 || p.R <= 0 || p.G <= 0 || p.H % p.G != 0)
     return fail(M3B_ERR_INVALID_ARG, "step: bad dims H=%d P=%d N=%d R=%d G=%d", p.H, p.P, p.N, p.R, p.G);
   if (p.N % 4 != 0 || p.N > kStepMaxN || p.P > kStepMaxP)
     return fail(M3B_ERR_UNSUPPORTED, "step: needs N %% 4 == 0, N <= %d, P <= %d", kStepMaxN, kStepMaxP);
-  if (!aligned16(a->h) || !aligned16(a->prev_bx) || !aligned16(a->h_out) || !aligned16(a->bx_out))
+  if (!aligned16(a->h) || !aligned16(a->h_out) ||
+      (!compact && (!aligned16(a->prev_bx) || !aligned16(a->bx_out))))
     return fail(M3B_ERR_ALIGNMENT, "step: state buffers must be 16-byte aligned");
   if (a->batch <= 0) return M3B_OK;
   if (a->batch * p.H > 0x7fffffffLL) return fail(M3B_ERR_INVALID_ARG, "step: batch*H too large");

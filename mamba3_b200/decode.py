@@ -7,8 +7,10 @@ decode step -- embedding, the layers (norms, in_proj, step kernel, out_proj, MLP
 norm, lm_head and the sampling rule -- in a CUDA graph that it replays once per token.  The
 tokens collect on the device; the host reads them once at the end.
 
-Same results as KulaMambaLM.generate with the same sampling arguments (the same kernels run
-in the same order); greedy decoding (temperature 0) is deterministic.
+Same results as KulaMambaLM.generate with the same sampling arguments; greedy decoding
+(temperature 0) is deterministic.  By default the decoder keeps each layer's previous token in
+the compact form (its rotated B^ and MIMO x, allocate_inference_state(compact=True)), which
+halves the state bytes every step moves; compact=False keeps the reference's prev_BX.
 """
 
 from __future__ import annotations
@@ -19,7 +21,7 @@ from . import ops
 
 
 class GraphDecoder:
-    def __init__(self, lm, batch_size: int, max_new_tokens: int):
+    def __init__(self, lm, batch_size: int, max_new_tokens: int, compact: bool = True):
         self.lm = lm
         self.B = int(batch_size)
         self.n = int(max_new_tokens)
@@ -28,7 +30,9 @@ class GraphDecoder:
         if self.dev.type != "cuda":
             raise RuntimeError("GraphDecoder needs the model on a CUDA device")
         self.layers = list(lm.layers)
-        self.states = [blk.ssm.allocate_inference_state(self.B, device=self.dev) for blk in self.layers]
+        self.compact = bool(compact)
+        self.states = [blk.ssm.allocate_inference_state(self.B, device=self.dev, compact=self.compact)
+                       for blk in self.layers]
         self.dims = [self._dims(blk.ssm) for blk in self.layers]
         self.ybuf = [torch.empty(self.B, blk.ssm.nheads * blk.ssm.headdim, dtype=p.dtype, device=self.dev)
                      for blk in self.layers]
@@ -47,7 +51,12 @@ class GraphDecoder:
         ssm = blk.ssm
         proj = ssm.in_proj(blk.ssm_norm(x))
         st = self.states[i]
-        ops.step_ssm_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_BX"], st["angle"], self.ybuf[i])
+        if self.compact:
+            ops.step_ssm_compact_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_B"], st["prev_x"],
+                                  st["angle"], self.ybuf[i])
+        else:
+            ops.step_ssm_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_BX"], st["angle"],
+                          self.ybuf[i])
         h = ssm.out_proj(self.ybuf[i])
         return blk._mlp_residual(x + h * blk.residual_scale)
 
@@ -76,8 +85,8 @@ class GraphDecoder:
         self.sampling = (float(temperature), top_k)
         x = self.lm.embedding(input_ids)
         for i, blk in enumerate(self.layers):
-            x, st = blk.prefill(x)
-            for k in ("h", "prev_BX", "angle"):
+            x, st = blk.prefill(x, compact_state=self.compact)
+            for k in self.states[i]:
                 self.states[i][k].copy_(st[k])
         logits = self.lm.lm_head(self.lm.norm(x)[:, -1])
         self.tok.copy_(self._sample(logits))

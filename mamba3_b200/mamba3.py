@@ -117,6 +117,10 @@ class KulaMamba(nn.Module):
         return (self.A_log, self.D, self.dt_bias, self.B_norm.weight, self.C_norm.weight, self.B_bias,
                 self.C_bias, self.mimo_x, self.mimo_z, self.mimo_down)
 
+    def _dims_tuple(self):
+        d = self._dims()
+        return (d["H"], d["P"], d["N"], d["R"], d["G"], d["trapezoidal"], d["complex_ssm"], d["norm_eps"])
+
     def _dims(self):
         return dict(H=self.nheads, P=self.headdim, N=self.d_state, R=self.mimo_rank, G=self.ngroups,
                     trapezoidal=self.use_trapezoidal, complex_ssm=self.use_complex_ssm,
@@ -136,6 +140,11 @@ class KulaMamba(nn.Module):
             raise ValueError(f"expected (batch, seqlen>0, d_model), got {tuple(x.shape)}")
         proj = self.in_proj(x)
         st = state or {}
+        if "prev_B" in st:  # compact state in, compact state out
+            if dt_scale is not None:
+                raise NotImplementedError("dt_scale with a compact state")
+            y, out_st = ops.layer_state_compact(proj, self._param_tensors(), self._dims_tuple(), st)
+            return self.out_proj(y), out_st
         y, h, angle, prev_bx = ops.layer_ssd(proj, *self._param_tensors(), dt_scale, st.get("h"), st.get("angle"),
                                              st.get("prev_BX"), **self._dims(), return_state=return_state)
         out = self.out_proj(y)
@@ -148,8 +157,16 @@ class KulaMamba(nn.Module):
         """(B, T, d_model) -> (B, T, d_model)   (mamba3/mamba3.py:260-262)."""
         return self._ssd(x, dt_scale, False)[0]
 
-    def prefill(self, x, dt_scale=None):
-        """Forward plus the inference state after the last token (mamba3/mamba3.py:264-265)."""
+    def prefill(self, x, dt_scale=None, compact_state=False):
+        """Forward plus the inference state after the last token (mamba3/mamba3.py:264-265).
+        compact_state=True (extension) returns the compact state of allocate_inference_state."""
+        if compact_state:
+            if dt_scale is not None:
+                raise NotImplementedError("dt_scale with a compact state")
+            if x.dim() != 3 or x.shape[1] <= 0:
+                raise ValueError(f"expected (batch, seqlen>0, d_model), got {tuple(x.shape)}")
+            y, st = ops.layer_state_compact(self.in_proj(x), self._param_tensors(), self._dims_tuple())
+            return self.out_proj(y), st
         return self._ssd(x, dt_scale, True)
 
     def prefill_from(self, x, ssm_state, dt_scale=None):
@@ -204,17 +221,32 @@ class KulaMamba(nn.Module):
         squeeze = hidden_states.dim() == 2
         x_in = hidden_states if squeeze else hidden_states.squeeze(1)
         proj = self.in_proj(x_in)
-        y, h, bx, angle = ops.step_ssm(proj, *self._param_tensors(), ssm_state["h"], ssm_state["prev_BX"],
-                                       ssm_state["angle"], dt_scale, **self._dims())
+        if "prev_B" in ssm_state:  # compact previous-token state (allocate_inference_state(compact=True))
+            y, h, pb, px, angle = ops.step_ssm_compact(proj, *self._param_tensors(), ssm_state["h"],
+                                                       ssm_state["prev_B"], ssm_state["prev_x"],
+                                                       ssm_state["angle"], dt_scale, **self._dims())
+            new_state = {"h": h, "angle": angle, "prev_B": pb, "prev_x": px}
+        else:
+            y, h, bx, angle = ops.step_ssm(proj, *self._param_tensors(), ssm_state["h"], ssm_state["prev_BX"],
+                                           ssm_state["angle"], dt_scale, **self._dims())
+            new_state = {"h": h, "angle": angle, "prev_BX": bx}
         out = self.out_proj(y)
         if not squeeze:
             out = out.unsqueeze(1)
-        return out, {"h": h, "angle": angle, "prev_BX": bx}
+        return out, new_state
 
-    def allocate_inference_state(self, batch_size, dtype=None, device=None):
-        """Zero state {'h', 'angle', 'prev_BX'} (mamba3/mamba3.py:324-332); all fp32 (see module doc)."""
+    def allocate_inference_state(self, batch_size, dtype=None, device=None, compact=False):
+        """Zero state {'h', 'angle', 'prev_BX'} (mamba3/mamba3.py:324-332); all fp32 (see module doc).
+        compact=True (extension, opt-in) keeps the previous token as 'prev_B' (B,H,N,R) and
+        'prev_x' (B,H,P,R) instead of 'prev_BX' (B,H,P,N): step() then moves half the state
+        bytes per token; the outputs are the same."""
         device = device or self.in_proj.weight.device
         H, P, N = self.nheads, self.headdim, self.d_state
         f32 = dict(dtype=torch.float32, device=device)
+        if compact:
+            R = self.mimo_rank
+            return {"h": torch.zeros(batch_size, H, P, N, **f32), "angle": torch.zeros(batch_size, H, N // 2, **f32),
+                    "prev_B": torch.zeros(batch_size, H, N, R, **f32),
+                    "prev_x": torch.zeros(batch_size, H, P, R, **f32)}
         return {"h": torch.zeros(batch_size, H, P, N, **f32), "angle": torch.zeros(batch_size, H, N // 2, **f32),
                 "prev_BX": torch.zeros(batch_size, H, P, N, **f32)}

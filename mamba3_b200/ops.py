@@ -166,3 +166,74 @@ def step_ssm_(prm_tensors, dims, proj, h, prev_bx, angle, y, dt_scale=None):
     H, P, N, R, G, trap, cplx, eps = dims
     prm = _prm(H, P, N, R, G, trap, cplx, eps, *prm_tensors)
     _lib.step(prm, proj, dt_scale, h, prev_bx, angle, h, prev_bx, angle, y)
+
+
+# ---------------------------------------------------------------------------
+# compact decode step: previous token as (B^ (N, R), x_r (P, R)) instead of prev_BX (P, N)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("mamba3_b200::step_ssm_compact", mutates_args=())
+def step_ssm_compact(proj: torch.Tensor, A_log: torch.Tensor, D: torch.Tensor, dt_bias: torch.Tensor,
+                     B_norm_w: torch.Tensor, C_norm_w: torch.Tensor, B_bias: torch.Tensor, C_bias: torch.Tensor,
+                     mimo_x: torch.Tensor, mimo_z: torch.Tensor, mimo_down: torch.Tensor,
+                     h: torch.Tensor, prev_b: torch.Tensor, prev_x: torch.Tensor, angle: torch.Tensor,
+                     dt_scale: Optional[torch.Tensor], H: int, P: int, N: int, R: int, G: int, trapezoidal: bool,
+                     complex_ssm: bool, norm_eps: float
+                     ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    Bt = proj.shape[0]
+    proj = proj.contiguous()
+    prm = _prm(H, P, N, R, G, trapezoidal, complex_ssm, norm_eps, A_log, D, dt_bias, B_norm_w, C_norm_w,
+               B_bias, C_bias, mimo_x, mimo_z, mimo_down)
+    h = h.float().contiguous()
+    prev_b = prev_b.float().contiguous()
+    prev_x = prev_x.float().contiguous()
+    angle = angle.contiguous()
+    h_out = torch.empty_like(h)
+    b_out = torch.empty_like(prev_b)
+    x_out = torch.empty_like(prev_x)
+    angle_out = torch.empty(angle.shape, dtype=torch.float32, device=proj.device)
+    y = torch.empty(Bt, H * P, dtype=proj.dtype, device=proj.device)
+    ds = None if dt_scale is None else dt_scale.to(proj.dtype).reshape(Bt, -1).expand(Bt, H).contiguous()
+    _lib.step(prm, proj, ds, h, None, angle, h_out, None, angle_out, y, prev_b=prev_b, prev_x=prev_x,
+              prev_b_out=b_out, prev_x_out=x_out)
+    return y, h_out, b_out, x_out, angle_out
+
+
+@step_ssm_compact.register_fake
+def _(proj, A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_z, mimo_down, h, prev_b, prev_x,
+      angle, dt_scale, H, P, N, R, G, trapezoidal, complex_ssm, norm_eps):
+    Bt = proj.shape[0]
+    f = dict(dtype=torch.float32)
+    return (proj.new_empty(Bt, H * P), torch.empty_like(h, **f), torch.empty_like(prev_b, **f),
+            torch.empty_like(prev_x, **f), torch.empty(angle.shape, dtype=torch.float32, device=proj.device))
+
+
+def step_ssm_compact_(prm_tensors, dims, proj, h, prev_b, prev_x, angle, y, dt_scale=None):
+    """In-place compact decode step for CUDA-graph loops: updates h, prev_b, prev_x, angle."""
+    H, P, N, R, G, trap, cplx, eps = dims
+    prm = _prm(H, P, N, R, G, trap, cplx, eps, *prm_tensors)
+    _lib.step(prm, proj, dt_scale, h, None, angle, h, None, angle, y, prev_b=prev_b, prev_x=prev_x,
+              prev_b_out=prev_b, prev_x_out=prev_x)
+
+
+def layer_state_compact(proj, prm_tensors, dims, state=None):
+    """Final state of the layer over proj's tokens in compact form: {'h', 'angle', 'prev_B',
+    'prev_x'}; y is computed (and returned) as in the forward.  `state` (either form) is the
+    state before the first token."""
+    H, P, N, R, G, trap, cplx, eps = dims
+    prm = _prm(H, P, N, R, G, trap, cplx, eps, *prm_tensors)
+    proj = proj.contiguous()
+    Bt, T, _ = proj.shape
+    dev = proj.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    y = torch.empty(Bt, T, H * P, dtype=proj.dtype, device=dev)
+    out = {"h": torch.empty(Bt, H, P, N, **f32), "angle": torch.empty(Bt, H, N // 2, **f32),
+           "prev_B": torch.empty(Bt, H, N, R, **f32), "prev_x": torch.empty(Bt, H, P, R, **f32)}
+    st = state or {}
+    pb = st.get("prev_BX")
+    if pb is None and "prev_B" in st:
+        pb = torch.einsum("bhnr,bhpr->bhpn", st["prev_B"].float(), st["prev_x"].float())
+    f = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
+    _lib.layer_fwd(prm, proj, y, h_init=f(st.get("h")), angle_init=f(st.get("angle")), prev_bx_init=f(pb),
+                   h_final=out["h"], angle_final=out["angle"], prev_b_final=out["prev_B"],
+                   prev_x_final=out["prev_x"], stage_events=current_stage_events(), algo=_LAYER_ALGO)
+    return y, out

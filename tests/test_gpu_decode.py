@@ -19,15 +19,16 @@ def _lm(dtype, seed=8, vocab=1000, n_layers=2):
                        mimo_rank=2).cuda().to(dtype).eval()
 
 
+@pytest.mark.parametrize("compact", [True, False], ids=["compact", "prev_BX"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_graph_decoder_matches_generate(dtype):
+def test_graph_decoder_matches_generate(dtype, compact):
     from mamba3_b200.decode import GraphDecoder
 
     lm = _lm(dtype)
     g = torch.Generator().manual_seed(9)
     ids = torch.randint(0, 1000, (3, 20), generator=g).cuda()
     ref = lm.generate(ids, max_new_tokens=12, temperature=0.0)
-    dec = GraphDecoder(lm, batch_size=3, max_new_tokens=12)
+    dec = GraphDecoder(lm, batch_size=3, max_new_tokens=12, compact=compact)
     out = dec.generate(ids, temperature=0.0)
     assert out.shape == ref.shape == (3, 32)
     assert torch.equal(out, ref)
@@ -55,3 +56,31 @@ def test_step_logits_equal_parallel_forward():
             steps.append(lm.lm_head(lm.norm(x)))
     got = torch.stack(steps, 1)  # logits after tokens 24 .. 39
     assert max_rel(to_np(got), to_np(full[:, 24:40])) < 2e-2
+
+
+@pytest.mark.parametrize("N,R", [(128, 1), (128, 2), (128, 4), (16, 2), (16, 3)])
+def test_compact_state_steps_equal_prev_bx_steps(N, R):
+    """Compact previous-token state (prev_B, prev_x): prefill gives factors whose product is
+    prefill's prev_BX, and steps from either form give the same outputs and states."""
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(30 + R)
+    m = KulaMamba(d_model=128, d_state=N, headdim=64 if N == 128 else 16, mimo_rank=R).cuda().eval()
+    g = torch.Generator().manual_seed(31)
+    x = torch.randn(2, 50, 128, generator=g).cuda()
+    with torch.no_grad():
+        y_a, st_a = m.prefill(x[:, :40])
+        y_b, st_b = m.prefill(x[:, :40], compact_state=True)
+        assert torch.equal(y_a, y_b)
+        pbx = torch.einsum("bhnr,bhpr->bhpn", st_b["prev_B"], st_b["prev_x"])
+        assert max_rel(to_np(pbx), to_np(st_a["prev_BX"])) < 1e-6
+        for t in range(40, 50):
+            ya, st_a = m.step(x[:, t], st_a)
+            yb, st_b = m.step(x[:, t], st_b)
+            assert max_rel(to_np(yb), to_np(ya)) < 1e-5
+        assert max_rel(to_np(st_b["h"]), to_np(st_a["h"])) < 1e-5
+        # a compact state also continues a prefill
+        y_c, st_c = m.prefill_from(x[:, 40:], m.prefill(x[:, :40], compact_state=True)[1])
+        y_d, st_d = m.prefill_from(x[:, 40:], m.prefill(x[:, :40])[1])
+    assert max_rel(to_np(y_c), to_np(y_d)) < 1e-5
+    assert "prev_B" in st_c and max_rel(to_np(st_c["h"]), to_np(st_d["h"])) < 1e-5

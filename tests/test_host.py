@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(h, n), n
     assert set(names) == set(_lib.SIGNATURES), "ctypes binding must cover exactly the header"
     L = _lib.lib()
-    assert L.m3b_abi_version() == 2
+    assert L.m3b_abi_version() == 3
     assert L.m3b_strerror(0) == b"ok"
 
 
@@ -115,4 +115,15 @@ def test_state_shapes_and_dtypes():
     st = m.allocate_inference_state(2, dtype=torch.bfloat16, device="cpu")
     assert st["h"].shape == (2, 8, 16, 16) and st["prev_BX"].shape == (2, 8, 16, 16)
     assert st["angle"].shape == (2, 8, 8)
+    assert all(v.dtype == torch.float32 for v in st.values())
+
+
+def test_compact_state_shapes():
+    """allocate_inference_state(compact=True): the previous token as (N, R) and (P, R) factors."""
+    from mamba3_b200 import KulaMamba
+
+    m = KulaMamba(d_model=64, d_state=16, headdim=16, mimo_rank=2, chunk_size=8)
+    st = m.allocate_inference_state(2, device="cpu", compact=True)
+    assert set(st) == {"h", "angle", "prev_B", "prev_x"}
+    assert st["prev_B"].shape == (2, 8, 16, 2) and st["prev_x"].shape == (2, 8, 16, 2)
     assert all(v.dtype == torch.float32 for v in st.values())
