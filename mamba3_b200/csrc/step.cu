@@ -27,7 +27,7 @@ constexpr int kStepMaxP = 256;
 // COMPACT: the previous token is kept as its rotated B^ (N, R) and MIMO x (P, R) instead of the
 // (P, N) product prev_BX, which the state loop rebuilds on the fly: half the state traffic.
 template <typename TA, int R, bool ROW32, bool COMPACT>
-__global__ void __launch_bounds__(kStepThreads) step_kernel(m3b_step_args a) {
+__global__ void __launch_bounds__(kStepThreads, COMPACT ? 4 : 2) step_kernel(m3b_step_args a) {
   const m3b_layer_params& prm = a.prm;
   const int H = prm.H, P = prm.P, N = prm.N, G = prm.G;
   const int b = blockIdx.x / H;
