@@ -191,3 +191,21 @@ def test_cfg1_full_size_prefix_parity(B, T, seed):
     for b in (0, B - 1):
         oy, _ = oracle.layer_forward(p, to_np(x[b:b + 1, :Tp]))
         assert max_rel(to_np(y[b:b + 1, :Tp]), oy) < BF16_TOL
+
+
+@pytest.mark.parametrize("T", [1, 2, 31, 63, 64, 65, 129])
+@pytest.mark.parametrize("R", [1, 2, 4])
+def test_ragged_lengths_n128(T, R):
+    """Sequence lengths around the kernels' chunk length (128 / R tokens), down to one token,
+    with d_state 128 (the TMA-staged fused path): prefill vs the oracle, bf16."""
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(40 + R)
+    m = KulaMamba(d_model=128, d_state=128, headdim=64, mimo_rank=R).cuda().to(torch.bfloat16).eval()
+    x = torch.randn(3, T, 128, generator=torch.Generator().manual_seed(T)).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        y, st = m.prefill(x)
+    oy, ost = oracle.layer_prefill(oracle_params(m), to_np(x))
+    assert max_rel(to_np(y), oy) < BF16_TOL
+    assert max_rel(to_np(st["h"]), ost["h"]) < BF16_TOL
+    assert max_rel(to_np(st["prev_BX"]), ost["prev_BX"]) < BF16_TOL
