@@ -84,3 +84,29 @@ def test_compact_state_steps_equal_prev_bx_steps(N, R):
         y_d, st_d = m.prefill_from(x[:, 40:], m.prefill(x[:, :40])[1])
     assert max_rel(to_np(y_c), to_np(y_d)) < 1e-5
     assert "prev_B" in st_c and max_rel(to_np(st_c["h"]), to_np(st_d["h"])) < 1e-5
+
+
+def test_compact_step_many_items_per_cta():
+    """Config-4 shapes (batch 256 x 24 heads): the compact step from random factors equals the
+    prev_BX step from their product, over three consecutive tokens."""
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(50)
+    m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
+    B = 256
+    g = torch.Generator().manual_seed(51)
+    full = m.allocate_inference_state(B)
+    comp = m.allocate_inference_state(B, compact=True)
+    for k in ("h", "angle"):
+        full[k].copy_(torch.randn(full[k].shape, generator=g))
+        comp[k].copy_(full[k])
+    comp["prev_B"].copy_(torch.randn(comp["prev_B"].shape, generator=g))
+    comp["prev_x"].copy_(torch.randn(comp["prev_x"].shape, generator=g))
+    full["prev_BX"].copy_(torch.einsum("bhnr,bhpr->bhpn", comp["prev_B"], comp["prev_x"]))
+    with torch.no_grad():
+        for t in range(3):
+            x = torch.randn(B, 768, generator=g).cuda().to(torch.bfloat16)
+            ya, full = m.step(x, full)
+            yb, comp = m.step(x, comp)
+            assert max_rel(to_np(yb), to_np(ya)) < 1e-2, t
+    assert max_rel(to_np(comp["h"]), to_np(full["h"])) < 1e-5
