@@ -173,14 +173,17 @@ class KulaMamba(nn.Module):
         """Continue a prefill from an inference state (chunked prefill; no reference counterpart)."""
         return self._ssd(x, dt_scale, True, ssm_state)
 
-    def forward_host(self, x_host, out=None, pieces=4):
+    def forward_host(self, x_host, out=None, pieces=4, graph=False):
         """forward() of a batch held in pinned host memory, streamed through the GPU in `pieces`
         token ranges (no reference counterpart): the host->device copy of range i+1, the layer on
         range i and the device->host copy of range i-1 run on three streams and overlap, the
         state crossing range boundaries as in prefill_from.  Returns `out` (pinned host memory,
-        allocated when None).  The caller's current stream is ordered after the last copy."""
-        from . import _lib
+        allocated when None).  The caller's current stream is ordered after the last copy.
 
+        graph=True captures the whole streamed forward for this (x_host, out) pair in a CUDA
+        graph on first use and replays it afterwards: the same work without the per-range host
+        overhead.  The graph keeps reading x_host and writing out, so it is only for callers that
+        reuse the same pinned buffers (and the same weights) from call to call."""
         if x_host.is_cuda or x_host.dim() != 3 or not x_host.is_pinned():
             raise ValueError("forward_host expects a pinned host tensor (batch, seqlen, d_model)")
         dev = self.in_proj.weight.device
@@ -188,6 +191,33 @@ class KulaMamba(nn.Module):
         if out is None:
             out = torch.empty(B, T, D, dtype=x_host.dtype, pin_memory=True)
         n = max(1, min(int(pieces), T))
+        if not graph:
+            self._forward_host_run(x_host, out, n, dev, [])
+            return out
+        cache = self.__dict__.get("_host_graphs")
+        if cache is None:
+            cache = {}
+            object.__setattr__(self, "_host_graphs", cache)
+        key = (x_host.data_ptr(), out.data_ptr(), tuple(x_host.shape), x_host.dtype, n, dev)
+        if key not in cache:
+            self._forward_host_run(x_host, out, n, dev, [])  # warm-up outside the capture
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            keep = []
+            with torch.cuda.graph(g, stream=s):
+                self._forward_host_run(x_host, out, n, dev, keep)
+            torch.cuda.current_stream(dev).wait_stream(s)
+            cache[key] = (g, keep)
+        cache[key][0].replay()
+        return out
+
+    def _forward_host_run(self, x_host, out, n, dev, keep):
+        from . import _lib
+
+        B, T, D = x_host.shape
+        capturing = torch.cuda.is_current_stream_capturing()
         edges = [T * i // n for i in range(n + 1)]
         span = max(edges[i + 1] - edges[i] for i in range(n))
         cmp = torch.cuda.current_stream(dev)
@@ -210,11 +240,15 @@ class KulaMamba(nn.Module):
             ev_cmp[i].record(cmp)
             s_out.wait_event(ev_cmp[i])
             _lib.copy_token_range(out, t0, y, 0, nt, s_out)
-            y.record_stream(s_out)  # its memory is not reused before this copy has run
+            if capturing:
+                keep.append(y)  # held until the capture ends; the graph's pool keeps it after
+            else:
+                y.record_stream(s_out)  # its memory is not reused before this copy has run
             ev_out[i].record(s_out)
         cmp.wait_event(ev_out[n - 1])
         cmp.wait_stream(s_in)
-        return out
+        cmp.wait_stream(s_out)
+        keep.extend(xb)
 
     def step(self, hidden_states, ssm_state, dt_scale=None):
         """One token: (B, d_model) or (B, 1, d_model) -> same shape, new state (mamba3/mamba3.py:267-322)."""

@@ -157,8 +157,9 @@ def test_mixed_decay_heads_n128():
     assert max_rel(to_np(st["h"]), ost["h"]) < BF16_TOL
 
 
+@pytest.mark.parametrize("graph", [False, True], ids=["eager", "graph"])
 @pytest.mark.parametrize("pieces", [1, 3, 8])
-def test_forward_host_streaming_equals_forward(pieces):
+def test_forward_host_streaming_equals_forward(pieces, graph):
     """forward_host (pinned host input streamed through the GPU in token ranges) == forward."""
     from mamba3_b200 import KulaMamba
 
@@ -168,10 +169,19 @@ def test_forward_host_streaming_equals_forward(pieces):
     x = torch.randn(2, 333, 256, generator=g).to(torch.bfloat16).pin_memory()
     with torch.no_grad():
         ref = m(x.cuda())
-        out = m.forward_host(x, pieces=pieces)
-    torch.cuda.synchronize()
+        out = torch.empty_like(x).pin_memory()
+        for _ in range(2 if graph else 1):  # a graph is captured on the first call, replayed after
+            out.zero_()
+            m.forward_host(x, out, pieces=pieces, graph=graph)
+            torch.cuda.synchronize()
+            assert max_rel(to_np(out), to_np(ref)) < BF16_TOL
+        if graph:  # new input in the same buffer: the replay reads it
+            x.copy_(torch.randn(x.shape, generator=g).to(torch.bfloat16))
+            ref = m(x.cuda())
+            m.forward_host(x, out, pieces=pieces, graph=True)
+            torch.cuda.synchronize()
+            assert max_rel(to_np(out), to_np(ref)) < BF16_TOL
     assert not out.is_cuda and out.is_pinned()
-    assert max_rel(to_np(out), to_np(ref)) < BF16_TOL
 
 
 @pytest.mark.parametrize("B,T,seed", [(16, 4096, 1)])
