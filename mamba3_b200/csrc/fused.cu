@@ -336,6 +336,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     struct TokRaw {
       float dt, lam, rb, rc, dts;
       bool ok;
+      bool pre;            // sdt / sgam / sbp below already hold the token scalars
+      float sdt, sgam, sbp;
+    };
+    // dt = softplus(dt_raw + dt_bias) * dt_scale; gamma = lam dt; (1 - lam) dt (trapezoid)
+    auto tok_scalars = [&](TokRaw& tr) {
+      float dt = 0.f, gmm = 0.f, bp = 0.f;
+      if (tr.ok) {
+        dt = softplus_fast(tr.dt + sp[1]) * tr.dts;
+        if (p.trapezoidal) {
+          const float lam = sigmoid_fast(tr.lam);
+          gmm = lam * dt;
+          bp = (1.f - lam) * dt;
+        } else {
+          gmm = dt;
+        }
+      }
+      tr.sdt = dt;
+      tr.sgam = gmm;
+      tr.sbp = bp;
+      tr.pre = true;
     };
     auto load_tok = [&](const ChunkPos& c, TokRaw& tr) {
       const int bb = c.b, hh = c.h, gr = c.grp;
@@ -343,6 +363,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       tr.dt = tr.lam = tr.rb = tr.rc = 0.f;
       tr.dts = 1.f;
       tr.ok = ptid <= L && tt < a.T;
+      tr.pre = false;
       if (tr.ok) {
         const TA* row = proj + ((int64_t)bb * a.T + tt) * a.proj_stride;
         tr.dt = io<TA>::ld(row + offDt + hh);
@@ -448,22 +469,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         else return th[jj];
       };
       if (ptid == 0) M3B_TL(g, 5);
-      // (1) token scalars (token L is the next chunk's first token)
+      // (1) token scalars (token L is the next chunk's first token); within a sequence they were
+      // computed at the end of the previous chunk
       if (ptid <= L) {
-        float dt = 0.f, gmm = 0.f, bp = 0.f;
-        if (cur.ok) {
-          dt = softplus_fast(cur.dt + sp[1]) * cur.dts;
-          if (p.trapezoidal) {
-            const float lam = sigmoid_fast(cur.lam);
-            gmm = lam * dt;
-            bp = (1.f - lam) * dt;
-          } else {
-            gmm = dt;
-          }
-        }
-        dtv[ptid] = dt;
-        gam[ptid] = gmm;
-        bpr[ptid] = bp;
+        TokRaw c2 = cur;
+        if (!c2.pre) tok_scalars(c2);
+        dtv[ptid] = c2.sdt;
+        gam[ptid] = c2.sgam;
+        bpr[ptid] = c2.sbp;
         if (ptid < L) {
           rmsB[ptid] = cur.rb;
           rmsC[ptid] = cur.rc;
@@ -687,6 +700,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           sw128_store_chunk(st + PL::tB, u / ncz, c0 + u % ncz, 128, make_uint4(0, 0, 0, 0));
       }
       if (ptid == 0) M3B_TL(g, 3);
+      // the next chunk's token scalars, while the other warps finish their rotations (its raw
+      // values were requested at the start of this chunk; same sequence, so same dt_bias)
+      if (ptid <= L && g + 1 < G && pnext.k != 0) tok_scalars(nxt);
       fence_async_smem();
       named_bar(kBarProd, kProdThreads);  // B^, C^ tiles and the token scalars (wst, gbw) complete
       if (ptid == 0) {
