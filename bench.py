@@ -44,6 +44,7 @@ def parse():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-4 decode measurement")
     ap.add_argument("--no-seqpar", action="store_true", help="skip the config-3 sequence-sharded measurement")
     ap.add_argument("--no-lm", action="store_true", help="skip the config-2 LM forward measurement")
+    ap.add_argument("--no-scan", action="store_true", help="skip the scan forward / backward measurement")
     ap.add_argument("--e2e-pieces", type=int, default=8,
                     help="token ranges forward_host streams the host batch in (copy/compute overlap)")
     return ap.parse_args()
@@ -214,6 +215,57 @@ def run_decode(dev, world, rank, barrier):
                             "batch": B, "heads": H},
             "step_kernel_prev_bx": {"ms": ms_f, "state_bytes": full_bytes, "achieved_gbs": gbs_f,
                                     "frac": gbs_f / peaks["hbm_gbs"]}}
+
+
+def run_scan(dev, world, rank, barrier):
+    """The inter-chunk scan alone, forward and backward, on config-1 shaped states in fp32 (the
+    dtype the reference's scan_forward / scan_backward run in): B 16 per GPU, K 64 chunks, H 24,
+    PN 64 x 128.  Algorithmic bytes: forward h_chunk read + h_states write, backward h_states
+    and grad_h read + d_chunk write (the (B, K, H) decays are negligible).  Each tensor is
+    805 MB, larger than L2, so consecutive launches do not hit in L2."""
+    import torch
+    import torch.distributed as dist
+
+    from mamba3_b200 import _lib
+
+    B, K, H, PN = 16, 64, 24, 64 * 128
+    g = torch.Generator(device=dev).manual_seed(5)
+    decay = torch.rand(B, K, H, device=dev, generator=g)
+    hc = torch.randn(B, K, H, PN, device=dev, generator=g)
+    gh = torch.randn(B, K, H, PN, device=dev, generator=g)
+    hs = torch.empty_like(hc)
+    fwd = lambda: _lib.scan_fwd(decay, hc, None, h_states=hs)  # noqa: E731
+    bwd = lambda: _lib.scan_bwd(decay, hs, gh, False)  # noqa: E731
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    ms_f, ms_b = timed(fwd), timed(bwd)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() \
+        else {"hbm_gbs": 6650.0}
+    el = B * K * H * PN
+    out = {"workload": f"inter-chunk scan, fp32 states ({B}, {K}, {H}, {PN}) per GPU"}
+    for name, ms, nbytes in (("fwd", ms_f, 2 * 4 * el), ("bwd", ms_b, 3 * 4 * el)):
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"ms": ms, "bytes": nbytes, "achieved_gbs": gbs, "frac": gbs / peaks["hbm_gbs"]}
+    del hc, gh, hs
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_lm(dev, world, rank, barrier):
@@ -440,6 +492,7 @@ def run_ours(args):
     decode = None if args.no_decode else run_decode(dev, world, rank, barrier)
     seqp = None if args.no_seqpar else run_seqpar(dev, world, rank, barrier)
     lmf = None if args.no_lm else run_lm(dev, world, rank, barrier)
+    scan = None if args.no_scan else run_scan(dev, world, rank, barrier)
 
     if rank == 0:
         import math
@@ -495,6 +548,8 @@ def run_ours(args):
             line["seqpar"] = seqp
         if lmf is not None:
             line["lm_forward"] = lmf
+        if scan is not None:
+            line["scan"] = scan
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_sample_tokens)
         print(json.dumps(line), flush=True)

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3B_ABI_VERSION 3
+#define M3B_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define M3B_API __attribute__((visibility("default")))
@@ -74,6 +74,31 @@ typedef struct m3b_scan_args {
   int32_t dtype;          /* M3B_F32 or M3B_BF16 */
 } m3b_scan_args;
 M3B_API int m3b_scan_fwd(const m3b_scan_args* a, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Inter-chunk scan, backward.
+ * Replaces the reference's pybind entry `scan_backward(decay, h_states, grad_h, has_h_init)`
+ * (mamba3/csrc/scan.cu:168-211, kernel :52-126; called from mamba3/scan.py:102-118 in
+ * SSDScanFn.backward; torch loop mamba3/scan.py:47-62).  With the fp32 carry
+ * g_{K-1} = grad_h[:,K-1], g_k = grad_h[:,k] + decay[:,k] * g_{k+1}:
+ *   d_chunk[:,k] = g_{k+1} and d_decay[:,k] = sum_j g_{k+1}[j] * h_states[:,k,j] for k < K-1,
+ *   d_chunk[:,K-1] = 0, d_decay[:,K-1] = 0, d_h_init = g_0 (when d_h_init != NULL).
+ * d_decay is summed in a fixed order: results are bitwise reproducible run to run.
+ * m3b_scan_bwd_workspace gives the caller-owned workspace size (0 when none is needed;
+ * 16-byte aligned otherwise).
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_scan_bwd_args {
+  const float* decay;     /* (B,K,H) */
+  const void* h_states;   /* (B,K,H,PN), `dtype` (the forward's exclusive states) */
+  const void* grad_h;     /* (B,K,H,PN), `dtype` */
+  void* d_chunk;          /* (B,K,H,PN), `dtype` (may not alias the inputs) */
+  float* d_decay;         /* (B,K,H) */
+  float* d_h_init;        /* (B,H,PN) or NULL */
+  int64_t B, K, H, PN;
+  int32_t dtype;          /* M3B_F32 or M3B_BF16 */
+} m3b_scan_bwd_args;
+M3B_API size_t m3b_scan_bwd_workspace(const m3b_scan_bwd_args* a);
+M3B_API int m3b_scan_bwd(const m3b_scan_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Parameters of one KulaMamba layer (names and shapes of mamba3/mamba3.py:95-111). */
 typedef struct m3b_layer_params {

@@ -40,6 +40,12 @@ class ScanArgs(C.Structure):
                 ("dtype", C.c_int32)]
 
 
+class ScanBwdArgs(C.Structure):
+    _fields_ = [("decay", C.c_void_p), ("h_states", C.c_void_p), ("grad_h", C.c_void_p), ("d_chunk", C.c_void_p),
+                ("d_decay", C.c_void_p), ("d_h_init", C.c_void_p), ("B", C.c_int64), ("K", C.c_int64),
+                ("H", C.c_int64), ("PN", C.c_int64), ("dtype", C.c_int32)]
+
+
 class LayerParams(C.Structure):
     _fields_ = [("H", C.c_int32), ("P", C.c_int32), ("N", C.c_int32), ("R", C.c_int32), ("G", C.c_int32),
                 ("trapezoidal", C.c_int32), ("complex_ssm", C.c_int32), ("param_dtype", C.c_int32),
@@ -84,6 +90,8 @@ SIGNATURES = {
     "m3b_last_error": (C.c_char_p, []),
     "m3b_abi_version": (C.c_int, []),
     "m3b_scan_fwd": (C.c_int, [C.POINTER(ScanArgs), C.c_void_p]),
+    "m3b_scan_bwd_workspace": (C.c_size_t, [C.POINTER(ScanBwdArgs)]),
+    "m3b_scan_bwd": (C.c_int, [C.POINTER(ScanBwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_step": (C.c_int, [C.POINTER(StepArgs), C.c_void_p]),
     "m3b_layer_fwd_workspace": (C.c_size_t, [C.POINTER(LayerFwdArgs)]),
     "m3b_layer_fwd": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
@@ -163,6 +171,26 @@ def scan_fwd(decay, h_chunk, h_init=None, h_states=None, h_final=None):
     with torch.cuda.device(dev):
         _check(lib().m3b_scan_fwd(C.byref(a), _stream(dev)), "m3b_scan_fwd")
     return h_states
+
+
+def scan_bwd(decay, h_states, grad_h, with_h_init=False):
+    """Launch the scan backward; decay (B,K,H) fp32, h_states / grad_h (B,K,H,PN) of one dtype
+    (fp32 or bf16).  Returns (d_decay fp32, d_chunk in grad_h's dtype, d_h_init fp32 or None)."""
+    dev = _cuda(decay, h_states, grad_h)
+    B, K, H, PN = h_states.shape
+    if grad_h.shape != h_states.shape or grad_h.dtype != h_states.dtype or decay.shape != (B, K, H):
+        raise M3bError("scan_bwd: decay (B,K,H) and h_states / grad_h (B,K,H,PN) of one dtype expected")
+    d_chunk = torch.empty_like(grad_h)
+    d_decay = torch.empty((B, K, H), dtype=torch.float32, device=dev)
+    d_h_init = torch.empty((B, H, PN), dtype=torch.float32, device=dev) if with_h_init else None
+    a = ScanBwdArgs(_ptr(decay), _ptr(h_states), _ptr(grad_h), _ptr(d_chunk), _ptr(d_decay), _ptr(d_h_init),
+                    B, K, H, PN, dtype_code(grad_h.dtype))
+    L = lib()
+    nbytes = L.m3b_scan_bwd_workspace(C.byref(a))
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(L.m3b_scan_bwd(C.byref(a), _ptr(ws), nbytes, _stream(dev)), "m3b_scan_bwd")
+    return d_decay, d_chunk, d_h_init
 
 
 def step(prm: LayerParams, proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y, prev_b=None,

@@ -78,6 +78,21 @@ int m3b_scan_fwd(const m3b_scan_args* a, void* stream) {
   return m3b::launch_scan(s, static_cast<cudaStream_t>(stream));
 }
 
+static m3b::ScanBwdLaunch scan_bwd_launch(const m3b_scan_bwd_args* a) {
+  return m3b::ScanBwdLaunch{a->decay, a->h_states, a->grad_h, a->d_chunk, a->d_decay, a->d_h_init,
+                            a->B, a->K, a->H, a->PN, a->dtype};
+}
+
+size_t m3b_scan_bwd_workspace(const m3b_scan_bwd_args* a) { return a ? m3b::scan_bwd_workspace(scan_bwd_launch(a)) : 0; }
+
+int m3b_scan_bwd(const m3b_scan_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+  m3b::g_last_error[0] = 0;
+  if (!a || !a->decay || !a->h_states || !a->grad_h || !a->d_chunk || !a->d_decay)
+    return m3b::fail(M3B_ERR_INVALID_ARG, "scan_bwd: null pointer");
+  if (a->B < 0 || a->K < 0 || a->H < 0 || a->PN < 0) return m3b::fail(M3B_ERR_INVALID_ARG, "scan_bwd: negative dim");
+  return m3b::launch_scan_bwd(scan_bwd_launch(a), workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
 int m3b_step(const m3b_step_args* a, void* stream) {
   m3b::g_last_error[0] = 0;
   if (!a) return m3b::fail(M3B_ERR_INVALID_ARG, "step: null args");

@@ -30,6 +30,19 @@ struct ScanLaunch {
 };
 int launch_scan(const ScanLaunch& s, cudaStream_t st);
 
+struct ScanBwdLaunch {
+  const float* decay;
+  const void* h_states;
+  const void* grad_h;
+  void* d_chunk;
+  float* d_decay;
+  float* d_h_init;
+  int64_t B, K, H, PN;
+  int dtype;
+};
+size_t scan_bwd_workspace(const ScanBwdLaunch& s);
+int launch_scan_bwd(const ScanBwdLaunch& s, void* ws, size_t ws_bytes, cudaStream_t st);
+
 int launch_step(const m3b_step_args* a, cudaStream_t st);
 int layer_fwd(const m3b_layer_fwd_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t layer_fwd_workspace(const m3b_layer_fwd_args* a);

@@ -47,6 +47,22 @@ def _(decay, h_chunk, h_init):
     return torch.empty_like(h_chunk)
 
 
+@torch.library.custom_op("mamba3_b200::scan_bwd", mutates_args=())
+def scan_bwd(decay: torch.Tensor, h_states: torch.Tensor, grad_h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor,
+                                                                                          torch.Tensor]:
+    """fp32 backward of the scan (mamba3/scan.py:102-140): (d_decay, d_chunk, d_h_init), all fp32;
+    the caller drops d_h_init when the forward had no h_init and casts to its dtypes."""
+    return _lib.scan_bwd(decay.float().contiguous(), h_states.float().contiguous(), grad_h.float().contiguous(),
+                         True)
+
+
+@scan_bwd.register_fake
+def _(decay, h_states, grad_h):
+    B, K, H, PN = h_states.shape
+    f32 = dict(dtype=torch.float32, device=h_states.device)
+    return torch.empty((B, K, H), **f32), torch.empty((B, K, H, PN), **f32), torch.empty((B, H, PN), **f32)
+
+
 # ---------------------------------------------------------------------------
 # layer forward / prefill (everything between in_proj and out_proj)
 # ---------------------------------------------------------------------------

@@ -27,5 +27,6 @@ from .mamba3_oracle import (  # noqa: F401
     rmsnorm,
     softplus,
     ssd_scan,
+    ssd_scan_backward,
     swiglu,
 )

@@ -212,6 +212,25 @@ def ssd_scan(decay, h_chunk, h_init=None):
     return out
 
 
+def ssd_scan_backward(decay, h_states, grad_h, has_h_init=False):
+    """Gradients of ``ssd_scan`` (mamba3/scan.py:47-62, mamba3/csrc/scan.cu:52-126).
+
+    The carry g starts at grad_h[:, K-1]; walking k = K-2 .. 0, chunk k's gradient is the
+    carry g_{k+1}, the decay's is sum_j g_{k+1}[j] h_states[:, k, j], and the carry becomes
+    grad_h[:, k] + decay[:, k] g_{k+1}.  The last chunk's gradients are zero; d_h_init is g_0.
+    Returns (d_decay (B,K,H), d_chunk (B,K,H,PN), d_h_init (B,H,PN) or None).
+    """
+    B, K, H, PN = h_states.shape
+    g = np.array(grad_h[:, K - 1], dtype=np.float64)
+    d_decay = np.zeros((B, K, H))
+    d_chunk = np.zeros((B, K, H, PN))
+    for k in range(K - 2, -1, -1):
+        d_chunk[:, k] = g
+        d_decay[:, k] = (g * h_states[:, k]).sum(-1)
+        g = grad_h[:, k] + decay[:, k, :, None] * g
+    return d_decay, d_chunk, (g if has_h_init else None)
+
+
 def chunked_ssd(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, chunk_size=64, h_init=None,
                 return_final_state=False):
     """Chunked SSD forward (mamba3/ssd.py:118-244) with the factored intra-chunk cumsum

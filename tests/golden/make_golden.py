@@ -111,6 +111,24 @@ def scan_case(M, name, seed, B, K, H, PN, with_h_init):
     np.savez_compressed(HERE / f"scan_{name}.npz", **d)
 
 
+def scan_bwd_case(M, name, seed, B, K, H, PN, with_h_init):
+    """Gradients of the reference's ssd_scan through its autograd Function (SSDScanFn.backward,
+    mamba3/scan.py:102-140; on CPU its torch loop mamba3/scan.py:47-62)."""
+    g = torch.Generator().manual_seed(seed)
+    decay = (torch.rand(B, K, H, generator=g) * 0.9).requires_grad_(True)
+    h_chunk = torch.randn(B, K, H, PN, generator=g).requires_grad_(True)
+    h_init = torch.randn(B, H, PN, generator=g).requires_grad_(True) if with_h_init else None
+    grad_h = torch.randn(B, K, H, PN, generator=g)
+    hs = M.ssd_scan(decay, h_chunk, h_init)
+    ins = [decay, h_chunk] + ([h_init] if with_h_init else [])
+    grads = torch.autograd.grad(hs, ins, grad_h)
+    d = dict(decay=_np(decay), h_chunk=_np(h_chunk), grad_h=_np(grad_h), h_states=_np(hs), d_decay=_np(grads[0]),
+             d_chunk=_np(grads[1]))
+    if with_h_init:
+        d.update(h_init=_np(h_init), d_h_init=_np(grads[2]))
+    np.savez_compressed(HERE / f"scanbwd_{name}.npz", **d)
+
+
 def lm_case(M, name, seed, B, T, n_new, **kw):
     torch.manual_seed(seed)
     lm = M.KulaMambaLM(**kw).eval()
@@ -126,14 +144,25 @@ def lm_case(M, name, seed, B, T, n_new, **kw):
     np.savez_compressed(HERE / f"lm_{name}.npz", **out)
 
 
+def scan_bwd_groups(M):
+    scan_bwd_case(M, "hinit", 33, 2, 5, 3, 16, True)
+    scan_bwd_case(M, "zero", 34, 1, 9, 2, 24, False)
+    scan_bwd_case(M, "k1", 35, 2, 1, 2, 8, True)
+    scan_bwd_case(M, "odd", 36, 1, 6, 3, 13, True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("MAMBA3_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", default="", help="write only the fixture groups with this name prefix (e.g. scanbwd)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import mamba3 as M  # the unmodified reference package
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if args.only == "scanbwd":
+        scan_bwd_groups(M)
+        return
     small = dict(d_model=64, d_state=16, headdim=16, mimo_rank=2, expand=2, chunk_size=8)
     layer_case(M, "default", 11, 2, 24, False, **small)
     layer_case(M, "perturbed", 12, 2, 37, True, **small)
@@ -153,6 +182,7 @@ def main():
     ssd_case(M, "rank4", 23, 1, 40, 2, 16, 4, 16, 16)
     scan_case(M, "hinit", 31, 2, 4, 3, 8, True)
     scan_case(M, "zero", 32, 2, 7, 2, 24, False)
+    scan_bwd_groups(M)
     lm_case(M, "small", 41, 2, 12, 6, vocab_size=256, d_model=64, n_layers=2, d_state=16, headdim=16,
             mimo_rank=2, chunk_size=8, use_mlp=True, residual_scale="depth")
     total = sum(p.stat().st_size for p in HERE.glob("*.npz"))

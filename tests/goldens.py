@@ -12,6 +12,7 @@ LAYER_CASES = ["default", "perturbed", "rank1", "rank4", "euler", "real", "allof
                "n128p64"]
 SSD_CASES = ["trap", "euler", "rank4"]
 SCAN_CASES = ["hinit", "zero"]
+SCAN_BWD_CASES = ["hinit", "zero", "k1", "odd"]
 
 
 def load(name):

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import oracle
-from goldens import LAYER_CASES, SCAN_CASES, load, max_rel
+from goldens import LAYER_CASES, SCAN_BWD_CASES, SCAN_CASES, load, max_rel
 from helpers import ours_layer_from_golden, to_np
 
 pytestmark = pytest.mark.gpu
@@ -58,6 +58,71 @@ def test_scan_vs_oracle(dtype, shape, with_init):
     tol = 1e-5 if dtype == torch.float32 else 1e-2  # bf16 output rounding
     assert max_rel(to_np(hs), exp) < tol
     assert max_rel(to_np(hf), fin) < 1e-5
+
+
+@pytest.mark.parametrize("case", SCAN_BWD_CASES)
+def test_scan_backward_golden(case):
+    """ssd_scan's autograd gradients (reverse-scan kernel) == the reference's SSDScanFn.backward."""
+    from mamba3_b200 import ssd_scan
+
+    d = load(f"scanbwd_{case}")
+    decay = torch.from_numpy(d["decay"]).cuda().requires_grad_(True)
+    hc = torch.from_numpy(d["h_chunk"]).cuda().requires_grad_(True)
+    hi = torch.from_numpy(d["h_init"]).cuda().requires_grad_(True) if "h_init" in d else None
+    hs = ssd_scan(decay, hc, hi)
+    assert max_rel(to_np(hs), d["h_states"]) < 1e-6
+    ins = [decay, hc] + ([hi] if hi is not None else [])
+    grads = torch.autograd.grad(hs, ins, torch.from_numpy(d["grad_h"]).cuda())
+    assert max_rel(to_np(grads[0]), d["d_decay"]) < 1e-5
+    assert max_rel(to_np(grads[1]), d["d_chunk"]) < 1e-6
+    if hi is not None:
+        assert max_rel(to_np(grads[2]), d["d_h_init"]) < 1e-6
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(2, 5, 3, 16), (3, 64, 24, 8192), (1, 9, 2, 100), (2, 2, 2, 8), (1, 33, 4, 24576),
+                                   (8, 4, 48, 8192)])
+def test_scan_backward_vs_oracle(dtype, shape):
+    """The reverse-scan kernel through the C ABI against the oracle: vector paths (one block per
+    state, several blocks per state with fixed-order partial sums), the scalar path (PN = 100),
+    bf16 I/O; the result is bitwise the same on a second launch."""
+    from mamba3_b200 import _lib
+
+    B, K, H, PN = shape
+    g = torch.Generator().manual_seed(7 + sum(shape))
+    decay = torch.rand(B, K, H, generator=g)
+    hs = torch.randn(B, K, H, PN, generator=g).to(dtype)
+    gh = torch.randn(B, K, H, PN, generator=g).to(dtype)
+    dd, dc, dhi = _lib.scan_bwd(decay.cuda(), hs.cuda(), gh.cuda(), True)
+    dd2, dc2, dhi2 = _lib.scan_bwd(decay.cuda(), hs.cuda(), gh.cuda(), True)
+    assert torch.equal(dd, dd2) and torch.equal(dc, dc2) and torch.equal(dhi, dhi2)
+    ed, ec, ehi = oracle.ssd_scan_backward(decay.double().numpy(), hs.double().numpy(), gh.double().numpy(), True)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2  # bf16 d_chunk rounding
+    assert dc.dtype == dtype
+    assert max_rel(to_np(dc), ec) < tol
+    assert max_rel(to_np(dd), ed) < 1e-4
+    assert max_rel(to_np(dhi), ehi) < 1e-5
+
+
+def test_scan_backward_bf16_autograd_matches_fp32():
+    """bf16 h_chunk: the states are scanned and saved in fp32 (as the reference's CUDA path
+    does), so the gradients equal the fp32 gradients up to the bf16 rounding of grad_h."""
+    from mamba3_b200 import ssd_scan
+
+    g = torch.Generator().manual_seed(3)
+    decay = torch.rand(2, 12, 4, generator=g).cuda()
+    hc = torch.randn(2, 12, 4, 64, 128, generator=g).cuda()
+    gh = torch.randn(2, 12, 4, 64, 128, generator=g).cuda()
+    out = {}
+    for dt in (torch.float32, torch.bfloat16):
+        d = decay.clone().requires_grad_(True)
+        h = hc.to(dt).requires_grad_(True)
+        hs = ssd_scan(d, h)
+        assert hs.dtype == dt and hs.shape == hc.shape
+        out[dt] = torch.autograd.grad(hs, [d, h], gh.to(dt))
+    assert out[torch.bfloat16][1].dtype == torch.bfloat16
+    assert max_rel(to_np(out[torch.bfloat16][0]), to_np(out[torch.float32][0])) < 2e-2
+    assert max_rel(to_np(out[torch.bfloat16][1]), to_np(out[torch.float32][1])) < 2e-2
 
 
 @pytest.mark.parametrize("case", LAYER_CASES)

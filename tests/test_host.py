@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(h, n), n
     assert set(names) == set(_lib.SIGNATURES), "ctypes binding must cover exactly the header"
     L = _lib.lib()
-    assert L.m3b_abi_version() == 3
+    assert L.m3b_abi_version() == 4
     assert L.m3b_strerror(0) == b"ok"
 
 
@@ -47,6 +47,10 @@ def test_library_rejects_bad_args_without_gpu():
     f = _lib.LayerFwdArgs()
     assert L.m3b_layer_fwd_workspace(ctypes.byref(f)) == 0
     assert L.m3b_layer_fwd(ctypes.byref(f), None, 0, None) == 1
+    sb = _lib.ScanBwdArgs()
+    assert L.m3b_scan_bwd_workspace(ctypes.byref(sb)) == 0
+    assert L.m3b_scan_bwd(ctypes.byref(sb), None, 0, None) == 1
+    assert b"null" in L.m3b_last_error()
 
 
 @pytest.mark.parametrize("case", ["default", "rank1", "ngroups2", "euler", "real"])

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 import oracle
-from goldens import LAYER_CASES, SCAN_CASES, SSD_CASES, layer_cfg, load, max_rel, state_dict
+from goldens import LAYER_CASES, SCAN_BWD_CASES, SCAN_CASES, SSD_CASES, layer_cfg, load, max_rel, state_dict
 
 
 @pytest.mark.parametrize("case", LAYER_CASES)
@@ -51,6 +51,23 @@ def test_ssd_scan(case):
     d = load(f"scan_{case}")
     hs = oracle.ssd_scan(d["decay"].astype(np.float64), d["h_chunk"].astype(np.float64), d.get("h_init"))
     assert max_rel(hs, d["h_states"]) < 1e-6
+
+
+@pytest.mark.parametrize("case", SCAN_BWD_CASES)
+def test_ssd_scan_backward(case):
+    """The oracle's scan gradients == the reference's autograd gradients (SSDScanFn.backward)."""
+    d = load(f"scanbwd_{case}")
+    hi = d.get("h_init")
+    hs = oracle.ssd_scan(d["decay"].astype(np.float64), d["h_chunk"].astype(np.float64), hi)
+    assert max_rel(hs, d["h_states"]) < 1e-6
+    dd, dc, dhi = oracle.ssd_scan_backward(d["decay"].astype(np.float64), hs, d["grad_h"].astype(np.float64),
+                                          has_h_init=hi is not None)
+    assert max_rel(dd, d["d_decay"]) < 1e-5
+    assert max_rel(dc, d["d_chunk"]) < 1e-6
+    if hi is not None:
+        assert max_rel(dhi, d["d_h_init"]) < 1e-6
+    else:
+        assert dhi is None
 
 
 def test_lm_forward_and_greedy_generate():
