@@ -262,6 +262,46 @@ M3B_API size_t m3b_chunked_ssd_workspace(const m3b_ssd_args* a);
 M3B_API int m3b_chunked_ssd(const m3b_ssd_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Backward of chunked_ssd: the gradients torch autograd gives the reference through
+ * _IntraChunkFn (mamba3/ssd.py:27-115), SSDScanFn (mamba3/scan.py:65-140) and the torch
+ * ops of chunked_ssd (mamba3/ssd.py:118-244), for the same inputs as m3b_ssd_args plus the
+ * output gradients dy (and dh_final when h_final was used).  fp32 arithmetic; gradients
+ * in the dtypes of their inputs (ddt in dt_dtype; dA, dD per head and dh_init in fp32).
+ * Deterministic: no atomics, every sum in a fixed order.
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_ssd_bwd_args {
+  int64_t batch, seqlen;
+  int32_t H, P, N, R;
+  int32_t dtype;             /* of x_g, x_b, B_g, B_b, C, x_raw, dy and their gradients */
+  const void* x_g;           /* (batch,seqlen,H,P,R) */
+  const void* x_b;           /* (batch,seqlen,H,P,R) or NULL (Euler) */
+  const void* B_g;           /* (batch,seqlen,H,N,R) */
+  const void* B_b;           /* (batch,seqlen,H,N,R) or NULL (NULL iff x_b is NULL) */
+  const void* C;             /* (batch,seqlen,H,N,R) */
+  const void* x_raw;         /* (batch,seqlen,H,P,R) */
+  const void* dt;            /* (batch,seqlen,H), dt_dtype */
+  int32_t dt_dtype;
+  const void* A;             /* (H), ad_dtype */
+  const void* D;             /* (H), ad_dtype */
+  int32_t ad_dtype;
+  const float* h_init;       /* (batch,H,P,N) or NULL */
+  const void* dy;            /* (batch,seqlen,H,P,R), dtype */
+  const float* dh_final;     /* (batch,H,P,N) or NULL */
+  void* dx_g;                /* (batch,seqlen,H,P,R), dtype */
+  void* dx_b;                /* (batch,seqlen,H,P,R) or NULL (NULL iff x_b is NULL) */
+  void* dB_g;                /* (batch,seqlen,H,N,R) */
+  void* dB_b;                /* (batch,seqlen,H,N,R) or NULL (NULL iff x_b is NULL) */
+  void* dC;                  /* (batch,seqlen,H,N,R) */
+  void* dx_raw;              /* (batch,seqlen,H,P,R) */
+  void* ddt;                 /* (batch,seqlen,H), dt_dtype */
+  float* dA;                 /* (H) */
+  float* dD;                 /* (H) */
+  float* dh_init;            /* (batch,H,P,N) or NULL */
+} m3b_ssd_bwd_args;
+M3B_API size_t m3b_chunked_ssd_bwd_workspace(const m3b_ssd_bwd_args* a);
+M3B_API int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Tensor-core self-test (diagnostic; no counterpart in the reference).
  * D (128 x 64, fp32) = A (128 x 128 bf16, row-major) x B (64 x 128 bf16, row-major)^T,
  * staged through the same shared-memory layouts and UMMA descriptors as the chunk

@@ -81,6 +81,17 @@ class SsdArgs(C.Structure):
                 ("err", C.c_void_p)]
 
 
+class SsdBwdArgs(C.Structure):
+    _fields_ = [("batch", C.c_int64), ("seqlen", C.c_int64), ("H", C.c_int32), ("P", C.c_int32), ("N", C.c_int32),
+                ("R", C.c_int32), ("dtype", C.c_int32), ("x_g", C.c_void_p), ("x_b", C.c_void_p),
+                ("B_g", C.c_void_p), ("B_b", C.c_void_p), ("C", C.c_void_p), ("x_raw", C.c_void_p),
+                ("dt", C.c_void_p), ("dt_dtype", C.c_int32), ("A", C.c_void_p), ("D", C.c_void_p),
+                ("ad_dtype", C.c_int32), ("h_init", C.c_void_p), ("dy", C.c_void_p), ("dh_final", C.c_void_p),
+                ("dx_g", C.c_void_p), ("dx_b", C.c_void_p), ("dB_g", C.c_void_p), ("dB_b", C.c_void_p),
+                ("dC", C.c_void_p), ("dx_raw", C.c_void_p), ("ddt", C.c_void_p), ("dA", C.c_void_p),
+                ("dD", C.c_void_p), ("dh_init", C.c_void_p)]
+
+
 LAYER_FWD_STAGES = ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out", "last_bx")
 
 
@@ -100,6 +111,8 @@ SIGNATURES = {
                                       C.c_void_p]),
     "m3b_chunked_ssd_workspace": (C.c_size_t, [C.POINTER(SsdArgs)]),
     "m3b_chunked_ssd": (C.c_int, [C.POINTER(SsdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_chunked_ssd_bwd_workspace": (C.c_size_t, [C.POINTER(SsdBwdArgs)]),
+    "m3b_chunked_ssd_bwd": (C.c_int, [C.POINTER(SsdBwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_selftest_umma": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
 }
 
@@ -252,6 +265,32 @@ def chunked_ssd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, y, h_init=None, h_final
     ws = torch.empty(need, dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         _check(L.m3b_chunked_ssd(C.byref(a), _ptr(ws), need, _stream(dev)), "m3b_chunked_ssd")
+
+
+def chunked_ssd_bwd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init=None, dh_final=None):
+    """Launch the chunked SSD backward.  Activations, dy contiguous and of one dtype (fp32 / bf16);
+    dt fp32 / bf16 / fp16; A, D of one dtype; h_init, dh_final fp32 or None.  Returns a dict of
+    gradients (x_g, x_b, B_g, B_b, C, x_raw in the activation dtype, dt in dt's dtype, A, D, h_init
+    fp32; None for absent inputs)."""
+    dev = _cuda(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init, dh_final)
+    Bt, T, H, P, R = x_g.shape
+    N = B_g.shape[3]
+    e = lambda t: None if t is None else torch.empty_like(t)  # noqa: E731
+    g = dict(x_g=e(x_g), x_b=e(x_b), B_g=e(B_g), B_b=e(B_b), C=e(Cm), x_raw=e(x_raw), dt=e(dt),
+             A=torch.empty(H, dtype=torch.float32, device=dev), D=torch.empty(H, dtype=torch.float32, device=dev),
+             h_init=None if h_init is None else torch.empty(Bt, H, P, N, dtype=torch.float32, device=dev))
+    a = SsdBwdArgs(Bt, T, H, P, N, R, dtype_code(x_g.dtype), _ptr(x_g), _ptr(x_b), _ptr(B_g), _ptr(B_b), _ptr(Cm),
+                   _ptr(x_raw), _ptr(dt), dtype_code(dt.dtype), _ptr(A), _ptr(D), dtype_code(A.dtype), _ptr(h_init),
+                   _ptr(dy), _ptr(dh_final), _ptr(g["x_g"]), _ptr(g["x_b"]), _ptr(g["B_g"]), _ptr(g["B_b"]),
+                   _ptr(g["C"]), _ptr(g["x_raw"]), _ptr(g["dt"]), _ptr(g["A"]), _ptr(g["D"]), _ptr(g["h_init"]))
+    L = lib()
+    need = L.m3b_chunked_ssd_bwd_workspace(C.byref(a))
+    if need == 0:
+        _check(L.m3b_chunked_ssd_bwd(C.byref(a), None, 0, None), "m3b_chunked_ssd_bwd")
+    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(L.m3b_chunked_ssd_bwd(C.byref(a), _ptr(ws), need, _stream(dev)), "m3b_chunked_ssd_bwd")
+    return g
 
 
 def selftest_umma(A, B, mode):

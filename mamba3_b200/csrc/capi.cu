@@ -18,6 +18,8 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+void clear_error() { g_last_error[0] = 0; }
+
 int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));

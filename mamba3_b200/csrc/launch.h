@@ -10,6 +10,8 @@ namespace m3b {
 
 // Record a failure detail for m3b_last_error() and return `code`.
 int fail(int code, const char* fmt, ...);
+// Clear the calling thread's m3b_last_error() detail (at the start of an entry point).
+void clear_error();
 // cudaGetLastError() after a launch -> M3B_OK or M3B_ERR_CUDA (with detail).
 int check_launch(const char* what);
 // Number of SMs of the current device (cached per device).

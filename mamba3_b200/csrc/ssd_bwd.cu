@@ -1,0 +1,443 @@
+// Backward of chunked_ssd on pre-processed tensors (the gradients of mamba3/ssd.py:118-244,
+// which the reference obtains from torch autograd through _IntraChunkFn, mamba3/ssd.py:27-115,
+// and SSDScanFn, mamba3/scan.py:65-140).
+//
+// The chunked forward is the token recurrence (per batch row b and head h; chunking only
+// regroups it):
+//   h_t = a_t h_{t-1} + dt_t Xt_t Bt_t^T,  a_t = exp(A dt_t),  h_{-1} = h_init,
+//   y_t = h_t C_t + D x_raw_t,             h_final = h_{T-1}
+// with Xt = [x_g | x_b] (P x RI), Bt = [B_g | B_b] (N x RI), C (N x R).  Its gradients, with
+// G_t = dL/dh_t = a_{t+1} G_{t+1} + dy_t C_t^T (G_T = dh_final, a_T = 1):
+//   dXt_t = dt_t G_t Bt_t,  dBt_t = dt_t G_t^T Xt_t,  dC_t = h_t^T dy_t,
+//   dx_raw = D dy,  dD = sum dy . x_raw,  dh_init = a_0 G_0,
+//   ddt_t = fr_t + A m_t,  dA = sum_t dt_t m_t,
+// where fr_t = <G_t, Xt_t Bt_t^T> and m_t = a_t <G_t, h_{t-1}>.  m_t needs h_{t-1} and G_t
+// together, but satisfies a scalar recurrence: <G_t, h_t> = m_{t+1} + e_t with
+// e_t = <dy_t, h_t C_t> = <C_t, dC_t>, and <G_t, h_t> = m_t + dt_t fr_t, so
+//   m_t = m_{t+1} + e_t - dt_t fr_t,  m_T = <dh_final, h_final>:
+// a suffix sum of per-token scalars from the two sweeps.
+//
+// Design: one CTA per (batch row, head) walks the tokens twice with the P x N state in
+// shared memory (rows padded to N + 1 floats: column walks are conflict free): a forward
+// sweep (h, dC, e_t, dx_raw, dD) and a reverse sweep (G, dXt, dBt, fr_t, dh_init), then the
+// suffix sum gives ddt and this row's share of dA.  Each token's operands are staged in a
+// double-buffered shared-memory slot loaded one token ahead; per-token scalars go to the
+// workspace as per-warp partial sums, added in warp order, and the (b, h) shares of dA / dD
+// are added over b in order by a second kernel: no atomics, bitwise reproducible.  fp32
+// arithmetic throughout; gradients are stored in the dtypes of their inputs.
+#include "chunk.cuh"
+#include "launch.h"
+
+namespace m3b {
+
+namespace {
+
+constexpr int kBwdThreads = 256;
+constexpr int kBwdWarps = kBwdThreads / 32;
+constexpr int kMaxRI = 16;  // 2 R with R <= 8
+
+struct BwdParams {
+  int64_t B, T;
+  int H, P, N, R, RI;
+  const void *x_g, *x_b, *B_g, *B_b, *C, *x_raw, *dt, *A, *D, *dy;
+  int dt_dtype, ad_dtype;
+  const float* h_init;
+  const float* dh_final;
+  void *dx_g, *dx_b, *dB_g, *dB_b, *dC, *dx_raw, *ddt;
+  float* dh_init;
+  float* ew;   // (B*H, T, kBwdWarps) per-warp partials of e_t
+  float* fw;   // (B*H, T, kBwdWarps) per-warp partials of fr_t
+  float* dA_bh;  // (B, H)
+  float* dD_bh;  // (B, H)
+};
+
+// One token's operands in shared memory (floats): Xt [p][j], Bt^T [j][n], C^T [q][n], dy [p][q]
+struct Slot {
+  float* x;
+  float* bt;
+  float* ct;
+  float* dy;
+  float* sc;  // dt, a
+};
+
+__host__ __device__ inline int slot_floats(int P, int N, int R, int RI) {
+  return ((P * RI + RI * N + R * N + P * R + 4) + 3) & ~3;
+}
+
+__device__ __forceinline__ Slot slot_at(float* base, int P, int N, int R, int RI) {
+  Slot s;
+  s.x = base;
+  s.bt = s.x + P * RI;
+  s.ct = s.bt + RI * N;
+  s.dy = s.ct + R * N;
+  s.sc = s.dy + P * R;
+  return s;
+}
+
+template <typename T>
+__device__ __forceinline__ void load_slot(const BwdParams& a, const Slot& s, int64_t b, int h, int64_t t,
+                                          float Aval) {
+  const int P = a.P, N = a.N, R = a.R, RI = a.RI;
+  const int64_t row = (b * a.T + t) * a.H + h;
+  const T* xg = static_cast<const T*>(a.x_g) + row * P * R;
+  const T* xb = a.x_b ? static_cast<const T*>(a.x_b) + row * P * R : nullptr;
+  const T* bg = static_cast<const T*>(a.B_g) + row * N * R;
+  const T* bb = a.B_b ? static_cast<const T*>(a.B_b) + row * N * R : nullptr;
+  const T* cc = static_cast<const T*>(a.C) + row * N * R;
+  const T* gy = static_cast<const T*>(a.dy) + row * P * R;
+  for (int e = threadIdx.x; e < P * R; e += kBwdThreads) {
+    const int p = e / R, r = e - p * R;
+    s.x[p * RI + r] = io<T>::ld(xg + e);
+    if (xb) s.x[p * RI + R + r] = io<T>::ld(xb + e);
+    s.dy[e] = io<T>::ld(gy + e);
+  }
+  for (int e = threadIdx.x; e < N * R; e += kBwdThreads) {
+    const int n = e / R, r = e - n * R;
+    s.bt[r * N + n] = io<T>::ld(bg + e);
+    if (bb) s.bt[(R + r) * N + n] = io<T>::ld(bb + e);
+    s.ct[r * N + n] = io<T>::ld(cc + e);
+  }
+  if (threadIdx.x == 0) {
+    const float dtv = ldf(a.dt, row, a.dt_dtype);
+    s.sc[0] = dtv;
+    s.sc[1] = expf(Aval * dtv);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kBwdThreads) ssd_bwd_kernel(BwdParams a) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int P = a.P, N = a.N, R = a.R, RI = a.RI;
+  const int NS = N + 1;  // padded row of the state
+  const int64_t bh = blockIdx.x;
+  const int64_t b = bh / a.H;
+  const int h = (int)(bh - b * a.H);
+  const int64_t TT = a.T;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* S = sm;  // [P][N+1]: h in the forward sweep, G in the reverse sweep
+  const int sf = slot_floats(P, N, R, RI);
+  float* slots = S + ((P * NS + 3) & ~3);
+  float* red = slots + (2 * sf > kBwdThreads ? 2 * sf : kBwdThreads);  // [kBwdWarps] block reductions
+  auto slot = [&](int64_t t) { return slot_at(slots + (t & 1) * sf, P, N, R, RI); };
+  const float Aval = ldf(a.A, h, a.ad_dtype);
+  const float Dval = ldf(a.D, h, a.ad_dtype);
+  const int64_t state_base = bh * (int64_t)P * N;
+  float* ew = a.ew + bh * TT * kBwdWarps;
+  float* fw = a.fw + bh * TT * kBwdWarps;
+
+  // ---------------- forward sweep: h_t, dC_t, e_t, dx_raw, dD ----------------
+  for (int e = tid; e < P * N; e += kBwdThreads) {
+    const int p = e / N, n = e - p * N;
+    S[p * NS + n] = a.h_init ? a.h_init[state_base + e] : 0.f;
+  }
+  float dD_acc = 0.f;
+  if (TT > 0) load_slot<T>(a, slot(0), b, h, 0, Aval);
+  __syncthreads();
+  for (int64_t t = 0; t < TT; ++t) {
+    const Slot s = slot(t);
+    const float dtv = s.sc[0], av = s.sc[1];
+    // h_t = a_t h_{t-1} + dt_t Xt Bt^T
+    for (int e = tid; e < P * N; e += kBwdThreads) {
+      const int p = e / N, n = e - p * N;
+      float u = 0.f;
+      for (int j = 0; j < RI; ++j) u = fmaf(s.x[p * RI + j], s.bt[j * N + n], u);
+      S[p * NS + n] = fmaf(av, S[p * NS + n], dtv * u);
+    }
+    // dx_raw = D dy and dD (this slot's dy; x_raw straight from global memory)
+    {
+      const int64_t row = (b * TT + t) * a.H + h;
+      const T* xr = static_cast<const T*>(a.x_raw) + row * P * R;
+      T* dxr = static_cast<T*>(a.dx_raw) + row * P * R;
+      for (int e = tid; e < P * R; e += kBwdThreads) {
+        const float g = s.dy[e];
+        dD_acc = fmaf(g, io<T>::ld(xr + e), dD_acc);
+        io<T>::st(dxr + e, Dval * g);
+      }
+    }
+    __syncthreads();
+    if (t + 1 < TT) load_slot<T>(a, slot(t + 1), b, h, t + 1, Aval);
+    // dC_t[n, q] = sum_p h_t[p, n] dy_t[p, q];  e_t = <C_t, dC_t>
+    {
+      const int64_t row = (b * TT + t) * a.H + h;
+      T* dc = static_cast<T*>(a.dC) + row * N * R;
+      float e_acc = 0.f;
+      for (int o = tid; o < N * R; o += kBwdThreads) {
+        const int q = o / N, n = o - q * N;
+        float v = 0.f;
+        for (int p = 0; p < P; ++p) v = fmaf(S[p * NS + n], s.dy[p * R + q], v);
+        io<T>::st(dc + (int64_t)n * R + q, v);
+        e_acc = fmaf(s.ct[q * N + n], v, e_acc);
+      }
+      e_acc = warp_sum(e_acc);
+      if (lane == 0) ew[t * kBwdWarps + warp] = e_acc;
+    }
+    __syncthreads();
+  }
+  // h_final = h_{T-1};  m_T = <dh_final, h_final>
+  float mT = 0.f;
+  {
+    float acc = 0.f;
+    if (a.dh_final)
+      for (int e = tid; e < P * N; e += kBwdThreads) {
+        const int p = e / N, n = e - p * N;
+        acc = fmaf(a.dh_final[state_base + e], S[p * NS + n], acc);
+      }
+    acc = warp_sum(acc);
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    for (int w = 0; w < kBwdWarps; ++w) mT += red[w];
+    __syncthreads();
+  }
+
+  // ---------------- reverse sweep: G_t, dXt_t, dBt_t, fr_t, dh_init ----------------
+  for (int e = tid; e < P * N; e += kBwdThreads) {
+    const int p = e / N, n = e - p * N;
+    S[p * NS + n] = a.dh_final ? a.dh_final[state_base + e] : 0.f;
+  }
+  if (TT > 0) load_slot<T>(a, slot(TT - 1), b, h, TT - 1, Aval);
+  __syncthreads();
+  float a_next = 1.f;  // a_{t+1} (1 past the last token)
+  for (int64_t t = TT - 1; t >= 0; --t) {
+    const Slot s = slot(t);
+    const float dtv = s.sc[0], av = s.sc[1];
+    // G_t = a_{t+1} G_{t+1} + dy_t C_t^T
+    for (int e = tid; e < P * N; e += kBwdThreads) {
+      const int p = e / N, n = e - p * N;
+      float u = 0.f;
+      for (int q = 0; q < R; ++q) u = fmaf(s.dy[p * R + q], s.ct[q * N + n], u);
+      S[p * NS + n] = fmaf(a_next, S[p * NS + n], u);
+    }
+    __syncthreads();
+    if (t > 0) load_slot<T>(a, slot(t - 1), b, h, t - 1, Aval);
+    const int64_t row = (b * TT + t) * a.H + h;
+    // dXt[p, j] = dt_t sum_n G_t[p, n] Bt[n, j]
+    for (int o = tid; o < P * RI; o += kBwdThreads) {
+      const int j = o / P, p = o - j * P;
+      float v = 0.f;
+      for (int n = 0; n < N; ++n) v = fmaf(S[p * NS + n], s.bt[j * N + n], v);
+      v *= dtv;
+      if (j < R) io<T>::st(static_cast<T*>(a.dx_g) + row * P * R + (int64_t)p * R + j, v);
+      else io<T>::st(static_cast<T*>(a.dx_b) + row * P * R + (int64_t)p * R + (j - R), v);
+    }
+    // E[n, j] = sum_p G_t[p, n] Xt[p, j];  dBt = dt_t E;  fr_t = <Bt, E>
+    float f_acc = 0.f;
+    for (int o = tid; o < N * RI; o += kBwdThreads) {
+      const int j = o / N, n = o - j * N;
+      float v = 0.f;
+      for (int p = 0; p < P; ++p) v = fmaf(S[p * NS + n], s.x[p * RI + j], v);
+      f_acc = fmaf(s.bt[j * N + n], v, f_acc);
+      v *= dtv;
+      if (j < R) io<T>::st(static_cast<T*>(a.dB_g) + row * N * R + (int64_t)n * R + j, v);
+      else io<T>::st(static_cast<T*>(a.dB_b) + row * N * R + (int64_t)n * R + (j - R), v);
+    }
+    f_acc = warp_sum(f_acc);
+    if (lane == 0) fw[t * kBwdWarps + warp] = f_acc;
+    a_next = av;
+    __syncthreads();
+  }
+  // dh_init = a_0 G_0
+  if (a.dh_init)
+    for (int e = tid; e < P * N; e += kBwdThreads) {
+      const int p = e / N, n = e - p * N;
+      a.dh_init[state_base + e] = a_next * S[p * NS + n];
+    }
+
+  // ---------------- suffix sum: m_t = m_{t+1} + e_t - dt_t fr_t; ddt, dA ----------------
+  // thread i owns tokens [i*seg, (i+1)*seg); the per-warp partials of e_t, fr_t are visible
+  // (written before the last barrier of the reverse sweep, or the forward sweep's)
+  const int64_t seg = (TT + kBwdThreads - 1) / kBwdThreads;
+  const int64_t t0 = tid * seg, t1 = t0 + seg < TT ? t0 + seg : TT;
+  auto tok = [&](int64_t t, float& e, float& f, float& dtv) {
+    e = 0.f;
+    f = 0.f;
+    for (int w = 0; w < kBwdWarps; ++w) {
+      e += ew[t * kBwdWarps + w];
+      f += fw[t * kBwdWarps + w];
+    }
+    dtv = ldf(a.dt, (b * TT + t) * a.H + h, a.dt_dtype);
+  };
+  float local = 0.f;
+  for (int64_t t = t0; t < t1; ++t) {
+    float e, f, dtv;
+    tok(t, e, f, dtv);
+    local += e - dtv * f;
+  }
+  float* suf = slots;  // reuse: kBwdThreads segment sums (slots hold >= 2 * 4 floats per thread)
+  suf[tid] = local;
+  __syncthreads();
+  if (tid == 0) {  // exclusive suffix sums of the segment sums, in segment order
+    float acc = mT;
+    for (int i = kBwdThreads - 1; i >= 0; --i) {
+      const float v = suf[i];
+      suf[i] = acc;
+      acc += v;
+    }
+  }
+  __syncthreads();
+  float m = suf[tid];
+  float dA_acc = 0.f;
+  for (int64_t t = t1 - 1; t >= t0; --t) {
+    float e, f, dtv;
+    tok(t, e, f, dtv);
+    m += e - dtv * f;
+    const int64_t row = (b * TT + t) * a.H + h;
+    const float g = f + Aval * m;
+    if (a.dt_dtype == M3B_F32) static_cast<float*>(a.ddt)[row] = g;
+    else if (a.dt_dtype == M3B_BF16) static_cast<__nv_bfloat16*>(a.ddt)[row] = __float2bfloat16_rn(g);
+    else static_cast<__half*>(a.ddt)[row] = __float2half_rn(g);
+    dA_acc = fmaf(dtv, m, dA_acc);
+  }
+  __syncthreads();
+  dA_acc = warp_sum(dA_acc);
+  dD_acc = warp_sum(dD_acc);
+  if (lane == 0) {
+    red[warp] = dA_acc;
+    suf[warp] = dD_acc;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float sa = 0.f, sd = 0.f;
+    for (int w = 0; w < kBwdWarps; ++w) {
+      sa += red[w];
+      sd += suf[w];
+    }
+    a.dA_bh[bh] = sa;
+    a.dD_bh[bh] = sd;
+  }
+}
+
+// dA[h] = sum_b dA_bh[b, h], dD likewise, in b order
+__global__ void ssd_bwd_head_sums(const float* __restrict__ dA_bh, const float* __restrict__ dD_bh,
+                                  float* __restrict__ dA, float* __restrict__ dD, int64_t B, int H) {
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= H) return;
+  float sa = 0.f, sd = 0.f;
+  for (int64_t b = 0; b < B; ++b) {
+    sa += dA_bh[b * H + h];
+    sd += dD_bh[b * H + h];
+  }
+  dA[h] = sa;
+  dD[h] = sd;
+}
+
+struct BwdLayout {
+  size_t ew, fw, dA, dD, total;
+};
+
+BwdLayout bwd_layout(const m3b_ssd_bwd_args* a) {
+  auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  BwdLayout w{};
+  const size_t bh = (size_t)a->batch * a->H;
+  const size_t tok = bh * (size_t)a->seqlen * kBwdWarps * sizeof(float);
+  w.ew = 0;
+  w.fw = up(tok);
+  w.dA = w.fw + up(tok);
+  w.dD = w.dA + up(bh * sizeof(float));
+  w.total = w.dD + up(bh * sizeof(float));
+  return w;
+}
+
+int bvalidate(const m3b_ssd_bwd_args* a) {
+  if (!a->A || !a->D || !a->dA || !a->dD) return fail(M3B_ERR_INVALID_ARG, "chunked_ssd_bwd: null pointer");
+  // per-token tensors may be empty (NULL) when there are no tokens
+  if (a->seqlen > 0 && (!a->x_g || !a->B_g || !a->C || !a->x_raw || !a->dt || !a->dy || !a->dx_g || !a->dB_g ||
+                        !a->dC || !a->dx_raw || !a->ddt))
+    return fail(M3B_ERR_INVALID_ARG, "chunked_ssd_bwd: null pointer");
+  if ((a->x_b == nullptr) != (a->B_b == nullptr) || (a->x_b == nullptr) != (a->dx_b == nullptr) ||
+      (a->x_b == nullptr) != (a->dB_b == nullptr))
+    return fail(M3B_ERR_INVALID_ARG, "chunked_ssd_bwd: x_b, B_b, dx_b, dB_b must all be given or all be NULL");
+  if (a->batch < 0 || a->seqlen < 0 || a->H <= 0 || a->P <= 0 || a->N <= 0 || a->R <= 0)
+    return fail(M3B_ERR_INVALID_ARG, "chunked_ssd_bwd: bad dims");
+  if (a->P > 256 || a->N > 256 || a->R > kMaxRI / 2)
+    return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: needs P <= 256, N <= 256, R <= 8");
+  if (a->dtype != M3B_BF16 && a->dtype != M3B_F32) return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: dtype");
+  if (a->dt_dtype != M3B_F32 && a->dt_dtype != M3B_BF16 && a->dt_dtype != M3B_F16)
+    return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: dt dtype");
+  if (a->batch * a->H > 0x7fffffffLL) return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: batch * H too large");
+  return M3B_OK;
+}
+
+size_t bwd_smem(const m3b_ssd_bwd_args* a) {
+  const int RI = a->x_b ? 2 * a->R : a->R;
+  const size_t st = ((size_t)a->P * (a->N + 1) + 3) & ~(size_t)3;
+  size_t sl = 2 * (size_t)slot_floats(a->P, a->N, a->R, RI);
+  if (sl < kBwdThreads) sl = kBwdThreads;  // the suffix-sum pass reuses the slots
+  return (st + sl + kBwdWarps) * sizeof(float);
+}
+
+}  // namespace
+
+}  // namespace m3b
+
+extern "C" size_t m3b_chunked_ssd_bwd_workspace(const m3b_ssd_bwd_args* a) {
+  if (!a || m3b::bvalidate(a) != M3B_OK) return 0;
+  return m3b::bwd_layout(a).total;
+}
+
+extern "C" int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* ws, size_t ws_bytes, void* stream) {
+  using namespace m3b;
+  clear_error();
+  if (!a) return fail(M3B_ERR_INVALID_ARG, "chunked_ssd_bwd: null args");
+  int rc = bvalidate(a);
+  if (rc != M3B_OK) return rc;
+  if (a->batch == 0) return M3B_OK;
+  const BwdLayout w = bwd_layout(a);
+  if (!ws || ws_bytes < w.total)
+    return fail(M3B_ERR_WORKSPACE, "chunked_ssd_bwd: need %zu workspace bytes", w.total);
+  const size_t smem = bwd_smem(a);
+  if (smem > 227 * 1024) return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: state too large for shared memory");
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  BwdParams p{};
+  p.B = a->batch;
+  p.T = a->seqlen;
+  p.H = a->H;
+  p.P = a->P;
+  p.N = a->N;
+  p.R = a->R;
+  p.RI = a->x_b ? 2 * a->R : a->R;
+  p.x_g = a->x_g;
+  p.x_b = a->x_b;
+  p.B_g = a->B_g;
+  p.B_b = a->B_b;
+  p.C = a->C;
+  p.x_raw = a->x_raw;
+  p.dt = a->dt;
+  p.A = a->A;
+  p.D = a->D;
+  p.dy = a->dy;
+  p.dt_dtype = a->dt_dtype;
+  p.ad_dtype = a->ad_dtype;
+  p.h_init = a->h_init;
+  p.dh_final = a->dh_final;
+  p.dx_g = a->dx_g;
+  p.dx_b = a->dx_b;
+  p.dB_g = a->dB_g;
+  p.dB_b = a->dB_b;
+  p.dC = a->dC;
+  p.dx_raw = a->dx_raw;
+  p.ddt = a->ddt;
+  p.dh_init = a->dh_init;
+  p.ew = reinterpret_cast<float*>(base + w.ew);
+  p.fw = reinterpret_cast<float*>(base + w.fw);
+  p.dA_bh = reinterpret_cast<float*>(base + w.dA);
+  p.dD_bh = reinterpret_cast<float*>(base + w.dD);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)(a->batch * a->H);
+  if (a->dtype == M3B_F32) {
+    cudaFuncSetAttribute(ssd_bwd_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ssd_bwd_kernel<float><<<grid, kBwdThreads, smem, st>>>(p);
+  } else {
+    cudaFuncSetAttribute(ssd_bwd_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ssd_bwd_kernel<__nv_bfloat16><<<grid, kBwdThreads, smem, st>>>(p);
+  }
+  if ((rc = check_launch("chunked_ssd_bwd")) != M3B_OK) return rc;
+  ssd_bwd_head_sums<<<(a->H + 127) / 128, 128, 0, st>>>(p.dA_bh, p.dD_bh, a->dA, a->dD, a->batch, a->H);
+  return check_launch("chunked_ssd_bwd_head_sums");
+}

@@ -8,6 +8,9 @@ kernels of ``libmamba3_b200`` (see ``ops.py``):
 
 * ``forward`` / ``prefill`` -> ``mamba3_b200::layer_ssd`` (chunked parallel form)
 * ``step``                  -> ``mamba3_b200::step_ssm`` (O(1) recurrent form)
+* with gradients (training) -> torch autograd for the projection split, norms, rotation,
+  MIMO and gate around ``chunked_ssd``, whose forward and backward are the library's
+  kernels (``ssd.ChunkedSSDFn``)
 
 Deviation from the reference (documented): the ``angle`` entry of the inference
 state is kept in fp32 whatever the model dtype (the reference accumulates it in
@@ -20,8 +23,10 @@ import math
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import ops
+from .ssd import chunked_ssd
 
 
 class RMSNorm(nn.Module):
@@ -38,6 +43,16 @@ class RMSNorm(nn.Module):
         shape = [1] * x.ndim
         shape[self.dim] = -1
         return x * inv * self.weight.view(*shape)
+
+
+def _rope_pairs(t, c, s):
+    """Rotate (..., N, R) pairwise along N -- pairs (2i, 2i+1), the same angle for every rank --
+    by angles with cosines c and sines s of shape (..., N/2) (mamba3/mamba3.py:38-45)."""
+    *lead, N, R = t.shape
+    tp = t.reshape(*lead, N // 2, 2, R)
+    a, b = tp[..., 0, :], tp[..., 1, :]
+    c, s = c[..., None], s[..., None]
+    return torch.stack([a * c - b * s, a * s + b * c], dim=-2).reshape(*lead, N, R)
 
 
 class KulaMamba(nn.Module):
@@ -135,11 +150,65 @@ class KulaMamba(nn.Module):
             return y
         return y, {"h": h, "angle": angle, "prev_BX": prev_bx}
 
+    def _needs_grad(self, x):
+        return torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters()))
+
+    def _ssd_train(self, proj, dt_scale, return_state):
+        """Differentiable path between in_proj and out_proj (mamba3/mamba3.py:192-256): torch ops
+        for the split, dt, B/C norm + bias + rotation, MIMO and trapezoid scaling and the gate,
+        around chunked_ssd (forward and backward kernels).  -> y (B,T,d_inner) [, state]."""
+        Bat, T, _ = proj.shape
+        H, P, N, R, G = self.nheads, self.headdim, self.d_state, self.mimo_rank, self.ngroups
+        sizes = [self.d_inner, self._d_x, self._d_bc, self._d_bc, H]
+        sizes += [H] if self.use_trapezoidal else []
+        sizes += [N // 2] if self.use_complex_ssm else []
+        parts = list(torch.split(proj, sizes, dim=-1))
+        z, xf, Bf, Cf, dt_raw = parts[:5]
+        lam_raw = parts[5] if self.use_trapezoidal else None
+        theta = parts[-1] if self.use_complex_ssm else None
+        dt = F.softplus(dt_raw + self.dt_bias)
+        if dt_scale is not None:
+            dt = dt * dt_scale
+        A = -torch.exp(self.A_log)
+        B_r = self.B_norm(Bf.reshape(Bat, T, G, N * R)).reshape(Bat, T, G, N, R) + self.B_bias
+        C_r = self.C_norm(Cf.reshape(Bat, T, G, N * R)).reshape(Bat, T, G, N, R) + self.C_bias
+        if self.heads_per_group > 1:
+            B_r = B_r.repeat_interleave(self.heads_per_group, dim=2)
+            C_r = C_r.repeat_interleave(self.heads_per_group, dim=2)
+        cum = None
+        if self.use_complex_ssm:
+            cum = -(dt[..., None] * theta[..., None, :]).cumsum(dim=1)  # (B,T,H,N/2)
+            c, s = torch.cos(cum), torch.sin(cum)
+            B_r, C_r = _rope_pairs(B_r, c, s), _rope_pairs(C_r, c, s)
+        x_r = xf.reshape(Bat, T, H, P, 1) * self.mimo_x
+        if self.use_trapezoidal:
+            lam = torch.sigmoid(lam_raw)
+            x_g = x_r * lam[..., None, None]
+            scale_b = ((1.0 - lam) * torch.exp(A * dt))[..., None, None]
+            x_b = F.pad(x_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) * scale_b
+            B_b = F.pad(B_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0))
+        else:
+            x_g, x_b, B_b = x_r, None, None
+        out = chunked_ssd(x_g, x_b, B_r, B_b, C_r, dt, A, self.D, x_r, self.chunk_size,
+                          return_final_state=return_state)
+        z_r = z.reshape(Bat, T, H, P, 1) * self.mimo_z
+        y = (out.y * F.silu(z_r) * self.mimo_down).sum(-1).reshape(Bat, T, self.d_inner)
+        if not return_state:
+            return y, None
+        angle = cum[:, T - 1].float() if cum is not None else torch.zeros(Bat, H, N // 2, device=proj.device)
+        prev_bx = torch.einsum("bhnr,bhpr->bhpn", B_r[:, T - 1], x_r[:, T - 1]).float()
+        return y, {"h": out.h_final.float(), "angle": angle, "prev_BX": prev_bx}
+
     def _ssd(self, x, dt_scale, return_state, state=None):
         if x.dim() != 3 or x.shape[1] <= 0:
             raise ValueError(f"expected (batch, seqlen>0, d_model), got {tuple(x.shape)}")
         proj = self.in_proj(x)
         st = state or {}
+        if self._needs_grad(x):
+            if st:
+                raise NotImplementedError("prefill from a state with gradients enabled")
+            y, out_st = self._ssd_train(proj, dt_scale, return_state)
+            return self.out_proj(y), out_st
         if "prev_B" in st:  # compact state in, compact state out
             if dt_scale is not None:
                 raise NotImplementedError("dt_scale with a compact state")

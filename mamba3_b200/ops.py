@@ -142,6 +142,39 @@ def _(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, h_init, return_final_state):
     return torch.empty_like(x_g), hf
 
 
+_NONE = lambda dev: torch.empty(0, dtype=torch.float32, device=dev)  # noqa: E731
+
+
+@torch.library.custom_op("mamba3_b200::chunked_ssd_bwd", mutates_args=())
+def chunked_ssd_bwd(x_g: torch.Tensor, x_b: Optional[torch.Tensor], B_g: torch.Tensor, B_b: Optional[torch.Tensor],
+                    C: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, D: torch.Tensor, x_raw: torch.Tensor,
+                    h_init: Optional[torch.Tensor], dy: torch.Tensor,
+                    dh_final: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                               torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                               torch.Tensor, torch.Tensor]:
+    """Gradients of chunked_ssd: (dx_g, dx_b, dB_g, dB_b, dC, ddt, dA, dD, dx_raw, dh_init), in the
+    activation dtype (fp32 for ddt, dA, dD, dh_init); empty tensors stand for absent inputs."""
+    wd = x_g.dtype if x_g.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    c = lambda t: None if t is None else t.to(wd).contiguous()  # noqa: E731
+    f = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
+    A32 = A.float().contiguous()
+    g = _lib.chunked_ssd_bwd(c(x_g), c(x_b), c(B_g), c(B_b), c(C), f(dt), A32, D.to(A32.dtype).contiguous(),
+                             c(x_raw), c(dy), f(h_init), f(dh_final))
+    dev = x_g.device
+    o = lambda k: _NONE(dev) if g[k] is None else g[k]  # noqa: E731
+    return (o("x_g"), o("x_b"), o("B_g"), o("B_b"), o("C"), o("dt"), o("A"), o("D"), o("x_raw"), o("h_init"))
+
+
+@chunked_ssd_bwd.register_fake
+def _(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, h_init, dy, dh_final):
+    wd = x_g.dtype if x_g.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    dev = x_g.device
+    e = lambda t, dtype=wd: _NONE(dev) if t is None else torch.empty(t.shape, dtype=dtype, device=dev)  # noqa: E731
+    H = A.shape[0]
+    return (e(x_g), e(x_b), e(B_g), e(B_b), e(C), e(dt, torch.float32), torch.empty(H, device=dev),
+            torch.empty(H, device=dev), e(x_raw), e(h_init, torch.float32))
+
+
 # ---------------------------------------------------------------------------
 # decode step (everything between in_proj and out_proj of KulaMamba.step)
 # ---------------------------------------------------------------------------

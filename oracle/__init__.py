@@ -19,6 +19,7 @@ from .mamba3_oracle import (  # noqa: F401
     block_prefill,
     block_step,
     chunked_ssd,
+    chunked_ssd_backward,
     layer_forward,
     layer_prefill,
     layer_step,

@@ -231,6 +231,54 @@ def ssd_scan_backward(decay, h_states, grad_h, has_h_init=False):
     return d_decay, d_chunk, (g if has_h_init else None)
 
 
+def chunked_ssd_backward(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, dy, h_init=None, dh_final=None):
+    """Gradients of ``chunked_ssd`` (mamba3/ssd.py:118-244) -- what torch autograd returns
+    through _IntraChunkFn.backward (mamba3/ssd.py:67-115), SSDScanFn.backward
+    (mamba3/scan.py:102-140) and the surrounding torch ops -- for the loss
+    <y, dy> + <h_final, dh_final>.
+
+    The chunked forward is the token recurrence h_t = exp(A dt_t) h_{t-1} + dt_t Xt_t Bt_t^T
+    (Xt = [x_g | x_b], Bt = [B_g | B_b]), y_t = h_t C_t + D x_raw_t, h_final = h_{T-1}; its
+    gradients follow by the chain rule backwards in time with G_t = dL/dh_t.  Every state h_t
+    is kept (small cases only), so the decay terms use <G_t, h_{t-1}> directly.
+    Returns a dict: x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, h_init (None where absent).
+    """
+    f = lambda a: None if a is None else np.asarray(a, dtype=np.float64)  # noqa: E731
+    x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, dy, h_init, dh_final = map(
+        f, (x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, dy, h_init, dh_final))
+    Bat, T, H, P, R = x_g.shape
+    N = B_g.shape[3]
+    X2 = x_g if x_b is None else np.concatenate([x_g, x_b], axis=-1)   # (B,T,H,P,RI)
+    B2 = B_g if B_b is None else np.concatenate([B_g, B_b], axis=-1)   # (B,T,H,N,RI)
+    a = np.exp(A[None, None, :] * dt)                                  # (B,T,H)
+    hs = np.empty((T + 1, Bat, H, P, N))                                # hs[t + 1] = h_t
+    hs[0] = 0.0 if h_init is None else h_init
+    for t in range(T):
+        u = np.einsum("bhpj,bhnj->bhpn", X2[:, t], B2[:, t])
+        hs[t + 1] = a[:, t, :, None, None] * hs[t] + dt[:, t, :, None, None] * u
+    dX2 = np.zeros_like(X2)
+    dB2 = np.zeros_like(B2)
+    dC = np.einsum("tbhpn,bthpq->bthnq", hs[1:], dy)
+    ddt = np.zeros_like(dt)
+    dA = np.zeros(H)
+    G = np.zeros((Bat, H, P, N)) if dh_final is None else dh_final.copy()
+    a_next = np.ones((Bat, H))
+    for t in range(T - 1, -1, -1):
+        G = a_next[:, :, None, None] * G + np.einsum("bhpq,bhnq->bhpn", dy[:, t], C[:, t])
+        dX2[:, t] = dt[:, t, :, None, None] * np.einsum("bhpn,bhnj->bhpj", G, B2[:, t])
+        dB2[:, t] = dt[:, t, :, None, None] * np.einsum("bhpn,bhpj->bhnj", G, X2[:, t])
+        u = np.einsum("bhpj,bhnj->bhpn", X2[:, t], B2[:, t])
+        q = (G * hs[t]).sum(axis=(-2, -1))                             # <G_t, h_{t-1}>
+        ddt[:, t] = (G * u).sum(axis=(-2, -1)) + A[None, :] * a[:, t] * q
+        dA += (dt[:, t] * a[:, t] * q).sum(axis=0)
+        a_next = a[:, t]
+    out = dict(x_g=dX2[..., :R], x_b=None if x_b is None else dX2[..., R:], B_g=dB2[..., :R],
+               B_b=None if B_b is None else dB2[..., R:], C=dC, dt=ddt, A=dA,
+               D=(dy * x_raw).sum(axis=(0, 1, 3, 4)), x_raw=D[None, None, :, None, None] * dy,
+               h_init=None if h_init is None else a_next[:, :, None, None] * G)
+    return out
+
+
 def chunked_ssd(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, chunk_size=64, h_init=None,
                 return_final_state=False):
     """Chunked SSD forward (mamba3/ssd.py:118-244) with the factored intra-chunk cumsum

@@ -63,6 +63,27 @@ def layer_case(M, name, seed, B, T, perturb, n_steps=4, **kw):
     np.savez_compressed(HERE / f"layer_{name}.npz", **out)
 
 
+def layer_grad_case(M, name, seed, B, T, perturb, **kw):
+    """Parameter and input gradients of the reference layer for the loss <y, gy> (CPU fp32,
+    train mode): what loss.backward() leaves in .grad (mamba3 tests:81-91 check only that
+    they exist and are finite; these pin their values)."""
+    torch.manual_seed(seed)
+    layer = M.KulaMamba(**kw).train()
+    if perturb:
+        _perturb(layer, seed)
+    g = torch.Generator().manual_seed(seed + 7)
+    x = torch.randn(B, T, kw["d_model"], generator=g).requires_grad_(True)
+    gy = torch.randn(B, T, kw["d_model"], generator=g)
+    y = layer(x)
+    (y * gy).sum().backward()
+    out = {f"sd.{k}": _np(v) for k, v in layer.state_dict().items()}
+    out.update({f"grad.{k}": _np(p.grad) for k, p in layer.named_parameters()})
+    out.update(x=_np(x), gy=_np(gy), y=_np(y), grad_x=_np(x.grad), T=np.int64(T), seed=np.int64(seed))
+    for k, v in kw.items():
+        out[f"cfg.{k}"] = np.asarray(v)
+    np.savez_compressed(HERE / f"grad_{name}.npz", **out)
+
+
 def big_layer_case(M, name, seed, B, T):
     """BASELINE layer dims; weights are not stored (regenerated from ``seed``), only checksums."""
     kw = dict(d_model=768, d_state=128, expand=2, headdim=64, mimo_rank=2, chunk_size=64)
@@ -97,6 +118,34 @@ def ssd_case(M, name, seed, B, T, H, P, R, N, CS, beta=True, with_h_init=True):
         d["h_init"] = h_init
     d = {k: _np(v) for k, v in d.items()}
     np.savez_compressed(HERE / f"ssd_{name}.npz", CS=np.int64(CS), beta=np.int64(beta), **d)
+
+
+def ssd_bwd_case(M, name, seed, B, T, H, P, R, N, CS, beta=True, with_h_init=True, with_final=True):
+    """Gradients of the reference's chunked_ssd through torch autograd (CPU fp32) for the loss
+    <y, gy> + <h_final, ghf>: every input that takes a gradient, seeded inputs as ssd_case."""
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    ins = dict(x_g=r(B, T, H, P, R), x_b=r(B, T, H, P, R), B_g=r(B, T, H, N, R), B_b=r(B, T, H, N, R),
+               C=r(B, T, H, N, R), dt=torch.rand(B, T, H, generator=g) * 0.1 + 0.01,
+               A=-torch.exp(r(H).clamp(-4, -1)), D=r(H), x_raw=r(B, T, H, P, R))
+    ins["h_init"] = r(B, H, P, N) if with_h_init else None
+    if not beta:
+        ins["x_b"] = ins["B_b"] = None
+    gy = r(B, T, H, P, R)
+    ghf = r(B, H, P, N) if with_final else None
+    leaves = {k: v.clone().requires_grad_(True) for k, v in ins.items() if v is not None}
+    args = {k: leaves.get(k) for k in ins}
+    out = M.chunked_ssd(args["x_g"], args["x_b"], args["B_g"], args["B_b"], args["C"], args["dt"], args["A"],
+                        args["D"], args["x_raw"], CS, h_init=args["h_init"], return_final_state=with_final)
+    loss = (out.y * gy).sum() + ((out.h_final * ghf).sum() if with_final else 0.0)
+    names = list(leaves)
+    grads = torch.autograd.grad(loss, [leaves[k] for k in names])
+    d = {k: _np(v) for k, v in ins.items() if v is not None}
+    d.update({f"d_{k}": _np(gr) for k, gr in zip(names, grads)})
+    d.update(gy=_np(gy), y=_np(out.y))
+    if with_final:
+        d.update(ghf=_np(ghf), h_final=_np(out.h_final))
+    np.savez_compressed(HERE / f"ssdbwd_{name}.npz", CS=np.int64(CS), beta=np.int64(beta), **d)
 
 
 def scan_case(M, name, seed, B, K, H, PN, with_h_init):
@@ -144,6 +193,20 @@ def lm_case(M, name, seed, B, T, n_new, **kw):
     np.savez_compressed(HERE / f"lm_{name}.npz", **out)
 
 
+def grad_groups(M):
+    small = dict(d_model=64, d_state=16, headdim=16, mimo_rank=2, expand=2, chunk_size=8)
+    layer_grad_case(M, "default", 61, 2, 21, True, **small)
+    layer_grad_case(M, "rank1_ngroups2", 62, 1, 17, True, **{**small, "mimo_rank": 1, "ngroups": 2})
+    layer_grad_case(M, "alloff", 63, 2, 12, True, **{**small, "use_trapezoidal": False, "use_complex_ssm": False})
+
+
+def ssd_bwd_groups(M):
+    ssd_bwd_case(M, "trap", 51, 2, 19, 2, 8, 2, 16, 8)
+    ssd_bwd_case(M, "euler", 52, 1, 16, 3, 4, 1, 8, 4, beta=False, with_h_init=False, with_final=False)
+    ssd_bwd_case(M, "rank4", 53, 1, 13, 2, 16, 4, 16, 8, with_final=False)
+    ssd_bwd_case(M, "single", 54, 2, 1, 1, 4, 2, 8, 8)
+
+
 def scan_bwd_groups(M):
     scan_bwd_case(M, "hinit", 33, 2, 5, 3, 16, True)
     scan_bwd_case(M, "zero", 34, 1, 9, 2, 24, False)
@@ -162,6 +225,12 @@ def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     if args.only == "scanbwd":
         scan_bwd_groups(M)
+        return
+    if args.only == "ssdbwd":
+        ssd_bwd_groups(M)
+        return
+    if args.only == "grad":
+        grad_groups(M)
         return
     small = dict(d_model=64, d_state=16, headdim=16, mimo_rank=2, expand=2, chunk_size=8)
     layer_case(M, "default", 11, 2, 24, False, **small)
@@ -183,6 +252,8 @@ def main():
     scan_case(M, "hinit", 31, 2, 4, 3, 8, True)
     scan_case(M, "zero", 32, 2, 7, 2, 24, False)
     scan_bwd_groups(M)
+    ssd_bwd_groups(M)
+    grad_groups(M)
     lm_case(M, "small", 41, 2, 12, 6, vocab_size=256, d_model=64, n_layers=2, d_state=16, headdim=16,
             mimo_rank=2, chunk_size=8, use_mlp=True, residual_scale="depth")
     total = sum(p.stat().st_size for p in HERE.glob("*.npz"))

@@ -13,6 +13,7 @@ LAYER_CASES = ["default", "perturbed", "rank1", "rank4", "euler", "real", "allof
 SSD_CASES = ["trap", "euler", "rank4"]
 SCAN_CASES = ["hinit", "zero"]
 SCAN_BWD_CASES = ["hinit", "zero", "k1", "odd"]
+SSD_BWD_CASES = ["trap", "euler", "rank4", "single"]
 
 
 def load(name):

@@ -8,7 +8,8 @@ import numpy as np
 import pytest
 
 import oracle
-from goldens import LAYER_CASES, SCAN_BWD_CASES, SCAN_CASES, SSD_CASES, layer_cfg, load, max_rel, state_dict
+from goldens import (LAYER_CASES, SCAN_BWD_CASES, SCAN_CASES, SSD_BWD_CASES, SSD_CASES, layer_cfg, load, max_rel,
+                     state_dict)
 
 
 @pytest.mark.parametrize("case", LAYER_CASES)
@@ -51,6 +52,21 @@ def test_ssd_scan(case):
     d = load(f"scan_{case}")
     hs = oracle.ssd_scan(d["decay"].astype(np.float64), d["h_chunk"].astype(np.float64), d.get("h_init"))
     assert max_rel(hs, d["h_states"]) < 1e-6
+
+
+@pytest.mark.parametrize("case", SSD_BWD_CASES)
+def test_chunked_ssd_backward(case):
+    """The oracle's chunked_ssd gradients == the reference's autograd gradients (fp32 CPU)."""
+    d = load(f"ssdbwd_{case}")
+    beta = bool(d["beta"])
+    g = oracle.chunked_ssd_backward(d["x_g"], d["x_b"] if beta else None, d["B_g"], d["B_b"] if beta else None,
+                                    d["C"], d["dt"], d["A"], d["D"], d["x_raw"], d["gy"], d.get("h_init"),
+                                    d.get("ghf"))
+    for k, v in g.items():
+        if v is None:
+            assert f"d_{k}" not in d
+        else:
+            assert max_rel(v, d[f"d_{k}"]) < 1e-5, k
 
 
 @pytest.mark.parametrize("case", SCAN_BWD_CASES)
