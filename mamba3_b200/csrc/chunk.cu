@@ -7,9 +7,12 @@
 //   last_bx_kernel           prefill's prev_BX (mamba3/mamba3.py:248-250)
 // The reference computation these replace is mamba3/mamba3.py:198-256 with
 // mamba3/ssd.py:118-244; the algebra is written out in chunk.cuh.
+#include <map>
 #include <mutex>
 #include <set>
+#include <tuple>
 #include <utility>
+#include <vector>
 
 #include "chunk.cuh"
 
@@ -454,8 +457,9 @@ __global__ void __launch_bounds__(kCT) last_bx_kernel(FwdParams a, const float* 
 namespace {
 
 struct WsLayout {
-  size_t rms, asum, omega, sstate, hstate, decay, coef0, angle_last, total;
+  size_t rms, asum, omega, sstate, hstate, decay, coef0, angle_last, ho_h, ho_ang, ho_flag, total;
   bool fused;
+  int kp;  // fused path: chunks per sequence part (K: sequences are not cut)
 };
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -465,7 +469,66 @@ bool use_fused(const m3b_layer_fwd_args* a) {
   return fused_supported(a->prm);
 }
 
-WsLayout ws_layout(const m3b_layer_fwd_args* a, int L) {
+// Chunks per part when the fused kernel cuts sequences into parts: equal-length sequences fill
+// ceil(nseq / nsm) rounds of the persistent grid, so e.g. 384 sequences on 148 SMs leave the
+// last round 40 % occupied; parts of K / np chunks make nseq * np jobs and fill the rounds
+// better; a job start costs about a chunk's time, a part's state hand-off a quarter more.  A part cannot start
+// before the previous part of its sequence has finished, so the time of a cut is modelled by
+// walking the static job order (job j on CTA j % grid, after the CTA's previous job and after
+// job j - nseq); with fewer sequences than SMs the parts of a sequence would only wait on one
+// another, and the model keeps whole sequences.  The number of parts np divides K; cutting must
+// save at least 1 % of the modelled time.
+int choose_kp_uncached(int64_t nseq, int K, int nsm) {
+  constexpr double kSwitch = 1.0;    // start of any job (new sequence or part), in chunk times
+  constexpr double kHandoff = 0.25;  // extra for a part that loads its predecessor's state
+  std::vector<double> cta_free, fin;
+  auto cost = [&](int np) {
+    const int64_t jobs = nseq * np;
+    const int64_t grid = jobs < nsm ? jobs : nsm;
+    const double len = (double)(K / np) + kSwitch + (np > 1 ? kHandoff : 0.0);
+    cta_free.assign((size_t)grid, 0.0);
+    fin.assign((size_t)jobs, 0.0);
+    double span = 0.0;
+    for (int64_t j = 0; j < jobs; ++j) {
+      double start = cta_free[(size_t)(j % grid)];
+      if (j >= nseq && fin[(size_t)(j - nseq)] > start) start = fin[(size_t)(j - nseq)];
+      fin[(size_t)j] = start + len;
+      cta_free[(size_t)(j % grid)] = fin[(size_t)j];
+      if (fin[(size_t)j] > span) span = fin[(size_t)j];
+    }
+    return span;
+  };
+  const double base = cost(1);
+  int best = 1;
+  double best_cost = base;
+  for (int np = 2; np <= 64 && np <= K; ++np) {
+    if (K % np != 0) continue;
+    const double c = cost(np);
+    if (c < best_cost) {
+      best_cost = c;
+      best = np;
+    }
+  }
+  return best_cost <= 0.99 * base ? K / best : K;
+}
+
+// choose_kp, remembered per (sequences, chunks, SMs): the model walks every job once
+int choose_kp(int64_t nseq, int K, int nsm) {
+  static std::mutex mu;
+  static std::map<std::tuple<int64_t, int, int>, int> memo;
+  const auto key = std::make_tuple(nseq, K, nsm);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    const auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+  }
+  const int kp = choose_kp_uncached(nseq, K, nsm);
+  std::lock_guard<std::mutex> lk(mu);
+  memo[key] = kp;
+  return kp;
+}
+
+WsLayout ws_layout(const m3b_layer_fwd_args* a, int L, bool allow_parts = true) {
   const m3b_layer_params& p = a->prm;
   const int64_t B = a->batch, T = a->seqlen, K = (T + L - 1) / L;
   const size_t ssz = (a->act_dtype == M3B_BF16) ? 2 : 4;
@@ -473,9 +536,17 @@ WsLayout ws_layout(const m3b_layer_fwd_args* a, int L) {
   WsLayout w{};
   size_t o = 0;
   w.fused = use_fused(a);
+  w.kp = (int)K;
   w.rms = o; o += up256((size_t)B * T * p.G * 2 * 4);
   w.angle_last = o; o += up256((size_t)B * p.H * (p.N / 2) * 4);
   if (w.fused) {
+    if (allow_parts) w.kp = choose_kp(B * p.H, (int)K, num_sms());
+    if (w.kp < K) {
+      const size_t nseq = (size_t)B * p.H;
+      w.ho_h = o; o += up256(nseq * p.P * p.N * 4);
+      w.ho_ang = o; o += up256(nseq * 64 * 8);
+      w.ho_flag = o; o += up256(nseq * 2 * 4);
+    }
     w.total = o;
     return w;
   }
@@ -600,6 +671,12 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
     f.angle_last = angle_last;
     f.err = a->err;
     f.state_only = a->state_only != 0;
+    f.KP = w.kp;
+    if (w.kp < fp.K) {
+      f.ho_h = reinterpret_cast<float*>(ws + w.ho_h);
+      f.ho_ang = reinterpret_cast<double*>(ws + w.ho_ang);
+      f.ho_flag = reinterpret_cast<int*>(ws + w.ho_flag);
+    }
     if ((rc = launch_fused(f, st, a->act_dtype == M3B_BF16)) != M3B_OK) return rc;
     if (a->angle_final) {
       const cudaError_t e = cudaMemcpyAsync(a->angle_final, angle_last, (size_t)fp.B * p.H * (p.N / 2) * 4,
@@ -669,12 +746,18 @@ size_t layer_fwd_workspace(const m3b_layer_fwd_args* a) {
   return ws_layout(a, 128 / rp_of(a->prm.R)).total;
 }
 
+size_t layer_fwd_workspace_min(const m3b_layer_fwd_args* a) {
+  if (validate(a) != M3B_OK) return 0;
+  return ws_layout(a, 128 / rp_of(a->prm.R), false).total;
+}
+
 int layer_fwd(const m3b_layer_fwd_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
   int rc = validate(a);
   if (rc != M3B_OK) return rc;
   if (a->batch <= 0 || a->seqlen <= 0) return M3B_OK;
   const int L = 128 / rp_of(a->prm.R);
-  const WsLayout w = ws_layout(a, L);
+  WsLayout w = ws_layout(a, L);
+  if (ws_bytes < w.total) w = ws_layout(a, L, false);  // a smaller workspace: whole sequences per CTA
   if (!ws || ws_bytes < w.total) return fail(M3B_ERR_WORKSPACE, "layer_fwd: need %zu workspace bytes", w.total);
   if ((a->seqlen + L - 1) / L > 65535) return fail(M3B_ERR_UNSUPPORTED, "layer_fwd: too many chunks");
   uint8_t* base = static_cast<uint8_t*>(ws);

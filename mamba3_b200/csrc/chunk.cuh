@@ -70,6 +70,14 @@ struct FusedParams {
   float* angle_last;  // (B,H,N/2): angle after the last token (always written)
   int* err;
   bool state_only;    // y not needed: the kernel may skip the outputs (TMA path)
+  // Sequences cut into parts of KP chunks (KP == K: whole sequences).  Part q > 0 of sequence s
+  // starts from the state part q - 1 hands over: H in ho_h[s] (P x N fp32, h_final layout), the
+  // angles in ho_ang[s] (64 doubles); ho_flag[2 s] / [2 s + 1] count the parts whose angles / H
+  // are written (zeroed before the launch).
+  int KP;
+  float* ho_h;
+  double* ho_ang;
+  int* ho_flag;
 };
 
 // Fused sequential path (fused.cu): supported shapes and launcher.

@@ -149,6 +149,26 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Flags that one CTA sets for another: release store / acquire load at GPU scope.
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until *flag >= target, giving up after kWaitLimitNs (returns false then).
+__device__ __forceinline__ bool flag_wait_geq(const int* flag, int target) {
+  if (ld_acquire_gpu(flag) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(500);
+    if (ld_acquire_gpu(flag) >= target) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // shared memory / mbarrier
 // ---------------------------------------------------------------------------
@@ -387,6 +407,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+
+// 8 columns of this warp's 32 lanes (no wait: callers end a series of stores with tmem_wait_st)
+__device__ __forceinline__ void tmem_st8_nowait(uint32_t taddr, const float (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");

@@ -74,33 +74,41 @@ struct FPlan {
 enum { BAR_FULL0 = 0, BAR_FULL1 = 1, BAR_EMPTY0 = 2, BAR_EMPTY1 = 3, BAR_SDONE0 = 4, BAR_SDONE1 = 5,
        BAR_HDONE = 6, BAR_YDONE = 7, BAR_STAGE0 = 8, BAR_STAGE1 = 9 };
 
-// Position of one chunk: sequence index, batch row, head, chunk within the sequence, group.
+// Position of one chunk: job, part of the sequence, sequence index, batch row, head, group,
+// chunk within the sequence (k) and within the part (kk).
 struct ChunkPos {
-  int seq, b, h, k, grp;
+  int job, part, seq, b, h, grp, k, kk;
 };
 
-// CTA c walks sequences (batch, head) = c, c + stride, c + 2 stride, ... of nseq_total,
-// each chunk by chunk; g numbers the chunks of all its sequences.  The roles step a ChunkPos
-// cursor along g (a division only when a new sequence starts).
+// Every sequence (batch, head) is cut into nparts parts of KP chunks (K = nparts KP); job j is
+// part j / nseq_total of sequence j % nseq_total, so all first parts come before all second
+// parts.  CTA c walks jobs c, c + stride, c + 2 stride, ... chunk by chunk; g numbers the chunks
+// of all its jobs.  The predecessor of job j (part - 1 of the same sequence) is job j - nseq_total,
+// which a CTA took in an earlier round.  The roles step a ChunkPos cursor along g (divisions
+// only when a new job starts).
 struct Sched {
-  int K, H, nseq_total, stride, heads_per_group;
-  __device__ int count() const { return (nseq_total - (int)blockIdx.x + stride - 1) / stride; }
-  __device__ void set_seq(ChunkPos& c, int seq) const {
-    c.seq = seq;
-    c.b = seq / H;
-    c.h = seq - c.b * H;
+  int K, H, nseq_total, stride, heads_per_group, KP, nparts;
+  __device__ int count() const { return (nseq_total * nparts - (int)blockIdx.x + stride - 1) / stride; }
+  __device__ void set_job(ChunkPos& c, int job) const {
+    c.job = job;
+    c.part = job / nseq_total;
+    c.seq = job - c.part * nseq_total;
+    c.b = c.seq / H;
+    c.h = c.seq - c.b * H;
     c.grp = c.h / heads_per_group;
+    c.k = c.part * KP;
+    c.kk = 0;
   }
   __device__ ChunkPos first() const {
     ChunkPos c;
-    set_seq(c, (int)blockIdx.x);
-    c.k = 0;
+    set_job(c, (int)blockIdx.x);
     return c;
   }
   __device__ void advance(ChunkPos& c) const {
-    if (++c.k == K) {
-      c.k = 0;
-      set_seq(c, c.seq + stride);
+    if (++c.kk == KP) {
+      set_job(c, c.job + stride);
+    } else {
+      ++c.k;
     }
   }
   __device__ ChunkPos ahead(ChunkPos c, int n) const {
@@ -250,7 +258,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   volatile int* epi_abort = reinterpret_cast<volatile int*>(sm + PL::misc + 8);
   double* omega = reinterpret_cast<double*>(sm + PL::omega);
   float* segt = reinterpret_cast<float*>(sm + PL::segt);
-  const int G = sc.count() * sc.K;
+  const int G = sc.count() * sc.KP;
 
   if (warp == 0) {
     tmem_alloc(tslot, 512);
@@ -384,7 +392,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const ChunkPos pnext = sc.ahead(pos, 1);
       const int64_t t0 = (int64_t)k * L;
       const TA* rowbase = proj + (int64_t)b * a.T * a.proj_stride;
-      if (k == 0) {  // per-sequence parameters (every producer passed the last barrier of chunk g-1)
+      if (pos.kk == 0) {  // a new job: its sequence's parameters (every producer passed chunk g-1's last barrier)
         const int pd = p.param_dtype;
         for (int e = ptid; e < NR; e += kProdThreads) {
           nwB[e] = ldf(p.B_norm_w, e, pd);
@@ -392,8 +400,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           nbB[e] = ldf(p.B_bias, (int64_t)grp * NR + e, pd);
           nbC[e] = ldf(p.C_bias, (int64_t)grp * NR + e, pd);
         }
-        if (ptid < nh2)
-          omega[(g & 1) * 64 + ptid] = a.angle_init ? (double)a.angle_init[((int64_t)b * H + h) * nh2 + ptid] : 0.0;
+        if (pos.part == 0) {
+          if (ptid < nh2)
+            omega[(g & 1) * 64 + ptid] = a.angle_init ? (double)a.angle_init[((int64_t)b * H + h) * nh2 + ptid] : 0.0;
+        } else {
+          // the angles after the previous part of this sequence (another CTA, an earlier round)
+          if (ptid == 0 && !*abort_flag && !flag_wait_geq(a.ho_flag + 2 * pos.seq, pos.part)) {
+            *abort_flag = 1;
+            record_error(a.err, M3B_ERR_TIMEOUT);
+          }
+          __syncwarp();
+          named_bar(kBarProd, kProdThreads);
+          if (*abort_flag) break;
+          if (ptid < nh2) omega[(g & 1) * 64 + ptid] = __ldcg(a.ho_ang + (int64_t)pos.seq * 64 + ptid);
+        }
         if (ptid == 0) {
           float* spw = reinterpret_cast<float*>(sm + PL::seqp);
           spw[0] = -expf(ldf(p.A_log, h, pd));
@@ -690,7 +710,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           // angle after this chunk = before - (off + own segment sum); the next chunk reads the other slot
           const double nom = p.complex_ssm ? om - (double)(off + segsum) : om;
           omega[((g + 1) & 1) * 64 + pi] = nom;
-          if (k == sc.K - 1) a.angle_last[((int64_t)b * H + h) * nh2 + pi] = (float)nom;
+          if (k == sc.K - 1) {
+            a.angle_last[((int64_t)b * H + h) * nh2 + pi] = (float)nom;
+          } else if (pos.kk == sc.KP - 1) {  // end of a part: hand the angles to the next part
+            a.ho_ang[(int64_t)pos.seq * 64 + pi] = nom;
+            __threadfence();
+          }
         }
       }
       if (N < kNS) {  // zero columns [N, 128) of the B tile (P of an earlier chunk lives there)
@@ -702,9 +727,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if (ptid == 0) M3B_TL(g, 3);
       // the next chunk's token scalars, while the other warps finish their rotations (its raw
       // values were requested at the start of this chunk; same sequence, so same dt_bias)
-      if (ptid <= L && g + 1 < G && pnext.k != 0) tok_scalars(nxt);
+      if (ptid <= L && g + 1 < G && pnext.kk != 0) tok_scalars(nxt);
       fence_async_smem();
       named_bar(kBarProd, kProdThreads);  // B^, C^ tiles and the token scalars (wst, gbw) complete
+      if (ptid == 0 && pos.kk == sc.KP - 1 && pos.part + 1 < sc.nparts)
+        st_release_gpu(a.ho_flag + 2 * pos.seq, pos.part + 1);  // this part's angles are written
       if (ptid == 0) {
         mbar_arrive(&bars[BAR_FULL0 + s]);
         if constexpr (!SO) {
@@ -794,37 +821,44 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                   idH, 1u);
       umma_commit(&bars[BAR_HDONE]);
     };
-    // H'_0 of the sequence starting at chunk gs -> bf16 tile row n = m, and H = d * H'_0 in TMEM
+    // H'_0 of the job starting at chunk gs -> bf16 tile row n = m, and H = d * H'_0 in TMEM.  A first
+    // part starts from h_init (+ (1-lam_0) dt_0 prev_bx_init); a later part from the state the
+    // previous part of its sequence handed over (the beta term of its first token is in it)
     auto state_init = [&](const ChunkPos& c, int gs) -> bool {
       const int b = c.b, h = c.h;
       const int s2 = gs & 1;
+      if (c.part > 0 && lead && !*abort_flag && !flag_wait_geq(a.ho_flag + 2 * c.seq + 1, c.part)) {
+        *abort_flag = 1;
+        record_error(a.err, M3B_ERR_TIMEOUT);
+      }
       if (!role_wait(&bars[BAR_FULL0 + s2], (gs >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))
         return false;
       const float* scal = reinterpret_cast<const float*>(sm + PL::scal + s2 * PL::scalStride);
       const float d = exp2f(scal[L - 1]);
       const float c0 = scal[3 * NA];  // (1-lam_0) dt_0
-      const int64_t base = ((int64_t)b * H + h) * (int64_t)P * N;
-      float hv[32];
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int pp = 32 * ch + e;
-        float v = 0.f;
-        if (m < N && pp < P) {
-          if (a.h_init) v = a.h_init[base + (int64_t)pp * N + m];
-          if (a.prev_bx_init) v = fmaf(c0, a.prev_bx_init[base + (int64_t)pp * N + m], v);
-        }
-        hv[e] = v;
-      }
+      const int64_t o = ((int64_t)b * H + h) * (int64_t)P * N + (int64_t)(32 * ch) * N + m;
+      const float* hsrc = m < N ? (c.part > 0 ? a.ho_h : a.h_init) : nullptr;
+      const float* bxsrc = m < N && c.part == 0 ? a.prev_bx_init : nullptr;
+      // eight columns at a time: their loads are in flight together, and few registers are live
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
         float v8[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v8[e] = hv[8 * c8 + e];
-        st_pack_chunk(tileH, m, 4 * ch + c8, v8);
-      }
+        for (int e = 0; e < 8; ++e) {
+          const bool okp = 32 * ch + 8 * c8 + e < P;
+          v8[e] = hsrc && okp ? __ldcg(hsrc + o + (int64_t)(8 * c8 + e) * N) : 0.f;
+        }
+        if (bxsrc) {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) hv[e] *= d;
-      tmem_st32(trow + kColH + 32 * ch, hv);
+          for (int e = 0; e < 8; ++e)
+            if (32 * ch + 8 * c8 + e < P) v8[e] = fmaf(c0, bxsrc[o + (int64_t)(8 * c8 + e) * N], v8[e]);
+        }
+        st_pack_chunk(tileH, m, 4 * ch + c8, v8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v8[e] *= d;
+        tmem_st8_nowait(trow + kColH + 32 * ch + 8 * c8, v8);
+      }
+      tmem_wait_st();
       // this sequence's gate parameters (the previous sequence's last output is complete)
       const int pd = p.param_dtype;
       for (int e = tid; e < kPP * RP; e += kEpiThreads) {
@@ -837,17 +871,27 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       named_bar(kBarEpi, kEpiThreads);  // mimo_x is read by the X / W tiles below
       return true;
     };
+    // the state after the last chunk of job c: h_final after a sequence's last part, otherwise
+    // handed to the sequence's next part (written, then flagged)
     auto write_h_final = [&](const ChunkPos& c) {
-      if (!a.h_final) return;
-      const int64_t base = ((int64_t)c.b * H + c.h) * (int64_t)P * N;
-      float v[32];
-      tmem_ld32(trow + kColH + 32 * ch, v);
-      if (m < N) {
+      const bool handoff = c.part + 1 < sc.nparts;
+      float* dst = handoff ? a.ho_h : a.h_final;
+      if (dst) {
+        const int64_t base = ((int64_t)c.b * H + c.h) * (int64_t)P * N;
+        float v[32];
+        tmem_ld32(trow + kColH + 32 * ch, v);
+        if (m < N) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int pp = 32 * ch + e;
-          if (pp < P) a.h_final[base + (int64_t)pp * N + m] = v[e];
+          for (int e = 0; e < 32; ++e) {
+            const int pp = 32 * ch + e;
+            if (pp < P) dst[base + (int64_t)pp * N + m] = v[e];
+          }
         }
+      }
+      if (handoff) {
+        __threadfence();
+        named_bar(kBarEpi, kEpiThreads);
+        if (lead) st_release_gpu(a.ho_flag + 2 * c.seq + 1, c.part + 1);
       }
     };
     Raw8<TA> xn[XU];  // x of the next chunk
@@ -1034,7 +1078,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                 acc[i + 1] = o.y;
               }
             }
-#pragma unroll
             // sum over the RP lanes (t, r) of a token, reduce-scatter style: each halving step
             // keeps the half picked by one bit of r, so lane r ends with columns [r W, r W + W)
             constexpr int W = 16 / RP;  // outputs written by each of the RP lanes of a token
@@ -1091,7 +1134,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
       // ---- state for chunk g+1: H'_{g+1} -> bf16 tile, H *= d_{g+1}; then Yi_{g+1}, H += ...
       if (g + 1 < G) {
-        if (pnext.k == 0) {
+        if (pnext.kk == 0) {  // a new job starts with chunk g+1
           write_h_final(pos);
           if (!(ok = state_init(pnext, g + 1))) break;
         } else {
@@ -1200,7 +1243,6 @@ int launch_fused_t(const FusedParams& fp, cudaStream_t st, const CUtensorMap& tm
   using PL = FPlan<RP>;
   const int nseq_total = (int)(fp.B * fp.prm.H);
   const int nsm = num_sms();
-  const int grid = nseq_total < nsm ? nseq_total : nsm;
   const void* fn = (const void*)ssd_fused_kernel<TA, R, TMA, SO>;
   int rc;
   if ((rc = ensure_smem_f(fn, PL::bytes)) != M3B_OK) return rc;
@@ -1208,7 +1250,16 @@ int launch_fused_t(const FusedParams& fp, cudaStream_t st, const CUtensorMap& tm
   if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess && fa.maxThreadsPerBlock < kFusedThreads)
     return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: %d registers/thread allow only %d threads per block (need %d)",
                 fa.numRegs, fa.maxThreadsPerBlock, kFusedThreads);
-  const Sched sc{fp.K, fp.prm.H, nseq_total, grid, fp.prm.H / fp.prm.G};
+  const int KP = fp.KP > 0 && fp.K % fp.KP == 0 ? fp.KP : fp.K;
+  const int nparts = fp.K / KP;
+  const int njobs = nseq_total * nparts;
+  const int grid = njobs < nsm ? njobs : nsm;
+  if (nparts > 1) {
+    if (!fp.ho_h || !fp.ho_ang || !fp.ho_flag) return fail(M3B_ERR_INVALID_ARG, "ssd_fused: hand-off buffers missing");
+    const cudaError_t e = cudaMemsetAsync(fp.ho_flag, 0, sizeof(int) * 2 * (size_t)nseq_total, st);
+    if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "ssd_fused: %s", cudaGetErrorString(e));
+  }
+  const Sched sc{fp.K, fp.prm.H, nseq_total, grid, fp.prm.H / fp.prm.G, KP, nparts};
   ssd_fused_kernel<TA, R, TMA, SO><<<grid, kFusedThreads, PL::bytes, st>>>(fp, sc, tm_bc, tm_th);
   return check_launch("ssd_fused");
 }

@@ -54,7 +54,7 @@ int scratch_address(void** out) {
 
 extern "C" int m3b_layer_fwd_noalloc(const m3b_layer_fwd_args* a, void* stream) {
   if (!a) return m3b::fail(M3B_ERR_INVALID_ARG, "layer_fwd_noalloc: null args");
-  const size_t need = m3b::layer_fwd_workspace(a);
+  const size_t need = m3b::layer_fwd_workspace_min(a);
   if (need == 0) return m3b::layer_fwd(a, nullptr, 0, static_cast<cudaStream_t>(stream));  // reports why
   if (need > kNoallocScratchBytes)
     return m3b::fail(M3B_ERR_WORKSPACE,

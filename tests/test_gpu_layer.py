@@ -219,3 +219,30 @@ def test_ragged_lengths_n128(T, R):
     assert max_rel(to_np(y), oy) < BF16_TOL
     assert max_rel(to_np(st["h"]), ost["h"]) < BF16_TOL
     assert max_rel(to_np(st["prev_BX"]), ost["prev_BX"]) < BF16_TOL
+
+
+@pytest.mark.parametrize("d_model,R,B,T", [(768, 2, 8, 1000), (640, 2, 8, 500), (768, 4, 8, 256), (768, 1, 8, 1024)])
+def test_fused_sequence_parts_equal_chunk_parallel(d_model, R, B, T, layer_algo):
+    """With at least as many (batch, head) sequences as SMs the fused kernel cuts sequences into
+    parts handed from CTA to CTA (state and angles through global memory): its outputs and final
+    states equal the chunk-parallel algorithm's, which never cuts, and the state-only variant
+    ends in the same state."""
+    from mamba3_b200 import KulaMamba, ops, seqpar
+
+    if layer_algo != 1:
+        pytest.skip("runs both algorithms itself")
+    torch.manual_seed(50 + R)
+    m = KulaMamba(d_model=d_model, d_state=128, headdim=64, mimo_rank=R).cuda().to(torch.bfloat16).eval()
+    x = torch.randn(B, T, d_model, generator=torch.Generator().manual_seed(T)).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        y1, st1 = m.prefill(x)
+        so = seqpar.layer_state_only(m, m.in_proj(x))
+        prev = ops.set_layer_algo(2)
+        try:
+            y2, st2 = m.prefill(x)
+        finally:
+            ops.set_layer_algo(prev)
+    assert max_rel(to_np(y1), to_np(y2)) < BF16_TOL
+    for k in ("h", "angle", "prev_BX"):
+        assert max_rel(to_np(st1[k]), to_np(st2[k])) < (1e-4 if k == "angle" else BF16_TOL), k
+        assert max_rel(to_np(so[k]), to_np(st2[k])) < (1e-4 if k == "angle" else BF16_TOL), k
