@@ -265,6 +265,19 @@ def run_scan(dev, world, rank, barrier):
         out[name] = {"ms": ms, "bytes": nbytes, "achieved_gbs": gbs, "frac": gbs / peaks["hbm_gbs"]}
     del hc, gh, hs
     torch.cuda.empty_cache()
+    # chunked_ssd backward (m3b_chunked_ssd_bwd) on config-1 shaped rows: the gradients of one
+    # layer's SSD core for 2 batch rows of 4096 tokens, 24 heads, P 64, N 128, R 2 (trapezoid)
+    Bb, T, Hh, P, N, R = 2, 4096, 24, 64, 128, 2
+    r = lambda *s: torch.randn(*s, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
+    args = (r(Bb, T, Hh, P, R), r(Bb, T, Hh, P, R), r(Bb, T, Hh, N, R), r(Bb, T, Hh, N, R), r(Bb, T, Hh, N, R),
+            torch.rand(Bb, T, Hh, device=dev, generator=g) * 0.1, -torch.rand(Hh, device=dev, generator=g) - 0.1,
+            torch.randn(Hh, device=dev, generator=g), r(Bb, T, Hh, P, R), r(Bb, T, Hh, P, R))
+    ms_s = timed(lambda: _lib.chunked_ssd_bwd(*args), reps=3)
+    # fp32 multiply-adds per (token, head): h and G updates P N (RI + R), dC N R P, dX P RI N, dB N RI P
+    ri = 2 * R
+    flops = 2.0 * P * N * (3 * ri + 2 * R) * Bb * T * Hh
+    out["ssd_bwd"] = {"workload": f"chunked_ssd backward, bf16 ({Bb}, {T}) x {Hh} heads, P {P}, N {N}, R {R}",
+                      "ms": ms_s, "tokens_per_s": Bb * T / (ms_s / 1e3), "fp32_tflops": flops / (ms_s / 1e3) / 1e12}
     return out
 
 

@@ -110,6 +110,76 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Suffix pass shared by the backward kernels: m_t = m_{t+1} + e_t - dt_t fr_t (m_T = mT) from the
+// per-warp partials ew / fw, then ddt_t = fr_t + A m_t and this (b, h)'s shares of dA and dD.
+// suf: >= kBwdThreads floats of shared memory, red: >= kBwdWarps; both free for reuse here.
+template <typename T>
+__device__ void bwd_finish(const BwdParams& a, int64_t bh, int64_t b, int h, float Aval, float mT, float dD_acc,
+                           const float* ew, const float* fw, float* suf, float* red) {
+  const int64_t TT = a.T;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // thread i owns tokens [i*seg, (i+1)*seg); the per-warp partials of e_t, fr_t are visible
+  // (written before the last barrier of the reverse sweep, or the forward sweep's)
+  const int64_t seg = (TT + kBwdThreads - 1) / kBwdThreads;
+  const int64_t t0 = tid * seg, t1 = t0 + seg < TT ? t0 + seg : TT;
+  auto tok = [&](int64_t t, float& e, float& f, float& dtv) {
+    e = 0.f;
+    f = 0.f;
+    for (int w = 0; w < kBwdWarps; ++w) {
+      e += ew[t * kBwdWarps + w];
+      f += fw[t * kBwdWarps + w];
+    }
+    dtv = ldf(a.dt, (b * TT + t) * a.H + h, a.dt_dtype);
+  };
+  float local = 0.f;
+  for (int64_t t = t0; t < t1; ++t) {
+    float e, f, dtv;
+    tok(t, e, f, dtv);
+    local += e - dtv * f;
+  }
+  suf[tid] = local;
+  __syncthreads();
+  if (tid == 0) {  // exclusive suffix sums of the segment sums, in segment order
+    float acc = mT;
+    for (int i = kBwdThreads - 1; i >= 0; --i) {
+      const float v = suf[i];
+      suf[i] = acc;
+      acc += v;
+    }
+  }
+  __syncthreads();
+  float m = suf[tid];
+  float dA_acc = 0.f;
+  for (int64_t t = t1 - 1; t >= t0; --t) {
+    float e, f, dtv;
+    tok(t, e, f, dtv);
+    m += e - dtv * f;
+    const int64_t row = (b * TT + t) * a.H + h;
+    const float g = f + Aval * m;
+    if (a.dt_dtype == M3B_F32) static_cast<float*>(a.ddt)[row] = g;
+    else if (a.dt_dtype == M3B_BF16) static_cast<__nv_bfloat16*>(a.ddt)[row] = __float2bfloat16_rn(g);
+    else static_cast<__half*>(a.ddt)[row] = __float2half_rn(g);
+    dA_acc = fmaf(dtv, m, dA_acc);
+  }
+  __syncthreads();
+  dA_acc = warp_sum(dA_acc);
+  dD_acc = warp_sum(dD_acc);
+  if (lane == 0) {
+    red[warp] = dA_acc;
+    suf[warp] = dD_acc;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float sa = 0.f, sd = 0.f;
+    for (int w = 0; w < kBwdWarps; ++w) {
+      sa += red[w];
+      sd += suf[w];
+    }
+    a.dA_bh[bh] = sa;
+    a.dD_bh[bh] = sd;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kBwdThreads) ssd_bwd_kernel(BwdParams a) {
   extern __shared__ float4 smem4[];
@@ -249,68 +319,344 @@ __global__ void __launch_bounds__(kBwdThreads) ssd_bwd_kernel(BwdParams a) {
       a.dh_init[state_base + e] = a_next * S[p * NS + n];
     }
 
-  // ---------------- suffix sum: m_t = m_{t+1} + e_t - dt_t fr_t; ddt, dA ----------------
-  // thread i owns tokens [i*seg, (i+1)*seg); the per-warp partials of e_t, fr_t are visible
-  // (written before the last barrier of the reverse sweep, or the forward sweep's)
-  const int64_t seg = (TT + kBwdThreads - 1) / kBwdThreads;
-  const int64_t t0 = tid * seg, t1 = t0 + seg < TT ? t0 + seg : TT;
-  auto tok = [&](int64_t t, float& e, float& f, float& dtv) {
-    e = 0.f;
-    f = 0.f;
-    for (int w = 0; w < kBwdWarps; ++w) {
-      e += ew[t * kBwdWarps + w];
-      f += fw[t * kBwdWarps + w];
+  bwd_finish<T>(a, bh, b, h, Aval, mT, dD_acc, ew, fw, slots, red);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Register-tiled variant (P <= 64, N <= 128, R <= 4): the same two sweeps with the state held
+// in registers.  Thread (pb, nb) owns rows p = 4 pb + i (i < 4) and columns n = 8 nb + k
+// (k < 8) of h / G; lanes carry nbl = lane & 7 and pbl = lane >> 3, warps nbh = warp & 1 and
+// pbh = warp >> 1 (nb = nbl + 8 nbh, pb = pbl + 4 pbh).  Per token the sums over n (dX) and
+// over p (dB, dC) are reduce-scattered across the lanes of a warp with shuffles and finished
+// across warps in shared memory, one barrier per token.  Token operands are fetched into
+// registers one token ahead and stored into a three-deep ring of shared-memory slots.
+constexpr int kTileItems = 10;  // operand words one thread fetches per token (<= 2560 / 256)
+
+template <int R, int RI>
+struct TPlan {
+  static constexpr int JB = RI > 4 ? 4 : RI;  // j block of one reduction pass
+  static constexpr int NJ = RI / JB;
+  static constexpr int VX = 4 * JB < 8 ? 8 : 4 * JB;  // dX partials per thread and pass (padded)
+  static constexpr int VE = 8 * JB;                    // dB partials per thread and pass
+  static constexpr int VC = 8 * R;                     // dC partials per thread
+  // one slot: Xt [64][RI], Bt^T [RI][128], C^T [R][128], dy [64][R], x_raw [64][R], dt, a
+  static constexpr int sx = 0, sbt = sx + 64 * RI, sct = sbt + RI * 128, sdy = sct + R * 128,
+                       sxr = sdy + 64 * R, ssc = sxr + 64 * R, slot = (ssc + 4 + 31) & ~31;
+  static constexpr int redx = 2 * 16 * NJ * VX;  // [nbh][pb][jb][VX]
+  static constexpr int rede = 4 * 16 * NJ * VE;  // [pbh][nb][jb][VE]
+  static constexpr int redc = 4 * 16 * VC;       // [pbh][nb][VC]
+  static constexpr int red = (redx + rede > redc ? redx + rede : redc);
+  static constexpr int floats = 3 * slot + 2 * red + 32;
+};
+
+// v[0..V) summed over the 2^NB lanes that differ in lane bits lo .. lo+NB-1; afterwards this lane
+// holds the sums of V >> NB consecutive values, v[0 ..) = global values [returned offset ..).
+template <int V, int NB>
+__device__ __forceinline__ int reduce_scatter(float (&v)[V], int lane, int lo) {
+  int off = 0;
+#pragma unroll
+  for (int r = 0; r < NB; ++r) {
+    const int bit = 1 << (lo + r);
+    const bool up = (lane & bit) != 0;
+    const int half = V >> (r + 1);
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = up ? v[i] : v[half + i];
+      const float keep = up ? v[half + i] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
     }
-    dtv = ldf(a.dt, (b * TT + t) * a.H + h, a.dt_dtype);
-  };
-  float local = 0.f;
-  for (int64_t t = t0; t < t1; ++t) {
-    float e, f, dtv;
-    tok(t, e, f, dtv);
-    local += e - dtv * f;
+    off += up ? half : 0;
   }
-  float* suf = slots;  // reuse: kBwdThreads segment sums (slots hold >= 2 * 4 floats per thread)
-  suf[tid] = local;
+  return off;
+}
+
+struct TokFetch {
+  float v[kTileItems];
+  float dt;
+};
+
+// the operands of token `row` (flat (b, t, h) index): Xt, Bt, C, dy and, in the forward sweep,
+// x_raw; as registers (fetch) and then into a slot (store)
+template <typename T, int R, int RI>
+__device__ __forceinline__ void tile_fetch(const BwdParams& a, int64_t row, bool with_xr, TokFetch& f) {
+  const int P = a.P, N = a.N;
+  const int PR = P * R, NR = N * R;
+  const bool beta = RI == 2 * R;
+  const int s0 = PR, s1 = s0 + (beta ? PR : 0), s2 = s1 + NR, s3 = s2 + (beta ? NR : 0), s4 = s3 + NR, s5 = s4 + PR,
+            s6 = s5 + (with_xr ? PR : 0);
+  const int64_t rp = row * PR, rn = row * NR;
+#pragma unroll
+  for (int u = 0; u < kTileItems; ++u) {
+    const int e = threadIdx.x + kBwdThreads * u;
+    float v = 0.f;
+    if (e < s0) v = io<T>::ld(static_cast<const T*>(a.x_g) + rp + e);
+    else if (e < s1) v = io<T>::ld(static_cast<const T*>(a.x_b) + rp + (e - s0));
+    else if (e < s2) v = io<T>::ld(static_cast<const T*>(a.B_g) + rn + (e - s1));
+    else if (e < s3) v = io<T>::ld(static_cast<const T*>(a.B_b) + rn + (e - s2));
+    else if (e < s4) v = io<T>::ld(static_cast<const T*>(a.C) + rn + (e - s3));
+    else if (e < s5) v = io<T>::ld(static_cast<const T*>(a.dy) + rp + (e - s4));
+    else if (e < s6) v = io<T>::ld(static_cast<const T*>(a.x_raw) + rp + (e - s5));
+    f.v[u] = v;
+  }
+  f.dt = threadIdx.x == 0 ? ldf(a.dt, row, a.dt_dtype) : 0.f;
+}
+
+template <int R, int RI>
+__device__ __forceinline__ void tile_store(const BwdParams& a, float* slot, bool with_xr, const TokFetch& f,
+                                           float Aval) {
+  using TP = TPlan<R, RI>;
+  const int P = a.P, N = a.N;
+  const int PR = P * R, NR = N * R;
+  const bool beta = RI == 2 * R;
+  const int s0 = PR, s1 = s0 + (beta ? PR : 0), s2 = s1 + NR, s3 = s2 + (beta ? NR : 0), s4 = s3 + NR, s5 = s4 + PR,
+            s6 = s5 + (with_xr ? PR : 0);
+#pragma unroll
+  for (int u = 0; u < kTileItems; ++u) {
+    const int e = threadIdx.x + kBwdThreads * u;
+    const float v = f.v[u];
+    if (e < s0) slot[TP::sx + (e / R) * RI + e % R] = v;
+    else if (e < s1) slot[TP::sx + ((e - s0) / R) * RI + R + (e - s0) % R] = v;
+    else if (e < s2) slot[TP::sbt + ((e - s1) % R) * 128 + (e - s1) / R] = v;
+    else if (e < s3) slot[TP::sbt + (R + (e - s2) % R) * 128 + (e - s2) / R] = v;
+    else if (e < s4) slot[TP::sct + ((e - s3) % R) * 128 + (e - s3) / R] = v;
+    else if (e < s5) slot[TP::sdy + (e - s4)] = v;
+    else if (e < s6) slot[TP::sxr + (e - s5)] = v;
+  }
+  if (threadIdx.x == 0) {
+    slot[TP::ssc] = f.dt;
+    slot[TP::ssc + 1] = expf(Aval * f.dt);
+  }
+}
+
+template <typename T, int R, int RI>
+__global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams a) {
+  using TP = TPlan<R, RI>;
+  constexpr int JB = TP::JB, NJ = TP::NJ, VX = TP::VX, VE = TP::VE, VC = TP::VC;
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int P = a.P, N = a.N;
+  const int64_t bh = blockIdx.x;
+  const int64_t b = bh / a.H;
+  const int h = (int)(bh - b * a.H);
+  const int64_t TT = a.T;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nbl = lane & 7, pbl = lane >> 3, nbh = warp & 1, pbh = warp >> 1;
+  const int nb = nbl + 8 * nbh, pb = pbl + 4 * pbh;
+  const int p0 = 4 * pb, n0 = 8 * nb;
+  float* slots = sm;                       // 3 x TP::slot
+  float* redbuf = sm + 3 * TP::slot;       // 2 x TP::red
+  float* red = redbuf + 2 * TP::red;       // 32 floats
+  auto slot = [&](int64_t t) { return slots + (int)(t % 3) * TP::slot; };
+  const float Aval = ldf(a.A, h, a.ad_dtype);
+  const float Dval = ldf(a.D, h, a.ad_dtype);
+  const int64_t state_base = bh * (int64_t)P * N;
+  float* ew = a.ew + bh * TT * kBwdWarps;
+  float* fw = a.fw + bh * TT * kBwdWarps;
+  // rows / columns past P / N stay zero in every slot
+  for (int e = tid; e < 3 * TP::slot; e += kBwdThreads) slots[e] = 0.f;
+  auto ok_pk = [&](int i, int k) { return p0 + i < P && n0 + k < N; };
+
+  // ---------------- forward sweep: h_t, dC_t, e_t, dx_raw, dD ----------------
+  float st[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      st[i][k] = a.h_init && ok_pk(i, k) ? a.h_init[state_base + (int64_t)(p0 + i) * N + n0 + k] : 0.f;
+  float dD_acc = 0.f;
+  TokFetch f;
+  __syncthreads();  // slots zeroed
+  if (TT > 0) {
+    tile_fetch<T, R, RI>(a, (b * TT) * a.H + h, true, f);
+    tile_store<R, RI>(a, slot(0), true, f, Aval);
+  }
   __syncthreads();
-  if (tid == 0) {  // exclusive suffix sums of the segment sums, in segment order
-    float acc = mT;
-    for (int i = kBwdThreads - 1; i >= 0; --i) {
-      const float v = suf[i];
-      suf[i] = acc;
-      acc += v;
+  for (int64_t t = 0; t < TT; ++t) {
+    if (t + 1 < TT) tile_fetch<T, R, RI>(a, (b * TT + t + 1) * a.H + h, true, f);
+    const float* sl = slot(t);
+    const float dtv = sl[TP::ssc], av = sl[TP::ssc + 1];
+    // h_t = a_t h_{t-1} + dt_t Xt Bt^T
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) st[i][k] *= av;
+#pragma unroll
+    for (int j = 0; j < RI; ++j) {
+      float bv[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) bv[k] = sl[TP::sbt + j * 128 + n0 + k];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float xv = dtv * sl[TP::sx + (p0 + i) * RI + j];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) st[i][k] = fmaf(xv, bv[k], st[i][k]);
+      }
     }
-  }
-  __syncthreads();
-  float m = suf[tid];
-  float dA_acc = 0.f;
-  for (int64_t t = t1 - 1; t >= t0; --t) {
-    float e, f, dtv;
-    tok(t, e, f, dtv);
-    m += e - dtv * f;
+    // dC partials over this thread's rows: pc[k R + q] = sum_i h[i][k] dy[p0 + i][q]
+    float pc[VC];
+#pragma unroll
+    for (int e = 0; e < VC; ++e) pc[e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        const float g = sl[TP::sdy + (p0 + i) * R + q];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) pc[k * R + q] = fmaf(st[i][k], g, pc[k * R + q]);
+      }
+    }
+    const int offc = reduce_scatter<VC, 2>(pc, lane, 3);
+    float* rc = redbuf + (int)(t & 1) * TP::red + (pbh * 16 + nb) * VC + offc;
+#pragma unroll
+    for (int e = 0; e < VC / 4; ++e) rc[e] = pc[e];
+    if (t + 1 < TT) tile_store<R, RI>(a, slot(t + 1), true, f, Aval);
+    __syncthreads();
+    // dC_t, e_t = <C_t, dC_t>; dx_raw = D dy, dD
     const int64_t row = (b * TT + t) * a.H + h;
-    const float g = f + Aval * m;
-    if (a.dt_dtype == M3B_F32) static_cast<float*>(a.ddt)[row] = g;
-    else if (a.dt_dtype == M3B_BF16) static_cast<__nv_bfloat16*>(a.ddt)[row] = __float2bfloat16_rn(g);
-    else static_cast<__half*>(a.ddt)[row] = __float2half_rn(g);
-    dA_acc = fmaf(dtv, m, dA_acc);
-  }
-  __syncthreads();
-  dA_acc = warp_sum(dA_acc);
-  dD_acc = warp_sum(dD_acc);
-  if (lane == 0) {
-    red[warp] = dA_acc;
-    suf[warp] = dD_acc;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    float sa = 0.f, sd = 0.f;
-    for (int w = 0; w < kBwdWarps; ++w) {
-      sa += red[w];
-      sd += suf[w];
+    const float* rcs = redbuf + (int)(t & 1) * TP::red;
+    float e_acc = 0.f;
+    for (int o = tid; o < N * R; o += kBwdThreads) {
+      const int n = o / R, q = o - n * R;
+      const int idx = (n & 7) * R + q, nbo = n >> 3;
+      const float v = rcs[(0 * 16 + nbo) * VC + idx] + rcs[(1 * 16 + nbo) * VC + idx] +
+                      rcs[(2 * 16 + nbo) * VC + idx] + rcs[(3 * 16 + nbo) * VC + idx];
+      io<T>::st(static_cast<T*>(a.dC) + row * N * R + o, v);
+      e_acc = fmaf(sl[TP::sct + q * 128 + n], v, e_acc);
     }
-    a.dA_bh[bh] = sa;
-    a.dD_bh[bh] = sd;
+    for (int o = tid; o < P * R; o += kBwdThreads) {
+      const float g = sl[TP::sdy + o];
+      dD_acc = fmaf(g, sl[TP::sxr + o], dD_acc);
+      io<T>::st(static_cast<T*>(a.dx_raw) + row * P * R + o, Dval * g);
+    }
+    e_acc = warp_sum(e_acc);
+    if (lane == 0) ew[t * kBwdWarps + warp] = e_acc;
   }
+  // m_T = <dh_final, h_final>; then G_T = dh_final
+  float mT = 0.f;
+  {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float g = a.dh_final && ok_pk(i, k) ? a.dh_final[state_base + (int64_t)(p0 + i) * N + n0 + k] : 0.f;
+        acc = fmaf(g, st[i][k], acc);
+        st[i][k] = g;
+      }
+    acc = warp_sum(acc);
+    __syncthreads();  // the last token's reads of the slots and reductions are done
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    for (int w = 0; w < kBwdWarps; ++w) mT += red[w];
+  }
+
+  // ---------------- reverse sweep: G_t, dXt_t, dBt_t, fr_t, dh_init ----------------
+  if (TT > 0) {
+    tile_fetch<T, R, RI>(a, (b * TT + TT - 1) * a.H + h, false, f);
+    tile_store<R, RI>(a, slot(TT - 1), false, f, Aval);
+  }
+  __syncthreads();
+  float a_next = 1.f;  // a_{t+1} (1 past the last token)
+  for (int64_t t = TT - 1; t >= 0; --t) {
+    if (t > 0) tile_fetch<T, R, RI>(a, (b * TT + t - 1) * a.H + h, false, f);
+    const float* sl = slot(t);
+    const float dtv = sl[TP::ssc], av = sl[TP::ssc + 1];
+    // G_t = a_{t+1} G_{t+1} + dy_t C_t^T
+    {
+      float ct[R][8];
+#pragma unroll
+      for (int q = 0; q < R; ++q)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ct[q][k] = sl[TP::sct + q * 128 + n0 + k];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float g[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) g[q] = sl[TP::sdy + (p0 + i) * R + q];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float u = 0.f;
+#pragma unroll
+          for (int q = 0; q < R; ++q) u = fmaf(g[q], ct[q][k], u);
+          st[i][k] = fmaf(a_next, st[i][k], u);
+        }
+      }
+    }
+    float* rb = redbuf + (int)(t & 1) * TP::red;
+#pragma unroll
+    for (int jb = 0; jb < NJ; ++jb) {
+      // dX partials over this thread's columns: px[i JB + jj] = sum_k G[i][k] Bt[jb JB + jj][n0 + k]
+      float px[VX];
+#pragma unroll
+      for (int e = 0; e < VX; ++e) px[e] = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < JB; ++jj) {
+        float bv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) bv[k] = sl[TP::sbt + (jb * JB + jj) * 128 + n0 + k];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) px[i * JB + jj] = fmaf(st[i][k], bv[k], px[i * JB + jj]);
+      }
+      const int offx = reduce_scatter<VX, 3>(px, lane, 0);
+      float* rx = rb + ((nbh * 16 + pb) * NJ + jb) * VX + offx;
+#pragma unroll
+      for (int e = 0; e < VX / 8; ++e) rx[e] = px[e];
+      // dB partials over this thread's rows: pe[k JB + jj] = sum_i G[i][k] Xt[p0 + i][jb JB + jj]
+      float pe[VE];
+#pragma unroll
+      for (int e = 0; e < VE; ++e) pe[e] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int jj = 0; jj < JB; ++jj) {
+          const float xv = sl[TP::sx + (p0 + i) * RI + jb * JB + jj];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) pe[k * JB + jj] = fmaf(st[i][k], xv, pe[k * JB + jj]);
+        }
+      }
+      const int offe = reduce_scatter<VE, 2>(pe, lane, 3);
+      float* re = rb + TP::redx + ((pbh * 16 + nb) * NJ + jb) * VE + offe;
+#pragma unroll
+      for (int e = 0; e < VE / 4; ++e) re[e] = pe[e];
+    }
+    if (t > 0) tile_store<R, RI>(a, slot(t - 1), false, f, Aval);
+    a_next = av;
+    __syncthreads();
+    // dXt = dt sum over the two column halves; E = sum over the four row quarters, dBt = dt E
+    const int64_t row = (b * TT + t) * a.H + h;
+    for (int o = tid; o < P * RI; o += kBwdThreads) {
+      const int p = o / RI, j = o - p * RI;
+      const int jb = j / JB, idx = (p & 3) * JB + (j - jb * JB), pbo = p >> 2;
+      const float v = dtv * (rb[((0 * 16 + pbo) * NJ + jb) * VX + idx] + rb[((1 * 16 + pbo) * NJ + jb) * VX + idx]);
+      if (j < R) io<T>::st(static_cast<T*>(a.dx_g) + row * P * R + (int64_t)p * R + j, v);
+      else io<T>::st(static_cast<T*>(a.dx_b) + row * P * R + (int64_t)p * R + (j - R), v);
+    }
+    float f_acc = 0.f;
+    for (int o = tid; o < N * RI; o += kBwdThreads) {
+      const int n = o / RI, j = o - n * RI;
+      const int jb = j / JB, idx = (n & 7) * JB + (j - jb * JB), nbo = n >> 3;
+      const float* re = rb + TP::redx;
+      const float v = re[((0 * 16 + nbo) * NJ + jb) * VE + idx] + re[((1 * 16 + nbo) * NJ + jb) * VE + idx] +
+                      re[((2 * 16 + nbo) * NJ + jb) * VE + idx] + re[((3 * 16 + nbo) * NJ + jb) * VE + idx];
+      f_acc = fmaf(sl[TP::sbt + j * 128 + n], v, f_acc);
+      if (j < R) io<T>::st(static_cast<T*>(a.dB_g) + row * N * R + (int64_t)n * R + j, dtv * v);
+      else io<T>::st(static_cast<T*>(a.dB_b) + row * N * R + (int64_t)n * R + (j - R), dtv * v);
+    }
+    f_acc = warp_sum(f_acc);
+    if (lane == 0) fw[t * kBwdWarps + warp] = f_acc;
+  }
+  // dh_init = a_0 G_0
+  if (a.dh_init) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (ok_pk(i, k)) a.dh_init[state_base + (int64_t)(p0 + i) * N + n0 + k] = a_next * st[i][k];
+  }
+  __syncthreads();  // the last token's reads of the slots are done: the suffix pass reuses them
+  bwd_finish<T>(a, bh, b, h, Aval, mT, dD_acc, ew, fw, slots, red);
 }
 
 // dA[h] = sum_b dA_bh[b, h], dD likewise, in b order
@@ -364,6 +710,16 @@ int bvalidate(const m3b_ssd_bwd_args* a) {
   return M3B_OK;
 }
 
+template <typename T, int R, int RI>
+int launch_tiled(const BwdParams& p, unsigned grid, cudaStream_t st) {
+  const int smem = TPlan<R, RI>::floats * (int)sizeof(float);
+  const cudaError_t e =
+      cudaFuncSetAttribute(ssd_bwd_tiled_kernel<T, R, RI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "chunked_ssd_bwd: %s", cudaGetErrorString(e));
+  ssd_bwd_tiled_kernel<T, R, RI><<<grid, kBwdThreads, smem, st>>>(p);
+  return check_launch("chunked_ssd_bwd");
+}
+
 size_t bwd_smem(const m3b_ssd_bwd_args* a) {
   const int RI = a->x_b ? 2 * a->R : a->R;
   const size_t st = ((size_t)a->P * (a->N + 1) + 3) & ~(size_t)3;
@@ -391,7 +747,8 @@ extern "C" int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* ws, size_t w
   const BwdLayout w = bwd_layout(a);
   if (!ws || ws_bytes < w.total)
     return fail(M3B_ERR_WORKSPACE, "chunked_ssd_bwd: need %zu workspace bytes", w.total);
-  const size_t smem = bwd_smem(a);
+  const bool tiled = a->P <= 64 && a->N <= 128 && (a->R == 1 || a->R == 2 || a->R == 4);
+  const size_t smem = tiled ? 0 : bwd_smem(a);
   if (smem > 227 * 1024) return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: state too large for shared memory");
   uint8_t* base = static_cast<uint8_t*>(ws);
   BwdParams p{};
@@ -430,7 +787,18 @@ extern "C" int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* ws, size_t w
   p.dD_bh = reinterpret_cast<float*>(base + w.dD);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned grid = (unsigned)(a->batch * a->H);
-  if (a->dtype == M3B_F32) {
+  if (tiled) {
+    const bool f32 = a->dtype == M3B_F32, beta = a->x_b != nullptr;
+    switch (a->R * 2 + (beta ? 1 : 0)) {
+      case 2: rc = f32 ? launch_tiled<float, 1, 1>(p, grid, st) : launch_tiled<__nv_bfloat16, 1, 1>(p, grid, st); break;
+      case 3: rc = f32 ? launch_tiled<float, 1, 2>(p, grid, st) : launch_tiled<__nv_bfloat16, 1, 2>(p, grid, st); break;
+      case 4: rc = f32 ? launch_tiled<float, 2, 2>(p, grid, st) : launch_tiled<__nv_bfloat16, 2, 2>(p, grid, st); break;
+      case 5: rc = f32 ? launch_tiled<float, 2, 4>(p, grid, st) : launch_tiled<__nv_bfloat16, 2, 4>(p, grid, st); break;
+      case 8: rc = f32 ? launch_tiled<float, 4, 4>(p, grid, st) : launch_tiled<__nv_bfloat16, 4, 4>(p, grid, st); break;
+      default: rc = f32 ? launch_tiled<float, 4, 8>(p, grid, st) : launch_tiled<__nv_bfloat16, 4, 8>(p, grid, st); break;
+    }
+    if (rc != M3B_OK) return rc;
+  } else if (a->dtype == M3B_F32) {
     cudaFuncSetAttribute(ssd_bwd_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     ssd_bwd_kernel<float><<<grid, kBwdThreads, smem, st>>>(p);
   } else {

@@ -163,3 +163,30 @@ def test_chunked_ssd_backward_ragged_and_empty():
         else:
             for k in ("x_g", "B_g", "C", "dt", "A", "D"):
                 assert max_rel(to_np(got[k]), exp[k]) < 1e-4, k
+
+
+@pytest.mark.parametrize("P,N,R,beta", [(96, 160, 2, True), (16, 256, 1, False)])
+def test_chunked_ssd_backward_large_state_vs_oracle(P, N, R, beta):
+    """State shapes past the register-tiled kernel (P > 64 or N > 128) take the shared-memory
+    sweep kernel: same gradients."""
+    from mamba3_b200 import _lib
+
+    B, T, H = 1, 23, 2
+    g = torch.Generator().manual_seed(P + N)
+    r = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    x_g, x_b, x_raw, dy = r(B, T, H, P, R), r(B, T, H, P, R), r(B, T, H, P, R), r(B, T, H, P, R)
+    B_g, B_b, C = r(B, T, H, N, R) * 0.3, r(B, T, H, N, R) * 0.3, r(B, T, H, N, R) * 0.3
+    dt = torch.rand(B, T, H, generator=g) * 0.1 + 0.01
+    A, D = -torch.exp(r(H).clamp(-4, -1)), r(H)
+    h_init, dhf = r(B, H, P, N), r(B, H, P, N)
+    if not beta:
+        x_b = B_b = None
+    cu = lambda t: None if t is None else t.cuda().contiguous()  # noqa: E731
+    got = _lib.chunked_ssd_bwd(*[cu(t) for t in (x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, dy, h_init, dhf)])
+    npd = lambda t: None if t is None else t.double().numpy()  # noqa: E731
+    exp = oracle.chunked_ssd_backward(*[npd(t) for t in (x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, dy, h_init, dhf)])
+    for k, v in exp.items():
+        if v is None:
+            assert got[k] is None, k
+        else:
+            assert max_rel(to_np(got[k]), v) < 1e-4, k
