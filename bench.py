@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--no-seqpar", action="store_true", help="skip the config-3 sequence-sharded measurement")
     ap.add_argument("--no-lm", action="store_true", help="skip the config-2 LM forward measurement")
     ap.add_argument("--no-scan", action="store_true", help="skip the scan forward / backward measurement")
+    ap.add_argument("--no-train", action="store_true", help="skip the layer training-step measurement")
     ap.add_argument("--e2e-pieces", type=int, default=8,
                     help="token ranges forward_host streams the host batch in (copy/compute overlap)")
     return ap.parse_args()
@@ -281,6 +282,44 @@ def run_scan(dev, world, rank, barrier):
     return out
 
 
+def run_train(dev, world, rank, barrier):
+    """One training step of the config-1 layer (16 x 4096 tokens, d_model 768, bf16): forward through
+    the differentiable path (torch ops around chunked_ssd) and backward (the chunked_ssd and scan
+    backward kernels plus torch autograd for the rest), loss = sum of the output."""
+    import torch
+    import torch.distributed as dist
+
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(0)
+    layer = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).to(dev, torch.bfloat16).train()
+    g = torch.Generator(device=dev).manual_seed(6)
+    x = torch.randn(16, 4096, 768, device=dev, generator=g).to(torch.bfloat16)
+
+    def step():
+        layer.zero_grad(set_to_none=True)
+        layer(x).float().sum().backward()
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    a.record()
+    for _ in range(reps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"workload": "config-1 layer training step (forward + backward), x (16, 4096, 768) bf16 per GPU",
+            "ms_per_step": ms, "tokens_per_s": world * 16 * 4096 / (ms / 1e3)}
+
+
 def run_lm(dev, world, rank, barrier):
     """Config 2: KulaMambaLM forward (vocab 32000, d_model 768, 24 layers, bf16, weights seed 2)
     on input_ids (64, 2048) U[0, 32000), batch-sharded: 64 / G rows per rank, no collective."""
@@ -506,6 +545,7 @@ def run_ours(args):
     seqp = None if args.no_seqpar else run_seqpar(dev, world, rank, barrier)
     lmf = None if args.no_lm else run_lm(dev, world, rank, barrier)
     scan = None if args.no_scan else run_scan(dev, world, rank, barrier)
+    train = None if args.no_train else run_train(dev, world, rank, barrier)
 
     if rank == 0:
         import math
@@ -563,6 +603,8 @@ def run_ours(args):
             line["lm_forward"] = lmf
         if scan is not None:
             line["scan"] = scan
+        if train is not None:
+            line["train_step"] = train
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_sample_tokens)
         print(json.dumps(line), flush=True)
