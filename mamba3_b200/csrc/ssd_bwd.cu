@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(kBwdThreads) ssd_bwd_kernel(BwdParams a) {
 // over p (dB, dC) are reduce-scattered across the lanes of a warp with shuffles and finished
 // across warps in shared memory, one barrier per token.  Token operands are fetched into
 // registers one token ahead and stored into a three-deep ring of shared-memory slots.
-constexpr int kTileItems = 10;  // operand words one thread fetches per token (<= 2560 / 256)
+constexpr int kTilePairs = 5;  // operand element pairs one thread fetches per token (<= 2560 / 2 / 256)
 
 template <int R, int RI>
 struct TPlan {
@@ -370,15 +370,36 @@ __device__ __forceinline__ int reduce_scatter(float (&v)[V], int lane, int lo) {
   return off;
 }
 
+// raw storage of two consecutive elements: one 32-bit word for bf16, two floats for fp32
+template <typename T>
+struct PairT;
+template <>
+struct PairT<__nv_bfloat16> {
+  using type = uint32_t;
+  static __device__ __forceinline__ type ld(const __nv_bfloat16* p) { return __ldg(reinterpret_cast<const unsigned*>(p)); }
+  static __device__ __forceinline__ float lo(type w) { return __uint_as_float(w << 16); }
+  static __device__ __forceinline__ float hi(type w) { return __uint_as_float(w & 0xffff0000u); }
+};
+template <>
+struct PairT<float> {
+  using type = float2;
+  static __device__ __forceinline__ type ld(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
+  static __device__ __forceinline__ float lo(type w) { return w.x; }
+  static __device__ __forceinline__ float hi(type w) { return w.y; }
+};
+
+template <typename T>
 struct TokFetch {
-  float v[kTileItems];
+  typename PairT<T>::type w[kTilePairs];
   float dt;
 };
 
 // the operands of token `row` (flat (b, t, h) index): Xt, Bt, C, dy and, in the forward sweep,
-// x_raw; as registers (fetch) and then into a slot (store)
+// x_raw; as registers (fetch: element pairs, every segment has an even length) and then into a
+// slot (store)
 template <typename T, int R, int RI>
-__device__ __forceinline__ void tile_fetch(const BwdParams& a, int64_t row, bool with_xr, TokFetch& f) {
+__device__ __forceinline__ void tile_fetch(const BwdParams& a, int64_t row, bool with_xr, TokFetch<T>& f) {
+  using PT = PairT<T>;
   const int P = a.P, N = a.N;
   const int PR = P * R, NR = N * R;
   const bool beta = RI == 2 * R;
@@ -386,34 +407,33 @@ __device__ __forceinline__ void tile_fetch(const BwdParams& a, int64_t row, bool
             s6 = s5 + (with_xr ? PR : 0);
   const int64_t rp = row * PR, rn = row * NR;
 #pragma unroll
-  for (int u = 0; u < kTileItems; ++u) {
-    const int e = threadIdx.x + kBwdThreads * u;
-    float v = 0.f;
-    if (e < s0) v = io<T>::ld(static_cast<const T*>(a.x_g) + rp + e);
-    else if (e < s1) v = io<T>::ld(static_cast<const T*>(a.x_b) + rp + (e - s0));
-    else if (e < s2) v = io<T>::ld(static_cast<const T*>(a.B_g) + rn + (e - s1));
-    else if (e < s3) v = io<T>::ld(static_cast<const T*>(a.B_b) + rn + (e - s2));
-    else if (e < s4) v = io<T>::ld(static_cast<const T*>(a.C) + rn + (e - s3));
-    else if (e < s5) v = io<T>::ld(static_cast<const T*>(a.dy) + rp + (e - s4));
-    else if (e < s6) v = io<T>::ld(static_cast<const T*>(a.x_raw) + rp + (e - s5));
-    f.v[u] = v;
+  for (int u = 0; u < kTilePairs; ++u) {
+    const int e = 2 * (threadIdx.x + kBwdThreads * u);
+    typename PT::type v{};
+    if (e < s0) v = PT::ld(static_cast<const T*>(a.x_g) + rp + e);
+    else if (e < s1) v = PT::ld(static_cast<const T*>(a.x_b) + rp + (e - s0));
+    else if (e < s2) v = PT::ld(static_cast<const T*>(a.B_g) + rn + (e - s1));
+    else if (e < s3) v = PT::ld(static_cast<const T*>(a.B_b) + rn + (e - s2));
+    else if (e < s4) v = PT::ld(static_cast<const T*>(a.C) + rn + (e - s3));
+    else if (e < s5) v = PT::ld(static_cast<const T*>(a.dy) + rp + (e - s4));
+    else if (e < s6) v = PT::ld(static_cast<const T*>(a.x_raw) + rp + (e - s5));
+    f.w[u] = v;
   }
   f.dt = threadIdx.x == 0 ? ldf(a.dt, row, a.dt_dtype) : 0.f;
 }
 
-template <int R, int RI>
-__device__ __forceinline__ void tile_store(const BwdParams& a, float* slot, bool with_xr, const TokFetch& f,
+template <typename T, int R, int RI>
+__device__ __forceinline__ void tile_store(const BwdParams& a, float* slot, bool with_xr, const TokFetch<T>& f,
                                            float Aval) {
   using TP = TPlan<R, RI>;
+  using PT = PairT<T>;
   const int P = a.P, N = a.N;
   const int PR = P * R, NR = N * R;
   const bool beta = RI == 2 * R;
   const int s0 = PR, s1 = s0 + (beta ? PR : 0), s2 = s1 + NR, s3 = s2 + (beta ? NR : 0), s4 = s3 + NR, s5 = s4 + PR,
             s6 = s5 + (with_xr ? PR : 0);
-#pragma unroll
-  for (int u = 0; u < kTileItems; ++u) {
-    const int e = threadIdx.x + kBwdThreads * u;
-    const float v = f.v[u];
+  // element e of a segment -> its slot position
+  auto put = [&](int e, float v) {
     if (e < s0) slot[TP::sx + (e / R) * RI + e % R] = v;
     else if (e < s1) slot[TP::sx + ((e - s0) / R) * RI + R + (e - s0) % R] = v;
     else if (e < s2) slot[TP::sbt + ((e - s1) % R) * 128 + (e - s1) / R] = v;
@@ -421,6 +441,14 @@ __device__ __forceinline__ void tile_store(const BwdParams& a, float* slot, bool
     else if (e < s4) slot[TP::sct + ((e - s3) % R) * 128 + (e - s3) / R] = v;
     else if (e < s5) slot[TP::sdy + (e - s4)] = v;
     else if (e < s6) slot[TP::sxr + (e - s5)] = v;
+  };
+#pragma unroll
+  for (int u = 0; u < kTilePairs; ++u) {
+    const int e = 2 * (threadIdx.x + kBwdThreads * u);
+    if (e < s6) {
+      put(e, PT::lo(f.w[u]));
+      put(e + 1, PT::hi(f.w[u]));
+    }
   }
   if (threadIdx.x == 0) {
     slot[TP::ssc] = f.dt;
@@ -464,15 +492,19 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
     for (int k = 0; k < 8; ++k)
       st[i][k] = a.h_init && ok_pk(i, k) ? a.h_init[state_base + (int64_t)(p0 + i) * N + n0 + k] : 0.f;
   float dD_acc = 0.f;
-  TokFetch f;
+  // token operands are fetched two tokens ahead into two register sets that trade roles every
+  // token (so a set is stored one full token after its loads were issued)
+  TokFetch<T> fa, fb;
   __syncthreads();  // slots zeroed
   if (TT > 0) {
-    tile_fetch<T, R, RI>(a, (b * TT) * a.H + h, true, f);
-    tile_store<R, RI>(a, slot(0), true, f, Aval);
+    tile_fetch<T, R, RI>(a, (b * TT) * a.H + h, true, fa);
+    tile_store<T, R, RI>(a, slot(0), true, fa, Aval);
   }
+  if (TT > 1) tile_fetch<T, R, RI>(a, (b * TT + 1) * a.H + h, true, fa);
   __syncthreads();
-  for (int64_t t = 0; t < TT; ++t) {
-    if (t + 1 < TT) tile_fetch<T, R, RI>(a, (b * TT + t + 1) * a.H + h, true, f);
+  // token t; fcur holds token t + 1 (stored here), fnext receives token t + 2
+  auto fwd_tok = [&](int64_t t, TokFetch<T>& fcur, TokFetch<T>& fnext) {
+    if (t + 2 < TT) tile_fetch<T, R, RI>(a, (b * TT + t + 2) * a.H + h, true, fnext);
     const float* sl = slot(t);
     const float dtv = sl[TP::ssc], av = sl[TP::ssc + 1];
     // h_t = a_t h_{t-1} + dt_t Xt Bt^T
@@ -509,7 +541,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
     float* rc = redbuf + (int)(t & 1) * TP::red + (pbh * 16 + nb) * VC + offc;
 #pragma unroll
     for (int e = 0; e < VC / 4; ++e) rc[e] = pc[e];
-    if (t + 1 < TT) tile_store<R, RI>(a, slot(t + 1), true, f, Aval);
+    if (t + 1 < TT) tile_store<T, R, RI>(a, slot(t + 1), true, fcur, Aval);
     __syncthreads();
     // dC_t, e_t = <C_t, dC_t>; dx_raw = D dy, dD
     const int64_t row = (b * TT + t) * a.H + h;
@@ -530,6 +562,10 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
     }
     e_acc = warp_sum(e_acc);
     if (lane == 0) ew[t * kBwdWarps + warp] = e_acc;
+  };
+  for (int64_t t = 0; t < TT; t += 2) {
+    fwd_tok(t, fa, fb);
+    if (t + 1 < TT) fwd_tok(t + 1, fb, fa);
   }
   // m_T = <dh_final, h_final>; then G_T = dh_final
   float mT = 0.f;
@@ -552,13 +588,15 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
 
   // ---------------- reverse sweep: G_t, dXt_t, dBt_t, fr_t, dh_init ----------------
   if (TT > 0) {
-    tile_fetch<T, R, RI>(a, (b * TT + TT - 1) * a.H + h, false, f);
-    tile_store<R, RI>(a, slot(TT - 1), false, f, Aval);
+    tile_fetch<T, R, RI>(a, (b * TT + TT - 1) * a.H + h, false, fa);
+    tile_store<T, R, RI>(a, slot(TT - 1), false, fa, Aval);
   }
+  if (TT > 1) tile_fetch<T, R, RI>(a, (b * TT + TT - 2) * a.H + h, false, fa);
   __syncthreads();
   float a_next = 1.f;  // a_{t+1} (1 past the last token)
-  for (int64_t t = TT - 1; t >= 0; --t) {
-    if (t > 0) tile_fetch<T, R, RI>(a, (b * TT + t - 1) * a.H + h, false, f);
+  // token t; fcur holds token t - 1 (stored here), fnext receives token t - 2
+  auto rev_tok = [&](int64_t t, TokFetch<T>& fcur, TokFetch<T>& fnext) {
+    if (t > 1) tile_fetch<T, R, RI>(a, (b * TT + t - 2) * a.H + h, false, fnext);
     const float* sl = slot(t);
     const float dtv = sl[TP::ssc], av = sl[TP::ssc + 1];
     // G_t = a_{t+1} G_{t+1} + dy_t C_t^T
@@ -621,7 +659,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
 #pragma unroll
       for (int e = 0; e < VE / 4; ++e) re[e] = pe[e];
     }
-    if (t > 0) tile_store<R, RI>(a, slot(t - 1), false, f, Aval);
+    if (t > 0) tile_store<T, R, RI>(a, slot(t - 1), false, fcur, Aval);
     a_next = av;
     __syncthreads();
     // dXt = dt sum over the two column halves; E = sum over the four row quarters, dBt = dt E
@@ -646,6 +684,10 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
     }
     f_acc = warp_sum(f_acc);
     if (lane == 0) fw[t * kBwdWarps + warp] = f_acc;
+  };
+  for (int64_t t = TT - 1; t >= 0; t -= 2) {
+    rev_tok(t, fa, fb);
+    if (t >= 1) rev_tok(t - 1, fb, fa);
   }
   // dh_init = a_0 G_0
   if (a.dh_init) {
