@@ -827,6 +827,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     auto state_init = [&](const ChunkPos& c, int gs) -> bool {
       const int b = c.b, h = c.h;
       const int s2 = gs & 1;
+      // this sequence's gate parameters (one entry per thread), requested before the waits below
+      static_assert(kPP * 4 <= kEpiThreads, "one gate parameter entry per epilogue thread");
+      const int pd = p.param_dtype;
+      const int gpp = tid / RP, gq = tid % RP;
+      const bool gok = tid < kPP * RP && gpp < P && gq < R;
+      const int64_t gi = ((int64_t)h * P + gpp) * R + gq;
+      const float gmz = gok ? ldf(p.mimo_z, gi, pd) : 0.f;
+      const float gmd = gok ? ldf(p.mimo_down, gi, pd) : 0.f;
+      const float gmx = gok ? ldf(p.mimo_x, gi, pd) : 0.f;
       if (c.part > 0 && lead && !*abort_flag && !flag_wait_geq(a.ho_flag + 2 * c.seq + 1, c.part)) {
         *abort_flag = 1;
         record_error(a.err, M3B_ERR_TIMEOUT);
@@ -859,14 +868,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         tmem_st8_nowait(trow + kColH + 32 * ch + 8 * c8, v8);
       }
       tmem_wait_st();
-      // this sequence's gate parameters (the previous sequence's last output is complete)
-      const int pd = p.param_dtype;
-      for (int e = tid; e < kPP * RP; e += kEpiThreads) {
-        const int pp = e / RP, q = e % RP;
-        const bool okp = pp < P && q < R;
-        emz[q * kPP + pp] = okp ? ldf(p.mimo_z, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
-        emd[q * kPP + pp] = okp ? ldf(p.mimo_down, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
-        emx[q * kPP + pp] = okp ? ldf(p.mimo_x, ((int64_t)h * P + pp) * R + q, pd) : 0.f;
+      // the gate parameters into shared memory (the previous sequence's last output is complete)
+      if (tid < kPP * RP) {
+        emz[gq * kPP + gpp] = gmz;
+        emd[gq * kPP + gpp] = gmd;
+        emx[gq * kPP + gpp] = gmx;
       }
       named_bar(kBarEpi, kEpiThreads);  // mimo_x is read by the X / W tiles below
       return true;
