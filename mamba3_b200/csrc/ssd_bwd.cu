@@ -113,7 +113,6 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Suffix pass shared by the backward kernels: m_t = m_{t+1} + e_t - dt_t fr_t (m_T = mT) from the
 // per-warp partials ew / fw, then ddt_t = fr_t + A m_t and this (b, h)'s shares of dA and dD.
 // suf: >= kBwdThreads floats of shared memory, red: >= kBwdWarps; both free for reuse here.
-template <typename T>
 __device__ void bwd_finish(const BwdParams& a, int64_t bh, int64_t b, int h, float Aval, float mT, float dD_acc,
                            const float* ew, const float* fw, float* suf, float* red) {
   const int64_t TT = a.T;
@@ -319,7 +318,7 @@ __global__ void __launch_bounds__(kBwdThreads) ssd_bwd_kernel(BwdParams a) {
       a.dh_init[state_base + e] = a_next * S[p * NS + n];
     }
 
-  bwd_finish<T>(a, bh, b, h, Aval, mT, dD_acc, ew, fw, slots, red);
+  bwd_finish(a, bh, b, h, Aval, mT, dD_acc, ew, fw, slots, red);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -698,7 +697,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
         if (ok_pk(i, k)) a.dh_init[state_base + (int64_t)(p0 + i) * N + n0 + k] = a_next * st[i][k];
   }
   __syncthreads();  // the last token's reads of the slots are done: the suffix pass reuses them
-  bwd_finish<T>(a, bh, b, h, Aval, mT, dD_acc, ew, fw, slots, red);
+  bwd_finish(a, bh, b, h, Aval, mT, dD_acc, ew, fw, slots, red);
 }
 
 // dA[h] = sum_b dA_bh[b, h], dD likewise, in b order
