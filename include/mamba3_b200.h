@@ -226,7 +226,10 @@ M3B_API int m3b_layer_fwd_noalloc(const m3b_layer_fwd_args* a, void* stream);
  * ------------------------------------------------------------------------ */
 M3B_API int m3b_copy_rows_async(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t row_bytes,
                                 size_t rows, void* stream);
-/* Bytes of device workspace m3b_layer_fwd needs for these arguments. */
+/* Bytes of device workspace m3b_layer_fwd uses for these arguments on the current device.
+ * With enough (batch, head) sequences the fused kernel cuts them into parts handed from CTA to
+ * CTA, and this size includes the hand-off buffers; given less (but at least what the same
+ * call needs without them), m3b_layer_fwd keeps whole sequences per CTA instead. */
 M3B_API size_t m3b_layer_fwd_workspace(const m3b_layer_fwd_args* a);
 M3B_API int m3b_layer_fwd(const m3b_layer_fwd_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
