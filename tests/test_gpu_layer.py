@@ -246,3 +246,23 @@ def test_fused_sequence_parts_equal_chunk_parallel(d_model, R, B, T, layer_algo)
     for k in ("h", "angle", "prev_BX"):
         assert max_rel(to_np(st1[k]), to_np(st2[k])) < (1e-4 if k == "angle" else BF16_TOL), k
         assert max_rel(to_np(so[k]), to_np(st2[k])) < (1e-4 if k == "angle" else BF16_TOL), k
+
+
+def test_fused_sequence_parts_from_a_state(layer_algo):
+    """Parts with an initial state: prefill_from over a range long enough to be cut into parts
+    (8 x 24 sequences, 14 chunks) continues a prefill exactly as the whole prefill does."""
+    from mamba3_b200 import KulaMamba
+
+    if layer_algo != 1:
+        pytest.skip("fused algorithm only")
+    torch.manual_seed(61)
+    m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
+    x = torch.randn(8, 1000, 768, generator=torch.Generator().manual_seed(62)).cuda().to(torch.bfloat16)
+    T1 = 104
+    with torch.no_grad():
+        y, st = m.prefill(x)
+        y1, st1 = m.prefill(x[:, :T1])
+        y2, st2 = m.prefill_from(x[:, T1:], st1)
+    assert max_rel(to_np(torch.cat([y1, y2], 1)), to_np(y)) < BF16_TOL
+    for k in ("h", "angle", "prev_BX"):
+        assert max_rel(to_np(st2[k]), to_np(st[k])) < BF16_TOL, k
