@@ -305,6 +305,26 @@ M3B_API size_t m3b_chunked_ssd_bwd_workspace(const m3b_ssd_bwd_args* a);
 M3B_API int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * RMSNorm of the blocks around the layer (mamba3/mamba3.py:19-35; used by
+ * mamba3/block.py:53,70,81-103 and KulaMambaLM's final norm): for each of `rows` rows of d
+ * contiguous elements, y = (x * rsqrt(mean(x^2) + eps)) * weight, the mean in fp32, the
+ * scale and both products rounded to `dtype` as the reference's torch ops store them.
+ * x, weight (d) and y share `dtype` (M3B_F32, M3B_BF16 or M3B_F16); y may alias x.
+ * ------------------------------------------------------------------------ */
+M3B_API int m3b_rmsnorm(const void* x, const void* weight, void* y, int64_t rows, int32_t d, float eps,
+                        int32_t dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Element-wise steps of the blocks, one pass each, results rounded to `dtype` as the
+ * reference's torch ops store them; n elements, out may alias an input.
+ *   m3b_swiglu_act: out = silu(g) * u   (SwiGLU.forward, mamba3/block.py:16-26)
+ *   m3b_scaled_add: out = x + h * scale (the residuals of mamba3/block.py:79-107)
+ * ------------------------------------------------------------------------ */
+M3B_API int m3b_swiglu_act(const void* g, const void* u, void* out, int64_t n, int32_t dtype, void* stream);
+M3B_API int m3b_scaled_add(const void* x, const void* h, float scale, void* out, int64_t n, int32_t dtype,
+                           void* stream);
+
+/* ------------------------------------------------------------------------
  * Tensor-core self-test (diagnostic; no counterpart in the reference).
  * D (128 x 64, fp32) = A (128 x 128 bf16, row-major) x B (64 x 128 bf16, row-major)^T,
  * staged through the same shared-memory layouts and UMMA descriptors as the chunk

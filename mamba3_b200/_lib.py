@@ -113,6 +113,10 @@ SIGNATURES = {
     "m3b_chunked_ssd": (C.c_int, [C.POINTER(SsdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_chunked_ssd_bwd_workspace": (C.c_size_t, [C.POINTER(SsdBwdArgs)]),
     "m3b_chunked_ssd_bwd": (C.c_int, [C.POINTER(SsdBwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_float, C.c_int32,
+                              C.c_void_p]),
+    "m3b_swiglu_act": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
+    "m3b_scaled_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
     "m3b_selftest_umma": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
 }
 
@@ -291,6 +295,48 @@ def chunked_ssd_bwd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init=None, dh
     with torch.cuda.device(dev):
         _check(L.m3b_chunked_ssd_bwd(C.byref(a), _ptr(ws), need, _stream(dev)), "m3b_chunked_ssd_bwd")
     return g
+
+
+def rmsnorm(x, weight, eps, out=None):
+    """RMSNorm over the last dim of x (contiguous) with weight (d,) of x's dtype."""
+    dev = _cuda(x, weight, out)
+    d = x.shape[-1]
+    if x.stride(-1) != 1 or not x.is_contiguous() or weight.numel() != d or weight.dtype != x.dtype:
+        raise M3bError("rmsnorm: contiguous x and a weight of x's dtype with x.shape[-1] entries expected")
+    y = torch.empty_like(x) if out is None else out
+    with torch.cuda.device(dev):
+        _check(lib().m3b_rmsnorm(_ptr(x), _ptr(weight.contiguous()), _ptr(y), x.numel() // d, d, float(eps),
+                                 dtype_code(x.dtype), _stream(dev)), "m3b_rmsnorm")
+    return y
+
+
+def _same(*ts):
+    t0 = ts[0]
+    for t in ts:
+        if t.shape != t0.shape or t.dtype != t0.dtype or not t.is_contiguous():
+            raise M3bError("element-wise op: contiguous tensors of one shape and dtype expected")
+
+
+def swiglu_act(g, u, out=None):
+    """silu(g) * u in g's dtype."""
+    dev = _cuda(g, u, out)
+    _same(g, u)
+    out = torch.empty_like(g) if out is None else out
+    with torch.cuda.device(dev):
+        _check(lib().m3b_swiglu_act(_ptr(g), _ptr(u), _ptr(out), g.numel(), dtype_code(g.dtype), _stream(dev)),
+               "m3b_swiglu_act")
+    return out
+
+
+def scaled_add(x, h, scale, out=None):
+    """x + h * scale in x's dtype."""
+    dev = _cuda(x, h, out)
+    _same(x, h)
+    out = torch.empty_like(x) if out is None else out
+    with torch.cuda.device(dev):
+        _check(lib().m3b_scaled_add(_ptr(x), _ptr(h), float(scale), _ptr(out), x.numel(), dtype_code(x.dtype),
+                                    _stream(dev)), "m3b_scaled_add")
+    return out
 
 
 def selftest_umma(A, B, mode):

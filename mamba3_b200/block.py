@@ -15,7 +15,13 @@ import torch.nn as nn
 import torch.nn.functional as F
 from torch.utils.checkpoint import checkpoint as grad_checkpoint
 
+from . import ops
 from .mamba3 import KulaMamba, RMSNorm
+
+
+def _residual(x, h, scale):
+    """x + h * scale (the blocks' scaled residuals): one kernel when no autograd goes through."""
+    return ops.scaled_add(x, h, scale) if ops.kernel_ok(x, h) else x + h * scale
 
 
 class SwiGLU(nn.Module):
@@ -29,7 +35,9 @@ class SwiGLU(nn.Module):
         self.w_down = nn.Linear(d_ff, d_model, bias=bias)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.w_down(F.silu(self.w_gate(x)) * self.w_up(x))
+        g, u = self.w_gate(x), self.w_up(x)
+        a = ops.swiglu_act(g, u) if ops.kernel_ok(g, u) else F.silu(g) * u
+        return self.w_down(a)
 
 
 class KulaMambaBlock(nn.Module):
@@ -72,7 +80,7 @@ class KulaMambaBlock(nn.Module):
                 m = grad_checkpoint(lambda t: self.mlp(self.mlp_norm(t)), x, use_reentrant=False)
             else:
                 m = self.mlp(self.mlp_norm(x))
-            x = x + m * self.residual_scale
+            x = _residual(x, m, self.residual_scale)
         return x
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -80,15 +88,15 @@ class KulaMambaBlock(nn.Module):
             h = grad_checkpoint(lambda t: self.ssm(self.ssm_norm(t)), x, use_reentrant=False)
         else:
             h = self.ssm(self.ssm_norm(x))
-        return self._mlp_residual(x + h * self.residual_scale)
+        return self._mlp_residual(_residual(x, h, self.residual_scale))
 
     def step(self, x, ssm_state):
         h, new_state = self.ssm.step(self.ssm_norm(x), ssm_state)
-        return self._mlp_residual(x + h * self.residual_scale), new_state
+        return self._mlp_residual(_residual(x, h, self.residual_scale)), new_state
 
     def prefill(self, x, compact_state=False):
         h, state = self.ssm.prefill(self.ssm_norm(x), compact_state=compact_state)
-        return self._mlp_residual(x + h * self.residual_scale), state
+        return self._mlp_residual(_residual(x, h, self.residual_scale)), state
 
 
 class KulaMambaLM(nn.Module):

@@ -18,6 +18,7 @@ from __future__ import annotations
 import torch
 
 from . import ops
+from .block import _residual
 
 
 class GraphDecoder:
@@ -58,7 +59,7 @@ class GraphDecoder:
             ops.step_ssm_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_BX"], st["angle"],
                           self.ybuf[i])
         h = ssm.out_proj(self.ybuf[i])
-        return blk._mlp_residual(x + h * blk.residual_scale)
+        return blk._mlp_residual(_residual(x, h, blk.residual_scale))
 
     def _sample(self, logits):
         from .block import _sample

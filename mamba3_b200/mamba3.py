@@ -30,7 +30,9 @@ from .ssd import chunked_ssd
 
 
 class RMSNorm(nn.Module):
-    """RMSNorm with the reference's semantics (mamba3/mamba3.py:19-35)."""
+    """RMSNorm with the reference's semantics (mamba3/mamba3.py:19-35).  On CUDA without
+    gradients (inference, decode) it is one kernel (``mamba3_b200::rmsnorm``); when autograd
+    needs it (training) it runs as torch ops."""
 
     def __init__(self, d: int, eps: float = 1e-5, dim: int = -1):
         super().__init__()
@@ -39,6 +41,9 @@ class RMSNorm(nn.Module):
         self.dim = dim
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if (x.is_cuda and self.dim in (-1, x.ndim - 1) and x.dtype in (torch.float32, torch.bfloat16, torch.float16)
+                and not (torch.is_grad_enabled() and (x.requires_grad or self.weight.requires_grad))):
+            return ops.rmsnorm(x, self.weight, self.eps)
         inv = torch.rsqrt(x.float().pow(2).mean(self.dim, keepdim=True) + self.eps).to(x.dtype)
         shape = [1] * x.ndim
         shape[self.dim] = -1

@@ -176,6 +176,50 @@ def _(x_g, x_b, B_g, B_b, C, dt, A, D, x_raw, h_init, dy, dh_final):
 
 
 # ---------------------------------------------------------------------------
+# RMSNorm of the blocks (mamba3/mamba3.py:19-35)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("mamba3_b200::rmsnorm", mutates_args=())
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    return _lib.rmsnorm(x.contiguous(), weight.to(x.dtype), eps)
+
+
+@rmsnorm.register_fake
+def _(x, weight, eps):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("mamba3_b200::swiglu_act", mutates_args=())
+def swiglu_act(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    return _lib.swiglu_act(g.contiguous(), u.contiguous())
+
+
+@swiglu_act.register_fake
+def _(g, u):
+    return torch.empty_like(g)
+
+
+@torch.library.custom_op("mamba3_b200::scaled_add", mutates_args=())
+def scaled_add(x: torch.Tensor, h: torch.Tensor, scale: float) -> torch.Tensor:
+    return _lib.scaled_add(x.contiguous(), h.contiguous(), scale)
+
+
+@scaled_add.register_fake
+def _(x, h, scale):
+    return torch.empty_like(x)
+
+
+def kernel_ok(*ts) -> bool:
+    """True when the element-wise block kernels apply: CUDA tensors of one float dtype and shape,
+    and no autograd through them (training keeps the torch ops and their backward)."""
+    t0 = ts[0]
+    if not t0.is_cuda or t0.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        return False
+    if any(t.shape != t0.shape or t.dtype != t0.dtype or t.device != t0.device for t in ts):
+        return False
+    return not (torch.is_grad_enabled() and any(t.requires_grad for t in ts))
+
+
+# ---------------------------------------------------------------------------
 # decode step (everything between in_proj and out_proj of KulaMamba.step)
 # ---------------------------------------------------------------------------
 @torch.library.custom_op("mamba3_b200::step_ssm", mutates_args=())

@@ -190,3 +190,64 @@ def test_step_full_batch_state_layout():
         # bf16 projection output feeds the fp32 state update: bf16 I/O tolerance
         assert max_rel(to_np(st2["h"][b:b + 1]), o2["h"]) < 2e-2
         assert max_rel(to_np(st2["prev_BX"][b:b + 1]), o2["prev_BX"]) < 2e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("shape", [(4, 512, 768), (3, 5, 100), (2, 2048), (7, 64)])
+def test_rmsnorm_kernel_matches_reference_formula(dtype, shape):
+    """m3b_rmsnorm against the reference's torch formula (mamba3/mamba3.py:28-35): the same
+    roundings, so bf16 / fp16 results agree to the last bit but for rare summation-order ties."""
+    from mamba3_b200 import _lib
+
+    g = torch.Generator().manual_seed(sum(shape))
+    x = (torch.randn(*shape, generator=g) * 3).to("cuda", dtype)
+    w = (torch.randn(shape[-1], generator=g) * 0.5 + 1).to("cuda", dtype)
+    rms = torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-5).to(dtype)
+    ref = x * rms * w
+    y = _lib.rmsnorm(x, w, 1e-5)
+    tol = 1e-6 if dtype == torch.float32 else 1e-2
+    assert max_rel(to_np(y), to_np(ref)) < tol
+    if dtype != torch.float32:
+        assert (y == ref).float().mean().item() > 0.99
+    x2 = x.clone()
+    _lib.rmsnorm(x2, w, 1e-5, out=x2)  # in place
+    assert torch.equal(x2, y)
+
+
+def test_rmsnorm_module_uses_kernel_without_grad():
+    """RMSNorm: the kernel under no_grad and the torch ops with autograd give the same values."""
+    from mamba3_b200.mamba3 import RMSNorm
+
+    norm = RMSNorm(768).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_(torch.randn(768) * 0.3 + 1)
+    x = torch.randn(8, 33, 768, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        y_k = norm(x)
+    y_t = norm(x.requires_grad_(True))
+    assert y_t.requires_grad
+    assert max_rel(to_np(y_k), to_np(y_t)) < 1e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("n", [8 * 4096 * 2112, 1001])
+def test_swiglu_and_residual_kernels_match_torch(dtype, n):
+    """m3b_swiglu_act == F.silu(g) * u and m3b_scaled_add == x + h * s, rounded as torch stores
+    them (vector path for n % 8 == 0, scalar path otherwise)."""
+    import torch.nn.functional as F
+
+    from mamba3_b200 import _lib
+
+    g = torch.Generator().manual_seed(n % 97)
+    a = (torch.randn(n, generator=g) * 3).to("cuda", dtype)
+    b = torch.randn(n, generator=g).to("cuda", dtype)
+    tol = 1e-6 if dtype == torch.float32 else 1e-2
+    act = _lib.swiglu_act(a, b)
+    ref = F.silu(a) * b
+    assert max_rel(to_np(act), to_np(ref)) < tol
+    res = _lib.scaled_add(a, b, 0.1443)
+    ref2 = a + b * 0.1443
+    assert max_rel(to_np(res), to_np(ref2)) < tol
+    if dtype != torch.float32:
+        assert (act == ref).float().mean().item() > 0.99
+        assert (res == ref2).float().mean().item() > 0.99
