@@ -2,8 +2,9 @@
 
 This is the harness the decode and LM configs run through; it mirrors the
 reference's module structure, names and init order (mamba3/block.py:16-231) so
-seeded weights and state dicts match.  The SwiGLU MLP, norms and residuals are
-plain torch (cuBLAS); the SSM layer is ``mamba3_b200.mamba3.KulaMamba``.
+seeded weights and state dicts match.  The MLP's GEMMs are cuBLAS; at inference the norms,
+the SwiGLU activation and the scaled residuals are one library kernel each (torch ops when
+autograd runs through them); the SSM layer is ``mamba3_b200.mamba3.KulaMamba``.
 """
 
 from __future__ import annotations
