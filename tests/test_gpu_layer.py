@@ -321,3 +321,24 @@ def test_mimo_ranks_interact():
         m.mimo_x[:, :, 1] = 0.0
         y1 = m(x)
     assert (y - y1).abs().max().item() > 1e-5
+
+
+@pytest.mark.parametrize("compact", [False, True], ids=["prev_bx", "compact"])
+def test_dt_scale_steps_equal_forward(compact):
+    """Decode steps with a per-token dt scale (mamba3/mamba3.py:279-280) reproduce the forward
+    with the same scale (fp32 model)."""
+    from mamba3_b200 import KulaMamba
+
+    torch.manual_seed(75)
+    m = KulaMamba(d_model=128, d_state=128, headdim=64, mimo_rank=2).cuda().eval()
+    g = torch.Generator().manual_seed(76)
+    x = torch.randn(2, 40, 128, generator=g).cuda()
+    ds = (torch.rand(2, 40, m.nheads, generator=g) * 1.5 + 0.25).cuda()
+    with torch.no_grad():
+        y_par = m(x, dt_scale=ds)
+        st = m.allocate_inference_state(2, compact=compact)
+        ys = []
+        for t in range(40):
+            yt, st = m.step(x[:, t:t + 1], st, dt_scale=ds[:, t])
+            ys.append(yt[:, 0])
+    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < BF16_TOL
