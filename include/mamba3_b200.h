@@ -315,6 +315,35 @@ M3B_API int m3b_rmsnorm(const void* x, const void* weight, void* y, int64_t rows
                         int32_t dtype, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Gate and MIMO down-projection of the layer (mamba3/mamba3.py:234-238) for the training path,
+ * forward and backward, over `rows` rows of `channels` = H*P channels with R ranks:
+ *   out[c] = sum_r y[c,r] silu(z[c] mimo_z[c,r]) mimo_down[c,r]
+ * y (rows, channels, R), z (rows, channels; rows z_stride elements apart, 0 = channels),
+ * out / dout / dz (rows, channels), mimo_z / mimo_down and their gradients (channels, R), all
+ * of `dtype` and otherwise contiguous.  The backward gives dy, dz and the
+ * parameter gradients (summed over the rows in a fixed order; caller-owned workspace of
+ * m3b_gate_bwd_workspace bytes).  With rows == 0 the per-row pointers may be null and the
+ * backward writes zero parameter gradients.
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_gate_args {
+  int64_t rows, z_stride;
+  int32_t channels, R, dtype;
+  const void* y;
+  const void* z;
+  const void* mimo_z;
+  const void* mimo_down;
+  void* out;              /* forward */
+  const void* dout;       /* backward: */
+  void* dy;
+  void* dz;
+  void* d_mimo_z;
+  void* d_mimo_down;
+} m3b_gate_args;
+M3B_API int m3b_gate_fwd(const m3b_gate_args* a, void* stream);
+M3B_API size_t m3b_gate_bwd_workspace(const m3b_gate_args* a);
+M3B_API int m3b_gate_bwd(const m3b_gate_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Element-wise steps of the blocks, one pass each, results rounded to `dtype` as the
  * reference's torch ops store them; n elements, out may alias an input.
  *   m3b_swiglu_act: out = silu(g) * u   (SwiGLU.forward, mamba3/block.py:16-26)

@@ -92,6 +92,13 @@ class SsdBwdArgs(C.Structure):
                 ("dD", C.c_void_p), ("dh_init", C.c_void_p)]
 
 
+class GateArgs(C.Structure):
+    _fields_ = [("rows", C.c_int64), ("z_stride", C.c_int64), ("channels", C.c_int32), ("R", C.c_int32),
+                ("dtype", C.c_int32), ("y", C.c_void_p), ("z", C.c_void_p), ("mimo_z", C.c_void_p),
+                ("mimo_down", C.c_void_p), ("out", C.c_void_p), ("dout", C.c_void_p), ("dy", C.c_void_p),
+                ("dz", C.c_void_p), ("d_mimo_z", C.c_void_p), ("d_mimo_down", C.c_void_p)]
+
+
 LAYER_FWD_STAGES = ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out", "last_bx")
 
 
@@ -113,6 +120,9 @@ SIGNATURES = {
     "m3b_chunked_ssd": (C.c_int, [C.POINTER(SsdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_chunked_ssd_bwd_workspace": (C.c_size_t, [C.POINTER(SsdBwdArgs)]),
     "m3b_chunked_ssd_bwd": (C.c_int, [C.POINTER(SsdBwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_gate_fwd": (C.c_int, [C.POINTER(GateArgs), C.c_void_p]),
+    "m3b_gate_bwd_workspace": (C.c_size_t, [C.POINTER(GateArgs)]),
+    "m3b_gate_bwd": (C.c_int, [C.POINTER(GateArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_float, C.c_int32,
                               C.c_void_p]),
     "m3b_swiglu_act": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
@@ -295,6 +305,52 @@ def chunked_ssd_bwd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init=None, dh
     with torch.cuda.device(dev):
         _check(L.m3b_chunked_ssd_bwd(C.byref(a), _ptr(ws), need, _stream(dev)), "m3b_chunked_ssd_bwd")
     return g
+
+
+def _gate_args(y, z, mimo_z, mimo_down):
+    """(rows, channels, R) view of the gate operands: y (..., H, P, R) contiguous, z (..., H*P)
+    with unit channel stride and a uniform row stride, parameters (H, P, R) contiguous."""
+    H, P, R = mimo_z.shape
+    Cn = H * P
+    rows = y.numel() // (Cn * R) if Cn * R else 0
+    if (not y.is_contiguous() or y.shape[-3:] != (H, P, R) or mimo_down.shape != (H, P, R)
+            or not mimo_z.is_contiguous() or not mimo_down.is_contiguous()
+            or len({y.dtype, z.dtype, mimo_z.dtype, mimo_down.dtype}) != 1):
+        raise M3bError("gate: y (..., H, P, R) contiguous, parameters (H, P, R), one dtype expected")
+    z2 = z.reshape(rows, Cn) if rows else z.reshape(0, Cn)
+    if rows and (z2.stride(1) != 1 or z2.data_ptr() != z.data_ptr()):
+        raise M3bError("gate: z must be a strided view of (rows, H*P) with unit channel stride")
+    return GateArgs(rows, z2.stride(0) if rows else 0, Cn, R, dtype_code(y.dtype), _ptr(y), _ptr(z),
+                    _ptr(mimo_z), _ptr(mimo_down))
+
+
+def gate_fwd(y, z, mimo_z, mimo_down):
+    """out = sum_r y * silu(z * mimo_z) * mimo_down over the rank -> (..., H*P) in y's dtype."""
+    dev = _cuda(y, z, mimo_z, mimo_down)
+    a = _gate_args(y, z, mimo_z, mimo_down)
+    out = torch.empty(*y.shape[:-3], a.channels, dtype=y.dtype, device=dev)
+    a.out = _ptr(out)
+    with torch.cuda.device(dev):
+        _check(lib().m3b_gate_fwd(C.byref(a), _stream(dev)), "m3b_gate_fwd")
+    return out
+
+
+def gate_bwd(y, z, mimo_z, mimo_down, dout):
+    """Gradients of gate_fwd -> (dy like y, dz (..., H*P) contiguous, d_mimo_z, d_mimo_down)."""
+    dev = _cuda(y, z, mimo_z, mimo_down, dout)
+    a = _gate_args(y, z, mimo_z, mimo_down)
+    dout = dout.contiguous()
+    if dout.dtype != y.dtype or dout.numel() != a.rows * a.channels:
+        raise M3bError("gate_bwd: dout of the forward output's shape and dtype expected")
+    dy, dz = torch.empty_like(y), torch.empty(*y.shape[:-3], a.channels, dtype=y.dtype, device=dev)
+    dmz, dmd = torch.empty_like(mimo_z), torch.empty_like(mimo_down)
+    a.dout, a.dy, a.dz, a.d_mimo_z, a.d_mimo_down = _ptr(dout), _ptr(dy), _ptr(dz), _ptr(dmz), _ptr(dmd)
+    L = lib()
+    need = L.m3b_gate_bwd_workspace(C.byref(a))
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(L.m3b_gate_bwd(C.byref(a), _ptr(ws), ws.numel(), _stream(dev)), "m3b_gate_bwd")
+    return dy, dz, dmz, dmd
 
 
 def rmsnorm(x, weight, eps, out=None):

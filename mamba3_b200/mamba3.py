@@ -50,6 +50,33 @@ class RMSNorm(nn.Module):
         return x * inv * self.weight.view(*shape)
 
 
+class _GateFn(torch.autograd.Function):
+    """(y * silu(z * mimo_z) * mimo_down).sum(-1) (mamba3/mamba3.py:234-238) as one kernel each
+    way (``mamba3_b200::gate_fwd`` / ``gate_bwd``): fp32 arithmetic inside, the parameter
+    gradients summed over the rows in a fixed order."""
+
+    @staticmethod
+    def forward(ctx, y, z, mimo_z, mimo_down):
+        ctx.save_for_backward(y, z, mimo_z, mimo_down)
+        return ops.gate_fwd(y, z, mimo_z, mimo_down)
+
+    @staticmethod
+    def backward(ctx, dout):
+        return ops.gate_bwd(*ctx.saved_tensors, dout.contiguous())
+
+
+def _gate(y, z, mimo_z, mimo_down):
+    """y (B,T,H,P,R), z (B,T,H*P) -> (B,T,H*P).  The kernels take one dtype and R <= 4; other
+    combinations (e.g. fp32 parameters with bf16 activations) use the torch expression."""
+    R = mimo_z.shape[-1]
+    if (y.is_cuda and R <= 4 and y.is_contiguous() and z.stride(-1) == 1
+            and len({y.dtype, z.dtype, mimo_z.dtype, mimo_down.dtype}) == 1):
+        return _GateFn.apply(y, z, mimo_z, mimo_down)
+    Bat, T = y.shape[:2]
+    z_r = z.reshape(Bat, T, *mimo_z.shape[:2], 1) * mimo_z
+    return (y * F.silu(z_r) * mimo_down).sum(-1).reshape(Bat, T, -1)
+
+
 def _rope_pairs(t, c, s):
     """Rotate (..., N, R) pairwise along N -- pairs (2i, 2i+1), the same angle for every rank --
     by angles with cosines c and sines s of shape (..., N/2) (mamba3/mamba3.py:38-45)."""
@@ -196,8 +223,7 @@ class KulaMamba(nn.Module):
             x_g, x_b, B_b = x_r, None, None
         out = chunked_ssd(x_g, x_b, B_r, B_b, C_r, dt, A, self.D, x_r, self.chunk_size,
                           return_final_state=return_state)
-        z_r = z.reshape(Bat, T, H, P, 1) * self.mimo_z
-        y = (out.y * F.silu(z_r) * self.mimo_down).sum(-1).reshape(Bat, T, self.d_inner)
+        y = _gate(out.y, z, self.mimo_z, self.mimo_down).reshape(Bat, T, self.d_inner)
         if not return_state:
             return y, None
         angle = cum[:, T - 1].float() if cum is not None else torch.zeros(Bat, H, N // 2, device=proj.device)

@@ -208,6 +208,28 @@ def _(x, h, scale):
     return torch.empty_like(x)
 
 
+@torch.library.custom_op("mamba3_b200::gate_fwd", mutates_args=())
+def gate_fwd(y: torch.Tensor, z: torch.Tensor, mimo_z: torch.Tensor, mimo_down: torch.Tensor) -> torch.Tensor:
+    return _lib.gate_fwd(y, z, mimo_z, mimo_down)
+
+
+@gate_fwd.register_fake
+def _(y, z, mimo_z, mimo_down):
+    return y.new_empty(*y.shape[:-3], y.shape[-3] * y.shape[-2])
+
+
+@torch.library.custom_op("mamba3_b200::gate_bwd", mutates_args=())
+def gate_bwd(y: torch.Tensor, z: torch.Tensor, mimo_z: torch.Tensor, mimo_down: torch.Tensor,
+             dout: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    return _lib.gate_bwd(y, z, mimo_z, mimo_down, dout)
+
+
+@gate_bwd.register_fake
+def _(y, z, mimo_z, mimo_down, dout):
+    return (torch.empty_like(y), y.new_empty(*y.shape[:-3], y.shape[-3] * y.shape[-2]),
+            torch.empty_like(mimo_z), torch.empty_like(mimo_down))
+
+
 def kernel_ok(*ts) -> bool:
     """True when the element-wise block kernels apply: CUDA tensors of one float dtype and shape,
     and no autograd through them (training keeps the torch ops and their backward)."""

@@ -251,3 +251,39 @@ def test_swiglu_and_residual_kernels_match_torch(dtype, n):
     if dtype != torch.float32:
         assert (act == ref).float().mean().item() > 0.99
         assert (res == ref2).float().mean().item() > 0.99
+
+
+@pytest.mark.parametrize("R,rows,dtype", [(1, 300, torch.float32), (2, 1000, torch.float32), (3, 129, torch.float32),
+                                          (4, 257, torch.float32), (2, 1000, torch.bfloat16), (2, 0, torch.float32)])
+def test_gate_kernels_match_torch_autograd(R, rows, dtype):
+    """m3b_gate_fwd / m3b_gate_bwd (the gate and MIMO down-projection of mamba3/mamba3.py:234-238)
+    against torch autograd of (y * silu(z * mimo_z) * mimo_down).sum(-1) in fp64, with z a
+    strided column slice of a wider projection, as in the layer.  Tolerance (max abs error over
+    max abs value): fp32 2e-5; bf16 2e-2 (inputs and outputs rounded to bf16)."""
+    import torch.nn.functional as F
+
+    from mamba3_b200 import _lib
+
+    H, P, W = 3, 40, 3 * 40 + 17
+    g = torch.Generator().manual_seed(R * 1000 + rows)
+    y = torch.randn(rows, H, P, R, generator=g)
+    proj = torch.randn(rows, W, generator=g) * 2
+    mz = 1 + 0.3 * torch.randn(H, P, R, generator=g)
+    md = torch.randn(H, P, R, generator=g) / R
+    dout = torch.randn(rows, H * P, generator=g)
+    dev = [t.to("cuda", dtype) for t in (y, proj, mz, md, dout)]
+    yd, projd, mzd, mdd, doutd = dev
+    out = _lib.gate_fwd(yd, projd[:, : H * P], mzd, mdd)
+    dy, dz, dmz, dmd = _lib.gate_bwd(yd, projd[:, : H * P], mzd, mdd, doutd)
+    ref_in = [t.to("cpu", torch.float64).clone().requires_grad_(True) for t in (yd, projd[:, : H * P], mzd, mdd)]
+    yr, zr, mzr, mdr = ref_in
+    ref = (yr * F.silu(zr.reshape(rows, H, P, 1) * mzr) * mdr).sum(-1).reshape(rows, H * P)
+    ref.backward(doutd.to("cpu", torch.float64))
+    tol = 2e-5 if dtype == torch.float32 else 2e-2
+    if rows == 0:
+        assert out.numel() == 0 and float(dmz.abs().sum()) == 0 and float(dmd.abs().sum()) == 0
+        return
+    assert max_rel(to_np(out), ref.detach().numpy()) < tol
+    for got, want in ((dy, yr.grad), (dz, zr.grad), (dmz, mzr.grad), (dmd, mdr.grad)):
+        assert got.shape == want.shape and got.dtype == dtype
+        assert max_rel(to_np(got), want.numpy()) < tol
