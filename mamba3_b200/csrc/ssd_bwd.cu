@@ -49,6 +49,8 @@ struct BwdParams {
   float* fw;   // (B*H, T, kBwdWarps) per-warp partials of fr_t
   float* dA_bh;  // (B, H)
   float* dD_bh;  // (B, H)
+  float* mT_bh;   // (B, H) <dh_final, h_final>, from the tiled kernel's forward-sweep CTAs
+  float* dDf_bh;  // (B, H) sum dy . x_raw, likewise
 };
 
 // One token's operands in shared memory (floats): Xt [p][j], Bt^T [j][n], C^T [q][n], dy [p][q]
@@ -323,7 +325,9 @@ __global__ void __launch_bounds__(kBwdThreads) ssd_bwd_kernel(BwdParams a) {
 
 // ---------------------------------------------------------------------------------------------
 // Register-tiled variant (P <= 64, N <= 128, R <= 4): the same two sweeps with the state held
-// in registers.  Thread (pb, nb) owns rows p = 4 pb + i (i < 4) and columns n = 8 nb + k
+// in registers, each sweep in its own CTA (the sweeps share nothing but per-token scalars):
+// CTAs [0, B*H) walk the tokens in reverse (G, the larger share of the work, scheduled first),
+// CTAs [B*H, 2*B*H) walk them forward (h), and ssd_bwd_finish_kernel runs the suffix pass.  Thread (pb, nb) owns rows p = 4 pb + i (i < 4) and columns n = 8 nb + k
 // (k < 8) of h / G; lanes carry nbl = lane & 7 and pbl = lane >> 3, warps nbh = warp & 1 and
 // pbh = warp >> 1 (nb = nbl + 8 nbh, pb = pbl + 4 pbh).  Per token the sums over n (dX) and
 // over p (dB, dC) are reduce-scattered across the lanes of a warp with shuffles and finished
@@ -462,7 +466,9 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
   const int P = a.P, N = a.N;
-  const int64_t bh = blockIdx.x;
+  const int64_t nbhs = a.B * a.H;
+  const bool rev_role = (int64_t)blockIdx.x < nbhs;
+  const int64_t bh = rev_role ? (int64_t)blockIdx.x : (int64_t)blockIdx.x - nbhs;
   const int64_t b = bh / a.H;
   const int h = (int)(bh - b * a.H);
   const int64_t TT = a.T;
@@ -483,18 +489,19 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
   for (int e = tid; e < 3 * TP::slot; e += kBwdThreads) slots[e] = 0.f;
   auto ok_pk = [&](int i, int k) { return p0 + i < P && n0 + k < N; };
 
-  // ---------------- forward sweep: h_t, dC_t, e_t, dx_raw, dD ----------------
   float st[4][8];
+  // token operands are fetched two tokens ahead into two register sets that trade roles every
+  // token (so a set is stored one full token after its loads were issued)
+  TokFetch<T> fa, fb;
+  __syncthreads();  // slots zeroed
+  if (!rev_role) {
+  // ---------------- forward sweep: h_t, dC_t, e_t, dx_raw, dD ----------------
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int k = 0; k < 8; ++k)
       st[i][k] = a.h_init && ok_pk(i, k) ? a.h_init[state_base + (int64_t)(p0 + i) * N + n0 + k] : 0.f;
   float dD_acc = 0.f;
-  // token operands are fetched two tokens ahead into two register sets that trade roles every
-  // token (so a set is stored one full token after its loads were issued)
-  TokFetch<T> fa, fb;
-  __syncthreads();  // slots zeroed
   if (TT > 0) {
     tile_fetch<T, R, RI>(a, (b * TT) * a.H + h, true, fa);
     tile_store<T, R, RI>(a, slot(0), true, fa, Aval);
@@ -566,8 +573,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
     fwd_tok(t, fa, fb);
     if (t + 1 < TT) fwd_tok(t + 1, fb, fa);
   }
-  // m_T = <dh_final, h_final>; then G_T = dh_final
-  float mT = 0.f;
+  // m_T = <dh_final, h_final> and this (b, h)'s share of dD, for the suffix pass
   {
     float acc = 0.f;
 #pragma unroll
@@ -576,16 +582,35 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
       for (int k = 0; k < 8; ++k) {
         const float g = a.dh_final && ok_pk(i, k) ? a.dh_final[state_base + (int64_t)(p0 + i) * N + n0 + k] : 0.f;
         acc = fmaf(g, st[i][k], acc);
-        st[i][k] = g;
       }
     acc = warp_sum(acc);
+    dD_acc = warp_sum(dD_acc);
     __syncthreads();  // the last token's reads of the slots and reductions are done
-    if (lane == 0) red[warp] = acc;
+    if (lane == 0) {
+      red[warp] = acc;
+      red[kBwdWarps + warp] = dD_acc;
+    }
     __syncthreads();
-    for (int w = 0; w < kBwdWarps; ++w) mT += red[w];
+    if (tid == 0) {
+      float mT = 0.f, dD = 0.f;
+      for (int w = 0; w < kBwdWarps; ++w) {
+        mT += red[w];
+        dD += red[kBwdWarps + w];
+      }
+      a.mT_bh[bh] = mT;
+      a.dDf_bh[bh] = dD;
+    }
+  }
+  return;
   }
 
   // ---------------- reverse sweep: G_t, dXt_t, dBt_t, fr_t, dh_init ----------------
+  // G_T = dh_final
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      st[i][k] = a.dh_final && ok_pk(i, k) ? a.dh_final[state_base + (int64_t)(p0 + i) * N + n0 + k] : 0.f;
   if (TT > 0) {
     tile_fetch<T, R, RI>(a, (b * TT + TT - 1) * a.H + h, false, fa);
     tile_store<T, R, RI>(a, slot(TT - 1), false, fa, Aval);
@@ -696,8 +721,18 @@ __global__ void __launch_bounds__(kBwdThreads, 2) ssd_bwd_tiled_kernel(BwdParams
       for (int k = 0; k < 8; ++k)
         if (ok_pk(i, k)) a.dh_init[state_base + (int64_t)(p0 + i) * N + n0 + k] = a_next * st[i][k];
   }
-  __syncthreads();  // the last token's reads of the slots are done: the suffix pass reuses them
-  bwd_finish(a, bh, b, h, Aval, mT, dD_acc, ew, fw, slots, red);
+}
+
+// the suffix pass after the tiled kernel's two sweeps, one CTA per (batch row, head)
+__global__ void __launch_bounds__(kBwdThreads) ssd_bwd_finish_kernel(BwdParams a) {
+  __shared__ float suf[kBwdThreads];
+  __shared__ float red[kBwdWarps];
+  const int64_t bh = blockIdx.x;
+  const int64_t b = bh / a.H;
+  const int h = (int)(bh - b * a.H);
+  const float dD = threadIdx.x == 0 ? a.dDf_bh[bh] : 0.f;
+  bwd_finish(a, bh, b, h, ldf(a.A, h, a.ad_dtype), a.mT_bh[bh], dD, a.ew + bh * a.T * kBwdWarps,
+             a.fw + bh * a.T * kBwdWarps, suf, red);
 }
 
 // dA[h] = sum_b dA_bh[b, h], dD likewise, in b order
@@ -715,7 +750,7 @@ __global__ void ssd_bwd_head_sums(const float* __restrict__ dA_bh, const float* 
 }
 
 struct BwdLayout {
-  size_t ew, fw, dA, dD, total;
+  size_t ew, fw, dA, dD, mT, dDf, total;
 };
 
 BwdLayout bwd_layout(const m3b_ssd_bwd_args* a) {
@@ -727,7 +762,9 @@ BwdLayout bwd_layout(const m3b_ssd_bwd_args* a) {
   w.fw = up(tok);
   w.dA = w.fw + up(tok);
   w.dD = w.dA + up(bh * sizeof(float));
-  w.total = w.dD + up(bh * sizeof(float));
+  w.mT = w.dD + up(bh * sizeof(float));
+  w.dDf = w.mT + up(bh * sizeof(float));
+  w.total = w.dDf + up(bh * sizeof(float));
   return w;
 }
 
@@ -747,7 +784,7 @@ int bvalidate(const m3b_ssd_bwd_args* a) {
   if (a->dtype != M3B_BF16 && a->dtype != M3B_F32) return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: dtype");
   if (a->dt_dtype != M3B_F32 && a->dt_dtype != M3B_BF16 && a->dt_dtype != M3B_F16)
     return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: dt dtype");
-  if (a->batch * a->H > 0x7fffffffLL) return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: batch * H too large");
+  if (a->batch * a->H > 0x3fffffffLL) return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: batch * H too large");
   return M3B_OK;
 }
 
@@ -757,8 +794,11 @@ int launch_tiled(const BwdParams& p, unsigned grid, cudaStream_t st) {
   const cudaError_t e =
       cudaFuncSetAttribute(ssd_bwd_tiled_kernel<T, R, RI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "chunked_ssd_bwd: %s", cudaGetErrorString(e));
-  ssd_bwd_tiled_kernel<T, R, RI><<<grid, kBwdThreads, smem, st>>>(p);
-  return check_launch("chunked_ssd_bwd");
+  ssd_bwd_tiled_kernel<T, R, RI><<<2 * grid, kBwdThreads, smem, st>>>(p);
+  const int rc = check_launch("chunked_ssd_bwd");
+  if (rc != M3B_OK) return rc;
+  ssd_bwd_finish_kernel<<<grid, kBwdThreads, 0, st>>>(p);
+  return check_launch("chunked_ssd_bwd_finish");
 }
 
 size_t bwd_smem(const m3b_ssd_bwd_args* a) {
@@ -826,6 +866,8 @@ extern "C" int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* ws, size_t w
   p.fw = reinterpret_cast<float*>(base + w.fw);
   p.dA_bh = reinterpret_cast<float*>(base + w.dA);
   p.dD_bh = reinterpret_cast<float*>(base + w.dD);
+  p.mT_bh = reinterpret_cast<float*>(base + w.mT);
+  p.dDf_bh = reinterpret_cast<float*>(base + w.dDf);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned grid = (unsigned)(a->batch * a->H);
   if (tiled) {
