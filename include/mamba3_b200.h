@@ -344,6 +344,58 @@ M3B_API size_t m3b_gate_bwd_workspace(const m3b_gate_args* a);
 M3B_API int m3b_gate_bwd(const m3b_gate_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * B / C preparation of the layer for the training path (mamba3/mamba3.py:203-232), forward and
+ * backward: RMSNorm over each group's N*R values + bias, broadcast of the G groups to the H
+ * heads, the data-dependent rotation of (n = 2k, 2k+1) pairs by
+ * phi[t, h, k] = -sum_{t' <= t} dt[t', h] theta[t', k]  (rotate != 0), and B_b[t] = B_g[t-1],
+ * B_b[0] = 0  (shift != 0, the trapezoidal rule's previous-token B).
+ * Bf, Cf (batch, seqlen, G*N*R) and theta (batch, seqlen, N/2): rows bc_stride / theta_stride
+ * elements apart (0 = contiguous), so column slices of the input projection pass as they are;
+ * dt (batch, seqlen, H) contiguous, of dt_dtype; wB / wC (N*R) and bB / bC (G, N, R) the norm
+ * weights and biases.  Forward outputs B_g, B_b, C: (batch, seqlen, H, N, R).  Backward inputs
+ * their gradients (dB_b unused without shift); outputs dBf, dCf (batch, seqlen, G*N*R) and
+ * dtheta (batch, seqlen, N/2) contiguous, ddt (batch, seqlen, H) of dt_dtype (rotate only), and
+ * the parameter gradients.  Activations and parameters share `dtype`; fp32 arithmetic; the
+ * sums over heads, tokens and batch rows run in a fixed order.  Needs H*N/2 <= 2048.
+ * Caller-owned workspaces of m3b_bc_fwd_workspace / m3b_bc_bwd_workspace bytes (the backward's
+ * holds one fp32 angle gradient per (token, head, pair) when rotating).
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_bc_args {
+  int64_t batch, seqlen;
+  int32_t H, G, N, R;
+  int32_t rotate, shift;
+  int32_t dtype, dt_dtype;
+  float eps;
+  int64_t bc_stride, theta_stride;
+  const void* Bf;
+  const void* Cf;
+  const void* theta;
+  const void* dt;
+  const void* wB;
+  const void* bB;
+  const void* wC;
+  const void* bC;
+  void* B_g;            /* forward outputs */
+  void* B_b;
+  void* C;
+  const void* dB_g;     /* backward inputs */
+  const void* dB_b;
+  const void* dC;
+  void* dBf;            /* backward outputs */
+  void* dCf;
+  void* dtheta;
+  void* ddt;
+  void* dwB;
+  void* dbB;
+  void* dwC;
+  void* dbC;
+} m3b_bc_args;
+M3B_API size_t m3b_bc_fwd_workspace(const m3b_bc_args* a);
+M3B_API int m3b_bc_fwd(const m3b_bc_args* a, void* workspace, size_t workspace_bytes, void* stream);
+M3B_API size_t m3b_bc_bwd_workspace(const m3b_bc_args* a);
+M3B_API int m3b_bc_bwd(const m3b_bc_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Element-wise steps of the blocks, one pass each, results rounded to `dtype` as the
  * reference's torch ops store them; n elements, out may alias an input.
  *   m3b_swiglu_act: out = silu(g) * u   (SwiGLU.forward, mamba3/block.py:16-26)

@@ -99,6 +99,18 @@ class GateArgs(C.Structure):
                 ("dz", C.c_void_p), ("d_mimo_z", C.c_void_p), ("d_mimo_down", C.c_void_p)]
 
 
+class BcArgs(C.Structure):
+    _fields_ = [("batch", C.c_int64), ("seqlen", C.c_int64), ("H", C.c_int32), ("G", C.c_int32), ("N", C.c_int32),
+                ("R", C.c_int32), ("rotate", C.c_int32), ("shift", C.c_int32), ("dtype", C.c_int32),
+                ("dt_dtype", C.c_int32), ("eps", C.c_float), ("bc_stride", C.c_int64), ("theta_stride", C.c_int64),
+                ("Bf", C.c_void_p), ("Cf", C.c_void_p), ("theta", C.c_void_p), ("dt", C.c_void_p),
+                ("wB", C.c_void_p), ("bB", C.c_void_p), ("wC", C.c_void_p), ("bC", C.c_void_p),
+                ("B_g", C.c_void_p), ("B_b", C.c_void_p), ("C", C.c_void_p), ("dB_g", C.c_void_p),
+                ("dB_b", C.c_void_p), ("dC", C.c_void_p), ("dBf", C.c_void_p), ("dCf", C.c_void_p),
+                ("dtheta", C.c_void_p), ("ddt", C.c_void_p), ("dwB", C.c_void_p), ("dbB", C.c_void_p),
+                ("dwC", C.c_void_p), ("dbC", C.c_void_p)]
+
+
 LAYER_FWD_STAGES = ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out", "last_bx")
 
 
@@ -123,6 +135,10 @@ SIGNATURES = {
     "m3b_gate_fwd": (C.c_int, [C.POINTER(GateArgs), C.c_void_p]),
     "m3b_gate_bwd_workspace": (C.c_size_t, [C.POINTER(GateArgs)]),
     "m3b_gate_bwd": (C.c_int, [C.POINTER(GateArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_bc_fwd_workspace": (C.c_size_t, [C.POINTER(BcArgs)]),
+    "m3b_bc_fwd": (C.c_int, [C.POINTER(BcArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_bc_bwd_workspace": (C.c_size_t, [C.POINTER(BcArgs)]),
+    "m3b_bc_bwd": (C.c_int, [C.POINTER(BcArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_float, C.c_int32,
                               C.c_void_p]),
     "m3b_swiglu_act": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
@@ -351,6 +367,77 @@ def gate_bwd(y, z, mimo_z, mimo_down, dout):
     with torch.cuda.device(dev):
         _check(L.m3b_gate_bwd(C.byref(a), _ptr(ws), ws.numel(), _stream(dev)), "m3b_gate_bwd")
     return dy, dz, dmz, dmd
+
+
+def _row_stride(t, what):
+    """Element stride between the token rows of a (batch, seqlen, width) view with unit inner
+    stride and uniformly spaced rows (a column slice of a contiguous projection)."""
+    Bt, T, _ = t.shape
+    if t.stride(2) != 1 or (Bt > 1 and T > 0 and t.stride(0) != T * t.stride(1)):
+        raise M3bError(f"bc_prep: {what} must have unit inner stride and evenly spaced token rows")
+    return t.stride(1)
+
+
+def _bc_args(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift):
+    G, N, R = bB.shape
+    Bt, T, _ = Bf.shape
+    rotate = theta is not None
+    params = (wB, bB, wC, bC)
+    if (Bf.shape != (Bt, T, G * N * R) or Cf.shape != Bf.shape or wB.numel() != N * R or wC.numel() != N * R
+            or bC.shape != bB.shape or any(t.dtype != Bf.dtype or not t.is_contiguous() for t in params)
+            or Cf.dtype != Bf.dtype or dt.shape != (Bt, T, H) or not dt.is_contiguous()
+            or (rotate and (theta.shape != (Bt, T, N // 2) or theta.dtype != Bf.dtype))):
+        raise M3bError("bc_prep: inconsistent shapes or dtypes")
+    bs = _row_stride(Bf, "Bf")
+    if _row_stride(Cf, "Cf") != bs:
+        raise M3bError("bc_prep: Bf and Cf must share a row stride")
+    ts = _row_stride(theta, "theta") if rotate else 0
+    return BcArgs(Bt, T, H, G, N, R, int(rotate), int(bool(shift)), dtype_code(Bf.dtype), dtype_code(dt.dtype),
+                  float(eps), bs, ts, _ptr(Bf), _ptr(Cf), _ptr(theta), _ptr(dt), _ptr(wB), _ptr(bB), _ptr(wC),
+                  _ptr(bC))
+
+
+def bc_fwd(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift):
+    """B / C preparation (norm + bias, head broadcast, rotation when theta is given, previous-token
+    shift) -> (B_g, B_b or an empty tensor, C), each (batch, seqlen, H, N, R)."""
+    dev = _cuda(Bf, Cf, theta, dt, wB, bB, wC, bC)
+    a = _bc_args(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift)
+    shape = (a.batch, a.seqlen, H, a.N, a.R)
+    Bg, Co = torch.empty(shape, dtype=Bf.dtype, device=dev), torch.empty(shape, dtype=Bf.dtype, device=dev)
+    Bb = torch.empty(shape if shift else (0,), dtype=Bf.dtype, device=dev)
+    a.B_g, a.B_b, a.C = _ptr(Bg), _ptr(Bb) if shift else None, _ptr(Co)
+    L = lib()
+    need = L.m3b_bc_fwd_workspace(C.byref(a))
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(L.m3b_bc_fwd(C.byref(a), _ptr(ws), ws.numel(), _stream(dev)), "m3b_bc_fwd")
+    return Bg, Bb, Co
+
+
+def bc_bwd(Bf, Cf, theta, dt, wB, bB, wC, bC, dB_g, dB_b, dC, H, eps, shift):
+    """Gradients of bc_fwd -> (dBf, dCf, dtheta, ddt, dwB, dbB, dwC, dbC); dtheta / ddt are empty
+    tensors without rotation."""
+    dev = _cuda(Bf, Cf, theta, dt, wB, bB, wC, bC, dB_g, dB_b, dC)
+    a = _bc_args(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift)
+    shape = (a.batch, a.seqlen, H, a.N, a.R)
+    grads = [dB_g, dC] + ([dB_b] if shift else [])
+    if any(g.shape != shape or g.dtype != Bf.dtype or not g.is_contiguous() for g in grads):
+        raise M3bError("bc_bwd: gradients of the forward outputs' shape and dtype, contiguous, expected")
+    rotate = theta is not None
+    dBf = torch.empty(a.batch, a.seqlen, a.G * a.N * a.R, dtype=Bf.dtype, device=dev)
+    dCf = torch.empty_like(dBf)
+    dth = torch.empty((a.batch, a.seqlen, a.N // 2) if rotate else (0,), dtype=Bf.dtype, device=dev)
+    ddt = torch.empty(dt.shape if rotate else (0,), dtype=dt.dtype, device=dev)
+    dwB, dbB, dwC, dbC = (torch.empty_like(t) for t in (wB, bB, wC, bC))
+    a.dB_g, a.dB_b, a.dC = _ptr(dB_g), _ptr(dB_b) if shift else None, _ptr(dC)
+    a.dBf, a.dCf, a.dtheta, a.ddt = _ptr(dBf), _ptr(dCf), _ptr(dth) if rotate else None, _ptr(ddt) if rotate else None
+    a.dwB, a.dbB, a.dwC, a.dbC = _ptr(dwB), _ptr(dbB), _ptr(dwC), _ptr(dbC)
+    L = lib()
+    need = L.m3b_bc_bwd_workspace(C.byref(a))
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(L.m3b_bc_bwd(C.byref(a), _ptr(ws), ws.numel(), _stream(dev)), "m3b_bc_bwd")
+    return dBf, dCf, dth, ddt, dwB, dbB, dwC, dbC
 
 
 def rmsnorm(x, weight, eps, out=None):

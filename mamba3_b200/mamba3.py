@@ -77,6 +77,29 @@ def _gate(y, z, mimo_z, mimo_down):
     return (y * F.silu(z_r) * mimo_down).sum(-1).reshape(Bat, T, -1)
 
 
+class _BCFn(torch.autograd.Function):
+    """RMSNorm + bias of B and C, their broadcast to the heads, the data-dependent rotation and the
+    previous-token shift of B (mamba3/mamba3.py:203-232) as one kernel each way
+    (``mamba3_b200::bc_fwd`` / ``bc_bwd``).  Returns (B_g, B_b, C), B_b empty without shift."""
+
+    @staticmethod
+    def forward(ctx, Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift):
+        ctx.save_for_backward(Bf, Cf, theta, dt, wB, bB, wC, bC)
+        ctx.cfg = (H, eps, shift)
+        return ops.bc_fwd(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift)
+
+    @staticmethod
+    def backward(ctx, dBg, dBb, dC):
+        Bf, Cf, theta, dt, wB, bB, wC, bC = ctx.saved_tensors
+        H, eps, shift = ctx.cfg
+        shape = (*Bf.shape[:2], H, *bB.shape[1:])
+        z = lambda g: torch.zeros(shape, dtype=Bf.dtype, device=Bf.device) if g is None else g.contiguous()  # noqa: E731
+        g = ops.bc_bwd(Bf, Cf, theta, dt, wB, bB, wC, bC, z(dBg), z(dBb) if shift else None, z(dC), H, eps, shift)
+        dBf, dCf, dth, ddt, dwB, dbB, dwC, dbC = g
+        rot = theta is not None
+        return dBf, dCf, dth if rot else None, ddt if rot else None, dwB, dbB, dwC, dbC, None, None, None
+
+
 def _rope_pairs(t, c, s):
     """Rotate (..., N, R) pairwise along N -- pairs (2i, 2i+1), the same angle for every rank --
     by angles with cosines c and sines s of shape (..., N/2) (mamba3/mamba3.py:38-45)."""
@@ -187,8 +210,9 @@ class KulaMamba(nn.Module):
 
     def _ssd_train(self, proj, dt_scale, return_state):
         """Differentiable path between in_proj and out_proj (mamba3/mamba3.py:192-256): torch ops
-        for the split, dt, B/C norm + bias + rotation, MIMO and trapezoid scaling and the gate,
-        around chunked_ssd (forward and backward kernels).  -> y (B,T,d_inner) [, state]."""
+        for the split, dt, MIMO and trapezoid scaling; library kernels (forward and backward) for
+        the B/C norm + bias + rotation + shift (_BCFn), chunked_ssd and the gate (_GateFn).
+        -> y (B,T,d_inner) [, state]."""
         Bat, T, _ = proj.shape
         H, P, N, R, G = self.nheads, self.headdim, self.d_state, self.mimo_rank, self.ngroups
         sizes = [self.d_inner, self._d_x, self._d_bc, self._d_bc, H]
@@ -202,6 +226,46 @@ class KulaMamba(nn.Module):
         if dt_scale is not None:
             dt = dt * dt_scale
         A = -torch.exp(self.A_log)
+        if self._bc_kernel_ok(proj, dt):
+            B_r, B_b, C_r = _BCFn.apply(Bf, Cf, theta, dt, self.B_norm.weight, self.B_bias, self.C_norm.weight,
+                                        self.C_bias, H, self.B_norm.eps, self.use_trapezoidal)
+            cum = None
+            if return_state and self.use_complex_ssm:
+                cum = -(dt.float()[..., None] * theta.float()[..., None, :]).sum(1, keepdim=True)  # (B,1,H,N/2)
+        else:
+            B_r, B_b, C_r, cum = self._bc_torch(Bf, Cf, theta, dt)
+        x_r = xf.reshape(Bat, T, H, P, 1) * self.mimo_x
+        if self.use_trapezoidal:
+            lam = torch.sigmoid(lam_raw)
+            x_g = x_r * lam[..., None, None]
+            scale_b = ((1.0 - lam) * torch.exp(A * dt))[..., None, None]
+            x_b = F.pad(x_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) * scale_b
+        else:
+            x_g, x_b, B_b = x_r, None, None
+        out = chunked_ssd(x_g, x_b, B_r, B_b, C_r, dt, A, self.D, x_r, self.chunk_size,
+                          return_final_state=return_state)
+        y = _gate(out.y, z, self.mimo_z, self.mimo_down).reshape(Bat, T, self.d_inner)
+        if not return_state:
+            return y, None
+        angle = cum[:, -1].float() if cum is not None else torch.zeros(Bat, H, N // 2, device=proj.device)
+        prev_bx = torch.einsum("bhnr,bhpr->bhpn", B_r[:, T - 1], x_r[:, T - 1]).float()
+        return y, {"h": out.h_final.float(), "angle": angle, "prev_BX": prev_bx}
+
+    def _bc_kernel_ok(self, proj, dt):
+        """The B / C kernels apply: CUDA, one float dtype for the projection and the four B / C
+        parameters, equal norm eps, H * N / 2 <= 2048 and the backward's rows in shared memory."""
+        H, N, R, G = self.nheads, self.d_state, self.mimo_rank, self.ngroups
+        ps = (self.B_norm.weight, self.B_bias, self.C_norm.weight, self.C_bias)
+        floats = 10 * G * N * R + 2 * H * N * R + 2 * N * R + 4 * G
+        return (proj.is_cuda and proj.dtype in (torch.float32, torch.bfloat16, torch.float16)
+                and all(p.dtype == proj.dtype for p in ps) and dt.dtype in (torch.float32, torch.bfloat16, torch.float16)
+                and self.B_norm.eps == self.C_norm.eps and H * (N // 2) <= 2048 and floats * 4 <= 200 * 1024)
+
+    def _bc_torch(self, Bf, Cf, theta, dt):
+        """The same as _BCFn in torch ops (mamba3/mamba3.py:203-232) for the cases the kernels
+        do not take.  -> (B_g, B_b or None, C, cum or None)."""
+        Bat, T = Bf.shape[:2]
+        N, R, G = self.d_state, self.mimo_rank, self.ngroups
         B_r = self.B_norm(Bf.reshape(Bat, T, G, N * R)).reshape(Bat, T, G, N, R) + self.B_bias
         C_r = self.C_norm(Cf.reshape(Bat, T, G, N * R)).reshape(Bat, T, G, N, R) + self.C_bias
         if self.heads_per_group > 1:
@@ -212,23 +276,8 @@ class KulaMamba(nn.Module):
             cum = -(dt[..., None] * theta[..., None, :]).cumsum(dim=1)  # (B,T,H,N/2)
             c, s = torch.cos(cum), torch.sin(cum)
             B_r, C_r = _rope_pairs(B_r, c, s), _rope_pairs(C_r, c, s)
-        x_r = xf.reshape(Bat, T, H, P, 1) * self.mimo_x
-        if self.use_trapezoidal:
-            lam = torch.sigmoid(lam_raw)
-            x_g = x_r * lam[..., None, None]
-            scale_b = ((1.0 - lam) * torch.exp(A * dt))[..., None, None]
-            x_b = F.pad(x_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) * scale_b
-            B_b = F.pad(B_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0))
-        else:
-            x_g, x_b, B_b = x_r, None, None
-        out = chunked_ssd(x_g, x_b, B_r, B_b, C_r, dt, A, self.D, x_r, self.chunk_size,
-                          return_final_state=return_state)
-        y = _gate(out.y, z, self.mimo_z, self.mimo_down).reshape(Bat, T, self.d_inner)
-        if not return_state:
-            return y, None
-        angle = cum[:, T - 1].float() if cum is not None else torch.zeros(Bat, H, N // 2, device=proj.device)
-        prev_bx = torch.einsum("bhnr,bhpr->bhpn", B_r[:, T - 1], x_r[:, T - 1]).float()
-        return y, {"h": out.h_final.float(), "angle": angle, "prev_BX": prev_bx}
+        B_b = F.pad(B_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) if self.use_trapezoidal else None
+        return B_r, B_b, C_r, cum
 
     def _ssd(self, x, dt_scale, return_state, state=None):
         if x.dim() != 3 or x.shape[1] <= 0:

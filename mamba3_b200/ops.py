@@ -230,6 +230,38 @@ def _(y, z, mimo_z, mimo_down, dout):
             torch.empty_like(mimo_z), torch.empty_like(mimo_down))
 
 
+@torch.library.custom_op("mamba3_b200::bc_fwd", mutates_args=())
+def bc_fwd(Bf: torch.Tensor, Cf: torch.Tensor, theta: Optional[torch.Tensor], dt: torch.Tensor, wB: torch.Tensor,
+           bB: torch.Tensor, wC: torch.Tensor, bC: torch.Tensor, H: int, eps: float,
+           shift: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return _lib.bc_fwd(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift)
+
+
+@bc_fwd.register_fake
+def _(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift):
+    G, N, R = bB.shape
+    shape = (*Bf.shape[:2], H, N, R)
+    return Bf.new_empty(shape), Bf.new_empty(shape if shift else (0,)), Bf.new_empty(shape)
+
+
+@torch.library.custom_op("mamba3_b200::bc_bwd", mutates_args=())
+def bc_bwd(Bf: torch.Tensor, Cf: torch.Tensor, theta: Optional[torch.Tensor], dt: torch.Tensor, wB: torch.Tensor,
+           bB: torch.Tensor, wC: torch.Tensor, bC: torch.Tensor, dB_g: torch.Tensor, dB_b: Optional[torch.Tensor],
+           dC: torch.Tensor, H: int, eps: float, shift: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor,
+                                                                     torch.Tensor, torch.Tensor, torch.Tensor,
+                                                                     torch.Tensor, torch.Tensor]:
+    return _lib.bc_bwd(Bf, Cf, theta, dt, wB, bB, wC, bC, dB_g, dB_b, dC, H, eps, shift)
+
+
+@bc_bwd.register_fake
+def _(Bf, Cf, theta, dt, wB, bB, wC, bC, dB_g, dB_b, dC, H, eps, shift):
+    G, N, R = bB.shape
+    rot = theta is not None
+    return (Bf.new_empty(*Bf.shape[:2], G * N * R), Bf.new_empty(*Bf.shape[:2], G * N * R),
+            Bf.new_empty((*Bf.shape[:2], N // 2) if rot else (0,)), dt.new_empty(dt.shape if rot else (0,)),
+            torch.empty_like(wB), torch.empty_like(bB), torch.empty_like(wC), torch.empty_like(bC))
+
+
 def kernel_ok(*ts) -> bool:
     """True when the element-wise block kernels apply: CUDA tensors of one float dtype and shape,
     and no autograd through them (training keeps the torch ops and their backward)."""

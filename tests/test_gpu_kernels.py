@@ -287,3 +287,83 @@ def test_gate_kernels_match_torch_autograd(R, rows, dtype):
     for got, want in ((dy, yr.grad), (dz, zr.grad), (dmz, mzr.grad), (dmd, mdr.grad)):
         assert got.shape == want.shape and got.dtype == dtype
         assert max_rel(to_np(got), want.numpy()) < tol
+
+
+def _bc_reference(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift):
+    """B / C preparation of mamba3/mamba3.py:203-232 in torch ops (norm + bias, head broadcast,
+    pairwise rotation by -cumsum(dt theta), previous-token shift)."""
+    import torch.nn.functional as F
+
+    Bt, T, _ = Bf.shape
+    G, N, R = bB.shape
+
+    def norm(x, w, b):
+        x = x.reshape(Bt, T, G, N * R)
+        y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+        return (y.reshape(Bt, T, G, N, R) + b).repeat_interleave(H // G, dim=2)
+
+    Br, Cr = norm(Bf, wB, bB), norm(Cf, wC, bC)
+    if theta is not None:
+        cum = -(dt[..., None] * theta[..., None, :]).cumsum(dim=1)
+        c, s = torch.cos(cum)[..., None], torch.sin(cum)[..., None]
+
+        def rot(t):
+            tp = t.reshape(Bt, T, H, N // 2, 2, R)
+            a, b = tp[..., 0, :], tp[..., 1, :]
+            return torch.stack([a * c - b * s, a * s + b * c], dim=-2).reshape(Bt, T, H, N, R)
+
+        Br, Cr = rot(Br), rot(Cr)
+    Bb = F.pad(Br[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) if shift else None
+    return Br, Bb, Cr
+
+
+@pytest.mark.parametrize("G,H,R,T,rotate,shift,dtype", [
+    (1, 4, 2, 150, True, True, torch.float32), (2, 4, 1, 150, True, True, torch.float32),
+    (1, 3, 2, 64, False, True, torch.float32), (2, 2, 2, 70, True, False, torch.float32),
+    (1, 2, 2, 1, True, True, torch.float32), (1, 4, 2, 150, True, True, torch.bfloat16)])
+def test_bc_kernels_match_torch_autograd(G, H, R, T, rotate, shift, dtype):
+    """m3b_bc_fwd / m3b_bc_bwd against torch autograd of the reference's B / C preparation in
+    fp64, with Bf, Cf and theta column slices of one wider projection (as in the layer) and
+    ragged 64-token chunks.  Tolerance (max abs error over max abs value): fp32 1e-4 (fp32
+    angles of up to ~40 rad), bf16 3e-2 (inputs and outputs rounded to bf16)."""
+    from mamba3_b200 import _lib
+
+    Bt, N, eps = 2, 16, 1e-5
+    gnr, K = G * N * R, N // 2
+    W = 2 * gnr + K + 5
+    g = torch.Generator().manual_seed(G * 100 + H * 10 + T)
+    proj = torch.randn(Bt, T, W, generator=g)
+    dt = torch.rand(Bt, T, H, generator=g) * 0.3
+    wB, wC = 1 + 0.2 * torch.randn(N * R, generator=g), 1 + 0.2 * torch.randn(N * R, generator=g)
+    bB, bC = 1 + 0.2 * torch.randn(G, N, R, generator=g), 1 + 0.2 * torch.randn(G, N, R, generator=g)
+    gouts = [torch.randn(Bt, T, H, N, R, generator=g) for _ in range(3)]
+    dev = [t.to("cuda", dtype) for t in (proj, wB, bB, wC, bC, *gouts)]
+    projd, wBd, bBd, wCd, bCd, gBd, gBbd, gCd = dev
+    dtd = dt.to("cuda", dtype)
+    sl = lambda p: (p[..., :gnr], p[..., gnr:2 * gnr], p[..., 2 * gnr:2 * gnr + K] if rotate else None)  # noqa: E731
+    Bfd, Cfd, thd = sl(projd)
+    Bg, Bb, Co = _lib.bc_fwd(Bfd, Cfd, thd, dtd, wBd, bBd, wCd, bCd, H, eps, shift)
+    grads = _lib.bc_bwd(Bfd, Cfd, thd, dtd, wBd, bBd, wCd, bCd, gBd, gBbd if shift else None, gCd, H, eps, shift)
+
+    f64 = lambda t: t.to("cpu", torch.float64).clone().requires_grad_(True)  # noqa: E731
+    projr, dtr, wBr, bBr, wCr, bCr = (f64(t) for t in (projd, dtd, wBd, bBd, wCd, bCd))
+    Bfr, Cfr, thr = sl(projr)
+    rB, rBb, rC = _bc_reference(Bfr, Cfr, thr, dtr, wBr, bBr, wCr, bCr, H, eps, shift)
+    loss = (rB * gBd.double().cpu()).sum() + (rC * gCd.double().cpu()).sum()
+    if shift:
+        loss = loss + (rBb * gBbd.double().cpu()).sum()
+    loss.backward()
+    tol = 1e-4 if dtype == torch.float32 else 3e-2
+    assert max_rel(to_np(Bg), rB.detach().numpy()) < tol
+    assert max_rel(to_np(Co), rC.detach().numpy()) < tol
+    if shift:
+        assert max_rel(to_np(Bb), rBb.detach().numpy()) < tol
+    dBf, dCf, dth, ddt, dwB, dbB, dwC, dbC = grads
+    pg = projr.grad
+    want = [(dBf, pg[..., :gnr]), (dCf, pg[..., gnr:2 * gnr]), (dwB, wBr.grad), (dbB, bBr.grad),
+            (dwC, wCr.grad), (dbC, bCr.grad)]
+    if rotate:
+        want += [(dth, pg[..., 2 * gnr:2 * gnr + K]), (ddt, dtr.grad)]
+    for i, (got, ref) in enumerate(want):
+        assert got.shape == ref.shape, i
+        assert max_rel(to_np(got), ref.numpy()) < tol, i
