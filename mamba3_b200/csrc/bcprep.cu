@@ -13,6 +13,8 @@
 // and the parameter gradients.  fp32 arithmetic; the angle prefix runs over 64-token chunks
 // (chunk sums first, then each chunk from its start angle).  Every sum has a fixed order (no
 // atomics): results are bitwise reproducible.
+#include <type_traits>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -112,7 +114,38 @@ __device__ __forceinline__ void bc_start_angles(const BcParams& p, int64_t b, in
   }
 }
 
-template <typename T>
+// 2 RV consecutive outputs of one (head, pair) slot, as one store of 2 RV elements (the slot's
+// offset is a multiple of 2 RV elements: aligned for the vector)
+template <typename T, int RV>
+__device__ __forceinline__ void bc_store_slot(T* dst, const float (&v)[2 * RV]) {
+  if constexpr (std::is_same<T, float>::value) {
+    if constexpr (RV == 1) {
+      *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < RV / 2; ++q)
+        reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+  } else {
+    uint32_t w[RV];
+#pragma unroll
+    for (int q = 0; q < RV; ++q) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        __nv_bfloat162 x = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
+        w[q] = *reinterpret_cast<uint32_t*>(&x);
+      } else {
+        __half2 x = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
+        w[q] = *reinterpret_cast<uint32_t*>(&x);
+      }
+    }
+    if constexpr (RV == 1) *reinterpret_cast<uint32_t*>(dst) = w[0];
+    else if constexpr (RV == 2) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// RV: the rank R at compile time (1, 2, 4: vector stores), or 0 (R at run time, scalar stores)
+template <typename T, int RV>
 __global__ void __launch_bounds__(kBcThreads) bc_fwd_kernel(BcParams p) {
   extern __shared__ float4 bc_smem4[];
   float* xB = reinterpret_cast<float*>(bc_smem4);
@@ -148,6 +181,34 @@ __global__ void __launch_bounds__(kBcThreads) bc_fwd_kernel(BcParams p) {
       }
       const int64_t o = (row * p.H + h) * NR;
       const float iB = inv[g], iC = inv[p.G + g];
+      if constexpr (RV > 0) {
+        float vb[2 * RV], vc[2 * RV];
+#pragma unroll
+        for (int r = 0; r < RV; ++r) {
+          const int e0 = 2 * k * RV + r, e1 = e0 + RV;
+          const float a0 = xB[g * NR + e0] * iB * wB[e0] + bB[g * NR + e0];
+          const float a1 = xB[g * NR + e1] * iB * wB[e1] + bB[g * NR + e1];
+          vb[r] = a0 * cs - a1 * sn;
+          vb[RV + r] = a0 * sn + a1 * cs;
+          const float q0 = xC[g * NR + e0] * iC * wC[e0] + bC[g * NR + e0];
+          const float q1 = xC[g * NR + e1] * iC * wC[e1] + bC[g * NR + e1];
+          vc[r] = q0 * cs - q1 * sn;
+          vc[RV + r] = q0 * sn + q1 * cs;
+        }
+        const int64_t so = o + 2 * k * RV;
+        bc_store_slot<T, RV>(Bg + so, vb);
+        bc_store_slot<T, RV>(Co + so, vc);
+        if (p.shift) {
+          if (t + 1 < p.T) bc_store_slot<T, RV>(Bb + so + (int64_t)p.H * NR, vb);
+          if (t == 0) {
+            float zero[2 * RV];
+#pragma unroll
+            for (int q = 0; q < 2 * RV; ++q) zero[q] = 0.f;
+            bc_store_slot<T, RV>(Bb + so, zero);
+          }
+        }
+        continue;
+      }
       for (int r = 0; r < R; ++r) {
         const int e0 = 2 * k * R + r, e1 = e0 + R;
         const float a0 = xB[g * NR + e0] * iB * wB[e0] + bB[g * NR + e0];
@@ -347,29 +408,44 @@ __global__ void __launch_bounds__(kBcThreads) bc_angle_bwd(BcParams p) {
   }
 }
 
-// parameter gradients: the CTA partials summed over (batch row, chunk) in order, the weights
-// also over the groups (group order inside each partial)
+// parameter gradients: the CTA partials summed over (batch row, chunk), the weights also over
+// the groups.  A CTA takes 32 elements; its 8 warps sum the partials q = warp (mod 8), each in
+// q order, and the 8 warp sums are added in warp order: a fixed order for every launch.
+constexpr int kBcSumSegs = kBcWarps;
 template <typename T>
-__global__ void bc_param_sums(BcParams p) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= p.GNR) return;
+__global__ void __launch_bounds__(kBcThreads) bc_param_sums(BcParams p) {
+  __shared__ float red[kBcSumSegs][4][32];
+  const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
+  const int e = blockIdx.x * 32 + lane;
   const int64_t nparts = p.B * p.nchunks;
   float sbB = 0.f, sbC = 0.f, swB = 0.f, swC = 0.f;
-  for (int64_t q = 0; q < nparts; ++q) {
-    const float* pq = p.part + q * 4 * p.GNR;
-    sbB += pq[p.GNR + e];
-    sbC += pq[3 * p.GNR + e];
-    if (e < p.NR)
-      for (int g = 0; g < p.G; ++g) {
-        swB += pq[g * p.NR + e];
-        swC += pq[2 * p.GNR + g * p.NR + e];
-      }
+  if (e < p.GNR) {
+    for (int64_t q = seg; q < nparts; q += kBcSumSegs) {
+      const float* pq = p.part + q * 4 * p.GNR;
+      sbB += pq[p.GNR + e];
+      sbC += pq[3 * p.GNR + e];
+      if (e < p.NR)
+        for (int g = 0; g < p.G; ++g) {
+          swB += pq[g * p.NR + e];
+          swC += pq[2 * p.GNR + g * p.NR + e];
+        }
+    }
   }
-  io<T>::st(static_cast<T*>(p.dbB) + e, sbB);
-  io<T>::st(static_cast<T*>(p.dbC) + e, sbC);
+  red[seg][0][lane] = sbB;
+  red[seg][1][lane] = sbC;
+  red[seg][2][lane] = swB;
+  red[seg][3][lane] = swC;
+  __syncthreads();
+  if (seg != 0 || e >= p.GNR) return;
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int w = 0; w < kBcSumSegs; ++w)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s[k] += red[w][k][lane];
+  io<T>::st(static_cast<T*>(p.dbB) + e, s[0]);
+  io<T>::st(static_cast<T*>(p.dbC) + e, s[1]);
   if (e < p.NR) {
-    io<T>::st(static_cast<T*>(p.dwB) + e, swB);
-    io<T>::st(static_cast<T*>(p.dwC) + e, swC);
+    io<T>::st(static_cast<T*>(p.dwB) + e, s[2]);
+    io<T>::st(static_cast<T*>(p.dwC) + e, s[3]);
   }
 }
 
@@ -495,8 +571,18 @@ int bc_run_t(const BcParams& p, bool bwd, cudaStream_t st) {
   }
   if (!bwd) {
     const size_t smem = fwd_smem(p);
-    cudaFuncSetAttribute(bc_fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    bc_fwd_kernel<T><<<grid, kBcThreads, smem, st>>>(p);
+    auto launch = [&](auto kern) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      kern<<<grid, kBcThreads, smem, st>>>(p);
+    };
+    // vector stores need 16-byte aligned output buffers (each slot is then aligned as well)
+    const bool al = aligned16(p.B_g) && aligned16(p.C) && (!p.shift || aligned16(p.B_b));
+    switch (al ? p.R : 0) {
+      case 1: launch(bc_fwd_kernel<T, 1>); break;
+      case 2: launch(bc_fwd_kernel<T, 2>); break;
+      case 4: launch(bc_fwd_kernel<T, 4>); break;
+      default: launch(bc_fwd_kernel<T, 0>); break;
+    }
     return check_launch("bc_fwd");
   }
   const size_t smem = bwd_smem(p);
@@ -508,7 +594,7 @@ int bc_run_t(const BcParams& p, bool bwd, cudaStream_t st) {
     bc_angle_bwd<T><<<grid, kBcThreads, s2, st>>>(p);
     if ((rc = check_launch("bc_angle_bwd")) != M3B_OK) return rc;
   }
-  bc_param_sums<T><<<(unsigned)((p.GNR + 255) / 256), 256, 0, st>>>(p);
+  bc_param_sums<T><<<(unsigned)((p.GNR + 31) / 32), kBcThreads, 0, st>>>(p);
   return check_launch("bc_param_sums");
 }
 

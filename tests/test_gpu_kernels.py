@@ -320,7 +320,9 @@ def _bc_reference(Bf, Cf, theta, dt, wB, bB, wC, bC, H, eps, shift):
 @pytest.mark.parametrize("G,H,R,T,rotate,shift,dtype", [
     (1, 4, 2, 150, True, True, torch.float32), (2, 4, 1, 150, True, True, torch.float32),
     (1, 3, 2, 64, False, True, torch.float32), (2, 2, 2, 70, True, False, torch.float32),
-    (1, 2, 2, 1, True, True, torch.float32), (1, 4, 2, 150, True, True, torch.bfloat16)])
+    (1, 2, 2, 1, True, True, torch.float32), (1, 2, 4, 100, True, True, torch.float32),
+    (1, 2, 3, 100, True, True, torch.float32), (1, 4, 2, 150, True, True, torch.bfloat16),
+    (1, 2, 4, 100, True, True, torch.bfloat16)])
 def test_bc_kernels_match_torch_autograd(G, H, R, T, rotate, shift, dtype):
     """m3b_bc_fwd / m3b_bc_bwd against torch autograd of the reference's B / C preparation in
     fp64, with Bf, Cf and theta column slices of one wider projection (as in the layer) and
