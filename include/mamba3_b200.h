@@ -396,6 +396,46 @@ M3B_API size_t m3b_bc_bwd_workspace(const m3b_bc_args* a);
 M3B_API int m3b_bc_bwd(const m3b_bc_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * MIMO expansion and trapezoid weights of x for the training path (mamba3/mamba3.py:218-230),
+ * forward and backward:
+ *   x_raw[t,h,p,r] = xf[t,h,p] mimo_x[h,p,r];  with trapezoidal != 0, lam = sigmoid(lam_raw),
+ *   x_g[t] = x_raw[t] lam[t],  x_b[t] = x_raw[t-1] (1 - lam[t]) exp(A dt[t]),  x_b[0] = 0.
+ * xf (batch, seqlen, H*P) and lam_raw (batch, seqlen, H): rows x_stride / lam_stride elements
+ * apart (0 = contiguous), so column slices of the input projection pass as they are; dt
+ * (batch, seqlen, H) contiguous of dt_dtype; A (H) of a_dtype (A = -exp(A_log)); mimo_x
+ * (H, P, R).  Outputs (batch, seqlen, H, P, R).  The backward takes the gradients of x_raw,
+ * x_g, x_b and gives dxf (batch, seqlen, H*P) contiguous, dmimo_x, and with trapezoidal
+ * dlam_raw (batch, seqlen, H), ddt (dt's share through the weights) and dA.  Needs P <= 256,
+ * R <= 4; fp32 arithmetic; fixed-order sums; caller-owned workspace of
+ * m3b_xprep_bwd_workspace bytes for the backward.
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_xprep_args {
+  int64_t batch, seqlen;
+  int32_t H, P, R, trapezoidal;
+  int32_t dtype, dt_dtype, a_dtype;
+  int64_t x_stride, lam_stride;
+  const void* xf;
+  const void* mimo_x;
+  const void* lam_raw;
+  const void* dt;
+  const void* A;
+  void* x_raw;          /* forward outputs */
+  void* x_g;
+  void* x_b;
+  const void* dx_raw;   /* backward inputs */
+  const void* dx_g;
+  const void* dx_b;
+  void* dxf;            /* backward outputs */
+  void* dmimo_x;
+  void* dlam_raw;
+  void* ddt;
+  void* dA;
+} m3b_xprep_args;
+M3B_API int m3b_xprep_fwd(const m3b_xprep_args* a, void* stream);
+M3B_API size_t m3b_xprep_bwd_workspace(const m3b_xprep_args* a);
+M3B_API int m3b_xprep_bwd(const m3b_xprep_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Element-wise steps of the blocks, one pass each, results rounded to `dtype` as the
  * reference's torch ops store them; n elements, out may alias an input.
  *   m3b_swiglu_act: out = silu(g) * u   (SwiGLU.forward, mamba3/block.py:16-26)

@@ -111,6 +111,16 @@ class BcArgs(C.Structure):
                 ("dwC", C.c_void_p), ("dbC", C.c_void_p)]
 
 
+class XprepArgs(C.Structure):
+    _fields_ = [("batch", C.c_int64), ("seqlen", C.c_int64), ("H", C.c_int32), ("P", C.c_int32), ("R", C.c_int32),
+                ("trapezoidal", C.c_int32), ("dtype", C.c_int32), ("dt_dtype", C.c_int32), ("a_dtype", C.c_int32),
+                ("x_stride", C.c_int64), ("lam_stride", C.c_int64), ("xf", C.c_void_p), ("mimo_x", C.c_void_p),
+                ("lam_raw", C.c_void_p), ("dt", C.c_void_p), ("A", C.c_void_p), ("x_raw", C.c_void_p),
+                ("x_g", C.c_void_p), ("x_b", C.c_void_p), ("dx_raw", C.c_void_p), ("dx_g", C.c_void_p),
+                ("dx_b", C.c_void_p), ("dxf", C.c_void_p), ("dmimo_x", C.c_void_p), ("dlam_raw", C.c_void_p),
+                ("ddt", C.c_void_p), ("dA", C.c_void_p)]
+
+
 LAYER_FWD_STAGES = ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out", "last_bx")
 
 
@@ -139,6 +149,9 @@ SIGNATURES = {
     "m3b_bc_fwd": (C.c_int, [C.POINTER(BcArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_bc_bwd_workspace": (C.c_size_t, [C.POINTER(BcArgs)]),
     "m3b_bc_bwd": (C.c_int, [C.POINTER(BcArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "m3b_xprep_fwd": (C.c_int, [C.POINTER(XprepArgs), C.c_void_p]),
+    "m3b_xprep_bwd_workspace": (C.c_size_t, [C.POINTER(XprepArgs)]),
+    "m3b_xprep_bwd": (C.c_int, [C.POINTER(XprepArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_float, C.c_int32,
                               C.c_void_p]),
     "m3b_swiglu_act": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
@@ -438,6 +451,60 @@ def bc_bwd(Bf, Cf, theta, dt, wB, bB, wC, bC, dB_g, dB_b, dC, H, eps, shift):
     with torch.cuda.device(dev):
         _check(L.m3b_bc_bwd(C.byref(a), _ptr(ws), ws.numel(), _stream(dev)), "m3b_bc_bwd")
     return dBf, dCf, dth, ddt, dwB, dbB, dwC, dbC
+
+
+def _xprep_args(xf, mimo_x, lam_raw, dt, A):
+    H, P, R = mimo_x.shape
+    Bt, T, _ = xf.shape
+    trap = lam_raw is not None
+    if (xf.shape[2] != H * P or mimo_x.dtype != xf.dtype or not mimo_x.is_contiguous()
+            or (trap and (lam_raw.shape != (Bt, T, H) or lam_raw.dtype != xf.dtype or dt.shape != (Bt, T, H)
+                          or not dt.is_contiguous() or A.shape != (H,) or not A.is_contiguous()))):
+        raise M3bError("xprep: inconsistent shapes or dtypes")
+    return XprepArgs(Bt, T, H, P, R, int(trap), dtype_code(xf.dtype), dtype_code(dt.dtype) if trap else 0,
+                     dtype_code(A.dtype) if trap else 0, _row_stride(xf, "xf"),
+                     _row_stride(lam_raw, "lam_raw") if trap else 0, _ptr(xf), _ptr(mimo_x),
+                     _ptr(lam_raw), _ptr(dt) if trap else None, _ptr(A) if trap else None)
+
+
+def xprep_fwd(xf, mimo_x, lam_raw, dt, A):
+    """x_raw = xf * mimo_x per rank; with lam_raw also x_g and x_b (trapezoid weights) ->
+    (x_raw, x_g, x_b), each (batch, seqlen, H, P, R); x_g / x_b empty without lam_raw."""
+    dev = _cuda(xf, mimo_x, lam_raw, dt, A)
+    a = _xprep_args(xf, mimo_x, lam_raw, dt, A)
+    shape = (a.batch, a.seqlen, a.H, a.P, a.R)
+    trap = lam_raw is not None
+    outs = [torch.empty(shape if (i == 0 or trap) else (0,), dtype=xf.dtype, device=dev) for i in range(3)]
+    a.x_raw, a.x_g, a.x_b = _ptr(outs[0]), _ptr(outs[1]) if trap else None, _ptr(outs[2]) if trap else None
+    with torch.cuda.device(dev):
+        _check(lib().m3b_xprep_fwd(C.byref(a), _stream(dev)), "m3b_xprep_fwd")
+    return tuple(outs)
+
+
+def xprep_bwd(xf, mimo_x, lam_raw, dt, A, dx_raw, dx_g, dx_b):
+    """Gradients of xprep_fwd -> (dxf, dmimo_x, dlam_raw, ddt, dA); the last three empty without
+    lam_raw."""
+    dev = _cuda(xf, mimo_x, lam_raw, dt, A, dx_raw, dx_g, dx_b)
+    a = _xprep_args(xf, mimo_x, lam_raw, dt, A)
+    shape = (a.batch, a.seqlen, a.H, a.P, a.R)
+    trap = lam_raw is not None
+    grads = [dx_raw] + ([dx_g, dx_b] if trap else [])
+    if any(g.shape != shape or g.dtype != xf.dtype or not g.is_contiguous() for g in grads):
+        raise M3bError("xprep_bwd: gradients of the forward outputs' shape and dtype, contiguous, expected")
+    dxf = torch.empty(a.batch, a.seqlen, a.H * a.P, dtype=xf.dtype, device=dev)
+    dmx = torch.empty_like(mimo_x)
+    dlam = torch.empty((a.batch, a.seqlen, a.H) if trap else (0,), dtype=xf.dtype, device=dev)
+    ddt = torch.empty(dt.shape if trap else (0,), dtype=dt.dtype, device=dev)
+    dA = torch.empty(A.shape if trap else (0,), dtype=A.dtype, device=dev)
+    a.dx_raw, a.dx_g, a.dx_b = _ptr(dx_raw), _ptr(dx_g) if trap else None, _ptr(dx_b) if trap else None
+    a.dxf, a.dmimo_x = _ptr(dxf), _ptr(dmx)
+    a.dlam_raw, a.ddt, a.dA = (_ptr(dlam), _ptr(ddt), _ptr(dA)) if trap else (None, None, None)
+    L = lib()
+    need = L.m3b_xprep_bwd_workspace(C.byref(a))
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(L.m3b_xprep_bwd(C.byref(a), _ptr(ws), ws.numel(), _stream(dev)), "m3b_xprep_bwd")
+    return dxf, dmx, dlam, ddt, dA
 
 
 def rmsnorm(x, weight, eps, out=None):

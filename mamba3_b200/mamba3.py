@@ -100,6 +100,28 @@ class _BCFn(torch.autograd.Function):
         return dBf, dCf, dth if rot else None, ddt if rot else None, dwB, dbB, dwC, dbC, None, None, None
 
 
+class _XFn(torch.autograd.Function):
+    """x_raw = xf * mimo_x and, with the trapezoid, x_g = x_raw * lam and x_b = shifted x_raw *
+    (1 - lam) exp(A dt) (mamba3/mamba3.py:218-230) as one kernel each way
+    (``mamba3_b200::xprep_fwd`` / ``xprep_bwd``).  Returns (x_raw, x_g, x_b), the last two
+    empty without the trapezoid."""
+
+    @staticmethod
+    def forward(ctx, xf, mimo_x, lam_raw, dt, A):
+        ctx.save_for_backward(xf, mimo_x, lam_raw, dt, A)
+        return ops.xprep_fwd(xf, mimo_x, lam_raw, dt, A)
+
+    @staticmethod
+    def backward(ctx, dxr, dxg, dxb):
+        xf, mimo_x, lam_raw, dt, A = ctx.saved_tensors
+        trap = lam_raw is not None
+        shape = (*xf.shape[:2], *mimo_x.shape)
+        z = lambda g: torch.zeros(shape, dtype=xf.dtype, device=xf.device) if g is None else g.contiguous()  # noqa: E731
+        dxf, dmx, dlam, ddt, dA = ops.xprep_bwd(xf, mimo_x, lam_raw, dt, A, z(dxr), z(dxg) if trap else None,
+                                                z(dxb) if trap else None)
+        return (dxf, dmx, dlam, ddt, dA) if trap else (dxf, dmx, None, None, None)
+
+
 def _rope_pairs(t, c, s):
     """Rotate (..., N, R) pairwise along N -- pairs (2i, 2i+1), the same angle for every rank --
     by angles with cosines c and sines s of shape (..., N/2) (mamba3/mamba3.py:38-45)."""
@@ -212,6 +234,7 @@ class KulaMamba(nn.Module):
         """Differentiable path between in_proj and out_proj (mamba3/mamba3.py:192-256): torch ops
         for the split, dt, MIMO and trapezoid scaling; library kernels (forward and backward) for
         the B/C norm + bias + rotation + shift (_BCFn), chunked_ssd and the gate (_GateFn).
+        The x-side MIMO expansion and trapezoid weights run as one kernel each way (_XFn).
         -> y (B,T,d_inner) [, state]."""
         Bat, T, _ = proj.shape
         H, P, N, R, G = self.nheads, self.headdim, self.d_state, self.mimo_rank, self.ngroups
@@ -234,14 +257,19 @@ class KulaMamba(nn.Module):
                 cum = -(dt.float()[..., None] * theta.float()[..., None, :]).sum(1, keepdim=True)  # (B,1,H,N/2)
         else:
             B_r, B_b, C_r, cum = self._bc_torch(Bf, Cf, theta, dt)
-        x_r = xf.reshape(Bat, T, H, P, 1) * self.mimo_x
-        if self.use_trapezoidal:
-            lam = torch.sigmoid(lam_raw)
-            x_g = x_r * lam[..., None, None]
-            scale_b = ((1.0 - lam) * torch.exp(A * dt))[..., None, None]
-            x_b = F.pad(x_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) * scale_b
+        if self._x_kernel_ok(proj, dt, A):
+            x_r, x_g, x_b = _XFn.apply(xf, self.mimo_x, lam_raw, dt, A)
+            if not self.use_trapezoidal:
+                x_g, x_b, B_b = x_r, None, None
         else:
-            x_g, x_b, B_b = x_r, None, None
+            x_r = xf.reshape(Bat, T, H, P, 1) * self.mimo_x
+            if self.use_trapezoidal:
+                lam = torch.sigmoid(lam_raw)
+                x_g = x_r * lam[..., None, None]
+                scale_b = ((1.0 - lam) * torch.exp(A * dt))[..., None, None]
+                x_b = F.pad(x_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) * scale_b
+            else:
+                x_g, x_b, B_b = x_r, None, None
         out = chunked_ssd(x_g, x_b, B_r, B_b, C_r, dt, A, self.D, x_r, self.chunk_size,
                           return_final_state=return_state)
         y = _gate(out.y, z, self.mimo_z, self.mimo_down).reshape(Bat, T, self.d_inner)
@@ -250,6 +278,12 @@ class KulaMamba(nn.Module):
         angle = cum[:, -1].float() if cum is not None else torch.zeros(Bat, H, N // 2, device=proj.device)
         prev_bx = torch.einsum("bhnr,bhpr->bhpn", B_r[:, T - 1], x_r[:, T - 1]).float()
         return y, {"h": out.h_final.float(), "angle": angle, "prev_BX": prev_bx}
+
+    def _x_kernel_ok(self, proj, dt, A):
+        """The x kernels apply: CUDA, mimo_x of the projection's float dtype, P <= 256, R <= 4."""
+        fl = (torch.float32, torch.bfloat16, torch.float16)
+        return (proj.is_cuda and proj.dtype in fl and self.mimo_x.dtype == proj.dtype and dt.dtype in fl
+                and A.dtype in fl and self.headdim <= 256 and self.mimo_rank <= 4)
 
     def _bc_kernel_ok(self, proj, dt):
         """The B / C kernels apply: CUDA, one float dtype for the projection and the four B / C

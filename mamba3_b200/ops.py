@@ -262,6 +262,35 @@ def _(Bf, Cf, theta, dt, wB, bB, wC, bC, dB_g, dB_b, dC, H, eps, shift):
             torch.empty_like(wB), torch.empty_like(bB), torch.empty_like(wC), torch.empty_like(bC))
 
 
+@torch.library.custom_op("mamba3_b200::xprep_fwd", mutates_args=())
+def xprep_fwd(xf: torch.Tensor, mimo_x: torch.Tensor, lam_raw: Optional[torch.Tensor], dt: torch.Tensor,
+              A: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return _lib.xprep_fwd(xf, mimo_x, lam_raw, dt, A)
+
+
+@xprep_fwd.register_fake
+def _(xf, mimo_x, lam_raw, dt, A):
+    shape = (*xf.shape[:2], *mimo_x.shape)
+    other = shape if lam_raw is not None else (0,)
+    return xf.new_empty(shape), xf.new_empty(other), xf.new_empty(other)
+
+
+@torch.library.custom_op("mamba3_b200::xprep_bwd", mutates_args=())
+def xprep_bwd(xf: torch.Tensor, mimo_x: torch.Tensor, lam_raw: Optional[torch.Tensor], dt: torch.Tensor,
+              A: torch.Tensor, dx_raw: torch.Tensor, dx_g: Optional[torch.Tensor],
+              dx_b: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                     torch.Tensor]:
+    return _lib.xprep_bwd(xf, mimo_x, lam_raw, dt, A, dx_raw, dx_g, dx_b)
+
+
+@xprep_bwd.register_fake
+def _(xf, mimo_x, lam_raw, dt, A, dx_raw, dx_g, dx_b):
+    trap = lam_raw is not None
+    return (xf.new_empty(*xf.shape[:2], mimo_x.shape[0] * mimo_x.shape[1]), torch.empty_like(mimo_x),
+            xf.new_empty(dt.shape if trap else (0,)), dt.new_empty(dt.shape if trap else (0,)),
+            A.new_empty(A.shape if trap else (0,)))
+
+
 def kernel_ok(*ts) -> bool:
     """True when the element-wise block kernels apply: CUDA tensors of one float dtype and shape,
     and no autograd through them (training keeps the torch ops and their backward)."""

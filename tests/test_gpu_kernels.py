@@ -369,3 +369,55 @@ def test_bc_kernels_match_torch_autograd(G, H, R, T, rotate, shift, dtype):
     for i, (got, ref) in enumerate(want):
         assert got.shape == ref.shape, i
         assert max_rel(to_np(got), ref.numpy()) < tol, i
+
+
+@pytest.mark.parametrize("H,P,R,T,trap,dtype", [
+    (4, 16, 2, 150, True, torch.float32), (3, 48, 1, 70, True, torch.float32), (2, 64, 4, 65, True, torch.float32),
+    (4, 16, 3, 1, True, torch.float32), (4, 16, 2, 100, False, torch.float32), (4, 64, 2, 130, True, torch.bfloat16)])
+def test_xprep_kernels_match_torch_autograd(H, P, R, T, trap, dtype):
+    """m3b_xprep_fwd / m3b_xprep_bwd against torch autograd of the reference's x-side MIMO
+    expansion and trapezoid weights (mamba3/mamba3.py:218-230) in fp64, with xf and lam_raw
+    column slices of a wider projection; P = 48 leaves CTAs with part of a 256-channel block
+    unused, and 64-row chunks cross sequence boundaries.  Tolerance (max abs error over max abs
+    value): fp32 1e-5, bf16 2e-2."""
+    import torch.nn.functional as F
+
+    from mamba3_b200 import _lib
+
+    Bt, C = 2, H * P
+    W = C + H + 3
+    g = torch.Generator().manual_seed(H * 1000 + P * 10 + T)
+    proj = torch.randn(Bt, T, W, generator=g)
+    dt = torch.rand(Bt, T, H, generator=g) * 0.3
+    A = -torch.rand(H, generator=g) * 2
+    mx = 1 + 0.3 * torch.randn(H, P, R, generator=g)
+    gouts = [torch.randn(Bt, T, H, P, R, generator=g) for _ in range(3)]
+    projd, dtd, Ad, mxd, g0, g1, g2 = (t.to("cuda", dtype) for t in (proj, dt, A, mx, *gouts))
+    sl = lambda p: (p[..., :C], p[..., C:C + H] if trap else None)  # noqa: E731
+    xfd, lrd = sl(projd)
+    xr, xg, xb = _lib.xprep_fwd(xfd, mxd, lrd, dtd, Ad)
+    dxf, dmx, dlam, ddt, dA = _lib.xprep_bwd(xfd, mxd, lrd, dtd, Ad, g0, g1 if trap else None,
+                                             g2 if trap else None)
+
+    f64 = lambda t: t.to("cpu", torch.float64).clone().requires_grad_(True)  # noqa: E731
+    projr, dtr, Ar, mxr = (f64(t) for t in (projd, dtd, Ad, mxd))
+    xfr, lrr = sl(projr)
+    rr = xfr.reshape(Bt, T, H, P, 1) * mxr
+    loss = (rr * g0.double().cpu()).sum()
+    outs = [(xr, rr)]
+    if trap:
+        lam = torch.sigmoid(lrr)
+        rg = rr * lam[..., None, None]
+        rb = F.pad(rr[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) * ((1 - lam) * torch.exp(Ar * dtr))[..., None, None]
+        loss = loss + (rg * g1.double().cpu()).sum() + (rb * g2.double().cpu()).sum()
+        outs += [(xg, rg), (xb, rb)]
+    loss.backward()
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    for got, ref in outs:
+        assert max_rel(to_np(got), ref.detach().numpy()) < tol
+    want = [(dxf, projr.grad[..., :C]), (dmx, mxr.grad)]
+    if trap:
+        want += [(dlam, projr.grad[..., C:C + H]), (ddt, dtr.grad), (dA, Ar.grad)]
+    for i, (got, ref) in enumerate(want):
+        assert got.shape == ref.shape, i
+        assert max_rel(to_np(got), ref.numpy()) < tol, i
