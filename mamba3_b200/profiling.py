@@ -89,3 +89,40 @@ class ClockSampler:
         reasons = sorted(n for b, n in _REASONS.items() if bits & b and n != "gpu_idle")
         return {"sm_mhz": statistics.median(sms), "sm_max_mhz": self.max_sm, "reasons": reasons,
                 "samples": len(sms), "power_w_max": round(max(s[3] for s in self.samples), 1)}
+
+
+def train_step_profile(batch: int = 16, seqlen: int = 4096, rows: int = 24) -> str:
+    """Per-kernel device time of one config-1 KulaMamba training step (forward + backward,
+    bf16, random init, synthetic input) from torch's profiler, after three warm-up steps.  For
+    reading where the time goes; the bench's training-step figure is timed without a profiler."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from .mamba3 import KulaMamba
+
+    torch.manual_seed(0)
+    layer = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).train()
+    x = torch.randn(batch, seqlen, 768, device="cuda").to(torch.bfloat16)
+
+    def step():
+        layer.zero_grad(set_to_none=True)
+        layer(x).float().sum().backward()
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    return prof.key_averages().table(sort_by="self_cuda_time_total", row_limit=rows, max_name_column_width=72)
+
+
+if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser(description="profiling helpers")
+    ap.add_argument("what", choices=["train"])
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--seqlen", type=int, default=4096)
+    args = ap.parse_args()
+    print(train_step_profile(args.batch, args.seqlen))
