@@ -9,8 +9,9 @@
 //   dlam_raw = dlam lam (1 - lam),  with ds = sum_{p,r} dx_b x_raw[t-1] (1 - lam) e:
 //   ddt = ds A,  dA = sum over rows of ds dt.
 // A CTA covers whole heads (floor(256 / P) of them, one thread per channel) and a chunk of 64
-// rows; the sums over (p, r) of a row run in shared memory in channel order, the sums over rows
-// per chunk and then over chunks in chunk order: no atomics, bitwise reproducible.  fp32
+// rows; the sums over (p, r) of a row run by warp shuffles and shared memory (or, when P is not
+// a multiple of 32, in channel order by one thread per head), the sums over rows per chunk and
+// then over chunks in chunk order: no atomics, bitwise reproducible.  fp32
 // arithmetic; torch builds these with a dozen broadcast passes over (B, T, H, P, R) tensors.
 #include "common.cuh"
 #include "launch.h"
@@ -126,12 +127,31 @@ __global__ void __launch_bounds__(kXThreads) xprep_bwd_kernel(XParams p) {
       io<T>::st(static_cast<T*>(p.dxf) + row * p.C + c, dxf);
     }
     if (p.trap) {
-      sl[tid] = gl * x;
-      ss[tid] = gs * xprev;
+      // per head: the sums over its P channels -- by warp shuffles when whole warps fall in a
+      // head (P a multiple of 32; then the warp sums in warp order), else one thread in channel order
+      const bool by_warp = p.P % 32 == 0;
+      int q0 = tid * p.P, q1 = (tid + 1) * p.P;
+      if (by_warp) {
+        float u = gl * x, v = gs * xprev;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          u += __shfl_xor_sync(0xffffffffu, u, off);
+          v += __shfl_xor_sync(0xffffffffu, v, off);
+        }
+        if ((tid & 31) == 0) {
+          sl[tid >> 5] = u;
+          ss[tid >> 5] = v;
+        }
+        q0 = tid * (p.P / 32);
+        q1 = (tid + 1) * (p.P / 32);
+      } else {
+        sl[tid] = gl * x;
+        ss[tid] = gs * xprev;
+      }
       __syncthreads();
       if (fin) {
         float DL = 0.f, DS = 0.f;
-        for (int q = tid * p.P; q < (tid + 1) * p.P; ++q) {
+        for (int q = q0; q < q1; ++q) {
           DL += sl[q];
           DS += ss[q];
         }
