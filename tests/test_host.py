@@ -53,6 +53,36 @@ def test_library_rejects_bad_args_without_gpu():
     assert b"null" in L.m3b_last_error()
 
 
+def test_training_entry_points_reject_bad_arguments_without_a_gpu():
+    """The training-path entry points (gate, B / C preparation, x-side weights) validate their
+    arguments on the host and report an error code and message before touching the device:
+    null structs and pointers, odd N, oversized P, ranks past the kernels' limit."""
+    import ctypes
+
+    from mamba3_b200 import _lib
+
+    L = _lib.lib()
+    assert L.m3b_gate_fwd(None, None) == 1
+    g = _lib.GateArgs(10, 0, 8, 2, 0)  # rows, z_stride, channels, R, dtype; no pointers
+    assert L.m3b_gate_fwd(ctypes.byref(g), None) == 1 and b"null" in L.m3b_last_error()
+    assert L.m3b_gate_bwd(ctypes.byref(g), None, 0, None) == 1
+    assert L.m3b_gate_bwd_workspace(ctypes.byref(g)) == 1 * 8 * 2 * 2 * 4  # one 128-row chunk of partials
+    assert L.m3b_bc_fwd(None, None, 0, None) == 1
+    bc = _lib.BcArgs(1, 0, 4, 1, 15, 2, 1, 1, 0, 0, 1e-5)  # N = 15: odd
+    assert L.m3b_bc_fwd_workspace(ctypes.byref(bc)) == 0
+    assert L.m3b_bc_fwd(ctypes.byref(bc), None, 0, None) == 1 and b"even" in L.m3b_last_error()
+    bc = _lib.BcArgs(1, 4, 4, 1, 16, 2, 1, 1, 0, 0, 1e-5)  # tokens but no pointers
+    assert L.m3b_bc_bwd(ctypes.byref(bc), None, 0, None) == 1 and b"null" in L.m3b_last_error()
+    bc = _lib.BcArgs(1, 4, 64, 1, 128, 2, 1, 1, 0, 0, 1e-5)  # H * N / 2 = 4096 > 2048
+    assert L.m3b_bc_fwd(ctypes.byref(bc), None, 0, None) == 2  # M3B_ERR_UNSUPPORTED
+    assert L.m3b_xprep_fwd(None, None) == 1
+    xp = _lib.XprepArgs(1, 4, 2, 300, 2, 1, 0, 0, 0)  # P = 300 > 256
+    assert L.m3b_xprep_fwd(ctypes.byref(xp), None) == 2 and b"P <= 256" in L.m3b_last_error()
+    xp = _lib.XprepArgs(1, 4, 2, 64, 5, 1, 0, 0, 0)  # R = 5 > 4
+    assert L.m3b_xprep_bwd_workspace(ctypes.byref(xp)) == 0
+    assert L.m3b_xprep_bwd(ctypes.byref(xp), None, 0, None) == 2
+
+
 @pytest.mark.parametrize("case", ["default", "rank1", "ngroups2", "euler", "real"])
 def test_seeded_init_matches_reference(case):
     """Same constructor, names, shapes and RNG draws as the reference: identical weights under a seed."""
