@@ -17,6 +17,7 @@ import argparse
 import hashlib
 import os
 import sys
+import time
 from pathlib import Path
 
 import numpy as np
@@ -193,6 +194,216 @@ def lm_case(M, name, seed, B, T, n_new, **kw):
     np.savez_compressed(HERE / f"lm_{name}.npz", **out)
 
 
+# ---------------------------------------------------------------------------
+# BASELINE configs 0-4 at their own sizes.  The full outputs are too large to commit,
+# so each fixture keeps evenly spaced token (or step) slices, a few heads of the states,
+# and whole-tensor statistics (absmax, sum of squares) that a test compares at full size.
+# ---------------------------------------------------------------------------
+CFG_LAYER = dict(d_model=768, d_state=128, expand=2, headdim=64, mimo_rank=2, chunk_size=64)
+CFG_LM = dict(vocab_size=32000, d_model=768, n_layers=24, d_state=128, headdim=64, mimo_rank=2,
+              residual_scale="depth")
+CFG3_LAYER = dict(d_model=2048, d_state=128, expand=2, headdim=64, mimo_rank=4, chunk_size=64)
+
+
+def _bf16_round_(module):
+    """Round every parameter to bf16 in place (values stay fp32): the weights a bf16 model holds."""
+    with torch.no_grad():
+        for p in module.parameters():
+            p.copy_(p.to(torch.bfloat16).float())
+
+
+def _stats(prefix, t):
+    t = t.detach().double()
+    return {f"{prefix}.absmax": np.float64(t.abs().max()), f"{prefix}.sumsq": np.float64((t * t).sum()),
+            f"{prefix}.sum": np.float64(t.sum()), f"{prefix}.numel": np.int64(t.numel())}
+
+
+def _state_slices(st, heads):
+    return {"h": _np(st["h"][:, heads]), "angle": _np(st["angle"].float()),
+            "prev_BX": _np(st["prev_BX"][:, heads]), **_stats("h", st["h"]), **_stats("prev_BX", st["prev_BX"])}
+
+
+def cfg0_case(M):
+    """Config 0: fp32 layer forward + prefill state, x (4, 1024, 768) ~ N(0,1) (CPU generator seed 0),
+    weights = the reference's default init under torch.manual_seed(0)."""
+    torch.manual_seed(0)
+    layer = M.KulaMamba(**CFG_LAYER).eval()
+    x = torch.randn(4, 1024, 768, generator=torch.Generator().manual_seed(0))
+    with torch.no_grad():
+        y, st = layer.prefill(x)
+    heads = [0, 11, 23]
+    out = {"y_tok": _np(y[:, ::16]), "tok_stride": np.int64(16), "heads": np.asarray(heads), **_stats("y", y)}
+    out.update({f"st.{k}": v for k, v in _state_slices(st, heads).items()})
+    np.savez_compressed(HERE / "cfg0_layer.npz", **out)
+
+
+def cfg1_case(M, rows=(0, 7, 15)):
+    """Config 1 rows: the config-0 weights rounded to bf16, x (16, 4096, 768) ~ N(0,1) (CPU generator
+    seed 1) rounded to bf16; the reference's fp32 path on those values, one row at a time."""
+    torch.manual_seed(0)
+    layer = M.KulaMamba(**CFG_LAYER).eval()
+    _bf16_round_(layer)
+    x = torch.randn(16, 4096, 768, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).float()
+    heads = [0, 12, 23]
+    out = {"rows": np.asarray(rows), "tok_stride": np.int64(32), "heads": np.asarray(heads)}
+    for i, r in enumerate(rows):
+        with torch.no_grad():
+            y, st = layer.prefill(x[r:r + 1])
+        out[f"r{i}.y_tok"] = _np(y[:, ::32])
+        out.update({f"r{i}.{k}": v for k, v in _stats("y", y).items()})
+        out.update({f"r{i}.st.{k}": v for k, v in _state_slices(st, heads).items()})
+    np.savez_compressed(HERE / "cfg1_rows.npz", **out)
+
+
+def _lm_bf16(M, seed=2):
+    torch.manual_seed(seed)
+    lm = M.KulaMambaLM(**CFG_LM).eval()
+    _bf16_round_(lm)
+    return lm
+
+
+def cfg2_case(M, rows=(0, 31, 63)):
+    """Config 2 rows: the 24-layer LM under torch.manual_seed(2) with bf16-rounded weights, input_ids
+    (64, 2048) uniform in [0, 32000) (CPU generator seed 2); final-norm hidden states every 32nd
+    position and full logits at three positions (mamba3/block.py:178-193)."""
+    lm = _lm_bf16(M)
+    ids = torch.randint(0, 32000, (64, 2048), generator=torch.Generator().manual_seed(2))
+    cap = {}
+    hk = lm.norm.register_forward_hook(lambda m, i, o: cap.__setitem__("h", o.detach()))
+    pos = [0, 1023, 2047]
+    out = {"rows": np.asarray(rows), "tok_stride": np.int64(32), "logit_pos": np.asarray(pos)}
+    for i, r in enumerate(rows):
+        with torch.no_grad():
+            logits = lm(ids[r:r + 1])["logits"]
+        out[f"r{i}.hid_tok"] = _np(cap["h"][:, ::32])
+        out[f"r{i}.logits"] = _np(logits[:, pos])
+        out.update({f"r{i}.{k}": v for k, v in _stats("logits", logits).items()})
+        out[f"r{i}.argmax"] = _np(logits.argmax(-1))
+    hk.remove()
+    np.savez_compressed(HERE / "cfg2_lm.npz", **out)
+
+
+def segmented_prefill(M, layer, x, seg):
+    """The reference's layer prefill over x (B, T, d) computed segment by segment, each segment a
+    call of the reference's chunked_ssd continuing from the previous one's state (h_init,
+    mamba3/ssd.py:118-131).  The projection, norms, rotation (with the angle carried across
+    segments), MIMO, trapezoid (with the previous token carried) and gate are the reference's own
+    modules and formulas (mamba3/mamba3.py:192-256).  Needed where the reference cannot hold the
+    whole sequence (config 3: its per-token P x N products would take hundreds of GB)."""
+    from mamba3 import mamba3 as MM
+
+    Bat, T, _ = x.shape
+    H, P, N, R, G = layer.nheads, layer.headdim, layer.d_state, layer.mimo_rank, layer.ngroups
+    h = None
+    ang = torch.zeros(Bat, 1, H, N // 2)
+    x_last = B_last = None
+    ys = []
+    for t0 in range(0, T, seg):
+        xs = x[:, t0:t0 + seg]
+        Ts = xs.shape[1]
+        proj = layer.in_proj(xs)
+        z, x_flat, B_flat, C_flat, dt_raw, lam_raw, theta_raw = layer._split_proj(proj)
+        dt = F_softplus(dt_raw + layer.dt_bias)
+        A = -torch.exp(layer.A_log)
+        dA = torch.exp(A[None, None, :] * dt)
+        B_r = layer.B_norm(B_flat.reshape(Bat, Ts, G, N * R)).reshape(Bat, Ts, G, N, R) + layer.B_bias[None, None]
+        C_r = layer.C_norm(C_flat.reshape(Bat, Ts, G, N * R)).reshape(Bat, Ts, G, N, R) + layer.C_bias[None, None]
+        B_r, C_r = layer._expand_groups(B_r), layer._expand_groups(C_r)
+        cum = ang - (dt.unsqueeze(-1) * theta_raw.unsqueeze(-2)).cumsum(dim=1)
+        c, s = torch.cos(cum).unsqueeze(-1).unsqueeze(-1), torch.sin(cum).unsqueeze(-1).unsqueeze(-1)
+        B_r, C_r = MM._apply_rope(B_r, c, s, N, R), MM._apply_rope(C_r, c, s, N, R)
+        ang = cum[:, -1:]
+        x_r = x_flat.reshape(Bat, Ts, H, P, 1) * layer.mimo_x[None, None]
+        lam = torch.sigmoid(lam_raw)
+        x_gamma = x_r * lam.unsqueeze(-1).unsqueeze(-1)
+        prev_x = torch.zeros_like(x_r[:, :1]) if x_last is None else x_last
+        prev_B = torch.zeros_like(B_r[:, :1]) if B_last is None else B_last
+        x_beta = torch.cat([prev_x, x_r[:, :-1]], 1) * ((1.0 - lam) * dA).unsqueeze(-1).unsqueeze(-1)
+        B_prev = torch.cat([prev_B, B_r[:, :-1]], 1)
+        o = M.chunked_ssd(x_gamma, x_beta, B_r, B_prev, C_r, dt, A, layer.D, x_r, layer.chunk_size, h_init=h,
+                          return_final_state=True)
+        h = o.h_final
+        z_r = z.reshape(Bat, Ts, H, P).unsqueeze(-1) * layer.mimo_z[None, None]
+        y = (o.y * F_silu(z_r) * layer.mimo_down[None, None]).sum(-1).reshape(Bat, Ts, layer.d_inner)
+        ys.append(layer.out_proj(y))
+        x_last, B_last = x_r[:, -1:], B_r[:, -1:]
+    prev_BX = torch.einsum("bhnr,bhpr->bhpn", B_last[:, 0], x_last[:, 0])
+    return torch.cat(ys, 1), {"h": h.float(), "angle": ang[:, 0], "prev_BX": prev_BX.float()}
+
+
+def F_softplus(t):
+    return torch.nn.functional.softplus(t)
+
+
+def F_silu(t):
+    return torch.nn.functional.silu(t)
+
+
+def cfg3_case(M, T=16384, seg=1024):
+    """Config 3, row 0 of x (2, 131072, 2048), first T tokens: the layer (d_model 2048, 64 heads,
+    mimo_rank 4) under torch.manual_seed(0) with bf16-rounded weights; x ~ N(0,1) drawn as
+    (1, T, 2048) from the CPU generator seed 3 and rounded to bf16; the segmented reference."""
+    # the segmented form first reproduces the reference's own prefill on a small layer
+    torch.manual_seed(5)
+    small = M.KulaMamba(d_model=64, d_state=16, headdim=16, mimo_rank=4, chunk_size=8).eval()
+    xs = torch.randn(2, 45, 64, generator=torch.Generator().manual_seed(5))
+    with torch.no_grad():
+        y0, s0 = small.prefill(xs)
+        y1, s1 = segmented_prefill(M, small, xs, 16)
+    for a, b in ((y0, y1), (s0["h"], s1["h"]), (s0["angle"], s1["angle"]), (s0["prev_BX"], s1["prev_BX"])):
+        assert float((a - b).abs().max() / b.abs().max()) < 1e-5
+    torch.manual_seed(0)
+    layer = M.KulaMamba(**CFG3_LAYER).eval()
+    _bf16_round_(layer)
+    x = torch.randn(1, T, 2048, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).float()
+    with torch.no_grad():
+        y, st = segmented_prefill(M, layer, x, seg)
+    heads = [0, 31, 63]
+    out = {"T": np.int64(T), "tok_stride": np.int64(128), "heads": np.asarray(heads), "y_tok": _np(y[:, ::128]),
+           **_stats("y", y)}
+    out.update({f"st.{k}": v for k, v in _state_slices(st, heads).items()})
+    np.savez_compressed(HERE / "cfg3_seg.npz", **out)
+
+
+def cfg4_case(M, rows=(0, 127, 255), new=256):
+    """Config 4 rows: the config-2 LM (bf16-rounded weights) prefills prompts (256, 512) uniform in
+    [0, 32000) (CPU generator seed 4) and generates `new` tokens greedily with the reference's own
+    generate loop (mamba3/block.py:195-231).  Kept: the generated tokens, the final-norm hidden
+    state of every 8th decode step, full logits at three steps, and each step's top-2 logit margin
+    (a bf16 run may legitimately pick the other token where the margin is tiny)."""
+    lm = _lm_bf16(M)
+    ids = torch.randint(0, 32000, (256, 512), generator=torch.Generator().manual_seed(4))[list(rows)]
+    hid, lg = [], []
+
+    def hook(m, i, o):
+        hid.append(o.detach()[:, -1] if o.dim() == 3 else o.detach())
+
+    hk = lm.norm.register_forward_hook(hook)
+    hk2 = lm.lm_head.register_forward_hook(lambda m, i, o: lg.append(o.detach()))
+    with torch.no_grad():
+        gen = lm.generate(ids, max_new_tokens=new, temperature=0.0)
+    hk.remove()
+    hk2.remove()
+    # hid[i] / lg[i]: after the prefill (i = 0) and after each decode step; logits lg[i] choose token i
+    logits = torch.stack(lg[:new], 1)  # (rows, new, vocab)
+    top2 = logits.topk(2, dim=-1).values
+    steps = [0, 127, 255]
+    hid_all = torch.stack(hid[:new], 1)
+    out = {"rows": np.asarray(rows), "prompt": _np(ids), "gen": _np(gen[:, 512:]), "step_stride": np.int64(8),
+           "hid_step": _np(hid_all[:, ::8]), "logit_steps": np.asarray(steps), "logits": _np(logits[:, steps]),
+           "margin": _np(top2[..., 0] - top2[..., 1])}
+    np.savez_compressed(HERE / "cfg4_decode.npz", **out)
+
+
+def config_groups(M, only=""):
+    for name, fn in (("cfg0", cfg0_case), ("cfg1", cfg1_case), ("cfg2", cfg2_case), ("cfg3", cfg3_case),
+                     ("cfg4", cfg4_case)):
+        if only in ("configs", name):
+            t0 = time.time()
+            fn(M)
+            print(f"{name}: {time.time() - t0:.1f} s", flush=True)
+
+
 def grad_groups(M):
     small = dict(d_model=64, d_state=16, headdim=16, mimo_rank=2, expand=2, chunk_size=8)
     layer_grad_case(M, "default", 61, 2, 21, True, **small)
@@ -231,6 +442,9 @@ def main():
         return
     if args.only == "grad":
         grad_groups(M)
+        return
+    if args.only == "configs" or args.only.startswith("cfg"):
+        config_groups(M, args.only)
         return
     small = dict(d_model=64, d_state=16, headdim=16, mimo_rank=2, expand=2, chunk_size=8)
     layer_case(M, "default", 11, 2, 24, False, **small)
