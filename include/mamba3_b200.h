@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3B_ABI_VERSION 4
+#define M3B_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define M3B_API __attribute__((visibility("default")))
@@ -198,6 +198,9 @@ typedef struct m3b_layer_fwd_args {
    * rotated B^ (batch,H,N,R) and MIMO x (batch,H,P,R), fp32. */
   float* prev_b_final;
   float* prev_x_final;
+  /* Limit in nanoseconds of every device-side wait of this call (0: the library's 2 s).  A wait
+   * that runs out records M3B_ERR_TIMEOUT in `err` and the kernel returns early. */
+  int64_t wait_limit_ns;
 } m3b_layer_fwd_args;
 #define M3B_LAYER_FWD_STAGES 6
 
@@ -450,9 +453,21 @@ M3B_API int m3b_scaled_add(const void* x, const void* h, float scale, void* out,
  * D (128 x 64, fp32) = A (128 x 128 bf16, row-major) x B (64 x 128 bf16, row-major)^T,
  * staged through the same shared-memory layouts and UMMA descriptors as the chunk
  * kernels: mode 0 reads A K-major, mode 1 stages A transposed and reads it MN-major,
- * mode 2 stages B transposed and reads it MN-major.
+ * mode 2 stages B transposed and reads it MN-major.  Modes 3-5 are the same three layouts
+ * with fp32 A and B on kind::tf32 (the tiles of the fp32 chunk kernels).
  * ------------------------------------------------------------------------ */
 M3B_API int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Bounded-wait self-test (diagnostic; no counterpart in the reference).
+ * One thread runs the library's bounded wait on a condition for at most limit_ns
+ * (0 < limit_ns <= 1 s): mode 0 waits for *flag >= target (the acquire-load flag wait the
+ * fused layer kernel uses when one CTA hands a sequence part to another), mode 1 for phase 0
+ * of a shared-memory mbarrier that nothing arrives on (the kernels' pipeline waits).  A wait
+ * that runs out records M3B_ERR_TIMEOUT in *err (first error wins) and the kernel returns, so
+ * a caller can check that an expired wait surfaces as a status and leaves the context usable.
+ * ------------------------------------------------------------------------ */
+M3B_API int m3b_selftest_wait(const int* flag, int target, int mode, int64_t limit_ns, int* err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -12,6 +12,7 @@ from .block import KulaMambaBlock, KulaMambaLM, SwiGLU  # noqa: E402
 from .ssd import SSDOutput, chunked_ssd  # noqa: E402
 from .scan import ssd_scan  # noqa: E402
 from .decode import GraphDecoder  # noqa: E402  (extension: CUDA-graph decode loop)
+from ._lib import M3bError, check_device_errors  # noqa: E402  (status codes, device error word)
 
 __all__ = [
     "KulaMamba",
@@ -23,4 +24,6 @@ __all__ = [
     "chunked_ssd",
     "ssd_scan",
     "GraphDecoder",
+    "M3bError",
+    "check_device_errors",
 ]

@@ -69,7 +69,8 @@ class LayerFwdArgs(C.Structure):
                 ("h_init", C.c_void_p), ("angle_init", C.c_void_p), ("prev_bx_init", C.c_void_p), ("y", C.c_void_p),
                 ("h_final", C.c_void_p), ("angle_final", C.c_void_p), ("prev_bx_final", C.c_void_p),
                 ("err", C.c_void_p), ("stage_events", C.POINTER(C.c_void_p)), ("algo", C.c_int32),
-                ("state_only", C.c_int32), ("prev_b_final", C.c_void_p), ("prev_x_final", C.c_void_p)]
+                ("state_only", C.c_int32), ("prev_b_final", C.c_void_p), ("prev_x_final", C.c_void_p),
+                ("wait_limit_ns", C.c_int64)]
 
 
 class SsdArgs(C.Structure):
@@ -157,6 +158,7 @@ SIGNATURES = {
     "m3b_swiglu_act": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
     "m3b_scaled_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
     "m3b_selftest_umma": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "m3b_selftest_wait": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int64, C.c_void_p, C.c_void_p]),
 }
 
 
@@ -264,9 +266,13 @@ def step(prm: LayerParams, proj, dt_scale, h, prev_bx, angle, h_out, bx_out, ang
 
 def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=None, prev_bx_init=None,
               h_final=None, angle_final=None, prev_bx_final=None, err=None, workspace=None, stage_events=None,
-              algo=0, state_only=False, prev_b_final=None, prev_x_final=None):
-    """Launch the chunked layer forward; proj (B,T,d_proj) with unit stride in the last dim."""
+              algo=0, state_only=False, prev_b_final=None, prev_x_final=None, wait_limit_ns=0):
+    """Launch the chunked layer forward; proj (B,T,d_proj) with unit stride in the last dim.
+    Without `err` the device's error word records expired device waits (check_device_errors);
+    wait_limit_ns bounds each device wait (0: the library's 2 s)."""
     dev = _cuda(proj, y, dt_scale, h_init, angle_init, prev_bx_init, h_final, angle_final, prev_bx_final, err)
+    if err is None:
+        err = device_err_word(dev)
     Bt, T, _ = proj.shape
     if proj.stride(2) != 1 or proj.stride(0) != T * proj.stride(1):
         raise M3bError("proj must be row-contiguous (B,T,d_proj)")
@@ -277,6 +283,7 @@ def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=
     a.state_only = int(bool(state_only))
     a.prev_b_final = _ptr(prev_b_final)
     a.prev_x_final = _ptr(prev_x_final)
+    a.wait_limit_ns = int(wait_limit_ns)
     if stage_events is not None:
         if len(stage_events) != len(LAYER_FWD_STAGES) + 1:
             raise M3bError("stage_events needs one event per stage plus one")
@@ -290,12 +297,15 @@ def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=
         workspace = torch.empty(need, dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         _check(L.m3b_layer_fwd(C.byref(a), _ptr(workspace), need, _stream(dev)), "m3b_layer_fwd")
+    _after_launch(dev)
     return workspace
 
 
 def chunked_ssd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, y, h_init=None, h_final=None, err=None):
     """Launch the general chunked SSD; all activations contiguous and of one dtype."""
     dev = _cuda(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, y, h_init, h_final, err)
+    if err is None:
+        err = device_err_word(dev)
     Bt, T, H, P, R = x_g.shape
     N = B_g.shape[3]
     a = SsdArgs(Bt, T, H, P, N, R, dtype_code(x_g.dtype), _ptr(x_g), _ptr(x_b), _ptr(B_g), _ptr(B_b), _ptr(Cm),
@@ -308,6 +318,7 @@ def chunked_ssd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, y, h_init=None, h_final
     ws = torch.empty(need, dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         _check(L.m3b_chunked_ssd(C.byref(a), _ptr(ws), need, _stream(dev)), "m3b_chunked_ssd")
+    _after_launch(dev)
 
 
 def chunked_ssd_bwd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init=None, dh_final=None):
@@ -556,6 +567,60 @@ def selftest_umma(A, B, mode):
     with torch.cuda.device(dev):
         _check(lib().m3b_selftest_umma(_ptr(A), _ptr(B), _ptr(D), mode, _ptr(err), _stream(dev)), "selftest_umma")
     return D, err
+
+
+def selftest_wait(flag, target, mode, limit_ns, err):
+    """Bounded wait on `flag` >= target (mode 0) or on an mbarrier nothing completes (mode 1)."""
+    dev = _cuda(flag, err)
+    with torch.cuda.device(dev):
+        _check(lib().m3b_selftest_wait(_ptr(flag), int(target), int(mode), int(limit_ns), _ptr(err), _stream(dev)),
+               "selftest_wait")
+
+
+# ---------------------------------------------------------------------------
+# device error word
+# ---------------------------------------------------------------------------
+# Kernels that wait on the device (the fused layer kernel's pipeline and hand-off waits, the
+# chunked kernels' tensor-core commits) give up after a bounded time and record
+# M3B_ERR_TIMEOUT in an error word.  Every layer forward and chunked_ssd call of this module
+# passes one word per device; it keeps the first error until check_device_errors() reads and
+# clears it.  Reading it synchronises the device, so the calls themselves never do; set
+# M3B_SYNC_CHECK=1 to check after every such call (debugging).
+_err_words = {}
+_SYNC_CHECK = __import__("os").environ.get("M3B_SYNC_CHECK", "0") not in ("", "0")
+
+
+def device_err_word(dev):
+    """The per-device int32 error word (allocated zeroed on first use; None when the first use
+    falls inside a CUDA graph capture, which must not allocate)."""
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _err_words.get(key)
+    if w is None:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+        _err_words[key] = w
+    return w
+
+
+def check_device_errors(dev=None):
+    """Synchronise `dev` (default: every device with an error word), read and clear its error
+    word, and raise M3bError if a kernel recorded one (e.g. an expired bounded wait)."""
+    keys = list(_err_words) if dev is None else [dev.index if dev.index is not None else torch.cuda.current_device()]
+    for key in keys:
+        w = _err_words.get(key)
+        if w is None:
+            continue
+        code = int(w.item())
+        if code != 0:
+            w.zero_()
+            L = lib()
+            raise M3bError(f"device cuda:{key}: a kernel reported {L.m3b_strerror(code).decode()} (code {code})")
+
+
+def _after_launch(dev):
+    if _SYNC_CHECK:
+        check_device_errors(dev)
 
 
 def copy_token_range(dst, dst_t0, src, src_t0, ntok, stream):

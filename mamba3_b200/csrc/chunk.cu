@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kCT) angle_prefix_kernel(FwdParams a) {
 template <typename TA, int R>
 __device__ void chunk_prologue(const FwdParams& a, uint8_t* sm, int b, int k, int h, int g, bool out_kernel) {
   constexpr int RP = rp_of(R);
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   constexpr int L = PL::L;
   float* rmsv = reinterpret_cast<float*>(sm + PL::rmsv);
   for (int s = threadIdx.x; s < L; s += kCT) {
@@ -132,7 +132,7 @@ __device__ void chunk_prologue(const FwdParams& a, uint8_t* sm, int b, int k, in
     rmsv[2 * s] = rb;
     rmsv[2 * s + 1] = rc;
   }
-  chunk_params<RP>(a, sm, h, g, out_kernel);
+  chunk_params<TA, RP>(a, sm, h, g, out_kernel);
   chunk_scalars<TA, RP>(a, sm, b, k, h);  // ends with __syncthreads
   if (a.prm.complex_ssm) chunk_angles<TA, RP>(a, sm, b, k, h);
   chunk_stage_xz<TA, RP>(a, sm, b, k, h, out_kernel);
@@ -145,7 +145,7 @@ __device__ void chunk_prologue(const FwdParams& a, uint8_t* sm, int b, int k, in
 template <typename TA, typename TS, int R>
 __global__ void __launch_bounds__(kCT, 1) chunk_state_kernel(FwdParams a) {
   constexpr int RP = rp_of(R);
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   constexpr int L = PL::L;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
@@ -175,18 +175,27 @@ __global__ void __launch_bounds__(kCT, 1) chunk_state_kernel(FwdParams a) {
   }
   __syncthreads();
   chunk_produce_bc<TA, R, true, false>(a, sm, b, k, g);
-  chunk_produce_x<RP, true>(a, sm);
+  if constexpr (PL::F32) __syncthreads();  // the angles (in the X tile region) have been read
+  chunk_produce_x<TA, RP, true>(a, sm, b, k, h);
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
   if (threadIdx.x == 0) {
-    constexpr uint32_t idesc = idesc_bf16(128, kPP, /*a_mn=*/true, /*b_mn=*/false);
+    if constexpr (PL::F32) {
+      constexpr uint32_t idesc = idesc_tf32(128, kPP, /*a_mn=*/true, /*b_mn=*/false);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, 128, kk * 16), kmajor_desc(sm + PL::tileX, kPP, kk * 16),
-                idesc, kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 16; ++kk)
+        umma_tf32(tbase, mnmajor_desc(sm + PL::tileB, 128, kk * 8), kmajor_desc_b(sm + PL::tileX, kPP, kk * 32),
+                  idesc, kk > 0 ? 1u : 0u);
+    } else {
+      constexpr uint32_t idesc = idesc_bf16(128, kPP, /*a_mn=*/true, /*b_mn=*/false);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, 128, kk * 16), kmajor_desc(sm + PL::tileX, kPP, kk * 16),
+                  idesc, kk > 0 ? 1u : 0u);
+    }
     umma_commit(&bar[0]);
   }
   bool ok = mbar_wait(&bar[0], 0);
@@ -224,7 +233,7 @@ __global__ void __launch_bounds__(kCT, 1) chunk_state_kernel(FwdParams a) {
 template <typename TA, typename TS, int R>
 __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
   constexpr int RP = rp_of(R);
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   constexpr int L = PL::L;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
@@ -262,33 +271,42 @@ __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = 0.f;
       }
-      uint4 o;
-      o.x = pack_bf16x2(v[0], v[1]);
-      o.y = pack_bf16x2(v[2], v[3]);
-      o.z = pack_bf16x2(v[4], v[5]);
-      o.w = pack_bf16x2(v[6], v[7]);
-      sw128_store_chunk(tH, pp, c, kPP, o);
+      tile_store8<TA>(tH, pp, c, kPP, v);
     }
   }
   __syncthreads();
   chunk_produce_bc<TA, R, true, true>(a, sm, b, k, g);
-  chunk_produce_x<RP, false>(a, sm);
+  if constexpr (PL::F32) __syncthreads();  // the angles (in the X tile region) have been read
+  chunk_produce_x<TA, RP, false>(a, sm, b, k, h);
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
   if (threadIdx.x == 0) {
-    constexpr uint32_t id_s = idesc_bf16(128, 128, false, false);
-    constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
+    if constexpr (PL::F32) {
+      constexpr uint32_t id_s = idesc_tf32(128, 128, false, false);
+      constexpr uint32_t id_o = idesc_tf32(128, kPP, false, false);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16(tbase, kmajor_desc(sm + PL::tileC, 128, kk * 16), kmajor_desc(sm + PL::tileB, 128, kk * 16), id_s,
-                kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 16; ++kk)
+        umma_tf32(tbase, kmajor_desc_b(sm + PL::tileC, 128, kk * 32), kmajor_desc_b(sm + PL::tileB, 128, kk * 32),
+                  id_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16(tbase + 192, kmajor_desc(sm + PL::tileC, 128, kk * 16), kmajor_desc(sm + PL::tileH, kPP, kk * 16),
-                id_o, kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 16; ++kk)
+        umma_tf32(tbase + 192, kmajor_desc_b(sm + PL::tileC, 128, kk * 32),
+                  kmajor_desc_b(sm + PL::tileH, kPP, kk * 32), id_o, kk > 0 ? 1u : 0u);
+    } else {
+      constexpr uint32_t id_s = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tbase, kmajor_desc(sm + PL::tileC, 128, kk * 16), kmajor_desc(sm + PL::tileB, 128, kk * 16), id_s,
+                  kk > 0 ? 1u : 0u);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tbase + 192, kmajor_desc(sm + PL::tileC, 128, kk * 16), kmajor_desc(sm + PL::tileH, kPP, kk * 16),
+                  id_o, kk > 0 ? 1u : 0u);
+    }
     umma_commit(&bar[0]);
   }
   bool ok = mbar_wait(&bar[0], 0);
@@ -318,12 +336,10 @@ __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
       }
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
-        uint4 o;
-        o.x = pack_bf16x2(v[8 * cc + 0], v[8 * cc + 1]);
-        o.y = pack_bf16x2(v[8 * cc + 2], v[8 * cc + 3]);
-        o.z = pack_bf16x2(v[8 * cc + 4], v[8 * cc + 5]);
-        o.w = pack_bf16x2(v[8 * cc + 6], v[8 * cc + 7]);
-        sw128_store_chunk(tP, m, c0 / 8 + cc, 128, o);
+        float v8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v8[e] = v[8 * cc + e];
+        tile_store8<TA>(tP, m, c0 / 8 + cc, 128, v8);
       }
     }
   }
@@ -332,11 +348,19 @@ __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
   __syncthreads();
   tc_fence_after();
   if (ok && threadIdx.x == 0) {
-    constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
+    if constexpr (PL::F32) {
+      constexpr uint32_t id_o = idesc_tf32(128, kPP, false, false);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16(tbase + 128, kmajor_desc(sm + PL::tileB, 128, kk * 16), kmajor_desc(sm + PL::tileX, kPP, kk * 16),
-                id_o, kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 16; ++kk)
+        umma_tf32(tbase + 128, kmajor_desc_b(sm + PL::tileB, 128, kk * 32),
+                  kmajor_desc_b(sm + PL::tileX, kPP, kk * 32), id_o, kk > 0 ? 1u : 0u);
+    } else {
+      constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tbase + 128, kmajor_desc(sm + PL::tileB, 128, kk * 16), kmajor_desc(sm + PL::tileX, kPP, kk * 16),
+                  id_o, kk > 0 ? 1u : 0u);
+    }
     umma_commit(&bar[1]);
   }
   if (ok) {
@@ -357,11 +381,22 @@ __global__ void __launch_bounds__(kCT, 1) chunk_out_kernel(FwdParams a) {
     const float ec = exp2f(cum2[t]);
     const float Dh = ldf(p.D, h, p.param_dtype);
     float acc[32];
+    const int64_t tok0 = (int64_t)k * L + t;
+    const TA* prow = reinterpret_cast<const TA*>(a.proj) + ((int64_t)b * a.T + (tok0 < a.T ? tok0 : 0)) * a.proj_stride;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int pp = 32 * half + j;
-      const float xr = xs[t * PL::XS + pp] * mx[pp * RP + r];
-      const float zz = zs[t * PL::XS + pp] * mz[pp * RP + r];
+      float xv, zv;
+      if constexpr (PL::F32) {  // x and z of this row straight from the projection
+        const bool okp = pp < p.P && tok0 < a.T;
+        xv = okp ? io<TA>::ld(prow + (int64_t)p.H * p.P + (int64_t)h * p.P + pp) : 0.f;
+        zv = okp ? io<TA>::ld(prow + (int64_t)h * p.P + pp) : 0.f;
+      } else {
+        xv = xs[t * PL::XS + pp];
+        zv = zs[t * PL::XS + pp];
+      }
+      const float xr = xv * mx[pp * RP + r];
+      const float zz = zv * mz[pp * RP + r];
       acc[j] = (Y[j] + ec * Yi[j] + Dh * xr) * silu_f(zz) * md[pp * RP + r];
     }
 #pragma unroll
@@ -464,8 +499,10 @@ struct WsLayout {
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// The fused sequential kernel takes bf16 activations; fp32 activations always run the
+// chunk-parallel kernels, whose fp32 operand tiles feed kind::tf32 MMAs (fp32-level accuracy).
 bool use_fused(const m3b_layer_fwd_args* a) {
-  if (a->algo == 2) return false;
+  if (a->algo == 2 || a->act_dtype != M3B_BF16) return false;
   return fused_supported(a->prm);
 }
 
@@ -577,7 +614,7 @@ int ensure_smem(const void* kernel, int bytes) {
 template <typename TA, typename TS, int R, typename Mark>
 int run_chunks(FwdParams& fp, const m3b_layer_fwd_args* a, cudaStream_t st, Mark& mark) {
   constexpr int RP = rp_of(R);
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   const m3b_layer_params& p = a->prm;
   int rc;
   dim3 grid((unsigned)p.H, (unsigned)fp.K, (unsigned)fp.B);
@@ -670,6 +707,7 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
     f.h_final = a->h_final;
     f.angle_last = angle_last;
     f.err = a->err;
+    f.wait_ns = a->wait_limit_ns > 0 ? (uint64_t)a->wait_limit_ns : kWaitLimitNs;
     f.state_only = a->state_only != 0;
     f.KP = w.kp;
     if (w.kp < fp.K) {

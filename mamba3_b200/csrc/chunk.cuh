@@ -69,6 +69,7 @@ struct FusedParams {
   float* h_final;
   float* angle_last;  // (B,H,N/2): angle after the last token (always written)
   int* err;
+  uint64_t wait_ns;   // limit of every device-side wait (the caller's, or kWaitLimitNs)
   bool state_only;    // y not needed: the kernel may skip the outputs (TMA path)
   // Sequences cut into parts of KP chunks (KP == K: whole sequences).  Part q > 0 of sequence s
   // starts from the state part q - 1 hands over: H in ho_h[s] (P x N fp32, h_final layout), the
@@ -96,19 +97,27 @@ __device__ __forceinline__ float token_dt(const FwdParams& a, const TA* row, int
   return dt;
 }
 
-// Shared-memory plan of one chunk CTA (byte offsets from a 1024-aligned base).
-template <int RP>
+// Shared-memory plan of one chunk CTA (byte offsets from a 1024-aligned base).  The tensor-core
+// operand tiles hold bf16 for 16-bit activations (kind::f16 MMAs) and fp32 words for fp32
+// activations (kind::tf32 MMAs: 10 mantissa bits instead of 7, so fp32 models keep fp32-level
+// accuracy).  fp32 tiles double the tile bytes, so that variant does not stage x and z (it reads
+// them from global memory, where the chunk's rows are L2-resident) and keeps the angles in the X
+// tile's region until the X tile is built.
+template <int RP, typename TA = __nv_bfloat16>
 struct Plan {
   static constexpr int L = 128 / RP;
+  static constexpr int E = (int)sizeof(TA) == 4 ? 4 : 2;  // operand tile element bytes
+  static constexpr bool F32 = E == 4;
   static constexpr int XS = kPP + 4;                 // fp32 row stride of the staged x / z tiles
-  static constexpr int tileC = 0;                    // 128 x 128 bf16 (K-major SW128)
-  static constexpr int tileB = tileC + 32768;        // 128 x 128 bf16; reused for P = mask(S)
-  static constexpr int tileX = tileB + 32768;        // 64 x 128 bf16
-  static constexpr int tileH = tileX + 16384;        // 64 x 128 bf16
-  static constexpr int xs = tileH + 16384;           // L x XS fp32
-  static constexpr int zs = xs + L * XS * 4;         // L x XS fp32
-  static constexpr int phi = zs + L * XS * 4;        // L x 64 fp32 angles
-  static constexpr int cum2 = phi + L * 64 * 4;      // (L+1) fp32: log2e * inclusive cumsum of A dt
+  static constexpr int tileC = 0;                    // 128 x 128 (K-major SW128)
+  static constexpr int tileB = tileC + 128 * 128 * E;  // 128 x 128; reused for P = mask(S)
+  static constexpr int tileX = tileB + 128 * 128 * E;  // 64 x 128
+  static constexpr int tileH = tileX + 64 * 128 * E;   // 64 x 128
+  static constexpr int xs = tileH + 64 * 128 * E;      // L x XS fp32 (bf16 tiles only)
+  static constexpr int zs = xs + (F32 ? 0 : L * XS * 4);  // L x XS fp32 (bf16 tiles only)
+  static constexpr int phi_own = zs + (F32 ? 0 : L * XS * 4);
+  static constexpr int phi = F32 ? tileX : phi_own;  // L x 64 fp32 angles
+  static constexpr int cum2 = phi_own + (F32 ? 0 : L * 64 * 4);  // (L+1) fp32: log2e * inclusive cumsum of A dt
   static constexpr int dtv = cum2 + (L + 1) * 4;     // (L+1) dt
   static constexpr int gam = dtv + (L + 1) * 4;      // (L+1) gamma
   static constexpr int bpr = gam + (L + 1) * 4;      // (L+1) (1-lam) dt
@@ -127,7 +136,29 @@ struct Plan {
   static constexpr int bytes = total + 1024;         // + alignment slack
   static_assert(bytes <= 227 * 1024, "chunk CTA shared memory exceeds 227 KB");
   static_assert(L % 32 == 0, "chunk length must be a multiple of 32");
+  static_assert(!F32 || L * 64 * 4 <= 64 * 128 * E, "fp32 plan: the angles fit the X tile region");
 };
+
+// Store 8 consecutive fp32 values (columns [8 c8, 8 c8 + 8) of `row`) into an operand tile of
+// element type TA's tile format: one 16-byte chunk of bf16, or two of fp32.
+template <typename TA>
+__device__ __forceinline__ void tile_store8(uint8_t* tile, int row, int c8, int rows, const float (&v)[8]) {
+  if constexpr (sizeof(TA) == 4) {
+    sw128_store_chunk(tile, row, 2 * c8, rows,
+                      make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                                 __float_as_uint(v[3])));
+    sw128_store_chunk(tile, row, 2 * c8 + 1, rows,
+                      make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]),
+                                 __float_as_uint(v[7])));
+  } else {
+    uint4 o;
+    o.x = pack_bf16x2(v[0], v[1]);
+    o.y = pack_bf16x2(v[2], v[3]);
+    o.z = pack_bf16x2(v[4], v[5]);
+    o.w = pack_bf16x2(v[6], v[7]);
+    sw128_store_chunk(tile, row, c8, rows, o);
+  }
+}
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -137,7 +168,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // dt, gamma, (1-lam) dt and the log2e-scaled inclusive cumsum of A*dt.
 template <typename TA, int RP>
 __device__ void chunk_scalars(const FwdParams& a, uint8_t* sm, int b, int k, int h) {
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   constexpr int L = PL::L;
   const m3b_layer_params& p = a.prm;
   float* cum2 = reinterpret_cast<float*>(sm + PL::cum2);
@@ -196,7 +227,7 @@ __device__ void chunk_scalars(const FwdParams& a, uint8_t* sm, int b, int k, int
 // nseg segments in parallel (segment totals combined in shared memory).
 template <typename TA, int RP>
 __device__ void chunk_angles(const FwdParams& a, uint8_t* sm, int b, int k, int h) {
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   constexpr int L = PL::L;
   const m3b_layer_params& p = a.prm;
   const int nh2 = p.N / 2;
@@ -246,9 +277,9 @@ __device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
 }
 
 // Layer parameters used by the producers / epilogue, staged in fp32.
-template <int RP>
+template <typename TA, int RP>
 __device__ void chunk_params(const FwdParams& a, uint8_t* sm, int h, int g, bool need_z) {
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   const m3b_layer_params& p = a.prm;
   const int NR = p.N * p.R, pd = p.param_dtype;
   float* nwB = reinterpret_cast<float*>(sm + PL::nwB);
@@ -284,8 +315,9 @@ __device__ void chunk_params(const FwdParams& a, uint8_t* sm, int h, int g, bool
 // Stage x (and z) of the chunk's tokens for head h as fp32 [L][XS].
 template <typename TA, int RP>
 __device__ void chunk_stage_xz(const FwdParams& a, uint8_t* sm, int b, int k, int h, bool need_z) {
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   constexpr int L = PL::L;
+  if constexpr (PL::F32) return;  // fp32 tiles read x and z from the projection where they use them
   const m3b_layer_params& p = a.prm;
   float* xs = reinterpret_cast<float*>(sm + PL::xs);
   float* zs = reinterpret_cast<float*>(sm + PL::zs);
@@ -321,7 +353,7 @@ __device__ void chunk_stage_xz(const FwdParams& a, uint8_t* sm, int b, int k, in
 template <typename TA, int R, bool WANT_B, bool WANT_C>
 __device__ void chunk_produce_bc(const FwdParams& a, uint8_t* sm, int b, int k, int g) {
   constexpr int RP = rp_of(R);
-  using PL = Plan<RP>;
+  using PL = Plan<RP, TA>;
   constexpr int L = PL::L;
   const m3b_layer_params& p = a.prm;
   const int NR = p.N * R;
@@ -391,31 +423,32 @@ __device__ void chunk_produce_bc(const FwdParams& a, uint8_t* sm, int b, int k, 
     }
 #pragma unroll
     for (int r = 0; r < RP; ++r) {
-      uint4 ob = make_uint4(0, 0, 0, 0), oc = make_uint4(0, 0, 0, 0);
-      if (valid && r < R) {
-        ob.x = pack_bf16x2(vb[0 * R + r], vb[1 * R + r]);
-        ob.y = pack_bf16x2(vb[2 * R + r], vb[3 * R + r]);
-        ob.z = pack_bf16x2(vb[4 * R + r], vb[5 * R + r]);
-        ob.w = pack_bf16x2(vb[6 * R + r], vb[7 * R + r]);
-        oc.x = pack_bf16x2(vc[0 * R + r], vc[1 * R + r]);
-        oc.y = pack_bf16x2(vc[2 * R + r], vc[3 * R + r]);
-        oc.z = pack_bf16x2(vc[4 * R + r], vc[5 * R + r]);
-        oc.w = pack_bf16x2(vc[6 * R + r], vc[7 * R + r]);
+      float ob[8], oc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ob[e] = (valid && r < R) ? vb[e * R + (r < R ? r : 0)] : 0.f;
+        oc[e] = (valid && r < R) ? vc[e * R + (r < R ? r : 0)] : 0.f;
       }
-      if (WANT_B) sw128_store_chunk(tB, s * RP + r, c, 128, ob);
-      if (WANT_C) sw128_store_chunk(tC, s * RP + r, c, 128, oc);
+      if (WANT_B) tile_store8<TA>(tB, s * RP + r, c, 128, ob);
+      if (WANT_C) tile_store8<TA>(tC, s * RP + r, c, 128, oc);
     }
   }
 }
 
 // X^T tile: row p, column (s*RP + q) = x[s,p] * mimo_x[p,q] (* w_s when WEIGHTED).  (mamba3/mamba3.py:210)
-template <int RP, bool WEIGHTED>
-__device__ void chunk_produce_x(const FwdParams& a, uint8_t* sm) {
-  using PL = Plan<RP>;
+// x comes from the staged fp32 rows (bf16 tiles) or straight from the projection (fp32 tiles).
+template <typename TA, int RP, bool WEIGHTED>
+__device__ void chunk_produce_x(const FwdParams& a, uint8_t* sm, int b, int k, int h) {
+  using PL = Plan<RP, TA>;
+  constexpr int L = PL::L;
   const float* xs = reinterpret_cast<const float*>(sm + PL::xs);
   const float* mx = reinterpret_cast<const float*>(sm + PL::mx);
   const float* wgt = reinterpret_cast<const float*>(sm + PL::wgt);
   uint8_t* tX = sm + PL::tileX;
+  const m3b_layer_params& p = a.prm;
+  const int64_t t0 = (int64_t)k * L;
+  const TA* xg = reinterpret_cast<const TA*>(a.proj) + (int64_t)b * a.T * a.proj_stride + (int64_t)p.H * p.P +
+                 (int64_t)h * p.P;
   for (int u = threadIdx.x; u < kPP * 16; u += kCT) {
     const int pp = u % kPP, cc = u / kPP;
     float v[8];
@@ -423,16 +456,17 @@ __device__ void chunk_produce_x(const FwdParams& a, uint8_t* sm) {
     for (int e = 0; e < 8; ++e) {
       const int col = cc * 8 + e;
       const int s = col / RP, q = col % RP;
-      float val = xs[s * PL::XS + pp] * mx[pp * RP + q];
+      float xv;
+      if constexpr (PL::F32) {
+        xv = (t0 + s < a.T && pp < p.P) ? io<TA>::ld(xg + (t0 + s) * a.proj_stride + pp) : 0.f;
+      } else {
+        xv = xs[s * PL::XS + pp];
+      }
+      float val = xv * mx[pp * RP + q];
       if (WEIGHTED) val *= wgt[s];
       v[e] = val;
     }
-    uint4 o;
-    o.x = pack_bf16x2(v[0], v[1]);
-    o.y = pack_bf16x2(v[2], v[3]);
-    o.z = pack_bf16x2(v[4], v[5]);
-    o.w = pack_bf16x2(v[6], v[7]);
-    sw128_store_chunk(tX, pp, cc, kPP, o);
+    tile_store8<TA>(tX, pp, cc, kPP, v);
   }
 }
 

@@ -141,8 +141,9 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Every device-side wait in this library gives up after this many nanoseconds,
-// records M3B_ERR_TIMEOUT in the caller's error word and lets the kernel return.
+// Every device-side wait in this library gives up after this many nanoseconds (unless the
+// caller gives another limit), records M3B_ERR_TIMEOUT in the caller's error word and lets the
+// kernel return.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -158,14 +159,14 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Wait until *flag >= target, giving up after kWaitLimitNs (returns false then).
-__device__ __forceinline__ bool flag_wait_geq(const int* flag, int target) {
+// Wait until *flag >= target, giving up after limit_ns (returns false then).
+__device__ __forceinline__ bool flag_wait_geq(const int* flag, int target, uint64_t limit_ns = kWaitLimitNs) {
   if (ld_acquire_gpu(flag) >= target) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     __nanosleep(500);
     if (ld_acquire_gpu(flag) >= target) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -211,13 +212,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return done != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete; false if the wait limit expired.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait for phase `parity` of `bar` to complete; false once limit_ns has expired.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -254,6 +255,18 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, tf32 inputs (fp32 words, the low 13 mantissa bits ignored),
+// fp32 accumulate; K = 8 per instruction; issued by one thread.
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -266,6 +279,17 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major,
   return (1u << 4)                               // D format: f32
          | (1u << 7)                             // A format: bf16
          | (1u << 10)                            // B format: bf16
+         | ((a_mn_major ? 1u : 0u) << 15)        // A major
+         | ((b_mn_major ? 1u : 0u) << 16)        // B major
+         | ((uint32_t)(N >> 3) << 17)            // N / 8
+         | ((uint32_t)(M >> 4) << 24);           // M / 16
+}
+
+// Instruction descriptor: kind::tf32 with tf32 A/B, fp32 D, dense.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                               // D format: f32
+         | (2u << 7)                             // A format: tf32
+         | (2u << 10)                            // B format: tf32
          | ((a_mn_major ? 1u : 0u) << 15)        // A major
          | ((b_mn_major ? 1u : 0u) << 16)        // B major
          | ((uint32_t)(N >> 3) << 17)            // N / 8
@@ -302,6 +326,13 @@ __device__ __forceinline__ void sw128_store_chunk(uint8_t* tile, int row, int co
 // Descriptor of a K-major operand tile (rows x K) at K offset `k0` (multiple of 16).
 __device__ __forceinline__ uint64_t kmajor_desc(const uint8_t* tile, int rows, int k0) {
   const uint32_t base = smem_u32(tile) + (uint32_t)((k0 >> 6) * rows * 128 + ((k0 & 63) >> 3) * 16);
+  return sdesc_sw128(base, 16, 1024);
+}
+
+// Descriptor of a K-major operand tile (rows x K, any element size) at K byte offset `kb`
+// (multiple of 16) within the row: the tile is stored in 128-byte column blocks of `rows` rows.
+__device__ __forceinline__ uint64_t kmajor_desc_b(const uint8_t* tile, int rows, int kb) {
+  const uint32_t base = smem_u32(tile) + (uint32_t)((kb >> 7) * rows * 128 + (kb & 127));
   return sdesc_sw128(base, 16, 1024);
 }
 

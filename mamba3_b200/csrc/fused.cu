@@ -120,9 +120,9 @@ struct Sched {
 // One leader waits on the mbarrier; the role's named barrier then releases the others.
 // Returns false (for every thread of the role) once any wait of this CTA has timed out.
 __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, bool leader, int bar_id, int nthreads,
-                                          volatile int* abort_flag, int* err) {
+                                          volatile int* abort_flag, int* err, uint64_t lim) {
   if (leader && !*abort_flag) {
-    if (!mbar_wait(bar, parity)) {
+    if (!mbar_wait(bar, parity, lim)) {
       *abort_flag = 1;
       record_error(err, M3B_ERR_TIMEOUT);
     }
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             omega[(g & 1) * 64 + ptid] = a.angle_init ? (double)a.angle_init[((int64_t)b * H + h) * nh2 + ptid] : 0.0;
         } else {
           // the angles after the previous part of this sequence (another CTA, an earlier round)
-          if (ptid == 0 && !*abort_flag && !flag_wait_geq(a.ho_flag + 2 * pos.seq, pos.part)) {
+          if (ptid == 0 && !*abort_flag && !flag_wait_geq(a.ho_flag + 2 * pos.seq, pos.part, a.wait_ns)) {
             *abort_flag = 1;
             record_error(a.err, M3B_ERR_TIMEOUT);
           }
@@ -423,7 +423,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
       if (ptid == 0) M3B_TL(g, 0);
       // the stage is free (and on the TMA path its raw rows have landed)
-      if (!role_wait(&bars[BAR_STAGE0 + s], (g >> 1) & 1, ptid == 0, kBarProd, kProdThreads, abort_flag, a.err))
+      if (!role_wait(&bars[BAR_STAGE0 + s], (g >> 1) & 1, ptid == 0, kBarProd, kProdThreads, abort_flag, a.err, a.wait_ns))
         break;
       if (ptid == 0) M3B_TL(g, 1);
       uint8_t* st = sm + s * PL::kStage;
@@ -836,11 +836,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const float gmz = gok ? ldf(p.mimo_z, gi, pd) : 0.f;
       const float gmd = gok ? ldf(p.mimo_down, gi, pd) : 0.f;
       const float gmx = gok ? ldf(p.mimo_x, gi, pd) : 0.f;
-      if (c.part > 0 && lead && !*abort_flag && !flag_wait_geq(a.ho_flag + 2 * c.seq + 1, c.part)) {
+      if (c.part > 0 && lead && !*abort_flag && !flag_wait_geq(a.ho_flag + 2 * c.seq + 1, c.part, a.wait_ns)) {
         *abort_flag = 1;
         record_error(a.err, M3B_ERR_TIMEOUT);
       }
-      if (!role_wait(&bars[BAR_FULL0 + s2], (gs >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))
+      if (!role_wait(&bars[BAR_FULL0 + s2], (gs >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err, a.wait_ns))
         return false;
       const float* scal = reinterpret_cast<const float*>(sm + PL::scal + s2 * PL::scalStride);
       const float d = exp2f(scal[L - 1]);
@@ -928,7 +928,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if constexpr (SO) {
         // state only: the H update of chunk g must be complete before the stage is handed
         // over and before state(g+1) reads H
-        if (!(ok = role_wait(&bars[BAR_HDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
+        if (!(ok = role_wait(&bars[BAR_HDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err, a.wait_ns))) break;
         tc_fence_after();
       } else {
         // z of this thread's row (t, r) and column half, prefetched while the tensor core works
@@ -945,7 +945,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         // S_g (producer) and Yi_g / H update (this role) must be complete before P overwrites B^
         if (lead && !*abort_flag) {
-          if (!mbar_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1) || !mbar_wait(&bars[BAR_HDONE], g & 1)) {
+          if (!mbar_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1, a.wait_ns) || !mbar_wait(&bars[BAR_HDONE], g & 1, a.wait_ns)) {
             *abort_flag = 1;
             record_error(a.err, M3B_ERR_TIMEOUT);
           }
@@ -1035,7 +1035,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           M3B_TL(g, 9);
         }
         // ---- output of chunk g (x_r comes from the X tile of this stage)
-        if (!(ok = role_wait(&bars[BAR_YDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err))) break;
+        if (!(ok = role_wait(&bars[BAR_YDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err, a.wait_ns))) break;
         tc_fence_after();
         if (lead) M3B_TL(g, 10);
         {
@@ -1131,7 +1131,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if (lead) M3B_TL(g, 11);
       // every epilogue thread is done with stage s for chunk g: hand it over for chunk g + 2
       if (lead && g + 2 < G && !*abort_flag) {
-        if (mbar_wait(&bars[BAR_EMPTY0 + s], (g >> 1) & 1)) {
+        if (mbar_wait(&bars[BAR_EMPTY0 + s], (g >> 1) & 1, a.wait_ns)) {
           issue_stage(sc.ahead(pnext, 1), g + 2);
         } else {
           *abort_flag = 1;
@@ -1146,7 +1146,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         } else {
           const int s1 = (g + 1) & 1;
           if (!(ok = role_wait(&bars[BAR_FULL0 + s1], ((g + 1) >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag,
-                               a.err)))
+                               a.err, a.wait_ns)))
             break;
           const float* scal1 = reinterpret_cast<const float*>(sm + PL::scal + s1 * PL::scalStride);
           const float d = exp2f(scal1[L - 1]);
@@ -1298,10 +1298,11 @@ bool fused_supported(const m3b_layer_params& p) {
 }
 
 int launch_fused(const FusedParams& fp, cudaStream_t st, bool bf16) {
+  if (!bf16) return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: bf16 activations only (fp32 runs the tf32 chunk path)");
   switch (fp.prm.R) {
-    case 1: return bf16 ? launch_fused_r<__nv_bfloat16, 1>(fp, st) : launch_fused_r<float, 1>(fp, st);
-    case 2: return bf16 ? launch_fused_r<__nv_bfloat16, 2>(fp, st) : launch_fused_r<float, 2>(fp, st);
-    case 4: return bf16 ? launch_fused_r<__nv_bfloat16, 4>(fp, st) : launch_fused_r<float, 4>(fp, st);
+    case 1: return launch_fused_r<__nv_bfloat16, 1>(fp, st);
+    case 2: return launch_fused_r<__nv_bfloat16, 2>(fp, st);
+    case 4: return launch_fused_r<__nv_bfloat16, 4>(fp, st);
     default: return fail(M3B_ERR_UNSUPPORTED, "ssd_fused: mimo_rank %d", fp.prm.R);
   }
 }

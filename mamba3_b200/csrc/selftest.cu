@@ -101,15 +101,139 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(const __nv_bfloat
   }
 }
 
+// The same GEMM with fp32 operands on kind::tf32 (modes 3-5 mirror 0-2): A (128 x 128 fp32),
+// B (64 x 128 fp32) row-major; tiles of fp32 words in 128-byte column blocks of 32 elements.
+__global__ void __launch_bounds__(128, 1) umma_selftest_tf32_kernel(const float* __restrict__ A,
+                                                                    const float* __restrict__ B,
+                                                                    float* __restrict__ D, int mode, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tA = sm;          // 64 KB
+  uint8_t* tB = sm + 65536;  // 32 KB
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 98304);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 98304 + 16);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    tmem_alloc(tslot, 64);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  // tile A: 128 rows x 128 columns (32 chunks of 4 words per row)
+  for (int u = threadIdx.x; u < 128 * 32; u += blockDim.x) {
+    const int row = u / 32, c = u % 32;
+    float w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) w[e] = mode != 4 ? A[row * 128 + c * 4 + e] : A[(c * 4 + e) * 128 + row];
+    sw128_store_chunk(tA, row, c, 128,
+                      make_uint4(__float_as_uint(w[0]), __float_as_uint(w[1]), __float_as_uint(w[2]),
+                                 __float_as_uint(w[3])));
+  }
+  if (mode != 5) {  // tile B: 64 rows (n) x 128 columns (k)
+    for (int u = threadIdx.x; u < 64 * 32; u += blockDim.x) {
+      const int row = u / 32, c = u % 32;
+      const float4 v = *reinterpret_cast<const float4*>(B + row * 128 + c * 4);
+      sw128_store_chunk(tB, row, c, 64,
+                        make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z),
+                                   __float_as_uint(v.w)));
+    }
+  } else {  // B^T: 128 rows (k) x 64 columns (n)
+    for (int u = threadIdx.x; u < 128 * 16; u += blockDim.x) {
+      const int row = u / 16, c = u % 16;
+      float w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[e] = B[(c * 4 + e) * 128 + row];
+      sw128_store_chunk(tB, row, c, 128,
+                        make_uint4(__float_as_uint(w[0]), __float_as_uint(w[1]), __float_as_uint(w[2]),
+                                   __float_as_uint(w[3])));
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = idesc_tf32(128, 64, mode == 4, mode == 5);
+    for (int kk = 0; kk < 16; ++kk) {
+      const uint64_t ad = mode == 4 ? mnmajor_desc(tA, 128, kk * 8) : kmajor_desc_b(tA, 128, kk * 32);
+      const uint64_t bd = mode == 5 ? mnmajor_desc(tB, 128, kk * 8) : kmajor_desc_b(tB, 64, kk * 32);
+      umma_tf32(tbase, ad, bd, idesc, kk > 0 ? 1u : 0u);
+    }
+    umma_commit(bar);
+  }
+  bool ok = mbar_wait(bar, 0);
+  __syncwarp();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  if (ok) {
+    const int m = 32 * warp + lane;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float v[32];
+      tmem_ld32(tbase + ((uint32_t)(32 * warp) << 16) + 32 * half, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) D[m * 64 + 32 * half + j] = v[j];
+    }
+  } else if (threadIdx.x == 0) {
+    record_error(err, M3B_ERR_TIMEOUT);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 64);
+  }
+}
+
+// One thread waits (bounded by limit_ns) on the flag (mode 0) or on an mbarrier phase nothing
+// completes (mode 1); a wait that runs out records M3B_ERR_TIMEOUT.
+__global__ void __launch_bounds__(32, 1) wait_selftest_kernel(const int* flag, int target, int mode,
+                                                             uint64_t limit_ns, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    const bool ok = mode == 0 ? flag_wait_geq(flag, target, limit_ns) : mbar_wait(&bar, 0, limit_ns);
+    if (!ok) record_error(err, M3B_ERR_TIMEOUT);
+  }
+}
+
 }  // namespace m3b
 
+extern "C" int m3b_selftest_wait(const int* flag, int target, int mode, int64_t limit_ns, int* err, void* stream) {
+  m3b::clear_error();
+  if (mode < 0 || mode > 1 || (mode == 0 && !flag) || !err)
+    return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_wait: mode 0 (flag) or 1 (mbarrier) and an err word");
+  if (limit_ns <= 0 || limit_ns > 1000000000ll)
+    return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_wait: limit_ns must be in (0, 1e9]");
+  m3b::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag, target, mode,
+                                                                            (uint64_t)limit_ns, err);
+  return m3b::check_launch("selftest_wait");
+}
+
 extern "C" int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream) {
-  if (!A || !B || !D || mode < 0 || mode > 2) return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_umma: bad args");
+  if (!A || !B || !D || mode < 0 || mode > 5) return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_umma: bad args");
   if (!m3b::aligned16(A) || !m3b::aligned16(B)) return m3b::fail(M3B_ERR_ALIGNMENT, "selftest_umma: alignment");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (mode >= 3) {
+    const int bytes = 98304 + 64 + 1024;
+    cudaError_t e =
+        cudaFuncSetAttribute(m3b::umma_selftest_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return m3b::fail(M3B_ERR_CUDA, "selftest_umma: %s", cudaGetErrorString(e));
+    m3b::umma_selftest_tf32_kernel<<<1, 128, bytes, st>>>(static_cast<const float*>(A),
+                                                          static_cast<const float*>(B), D, mode, err);
+    return m3b::check_launch("selftest_umma");
+  }
   const int bytes = 49152 + 64 + 1024;
   cudaError_t e = cudaFuncSetAttribute(m3b::umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return m3b::fail(M3B_ERR_CUDA, "selftest_umma: %s", cudaGetErrorString(e));
-  m3b::umma_selftest_kernel<<<1, 128, bytes, static_cast<cudaStream_t>(stream)>>>(
+  m3b::umma_selftest_kernel<<<1, 128, bytes, st>>>(
       static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(B), D, mode, err);
   return m3b::check_launch("selftest_umma");
 }

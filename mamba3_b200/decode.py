@@ -8,9 +8,11 @@ norm, lm_head and the sampling rule -- in a CUDA graph that it replays once per 
 tokens collect on the device; the host reads them once at the end.
 
 Same results as KulaMambaLM.generate with the same sampling arguments; greedy decoding
-(temperature 0) is deterministic.  By default the decoder keeps each layer's previous token in
-the compact form (its rotated B^ and MIMO x, allocate_inference_state(compact=True)), which
-halves the state bytes every step moves; compact=False keeps the reference's prev_BX.
+(temperature 0) is deterministic.  The sampling rule is part of the captured step, so the
+decoder keeps one graph per (temperature, top_k) that prefill() has been given.  By default
+the decoder keeps each layer's previous token in the compact form (its rotated B^ and MIMO x,
+allocate_inference_state(compact=True)), which halves the state bytes every step moves;
+compact=False keeps the reference's prev_BX.
 """
 
 from __future__ import annotations
@@ -40,7 +42,7 @@ class GraphDecoder:
         self.tok = torch.zeros(self.B, 1, dtype=torch.long, device=self.dev)
         self.out = torch.zeros(self.B, max(1, self.n), dtype=torch.long, device=self.dev)
         self.pos = torch.zeros(1, dtype=torch.long, device=self.dev)
-        self.graph = None
+        self.graphs = {}  # one captured step per sampling rule (temperature, top_k)
         self.sampling = None
 
     @staticmethod
@@ -110,7 +112,7 @@ class GraphDecoder:
                 st[k].copy_(sv[k])
         self.tok.copy_(tok0)
         self.pos.copy_(pos0)
-        self.graph = g
+        self.graphs[self.sampling] = g
 
     @torch.no_grad()
     def decode(self, steps=None):
@@ -118,11 +120,14 @@ class GraphDecoder:
         steps = self.n if steps is None else int(steps)
         if steps > self.n:
             raise ValueError("more steps than max_new_tokens")
-        if self.graph is None:
+        if self.sampling is None:
+            raise RuntimeError("decode() before prefill()")
+        if self.sampling not in self.graphs:  # the sampling rule is baked into the captured step
             self._capture()
+        g = self.graphs[self.sampling]
         first = self.tok.clone()
         for _ in range(steps):
-            self.graph.replay()
+            g.replay()
         return first, self.out[:, :steps]
 
     @torch.no_grad()

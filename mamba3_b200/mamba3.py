@@ -8,9 +8,10 @@ kernels of ``libmamba3_b200`` (see ``ops.py``):
 
 * ``forward`` / ``prefill`` -> ``mamba3_b200::layer_ssd`` (chunked parallel form)
 * ``step``                  -> ``mamba3_b200::step_ssm`` (O(1) recurrent form)
-* with gradients (training) -> torch autograd for the projection split, norms, rotation,
-  MIMO and gate around ``chunked_ssd``, whose forward and backward are the library's
-  kernels (``ssd.ChunkedSSDFn``)
+* with gradients (training) -> the library's kernels forward and backward for the B / C
+  preparation, the x-side MIMO weights, ``chunked_ssd`` and the gate; only the projection
+  split and dt are torch ops.  There is no other path: where the kernels do not apply the
+  call raises.
 
 Deviation from the reference (documented): the ``angle`` entry of the inference
 state is kept in fp32 whatever the model dtype (the reference accumulates it in
@@ -25,7 +26,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import ops
+from . import _lib, ops
 from .ssd import chunked_ssd
 
 
@@ -66,15 +67,13 @@ class _GateFn(torch.autograd.Function):
 
 
 def _gate(y, z, mimo_z, mimo_down):
-    """y (B,T,H,P,R), z (B,T,H*P) -> (B,T,H*P).  The kernels take one dtype and R <= 4; other
-    combinations (e.g. fp32 parameters with bf16 activations) use the torch expression."""
+    """y (B,T,H,P,R), z (B,T,H*P) -> (B,T,H*P) through the gate kernels.  Parameters of another
+    dtype than the activations (fp32 master weights under autocast) are cast to the activation
+    dtype first; the cast is part of the autograd graph, so their gradients still arrive."""
     R = mimo_z.shape[-1]
-    if (y.is_cuda and R <= 4 and y.is_contiguous() and z.stride(-1) == 1
-            and len({y.dtype, z.dtype, mimo_z.dtype, mimo_down.dtype}) == 1):
-        return _GateFn.apply(y, z, mimo_z, mimo_down)
-    Bat, T = y.shape[:2]
-    z_r = z.reshape(Bat, T, *mimo_z.shape[:2], 1) * mimo_z
-    return (y * F.silu(z_r) * mimo_down).sum(-1).reshape(Bat, T, -1)
+    if not (y.is_cuda and R <= 4 and z.stride(-1) == 1 and y.dtype == z.dtype):
+        raise _lib.M3bError("gate: CUDA activations of one dtype, mimo_rank <= 4 expected (no other path)")
+    return _GateFn.apply(y.contiguous(), z, mimo_z.to(y.dtype), mimo_down.to(y.dtype))
 
 
 class _BCFn(torch.autograd.Function):
@@ -120,16 +119,6 @@ class _XFn(torch.autograd.Function):
         dxf, dmx, dlam, ddt, dA = ops.xprep_bwd(xf, mimo_x, lam_raw, dt, A, z(dxr), z(dxg) if trap else None,
                                                 z(dxb) if trap else None)
         return (dxf, dmx, dlam, ddt, dA) if trap else (dxf, dmx, None, None, None)
-
-
-def _rope_pairs(t, c, s):
-    """Rotate (..., N, R) pairwise along N -- pairs (2i, 2i+1), the same angle for every rank --
-    by angles with cosines c and sines s of shape (..., N/2) (mamba3/mamba3.py:38-45)."""
-    *lead, N, R = t.shape
-    tp = t.reshape(*lead, N // 2, 2, R)
-    a, b = tp[..., 0, :], tp[..., 1, :]
-    c, s = c[..., None], s[..., None]
-    return torch.stack([a * c - b * s, a * s + b * c], dim=-2).reshape(*lead, N, R)
 
 
 class KulaMamba(nn.Module):
@@ -232,10 +221,11 @@ class KulaMamba(nn.Module):
 
     def _ssd_train(self, proj, dt_scale, return_state):
         """Differentiable path between in_proj and out_proj (mamba3/mamba3.py:192-256): torch ops
-        for the split, dt, MIMO and trapezoid scaling; library kernels (forward and backward) for
-        the B/C norm + bias + rotation + shift (_BCFn), chunked_ssd and the gate (_GateFn).
-        The x-side MIMO expansion and trapezoid weights run as one kernel each way (_XFn).
-        -> y (B,T,d_inner) [, state]."""
+        for the split and dt; library kernels (forward and backward) for the B/C norm + bias +
+        rotation + shift (_BCFn), the x-side MIMO expansion and trapezoid weights (_XFn),
+        chunked_ssd and the gate (_GateFn).  Parameters are cast to the activation dtype (so fp32
+        master weights train under autocast); the returned angle state is fp32, as everywhere in
+        this package.  -> y (B,T,d_inner) [, state]."""
         Bat, T, _ = proj.shape
         H, P, N, R, G = self.nheads, self.headdim, self.d_state, self.mimo_rank, self.ngroups
         sizes = [self.d_inner, self._d_x, self._d_bc, self._d_bc, H]
@@ -249,27 +239,22 @@ class KulaMamba(nn.Module):
         if dt_scale is not None:
             dt = dt * dt_scale
         A = -torch.exp(self.A_log)
-        if self._bc_kernel_ok(proj, dt):
-            B_r, B_b, C_r = _BCFn.apply(Bf, Cf, theta, dt, self.B_norm.weight, self.B_bias, self.C_norm.weight,
-                                        self.C_bias, H, self.B_norm.eps, self.use_trapezoidal)
-            cum = None
-            if return_state and self.use_complex_ssm:
-                cum = -(dt.float()[..., None] * theta.float()[..., None, :]).sum(1, keepdim=True)  # (B,1,H,N/2)
-        else:
-            B_r, B_b, C_r, cum = self._bc_torch(Bf, Cf, theta, dt)
-        if self._x_kernel_ok(proj, dt, A):
-            x_r, x_g, x_b = _XFn.apply(xf, self.mimo_x, lam_raw, dt, A)
-            if not self.use_trapezoidal:
-                x_g, x_b, B_b = x_r, None, None
-        else:
-            x_r = xf.reshape(Bat, T, H, P, 1) * self.mimo_x
-            if self.use_trapezoidal:
-                lam = torch.sigmoid(lam_raw)
-                x_g = x_r * lam[..., None, None]
-                scale_b = ((1.0 - lam) * torch.exp(A * dt))[..., None, None]
-                x_b = F.pad(x_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) * scale_b
-            else:
-                x_g, x_b, B_b = x_r, None, None
+        ad = proj.dtype
+        if not self._bc_kernel_ok(proj, dt):
+            raise _lib.M3bError("training path: the B / C kernels take CUDA activations, H * d_state / 2 <= 2048 "
+                                "and equal B / C norm eps (no other path)")
+        B_r, B_b, C_r = _BCFn.apply(Bf, Cf, theta, dt, self.B_norm.weight.to(ad), self.B_bias.to(ad),
+                                    self.C_norm.weight.to(ad), self.C_bias.to(ad), H, self.B_norm.eps,
+                                    self.use_trapezoidal)
+        cum = None
+        if return_state and self.use_complex_ssm:
+            cum = -(dt.float()[..., None] * theta.float()[..., None, :]).sum(1, keepdim=True)  # (B,1,H,N/2)
+        if not self._x_kernel_ok(proj, dt, A):
+            raise _lib.M3bError("training path: the x kernels take CUDA activations, headdim <= 256 and "
+                                "mimo_rank <= 4 (no other path)")
+        x_r, x_g, x_b = _XFn.apply(xf, self.mimo_x.to(ad), lam_raw, dt, A)
+        if not self.use_trapezoidal:
+            x_g, x_b, B_b = x_r, None, None
         out = chunked_ssd(x_g, x_b, B_r, B_b, C_r, dt, A, self.D, x_r, self.chunk_size,
                           return_final_state=return_state)
         y = _gate(out.y, z, self.mimo_z, self.mimo_down).reshape(Bat, T, self.d_inner)
@@ -280,38 +265,20 @@ class KulaMamba(nn.Module):
         return y, {"h": out.h_final.float(), "angle": angle, "prev_BX": prev_bx}
 
     def _x_kernel_ok(self, proj, dt, A):
-        """The x kernels apply: CUDA, mimo_x of the projection's float dtype, P <= 256, R <= 4."""
+        """The x kernels apply: CUDA float activations, P <= 256, R <= 4 (parameters are cast to the
+        activation dtype by the caller)."""
         fl = (torch.float32, torch.bfloat16, torch.float16)
-        return (proj.is_cuda and proj.dtype in fl and self.mimo_x.dtype == proj.dtype and dt.dtype in fl
-                and A.dtype in fl and self.headdim <= 256 and self.mimo_rank <= 4)
+        return (proj.is_cuda and proj.dtype in fl and dt.dtype in fl and A.dtype in fl and self.headdim <= 256
+                and self.mimo_rank <= 4)
 
     def _bc_kernel_ok(self, proj, dt):
-        """The B / C kernels apply: CUDA, one float dtype for the projection and the four B / C
-        parameters, equal norm eps, H * N / 2 <= 2048 and the backward's rows in shared memory."""
+        """The B / C kernels apply: CUDA float activations, equal norm eps, H * N / 2 <= 2048 and the
+        backward's rows in shared memory (parameters are cast to the activation dtype by the caller)."""
         H, N, R, G = self.nheads, self.d_state, self.mimo_rank, self.ngroups
-        ps = (self.B_norm.weight, self.B_bias, self.C_norm.weight, self.C_bias)
         floats = 10 * G * N * R + 2 * H * N * R + 2 * N * R + 4 * G
         return (proj.is_cuda and proj.dtype in (torch.float32, torch.bfloat16, torch.float16)
-                and all(p.dtype == proj.dtype for p in ps) and dt.dtype in (torch.float32, torch.bfloat16, torch.float16)
+                and dt.dtype in (torch.float32, torch.bfloat16, torch.float16)
                 and self.B_norm.eps == self.C_norm.eps and H * (N // 2) <= 2048 and floats * 4 <= 200 * 1024)
-
-    def _bc_torch(self, Bf, Cf, theta, dt):
-        """The same as _BCFn in torch ops (mamba3/mamba3.py:203-232) for the cases the kernels
-        do not take.  -> (B_g, B_b or None, C, cum or None)."""
-        Bat, T = Bf.shape[:2]
-        N, R, G = self.d_state, self.mimo_rank, self.ngroups
-        B_r = self.B_norm(Bf.reshape(Bat, T, G, N * R)).reshape(Bat, T, G, N, R) + self.B_bias
-        C_r = self.C_norm(Cf.reshape(Bat, T, G, N * R)).reshape(Bat, T, G, N, R) + self.C_bias
-        if self.heads_per_group > 1:
-            B_r = B_r.repeat_interleave(self.heads_per_group, dim=2)
-            C_r = C_r.repeat_interleave(self.heads_per_group, dim=2)
-        cum = None
-        if self.use_complex_ssm:
-            cum = -(dt[..., None] * theta[..., None, :]).cumsum(dim=1)  # (B,T,H,N/2)
-            c, s = torch.cos(cum), torch.sin(cum)
-            B_r, C_r = _rope_pairs(B_r, c, s), _rope_pairs(C_r, c, s)
-        B_b = F.pad(B_r[:, :-1], (0, 0, 0, 0, 0, 0, 1, 0)) if self.use_trapezoidal else None
-        return B_r, B_b, C_r, cum
 
     def _ssd(self, x, dt_scale, return_state, state=None):
         if x.dim() != 3 or x.shape[1] <= 0:

@@ -29,10 +29,10 @@ import torch.nn.functional as F
 
 
 def rotate_pairs(s: torch.Tensor, ang: torch.Tensor) -> torch.Tensor:
-    """Rot(ang) on the (2i, 2i+1) columns of s (B, H, P, N) with ang (B, H, N/2):
+    """Rot(ang) on the (2i, 2i+1) columns of s (..., P, N) with ang (..., N/2):
     (s0, s1) -> (s0 cos - s1 sin, s0 sin + s1 cos), the rotation the layer applies to B."""
-    c = torch.cos(ang).unsqueeze(2)
-    sn = torch.sin(ang).unsqueeze(2)
+    c = torch.cos(ang).unsqueeze(-2)
+    sn = torch.sin(ang).unsqueeze(-2)
     s0, s1 = s[..., 0::2], s[..., 1::2]
     return torch.stack((s0 * c - s1 * sn, s0 * sn + s1 * c), dim=-1).flatten(-2)
 
@@ -68,11 +68,24 @@ def zero_state(like: dict) -> dict:
 
 
 def fold(affs: list, upto: int) -> dict:
-    """Initial state of shard `upto` from the summaries of shards 0 .. upto-1."""
-    st = zero_state(affs[0])
-    for g in range(upto):
-        st = advance(st, affs[g])
-    return st
+    """Initial state of shard `upto` from the summaries of shards 0 .. upto-1, in a fixed number
+    of batched tensor operations whatever `upto` is.  Unrolling advance() from the zero state:
+    the angle before shard g is a_g = sum_{j<g} Om_j, shard g's incoming prev_BX is
+    pb_g = Rot(a_{g-1}) PB_{g-1} (zero for g = 0), and
+        h = sum_{g<upto} exp(sum_{g<j<upto} Lam_j) (e^Lam_g c0_g pb_g + Rot(a_g) S_g)."""
+    if upto <= 0:
+        return zero_state(affs[0])
+    st = {k: torch.stack([a[k] for a in affs[:upto]]) for k in _KEYS}  # leading dim: shard g
+    om_c = torch.cumsum(st["Om"], 0)
+    a_g = om_c - st["Om"]                                   # angle before shard g
+    rs = rotate_pairs(st["S"], a_g)
+    rpb = rotate_pairs(st["PB"], a_g)                       # shard g's final prev_BX, global frame
+    pb_in = torch.cat([torch.zeros_like(rpb[:1]), rpb[:-1]])
+    lam = st["Lam"]
+    after = lam.sum(0, keepdim=True) - torch.cumsum(lam, 0)  # sum_{g<j<upto} Lam_j
+    w = lambda t: t.unsqueeze(-1).unsqueeze(-1)  # noqa: E731  (B,H) -> (B,H,1,1)
+    h = (w(torch.exp(after)) * (w(torch.exp(lam) * st["c0"]) * pb_in + rs)).sum(0)
+    return {"h": h, "angle": om_c[-1], "prev_BX": rpb[-1]}
 
 
 _KEYS = ("S", "PB", "Om", "Lam", "c0")
@@ -92,11 +105,21 @@ def unpack(buf: torch.Tensor, like: dict) -> dict:
 
 
 def exchange(aff: dict, group=None) -> list:
-    """all_gather of every rank's summary (one flat fp32 buffer per rank)."""
+    """all_gather of every rank's summary (one flat fp32 buffer per rank).  A first all_gather of
+    the summaries' shapes makes every rank raise ValueError, instead of exchanging garbage, when
+    the ranks do not hold the same problem (batch rows, heads, headdim, d_state)."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     mine = pack(aff)
+    shape = torch.tensor([d for k in _KEYS for d in (*aff[k].shape, -1)], dtype=torch.int64, device=mine.device)
+    head = torch.zeros(64, dtype=torch.int64, device=mine.device)
+    head[:min(64, shape.numel())] = shape[:64]
+    heads = [torch.empty_like(head) for _ in range(world)]
+    dist.all_gather(heads, head, group=group)
+    if any(not torch.equal(h, heads[0]) for h in heads):
+        raise ValueError("seqpar.exchange: ranks hold summaries of different shapes "
+                         f"({[h[h != 0].tolist()[:8] for h in heads]})")
     bufs = [torch.empty_like(mine) for _ in range(world)]
     dist.all_gather(bufs, mine, group=group)
     return [unpack(b, aff) for b in bufs]

@@ -29,6 +29,23 @@ def test_umma_selftest(mode):
     assert max_rel(to_np(D), to_np(ref)) < 1e-5
 
 
+@pytest.mark.parametrize("mode", [3, 4, 5])
+def test_umma_selftest_tf32(mode):
+    """kind::tf32 with fp32 tiles (K-major A and B, MN-major A, MN-major B): the product of the
+    operands rounded to tf32 (10 mantissa bits), accumulated in fp32."""
+    from mamba3_b200 import _lib
+
+    g = torch.Generator().manual_seed(200 + mode)
+    A = torch.randn(128, 128, generator=g).cuda()
+    B = torch.randn(64, 128, generator=g).cuda()
+    D, err = _lib.selftest_umma(A, B, mode)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    exact = A.double() @ B.double().T
+    # tf32 operands (2^-11 relative per element): well inside 1e-3, where bf16 operands are not
+    assert max_rel(to_np(D), to_np(exact)) < 1e-3
+
+
 @pytest.mark.parametrize("case", SCAN_CASES)
 def test_scan_golden(case):
     from mamba3_b200 import ssd_scan

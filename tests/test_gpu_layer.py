@@ -1,8 +1,8 @@
 """Layer-level parity of the chunked tensor-core forward / prefill on the GPU.
 
-* fp32 models against the reference's golden outputs (the tensor-core operands are
-  bf16, so fp32 I/O is held to the bf16 tolerance 2e-2; fp32-accumulated states to 2e-2,
-  the angle -- pure fp32 arithmetic -- to 1e-4);
+* fp32 models against the reference's golden outputs at 1e-3 (fp32 activations run the
+  chunk-parallel kernels with tf32 tensor-core operands; the angle -- pure fp32
+  arithmetic -- to 1e-4);
 * bf16 models against the fp64 oracle on the same bf16-rounded weights (2e-2);
 * properties at the benchmark sizes: causality (a prefix of the full-size output equals
   the oracle on that prefix), chaining (prefill of a split sequence == prefill of the
@@ -20,6 +20,7 @@ from helpers import oracle_params, ours_layer_from_golden, to_np
 pytestmark = pytest.mark.gpu
 
 BF16_TOL = 2e-2
+FP32_TOL = 1e-3
 
 
 @pytest.fixture(params=[1, 2], ids=["fused", "chunked"], autouse=True)
@@ -41,9 +42,9 @@ def test_forward_prefill_golden_fp32(case):
     with torch.no_grad():
         y = m(x)
         y2, st = m.prefill(x)
-    assert max_rel(to_np(y), d["y"]) < BF16_TOL
-    assert max_rel(to_np(y2), d["y"]) < BF16_TOL
-    assert max_rel(to_np(st["h"]), d["pf_h"]) < BF16_TOL
+    assert max_rel(to_np(y), d["y"]) < FP32_TOL
+    assert max_rel(to_np(y2), d["y"]) < FP32_TOL
+    assert max_rel(to_np(st["h"]), d["pf_h"]) < FP32_TOL
     assert max_rel(to_np(st["angle"]), d["pf_angle"]) < 1e-4
     assert max_rel(to_np(st["prev_BX"]), d["pf_prev_BX"]) < 1e-4
 
@@ -77,7 +78,7 @@ def test_parallel_equals_recurrent(case):
         for t in range(T):
             yt, st = m.step(x[:, t:t + 1], st)
             ys.append(yt[:, 0])
-    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < BF16_TOL
+    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < FP32_TOL
 
 
 @pytest.mark.parametrize("R", [1, 2, 3, 4])
@@ -96,7 +97,7 @@ def test_parallel_equals_recurrent_n128(R):
         for t in range(x.shape[1]):
             yt, st = m.step(x[:, t:t + 1], st)
             ys.append(yt[:, 0])
-    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < BF16_TOL
+    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < FP32_TOL
 
 
 def test_chaining_prefill_from_state():
@@ -128,7 +129,7 @@ def test_extreme_decay_finite():
     assert torch.isfinite(y).all() and y.abs().max() > 0
     p = oracle_params(m)
     oy, _ = oracle.layer_forward(p, to_np(x))
-    assert max_rel(to_np(y), oy) < BF16_TOL
+    assert max_rel(to_np(y), oy) < FP32_TOL
 
 
 def test_mixed_decay_heads_n128():
@@ -291,8 +292,7 @@ def test_dt_scale_matches_oracle():
 
 def test_long_sequence_forward_equals_steps():
     """Reference test tests:698-728 at its size (T = 512, small layer, fp32): forward vs 512 decode
-    steps.  The forward's products run on bf16 tensor-core operands, hence 2e-2 here (the
-    reference, all fp32, asks 1e-3)."""
+    steps, at the reference's own 1e-3."""
     from mamba3_b200 import KulaMamba
 
     torch.manual_seed(73)
@@ -306,7 +306,7 @@ def test_long_sequence_forward_equals_steps():
             yt, st = m.step(x[:, t:t + 1], st)
             ys.append(yt[:, 0])
     assert torch.isfinite(y_par).all()
-    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < BF16_TOL
+    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < FP32_TOL
 
 
 def test_mimo_ranks_interact():
@@ -341,4 +341,4 @@ def test_dt_scale_steps_equal_forward(compact):
         for t in range(40):
             yt, st = m.step(x[:, t:t + 1], st, dt_scale=ds[:, t])
             ys.append(yt[:, 0])
-    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < BF16_TOL
+    assert max_rel(to_np(torch.stack(ys, 1)), to_np(y_par)) < FP32_TOL

@@ -116,6 +116,72 @@ def test_exchange_over_gloo_world2():
     assert res[1] < 1e-5  # fp32 exchange
 
 
+def _free_port():
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_fault_worker(rank, world, port, scenario, out_q):
+    """Failure scenarios of the exchange on CPU ranks (no GPU): 'mismatch' -- rank 1 holds a
+    different problem (one batch row instead of two); 'departed' -- rank 1 leaves the group
+    between steps, before the exchange, and rank 0's exchange must end with an error within the
+    process group's timeout instead of waiting for good."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from mamba3_b200 import seqpar
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    try:
+        m, p, x = _setup(seed=5)
+        a, b = _shards(x.shape[1], world)[rank]
+        if scenario == "mismatch" and rank == 1:
+            x = x[:1]
+        if scenario == "departed" and rank == 1:
+            out_q.put((rank, "left"))
+            return  # leaves between steps: no collective in flight
+        aff = {k: v.float() for k, v in _summary(m, p, x[:, a:b]).items()}
+        try:
+            seqpar.exchange(aff)
+            out_q.put((rank, "no error"))
+        except ValueError as e:
+            out_q.put((rank, f"ValueError: {e}"))
+        except Exception as e:  # noqa: BLE001  (gloo raises RuntimeError / DistBackendError)
+            out_q.put((rank, f"{type(e).__name__}"))
+    finally:
+        if not (scenario == "departed" and rank == 1):
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("scenario", ["mismatch", "departed"])
+def test_exchange_failures_over_gloo(scenario):
+    import time
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_fault_worker, args=(r, 2, port, scenario, q)) for r in range(2)]
+    t0 = time.time()
+    for pr in procs:
+        pr.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for pr in procs:
+        pr.join(timeout=60)
+    assert time.time() - t0 < 100
+    if scenario == "mismatch":
+        assert res[0].startswith("ValueError") and res[1].startswith("ValueError"), res
+        assert "different shapes" in res[0]
+    else:
+        assert res[1] == "left"
+        assert res[0] != "no error", res  # the remaining rank's exchange failed instead of hanging
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("shards", [2, 4])
 def test_sharded_prefill_on_one_gpu(shards):

@@ -22,11 +22,11 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-2  # the bf16 tolerance used by the layer parity tests
 
 
-def _layer():
+def _layer(d_model=128):
     from mamba3_b200 import KulaMamba
 
     torch.manual_seed(3)
-    return KulaMamba(d_model=128, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
+    return KulaMamba(d_model=d_model, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
 
 
 def _args(m, proj, y, h_final, angle, prev_bx):
@@ -47,16 +47,25 @@ def _outputs(proj, H, P, N):
             torch.empty(Bt, H, N // 2, **f32), torch.empty(Bt, H, P, N, **f32))
 
 
-def test_noalloc_matches_allocating_entry_point_twice():
+@pytest.mark.parametrize("d_model,B,T", [(128, 2, 150), (768, 8, 1000)], ids=["whole", "parts"])
+def test_noalloc_matches_allocating_entry_point_twice(d_model, B, T):
+    """"whole": 4 (batch, head) sequences, one per CTA.  "parts": 192 sequences of 16 chunks, more
+    than the SMs, so the fused kernel cuts them into parts handed from CTA to CTA through the
+    scratch (states, angles and the flags that order the hand-offs); the second call finds the
+    first call's flags in the shared scratch and must not be misled by them."""
     from mamba3_b200 import _lib
 
-    m = _layer()
+    m = _layer(d_model)
     L = _lib.lib()
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     H, P, N = m.nheads, m.headdim, m.d_state
+    if d_model == 768:  # the workspace holds the part hand-off buffers and fits the static scratch
+        proj0 = torch.empty(B, T, m.in_proj.out_features, dtype=torch.bfloat16, device="cuda")
+        ws = L.m3b_layer_fwd_workspace(C.byref(_args(m, proj0, *_outputs(proj0, H, P, N))))
+        assert B * H * P * N * 4 < ws <= (32 << 20), ws
     for call, seed in enumerate((11, 12)):
         g = torch.Generator().manual_seed(seed)
-        x = torch.randn(2, 150, 128, generator=g).cuda().to(torch.bfloat16)
+        x = torch.randn(B, T, d_model, generator=g).cuda().to(torch.bfloat16)
         with torch.no_grad():
             proj = m.in_proj(x).contiguous()
         ref = _outputs(proj, H, P, N)
