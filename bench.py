@@ -9,8 +9,9 @@ full config-1 batch on its own GPU (batch sharding, no collective).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-`--impl reference` times the reference algorithm on the host CPU (the numpy
-restatement in oracle/, all host cores) on a bounded sample of the same workload.
+`--impl reference` times the unmodified reference (pip-installed into baseline/_ref)
+on the host CPU, all cores, on a bounded sample of the same workload (2 rows x 512
+tokens per step); the GPU arm's cpu_baseline times the same sample.
 Prints one JSON line on rank 0.
 """
 
@@ -36,7 +37,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-sample-tokens", type=int, default=512)
+    ap.add_argument("--cpu-steps", type=int, default=12, help="timed reference steps of the cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override config-1 batch (profiling captures)")
     ap.add_argument("--seqlen", type=int, default=None, help="override config-1 seqlen (profiling captures)")
@@ -52,54 +53,91 @@ def parse():
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the oracle (numpy restatement of the reference) on host cores
+# CPU baseline and reference arm: the unmodified reference on the host cores
 # ---------------------------------------------------------------------------
-def cpu_baseline(sample_tokens: int, rows: int | None = None):
-    """Time the reference algorithm (oracle port, fp32) on `rows` rows x `sample_tokens` tokens of
-    config 1, one row per worker thread (numpy releases the GIL in its kernels)."""
-    import concurrent.futures as cf
+# One reference step is a bounded sample of the config-1 workload: REF_ROWS rows of REF_TOKENS
+# tokens through the reference's own KulaMamba.forward (mamba3/mamba3.py:260) on the CPU, fp32
+# (its CPU path; the bf16 cast of config 1 is a GPU-side choice).  The same sample serves the GPU
+# arm's cpu_baseline and the --impl reference arm.
+REF_ROWS, REF_TOKENS = 2, 512
 
-    import numpy as np
+
+def _reference_package():
+    """The unmodified reference package (dorayaku/mamba3), pip-installed into baseline/_ref, or None."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "mamba3" / "__init__.py").exists():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    import mamba3
+
+    return mamba3
+
+
+def _cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def reference_cpu(steps: int, warmup: int, rows: int = REF_ROWS, tokens: int = REF_TOKENS):
+    """Time `steps` reference steps (after `warmup` untimed ones) on all host cores.  Uses the
+    reference itself from baseline/_ref; without it, the numpy restatement in oracle/ (kind
+    "port")."""
     import torch
 
-    import oracle
-    from mamba3_b200.mamba3 import KulaMamba
-
     cores = len(os.sched_getaffinity(0))
-    rows = rows or cores
-    torch.manual_seed(0)
-    m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2, chunk_size=64)
-    sd = {k: v.float().numpy() for k, v in m.state_dict().items()}
-    p = oracle.LayerParams.from_state_dict(sd, d_model=768, d_state=128, headdim=64, mimo_rank=2, chunk_size=64,
-                                           dtype=np.float32)
-    g = torch.Generator().manual_seed(1)
-    x = torch.randn(rows, sample_tokens, 768, generator=g).numpy()
-    oracle.layer_forward(p, x[:1, :64])  # warm the allocator / BLAS
-    t0 = time.perf_counter()
-    with cf.ThreadPoolExecutor(max_workers=cores) as ex:
-        list(ex.map(lambda r: oracle.layer_forward(p, x[r:r + 1]), range(rows)))
-    dt = time.perf_counter() - t0
-    return {"value": rows * sample_tokens / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{rows} rows x {sample_tokens} tokens of config 1, fp32 numpy oracle, one row per thread",
-            "seconds": round(dt, 2)}
+    M = _reference_package()
+    x = torch.randn(rows, tokens, 768, generator=torch.Generator().manual_seed(1))
+    if M is not None:
+        torch.set_num_threads(cores)
+        torch.manual_seed(0)
+        layer = M.KulaMamba(d_model=768, d_state=128, expand=2, headdim=64, mimo_rank=2, chunk_size=64).eval()
+        run = lambda: layer(x)  # noqa: E731
+        kind, what = "reference", "the reference's KulaMamba.forward (baseline/_ref, torch CPU, fp32)"
+    else:
+        import numpy as np
+
+        import oracle
+        from mamba3_b200.mamba3 import KulaMamba
+
+        torch.manual_seed(0)
+        m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2, chunk_size=64)
+        sd = {k: v.float().numpy() for k, v in m.state_dict().items()}
+        p = oracle.LayerParams.from_state_dict(sd, d_model=768, d_state=128, headdim=64, mimo_rank=2,
+                                               chunk_size=64, dtype=np.float32)
+        xn = x.numpy()
+        run = lambda: oracle.layer_forward(p, xn)  # noqa: E731
+        kind, what = "port", "the numpy restatement of the reference in oracle/ (baseline/_ref absent), fp32"
+    with torch.no_grad():
+        for _ in range(max(1, warmup)):
+            run()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            run()
+        dt = time.perf_counter() - t0
+    return {"value": steps * rows * tokens / dt, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"{rows} rows x {tokens} tokens of config 1 per step, {steps} timed steps after {warmup}; "
+                      f"{what}; host CPU: {_cpu_model()}",
+            "seconds": round(dt, 2), "ms_per_step": dt / steps * 1e3}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    vals = []
-    cpu_baseline(64, rows=1)  # warm-up: allocator, BLAS threads
-    per_step = max(64, min(512, 2048 // max(1, args.steps)))
-    for _ in range(args.steps):
-        vals.append(cpu_baseline(per_step))
-    v = sum(b["value"] for b in vals) / len(vals)
-    cb = dict(vals[-1])
-    cb["value"] = v
+    cb = reference_cpu(args.steps, args.warmup)
+    v = cb["value"]
     line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config 1: KulaMamba layer forward, x (16, 4096, 768)", "sampled": cb["sample"]},
+            "config": {"workload": "config 1: KulaMamba layer forward (d_model 768, d_state 128, headdim 64, "
+                                   "mimo_rank 2), x (16, 4096, 768) per GPU",
+                       "sampled": cb["sample"]},
             "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -606,7 +644,7 @@ def run_ours(args):
         if train is not None:
             line["train_step"] = train
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args.cpu_sample_tokens)
+            line["cpu_baseline"] = reference_cpu(args.cpu_steps, 2)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
