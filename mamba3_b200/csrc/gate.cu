@@ -122,6 +122,9 @@ template <typename T, int R>
 int gate_bwd_t(const m3b_gate_args* a, float* part, cudaStream_t st) {
   const int C = a->channels;
   const int64_t nchunks = (a->rows + kGateRows - 1) / kGateRows;
+  if (nchunks > 65535)  // one grid row per chunk of rows; gridDim.y is at most 65535
+    return fail(M3B_ERR_UNSUPPORTED, "gate_bwd: %lld rows exceed %lld (65535 chunks of %d rows)",
+                (long long)a->rows, 65535LL * kGateRows, kGateRows);
   if (nchunks > 0) {
     dim3 grid((unsigned)((C + kGateThreads - 1) / kGateThreads), (unsigned)nchunks);
     gate_bwd_kernel<T, R><<<grid, kGateThreads, 0, st>>>(

@@ -824,7 +824,14 @@ extern "C" int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* ws, size_t w
   if (!a) return fail(M3B_ERR_INVALID_ARG, "chunked_ssd_bwd: null args");
   int rc = bvalidate(a);
   if (rc != M3B_OK) return rc;
-  if (a->batch == 0) return M3B_OK;
+  if (a->batch == 0) {  // no tokens: the per-head gradients are zero, not left unwritten
+    const cudaStream_t st0 = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (a->dA) e = cudaMemsetAsync(a->dA, 0, sizeof(float) * (size_t)a->H, st0);
+    if (e == cudaSuccess && a->dD) e = cudaMemsetAsync(a->dD, 0, sizeof(float) * (size_t)a->H, st0);
+    if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "chunked_ssd_bwd: %s", cudaGetErrorString(e));
+    return M3B_OK;
+  }
   const BwdLayout w = bwd_layout(a);
   if (!ws || ws_bytes < w.total)
     return fail(M3B_ERR_WORKSPACE, "chunked_ssd_bwd: need %zu workspace bytes", w.total);

@@ -145,5 +145,7 @@ def test_chunked_backward_with_bf16_operands_stays_within_training_tolerance():
                                                     dy[0, :, h], zero, zero, L, q=bf)
         assert rel(dX2[..., :R], ref["x_g"][0, :, h]) < 1e-2
         assert rel(dB2[..., :R], ref["B_g"][0, :, h]) < 1e-2
+        assert rel(dX2[..., R:], ref["x_b"][0, :, h]) < 1e-2  # the trapezoid halves feed the x / B
+        assert rel(dB2[..., R:], ref["B_b"][0, :, h]) < 1e-2  # preparation backwards
         assert rel(dC, ref["C"][0, :, h]) < 1e-2
         assert rel(ddt, ref["dt"][0, :, h]) < 3e-2
