@@ -453,8 +453,8 @@ M3B_API int m3b_scaled_add(const void* x, const void* h, float scale, void* out,
  * D (128 x 64, fp32) = A (128 x 128 bf16, row-major) x B (64 x 128 bf16, row-major)^T,
  * staged through the same shared-memory layouts and UMMA descriptors as the chunk
  * kernels: mode 0 reads A K-major, mode 1 stages A transposed and reads it MN-major,
- * mode 2 stages B transposed and reads it MN-major.  Modes 3-5 are the same three layouts
- * with fp32 A and B on kind::tf32 (the tiles of the fp32 chunk kernels).
+ * mode 2 stages B transposed and reads it MN-major.  Mode 3 takes fp32 A and B on
+ * kind::tf32, both K-major (the tiles of the fp32 chunk kernels).
  * ------------------------------------------------------------------------ */
 M3B_API int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream);
 

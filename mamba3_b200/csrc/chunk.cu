@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kCT, 1) chunk_state_kernel(FwdParams a) {
     if (k == 0) a.coef0[(int64_t)b * p.H + h] = bpr[0];
   }
   __syncthreads();
-  chunk_produce_bc<TA, R, true, false>(a, sm, b, k, g);
+  chunk_produce_bc<TA, R, true, false, PL::F32>(a, sm, b, k, g);  // fp32: B^ transposed (K-major A)
   if constexpr (PL::F32) __syncthreads();  // the angles (in the X tile region) have been read
   chunk_produce_x<TA, RP, true>(a, sm, b, k, h);
   fence_async_smem();
@@ -184,10 +184,10 @@ __global__ void __launch_bounds__(kCT, 1) chunk_state_kernel(FwdParams a) {
   const uint32_t tbase = *tslot;
   if (threadIdx.x == 0) {
     if constexpr (PL::F32) {
-      constexpr uint32_t idesc = idesc_tf32(128, kPP, /*a_mn=*/true, /*b_mn=*/false);
+      constexpr uint32_t idesc = idesc_tf32(128, kPP, /*a_mn=*/false, /*b_mn=*/false);
 #pragma unroll
       for (int kk = 0; kk < 16; ++kk)
-        umma_tf32(tbase, mnmajor_desc(sm + PL::tileB, 128, kk * 8), kmajor_desc_b(sm + PL::tileX, kPP, kk * 32),
+        umma_tf32(tbase, kmajor_desc_b(sm + PL::tileB, 128, kk * 32), kmajor_desc_b(sm + PL::tileX, kPP, kk * 32),
                   idesc, kk > 0 ? 1u : 0u);
     } else {
       constexpr uint32_t idesc = idesc_bf16(128, kPP, /*a_mn=*/true, /*b_mn=*/false);

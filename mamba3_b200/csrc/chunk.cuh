@@ -139,17 +139,31 @@ struct Plan {
   static_assert(!F32 || L * 64 * 4 <= 64 * 128 * E, "fp32 plan: the angles fit the X tile region");
 };
 
+// fp32 -> the nearest tf32 value (10 mantissa bits, ties away from zero), as an fp32 word.  The
+// tensor core reads only the upper 19 bits of a tf32 operand, i.e. it would truncate an fp32
+// word; rounding first halves the error and removes its bias towards zero.
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// Byte offset of fp32 element (row, col) in a K-major SW128 tile of `rows` rows (128-byte column
+// blocks of 32 elements).
+__device__ __forceinline__ uint32_t sw128_offset_f32(int row, int col, int rows) {
+  const int cb = col >> 5, c16 = (col & 31) >> 2;
+  return (uint32_t)(cb * rows * 128 + (row >> 3) * 1024 + (row & 7) * 128 + ((c16 ^ (row & 7)) << 4) +
+                    ((col & 3) << 2));
+}
+
 // Store 8 consecutive fp32 values (columns [8 c8, 8 c8 + 8) of `row`) into an operand tile of
-// element type TA's tile format: one 16-byte chunk of bf16, or two of fp32.
+// element type TA's tile format: one 16-byte chunk of bf16, or two of tf32-rounded fp32.
 template <typename TA>
 __device__ __forceinline__ void tile_store8(uint8_t* tile, int row, int c8, int rows, const float (&v)[8]) {
   if constexpr (sizeof(TA) == 4) {
-    sw128_store_chunk(tile, row, 2 * c8, rows,
-                      make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
-                                 __float_as_uint(v[3])));
+    sw128_store_chunk(tile, row, 2 * c8, rows, make_uint4(tf32_rna(v[0]), tf32_rna(v[1]), tf32_rna(v[2]), tf32_rna(v[3])));
     sw128_store_chunk(tile, row, 2 * c8 + 1, rows,
-                      make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]),
-                                 __float_as_uint(v[7])));
+                      make_uint4(tf32_rna(v[4]), tf32_rna(v[5]), tf32_rna(v[6]), tf32_rna(v[7])));
   } else {
     uint4 o;
     o.x = pack_bf16x2(v[0], v[1]);
@@ -350,7 +364,9 @@ __device__ void chunk_stage_xz(const FwdParams& a, uint8_t* sm, int b, int k, in
 
 // Normalised (+bias), rotated B^ and/or C^ rows of the chunk into K-major tiles:
 // row (s*RP + r), column n.  (mamba3/mamba3.py:151-166)
-template <typename TA, int R, bool WANT_B, bool WANT_C>
+// B_T: B^ goes in transposed (row n, column s*RP + r), the K-major A operand of the chunk-state
+// GEMM on fp32 tiles (kind::tf32 operands are read K-major here).
+template <typename TA, int R, bool WANT_B, bool WANT_C, bool B_T = false>
 __device__ void chunk_produce_bc(const FwdParams& a, uint8_t* sm, int b, int k, int g) {
   constexpr int RP = rp_of(R);
   using PL = Plan<RP, TA>;
@@ -421,16 +437,31 @@ __device__ void chunk_produce_bc(const FwdParams& a, uint8_t* sm, int b, int k, 
         }
       }
     }
-#pragma unroll
-    for (int r = 0; r < RP; ++r) {
-      float ob[8], oc[8];
+    if constexpr (B_T) {
+      static_assert(sizeof(TA) == 4 && !WANT_C, "transposed B^ tiles: fp32 state kernel only");
+      // row n = 8 c + e, columns s*RP .. s*RP + RP - 1 (4, 8 or 16 aligned bytes)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        ob[e] = (valid && r < R) ? vb[e * R + (r < R ? r : 0)] : 0.f;
-        oc[e] = (valid && r < R) ? vc[e * R + (r < R ? r : 0)] : 0.f;
+        uint32_t w[RP];
+#pragma unroll
+        for (int r = 0; r < RP; ++r) w[r] = (valid && r < R) ? tf32_rna(vb[e * R + (r < R ? r : 0)]) : 0u;
+        uint8_t* dst = tB + sw128_offset_f32(c * 8 + e, s * RP, 128);
+        if constexpr (RP == 4) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        else if constexpr (RP == 2) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+        else *reinterpret_cast<uint32_t*>(dst) = w[0];
       }
-      if (WANT_B) tile_store8<TA>(tB, s * RP + r, c, 128, ob);
-      if (WANT_C) tile_store8<TA>(tC, s * RP + r, c, 128, oc);
+    } else {
+#pragma unroll
+      for (int r = 0; r < RP; ++r) {
+        float ob[8], oc[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          ob[e] = (valid && r < R) ? vb[e * R + (r < R ? r : 0)] : 0.f;
+          oc[e] = (valid && r < R) ? vc[e * R + (r < R ? r : 0)] : 0.f;
+        }
+        if (WANT_B) tile_store8<TA>(tB, s * RP + r, c, 128, ob);
+        if (WANT_C) tile_store8<TA>(tC, s * RP + r, c, 128, oc);
+      }
     }
   }
 }

@@ -101,8 +101,9 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(const __nv_bfloat
   }
 }
 
-// The same GEMM with fp32 operands on kind::tf32 (modes 3-5 mirror 0-2): A (128 x 128 fp32),
-// B (64 x 128 fp32) row-major; tiles of fp32 words in 128-byte column blocks of 32 elements.
+// The same GEMM with fp32 operands on kind::tf32 (mode 3: A and B K-major, the layout the fp32
+// chunk kernels use): A (128 x 128 fp32), B (64 x 128 fp32) row-major; tiles of fp32 words in
+// 128-byte column blocks of 32 elements.
 __global__ void __launch_bounds__(128, 1) umma_selftest_tf32_kernel(const float* __restrict__ A,
                                                                     const float* __restrict__ B,
                                                                     float* __restrict__ D, int mode, int* err) {
@@ -126,29 +127,17 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_tf32_kernel(const float*
     const int row = u / 32, c = u % 32;
     float w[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) w[e] = mode != 4 ? A[row * 128 + c * 4 + e] : A[(c * 4 + e) * 128 + row];
+    for (int e = 0; e < 4; ++e) w[e] = A[row * 128 + c * 4 + e];
     sw128_store_chunk(tA, row, c, 128,
                       make_uint4(__float_as_uint(w[0]), __float_as_uint(w[1]), __float_as_uint(w[2]),
                                  __float_as_uint(w[3])));
   }
-  if (mode != 5) {  // tile B: 64 rows (n) x 128 columns (k)
-    for (int u = threadIdx.x; u < 64 * 32; u += blockDim.x) {
-      const int row = u / 32, c = u % 32;
-      const float4 v = *reinterpret_cast<const float4*>(B + row * 128 + c * 4);
-      sw128_store_chunk(tB, row, c, 64,
-                        make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z),
-                                   __float_as_uint(v.w)));
-    }
-  } else {  // B^T: 128 rows (k) x 64 columns (n)
-    for (int u = threadIdx.x; u < 128 * 16; u += blockDim.x) {
-      const int row = u / 16, c = u % 16;
-      float w[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) w[e] = B[(c * 4 + e) * 128 + row];
-      sw128_store_chunk(tB, row, c, 128,
-                        make_uint4(__float_as_uint(w[0]), __float_as_uint(w[1]), __float_as_uint(w[2]),
-                                   __float_as_uint(w[3])));
-    }
+  for (int u = threadIdx.x; u < 64 * 32; u += blockDim.x) {  // tile B: 64 rows (n) x 128 columns (k)
+    const int row = u / 32, c = u % 32;
+    const float4 v = *reinterpret_cast<const float4*>(B + row * 128 + c * 4);
+    sw128_store_chunk(tB, row, c, 64,
+                      make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z),
+                                 __float_as_uint(v.w)));
   }
   fence_async_smem();
   tc_fence_before();
@@ -156,12 +145,9 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_tf32_kernel(const float*
   tc_fence_after();
   const uint32_t tbase = *tslot;
   if (threadIdx.x == 0) {
-    const uint32_t idesc = idesc_tf32(128, 64, mode == 4, mode == 5);
-    for (int kk = 0; kk < 16; ++kk) {
-      const uint64_t ad = mode == 4 ? mnmajor_desc(tA, 128, kk * 8) : kmajor_desc_b(tA, 128, kk * 32);
-      const uint64_t bd = mode == 5 ? mnmajor_desc(tB, 128, kk * 8) : kmajor_desc_b(tB, 64, kk * 32);
-      umma_tf32(tbase, ad, bd, idesc, kk > 0 ? 1u : 0u);
-    }
+    const uint32_t idesc = idesc_tf32(128, 64, false, false);
+    for (int kk = 0; kk < 16; ++kk)
+      umma_tf32(tbase, kmajor_desc_b(tA, 128, kk * 32), kmajor_desc_b(tB, 64, kk * 32), idesc, kk > 0 ? 1u : 0u);
     umma_commit(bar);
   }
   bool ok = mbar_wait(bar, 0);
@@ -218,10 +204,10 @@ extern "C" int m3b_selftest_wait(const int* flag, int target, int mode, int64_t 
 }
 
 extern "C" int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream) {
-  if (!A || !B || !D || mode < 0 || mode > 5) return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_umma: bad args");
+  if (!A || !B || !D || mode < 0 || mode > 3) return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_umma: bad args");
   if (!m3b::aligned16(A) || !m3b::aligned16(B)) return m3b::fail(M3B_ERR_ALIGNMENT, "selftest_umma: alignment");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (mode >= 3) {
+  if (mode == 3) {
     const int bytes = 98304 + 64 + 1024;
     cudaError_t e =
         cudaFuncSetAttribute(m3b::umma_selftest_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

@@ -29,10 +29,10 @@ def test_umma_selftest(mode):
     assert max_rel(to_np(D), to_np(ref)) < 1e-5
 
 
-@pytest.mark.parametrize("mode", [3, 4, 5])
+@pytest.mark.parametrize("mode", [3])
 def test_umma_selftest_tf32(mode):
-    """kind::tf32 with fp32 tiles (K-major A and B, MN-major A, MN-major B): the product of the
-    operands rounded to tf32 (10 mantissa bits), accumulated in fp32."""
+    """kind::tf32 with fp32 tiles, A and B K-major (the fp32 chunk kernels' layout): the product
+    of the operands as tf32 (10 mantissa bits), accumulated in fp32."""
     from mamba3_b200 import _lib
 
     g = torch.Generator().manual_seed(200 + mode)
