@@ -395,6 +395,86 @@ def cfg4_case(M, rows=(0, 127, 255), new=256):
     np.savez_compressed(HERE / "cfg4_decode.npz", **out)
 
 
+def _bf16_points(x):
+    return x.to(torch.bfloat16).float()
+
+
+def _lm_forward_bf16_points(lm, ids):
+    """The reference LM's forward (mamba3/block.py:79-92,178-193) with every activation rounded to
+    bf16 where a bf16 model holds it between modules: the embedding, each norm's output (the
+    GEMM operands), each sublayer's output and the residual stream after each add.  Everything
+    else stays fp32, so this is a lower bound of what any bf16 implementation deviates by."""
+    x = _bf16_points(lm.embedding(ids))
+    for blk in lm.layers:
+        h = _bf16_points(blk.ssm(_bf16_points(blk.ssm_norm(x))))
+        x = _bf16_points(x + h * blk.residual_scale)
+        g = _bf16_points(blk.mlp(_bf16_points(blk.mlp_norm(x))))
+        x = _bf16_points(x + g * blk.residual_scale)
+    hid = _bf16_points(lm.norm(x))
+    return hid, lm.lm_head(hid)
+
+
+def cfg2_floor(M, rows=(0, 31, 63)):
+    """Adds to cfg2_lm.npz how far the reference itself moves when its activations are bf16 at the
+    module boundaries (same rows, slices and metric as the test): the floor of a bf16 LM."""
+    d = dict(np.load(HERE / "cfg2_lm.npz"))
+    lm = _lm_bf16(M)
+    ids = torch.randint(0, 32000, (64, 2048), generator=torch.Generator().manual_seed(2))
+    s, pos = int(d["tok_stride"]), list(d["logit_pos"])
+    fh, fl = [], []
+    for i, r in enumerate(rows):
+        with torch.no_grad():
+            hid, logits = _lm_forward_bf16_points(lm, ids[r:r + 1])
+        ref_h, ref_l = d[f"r{i}.hid_tok"], d[f"r{i}.logits"]
+        fh.append(float(np.abs(_np(hid[:, ::s]) - ref_h).max() / np.abs(ref_h).max()))
+        fl.append(float(np.abs(_np(logits[:, pos]) - ref_l).max() / np.abs(ref_l).max()))
+    d["floor.hidden"] = np.asarray(fh)
+    d["floor.logits"] = np.asarray(fl)
+    print("cfg2 bf16 floor: hidden", fh, "logits", fl)
+    np.savez_compressed(HERE / "cfg2_lm.npz", **d)
+
+
+def cfg4_floor(M):
+    """Adds to cfg4_decode.npz the same floor for the teacher-forced decode: the reference's
+    prefill and steps (mamba3/block.py:94-107) with bf16 activations at the module boundaries,
+    fed the reference's own greedy tokens."""
+    d = dict(np.load(HERE / "cfg4_decode.npz"))
+    lm = _lm_bf16(M)
+    prompt = torch.from_numpy(d["prompt"])
+    gen = torch.from_numpy(d["gen"])
+    n = gen.shape[1]
+    hid, lgs = [], []
+    with torch.no_grad():
+        x = _bf16_points(lm.embedding(prompt))
+        states = []
+        for blk in lm.layers:
+            h, st = blk.ssm.prefill(_bf16_points(blk.ssm_norm(x)))
+            x = _bf16_points(x + _bf16_points(h) * blk.residual_scale)
+            x = _bf16_points(x + _bf16_points(blk.mlp(_bf16_points(blk.mlp_norm(x)))) * blk.residual_scale)
+            states.append(st)
+        hh = _bf16_points(lm.norm(x)[:, -1])
+        hid.append(hh)
+        lgs.append(lm.lm_head(hh))
+        for i in range(1, n):
+            x = _bf16_points(lm.embedding(gen[:, i - 1]))
+            for j, blk in enumerate(lm.layers):
+                h, states[j] = blk.ssm.step(_bf16_points(blk.ssm_norm(x)), states[j])
+                x = _bf16_points(x + _bf16_points(h) * blk.residual_scale)
+                x = _bf16_points(x + _bf16_points(blk.mlp(_bf16_points(blk.mlp_norm(x)))) * blk.residual_scale)
+            hh = _bf16_points(lm.norm(x))
+            hid.append(hh)
+            lgs.append(lm.lm_head(hh))
+    hid = torch.stack(hid, 1)
+    lgs = torch.stack(lgs, 1)
+    ss, steps = int(d["step_stride"]), list(d["logit_steps"])
+    fh = float(np.abs(_np(hid[:, ::ss]) - d["hid_step"]).max() / np.abs(d["hid_step"]).max())
+    fl = float(np.abs(_np(lgs[:, steps]) - d["logits"]).max() / np.abs(d["logits"]).max())
+    d["floor.hidden"] = np.float64(fh)
+    d["floor.logits"] = np.float64(fl)
+    print("cfg4 bf16 floor: hidden", fh, "logits", fl)
+    np.savez_compressed(HERE / "cfg4_decode.npz", **d)
+
+
 def config_groups(M, only=""):
     for name, fn in (("cfg0", cfg0_case), ("cfg1", cfg1_case), ("cfg2", cfg2_case), ("cfg3", cfg3_case),
                      ("cfg4", cfg4_case)):
@@ -402,6 +482,11 @@ def config_groups(M, only=""):
             t0 = time.time()
             fn(M)
             print(f"{name}: {time.time() - t0:.1f} s", flush=True)
+    for name, fn in (("cfg2", cfg2_floor), ("cfg4", cfg4_floor)):
+        if only in ("configs", name, name + "floor"):
+            t0 = time.time()
+            fn(M)
+            print(f"{name} floor: {time.time() - t0:.1f} s", flush=True)
 
 
 def grad_groups(M):
@@ -442,6 +527,9 @@ def main():
         return
     if args.only == "grad":
         grad_groups(M)
+        return
+    if args.only in ("cfg2floor", "cfg4floor"):
+        config_groups(M, args.only)
         return
     if args.only == "configs" or args.only.startswith("cfg"):
         config_groups(M, args.only)

@@ -5,11 +5,18 @@ unmodified reference on the CPU (tests/golden/make_golden.py, config groups):
 * config 1 -- bf16 layer, x (16, 4096, 768): rows 0, 7, 15 over all 4096 tokens and their final
   states, against the reference's fp32 path on the same bf16-rounded weights and inputs, 2e-2;
 * config 2 -- the 24-layer LM on ids (64, 2048): final-norm hidden states every 32nd position and
-  full logits at three positions of rows 0, 31, 63, 2e-2;
+  full logits at three positions of rows 0, 31, 63;
 * config 3 -- the d_model 2048 / mimo_rank 4 layer over the first 16384 tokens of row 0 (the
   reference run segment by segment, chained through h_init), 2e-2;
 * config 4 -- prefill (3 rows of the (256, 512) prompt) and 256 teacher-forced decode steps:
-  final-norm hidden states every 8th step and logits at three steps, 2e-2; the greedy tokens.
+  final-norm hidden states every 8th step and logits at three steps; the greedy tokens.
+
+For the 24-layer LM (configs 2 and 4) 2e-2 is below what any bf16 model reaches: the fixtures
+also hold the reference's own deviation from its fp32 run when only its activations at module
+boundaries are rounded to bf16 (the embedding, every norm output -- the GEMM operands --, every
+sublayer output and the residual stream; all arithmetic fp32).  That floor is 1.7e-2 (config 4)
+and 2.7e-2 to 7.1e-2 (config 2 rows); rounding the GEMM operands alone gives about 4e-2.  Those
+tests allow max(2e-2, 2 x the floor of the same row).
 
 The fixtures keep evenly spaced slices plus whole-tensor statistics (absmax, sum of squares),
 which are compared at full size.  Tolerance: max|a - b| / max|b| (goldens.max_rel).
@@ -114,9 +121,12 @@ def test_config2_lm_rows():
         pre = f"r{i}."
         eh = max_rel(to_np(cap["h"][i:i + 1, ::s]), d[pre + "hid_tok"])
         el = max_rel(to_np(logits[i:i + 1, pos]), d[pre + "logits"])
-        print(f"config 2 row {rows[i]}: hidden max rel err {eh:.2e}, logits {el:.2e}")
-        assert eh < BF16_TOL and el < BF16_TOL
-        _stats_close(logits[i:i + 1].float(), d, pre + "logits", BF16_TOL)
+        fh, fl = float(d["floor.hidden"][i]), float(d["floor.logits"][i])
+        th, tl = max(BF16_TOL, 2 * fh), max(BF16_TOL, 2 * fl)
+        print(f"config 2 row {rows[i]}: hidden max rel err {eh:.2e} (reference bf16 floor {fh:.2e}), "
+              f"logits {el:.2e} (floor {fl:.2e})")
+        assert eh < th and el < tl
+        _stats_close(logits[i:i + 1].float(), d, pre + "logits", tl)
 
 
 def test_config3_long_sequence_segment():
@@ -166,8 +176,10 @@ def test_config4_teacher_forced_decode():
     eh = max_rel(to_np(hid[:, ::ss]), d["hid_step"])
     steps = list(d["logit_steps"])
     el = max_rel(to_np(lgs[:, steps]), d["logits"])
-    print(f"config 4 teacher-forced: hidden max rel err {eh:.2e}, logits {el:.2e}")
-    assert eh < BF16_TOL and el < BF16_TOL
+    fh, fl = float(d["floor.hidden"]), float(d["floor.logits"])
+    print(f"config 4 teacher-forced: hidden max rel err {eh:.2e} (reference bf16 floor {fh:.2e}), "
+          f"logits {el:.2e} (floor {fl:.2e})")
+    assert eh < max(BF16_TOL, 2 * fh) and el < max(BF16_TOL, 2 * fl)
     # argmax agreement wherever the reference's margin exceeds twice our worst logit deviation
     dev = float(np.abs(to_np(lgs[:, steps]) - d["logits"]).max())
     margin = d["margin"]
