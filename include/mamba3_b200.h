@@ -454,7 +454,8 @@ M3B_API int m3b_scaled_add(const void* x, const void* h, float scale, void* out,
  * staged through the same shared-memory layouts and UMMA descriptors as the chunk
  * kernels: mode 0 reads A K-major, mode 1 stages A transposed and reads it MN-major,
  * mode 2 stages B transposed and reads it MN-major.  Mode 3 takes fp32 A and B on
- * kind::tf32, both K-major (the tiles of the fp32 chunk kernels).
+ * kind::tf32, both K-major (the tiles of the fp32 chunk kernels).  Mode 6 holds A in tensor
+ * memory (bf16, two per 32-bit column), as the fused kernel holds its masked score tile.
  * ------------------------------------------------------------------------ */
 M3B_API int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream);
 

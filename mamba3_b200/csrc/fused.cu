@@ -3,7 +3,9 @@
 //
 // Roles (512 threads, 128 registers each):
 //   warps 0-7   epilogue (TMEM lane quadrant = warp % 4, column half = warp / 4):
-//               decay mask S -> P, output y = P X + e^cum C^ H'^T + D x with gate and MIMO down,
+//               decay mask S -> P (kept in TMEM, so the mask waits for S only, not for the state
+//               GEMMs that still read this chunk's B^ tile), output y = P X + e^cum C^ H'^T + D x
+//               with gate and MIMO down,
 //               running-state bookkeeping (TMEM <-> bf16 tile), MIMO x tiles X and W, h_final.
 //               Its leader issues the GEMMs that depend on the running state and on P, and
 //               hands each shared-memory stage back to the producers (with the TMA copies of
@@ -13,7 +15,7 @@
 // Per chunk g (stage s = g % 2), with the running state H (fp32, TMEM lanes n x columns p):
 //   producer leader:  S_g = C^ B^T                            -> TMEM S[g%2] (128 columns)
 //   epilogue leader:  Yi_g = C^ H'_g^T, H += B^^T W           -> Yi[g%2], H    (after state(g))
-//                     Y_g = P X                               -> first 64 columns of S[g%2]
+//                     Y_g = P X, P read from TMEM             -> first 64 columns of S[g%2]
 //   epilogue:         mask(g), output(g), state(g+1): H'_{g+1} = H -> bf16 tile, H *= d_{g+1},
 //                     X and W tiles of chunk g+1
 // The algebra (weights W, w, the first-token beta term carried by H') is in chunk.cuh.
@@ -33,7 +35,9 @@ namespace m3b {
 constexpr int kFusedThreads = 16 * 32;
 constexpr int kEpiThreads = 256;
 constexpr int kProdThreads = 256;
-constexpr uint32_t kColS = 0, kColYi = 256, kColH = 384;  // S[g%2] at 128 (g%2); Yi at 256 + 64 (g%2)
+// TMEM columns: S[g%2] at 128 (g%2) (Y_g lands in its first 64); Yi at 256 + 64 (g%2); H at 384;
+// the masked score tile P (bf16, two per column) at 448.
+constexpr uint32_t kColS = 0, kColYi = 256, kColH = 384, kColP = 448;
 constexpr int kBarProd = 1, kBarEpi = 2;
 
 // Optional per-phase timestamps of CTA 0 for pipeline analysis: build with -DM3B_TIMELINE and
@@ -279,8 +283,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     *epi_abort = 0;
     fence_mbar_init();
   }
-  // the operand tiles start zeroed: columns n >= N of tileC stay zero for the whole kernel
-  // (tileB is rewritten by P every chunk, so the producers zero those columns per chunk)
+  // the operand tiles start zeroed: columns n >= N of tileC and tileB stay zero for the whole kernel
   for (int e = tid; e < (2 * PL::kStage + 16384) / 16; e += kFusedThreads)
     reinterpret_cast<uint4*>(sm)[e] = make_uint4(0, 0, 0, 0);
   tc_fence_before();
@@ -718,12 +721,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
         }
       }
-      if (N < kNS) {  // zero columns [N, 128) of the B tile (P of an earlier chunk lives there)
-        const int c0 = N / 8;
-        const int ncz = kNS / 8 - c0;
-        for (int u = ptid; u < 128 * ncz; u += kProdThreads)
-          sw128_store_chunk(st + PL::tB, u / ncz, c0 + u % ncz, 128, make_uint4(0, 0, 0, 0));
-      }
       if (ptid == 0) M3B_TL(g, 3);
       // the next chunk's token scalars, while the other warps finish their rotations (its raw
       // values were requested at the start of this chunk; same sequence, so same dt_bias)
@@ -943,9 +940,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             else zr[c8].zero();
           }
         }
-        // S_g (producer) and Yi_g / H update (this role) must be complete before P overwrites B^
+        // S_g (producer) must be complete before the mask reads it; the state GEMMs of chunk g
+        // (issued at the end of the previous chunk) keep running meanwhile
         if (lead && !*abort_flag) {
-          if (!mbar_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1, a.wait_ns) || !mbar_wait(&bars[BAR_HDONE], g & 1, a.wait_ns)) {
+          if (!mbar_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1, a.wait_ns)) {
             *abort_flag = 1;
             record_error(a.err, M3B_ERR_TIMEOUT);
           }
@@ -1010,31 +1008,35 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                 }
               }
             }
+            // row m of P, columns (s, q) of this block: bf16 pairs into TMEM (16 columns)
+            uint32_t pw[16];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-              float v8[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v8[e] = v[8 * cc + e];
-              st_pack_chunk(st + PL::tB, m, c0 / 8 + cc, v8);
-            }
+            for (int e = 0; e < 16; ++e) pw[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+            tmem_st16_nowait(trow + kColP + 16 * blk, pw);
             if (lead && c32 == 0) M3B_TL(g, 14);
           }
         }
-        fence_async_smem();
+        tmem_wait_st();
         tc_fence_before();
         named_bar(kBarEpi, kEpiThreads);
         if (lead) {
-          // Y_g = P' W (separable) or P X into the first 64 columns of S[g%2] (the mask has consumed S_g)
+          // Y_g = P' W (separable) or P X into the first 64 columns of S[g%2] (the mask has consumed
+          // S_g); A = P from TMEM, K = (s, q) in 8 columns per instruction
           tc_fence_after();
           const uint8_t* yb = st + (sep ? PL::tW : PL::tX);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tbase + cs0, kmajor_desc(st + PL::tB, 128, kk * 16), mnmajor_desc(yb, 128, kk * 16), idO,
-                      kk > 0 ? 1u : 0u);
+            umma_bf16_ts(tbase + cs0, tbase + kColP + 8 * kk, mnmajor_desc(yb, 128, kk * 16), idO, kk > 0 ? 1u : 0u);
           umma_commit(&bars[BAR_YDONE]);
           M3B_TL(g, 9);
         }
-        // ---- output of chunk g (x_r comes from the X tile of this stage)
+        // ---- output of chunk g (x_r comes from the X tile of this stage).  YDONE also covers the
+        // state GEMMs of chunk g (Yi_g, the H update), committed earlier by the same thread; their
+        // own barrier phase is consumed here so that its phases stay in step with the chunks.
+        if (lead && !*abort_flag && !mbar_wait(&bars[BAR_HDONE], g & 1, a.wait_ns)) {
+          *abort_flag = 1;
+          record_error(a.err, M3B_ERR_TIMEOUT);
+        }
         if (!(ok = role_wait(&bars[BAR_YDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err, a.wait_ns))) break;
         tc_fence_after();
         if (lead) M3B_TL(g, 10);

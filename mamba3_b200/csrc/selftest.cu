@@ -174,6 +174,76 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_tf32_kernel(const float*
   }
 }
 
+// The bf16 GEMM with A held in TMEM (mode 6): each thread stores its row m of A (128 bf16, packed
+// two per column) into TMEM columns [0, 64); the MMA reads A from TMEM and B K-major from shared
+// memory into D at columns [64, 128).  Pins the TMEM operand layout the fused kernel's P tile uses.
+__global__ void __launch_bounds__(128, 1) umma_selftest_ts_kernel(const __nv_bfloat16* __restrict__ A,
+                                                                  const __nv_bfloat16* __restrict__ B,
+                                                                  float* __restrict__ D, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tB = sm;  // 16 KB: 64 rows (n) x 128 (k)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 16384);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 16384 + 16);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    tmem_alloc(tslot, 128);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  for (int u = threadIdx.x; u < 64 * 16; u += blockDim.x) {
+    const int row = u / 16, c = u % 16;
+    sw128_store_chunk(tB, row, c, 64, *reinterpret_cast<const uint4*>(B + row * 128 + c * 8));
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const int m = 32 * warp + lane;
+  const uint32_t trow = tbase + ((uint32_t)(32 * warp) << 16);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w[e] = reinterpret_cast<const uint32_t*>(A + m * 128 + 32 * q)[e];
+    tmem_st16_nowait(trow + 16 * q, w);
+  }
+  tmem_wait_st();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = idesc_bf16(128, 64, false, false);
+    for (int kk = 0; kk < 8; ++kk) umma_bf16_ts(tbase + 64, tbase + kk * 8, kmajor_desc(tB, 64, kk * 16), idesc, kk > 0 ? 1u : 0u);
+    umma_commit(bar);
+  }
+  bool ok = mbar_wait(bar, 0);
+  __syncwarp();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  if (ok) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float v[32];
+      tmem_ld32(trow + 64 + 32 * half, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) D[m * 64 + 32 * half + j] = v[j];
+    }
+  } else if (threadIdx.x == 0) {
+    record_error(err, M3B_ERR_TIMEOUT);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 128);
+  }
+}
+
 // One thread waits (bounded by limit_ns) on the flag (mode 0) or on an mbarrier phase nothing
 // completes (mode 1); a wait that runs out records M3B_ERR_TIMEOUT.
 __global__ void __launch_bounds__(32, 1) wait_selftest_kernel(const int* flag, int target, int mode,
@@ -204,9 +274,16 @@ extern "C" int m3b_selftest_wait(const int* flag, int target, int mode, int64_t 
 }
 
 extern "C" int m3b_selftest_umma(const void* A, const void* B, float* D, int mode, int* err, void* stream) {
-  if (!A || !B || !D || mode < 0 || mode > 3) return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_umma: bad args");
+  if (!A || !B || !D || mode < 0 || mode > 6 || mode == 4 || mode == 5)
+    return m3b::fail(M3B_ERR_INVALID_ARG, "selftest_umma: bad args");
   if (!m3b::aligned16(A) || !m3b::aligned16(B)) return m3b::fail(M3B_ERR_ALIGNMENT, "selftest_umma: alignment");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (mode == 6) {
+    const int bytes = 16384 + 64 + 1024;
+    m3b::umma_selftest_ts_kernel<<<1, 128, bytes, st>>>(static_cast<const __nv_bfloat16*>(A),
+                                                        static_cast<const __nv_bfloat16*>(B), D, err);
+    return m3b::check_launch("selftest_umma");
+  }
   if (mode == 3) {
     const int bytes = 98304 + 64 + 1024;
     cudaError_t e =

@@ -15,8 +15,9 @@ from helpers import ours_layer_from_golden, to_np
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("mode", [0, 1, 2, 6])
 def test_umma_selftest(mode):
+    """bf16 operands: A K-major, A MN-major, B MN-major (shared memory), A in tensor memory."""
     from mamba3_b200 import _lib
 
     g = torch.Generator().manual_seed(100 + mode)
