@@ -230,8 +230,11 @@ def run_decode(dev, world, rank, barrier):
         y = torch.empty(B, ssm.nheads * ssm.headdim, device=dev, dtype=torch.bfloat16)
         dims = GraphDecoder._dims(ssm)
         prm = ssm._param_tensors()
-        run_c = lambda: ops.step_ssm_compact_(prm, dims, proj, st["h"], st["prev_B"], st["prev_x"], st["angle"], y)  # noqa: E731
-        run_f = lambda: ops.step_ssm_(prm, dims, proj, full["h"], full["prev_BX"], full["angle"], y)  # noqa: E731
+        ws = dec.step_ws
+        run_c = lambda: ops.step_ssm_compact_(prm, dims, proj, st["h"], st["prev_B"], st["prev_x"], st["angle"], y,  # noqa: E731
+                                              workspace=ws)
+        run_f = lambda: ops.step_ssm_(prm, dims, proj, full["h"], full["prev_BX"], full["angle"], y,  # noqa: E731
+                                      workspace=ws)
         for _ in range(3):
             run_c()
             run_f()

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3B_ABI_VERSION 5
+#define M3B_ABI_VERSION 6
 
 #if defined(__GNUC__)
 #define M3B_API __attribute__((visibility("default")))
@@ -156,7 +156,15 @@ typedef struct m3b_step_args {
   const float* prev_x;
   float* prev_b_out;
   float* prev_x_out;
+  /* Optional workspace (no reference counterpart) of m3b_step_workspace() bytes, 16-byte
+   * aligned: with it, d_state 128 / headdim <= 64 / mimo_rank 1, 2 or 4 run as two kernels --
+   * per-(batch, head) operand preparation, then persistent CTAs that stream the state through a
+   * shared-memory ring by bulk copies.  NULL: one kernel, no workspace.  Same results. */
+  void* workspace;
+  size_t workspace_bytes;
 } m3b_step_args;
+/* Workspace bytes of the streaming decode step for these arguments (0: not applicable). */
+M3B_API size_t m3b_step_workspace(const m3b_step_args* a);
 M3B_API int m3b_step(const m3b_step_args* a, void* stream);
 
 /* ------------------------------------------------------------------------

@@ -60,7 +60,8 @@ class StepArgs(C.Structure):
                 ("act_dtype", C.c_int32), ("dt_scale", C.c_void_p), ("h", C.c_void_p), ("prev_bx", C.c_void_p),
                 ("angle", C.c_void_p), ("angle_dtype", C.c_int32), ("h_out", C.c_void_p), ("bx_out", C.c_void_p),
                 ("angle_out", C.c_void_p), ("y", C.c_void_p), ("prev_b", C.c_void_p), ("prev_x", C.c_void_p),
-                ("prev_b_out", C.c_void_p), ("prev_x_out", C.c_void_p)]
+                ("prev_b_out", C.c_void_p), ("prev_x_out", C.c_void_p), ("workspace", C.c_void_p),
+                ("workspace_bytes", C.c_size_t)]
 
 
 class LayerFwdArgs(C.Structure):
@@ -134,6 +135,7 @@ SIGNATURES = {
     "m3b_scan_bwd_workspace": (C.c_size_t, [C.POINTER(ScanBwdArgs)]),
     "m3b_scan_bwd": (C.c_int, [C.POINTER(ScanBwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_step": (C.c_int, [C.POINTER(StepArgs), C.c_void_p]),
+    "m3b_step_workspace": (C.c_size_t, [C.POINTER(StepArgs)]),
     "m3b_layer_fwd_workspace": (C.c_size_t, [C.POINTER(LayerFwdArgs)]),
     "m3b_layer_fwd": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_layer_fwd_noalloc": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p]),
@@ -252,16 +254,27 @@ def scan_bwd(decay, h_states, grad_h, with_h_init=False):
 
 
 def step(prm: LayerParams, proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y, prev_b=None,
-         prev_x=None, prev_b_out=None, prev_x_out=None):
+         prev_x=None, prev_b_out=None, prev_x_out=None, workspace=None, streaming=True):
     """One decode step.  Either prev_bx / bx_out (the reference's (P, N) previous-token state) or
-    the compact prev_b / prev_x / prev_b_out / prev_x_out ((N, R) and (P, R)) are given."""
+    the compact prev_b / prev_x / prev_b_out / prev_x_out ((N, R) and (P, R)) are given.  Where
+    the streaming two-kernel path applies (m3b_step_workspace > 0) it runs with `workspace`
+    (uint8, allocated here when None); returns the workspace so callers can keep it.
+    streaming=False runs the single-kernel path without a workspace."""
     dev = _cuda(proj, dt_scale, h, prev_bx, angle, h_out, bx_out, angle_out, y, prev_b, prev_x, prev_b_out,
-                prev_x_out)
+                prev_x_out, workspace)
     a = StepArgs(prm, proj.shape[0], _ptr(proj), proj.stride(0), dtype_code(proj.dtype), _ptr(dt_scale), _ptr(h),
                  _ptr(prev_bx), _ptr(angle), dtype_code(angle.dtype), _ptr(h_out), _ptr(bx_out), _ptr(angle_out),
                  _ptr(y), _ptr(prev_b), _ptr(prev_x), _ptr(prev_b_out), _ptr(prev_x_out))
+    L = lib()
+    need = L.m3b_step_workspace(C.byref(a)) if streaming else 0
+    if need:
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        a.workspace = _ptr(workspace)
+        a.workspace_bytes = need
     with torch.cuda.device(dev):
-        _check(lib().m3b_step(C.byref(a), _stream(dev)), "m3b_step")
+        _check(L.m3b_step(C.byref(a), _stream(dev)), "m3b_step")
+    return workspace
 
 
 def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=None, prev_bx_init=None,

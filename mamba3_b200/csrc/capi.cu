@@ -95,6 +95,8 @@ int m3b_scan_bwd(const m3b_scan_bwd_args* a, void* workspace, size_t workspace_b
   return m3b::launch_scan_bwd(scan_bwd_launch(a), workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+size_t m3b_step_workspace(const m3b_step_args* a) { return m3b::step_workspace(a); }
+
 int m3b_step(const m3b_step_args* a, void* stream) {
   m3b::g_last_error[0] = 0;
   if (!a) return m3b::fail(M3B_ERR_INVALID_ARG, "step: null args");

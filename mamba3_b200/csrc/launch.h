@@ -46,6 +46,7 @@ size_t scan_bwd_workspace(const ScanBwdLaunch& s);
 int launch_scan_bwd(const ScanBwdLaunch& s, void* ws, size_t ws_bytes, cudaStream_t st);
 
 int launch_step(const m3b_step_args* a, cudaStream_t st);
+size_t step_workspace(const m3b_step_args* a);
 int layer_fwd(const m3b_layer_fwd_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t layer_fwd_workspace(const m3b_layer_fwd_args* a);
 // The least workspace layer_fwd accepts (it then runs whole sequences per CTA).

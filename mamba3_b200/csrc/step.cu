@@ -13,6 +13,9 @@
 // shuffles.  The epilogue adds D x_r, applies the gate and sums the ranks
 // (mamba3/mamba3.py:310-316).  State traffic is the minimum of the reference
 // layout: read h + prev_BX, write h + BX.
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -350,6 +353,379 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 4 : 2) step_kernel(m3b
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two-kernel decode step for d_state 128, headdim <= 64 (a multiple of 8), mimo_rank 1, 2 or 4
+// (the decode configurations), used when the caller passes a workspace:
+//   step_prep_kernel   one CTA per (batch, head): the token's operands -- B^ and C^ (norm, bias,
+//                      rotation by the advanced angle), x_r, the gate, dA / gamma / beta and D --
+//                      into an operand block of the workspace; the new angle.
+//   step_stream_kernel persistent CTAs walk the (batch, head) items; the fp32 state of the next
+//                      item, its operand block and its previous-token state arrive by bulk copies
+//                      into the other half of a two-slot shared-memory ring while the current
+//                      item is computed, so the loop has no global-load latency of its own and
+//                      the state streams at HBM rate.  Stores go straight from registers.
+// Same arithmetic as step_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kStreamN = 128, kStreamPMax = 64;
+
+// operand block of one (batch, head) item, fp32: B^ and C^ rank-major (R x N each), x_r and
+// the gate (PMAX x R each, p-major), then dA, gamma, beta, D
+template <int R>
+struct OpBlock {
+  static constexpr int Bt = 0, Ct = R * kStreamN, Xr = 2 * R * kStreamN, Gate = Xr + kStreamPMax * R;
+  static constexpr int Scal = Gate + kStreamPMax * R;
+  static constexpr int floats = Scal + 4;
+  static constexpr int bytes = floats * 4;  // a multiple of 16
+  static_assert(bytes % 16 == 0, "operand blocks are copied in 16-byte units");
+};
+
+template <typename TA, int R>
+__global__ void __launch_bounds__(128) step_prep_kernel(m3b_step_args a, float* ws) {
+  using OB = OpBlock<R>;
+  constexpr int N = kStreamN, NR = N * R;
+  const m3b_layer_params& prm = a.prm;
+  const int H = prm.H, P = prm.P, G = prm.G, pd = prm.param_dtype;
+  const int item = blockIdx.x;
+  const int b = item / H, h = item - (item / H) * H, g = h / (H / G);
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  __shared__ float sBr[NR], sCr[NR];  // normalised, (n, r) order
+  __shared__ float sRed[2][4];
+  __shared__ float sDt;
+  float* ob = ws + (int64_t)item * OB::floats;
+  const TA* row = reinterpret_cast<const TA*>(a.proj) + (int64_t)b * a.proj_stride;
+  const int HP = H * P;
+  const int offB = 2 * HP + g * NR, offC = 2 * HP + G * NR + g * NR;
+  const int offDt = 2 * HP + 2 * G * NR, offLam = offDt + H, offTh = offLam + (prm.trapezoidal ? H : 0);
+  float bv[R], cv[R];
+  float sb = 0.f, sc = 0.f;
+#pragma unroll
+  for (int q = 0; q < R; ++q) {  // NR = 128 R: R entries per thread
+    const int e = tid + 128 * q;
+    bv[q] = io<TA>::ld(row + offB + e);
+    cv[q] = io<TA>::ld(row + offC + e);
+    sb = fmaf(bv[q], bv[q], sb);
+    sc = fmaf(cv[q], cv[q], sc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    sc += __shfl_xor_sync(0xffffffffu, sc, o);
+  }
+  if (lane == 0) {
+    sRed[0][wid] = sb;
+    sRed[1][wid] = sc;
+  }
+  if (tid == 0) {
+    const int64_t bh = (int64_t)b * H + h;
+    const float dts = a.dt_scale ? io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + bh) : 1.f;
+    const float dt = softplus_f(io<TA>::ld(row + offDt + h) + ldf(prm.dt_bias, h, pd)) * dts;
+    const float A = -expf(ldf(prm.A_log, h, pd));
+    const float dA = expf(A * dt);
+    float gamma = dt, beta = 0.f;
+    if (prm.trapezoidal) {
+      const float lam = sigmoid_f(io<TA>::ld(row + offLam + h));
+      gamma = lam * dt;
+      beta = (1.f - lam) * dt * dA;
+    }
+    ob[OB::Scal + 0] = dA;
+    ob[OB::Scal + 1] = gamma;
+    ob[OB::Scal + 2] = beta;
+    ob[OB::Scal + 3] = ldf(prm.D, h, pd);
+    sDt = dt;
+  }
+  if (tid < P) {  // x_r and the gate of channel p = tid
+    const float xv = io<TA>::ld(row + HP + h * P + tid);
+    const float zv = io<TA>::ld(row + h * P + tid);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t q = ((int64_t)h * P + tid) * R + r;
+      ob[OB::Xr + tid * R + r] = xv * ldf(prm.mimo_x, q, pd);
+      ob[OB::Gate + tid * R + r] = silu_f(zv * ldf(prm.mimo_z, q, pd)) * ldf(prm.mimo_down, q, pd);
+    }
+  }
+  __syncthreads();
+  const float rb = rsqrtf((sRed[0][0] + sRed[0][1] + sRed[0][2] + sRed[0][3]) / (float)NR + prm.norm_eps);
+  const float rc = rsqrtf((sRed[1][0] + sRed[1][1] + sRed[1][2] + sRed[1][3]) / (float)NR + prm.norm_eps);
+#pragma unroll
+  for (int q = 0; q < R; ++q) {
+    const int e = tid + 128 * q;
+    sBr[e] = fmaf(bv[q] * rb, ldf(prm.B_norm_w, e, pd), ldf(prm.B_bias, (int64_t)g * NR + e, pd));
+    sCr[e] = fmaf(cv[q] * rc, ldf(prm.C_norm_w, e, pd), ldf(prm.C_bias, (int64_t)g * NR + e, pd));
+  }
+  __syncthreads();
+  if (tid < N / 2) {  // pair i = tid: advance the angle, rotate (2i, 2i+1) for every rank
+    const int i = tid;
+    const int64_t abase = ((int64_t)b * H + h) * (N / 2);
+    float ang = ldf(a.angle, abase + i, a.angle_dtype);
+    float sn = 0.f, cs = 1.f;
+    if (prm.complex_ssm) {
+      ang -= sDt * io<TA>::ld(row + offTh + i);
+      sincosf(ang, &sn, &cs);
+    }
+    a.angle_out[abase + i] = ang;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float b0 = sBr[(2 * i) * R + r], b1 = sBr[(2 * i + 1) * R + r];
+      const float c0 = sCr[(2 * i) * R + r], c1 = sCr[(2 * i + 1) * R + r];
+      *reinterpret_cast<float2*>(ob + OB::Bt + r * N + 2 * i) = make_float2(b0 * cs - b1 * sn, b0 * sn + b1 * cs);
+      *reinterpret_cast<float2*>(ob + OB::Ct + r * N + 2 * i) = make_float2(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
+    }
+  }
+}
+
+template <int R, bool COMPACT>
+struct StreamPlan {
+  static constexpr int N = kStreamN, PMAX = kStreamPMax;
+  static constexpr int st = PMAX * N * 4;                              // h (and prev_BX) bytes
+  static constexpr int ob = (COMPACT ? 1 : 2) * st;                    // operand block
+  static constexpr int pb = ob + OpBlock<R>::bytes;                    // COMPACT: previous B^ (N, R)
+  static constexpr int px = pb + N * R * 4;                            // COMPACT: previous x_r (P, R)
+  static constexpr int slot_used = COMPACT ? px + PMAX * R * 4 : pb;
+  static constexpr int slot = (slot_used + 127) / 128 * 128;     // 128-byte aligned slots
+  static_assert(slot >= slot_used, "a slot holds everything copied into it");
+  static constexpr int sY = 2 * slot;                                  // PMAX x R
+  static constexpr int bars = sY + PMAX * R * 4;                       // 2 mbarriers
+  static constexpr int bytes = bars + 16;
+};
+
+template <typename TA, int R, bool COMPACT>
+__global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
+    step_stream_kernel(m3b_step_args a, const float* ws, int nitems, uint64_t wait_ns) {
+  using SP = StreamPlan<R, COMPACT>;
+  using OB = OpBlock<R>;
+  extern __shared__ __align__(128) uint8_t ssm[];
+  constexpr int N = kStreamN;
+  const m3b_layer_params& prm = a.prm;
+  const int H = prm.H, P = prm.P;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  float* sY = reinterpret_cast<float*>(ssm + SP::sY);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ssm + SP::bars);
+  const int nvec = P * N / 4;
+  const uint32_t sbytes = (uint32_t)(P * N * 4);
+  const uint32_t pbytes = (uint32_t)(N * R * 4), xbytes = (uint32_t)(P * R * 4);
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto bulk = [](void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+  };
+  // bulk copies of item `it` into slot `sl` (thread 0): state, operand block, previous token
+  auto issue = [&](int it, int sl) {
+    uint8_t* d = ssm + sl * SP::slot;
+    uint64_t* bar = &bars[sl];
+    const int64_t sbase = (int64_t)it * P * N;
+    mbar_arrive_expect_tx(bar, (COMPACT ? sbytes + pbytes + xbytes : 2 * sbytes) + (uint32_t)OB::bytes);
+    bulk(d, a.h + sbase, sbytes, bar);
+    if constexpr (COMPACT) {
+      bulk(d + SP::pb, a.prev_b + (int64_t)it * N * R, pbytes, bar);
+      bulk(d + SP::px, a.prev_x + (int64_t)it * P * R, xbytes, bar);
+    } else {
+      bulk(d + SP::st, a.prev_bx + sbase, sbytes, bar);
+    }
+    bulk(d + SP::ob, ws + (int64_t)it * OB::floats, (uint32_t)OB::bytes, bar);
+  };
+  const int stride = (int)gridDim.x;
+  if (tid == 0 && (int)blockIdx.x < nitems) issue((int)blockIdx.x, 0);
+  int k = 0;
+  for (int item = (int)blockIdx.x; item < nitems; item += stride, ++k) {
+    const int sl = k & 1;
+    const bool pending = item + stride < nitems;
+    // the next item streams into the other slot (released by the barrier ending the last item)
+    if (tid == 0 && pending) issue(item + stride, sl ^ 1);
+    bool ok = mbar_wait(&bars[sl], (k >> 1) & 1, wait_ns);
+    ok = __syncthreads_and(ok);
+    if (!ok) {
+      // a copy that never completed: the copy into the other slot must land before leaving
+      if (tid == 0 && pending) mbar_wait(&bars[sl ^ 1], ((k + 1) >> 1) & 1, wait_ns);
+      break;
+    }
+    const uint8_t* d = ssm + sl * SP::slot;
+    const float* obs = reinterpret_cast<const float*>(d + SP::ob);
+    const float* sB = obs + OB::Bt;
+    const float* sC = obs + OB::Ct;
+    const float* sXr = obs + OB::Xr;
+    const float dA = obs[OB::Scal + 0], gamma = obs[OB::Scal + 1], beta = obs[OB::Scal + 2];
+    const float4* hs4 = reinterpret_cast<const float4*>(d);
+    const float4* ps4 = reinterpret_cast<const float4*>(d + SP::st);
+    const float* spb = reinterpret_cast<const float*>(d + SP::pb);  // (n, r) order
+    const float* spx = reinterpret_cast<const float*>(d + SP::px);
+    float4* ho4 = reinterpret_cast<float4*>(a.h_out + (int64_t)item * P * N);
+    float4* bo4 = COMPACT ? nullptr : reinterpret_cast<float4*>(a.bx_out + (int64_t)item * P * N);
+    constexpr int BATCH = 8;  // float4 f = u * 256 + tid: row p = 8 u + warp, columns 4 lane ..
+    float part[BATCH][R];
+    const int n0 = 4 * lane;
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int f = u * kStepThreads + tid;
+      const int p = f >> 5;
+      float yr[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) yr[r] = 0.f;
+      if (f < nvec) {
+        const float4 h4 = hs4[f];
+        const float hin[4] = {h4.x, h4.y, h4.z, h4.w};
+        float pin[4];
+        if constexpr (COMPACT) {  // prev_BX[p, n] = sum_r prev_B[n, r] prev_x[p, r]
+          float pbv[4 * R];
+#pragma unroll
+          for (int q = 0; q < R; ++q) {
+            const float4 v4 = reinterpret_cast<const float4*>(spb + n0 * R)[q];
+            pbv[4 * q] = v4.x, pbv[4 * q + 1] = v4.y, pbv[4 * q + 2] = v4.z, pbv[4 * q + 3] = v4.w;
+          }
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            float acc = 0.f;
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc = fmaf(pbv[jj * R + r], spx[p * R + r], acc);
+            pin[jj] = acc;
+          }
+        } else {
+          const float4 p4 = ps4[f];
+          pin[0] = p4.x, pin[1] = p4.y, pin[2] = p4.z, pin[3] = p4.w;
+        }
+        float hn[4], bx[4];
+        float bq[R][4], cq[R][4], xq[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const float4 b4 = *reinterpret_cast<const float4*>(sB + r * N + n0);
+          const float4 c4 = *reinterpret_cast<const float4*>(sC + r * N + n0);
+          bq[r][0] = b4.x, bq[r][1] = b4.y, bq[r][2] = b4.z, bq[r][3] = b4.w;
+          cq[r][0] = c4.x, cq[r][1] = c4.y, cq[r][2] = c4.z, cq[r][3] = c4.w;
+          xq[r] = sXr[p * R + r];
+        }
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          float cur = 0.f;
+#pragma unroll
+          for (int r = 0; r < R; ++r) cur = fmaf(bq[r][jj], xq[r], cur);
+          bx[jj] = cur;
+          hn[jj] = fmaf(dA, hin[jj], fmaf(gamma, cur, beta * pin[jj]));
+#pragma unroll
+          for (int r = 0; r < R; ++r) yr[r] = fmaf(cq[r][jj], hn[jj], yr[r]);
+        }
+        __stcs(ho4 + f, make_float4(hn[0], hn[1], hn[2], hn[3]));
+        if constexpr (!COMPACT) __stcs(bo4 + f, make_float4(bx[0], bx[1], bx[2], bx[3]));
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) part[u][r] = yr[r];
+    }
+    // y_r of row p = 8 u + warp: one warp-wide reduce-scatter of the BATCH * R partials (each
+    // halving step keeps the lower or upper half by one lane bit; a single value left is then
+    // added across the remaining bits)
+    constexpr int NV = BATCH * R;
+    float v[NV];
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u)
+#pragma unroll
+      for (int r = 0; r < R; ++r) v[u * R + r] = part[u][r];
+    int idx = 0;
+#pragma unroll
+    for (int st = 0; st < 5; ++st) {
+      const int mask = 16 >> st;
+      const int cnt = NV >> st;
+      const bool upper = (lane & mask) != 0;
+      if (cnt >= 2) {
+        const int half = cnt / 2;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float send = upper ? v[i] : v[i + half];
+          const float keep = upper ? v[i + half] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+        }
+        if (upper) idx += half;
+      } else {
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], mask);
+      }
+    }
+    constexpr int dup = NV >= 32 ? 1 : 32 / NV;
+    {
+      const int u = idx / R, r = idx - (idx / R) * R;
+      const int fw = u * kStepThreads + wid * 32;
+      if ((lane & (dup - 1)) == 0 && fw < nvec) sY[(fw >> 5) * R + r] = v[0];
+    }
+    __syncthreads();
+    const int b = item / H, h = item - (item / H) * H;
+    if constexpr (COMPACT) {  // this token's B^ and x_r are the next step's previous token
+      for (int e = tid; e < N * R; e += kStepThreads) {
+        const int n = e / R, r = e - (e / R) * R;
+        a.prev_b_out[(int64_t)item * N * R + e] = sB[r * N + n];
+      }
+      for (int e = tid; e < P * R; e += kStepThreads) a.prev_x_out[(int64_t)item * P * R + e] = sXr[e];
+    }
+    if (tid < P) {  // readout + D, gate, MIMO down
+      const float* sG = obs + OB::Gate;
+      const float Dh = obs[OB::Scal + 3];
+      float acc = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc = fmaf(sY[tid * R + r] + Dh * sXr[tid * R + r], sG[tid * R + r], acc);
+      io<TA>::st(reinterpret_cast<TA*>(a.y) + (int64_t)b * H * P + (int64_t)h * P + tid, acc);
+    }
+    __syncthreads();  // the slot and sY are free for the next items
+  }
+}
+
+// The two-kernel path covers d_state 128, headdim <= 64 (a multiple of 8), mimo_rank 1, 2, 4.
+static bool stream_ok(const m3b_step_args* a) {
+  const m3b_layer_params& p = a->prm;
+  return p.N == kStreamN && p.P <= kStreamPMax && p.P % 8 == 0 && (p.R == 1 || p.R == 2 || p.R == 4) &&
+         a->batch * p.H <= 0x7fffffffLL;
+}
+
+static size_t stream_ws_bytes(const m3b_step_args* a) {
+  const int R = a->prm.R;
+  const size_t ob = R == 1 ? OpBlock<1>::bytes : R == 2 ? OpBlock<2>::bytes : OpBlock<4>::bytes;
+  return (size_t)a->batch * a->prm.H * ob;
+}
+
+template <typename TA, int R, bool COMPACT>
+static int launch_stream_t(const m3b_step_args* a, float* ws, cudaStream_t st) {
+  using SP = StreamPlan<R, COMPACT>;
+  const void* fn = (const void*)step_stream_kernel<TA, R, COMPACT>;
+  static std::mutex mu;
+  static std::map<int, int> per_sm;  // resident CTAs per SM, per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int occ = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = per_sm.find(dev);
+    if (it == per_sm.end()) {
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SP::bytes);
+      if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kStepThreads, SP::bytes);
+      if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "step (stream): %s", cudaGetErrorString(e));
+      per_sm[dev] = occ;
+    } else {
+      occ = it->second;
+    }
+  }
+  if (occ < 1) return fail(M3B_ERR_UNSUPPORTED, "step (stream): kernel does not fit an SM");
+  const int nitems = (int)(a->batch * a->prm.H);
+  step_prep_kernel<TA, R><<<nitems, 128, 0, st>>>(*a, ws);
+  int rc = check_launch("step (prep)");
+  if (rc != M3B_OK) return rc;
+  const int cap = num_sms() * occ;
+  const int grid = nitems < cap ? nitems : cap;
+  step_stream_kernel<TA, R, COMPACT><<<grid, kStepThreads, SP::bytes, st>>>(*a, ws, nitems, kWaitLimitNs);
+  return check_launch("step (stream)");
+}
+
+template <typename TA>
+static int launch_stream(const m3b_step_args* a, float* ws, cudaStream_t st) {
+  const bool compact = a->prev_b != nullptr;
+  switch (a->prm.R) {
+    case 1: return compact ? launch_stream_t<TA, 1, true>(a, ws, st) : launch_stream_t<TA, 1, false>(a, ws, st);
+    case 2: return compact ? launch_stream_t<TA, 2, true>(a, ws, st) : launch_stream_t<TA, 2, false>(a, ws, st);
+    default: return compact ? launch_stream_t<TA, 4, true>(a, ws, st) : launch_stream_t<TA, 4, false>(a, ws, st);
+  }
+}
+
 template <typename TA>
 static int launch_step_t(const m3b_step_args* a, cudaStream_t st) {
   const unsigned grid = (unsigned)(a->batch * a->prm.H);
@@ -375,6 +751,11 @@ static int launch_step_t(const m3b_step_args* a, cudaStream_t st) {
   return check_launch("step");
 }
 
+size_t step_workspace(const m3b_step_args* a) {
+  if (!a || !stream_ok(a) || a->batch <= 0) return 0;
+  return stream_ws_bytes(a);
+}
+
 int launch_step(const m3b_step_args* a, cudaStream_t st) {
   const m3b_layer_params& p = a->prm;
   const bool compact = a->prev_b != nullptr;
@@ -391,6 +772,19 @@ int launch_step(const m3b_step_args* a, cudaStream_t st) {
     return fail(M3B_ERR_ALIGNMENT, "step: state buffers must be 16-byte aligned");
   if (a->batch <= 0) return M3B_OK;
   if (a->batch * p.H > 0x7fffffffLL) return fail(M3B_ERR_INVALID_ARG, "step: batch*H too large");
+  if (a->workspace && stream_ok(a)) {
+    if (a->workspace_bytes < stream_ws_bytes(a))
+      return fail(M3B_ERR_WORKSPACE, "step: need %zu workspace bytes", stream_ws_bytes(a));
+    if (!aligned16(a->workspace) || (a->prev_b && (!aligned16(a->prev_b) || !aligned16(a->prev_x))))
+      return fail(M3B_ERR_ALIGNMENT, "step: workspace and previous-token buffers must be 16-byte aligned");
+    float* ws = static_cast<float*>(a->workspace);
+    switch (a->act_dtype) {
+      case M3B_F32: return launch_stream<float>(a, ws, st);
+      case M3B_BF16: return launch_stream<__nv_bfloat16>(a, ws, st);
+      case M3B_F16: return launch_stream<__half>(a, ws, st);
+      default: return fail(M3B_ERR_INVALID_ARG, "step: bad act dtype %d", a->act_dtype);
+    }
+  }
   switch (a->act_dtype) {
     case M3B_F32: return launch_step_t<float>(a, st);
     case M3B_BF16: return launch_step_t<__nv_bfloat16>(a, st);

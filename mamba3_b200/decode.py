@@ -43,6 +43,7 @@ class GraphDecoder:
         self.out = torch.zeros(self.B, max(1, self.n), dtype=torch.long, device=self.dev)
         self.pos = torch.zeros(1, dtype=torch.long, device=self.dev)
         self.graphs = {}  # one captured step per sampling rule (temperature, top_k)
+        self.step_ws = None
         self.sampling = None
 
     @staticmethod
@@ -54,12 +55,14 @@ class GraphDecoder:
         ssm = blk.ssm
         proj = ssm.in_proj(blk.ssm_norm(x))
         st = self.states[i]
+        # one step workspace for every layer (the layers run one after another on one stream);
+        # allocated by the first, uncaptured step
         if self.compact:
-            ops.step_ssm_compact_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_B"], st["prev_x"],
-                                  st["angle"], self.ybuf[i])
+            self.step_ws = ops.step_ssm_compact_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_B"],
+                                                 st["prev_x"], st["angle"], self.ybuf[i], workspace=self.step_ws)
         else:
-            ops.step_ssm_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_BX"], st["angle"],
-                          self.ybuf[i])
+            self.step_ws = ops.step_ssm_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_BX"],
+                                         st["angle"], self.ybuf[i], workspace=self.step_ws)
         h = ssm.out_proj(self.ybuf[i])
         return blk._mlp_residual(_residual(x, h, blk.residual_scale))
 

@@ -337,11 +337,12 @@ def _(proj, A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_
                                                                         device=proj.device))
 
 
-def step_ssm_(prm_tensors, dims, proj, h, prev_bx, angle, y, dt_scale=None):
-    """In-place decode step for CUDA-graph loops: updates h, prev_bx, angle (fp32) and writes y."""
+def step_ssm_(prm_tensors, dims, proj, h, prev_bx, angle, y, dt_scale=None, workspace=None):
+    """In-place decode step for CUDA-graph loops: updates h, prev_bx, angle (fp32) and writes y.
+    Returns the step workspace (pass it back in to reuse it)."""
     H, P, N, R, G, trap, cplx, eps = dims
     prm = _prm(H, P, N, R, G, trap, cplx, eps, *prm_tensors)
-    _lib.step(prm, proj, dt_scale, h, prev_bx, angle, h, prev_bx, angle, y)
+    return _lib.step(prm, proj, dt_scale, h, prev_bx, angle, h, prev_bx, angle, y, workspace=workspace)
 
 
 # ---------------------------------------------------------------------------
@@ -383,12 +384,13 @@ def _(proj, A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_
             torch.empty_like(prev_x, **f), torch.empty(angle.shape, dtype=torch.float32, device=proj.device))
 
 
-def step_ssm_compact_(prm_tensors, dims, proj, h, prev_b, prev_x, angle, y, dt_scale=None):
-    """In-place compact decode step for CUDA-graph loops: updates h, prev_b, prev_x, angle."""
+def step_ssm_compact_(prm_tensors, dims, proj, h, prev_b, prev_x, angle, y, dt_scale=None, workspace=None):
+    """In-place compact decode step for CUDA-graph loops: updates h, prev_b, prev_x, angle.
+    Returns the step workspace (pass it back in to reuse it)."""
     H, P, N, R, G, trap, cplx, eps = dims
     prm = _prm(H, P, N, R, G, trap, cplx, eps, *prm_tensors)
-    _lib.step(prm, proj, dt_scale, h, None, angle, h, None, angle, y, prev_b=prev_b, prev_x=prev_x,
-              prev_b_out=prev_b, prev_x_out=prev_x)
+    return _lib.step(prm, proj, dt_scale, h, None, angle, h, None, angle, y, prev_b=prev_b, prev_x=prev_x,
+                     prev_b_out=prev_b, prev_x_out=prev_x, workspace=workspace)
 
 
 def layer_state_compact(proj, prm_tensors, dims, state=None):

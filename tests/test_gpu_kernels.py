@@ -184,6 +184,46 @@ def test_step_bf16_vs_oracle(case):
     assert max_rel(to_np(st["h"]), ost["h"]) < 2e-2
 
 
+@pytest.mark.parametrize("compact", [False, True], ids=["prev_bx", "compact"])
+@pytest.mark.parametrize("R", [1, 2, 4])
+def test_step_streaming_equals_single_kernel(R, compact):
+    """d_state 128: the two-kernel streaming step (operand preparation + persistent state stream
+    through a shared-memory ring) and the single kernel give the same state and output, in place
+    and out of place, over more (batch, head) items than the persistent grid holds."""
+    from mamba3_b200 import KulaMamba, _lib, ops
+
+    torch.manual_seed(80 + R)
+    m = KulaMamba(d_model=256, d_state=128, headdim=64, mimo_rank=R).cuda().to(torch.bfloat16).eval()
+    B, H, P, N = 300, m.nheads, 64, 128
+    g = torch.Generator().manual_seed(81)
+    x = torch.randn(B, 256, generator=g).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        proj = m.in_proj(x)
+    st = {"h": torch.randn(B, H, P, N, generator=g), "angle": torch.randn(B, H, N // 2, generator=g),
+          "pb": torch.randn(B, H, N, R, generator=g), "px": torch.randn(B, H, P, R, generator=g),
+          "pbx": torch.randn(B, H, P, N, generator=g)}
+    st = {k: v.cuda() for k, v in st.items()}
+    prm = ops._prm(H, P, N, R, 1, True, True, m.B_norm.eps, *m._param_tensors())
+    outs = []
+    for streaming in (False, True):
+        s2 = {k: v.clone() for k, v in st.items()}
+        y = torch.empty(B, H * P, dtype=torch.bfloat16, device="cuda")
+        if compact:
+            ws = _lib.step(prm, proj, None, s2["h"], None, s2["angle"], s2["h"], None, s2["angle"], y,
+                           prev_b=s2["pb"], prev_x=s2["px"], prev_b_out=s2["pb"], prev_x_out=s2["px"],
+                           streaming=streaming)
+        else:
+            ws = _lib.step(prm, proj, None, s2["h"], s2["pbx"], s2["angle"], s2["h"], s2["pbx"], s2["angle"], y,
+                           streaming=streaming)
+        assert (ws is not None) == streaming
+        outs.append((y, s2))
+    torch.cuda.synchronize()
+    (y0, a0), (y1, a1) = outs
+    assert max_rel(to_np(y1), to_np(y0)) < 1e-3  # y is bf16: a different fp32 summation order may flip a rounding
+    for k in (("h", "angle", "pb", "px") if compact else ("h", "angle", "pbx")):
+        assert max_rel(to_np(a1[k]), to_np(a0[k])) < 1e-5, k
+
+
 def test_step_full_batch_state_layout():
     """cfg4 layer dims at batch 256: every (batch, head) state block is updated independently."""
     from mamba3_b200 import KulaMamba
