@@ -179,6 +179,27 @@ def algorithmic_work(B, T, H=24, P=64, N=128, R=2, d_model=768, d_proj=3696):
     }
 
 
+def _peaks():
+    if (ROOT / "MEASURED_PEAKS.json").exists():
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        d["source"] = "measured (MEASURED_PEAKS.json)"
+        return d
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def _flop_roofline(flops_per_token, tokens_per_s, issued_per_token=None):
+    """Tensor-core roofline of a whole forward: algorithmic FLOPs (SURVEY convention) per second
+    against the measured bf16 peak; beside it the FLOPs the kernels actually issue."""
+    pk = _peaks()
+    ach = flops_per_token * tokens_per_s / 1e12
+    out = {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+           "frac": ach / pk["bf16_tflops"], "flops_per_token": flops_per_token, "peak_source": pk["source"]}
+    if issued_per_token is not None:
+        iss = issued_per_token * tokens_per_s / 1e12
+        out.update(issued_flops_per_token=issued_per_token, issued_tflops=iss, issued_frac=iss / pk["bf16_tflops"])
+    return out
+
+
 def run_decode(dev, world, rank, barrier):
     """Config 4: the 24-layer config-2 LM prefills (256 / world, 512) prompt tokens per rank and
     decodes greedily with the CUDA-graph decoder (compact previous-token state).  Also times the
@@ -248,9 +269,25 @@ def run_decode(dev, world, rank, barrier):
         else {"hbm_gbs": 6650.0}
     gbs = state_bytes / (ms_k / 1e3) / 1e9
     gbs_f = full_bytes / (ms_f / 1e3) / 1e9
+    # decode roofline (HBM): every token step moves each layer's state once and reads the weights
+    # once; compact state = h read + write and the previous B^ / x_r, the convention of SURVEY
+    # 8(d) = the reference's layout (h read + write, prev_BX read, BX write)
+    w_bytes = sum(p.numel() * p.element_size() for p in lm.parameters())
+    nl = len(lm.layers)
+    per_tok_compact = nl * state_bytes + w_bytes
+    per_tok_ref = nl * full_bytes + w_bytes
+    t_tok = ms_dec / steps / 1e3
+    pk = _peaks()
+    roof = {"bound": "hbm", "achieved": per_tok_compact / t_tok / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": per_tok_compact / t_tok / 1e9 / pk["hbm_gbs"], "bytes_per_token_step": per_tok_compact,
+            "weights_bytes": w_bytes, "state_bytes_per_layer": state_bytes,
+            "convention_bytes_per_token_step": per_tok_ref,
+            "convention_ms_at_peak": per_tok_ref / (pk["hbm_gbs"] * 1e9) * 1e3,
+            "compact_ms_at_peak": per_tok_compact / (pk["hbm_gbs"] * 1e9) * 1e3, "peak_source": pk["source"]}
     return {"workload": f"config 4: 24-layer LM, prompt ({Bg}, {Tp}) + {new} greedy tokens, batch {B} per GPU, "
                         "CUDA-graph decode (GraphDecoder)",
             "decode_tokens_per_s": world * B * steps / (ms_dec / 1e3), "ms_per_token": ms_dec / steps,
+            "roofline": roof,
             "prefill_tokens_per_s": world * B * Tp / (ms_prefill / 1e3),
             "step_kernel": {"ms": ms_k, "state": "compact (h + previous B^, x_r)", "state_bytes": state_bytes,
                             "achieved_gbs": gbs, "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
@@ -394,16 +431,25 @@ def run_lm(dev, world, rank, barrier):
             ms = float(t.item())
     del lm
     torch.cuda.empty_cache()
+    # per token: 24 x (projections 8.04 + SSD core 7.08 (convention) + SwiGLU MLP 9.73) + lm_head 49.2
+    # MFLOP; the kernels issue 3.94 MFLOP of SSD tiles per token and layer (128 x 128 tiles per
+    # 64-token chunk and head: S, P W, C H, H update)
+    tps_gpu = B * T / (ms / 1e3)
+    conv = 24 * (8.04e6 + 7.08e6 + 9.73e6) + 49.2e6
+    issued = 24 * (8.04e6 + 10.49e6 * 24 / 64 + 9.73e6) + 49.2e6
     return {"workload": f"config 2: KulaMambaLM forward, 24 layers, vocab 32000, ids ({Bg}, {T}), "
                         f"{B} rows per GPU", "tokens_per_s": world * B * T / (ms / 1e3), "ms_per_step": ms,
-            "scaling": "strong (global batch 64 split over the GPUs)"}
+            "scaling": "strong (global batch 64 split over the GPUs)",
+            "roofline": _flop_roofline(conv, tps_gpu, issued)}
 
 
 def run_seqpar(dev, world, rank, barrier):
     """Config 3: one d_model 2048 / 64-head / mimo_rank 4 layer over x (2, 131072, 2048),
     sequence-sharded: rank r holds tokens [r T/G, (r+1) T/G) of both rows and runs
     seqpar.prefill_sharded (local pass, one all_gather of shard summaries, exact second pass).
-    On one GPU it is the plain prefill."""
+    On one GPU it is the plain prefill.  With G > 1 every rank also runs the unsharded prefill
+    once (untimed) and compares its own output rows and, on the last rank, the final state: the
+    line reports max |a - b| / max |b| over all ranks."""
     import torch
     import torch.distributed as dist
 
@@ -414,7 +460,8 @@ def run_seqpar(dev, world, rank, barrier):
     layer = KulaMamba(d_model=D, d_state=128, headdim=64, mimo_rank=4).to(dev, torch.bfloat16).eval()
     Ts = T // world
     g = torch.Generator(device=dev).manual_seed(3)
-    x = torch.randn(B, T, D, generator=g, device=dev)[:, rank * Ts:(rank + 1) * Ts].to(torch.bfloat16).contiguous()
+    x_full = torch.randn(B, T, D, generator=g, device=dev).to(torch.bfloat16)
+    x = x_full[:, rank * Ts:(rank + 1) * Ts].contiguous()
 
     def run():
         if world == 1:
@@ -437,10 +484,33 @@ def run_seqpar(dev, world, rank, barrier):
             t = torch.tensor([ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
-    return {"workload": f"config 3: layer d_model {D}, 64 heads, mimo_rank 4, x ({B}, {T}, {D}) bf16, "
-                        f"sequence-sharded over {world} GPU(s), {Ts} tokens per GPU",
-            "tokens_per_s": B * T / (ms / 1e3), "ms_per_step": ms, "scaling": "strong",
-            "exchange": "one all_gather of (S, PB, Om, Lam, c0) per layer" if world > 1 else "none"}
+        parity = None
+        if world > 1:
+            y_sh, st_sh = run()
+            y_ref, st_ref = layer.prefill(x_full)
+            ref = y_ref[:, rank * Ts:(rank + 1) * Ts].float()
+            last = rank == world - 1
+            num = torch.stack([(y_sh.float() - ref).abs().max(),
+                               (st_sh["h"] - st_ref["h"]).abs().max() if last else torch.zeros((), device=dev)])
+            den = torch.stack([ref.abs().max(), st_ref["h"].abs().max() if last else torch.zeros((), device=dev)])
+            dist.all_reduce(num, op=dist.ReduceOp.MAX)
+            dist.all_reduce(den, op=dist.ReduceOp.MAX)
+            parity = {"y_max_rel": float(num[0] / den[0]), "h_final_max_rel": float(num[1] / den[1]),
+                      "against": "the unsharded prefill of the same input on each rank's GPU"}
+            del y_ref, st_ref, y_sh, st_sh
+    del x_full
+    torch.cuda.empty_cache()
+    # per token: projections 55.3 + SSD core 62.9 (convention) MFLOP; the kernels issue 21.0
+    # MFLOP of SSD tiles per token (128 x 128 tiles per 32-token chunk and head, 64 heads)
+    tps = B * T / (ms / 1e3)
+    out = {"workload": f"config 3: layer d_model {D}, 64 heads, mimo_rank 4, x ({B}, {T}, {D}) bf16, "
+                       f"sequence-sharded over {world} GPU(s), {Ts} tokens per GPU",
+           "tokens_per_s": tps, "ms_per_step": ms, "scaling": "strong",
+           "exchange": "one all_gather of (S, PB, Om, Lam, c0) per layer" if world > 1 else "none",
+           "roofline": _flop_roofline(55.3e6 + 62.9e6, tps / world, 55.3e6 + 10.49e6 * 64 / 32)}
+    if parity is not None:
+        out["parity"] = parity
+    return out
 
 
 def profiled_traffic(kernel, B, T):
@@ -607,6 +677,13 @@ def run_ours(args):
             roof = {"bound": "hbm", "achieved": w["bytes"] / t_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
         roof["frac"] = roof["achieved"] / roof["peak"]
         roof["kernel"] = dom
+        if dom == "ssd_fused":
+            # what the kernel issues to the tensor cores: 128 x 128 tiles per (batch, 64-token
+            # chunk, head) -- S = C^B^T (K = 128), P W, C^H'^T, the H update (K = 128, N = 64)
+            chunks = B * ((T + 63) // 64) * 24
+            issued = chunks * (2 * 128 * 128 * 128 + 3 * 2 * 128 * 64 * 128)
+            roof["issued_tflops"] = issued / t_s / 1e12
+            roof["issued_frac"] = roof["issued_tflops"] / peaks["bf16_tflops"]
         roof["traffic"] = profiled_traffic(dom, B, T)
         roof["peak_source"] = "measured (MEASURED_PEAKS.json)" if not peaks.get("fallback") else "fallback"
         kern = {}
