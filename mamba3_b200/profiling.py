@@ -117,12 +117,72 @@ def train_step_profile(batch: int = 16, seqlen: int = 4096, rows: int = 24) -> s
     return prof.key_averages().table(sort_by="self_cuda_time_total", row_limit=rows, max_name_column_width=72)
 
 
+def kernel_workload(case: str, reps: int = 3) -> None:
+    """Small fixed workloads for per-kernel captures (ncu -k <kernel> -s <warm-up launches>):
+    each runs its kernels once as warm-up and then `reps` times.
+
+    cfg3     layer forward, d_model 2048 / 64 heads / mimo_rank 4, bf16, x (2, 8192, 2048): the
+             fused kernel at R = 4 (prep_kernel, ssd_fused_kernel per forward)
+    chunked  chunked_ssd on pre-processed bf16 tensors (2, 4096) x 24 heads, P 64, N 128, R 2,
+             trapezoid: gen_state_kernel, the scan, gen_out_kernel
+    step     one layer's decode step at config-4 shapes (batch 256 x 24 heads, compact state):
+             step_prep_kernel, step_stream_kernel
+    fp32     config-0 layer forward (4, 1024, 768) fp32: prep, angle prefix, the tf32
+             chunk_state_kernel, the scan, the tf32 chunk_out_kernel"""
+    import torch
+
+    from . import ops
+    from .mamba3 import KulaMamba
+    from .ssd import chunked_ssd
+
+    g = torch.Generator(device="cuda").manual_seed(11)
+    torch.manual_seed(0)
+    with torch.no_grad():
+        if case == "cfg3":
+            m = KulaMamba(d_model=2048, d_state=128, headdim=64, mimo_rank=4).cuda().to(torch.bfloat16).eval()
+            x = torch.randn(2, 8192, 2048, device="cuda", generator=g).to(torch.bfloat16)
+            run = lambda: m(x)  # noqa: E731
+        elif case == "fp32":
+            m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().eval()
+            x = torch.randn(4, 1024, 768, device="cuda", generator=g)
+            run = lambda: m(x)  # noqa: E731
+        elif case == "chunked":
+            B, T, H, P, N, R = 2, 4096, 24, 64, 128, 2
+            r = lambda *sh: torch.randn(*sh, device="cuda", generator=g).to(torch.bfloat16)  # noqa: E731
+            args = (r(B, T, H, P, R), r(B, T, H, P, R), r(B, T, H, N, R), r(B, T, H, N, R), r(B, T, H, N, R),
+                    torch.rand(B, T, H, device="cuda", generator=g) * 0.1, -torch.rand(H, device="cuda", generator=g),
+                    torch.randn(H, device="cuda", generator=g), r(B, T, H, P, R))
+            run = lambda: chunked_ssd(*args, return_final_state=True)  # noqa: E731
+        elif case == "step":
+            m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
+            B = 256
+            st = m.allocate_inference_state(B, compact=True)
+            proj = m.in_proj(torch.randn(B, 768, device="cuda", generator=g).to(torch.bfloat16))
+            y = torch.empty(B, m.nheads * m.headdim, device="cuda", dtype=torch.bfloat16)
+            d = m._dims()
+            dims = (d["H"], d["P"], d["N"], d["R"], d["G"], d["trapezoidal"], d["complex_ssm"], d["norm_eps"])
+            ws = [None]
+
+            def run():
+                ws[0] = ops.step_ssm_compact_(m._param_tensors(), dims, proj, st["h"], st["prev_B"], st["prev_x"],
+                                              st["angle"], y, workspace=ws[0])
+        else:
+            raise ValueError(case)
+        for _ in range(1 + reps):
+            run()
+        torch.cuda.synchronize()
+
+
 if __name__ == "__main__":
     import argparse
 
     ap = argparse.ArgumentParser(description="profiling helpers")
-    ap.add_argument("what", choices=["train"])
+    ap.add_argument("what", choices=["train", "cfg3", "chunked", "step", "fp32"])
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seqlen", type=int, default=4096)
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
-    print(train_step_profile(args.batch, args.seqlen))
+    if args.what == "train":
+        print(train_step_profile(args.batch, args.seqlen))
+    else:
+        kernel_workload(args.what, args.reps)
