@@ -561,6 +561,23 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
     constexpr int BATCH = 8;  // float4 f = u * 256 + tid: row p = 8 u + warp, columns 4 lane ..
     float part[BATCH][R];
     const int n0 = 4 * lane;
+    // this thread's four state columns n0 .. n0 + 3 are the same for all its rows: their B^, C^
+    // (and previous B^) entries are read from shared memory once per item
+    float bq[R][4], cq[R][4], pbv[COMPACT ? 4 * R : 1];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float4 b4 = *reinterpret_cast<const float4*>(sB + r * N + n0);
+      const float4 c4 = *reinterpret_cast<const float4*>(sC + r * N + n0);
+      bq[r][0] = b4.x, bq[r][1] = b4.y, bq[r][2] = b4.z, bq[r][3] = b4.w;
+      cq[r][0] = c4.x, cq[r][1] = c4.y, cq[r][2] = c4.z, cq[r][3] = c4.w;
+    }
+    if constexpr (COMPACT) {
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        const float4 v4 = reinterpret_cast<const float4*>(spb + n0 * R)[q];
+        pbv[4 * q] = v4.x, pbv[4 * q + 1] = v4.y, pbv[4 * q + 2] = v4.z, pbv[4 * q + 3] = v4.w;
+      }
+    }
 #pragma unroll
     for (int u = 0; u < BATCH; ++u) {
       const int f = u * kStepThreads + tid;
@@ -573,12 +590,6 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
         const float hin[4] = {h4.x, h4.y, h4.z, h4.w};
         float pin[4];
         if constexpr (COMPACT) {  // prev_BX[p, n] = sum_r prev_B[n, r] prev_x[p, r]
-          float pbv[4 * R];
-#pragma unroll
-          for (int q = 0; q < R; ++q) {
-            const float4 v4 = reinterpret_cast<const float4*>(spb + n0 * R)[q];
-            pbv[4 * q] = v4.x, pbv[4 * q + 1] = v4.y, pbv[4 * q + 2] = v4.z, pbv[4 * q + 3] = v4.w;
-          }
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             float acc = 0.f;
@@ -590,16 +601,9 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
           const float4 p4 = ps4[f];
           pin[0] = p4.x, pin[1] = p4.y, pin[2] = p4.z, pin[3] = p4.w;
         }
-        float hn[4], bx[4];
-        float bq[R][4], cq[R][4], xq[R];
+        float hn[4], bx[4], xq[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const float4 b4 = *reinterpret_cast<const float4*>(sB + r * N + n0);
-          const float4 c4 = *reinterpret_cast<const float4*>(sC + r * N + n0);
-          bq[r][0] = b4.x, bq[r][1] = b4.y, bq[r][2] = b4.z, bq[r][3] = b4.w;
-          cq[r][0] = c4.x, cq[r][1] = c4.y, cq[r][2] = c4.z, cq[r][3] = c4.w;
-          xq[r] = sXr[p * R + r];
-        }
+        for (int r = 0; r < R; ++r) xq[r] = sXr[p * R + r];
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           float cur = 0.f;
