@@ -533,6 +533,53 @@ def profiled_traffic(kernel, B, T):
     return b * (B * T) / tok
 
 
+def bind_to_gpu_numa_node(index):
+    """Restrict this process to the CPUs of the NUMA node its GPU hangs off (Linux sysfs), so the
+    pinned host buffers it allocates land in that node's memory.  Returns the node, or None
+    when the topology is not exposed (the process then keeps its CPUs)."""
+    import torch
+
+    try:
+        pr = torch.cuda.get_device_properties(index)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        node = int(open(f"/sys/bus/pci/devices/{bus}/numa_node").read().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in open(f"/sys/devices/system/node/node{node}/cpulist").read().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return node
+    except (OSError, ValueError, AttributeError):
+        pass
+    return None
+
+
+def host_copy_gbs(dev, nbytes=1 << 28, reps=5):
+    """Pinned host <-> device copy bandwidth of this rank (GB/s each way), CUDA events."""
+    import torch
+
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = {}
+    for name, fn in (("h2d_gbs", lambda: d.copy_(h, non_blocking=True)),
+                     ("d2h_gbs", lambda: h.copy_(d, non_blocking=True))):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        out[name] = nbytes * reps / (a.elapsed_time(b) / 1e3) / 1e9
+    del h, d
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -542,6 +589,7 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    numa = bind_to_gpu_numa_node(local)  # before any pinned host buffer is allocated
     if world > 1:
         from datetime import timedelta
 
@@ -651,6 +699,13 @@ def run_ours(args):
             tt = torch.tensor([ms_e2e], device=dev)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ms_e2e = float(tt.item())
+        # every rank's host link, measured alone and then all ranks at once (contention)
+        hc_alone = host_copy_gbs(dev) if rank == 0 else None
+        barrier()
+        hc = host_copy_gbs(dev)
+        hcv = torch.tensor([hc["h2d_gbs"], hc["d2h_gbs"]], device=dev)
+        if world > 1:
+            dist.all_reduce(hcv, op=dist.ReduceOp.MIN)
 
     decode = None if args.no_decode else run_decode(dev, world, rank, barrier)
     seqp = None if args.no_seqpar else run_seqpar(dev, world, rank, barrier)
@@ -710,7 +765,12 @@ def run_ours(args):
             "e2e": {"value": tokens / (ms_e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2,
                     "ms_per_step": ms_e2e,
-                    "api": f"KulaMamba.forward_host(pieces={args.e2e_pieces}, graph=True)"},
+                    "api": f"KulaMamba.forward_host(pieces={args.e2e_pieces}, graph=True)",
+                    "host_link": {"rank0_alone": hc_alone, "all_ranks_min_h2d_gbs": float(hcv[0]),
+                                  "all_ranks_min_d2h_gbs": float(hcv[1]), "numa_node_rank0": numa,
+                                  # copies in and out overlap (full-duplex link): the slower direction bounds a step
+                                  "bound_ms_per_step": max(x_host.numel() * 2 / (float(hcv[0]) * 1e9),
+                                                           y_host.numel() * 2 / (float(hcv[1]) * 1e9)) * 1e3}},
             "clocks": clk.summary(),
         }
         if decode is not None:
