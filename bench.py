@@ -632,9 +632,9 @@ def run_ours(args):
             return layer(x)
         e = ev[i]
         e[0].record()
-        proj = layer.in_proj(x)
+        proj, rms = layer._project(x)  # in_proj with the 1/rms of B and C from its epilogue
         with stage_events(e[1:1 + nst]):
-            y = layer.ssd_from_proj(proj)
+            y = layer.ssd_from_proj(proj, rms=rms)
         out = layer.out_proj(y)
         e[-1].record()
         return out
@@ -677,7 +677,11 @@ def run_ours(args):
             per["ssd_fused"] = per.pop("chunk_out")
             for k in ("angle_prefix", "chunk_state", "scan"):
                 per.pop(k)
-        launches_per_step = 2 if fused else 5  # prep + ssd_fused | prep, angle, state, scan, out
+        # in_proj_kernel + ssd_fused (the projection's epilogue replaces prep) | in_proj_kernel,
+        # prep, angle, state, scan, out
+        launches_per_step = 2 if fused else 6
+        if fused:
+            per.pop("prep")
 
         # end to end through the public API: pinned host x -> layer -> pinned host y, streamed by
         # forward_host in token ranges so the copies in, the layer and the copies out overlap

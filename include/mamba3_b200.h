@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3B_ABI_VERSION 6
+#define M3B_ABI_VERSION 7
 
 #if defined(__GNUC__)
 #define M3B_API __attribute__((visibility("default")))
@@ -209,8 +209,40 @@ typedef struct m3b_layer_fwd_args {
   /* Limit in nanoseconds of every device-side wait of this call (0: the library's 2 s).  A wait
    * that runs out records M3B_ERR_TIMEOUT in `err` and the kernel returns early. */
   int64_t wait_limit_ns;
+  /* Optional (batch*seqlen, G, 2) fp32: the 1/rms of every group's B and C row per token, as
+   * m3b_in_proj writes it.  When given (bf16 activations), the fused path reads it instead of
+   * making its own pass over the projection's B / C columns. */
+  const float* rms_in;
 } m3b_layer_fwd_args;
 #define M3B_LAYER_FWD_STAGES 6
+
+/* ------------------------------------------------------------------------
+ * Input projection with the layer's per-token prologue in its epilogue.
+ * Replaces `proj = self.in_proj(x)` (mamba3/mamba3.py:197, an nn.Linear) and the
+ * layer forward's own pass over the projection's B / C columns that B_norm /
+ * C_norm need (mamba3/mamba3.py:200-204): proj = x W^T (+ bias), bf16 operands
+ * and output, fp32 accumulation on the tensor cores; with `rms` given, the same
+ * epilogue also writes 1/rms of every group's B and C row of each token (the
+ * rms_in of m3b_layer_fwd_args).
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_in_proj_args {
+  int64_t rows;           /* tokens: batch * seqlen */
+  int32_t d_model;        /* multiple of 8 */
+  int32_t d_proj;         /* output columns, multiple of 8 */
+  const void* x;          /* (rows, x_stride) bf16, 16-byte aligned */
+  int64_t x_stride;       /* elements, multiple of 8 */
+  const void* weight;     /* (d_proj, d_model) bf16, row-contiguous (the nn.Linear weight) */
+  const void* bias;       /* (d_proj) bf16, or NULL */
+  void* proj;             /* (rows, proj_stride) bf16, 16-byte aligned */
+  int64_t proj_stride;    /* elements, multiple of 8 */
+  /* H, P, N, R, G and norm_eps place and normalise B and C in the projection row (only read
+   * when rms is given; the parameter pointers are not read) */
+  m3b_layer_params prm;
+  float* rms;             /* (rows, G, 2) fp32, or NULL */
+  int* err;               /* device int or NULL */
+  int64_t wait_limit_ns;  /* limit of every device-side wait (0: the library's 2 s) */
+} m3b_in_proj_args;
+M3B_API int m3b_in_proj(const m3b_in_proj_args* a, void* stream);
 
 /* ------------------------------------------------------------------------
  * Allocation-free layer forward (no counterpart in the reference).

@@ -71,6 +71,13 @@ class LayerFwdArgs(C.Structure):
                 ("h_final", C.c_void_p), ("angle_final", C.c_void_p), ("prev_bx_final", C.c_void_p),
                 ("err", C.c_void_p), ("stage_events", C.POINTER(C.c_void_p)), ("algo", C.c_int32),
                 ("state_only", C.c_int32), ("prev_b_final", C.c_void_p), ("prev_x_final", C.c_void_p),
+                ("wait_limit_ns", C.c_int64), ("rms_in", C.c_void_p)]
+
+
+class InProjArgs(C.Structure):
+    _fields_ = [("rows", C.c_int64), ("d_model", C.c_int32), ("d_proj", C.c_int32), ("x", C.c_void_p),
+                ("x_stride", C.c_int64), ("weight", C.c_void_p), ("bias", C.c_void_p), ("proj", C.c_void_p),
+                ("proj_stride", C.c_int64), ("prm", LayerParams), ("rms", C.c_void_p), ("err", C.c_void_p),
                 ("wait_limit_ns", C.c_int64)]
 
 
@@ -139,6 +146,7 @@ SIGNATURES = {
     "m3b_layer_fwd_workspace": (C.c_size_t, [C.POINTER(LayerFwdArgs)]),
     "m3b_layer_fwd": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_layer_fwd_noalloc": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p]),
+    "m3b_in_proj": (C.c_int, [C.POINTER(InProjArgs), C.c_void_p]),
     "m3b_copy_rows_async": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_void_p]),
     "m3b_chunked_ssd_workspace": (C.c_size_t, [C.POINTER(SsdArgs)]),
@@ -279,11 +287,13 @@ def step(prm: LayerParams, proj, dt_scale, h, prev_bx, angle, h_out, bx_out, ang
 
 def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=None, prev_bx_init=None,
               h_final=None, angle_final=None, prev_bx_final=None, err=None, workspace=None, stage_events=None,
-              algo=0, state_only=False, prev_b_final=None, prev_x_final=None, wait_limit_ns=0):
+              algo=0, state_only=False, prev_b_final=None, prev_x_final=None, wait_limit_ns=0, rms_in=None):
     """Launch the chunked layer forward; proj (B,T,d_proj) with unit stride in the last dim.
     Without `err` the device's error word records expired device waits (check_device_errors);
-    wait_limit_ns bounds each device wait (0: the library's 2 s)."""
-    dev = _cuda(proj, y, dt_scale, h_init, angle_init, prev_bx_init, h_final, angle_final, prev_bx_final, err)
+    wait_limit_ns bounds each device wait (0: the library's 2 s); rms_in: the (B*T, G, 2) fp32
+    1/rms rows of in_proj(..., prm=...), which spare the layer its own pass over B and C."""
+    dev = _cuda(proj, y, dt_scale, h_init, angle_init, prev_bx_init, h_final, angle_final, prev_bx_final, err,
+                rms_in)
     if err is None:
         err = device_err_word(dev)
     Bt, T, _ = proj.shape
@@ -297,6 +307,10 @@ def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=
     a.prev_b_final = _ptr(prev_b_final)
     a.prev_x_final = _ptr(prev_x_final)
     a.wait_limit_ns = int(wait_limit_ns)
+    if rms_in is not None:
+        if rms_in.dtype != torch.float32 or not rms_in.is_contiguous() or rms_in.numel() != Bt * T * prm.G * 2:
+            raise M3bError("rms_in must be a contiguous fp32 (B*T, G, 2) tensor")
+        a.rms_in = _ptr(rms_in)
     if stage_events is not None:
         if len(stage_events) != len(LAYER_FWD_STAGES) + 1:
             raise M3bError("stage_events needs one event per stage plus one")
@@ -312,6 +326,36 @@ def layer_fwd(prm: LayerParams, proj, y, dt_scale=None, h_init=None, angle_init=
         _check(L.m3b_layer_fwd(C.byref(a), _ptr(workspace), need, _stream(dev)), "m3b_layer_fwd")
     _after_launch(dev)
     return workspace
+
+
+def in_proj(x, weight, bias=None, proj=None, prm: LayerParams | None = None, rms=None, err=None):
+    """proj = x weight^T (+ bias) on the tensor cores, bf16 (x: (..., d_model), any leading shape,
+    unit stride in the last dim and one row stride).  With `prm` (the layer's dimensions and
+    norm eps) the epilogue also writes `rms`, the (rows, G, 2) fp32 1/rms of each token's B and C
+    rows, as layer_fwd(rms_in=...) takes it.  Returns (proj, rms)."""
+    dev = _cuda(x, weight, bias, proj, rms, err)
+    if err is None:
+        err = device_err_word(dev)
+    d_model = x.shape[-1]
+    x2 = x.reshape(-1, d_model)
+    if x2.stride(1) != 1 or weight.stride(1) != 1 or weight.stride(0) != d_model or weight.shape[1] != d_model:
+        raise M3bError("in_proj: x and weight need unit stride in d_model, weight row-contiguous")
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or (bias is not None and bias.dtype != torch.bfloat16):
+        raise M3bError("in_proj: bf16 x, weight and bias")
+    rows, d_proj = x2.shape[0], weight.shape[0]
+    if proj is None:
+        proj = torch.empty(*x.shape[:-1], d_proj, dtype=torch.bfloat16, device=dev)
+    p2 = proj.reshape(rows, d_proj)
+    if p2.stride(1) != 1 or p2.data_ptr() != proj.data_ptr():
+        raise M3bError("in_proj: proj must have unit stride in its last dim")
+    if prm is not None and rms is None:
+        rms = torch.empty(rows, prm.G, 2, dtype=torch.float32, device=dev)
+    a = InProjArgs(rows, d_model, d_proj, _ptr(x2), x2.stride(0), _ptr(weight), _ptr(bias), _ptr(p2), p2.stride(0),
+                   prm if prm is not None else LayerParams(), _ptr(rms) if prm is not None else None, _ptr(err), 0)
+    with torch.cuda.device(dev):
+        _check(lib().m3b_in_proj(C.byref(a), _stream(dev)), "m3b_in_proj")
+    _after_launch(dev)
+    return proj, (rms if prm is not None else None)
 
 
 def chunked_ssd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, y, h_init=None, h_final=None, err=None):

@@ -681,10 +681,16 @@ int layer_fwd_t(const m3b_layer_fwd_args* a, uint8_t* ws, const WsLayout& w, int
     if (a->stage_events) cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), st);
   };
   float* angle_last = reinterpret_cast<float*>(ws + w.angle_last);
+  // the fused path needs only the 1/rms rows from the pre-pass: a caller that has them (the input
+  // projection's epilogue, m3b_in_proj) skips it
+  const bool rms_given = w.fused && a->rms_in != nullptr;
+  if (rms_given) fp.rms = const_cast<float*>(a->rms_in);
   mark(0);
   if (w.fused) fp.asum = nullptr;
-  prep_kernel<TA><<<dim3((unsigned)fp.K, (unsigned)fp.B), kCT, 0, st>>>(fp);
-  if ((rc = check_launch("prep")) != M3B_OK) return rc;
+  if (!rms_given) {
+    prep_kernel<TA><<<dim3((unsigned)fp.K, (unsigned)fp.B), kCT, 0, st>>>(fp);
+    if ((rc = check_launch("prep")) != M3B_OK) return rc;
+  }
   if (w.fused) {
     mark(1);
     mark(2);
@@ -774,6 +780,8 @@ int validate(const m3b_layer_fwd_args* a) {
       (a->h_final && !aligned16(a->h_final)))
     return fail(M3B_ERR_ALIGNMENT, "layer_fwd: state buffers must be 16-byte aligned");
   if (a->batch > 65535) return fail(M3B_ERR_UNSUPPORTED, "layer_fwd: batch > 65535");
+  if (a->rms_in && (reinterpret_cast<uintptr_t>(a->rms_in) & 7u) != 0)
+    return fail(M3B_ERR_ALIGNMENT, "layer_fwd: rms_in must be 8-byte aligned");
   return M3B_OK;
 }
 

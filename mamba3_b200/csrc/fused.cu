@@ -29,6 +29,7 @@
 #include <utility>
 
 #include "chunk.cuh"
+#include "tmap.h"
 
 namespace m3b {
 
@@ -1191,6 +1192,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+// cuTensorMapEncodeTiled from the driver the runtime is bound to (no link-time libcuda dependency).
+EncodeTiledFn encode_tiled() {
+  static const EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
 namespace {
 int ensure_smem_f(const void* kernel, int bytes) {
   static std::mutex mu;
@@ -1205,22 +1219,6 @@ int ensure_smem_f(const void* kernel, int bytes) {
   return M3B_OK;
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled from the driver the runtime is bound to (no link-time libcuda dependency).
-EncodeTiledFn encode_tiled() {
-  static const EncodeTiledFn fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      f = nullptr;
-    return reinterpret_cast<EncodeTiledFn>(f);
-  }();
-  return fn;
-}
 
 // 3-D bf16 map over the projection (columns, tokens, batch rows) with box (box0, box1, 1); tokens
 // past T read as zeros.  False when the driver refuses the encoding.

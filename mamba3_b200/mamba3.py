@@ -207,14 +207,37 @@ class KulaMamba(nn.Module):
                     trapezoidal=self.use_trapezoidal, complex_ssm=self.use_complex_ssm,
                     norm_eps=float(self.B_norm.eps))
 
-    def ssd_from_proj(self, proj, dt_scale=None, return_state=False, state=None):
-        """Everything between in_proj and out_proj: proj (B,T,d_in_proj) -> y (B,T,d_inner) [+ state]."""
+    def ssd_from_proj(self, proj, dt_scale=None, return_state=False, state=None, rms=None):
+        """Everything between in_proj and out_proj: proj (B,T,d_in_proj) -> y (B,T,d_inner) [+ state].
+        rms: the 1/rms rows that _project returns with this proj (optional)."""
         st = state or {}
         y, h, angle, prev_bx = ops.layer_ssd(proj, *self._param_tensors(), dt_scale, st.get("h"), st.get("angle"),
-                                             st.get("prev_BX"), **self._dims(), return_state=return_state)
+                                             st.get("prev_BX"), **self._dims(), return_state=return_state,
+                                             rms=rms)
         if not return_state:
             return y
         return y, {"h": h, "angle": angle, "prev_BX": prev_bx}
+
+    def _project(self, x):
+        """(proj, rms): in_proj(x) and, where one kernel can give both, the layer's per-token 1/rms
+        of B and C from the projection's epilogue (m3b_in_proj; then the layer forward skips its
+        own pass over B and C).  That kernel takes bf16 CUDA inputs without gradients, 16-byte
+        aligned rows and B / C columns on multiples of 16; otherwise in_proj is the nn.Linear
+        (cuBLAS) and rms is None."""
+        W, b = self.in_proj.weight, self.in_proj.bias
+        if (x.is_cuda and x.dtype == torch.bfloat16 and W.dtype == torch.bfloat16
+                and (b is None or b.dtype == torch.bfloat16) and not self._needs_grad(x)
+                and x.shape[-1] % 8 == 0 and W.shape[0] % 8 == 0 and (2 * self.d_inner) % 16 == 0
+                and (self.d_state * self.mimo_rank) % 16 == 0 and self._proj_segments() <= 128):
+            d = self._dims()
+            return ops.in_proj_rms(x, W, b, d["H"], d["P"], d["N"], d["R"], d["G"], d["norm_eps"])
+        return self.in_proj(x), None
+
+    def _proj_segments(self):
+        """Column segments (of at most 256) m3b_in_proj cuts the projection row into."""
+        NR, W = self.d_state * self.mimo_rank, self.in_proj.weight.shape[0]
+        bc_end = 2 * self.d_inner + 2 * self.ngroups * NR
+        return -(-2 * self.d_inner // 256) + 2 * self.ngroups * -(-NR // 256) + -(-(W - bc_end) // 256)
 
     def _needs_grad(self, x):
         return torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters()))
@@ -283,7 +306,7 @@ class KulaMamba(nn.Module):
     def _ssd(self, x, dt_scale, return_state, state=None):
         if x.dim() != 3 or x.shape[1] <= 0:
             raise ValueError(f"expected (batch, seqlen>0, d_model), got {tuple(x.shape)}")
-        proj = self.in_proj(x)
+        proj, rms = self._project(x)
         st = state or {}
         if self._needs_grad(x):
             if st:
@@ -296,7 +319,8 @@ class KulaMamba(nn.Module):
             y, out_st = ops.layer_state_compact(proj, self._param_tensors(), self._dims_tuple(), st)
             return self.out_proj(y), out_st
         y, h, angle, prev_bx = ops.layer_ssd(proj, *self._param_tensors(), dt_scale, st.get("h"), st.get("angle"),
-                                             st.get("prev_BX"), **self._dims(), return_state=return_state)
+                                             st.get("prev_BX"), **self._dims(), return_state=return_state,
+                                             rms=rms)
         out = self.out_proj(y)
         if not return_state:
             return out, None

@@ -73,7 +73,9 @@ def layer_ssd(proj: torch.Tensor, A_log: torch.Tensor, D: torch.Tensor, dt_bias:
               dt_scale: Optional[torch.Tensor], h_init: Optional[torch.Tensor], angle_init: Optional[torch.Tensor],
               prev_bx_init: Optional[torch.Tensor],
               H: int, P: int, N: int, R: int, G: int, trapezoidal: bool, complex_ssm: bool, norm_eps: float,
-              return_state: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+              return_state: bool, rms: Optional[torch.Tensor] = None
+              ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """rms: the (B*T, G, 2) 1/rms rows of in_proj_rms for this proj (optional)."""
     Bt, T, _ = proj.shape
     proj = proj.contiguous()
     dev = proj.device
@@ -91,7 +93,7 @@ def layer_ssd(proj: torch.Tensor, A_log: torch.Tensor, D: torch.Tensor, dt_bias:
     f = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
     _lib.layer_fwd(prm, proj, y, dt_scale=ds, h_init=f(h_init), angle_init=f(angle_init),
                    prev_bx_init=f(prev_bx_init), h_final=h_final, angle_final=angle, prev_bx_final=prev_bx,
-                   stage_events=current_stage_events(), algo=_LAYER_ALGO)
+                   stage_events=current_stage_events(), algo=_LAYER_ALGO, rms_in=rms)
     if not return_state:
         e = torch.empty(0, **f32)
         return y, e, e.clone(), e.clone()
@@ -100,7 +102,7 @@ def layer_ssd(proj: torch.Tensor, A_log: torch.Tensor, D: torch.Tensor, dt_bias:
 
 @layer_ssd.register_fake
 def _(proj, A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_z, mimo_down, dt_scale, h_init,
-      angle_init, prev_bx_init, H, P, N, R, G, trapezoidal, complex_ssm, norm_eps, return_state):
+      angle_init, prev_bx_init, H, P, N, R, G, trapezoidal, complex_ssm, norm_eps, return_state, rms=None):
     Bt, T, _ = proj.shape
     y = proj.new_empty(Bt, T, H * P)
     f32 = dict(dtype=torch.float32, device=proj.device)
@@ -109,6 +111,26 @@ def _(proj, A_log, D, dt_bias, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_
                 torch.empty(Bt, H, P, N, **f32))
     e = torch.empty(0, **f32)
     return y, e, e.clone(), e.clone()
+
+
+# ---------------------------------------------------------------------------
+# input projection with the layer's per-token 1/rms of B and C in its epilogue
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("mamba3_b200::in_proj_rms", mutates_args=())
+def in_proj_rms(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], H: int, P: int, N: int,
+                R: int, G: int, norm_eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(proj, rms): proj = x weight^T (+ bias) in bf16 and the (rows, G, 2) fp32 1/rms of every
+    token's B and C rows (m3b_in_proj); x (..., d_model) bf16."""
+    prm = _lib.LayerParams()
+    prm.H, prm.P, prm.N, prm.R, prm.G, prm.norm_eps = H, P, N, R, G, norm_eps
+    return _lib.in_proj(x.contiguous(), weight.contiguous(), None if bias is None else bias.contiguous(), prm=prm)
+
+
+@in_proj_rms.register_fake
+def _(x, weight, bias, H, P, N, R, G, norm_eps):
+    rows = x.numel() // x.shape[-1]
+    return (x.new_empty(*x.shape[:-1], weight.shape[0]),
+            torch.empty(rows, G, 2, dtype=torch.float32, device=x.device))
 
 
 # ---------------------------------------------------------------------------

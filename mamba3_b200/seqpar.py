@@ -125,9 +125,10 @@ def exchange(aff: dict, group=None) -> list:
     return [unpack(b, aff) for b in bufs]
 
 
-def layer_state_only(layer, proj: torch.Tensor) -> dict:
+def layer_state_only(layer, proj: torch.Tensor, rms=None) -> dict:
     """The layer's state after `proj`'s tokens from the zero state, without the outputs: the
-    kernels skip C, the intra-chunk products and y where they can (m3b_layer_fwd state_only)."""
+    kernels skip C, the intra-chunk products and y where they can (m3b_layer_fwd state_only).
+    rms: the 1/rms rows the projection's epilogue gave with proj (optional)."""
     from . import _lib, ops
 
     d = layer._dims()
@@ -142,13 +143,13 @@ def layer_state_only(layer, proj: torch.Tensor) -> dict:
     st = {"h": torch.empty(Bt, H, P, N, **f32), "angle": torch.empty(Bt, H, N // 2, **f32),
           "prev_BX": torch.empty(Bt, H, P, N, **f32)}
     _lib.layer_fwd(prm, proj, y, h_final=st["h"], angle_final=st["angle"], prev_bx_final=st["prev_BX"],
-                   algo=ops._LAYER_ALGO, state_only=True)
+                   algo=ops._LAYER_ALGO, state_only=True, rms_in=rms)
     return st
 
 
-def layer_summary(layer, proj: torch.Tensor) -> dict:
+def layer_summary(layer, proj: torch.Tensor, rms=None) -> dict:
     """Step 1 on this rank's shard: the layer from the zero state, kept as an affine summary."""
-    st = layer_state_only(layer, proj)
+    st = layer_state_only(layer, proj, rms)
     d = layer._dims()
     lam_sum, c0 = shard_scalars(proj, layer.A_log, layer.dt_bias, d["H"], d["P"], d["N"], d["R"], d["G"],
                                 d["trapezoidal"])
@@ -163,9 +164,9 @@ def prefill_sharded(layer, x_shard: torch.Tensor, group=None, return_state: bool
     import torch.distributed as dist
 
     rank = dist.get_rank(group)
-    proj = layer.in_proj(x_shard)
-    affs = exchange(layer_summary(layer, proj), group)
+    proj, rms = layer._project(x_shard)
+    affs = exchange(layer_summary(layer, proj, rms), group)
     st = fold(affs, rank) if rank > 0 else None
-    y, st_out = layer.ssd_from_proj(proj, return_state=True, state=st)
+    y, st_out = layer.ssd_from_proj(proj, return_state=True, state=st, rms=rms)
     out = layer.out_proj(y)
     return (out, st_out) if return_state else out
