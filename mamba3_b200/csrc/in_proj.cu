@@ -3,11 +3,17 @@
 //   proj = x W^T (+ bias)        mamba3/mamba3.py:197 (nn.Linear), bf16 in / out, fp32 accumulate
 //   rms[t, g] = 1/rms(B_g), 1/rms(C_g) of the rounded proj row   B_norm / C_norm, mamba3.py:200-204
 //
-// One persistent CTA per SM, three roles:
-//   warp 0      TMA producer: x tile (128 rows x 64 K) and W tile (up to 256 output columns x 64 K)
-//               per stage, 128-byte swizzled, into a 4-stage shared-memory ring;
-//   warp 1      MMA issuer: tcgen05.mma 128 x width x 16 into one of two TMEM accumulators
-//               (256 columns each), so the epilogue of one tile overlaps the next tile's MMAs;
+// Persistent CTA pairs: a cluster of two CTAs on two SMs computes 256-row tiles with
+// tcgen05.mma.cta_group::2 (each CTA holds 128 rows of x and half of the tile's W rows, and gets
+// its 128 rows of the result in its own TMEM), so every SM stages half the W bytes per MMA that a
+// lone 128-row CTA would.  Three roles per CTA:
+//   warp 0      TMA producer: this CTA's x rows (128 x 64 K) and W rows (width / 2 x 64 K) per
+//               stage, 128-byte swizzled, into a 6-stage ring; the copies of both CTAs complete
+//               on the first CTA's stage barrier;
+//   warp 1      MMA issuer (first CTA only): 256 x width x 16 MMAs into one of two TMEM
+//               accumulators (256 columns each, in both SMs), so the epilogue of one tile
+//               overlaps the next tile's MMAs; its commits free the stage and hand the
+//               accumulator over in both CTAs;
 //   warps 2-5   epilogue: TMEM -> registers (one output row per thread), + bias, bf16 rounding;
 //               each warp stages 32 rows x 64 columns in a swizzled shared-memory box (two per
 //               warp, alternating) that one TMA store writes out, so a store request carries whole
@@ -15,10 +21,11 @@
 //               of its rounded values and, after the last piece, writes rsqrt(sum / (N R) + eps).
 // The output columns are cut into segments of at most 256: the z | x columns, every group's B and
 // C columns (one unit of ceil(N R / 256) pieces each, so one thread sees a whole B or C row), and
-// the dt | lam | theta tail.  A job is (128-row tile, unit); job j runs on CTA j mod grid.
+// the dt | lam | theta tail.  A job is (256-row tile, unit); job j runs on pair j mod pairs.
+// Where no CTA pair can be resident, the same kernel runs single CTAs over 128-row tiles
+// (cta_group::1, the whole W tile per CTA, 4 stages).
+#include <map>
 #include <mutex>
-#include <set>
-#include <utility>
 
 #include "common.cuh"
 #include "launch.h"
@@ -28,17 +35,16 @@ namespace m3b {
 
 namespace {
 
-constexpr int kIpBM = 128;      // rows per tile = TMEM lanes
+constexpr int kIpBM = 128;      // rows per CTA = TMEM lanes
 constexpr int kIpBN = 256;      // columns per segment at most = one TMEM accumulator
 constexpr int kIpBK = 64;       // K per stage: one 128-byte swizzle atom row of bf16
-constexpr int kIpStages = 4;
 constexpr int kIpThreads = 192;
 constexpr int kIpMaxSeg = 128;   // the segment tables travel in the kernel's parameters (4 KB)
 constexpr int kIpMaxUnit = 128;
 constexpr uint32_t kIpStageA = kIpBM * kIpBK * 2;  // 16 KB
-constexpr uint32_t kIpStageB = kIpBN * kIpBK * 2;  // 32 KB
+constexpr uint32_t kIpRing = 192 * 1024;            // stages: 6 x (16 + 16) KB paired, 4 x (16 + 32) KB single
 constexpr uint32_t kIpBox = 32 * 128;                          // staging box: 32 rows x 64 bf16
-constexpr uint32_t kIpStgOff = kIpStages * (kIpStageA + kIpStageB);
+constexpr uint32_t kIpStgOff = kIpRing;
 constexpr uint32_t kIpBarOff = kIpStgOff + 4 * 2 * kIpBox;      // two boxes per epilogue warp
 constexpr uint32_t kIpSmem = kIpBarOff + 256 + 1024;  // + barriers, TMEM slot, abort flag; + alignment
 static_assert(kIpSmem <= 227 * 1024, "shared memory plan");
@@ -65,9 +71,96 @@ __device__ __forceinline__ void ip_fail(const IpParams& a, volatile int* abort_f
   record_error(a.err, M3B_ERR_TIMEOUT);
 }
 
+// ---- CTA-pair forms (PAIR) next to the single-CTA ones ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of the same offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+template <bool PAIR>
+__device__ __forceinline__ void ip_tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  if constexpr (PAIR) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  } else {
+    tmem_alloc(dst, ncols);
+    tmem_relinquish();
+  }
+}
+template <bool PAIR>
+__device__ __forceinline__ void ip_tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  if constexpr (PAIR)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  else
+    tmem_dealloc(taddr, ncols);
+}
+// D (+)= A B^T over the pair: A rows [0, 128) from the first CTA's shared memory, [128, 256) from
+// the second's (same offset), B rows likewise split in halves; D rows in each CTA's TMEM.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at shared::cluster address `bar` (this CTA's or its peer's) when the
+// pair MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// TMA load into this CTA's shared memory whose completion counts on the mbarrier at shared::cluster
+// address `bar`, which may be the peer CTA's (no multicast: every CTA fetches its own box).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// mbar_wait with cluster-scope acquire (the phase completes by arrivals from the peer CTA too).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  auto try_wait = [&]() {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+        : "memory");
+    return done != 0;
+  };
+  if (try_wait()) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (try_wait()) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+template <bool PAIR>
 __global__ void __launch_bounds__(kIpThreads, 1)
     in_proj_kernel(const __grid_constant__ IpParams a, const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_o) {
+  constexpr int kIpStages = PAIR ? 6 : 4;
+  constexpr uint32_t kIpStageB = (PAIR ? kIpBN / 2 : kIpBN) * kIpBK * 2;  // 16 KB paired, 32 KB single
+  constexpr int kTileM = PAIR ? 2 * kIpBM : kIpBM;
+  static_assert(kIpStages * (kIpStageA + kIpStageB) == kIpRing, "stage ring");
   extern __shared__ uint8_t smraw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kIpBarOff);
@@ -86,15 +179,12 @@ __global__ void __launch_bounds__(kIpThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], 4);  // one arrival per epilogue warp
+      mbar_init(&acce[i], PAIR ? 8 : 4);  // one arrival per epilogue warp (of both CTAs)
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
-    tmem_alloc(tslot, 512);
-    tmem_relinquish();
-  }
+  if (warp == 0) ip_tmem_alloc<PAIR>(tslot, 512);
   if (warp == 1 && lane == 0) {
     prefetch_tensormap(&tm_x);
     prefetch_tensormap(&tm_w);
@@ -102,45 +192,71 @@ __global__ void __launch_bounds__(kIpThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers are initialised before any remote use
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int64_t worker = PAIR ? blockIdx.x / 2 : blockIdx.x, nworkers = PAIR ? gridDim.x / 2 : gridDim.x;
   const int64_t njobs = (int64_t)a.mtiles * a.nunit;
   const int nk = (a.K + kIpBK - 1) / kIpBK;
 
   if (warp == 0) {
     if (lane == 0) {
       uint32_t it = 0;
-      for (int64_t j = blockIdx.x; j < njobs && !*abort_flag; j += gridDim.x) {
+      for (int64_t j = worker; j < njobs && !*abort_flag; j += nworkers) {
         const int mt = (int)(j / a.nunit), u = (int)(j % a.nunit);
         for (int sg = a.unit[u].x; sg < a.unit[u].y; ++sg) {
-          const int col0 = a.seg[sg].x;
+          // this CTA's x rows and W rows (paired: the second CTA holds the upper half of the tile)
+          const int arow = mt * kTileM + (int)rank * kIpBM;
+          const int brow = a.seg[sg].x + (int)rank * (a.seg[sg].y / 2);
           for (int kb = 0; kb < nk; ++kb, ++it) {
             const int s = (int)(it % kIpStages);
             if (!mbar_wait(&empty[s], ((it / kIpStages) & 1) ^ 1, a.wait_ns)) {
               ip_fail(a, abort_flag);
               break;
             }
-            mbar_arrive_expect_tx(&full[s], kIpStageA + kIpStageB);
-            tma_load_2d(sm + s * kIpStageA, &tm_x, kb * kIpBK, mt * kIpBM, &full[s]);
-            tma_load_2d(sm + kIpStages * kIpStageA + s * kIpStageB, &tm_w, kb * kIpBK, col0, &full[s]);
+            uint8_t* dA = sm + s * kIpStageA;
+            uint8_t* dB = sm + kIpStages * kIpStageA + s * kIpStageB;
+            if constexpr (PAIR) {
+              // both CTAs' copies complete on the first CTA's barrier, which expects all of them
+              if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (kIpStageA + kIpStageB));
+              const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+              tma_load_2d_pair(dA, &tm_x, kb * kIpBK, arow, fb);
+              tma_load_2d_pair(dB, &tm_w, kb * kIpBK, brow, fb);
+            } else {
+              mbar_arrive_expect_tx(&full[s], kIpStageA + kIpStageB);
+              tma_load_2d(dA, &tm_x, kb * kIpBK, arow, &full[s]);
+              tma_load_2d(dB, &tm_w, kb * kIpBK, brow, &full[s]);
+            }
           }
           if (*abort_flag) break;
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
+      // the commits that hand a stage back / the accumulator over reach both CTAs when paired
+      auto commit_both = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          umma_commit_pair(smem_u32(bar));
+          umma_commit_pair(mapa_shared(smem_u32(bar), 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
       uint32_t it = 0, sc = 0;
-      for (int64_t j = blockIdx.x; j < njobs && !*abort_flag; j += gridDim.x) {
+      for (int64_t j = worker; j < njobs && !*abort_flag; j += nworkers) {
         const int u = (int)(j % a.nunit);
         for (int sg = a.unit[u].x; sg < a.unit[u].y; ++sg, ++sc) {
           const int acc = (int)(sc & 1);
-          if (!mbar_wait(&acce[acc], ((sc >> 1) & 1) ^ 1, a.wait_ns)) {
+          const bool drained = PAIR ? mbar_wait_cluster(&acce[acc], ((sc >> 1) & 1) ^ 1, a.wait_ns)
+                                    : mbar_wait(&acce[acc], ((sc >> 1) & 1) ^ 1, a.wait_ns);
+          if (!drained) {
             ip_fail(a, abort_flag);
             break;
           }
           tc_fence_after();
-          const uint32_t idesc = idesc_bf16(kIpBM, a.seg[sg].y, false, false);
+          const uint32_t idesc = idesc_bf16(kTileM, a.seg[sg].y, false, false);
           const uint32_t dt = tbase + (uint32_t)(acc * kIpBN);
           for (int kb = 0; kb < nk; ++kb, ++it) {
             const int s = (int)(it % kIpStages);
@@ -152,13 +268,17 @@ __global__ void __launch_bounds__(kIpThreads, 1)
             const uint8_t* tA = sm + s * kIpStageA;
             const uint8_t* tB = sm + kIpStages * kIpStageA + s * kIpStageB;
 #pragma unroll
-            for (int kk = 0; kk < kIpBK / 16; ++kk)
-              umma_bf16(dt, kmajor_desc(tA, kIpBM, kk * 16), kmajor_desc(tB, kIpBN, kk * 16), idesc,
-                        (kb | kk) != 0 ? 1u : 0u);
-            umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+            for (int kk = 0; kk < kIpBK / 16; ++kk) {
+              const uint64_t da = kmajor_desc(tA, kIpBM, kk * 16), db = kmajor_desc(tB, kIpBN, kk * 16);
+              if constexpr (PAIR)
+                umma_bf16_pair(dt, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+              else
+                umma_bf16(dt, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
+            commit_both(&empty[s]);  // the stage is free once these MMAs have read it
           }
           if (*abort_flag) break;
-          umma_commit(&accf[acc]);
+          commit_both(&accf[acc]);
         }
       }
     }
@@ -190,9 +310,9 @@ __global__ void __launch_bounds__(kIpThreads, 1)
         }
       }
     };
-    for (int64_t j = blockIdx.x; j < njobs && !*abort_flag; j += gridDim.x) {
+    for (int64_t j = worker; j < njobs && !*abort_flag; j += nworkers) {
       const int mt = (int)(j / a.nunit), u = (int)(j % a.nunit);
-      const int64_t grow = (int64_t)mt * kIpBM + row;
+      const int64_t grow = (int64_t)mt * kTileM + (int64_t)rank * kIpBM + row;
       const bool rok = grow < a.M;
       for (int sg = a.unit[u].x; sg < a.unit[u].y; ++sg, ++sc) {
         const int acc = (int)(sc & 1);
@@ -226,8 +346,10 @@ __global__ void __launch_bounds__(kIpThreads, 1)
                 make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
           fence_async_smem();
           __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tm_o, box, col0 + c, mt * kIpBM + q * 32);  // rows / columns past the end are not written
+          const int64_t brow0 = (int64_t)mt * kTileM + (int64_t)rank * kIpBM + q * 32;
+          if (lane == 0 && brow0 < a.M) {  // a box that starts past the last row is not issued
+            // rows / columns past the end are not written
+            tma_store_2d(&tm_o, box, col0 + c, (int)brow0);
             bulk_commit_group();
           }
           sb ^= 1;
@@ -250,7 +372,12 @@ __global__ void __launch_bounds__(kIpThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acce[acc]);
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_cluster(mapa_shared(smem_u32(&acce[acc]), 0));  // the MMA issuer's barrier
+          else
+            mbar_arrive(&acce[acc]);
+        }
         if (kind != 0 && sd.w) {  // last piece of a group's B or C row
           if (rok && a.rms) a.rms[(grow * a.G + (sd.z >> 2)) * 2 + (kind - 1)] = rsqrtf(ss / a.nr + a.eps);
           ss = 0.f;
@@ -261,9 +388,10 @@ __global__ void __launch_bounds__(kIpThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // no remote arrivals or MMAs into this CTA remain
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tbase, 512);
+    ip_tmem_dealloc<PAIR>(tbase, 512);
   }
 }
 
@@ -281,17 +409,41 @@ bool make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, in
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int opt_in_smem() {
+// Per device: opt both kernels into their shared memory and find how many CTA pairs can be
+// resident at once (0: run single CTAs).
+int device_setup(int* pairs) {
   static std::mutex mu;
-  static std::set<int> done;
+  static std::map<int, int> done;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(mu);
-  if (done.count(dev)) return M3B_OK;
-  const cudaError_t e =
-      cudaFuncSetAttribute((const void*)in_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kIpSmem);
-  if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "in_proj: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  done.insert(dev);
+  auto f = done.find(dev);
+  if (f != done.end()) {
+    *pairs = f->second;
+    return M3B_OK;
+  }
+  for (const void* k : {(const void*)in_proj_kernel<true>, (const void*)in_proj_kernel<false>}) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kIpSmem);
+    if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "in_proj: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (unsigned)(num_sms() / 2));
+  cfg.blockDim = dim3(kIpThreads);
+  cfg.dynamicSmemBytes = kIpSmem;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, (const void*)in_proj_kernel<true>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  done[dev] = n;
+  *pairs = n;
   return M3B_OK;
 }
 
@@ -358,17 +510,37 @@ int launch_in_proj(const m3b_in_proj_args* a, cudaStream_t st) {
     ok = add_range(p, 0, a->d_proj, 0, 0, false);
   }
   if (!ok) return fail(M3B_ERR_UNSUPPORTED, "in_proj: more than %d column segments", kIpMaxSeg);
-  p.mtiles = (int)((a->rows + kIpBM - 1) / kIpBM);
+  int pairs = 0;
+  int rc = device_setup(&pairs);
+  if (rc != M3B_OK) return rc;
+  const bool paired = pairs > 0;
+  const int tile_m = paired ? 2 * kIpBM : kIpBM;
+  p.mtiles = (int)((a->rows + tile_m - 1) / tile_m);
   CUtensorMap tm_x{}, tm_w{}, tm_o{};
   if (!make_map(&tm_x, a->x, a->d_model, a->rows, a->x_stride, kIpBM) ||
-      !make_map(&tm_w, a->weight, a->d_model, a->d_proj, a->d_model, kIpBN) ||
+      !make_map(&tm_w, a->weight, a->d_model, a->d_proj, a->d_model, paired ? kIpBN / 2 : kIpBN) ||
       !make_map(&tm_o, a->proj, a->d_proj, a->rows, a->proj_stride, 32))
     return fail(M3B_ERR_CUDA, "in_proj: cuTensorMapEncodeTiled refused the operands");
-  int rc = opt_in_smem();
-  if (rc != M3B_OK) return rc;
   const int64_t njobs = (int64_t)p.mtiles * p.nunit;
-  const int grid = (int)(njobs < num_sms() ? njobs : num_sms());
-  in_proj_kernel<<<grid, kIpThreads, kIpSmem, st>>>(p, tm_x, tm_w, tm_o);
+  if (!paired) {
+    const int grid = (int)(njobs < num_sms() ? njobs : num_sms());
+    in_proj_kernel<false><<<grid, kIpThreads, kIpSmem, st>>>(p, tm_x, tm_w, tm_o);
+    return check_launch("in_proj_kernel");
+  }
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (unsigned)(njobs < pairs ? njobs : pairs));
+  cfg.blockDim = dim3(kIpThreads);
+  cfg.dynamicSmemBytes = kIpSmem;
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, in_proj_kernel<true>, p, tm_x, tm_w, tm_o);
+  if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "in_proj_kernel: %s", cudaGetErrorString(e));
   return check_launch("in_proj_kernel");
 }
 
