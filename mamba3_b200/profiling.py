@@ -128,7 +128,9 @@ def kernel_workload(case: str, reps: int = 3) -> None:
     step     one layer's decode step at config-4 shapes (batch 256 x 24 heads, compact state):
              step_prep_kernel, step_stream_kernel
     fp32     config-0 layer forward (4, 1024, 768) fp32: prep, angle prefix, the tf32
-             chunk_state_kernel, the scan, the tf32 chunk_out_kernel"""
+             chunk_state_kernel, the scan, the tf32 chunk_out_kernel
+    in_proj  the config-1 input projection with its B / C 1/rms epilogue: x (16 x 4096, 768) bf16
+             -> proj (65536, 3696) (in_proj_kernel)"""
     import torch
 
     from . import ops
@@ -153,6 +155,10 @@ def kernel_workload(case: str, reps: int = 3) -> None:
                     torch.rand(B, T, H, device="cuda", generator=g) * 0.1, -torch.rand(H, device="cuda", generator=g),
                     torch.randn(H, device="cuda", generator=g), r(B, T, H, P, R))
             run = lambda: chunked_ssd(*args, return_final_state=True)  # noqa: E731
+        elif case == "in_proj":
+            m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
+            x = torch.randn(16, 4096, 768, device="cuda", generator=g).to(torch.bfloat16)
+            run = lambda: m._project(x)  # noqa: E731
         elif case == "step":
             m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
             B = 256
@@ -177,7 +183,7 @@ if __name__ == "__main__":
     import argparse
 
     ap = argparse.ArgumentParser(description="profiling helpers")
-    ap.add_argument("what", choices=["train", "cfg3", "chunked", "step", "fp32"])
+    ap.add_argument("what", choices=["train", "cfg3", "chunked", "step", "fp32", "in_proj"])
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seqlen", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=3)
