@@ -80,6 +80,14 @@ __device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
   for (int i = 0; i < 4; ++i) { float2 f = __half22float2(h[i]); v[2 * i] = f.x; v[2 * i + 1] = f.y; }
 }
 
+// 8 consecutive parameters [i, i + 8) of run-time dtype `dt` (16-byte aligned for 16-bit types,
+// 32-byte runs of two 16-byte loads for fp32)
+__device__ __forceinline__ void ldf8(const void* p, int64_t i, int dt, float (&v)[8]) {
+  if (dt == M3B_BF16) load8<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(p) + i, v);
+  else if (dt == M3B_F16) load8<__half>(reinterpret_cast<const __half*>(p) + i, v);
+  else load8<float>(reinterpret_cast<const float*>(p) + i, v);
+}
+
 template <typename T>
 __device__ __forceinline__ void store8(T* p, const float (&v)[8]);
 template <>

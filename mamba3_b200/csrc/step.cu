@@ -356,119 +356,188 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 4 : 2) step_kernel(m3b
 // ---------------------------------------------------------------------------
 // Two-kernel decode step for d_state 128, headdim <= 64 (a multiple of 8), mimo_rank 1, 2 or 4
 // (the decode configurations), used when the caller passes a workspace:
-//   step_prep_kernel   one CTA per (batch, head): the token's operands -- B^ and C^ (norm, bias,
-//                      rotation by the advanced angle), x_r, the gate, dA / gamma / beta and D --
-//                      into an operand block of the workspace; the new angle.
+//   step_prep_kernel   one warp per (batch, head): the token's operands -- the advanced angle's
+//                      cos / sin, x_r, the gate, dA / gamma / beta and D -- into the workspace,
+//                      the new angle; the warp of a group's first head also writes the group's
+//                      RMSNorm-ed (+ weight, bias) B and C rows, shared by the group's heads.
 //   step_stream_kernel persistent CTAs walk the (batch, head) items; the fp32 state of the next
-//                      item, its operand block and its previous-token state arrive by bulk copies
-//                      into the other half of a two-slot shared-memory ring while the current
-//                      item is computed, so the loop has no global-load latency of its own and
-//                      the state streams at HBM rate.  Stores go straight from registers.
+//                      item, its operands, its group's normalised B / C rows and its
+//                      previous-token state arrive by bulk copies into the other half of a
+//                      two-slot shared-memory ring while the current item is computed, so the
+//                      loop has no global-load latency of its own and the state streams at HBM
+//                      rate.  Each thread rotates the B^ / C^ entries of its four state columns
+//                      in registers.  Stores go straight from registers.
 // Same arithmetic as step_kernel.
 // ---------------------------------------------------------------------------
 constexpr int kStreamN = 128, kStreamPMax = 64;
 
-// operand block of one (batch, head) item, fp32: B^ and C^ rank-major (R x N each), x_r and
-// the gate (PMAX x R each, p-major), then dA, gamma, beta, D
+// operand block of one (batch, head) item, fp32: cos / sin of the advanced angle per pair
+// (interleaved), x_r and the gate (PMAX x R each, p-major), then dA, gamma, beta, D.  The
+// workspace holds batch x H of these, then per (batch row, group) the normalised B and C rows
+// (N R each, (n, r) order as in the projection).
 template <int R>
 struct OpBlock {
-  static constexpr int Bt = 0, Ct = R * kStreamN, Xr = 2 * R * kStreamN, Gate = Xr + kStreamPMax * R;
+  static constexpr int Cs = 0, Xr = kStreamN, Gate = Xr + kStreamPMax * R;
   static constexpr int Scal = Gate + kStreamPMax * R;
   static constexpr int floats = Scal + 4;
-  static constexpr int bytes = floats * 4;  // a multiple of 16
+  static constexpr int bytes = floats * 4;
+  static constexpr int bc_floats = 2 * kStreamN * R;  // one group's B and C rows
   static_assert(bytes % 16 == 0, "operand blocks are copied in 16-byte units");
 };
 
 template <typename TA, int R>
-__global__ void __launch_bounds__(128) step_prep_kernel(m3b_step_args a, float* ws) {
+__global__ void __launch_bounds__(256) step_prep_kernel(m3b_step_args a, float* ws, int nitems) {
+  // one warp per (batch, head) item; the warp of a group's first head also writes the group's
+  // normalised B / C rows.  Every load is issued before the first store (the workspace may alias
+  // nothing, but the compiler cannot know that), so an item costs about one memory round trip.
   using OB = OpBlock<R>;
   constexpr int N = kStreamN, NR = N * R;
+  constexpr int PC = kStreamPMax / 32;          // channels per lane
+  constexpr int Q = NR >= 256 ? NR / 256 : 1;   // 8-entry runs of the B / C rows per lane
+  constexpr int RUN = NR >= 256 ? 8 : 4;
   const m3b_layer_params& prm = a.prm;
   const int H = prm.H, P = prm.P, G = prm.G, pd = prm.param_dtype;
-  const int item = blockIdx.x;
-  const int b = item / H, h = item - (item / H) * H, g = h / (H / G);
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  __shared__ float sBr[NR], sCr[NR];  // normalised, (n, r) order
-  __shared__ float sRed[2][4];
-  __shared__ float sDt;
-  float* ob = ws + (int64_t)item * OB::floats;
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (item >= nitems) return;
+  const int b = item / H, h = item - b * H, hpg = H / G, g = h / hpg;
+  const bool leader = h % hpg == 0;
   const TA* row = reinterpret_cast<const TA*>(a.proj) + (int64_t)b * a.proj_stride;
   const int HP = H * P;
-  const int offB = 2 * HP + g * NR, offC = 2 * HP + G * NR + g * NR;
   const int offDt = 2 * HP + 2 * G * NR, offLam = offDt + H, offTh = offLam + (prm.trapezoidal ? H : 0);
-  float bv[R], cv[R];
+  const int offB = 2 * HP + g * NR, offC = 2 * HP + G * NR + g * NR;
+  // ---- loads
+  const float dt_raw = io<TA>::ld(row + offDt + h);
+  const float lam_raw = prm.trapezoidal ? io<TA>::ld(row + offLam + h) : 0.f;
+  const float dts = a.dt_scale ? io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + item) : 1.f;
+  const float dtb = ldf(prm.dt_bias, h, pd), alog = ldf(prm.A_log, h, pd), Dh = ldf(prm.D, h, pd);
+  const int64_t abase = (int64_t)item * (N / 2);
+  float ang[2], th[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {  // pairs lane and lane + 32
+    ang[k] = ldf(a.angle, abase + lane + 32 * k, a.angle_dtype);
+    th[k] = prm.complex_ssm ? io<TA>::ld(row + offTh + lane + 32 * k) : 0.f;
+  }
+  float xv[PC], zv[PC], mx[PC][R], mz[PC][R], md[PC][R];
+#pragma unroll
+  for (int k = 0; k < PC; ++k) {
+    const int p = lane + 32 * k;
+    const bool on = p < P;
+    xv[k] = on ? io<TA>::ld(row + HP + h * P + p) : 0.f;
+    zv[k] = on ? io<TA>::ld(row + h * P + p) : 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t q = ((int64_t)h * P + p) * R + r;
+      mx[k][r] = on ? ldf(prm.mimo_x, q, pd) : 0.f;
+      mz[k][r] = on ? ldf(prm.mimo_z, q, pd) : 0.f;
+      md[k][r] = on ? ldf(prm.mimo_down, q, pd) : 0.f;
+    }
+  }
+  // the group's raw B / C rows (leader warps): entries RUN lane + 256 j .. + RUN - 1
+  float bv[Q][RUN], cv[Q][RUN];
+  if (leader) {
+#pragma unroll
+    for (int j = 0; j < Q; ++j) {
+      const int e0 = RUN * lane + 256 * j;
+      if constexpr (RUN == 8) {
+        load8<TA>(row + offB + e0, bv[j]);
+        load8<TA>(row + offC + e0, cv[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < RUN; ++e) {
+          bv[j][e] = io<TA>::ld(row + offB + e0 + e);
+          cv[j][e] = io<TA>::ld(row + offC + e0 + e);
+        }
+      }
+    }
+  }
+  // ---- compute and store
+  float* ob = ws + (int64_t)item * OB::floats;
+  const float dt = softplus_f(dt_raw + dtb) * dts;
+  if (lane == 0) {
+    const float dA = expf(-expf(alog) * dt);
+    float gamma = dt, beta = 0.f;
+    if (prm.trapezoidal) {
+      const float lam = sigmoid_f(lam_raw);
+      gamma = lam * dt;
+      beta = (1.f - lam) * dt * dA;
+    }
+    *reinterpret_cast<float4*>(ob + OB::Scal) = make_float4(dA, gamma, beta, Dh);
+  }
+  // the advanced angle of pairs lane, lane + 32 and its cos / sin
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = lane + 32 * k;
+    float a_ = ang[k], sn = 0.f, cs = 1.f;
+    if (prm.complex_ssm) {
+      a_ -= dt * th[k];
+      sincosf(a_, &sn, &cs);
+    }
+    a.angle_out[abase + i] = a_;
+    *reinterpret_cast<float2*>(ob + OB::Cs + 2 * i) = make_float2(cs, sn);
+  }
+  // x_r and the gate of channels lane, lane + 32
+#pragma unroll
+  for (int k = 0; k < PC; ++k) {
+    const int p = lane + 32 * k;
+    if (p < P) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        ob[OB::Xr + p * R + r] = xv[k] * mx[k][r];
+        ob[OB::Gate + p * R + r] = silu_f(zv[k] * mz[k][r]) * md[k][r];
+      }
+    }
+  }
+  if (!leader) return;
+  // the group's joint N R RMSNorm of B and C, + weight and bias
   float sb = 0.f, sc = 0.f;
 #pragma unroll
-  for (int q = 0; q < R; ++q) {  // NR = 128 R: R entries per thread
-    const int e = tid + 128 * q;
-    bv[q] = io<TA>::ld(row + offB + e);
-    cv[q] = io<TA>::ld(row + offC + e);
-    sb = fmaf(bv[q], bv[q], sb);
-    sc = fmaf(cv[q], cv[q], sc);
-  }
+  for (int j = 0; j < Q; ++j)
+#pragma unroll
+    for (int e = 0; e < RUN; ++e) {
+      sb = fmaf(bv[j][e], bv[j][e], sb);
+      sc = fmaf(cv[j][e], cv[j][e], sc);
+    }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     sb += __shfl_xor_sync(0xffffffffu, sb, o);
     sc += __shfl_xor_sync(0xffffffffu, sc, o);
   }
-  if (lane == 0) {
-    sRed[0][wid] = sb;
-    sRed[1][wid] = sc;
-  }
-  if (tid == 0) {
-    const int64_t bh = (int64_t)b * H + h;
-    const float dts = a.dt_scale ? io<TA>::ld(reinterpret_cast<const TA*>(a.dt_scale) + bh) : 1.f;
-    const float dt = softplus_f(io<TA>::ld(row + offDt + h) + ldf(prm.dt_bias, h, pd)) * dts;
-    const float A = -expf(ldf(prm.A_log, h, pd));
-    const float dA = expf(A * dt);
-    float gamma = dt, beta = 0.f;
-    if (prm.trapezoidal) {
-      const float lam = sigmoid_f(io<TA>::ld(row + offLam + h));
-      gamma = lam * dt;
-      beta = (1.f - lam) * dt * dA;
-    }
-    ob[OB::Scal + 0] = dA;
-    ob[OB::Scal + 1] = gamma;
-    ob[OB::Scal + 2] = beta;
-    ob[OB::Scal + 3] = ldf(prm.D, h, pd);
-    sDt = dt;
-  }
-  if (tid < P) {  // x_r and the gate of channel p = tid
-    const float xv = io<TA>::ld(row + HP + h * P + tid);
-    const float zv = io<TA>::ld(row + h * P + tid);
+  const float rb = rsqrtf(sb / (float)NR + prm.norm_eps), rc = rsqrtf(sc / (float)NR + prm.norm_eps);
+  float* dst = ws + (int64_t)nitems * OB::floats + ((int64_t)b * G + g) * OB::bc_floats;
+  // the norm weights and biases: one more round trip for these warps only
+  float wb[Q][RUN], wc[Q][RUN], bb[Q][RUN], bc[Q][RUN];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int64_t q = ((int64_t)h * P + tid) * R + r;
-      ob[OB::Xr + tid * R + r] = xv * ldf(prm.mimo_x, q, pd);
-      ob[OB::Gate + tid * R + r] = silu_f(zv * ldf(prm.mimo_z, q, pd)) * ldf(prm.mimo_down, q, pd);
+  for (int j = 0; j < Q; ++j) {
+    const int e0 = RUN * lane + 256 * j;
+    if constexpr (RUN == 8) {
+      ldf8(prm.B_norm_w, e0, pd, wb[j]);
+      ldf8(prm.C_norm_w, e0, pd, wc[j]);
+      ldf8(prm.B_bias, (int64_t)g * NR + e0, pd, bb[j]);
+      ldf8(prm.C_bias, (int64_t)g * NR + e0, pd, bc[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < RUN; ++e) {
+        wb[j][e] = ldf(prm.B_norm_w, e0 + e, pd);
+        wc[j][e] = ldf(prm.C_norm_w, e0 + e, pd);
+        bb[j][e] = ldf(prm.B_bias, (int64_t)g * NR + e0 + e, pd);
+        bc[j][e] = ldf(prm.C_bias, (int64_t)g * NR + e0 + e, pd);
+      }
     }
   }
-  __syncthreads();
-  const float rb = rsqrtf((sRed[0][0] + sRed[0][1] + sRed[0][2] + sRed[0][3]) / (float)NR + prm.norm_eps);
-  const float rc = rsqrtf((sRed[1][0] + sRed[1][1] + sRed[1][2] + sRed[1][3]) / (float)NR + prm.norm_eps);
 #pragma unroll
-  for (int q = 0; q < R; ++q) {
-    const int e = tid + 128 * q;
-    sBr[e] = fmaf(bv[q] * rb, ldf(prm.B_norm_w, e, pd), ldf(prm.B_bias, (int64_t)g * NR + e, pd));
-    sCr[e] = fmaf(cv[q] * rc, ldf(prm.C_norm_w, e, pd), ldf(prm.C_bias, (int64_t)g * NR + e, pd));
-  }
-  __syncthreads();
-  if (tid < N / 2) {  // pair i = tid: advance the angle, rotate (2i, 2i+1) for every rank
-    const int i = tid;
-    const int64_t abase = ((int64_t)b * H + h) * (N / 2);
-    float ang = ldf(a.angle, abase + i, a.angle_dtype);
-    float sn = 0.f, cs = 1.f;
-    if (prm.complex_ssm) {
-      ang -= sDt * io<TA>::ld(row + offTh + i);
-      sincosf(ang, &sn, &cs);
+  for (int j = 0; j < Q; ++j) {
+    const int e0 = RUN * lane + 256 * j;
+    float ob8[RUN], oc8[RUN];
+#pragma unroll
+    for (int e = 0; e < RUN; ++e) {
+      ob8[e] = fmaf(bv[j][e] * rb, wb[j][e], bb[j][e]);
+      oc8[e] = fmaf(cv[j][e] * rc, wc[j][e], bc[j][e]);
     }
-    a.angle_out[abase + i] = ang;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const float b0 = sBr[(2 * i) * R + r], b1 = sBr[(2 * i + 1) * R + r];
-      const float c0 = sCr[(2 * i) * R + r], c1 = sCr[(2 * i + 1) * R + r];
-      *reinterpret_cast<float2*>(ob + OB::Bt + r * N + 2 * i) = make_float2(b0 * cs - b1 * sn, b0 * sn + b1 * cs);
-      *reinterpret_cast<float2*>(ob + OB::Ct + r * N + 2 * i) = make_float2(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
+    for (int e = 0; e < RUN; e += 4) {
+      *reinterpret_cast<float4*>(dst + e0 + e) = make_float4(ob8[e], ob8[e + 1], ob8[e + 2], ob8[e + 3]);
+      *reinterpret_cast<float4*>(dst + NR + e0 + e) = make_float4(oc8[e], oc8[e + 1], oc8[e + 2], oc8[e + 3]);
     }
   }
 }
@@ -478,7 +547,8 @@ struct StreamPlan {
   static constexpr int N = kStreamN, PMAX = kStreamPMax;
   static constexpr int st = PMAX * N * 4;                              // h (and prev_BX) bytes
   static constexpr int ob = (COMPACT ? 1 : 2) * st;                    // operand block
-  static constexpr int pb = ob + OpBlock<R>::bytes;                    // COMPACT: previous B^ (N, R)
+  static constexpr int bc = ob + OpBlock<R>::bytes;                    // the group's B / C rows
+  static constexpr int pb = bc + OpBlock<R>::bc_floats * 4;            // COMPACT: previous B^ (N, R)
   static constexpr int px = pb + N * R * 4;                            // COMPACT: previous x_r (P, R)
   static constexpr int slot_used = COMPACT ? px + PMAX * R * 4 : pb;
   static constexpr int slot = (slot_used + 127) / 128 * 128;     // 128-byte aligned slots
@@ -503,6 +573,9 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
   const int nvec = P * N / 4;
   const uint32_t sbytes = (uint32_t)(P * N * 4);
   const uint32_t pbytes = (uint32_t)(N * R * 4), xbytes = (uint32_t)(P * R * 4);
+  const uint32_t bcbytes = (uint32_t)(OB::bc_floats * 4);
+  const float* wbc = ws + (int64_t)nitems * OB::floats;  // the (batch row, group) B / C rows
+  const int hpg = H / prm.G;
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -521,8 +594,10 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
     uint8_t* d = ssm + sl * SP::slot;
     uint64_t* bar = &bars[sl];
     const int64_t sbase = (int64_t)it * P * N;
-    mbar_arrive_expect_tx(bar, (COMPACT ? sbytes + pbytes + xbytes : 2 * sbytes) + (uint32_t)OB::bytes);
+    mbar_arrive_expect_tx(bar, (COMPACT ? sbytes + pbytes + xbytes : 2 * sbytes) + (uint32_t)OB::bytes + bcbytes);
     bulk(d, a.h + sbase, sbytes, bar);
+    const int ib = it / H, ig = (it - ib * H) / hpg;
+    bulk(d + SP::bc, wbc + ((int64_t)ib * prm.G + ig) * OB::bc_floats, bcbytes, bar);
     if constexpr (COMPACT) {
       bulk(d + SP::pb, a.prev_b + (int64_t)it * N * R, pbytes, bar);
       bulk(d + SP::px, a.prev_x + (int64_t)it * P * R, xbytes, bar);
@@ -548,8 +623,8 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
     }
     const uint8_t* d = ssm + sl * SP::slot;
     const float* obs = reinterpret_cast<const float*>(d + SP::ob);
-    const float* sB = obs + OB::Bt;
-    const float* sC = obs + OB::Ct;
+    const float* sBn = reinterpret_cast<const float*>(d + SP::bc);  // normalised B, then C, (n, r) order
+    const float* sCn = sBn + N * R;
     const float* sXr = obs + OB::Xr;
     const float dA = obs[OB::Scal + 0], gamma = obs[OB::Scal + 1], beta = obs[OB::Scal + 2];
     const float4* hs4 = reinterpret_cast<const float4*>(d);
@@ -561,15 +636,33 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
     constexpr int BATCH = 8;  // float4 f = u * 256 + tid: row p = 8 u + warp, columns 4 lane ..
     float part[BATCH][R];
     const int n0 = 4 * lane;
-    // this thread's four state columns n0 .. n0 + 3 are the same for all its rows: their B^, C^
-    // (and previous B^) entries are read from shared memory once per item
+    // this thread's four state columns n0 .. n0 + 3 (pairs n0 / 2 and n0 / 2 + 1) are the same for
+    // all its rows: their normalised B / C entries (and previous B^) are read from shared memory
+    // once per item and rotated here by the head's angle: (x0 c - x1 s, x0 s + x1 c)
     float bq[R][4], cq[R][4], pbv[COMPACT ? 4 * R : 1];
+    {
+      const float4 cs4 = *reinterpret_cast<const float4*>(obs + OB::Cs + n0);  // c0, s0, c1, s1
+      float bn[4 * R], cn[4 * R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const float4 b4 = *reinterpret_cast<const float4*>(sB + r * N + n0);
-      const float4 c4 = *reinterpret_cast<const float4*>(sC + r * N + n0);
-      bq[r][0] = b4.x, bq[r][1] = b4.y, bq[r][2] = b4.z, bq[r][3] = b4.w;
-      cq[r][0] = c4.x, cq[r][1] = c4.y, cq[r][2] = c4.z, cq[r][3] = c4.w;
+      for (int q = 0; q < R; ++q) {
+        const float4 b4 = reinterpret_cast<const float4*>(sBn + n0 * R)[q];
+        const float4 c4 = reinterpret_cast<const float4*>(sCn + n0 * R)[q];
+        bn[4 * q] = b4.x, bn[4 * q + 1] = b4.y, bn[4 * q + 2] = b4.z, bn[4 * q + 3] = b4.w;
+        cn[4 * q] = c4.x, cn[4 * q + 1] = c4.y, cn[4 * q + 2] = c4.z, cn[4 * q + 3] = c4.w;
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float b0 = bn[r], b1 = bn[R + r], b2 = bn[2 * R + r], b3 = bn[3 * R + r];
+        const float c0 = cn[r], c1 = cn[R + r], c2 = cn[2 * R + r], c3 = cn[3 * R + r];
+        bq[r][0] = b0 * cs4.x - b1 * cs4.y;
+        bq[r][1] = b0 * cs4.y + b1 * cs4.x;
+        bq[r][2] = b2 * cs4.z - b3 * cs4.w;
+        bq[r][3] = b2 * cs4.w + b3 * cs4.z;
+        cq[r][0] = c0 * cs4.x - c1 * cs4.y;
+        cq[r][1] = c0 * cs4.y + c1 * cs4.x;
+        cq[r][2] = c2 * cs4.z - c3 * cs4.w;
+        cq[r][3] = c2 * cs4.w + c3 * cs4.z;
+      }
     }
     if constexpr (COMPACT) {
 #pragma unroll
@@ -657,9 +750,18 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
     __syncthreads();
     const int b = item / H, h = item - (item / H) * H;
     if constexpr (COMPACT) {  // this token's B^ and x_r are the next step's previous token
-      for (int e = tid; e < N * R; e += kStepThreads) {
-        const int n = e / R, r = e - (e / R) * R;
-        a.prev_b_out[(int64_t)item * N * R + e] = sB[r * N + n];
+      if (wid == 0) {  // warp 0 holds all N columns' rotated B^: (n, r) entries n0 .. n0 + 3
+        float4* pbo = reinterpret_cast<float4*>(a.prev_b_out + (int64_t)item * N * R + n0 * R);
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+          float v4[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int e = 4 * q + k;  // entry (n0 + e / R, e % R)
+            v4[k] = bq[e % R][e / R];
+          }
+          pbo[q] = make_float4(v4[0], v4[1], v4[2], v4[3]);
+        }
       }
       for (int e = tid; e < P * R; e += kStepThreads) a.prev_x_out[(int64_t)item * P * R + e] = sXr[e];
     }
@@ -678,14 +780,19 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
 // The two-kernel path covers d_state 128, headdim <= 64 (a multiple of 8), mimo_rank 1, 2, 4.
 static bool stream_ok(const m3b_step_args* a) {
   const m3b_layer_params& p = a->prm;
-  return p.N == kStreamN && p.P <= kStreamPMax && p.P % 8 == 0 && (p.R == 1 || p.R == 2 || p.R == 4) &&
+  const int esz = a->act_dtype == M3B_F32 ? 4 : 2;
+  // the prep's vector loads of the B / C rows: 16-byte aligned projection rows
+  const bool rows16 = aligned16(a->proj) && (a->proj_stride * esz) % 16 == 0 && (2 * p.H * p.P) % 8 == 0 &&
+                      aligned16(p.B_norm_w) && aligned16(p.C_norm_w) && aligned16(p.B_bias) && aligned16(p.C_bias);
+  return p.N == kStreamN && p.P <= kStreamPMax && p.P % 8 == 0 && (p.R == 1 || p.R == 2 || p.R == 4) && rows16 &&
          a->batch * p.H <= 0x7fffffffLL;
 }
 
 static size_t stream_ws_bytes(const m3b_step_args* a) {
   const int R = a->prm.R;
   const size_t ob = R == 1 ? OpBlock<1>::bytes : R == 2 ? OpBlock<2>::bytes : OpBlock<4>::bytes;
-  return (size_t)a->batch * a->prm.H * ob;
+  const size_t bc = (size_t)2 * kStreamN * R * 4;
+  return (size_t)a->batch * a->prm.H * ob + (size_t)a->batch * a->prm.G * bc;
 }
 
 template <typename TA, int R, bool COMPACT>
@@ -711,7 +818,7 @@ static int launch_stream_t(const m3b_step_args* a, float* ws, cudaStream_t st) {
   }
   if (occ < 1) return fail(M3B_ERR_UNSUPPORTED, "step (stream): kernel does not fit an SM");
   const int nitems = (int)(a->batch * a->prm.H);
-  step_prep_kernel<TA, R><<<nitems, 128, 0, st>>>(*a, ws);
+  step_prep_kernel<TA, R><<<(unsigned)((nitems + 7) / 8), 256, 0, st>>>(*a, ws, nitems);
   int rc = check_launch("step (prep)");
   if (rc != M3B_OK) return rc;
   const int cap = num_sms() * occ;
