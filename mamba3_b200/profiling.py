@@ -130,7 +130,9 @@ def kernel_workload(case: str, reps: int = 3) -> None:
     fp32     config-0 layer forward (4, 1024, 768) fp32: prep, angle prefix, the tf32
              chunk_state_kernel, the scan, the tf32 chunk_out_kernel
     in_proj  the config-1 input projection with its B / C 1/rms epilogue: x (16 x 4096, 768) bf16
-             -> proj (65536, 3696) (in_proj_kernel)"""
+             -> proj (65536, 3696) (in_proj_kernel)
+    decode   config-4 decoding: the 24-layer LM, batch 256, a 16-token prompt, then `reps` token
+             steps of the CUDA-graph decoder (every kernel of a token step, in graph order)"""
     import torch
 
     from . import ops
@@ -159,6 +161,21 @@ def kernel_workload(case: str, reps: int = 3) -> None:
             m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
             x = torch.randn(16, 4096, 768, device="cuda", generator=g).to(torch.bfloat16)
             run = lambda: m._project(x)  # noqa: E731
+        elif case == "decode":
+            from .block import KulaMambaLM
+            from .decode import GraphDecoder
+
+            lm = KulaMambaLM(vocab_size=32000, d_model=768, n_layers=24, d_state=128, headdim=64, mimo_rank=2,
+                             residual_scale="depth").cuda().to(torch.bfloat16).eval()
+            ids = torch.randint(0, 32000, (256, 16), device="cuda", generator=g)
+            dec = GraphDecoder(lm, batch_size=256, max_new_tokens=2 + reps)
+            dec.prefill(ids)
+            dec.decode(1)  # captures the step graph
+            torch.cuda.synchronize()
+            for _ in range(reps):
+                dec.decode(1)
+            torch.cuda.synchronize()
+            return
         elif case == "step":
             m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
             B = 256
@@ -183,7 +200,7 @@ if __name__ == "__main__":
     import argparse
 
     ap = argparse.ArgumentParser(description="profiling helpers")
-    ap.add_argument("what", choices=["train", "cfg3", "chunked", "step", "fp32", "in_proj"])
+    ap.add_argument("what", choices=["train", "cfg3", "chunked", "step", "fp32", "in_proj", "decode"])
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seqlen", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=3)
