@@ -173,13 +173,19 @@ SIGNATURES = {
 
 
 def lib():
-    """The loaded library (loaded once; raises if it was not built)."""
+    """The loaded library (loaded once).  A library that is missing, or was built from other
+    sources than the ones beside it (content digest), is compiled first; raises if that fails."""
     global _lib
     if _lib is None:
         with _lock:
             if _lib is None:
-                if not LIB_PATH.exists():
-                    raise M3bError(f"{LIB_PATH.name} is not built; run `python -m mamba3_b200.build`")
+                from . import build as _build
+
+                if not _build.is_current():
+                    try:
+                        _build.build()
+                    except Exception as e:  # noqa: BLE001 - reported with the reason
+                        raise M3bError(f"{LIB_PATH.name} is missing or stale and could not be built: {e}") from e
                 h = C.CDLL(str(LIB_PATH))
                 for name, (res, args) in SIGNATURES.items():
                     f = getattr(h, name)

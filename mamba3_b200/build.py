@@ -9,6 +9,7 @@ it travels with the source tree.
 
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -19,6 +20,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libmamba3_b200.so"
+# sha256 of the flags and every source the library was built from, written beside it
+DIGEST = PKG / "libmamba3_b200.so.digest"
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -40,10 +43,33 @@ def sources():
     return sorted(CSRC.glob("*.cu"))
 
 
+def _deps():
+    return sources() + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [ROOT / "include" / "mamba3_b200.h"]
+
+
+def source_digest() -> str:
+    """sha256 over the compiler flags and the contents of every file the library is built from."""
+    h = hashlib.sha256()
+    h.update("\0".join(NVCC_FLAGS[:-1]).encode())  # the include path itself is machine-specific
+    for p in _deps():
+        h.update(p.relative_to(ROOT).as_posix().encode() + b"\0")
+        h.update(p.read_bytes())
+    return h.hexdigest()
+
+
+def is_current() -> bool:
+    """True when the library exists and was built from exactly the sources and flags present now."""
+    try:
+        return LIB.exists() and DIGEST.read_text().strip() == source_digest()
+    except OSError:
+        return False
+
+
 def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> Path:
+    """Compile the library unless it is current (same sources and flags, by content, not by mtime)."""
     srcs = sources()
-    deps = srcs + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [ROOT / "include" / "mamba3_b200.h"]
-    if not force and LIB.exists() and LIB.stat().st_mtime >= max(p.stat().st_mtime for p in deps):
+    digest = source_digest()
+    if not force and is_current():
         return LIB
     objdir = ROOT / "_build"
     objdir.mkdir(exist_ok=True)
@@ -74,6 +100,7 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
         print(" ".join(cmd))
     subprocess.check_call(cmd)
     os.replace(tmp, LIB)
+    DIGEST.write_text(digest + "\n")
     return LIB
 
 
