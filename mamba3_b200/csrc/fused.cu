@@ -3,21 +3,21 @@
 //
 // Roles (512 threads, 128 registers each):
 //   warps 0-7   epilogue (TMEM lane quadrant = warp % 4, column half = warp / 4):
-//               decay mask S -> P (kept in TMEM, so the mask waits for S only, not for the state
-//               GEMMs that still read this chunk's B^ tile), output y = P X + e^cum C^ H'^T + D x
-//               with gate and MIMO down,
+//               decay mask S -> P (kept in TMEM), output y = P X + e^cum C^ H'^T + D x with gate
+//               and MIMO down,
 //               running-state bookkeeping (TMEM <-> bf16 tile), MIMO x tiles X and W, h_final.
 //               Its leader issues the GEMMs that depend on the running state and on P, and
 //               hands each shared-memory stage back to the producers (with the TMA copies of
-//               the chunk two ahead) once the output that read it is written.
+//               the chunk two ahead) as soon as the last GEMM that reads the stage has completed,
+//               before the output of that chunk is written.
 //   warps 8-15  producers: per chunk, token scalars, angle prefix + RoPE + norm of B/C into one
 //               of two shared-memory stages; their leader issues S = C^ B^T.
 // Per chunk g (stage s = g % 2), with the running state H (fp32, TMEM lanes n x columns p):
 //   producer leader:  S_g = C^ B^T                            -> TMEM S[g%2] (128 columns)
-//   epilogue leader:  Yi_g = C^ H'_g^T, H += B^^T W           -> Yi[g%2], H    (after state(g))
-//                     Y_g = P X, P read from TMEM             -> first 64 columns of S[g%2]
-//   epilogue:         mask(g), output(g), state(g+1): H'_{g+1} = H -> bf16 tile, H *= d_{g+1},
-//                     X and W tiles of chunk g+1
+//   epilogue leader:  Yi_g = C^ H'_g^T, H += B^^T W           -> Yi, H          (after state(g))
+//                     Y_g = P X, P read from TMEM             -> Y
+//   epilogue:         mask(g), [stage s handed over], output(g), state(g+1): H'_{g+1} = H -> bf16
+//                     tile, H *= d_{g+1}, X and W tiles of chunk g+1
 // The algebra (weights W, w, the first-token beta term carried by H') is in chunk.cuh.
 // Every wait is bounded.  On a timeout a role's leader raises that role's own abort flag, which
 // the role reads after its named barrier, so all its threads leave the loop together; the other
@@ -36,9 +36,10 @@ namespace m3b {
 constexpr int kFusedThreads = 16 * 32;
 constexpr int kEpiThreads = 256;
 constexpr int kProdThreads = 256;
-// TMEM columns: S[g%2] at 128 (g%2) (Y_g lands in its first 64); Yi at 256 + 64 (g%2); H at 384;
-// the masked score tile P (bf16, two per column) at 448.
-constexpr uint32_t kColS = 0, kColYi = 256, kColH = 384, kColP = 448;
+// TMEM columns: S[g%2] at 128 (g%2); Yi at 256; Y at 320; H at 384; the masked score tile P (bf16,
+// two per column) at 448.  Yi and Y have one buffer each: a chunk's GEMMs that write them are
+// issued only after the previous chunk's output has read them.
+constexpr uint32_t kColS = 0, kColYi = 256, kColY = 320, kColH = 384, kColP = 448;
 constexpr int kBarProd = 1, kBarEpi = 2;
 
 // Optional per-phase timestamps of CTA 0 for pipeline analysis: build with -DM3B_TIMELINE and
@@ -76,8 +77,8 @@ struct FPlan {
   static_assert(bytes <= 227 * 1024, "fused CTA shared memory exceeds 227 KB");
 };
 
-enum { BAR_FULL0 = 0, BAR_FULL1 = 1, BAR_EMPTY0 = 2, BAR_EMPTY1 = 3, BAR_SDONE0 = 4, BAR_SDONE1 = 5,
-       BAR_HDONE = 6, BAR_YDONE = 7, BAR_STAGE0 = 8, BAR_STAGE1 = 9 };
+enum { BAR_FULL0 = 0, BAR_FULL1 = 1, BAR_SDONE0 = 4, BAR_SDONE1 = 5, BAR_HDONE = 6, BAR_YDONE = 7,
+       BAR_STAGE0 = 8, BAR_STAGE1 = 9 };
 
 // Position of one chunk: job, part of the sequence, sequence index, batch row, head, group,
 // chunk within the sequence (k) and within the part (kk).
@@ -272,8 +273,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   if (tid == 32) {
     mbar_init(&bars[BAR_FULL0], 1);
     mbar_init(&bars[BAR_FULL1], 1);
-    mbar_init(&bars[BAR_EMPTY0], kEpiThreads);
-    mbar_init(&bars[BAR_EMPTY1], kEpiThreads);
     mbar_init(&bars[BAR_SDONE0], 1);
     mbar_init(&bars[BAR_SDONE1], 1);
     mbar_init(&bars[BAR_HDONE], 1);
@@ -806,11 +805,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const int s = g & 1;
       uint8_t* st = sm + s * PL::kStage;
       tc_fence_after();
-      const uint32_t cyi = kColYi + 64 * s;
       if constexpr (!SO) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tbase + cyi, kmajor_desc(st + PL::tC, 128, kk * 16), mnmajor_desc(tileH, 128, kk * 16), idO,
+          umma_bf16(tbase + kColYi, kmajor_desc(st + PL::tC, 128, kk * 16), mnmajor_desc(tileH, 128, kk * 16), idO,
                     kk > 0 ? 1u : 0u);
       }
 #pragma unroll
@@ -926,7 +924,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if constexpr (SO) {
         // state only: the H update of chunk g must be complete before the stage is handed
         // over and before state(g+1) reads H
-        if (!(ok = role_wait(&bars[BAR_HDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err, a.wait_ns))) break;
+        if (lead && !*abort_flag) {
+          if (!mbar_wait(&bars[BAR_HDONE], g & 1, a.wait_ns)) {
+            *abort_flag = 1;
+            record_error(a.err, M3B_ERR_TIMEOUT);
+          } else if (g + 2 < G) {
+            issue_stage(sc.ahead(pnext, 1), g + 2);
+          }
+        }
+        __syncwarp();
+        named_bar(kBarEpi, kEpiThreads);
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
       } else {
         // z of this thread's row (t, r) and column half, prefetched while the tensor core works
@@ -962,11 +973,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         // and W the chunk-state tile: no per-element exponentials.  Otherwise P = S * w, Y = P X.
         // Column block blk (32 columns) of warp quadrant lq lies below (blk < lq), on (blk == lq)
         // or above (blk > lq) the block diagonal, for every lane alike.
+        // Everything the output needs from this stage (scalars, the thread's x_r row of the X tile)
+        // is read here: the stage goes back to the producers before the output is written.
         constexpr float kSepRange = 64.f;
         const float c_last = cum2[L - 1];
         const bool sep = cum2[0] - c_last <= kSepRange;
+        const float Dh = ldf(p.D, h, p.param_dtype);
+        const float ct = cum2[t];
+        const float ec = exp2f(ct);
+        const float et = sep ? exp2f(ct - c_last) : 1.f;
         {
-          const float ct = cum2[t];
           const float gwt = gbw[t];
           const float rat = gwt > 0.f ? gam[t] / gwt : 0.f;
 #pragma unroll
@@ -996,16 +1012,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                   const int sj = (c0 + jj) / RP;
                   const float e = ex2_fast(fminf(ct - cum2[sj], 0.f));
                   const float w = sj < t ? e * gbw[sj] : (sj == t ? gam[sj] : 0.f);
-                  if constexpr (RP >= 2) {
 #pragma unroll
-                    for (int q = 0; q < RP; q += 2) {
-                      const float2 pr = mul2(make_float2(v[jj + q], v[jj + q + 1]), make_float2(w, w));
-                      v[jj + q] = pr.x;
-                      v[jj + q + 1] = pr.y;
-                    }
-                  } else {
-                    v[jj] *= w;
-                  }
+                  for (int q = 0; q < RP; ++q) v[jj + q] *= w;
                 }
               }
             }
@@ -1017,59 +1025,61 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             if (lead && c32 == 0) M3B_TL(g, 14);
           }
         }
+        // x_r of this thread's row (t, r) and column half, for D x (the X tile goes back with the stage)
+        uint4 xq[4];
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8)
+          xq[c8] = *reinterpret_cast<const uint4*>(st + PL::tX + sw128_offset(m, 32 * ch + c8 * 8, 128));
         tmem_wait_st();
         tc_fence_before();
         named_bar(kBarEpi, kEpiThreads);
         if (lead) {
-          // Y_g = P' W (separable) or P X into the first 64 columns of S[g%2] (the mask has consumed
-          // S_g); A = P from TMEM, K = (s, q) in 8 columns per instruction
+          // Y_g = P' W (separable) or P X into Y (the previous chunk's output has read it); A = P
+          // from TMEM, K = (s, q) in 8 columns per instruction
           tc_fence_after();
           const uint8_t* yb = st + (sep ? PL::tW : PL::tX);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ts(tbase + cs0, tbase + kColP + 8 * kk, mnmajor_desc(yb, 128, kk * 16), idO, kk > 0 ? 1u : 0u);
+            umma_bf16_ts(tbase + kColY, tbase + kColP + 8 * kk, mnmajor_desc(yb, 128, kk * 16), idO, kk > 0 ? 1u : 0u);
           umma_commit(&bars[BAR_YDONE]);
           M3B_TL(g, 9);
         }
-        // ---- output of chunk g (x_r comes from the X tile of this stage).  YDONE also covers the
-        // state GEMMs of chunk g (Yi_g, the H update), committed earlier by the same thread; their
-        // own barrier phase is consumed here so that its phases stay in step with the chunks.
-        if (lead && !*abort_flag && !mbar_wait(&bars[BAR_HDONE], g & 1, a.wait_ns)) {
-          *abort_flag = 1;
-          record_error(a.err, M3B_ERR_TIMEOUT);
+        // The state GEMMs of chunk g (Yi_g, the H update; committed to HDONE) and Y_g (YDONE) are
+        // the last readers of stage s: once both have completed, the stage goes to the producers
+        // for chunk g + 2 (with its TMA copies) while this chunk's output is written.
+        if (lead && !*abort_flag) {
+          if (!mbar_wait(&bars[BAR_HDONE], g & 1, a.wait_ns) || !mbar_wait(&bars[BAR_YDONE], g & 1, a.wait_ns)) {
+            *abort_flag = 1;
+            record_error(a.err, M3B_ERR_TIMEOUT);
+          } else if (g + 2 < G) {
+            issue_stage(sc.ahead(pnext, 1), g + 2);
+          }
         }
-        if (!(ok = role_wait(&bars[BAR_YDONE], g & 1, lead, kBarEpi, kEpiThreads, abort_flag, a.err, a.wait_ns))) break;
+        __syncwarp();
+        named_bar(kBarEpi, kEpiThreads);
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         if (lead) M3B_TL(g, 10);
+        // ---- output of chunk g: y = e_t Y + e^cum_t Yi + D x_r, gate, MIMO down
         {
-          const float ec = exp2f(cum2[t]);
-          const float et = sep ? exp2f(cum2[t] - c_last) : 1.f;
-          const float Dh = ldf(p.D, h, p.param_dtype);
           const float2 et2 = make_float2(et, et), ec2 = make_float2(ec, ec), D2 = make_float2(Dh, Dh);
           TA* yo = reinterpret_cast<TA*>(a.y) + ((int64_t)b * a.T + tok) * HP + (int64_t)h * P;
-          const uint32_t cyi = kColYi + 64 * s;
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
             // 16 columns of Y and of Yi in flight at once, combined right away
             uint32_t yraw[16], yiraw[16];
-            tmem_ld16_async(trow + cs0 + 32 * ch + 16 * qq, yraw);
-            tmem_ld16_async(trow + cyi + 32 * ch + 16 * qq, yiraw);
+            tmem_ld16_async(trow + kColY + 32 * ch + 16 * qq, yraw);
+            tmem_ld16_async(trow + kColYi + 32 * ch + 16 * qq, yiraw);
             tmem_wait_ld(yraw, yiraw);
-            float ysum[16];
-#pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              const float2 v = fma2(et2, make_float2(__uint_as_float(yraw[i]), __uint_as_float(yraw[i + 1])),
-                                    mul2(ec2, make_float2(__uint_as_float(yiraw[i]), __uint_as_float(yiraw[i + 1]))));
-              ysum[i] = v.x;
-              ysum[i + 1] = v.y;
-            }
             float acc[16];
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
               const int c8 = 2 * qq + hc;  // chunk within this column half
               const int p8 = 32 * ch + c8 * 8;
-              const uint4 xq = *reinterpret_cast<const uint4*>(st + PL::tX + sw128_offset(m, p8, 128));
-              const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
+              const uint32_t xw[4] = {xq[c8].x, xq[c8].y, xq[c8].z, xq[c8].w};
               const float4* mz4 = reinterpret_cast<const float4*>(emz + r * kPP + p8);
               const float4* md4 = reinterpret_cast<const float4*>(emd + r * kPP + p8);
               const float4 za = mz4[0], zb = mz4[1], da = md4[0], db = md4[1];
@@ -1080,7 +1090,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 #pragma unroll
               for (int e2 = 0; e2 < 4; ++e2) {
                 const int i = 8 * hc + 2 * e2;
-                const float2 yv = fma2(D2, bf2_to_f2(xw[e2]), make_float2(ysum[i], ysum[i + 1]));
+                const float2 ys = fma2(et2, make_float2(__uint_as_float(yraw[i]), __uint_as_float(yraw[i + 1])),
+                                       mul2(ec2, make_float2(__uint_as_float(yiraw[i]), __uint_as_float(yiraw[i + 1]))));
+                const float2 yv = fma2(D2, bf2_to_f2(xw[e2]), ys);
                 const float2 gz = silu_fast2(mul2(zr[c8].pair(2 * e2), mzp[e2]));
                 const float2 o = mul2(mul2(yv, gz), mdp[e2]);
                 acc[i] = o.x;
@@ -1129,18 +1141,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&bars[BAR_EMPTY0 + s]);
       if (lead) M3B_TL(g, 11);
-      // every epilogue thread is done with stage s for chunk g: hand it over for chunk g + 2
-      if (lead && g + 2 < G && !*abort_flag) {
-        if (mbar_wait(&bars[BAR_EMPTY0 + s], (g >> 1) & 1, a.wait_ns)) {
-          issue_stage(sc.ahead(pnext, 1), g + 2);
-        } else {
-          *abort_flag = 1;
-          record_error(a.err, M3B_ERR_TIMEOUT);
-        }
-      }
       // ---- state for chunk g+1: H'_{g+1} -> bf16 tile, H *= d_{g+1}; then Yi_{g+1}, H += ...
       if (g + 1 < G) {
         if (pnext.kk == 0) {  // a new job starts with chunk g+1
