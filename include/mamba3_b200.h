@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3B_ABI_VERSION 7
+#define M3B_ABI_VERSION 8
 
 #if defined(__GNUC__)
 #define M3B_API __attribute__((visibility("default")))
@@ -346,6 +346,31 @@ typedef struct m3b_ssd_bwd_args {
 } m3b_ssd_bwd_args;
 M3B_API size_t m3b_chunked_ssd_bwd_workspace(const m3b_ssd_bwd_args* a);
 M3B_API int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Cross-shard fold of the sequence-parallel prefill (no counterpart in the reference, which
+ * runs one sequence on one device; it replaces the h_init chaining of mamba3/ssd.py:118-131
+ * across devices).  Rank g's summary of its token range, run from the zero state, is one fp32
+ * block [S (batch,H,P,N) | PB (batch,H,P,N) | Om (batch,H,N/2) | Lam (batch,H) | c0 (batch,H)]:
+ * final state, final prev_BX, final angle, sum of A dt, and (1 - lam) dt of its first token.
+ * `summaries` holds the blocks of ranks 0, 1, ... rank_stride floats apart (an all_gather
+ * output).  Writes the exact state entering rank `upto`'s range:
+ *   h = sum_{g<upto} exp(sum_{g<j<upto} Lam_j) (exp(Lam_g) c0_g pb_g + Rot(a_g) S_g),
+ *   angle = a_upto, prev_bx = Rot(a_{upto-1}) PB_{upto-1}    (a_g = sum_{j<g} Om_j,
+ * pb_g = Rot(a_{g-1}) PB_{g-1}, Rot(a) turning the (2i, 2i+1) columns by a_i); upto = 0 gives
+ * the zero state.  h and prev_bx 8-byte aligned.
+ * ------------------------------------------------------------------------ */
+typedef struct m3b_seqpar_fold_args {
+  const float* summaries;
+  int64_t rank_stride;
+  int32_t upto;
+  int64_t batch;
+  int32_t H, P, N;
+  float* h;
+  float* angle;
+  float* prev_bx;
+} m3b_seqpar_fold_args;
+M3B_API int m3b_seqpar_fold(const m3b_seqpar_fold_args* a, void* stream);
 
 /* ------------------------------------------------------------------------
  * RMSNorm of the blocks around the layer (mamba3/mamba3.py:19-35; used by

@@ -130,6 +130,12 @@ class XprepArgs(C.Structure):
                 ("ddt", C.c_void_p), ("dA", C.c_void_p)]
 
 
+class SeqparFoldArgs(C.Structure):
+    _fields_ = [("summaries", C.c_void_p), ("rank_stride", C.c_int64), ("upto", C.c_int32), ("batch", C.c_int64),
+                ("H", C.c_int32), ("P", C.c_int32), ("N", C.c_int32), ("h", C.c_void_p), ("angle", C.c_void_p),
+                ("prev_bx", C.c_void_p)]
+
+
 LAYER_FWD_STAGES = ("prep", "angle_prefix", "chunk_state", "scan", "chunk_out", "last_bx")
 
 
@@ -147,6 +153,7 @@ SIGNATURES = {
     "m3b_layer_fwd": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p, C.c_size_t, C.c_void_p]),
     "m3b_layer_fwd_noalloc": (C.c_int, [C.POINTER(LayerFwdArgs), C.c_void_p]),
     "m3b_in_proj": (C.c_int, [C.POINTER(InProjArgs), C.c_void_p]),
+    "m3b_seqpar_fold": (C.c_int, [C.POINTER(SeqparFoldArgs), C.c_void_p]),
     "m3b_copy_rows_async": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_void_p]),
     "m3b_chunked_ssd_workspace": (C.c_size_t, [C.POINTER(SsdArgs)]),
@@ -703,3 +710,18 @@ def copy_token_range(dst, dst_t0, src, src_t0, ntok, stream):
     s_ptr = C.c_void_p(src.data_ptr() + src_t0 * src.stride(1) * es)
     _check(lib().m3b_copy_rows_async(d_ptr, dst.stride(0) * es, s_ptr, src.stride(0) * es, row, src.shape[0],
                                      C.c_void_p(stream.cuda_stream)), "m3b_copy_rows_async")
+
+
+def seqpar_fold(summaries, upto: int, batch: int, H: int, P: int, N: int, h, angle, prev_bx):
+    """m3b_seqpar_fold: the state entering shard `upto` from the summaries of shards 0 .. upto-1.
+    summaries: (world, rank_stride) fp32 CUDA tensor (each row one rank's [S | PB | Om | Lam | c0]);
+    h, prev_bx (batch, H, P, N) and angle (batch, H, N/2) fp32 outputs."""
+    import torch
+
+    for t in (summaries, h, angle, prev_bx):
+        if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+            raise M3bError("seqpar_fold: fp32 contiguous CUDA tensors required")
+    a = SeqparFoldArgs(C.c_void_p(summaries.data_ptr()), summaries.stride(0) if summaries.dim() > 1 else 0,
+                       upto, batch, H, P, N, C.c_void_p(h.data_ptr()), C.c_void_p(angle.data_ptr()),
+                       C.c_void_p(prev_bx.data_ptr()))
+    _check(lib().m3b_seqpar_fold(C.byref(a), _stream(h.device)), "m3b_seqpar_fold")

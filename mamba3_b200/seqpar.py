@@ -14,8 +14,10 @@ rotating both sides of a dot product leaves it unchanged, so the shard's own out
 depend on a).  So:
 
 1. every rank runs the layer on its shard from the zero state and keeps (S, PB, Om, Lam, c0);
-2. one all_gather exchanges the tuples (4 P N + N/2 + 2 floats per (batch, head));
-3. rank r folds the tuples of ranks 0 .. r-1 into its exact initial state;
+2. one all_gather exchanges the tuples (2 P N + N/2 + 2 floats per (batch, head)) into one
+   (world, summary) buffer;
+3. rank r folds the tuples of ranks 0 .. r-1 into its exact initial state (one kernel,
+   m3b_seqpar_fold; `fold` below is the same algebra in torch ops);
 4. rank r runs the layer on its shard again from that state (prefill_from).
 
 The exchange is the only collective.  Step 1 asks only for the state (no C^, no intra-chunk
@@ -104,10 +106,10 @@ def unpack(buf: torch.Tensor, like: dict) -> dict:
     return out
 
 
-def exchange(aff: dict, group=None) -> list:
-    """all_gather of every rank's summary (one flat fp32 buffer per rank).  A first all_gather of
-    the summaries' shapes makes every rank raise ValueError, instead of exchanging garbage, when
-    the ranks do not hold the same problem (batch rows, heads, headdim, d_state)."""
+def _gather_flat(aff: dict, group=None) -> torch.Tensor:
+    """all_gather of every rank's packed summary into one (world, n) buffer.  A first all_gather
+    of the summaries' shapes makes every rank raise ValueError, instead of exchanging garbage,
+    when the ranks do not hold the same problem (batch rows, heads, headdim, d_state)."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
@@ -115,14 +117,34 @@ def exchange(aff: dict, group=None) -> list:
     shape = torch.tensor([d for k in _KEYS for d in (*aff[k].shape, -1)], dtype=torch.int64, device=mine.device)
     head = torch.zeros(64, dtype=torch.int64, device=mine.device)
     head[:min(64, shape.numel())] = shape[:64]
-    heads = [torch.empty_like(head) for _ in range(world)]
-    dist.all_gather(heads, head, group=group)
-    if any(not torch.equal(h, heads[0]) for h in heads):
+    heads = torch.empty(world * 64, dtype=torch.int64, device=mine.device)
+    dist.all_gather_into_tensor(heads, head, group=group)
+    heads = heads.view(world, 64)
+    if not bool((heads == heads[:1]).all()):
         raise ValueError("seqpar.exchange: ranks hold summaries of different shapes "
                          f"({[h[h != 0].tolist()[:8] for h in heads]})")
-    bufs = [torch.empty_like(mine) for _ in range(world)]
-    dist.all_gather(bufs, mine, group=group)
-    return [unpack(b, aff) for b in bufs]
+    out = torch.empty(world * mine.numel(), dtype=mine.dtype, device=mine.device)
+    dist.all_gather_into_tensor(out, mine, group=group)
+    return out.view(world, mine.numel())
+
+
+def exchange(aff: dict, group=None) -> list:
+    """Every rank's summary, as a list of dicts (rank order)."""
+    flat = _gather_flat(aff, group)
+    return [unpack(flat[g], aff) for g in range(flat.shape[0])]
+
+
+def fold_device(flat: torch.Tensor, upto: int, like: dict) -> dict:
+    """fold() of the gathered (world, n) summaries in one kernel (m3b_seqpar_fold)."""
+    from . import _lib
+
+    Bt, H, P, N = like["S"].shape
+    dev = flat.device
+    st = {"h": torch.empty(Bt, H, P, N, dtype=torch.float32, device=dev),
+          "angle": torch.empty(Bt, H, N // 2, dtype=torch.float32, device=dev),
+          "prev_BX": torch.empty(Bt, H, P, N, dtype=torch.float32, device=dev)}
+    _lib.seqpar_fold(flat, upto, Bt, H, P, N, st["h"], st["angle"], st["prev_BX"])
+    return st
 
 
 def layer_state_only(layer, proj: torch.Tensor, rms=None) -> dict:
@@ -165,8 +187,9 @@ def prefill_sharded(layer, x_shard: torch.Tensor, group=None, return_state: bool
 
     rank = dist.get_rank(group)
     proj, rms = layer._project(x_shard)
-    affs = exchange(layer_summary(layer, proj, rms), group)
-    st = fold(affs, rank) if rank > 0 else None
+    aff = layer_summary(layer, proj, rms)
+    flat = _gather_flat(aff, group)
+    st = fold_device(flat, rank, aff) if rank > 0 else None
     y, st_out = layer.ssd_from_proj(proj, return_state=True, state=st, rms=rms)
     out = layer.out_proj(y)
     return (out, st_out) if return_state else out

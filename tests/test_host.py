@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(h, n), n
     assert set(names) == set(_lib.SIGNATURES), "ctypes binding must cover exactly the header"
     L = _lib.lib()
-    assert L.m3b_abi_version() == 7
+    assert L.m3b_abi_version() == 8
     assert L.m3b_strerror(0) == b"ok"
 
 

@@ -61,6 +61,27 @@ def test_fold_reaches_the_prefix_state(variant):
             assert max_rel(st[k].numpy(), ref[k]) < 1e-6, (g, k)  # Lam, c0 are formed in fp32
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_fold_kernel_matches_fold(world):
+    """m3b_seqpar_fold over a gathered (world, n) buffer against fold() in float64 on the CPU
+    (fold itself is pinned to the oracle's prefix states above), for every rank's upto."""
+    from mamba3_b200 import seqpar
+
+    g = torch.Generator().manual_seed(world)
+    B, H, P, N = 2, 5, 16, 32
+    affs = [{"S": torch.randn(B, H, P, N, generator=g), "PB": torch.randn(B, H, P, N, generator=g),
+             "Om": 3 * torch.randn(B, H, N // 2, generator=g), "Lam": -torch.rand(B, H, generator=g) * 4,
+             "c0": torch.rand(B, H, generator=g)} for _ in range(world)]
+    flat = torch.stack([seqpar.pack(a) for a in affs]).cuda()
+    for upto in range(world + 1):
+        st = seqpar.fold_device(flat, upto, {k: v.cuda() for k, v in affs[0].items()})
+        ref = seqpar.fold([{k: v.double() for k, v in a.items()} for a in affs], upto)
+        for k in ("h", "angle", "prev_BX"):
+            err = float((st[k].cpu().double() - ref[k]).abs().max() / max(float(ref[k].abs().max()), 1e-30))
+            assert err < 1e-5 if upto > 0 else float(st[k].abs().max()) == 0.0, (upto, k, err)
+
+
 def test_rotate_pairs_composes_angles():
     from mamba3_b200 import seqpar
 
