@@ -381,6 +381,13 @@ M3B_API int m3b_seqpar_fold(const m3b_seqpar_fold_args* a, void* stream);
  * ------------------------------------------------------------------------ */
 M3B_API int m3b_rmsnorm(const void* x, const void* weight, void* y, int64_t rows, int32_t d, float eps,
                         int32_t dtype, void* stream);
+/* The residual step that precedes each norm of the blocks (mamba3/block.py:79-107: x + h * scale
+ * feeding the next RMSNorm), in one pass: x_out = x + h * scale rounded as m3b_scaled_add stores
+ * it, and y = RMSNorm(x_out) with `weight`, bit for bit what m3b_scaled_add then m3b_rmsnorm give.
+ * 16-bit dtypes (M3B_BF16, M3B_F16), d % 8 == 0 and d <= 2048, 16-byte aligned rows; x_out may
+ * alias x. */
+M3B_API int m3b_add_rmsnorm(const void* x, const void* h, float scale, const void* weight, void* x_out, void* y,
+                            int64_t rows, int32_t d, float eps, int32_t dtype, void* stream);
 
 /* ------------------------------------------------------------------------
  * Gate and MIMO down-projection of the layer (mamba3/mamba3.py:234-238) for the training path,
@@ -510,6 +517,10 @@ M3B_API int m3b_xprep_bwd(const m3b_xprep_args* a, void* workspace, size_t works
  *   m3b_scaled_add: out = x + h * scale (the residuals of mamba3/block.py:79-107)
  * ------------------------------------------------------------------------ */
 M3B_API int m3b_swiglu_act(const void* g, const void* u, void* out, int64_t n, int32_t dtype, void* stream);
+/* m3b_swiglu_rows: the same activation when the gate and up projections come from one GEMM with
+ * the two weights stacked: gu (rows, 2f) = [g | u] per row, out (rows, f); f % 8 == 0, 16-byte
+ * aligned rows. */
+M3B_API int m3b_swiglu_rows(const void* gu, void* out, int64_t rows, int32_t f, int32_t dtype, void* stream);
 M3B_API int m3b_scaled_add(const void* x, const void* h, float scale, void* out, int64_t n, int32_t dtype,
                            void* stream);
 

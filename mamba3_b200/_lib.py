@@ -174,6 +174,9 @@ SIGNATURES = {
                               C.c_void_p]),
     "m3b_swiglu_act": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
     "m3b_scaled_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
+    "m3b_swiglu_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_void_p]),
+    "m3b_add_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
+                                  C.c_int32, C.c_float, C.c_int32, C.c_void_p]),
     "m3b_selftest_umma": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "m3b_selftest_wait": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int64, C.c_void_p, C.c_void_p]),
 }
@@ -628,6 +631,35 @@ def scaled_add(x, h, scale, out=None):
         _check(lib().m3b_scaled_add(_ptr(x), _ptr(h), float(scale), _ptr(out), x.numel(), dtype_code(x.dtype),
                                     _stream(dev)), "m3b_scaled_add")
     return out
+
+
+def swiglu_rows(gu, out=None):
+    """silu(g) * u for gu (..., 2f) = [g | u] per row (one GEMM of the stacked gate / up weights)."""
+    dev = _cuda(gu, out)
+    if not gu.is_contiguous() or gu.shape[-1] % 2:
+        raise M3bError("swiglu_rows: contiguous [g | u] rows expected")
+    f = gu.shape[-1] // 2
+    out = torch.empty(*gu.shape[:-1], f, dtype=gu.dtype, device=gu.device) if out is None else out
+    with torch.cuda.device(dev):
+        _check(lib().m3b_swiglu_rows(_ptr(gu), _ptr(out), gu.numel() // (2 * f), f, dtype_code(gu.dtype),
+                                     _stream(dev)), "m3b_swiglu_rows")
+    return out
+
+
+def add_rmsnorm(x, h, scale, weight, eps, x_out=None, y=None):
+    """x_out = x + h * scale (rounded as scaled_add stores it) and y = RMSNorm(x_out), one pass."""
+    dev = _cuda(x, h, weight, x_out, y)
+    _same(x, h)
+    d = x.shape[-1]
+    if weight.numel() != d or weight.dtype != x.dtype:
+        raise M3bError("add_rmsnorm: a weight of x's dtype with x.shape[-1] entries expected")
+    x_out = torch.empty_like(x) if x_out is None else x_out
+    y = torch.empty_like(x) if y is None else y
+    with torch.cuda.device(dev):
+        _check(lib().m3b_add_rmsnorm(_ptr(x), _ptr(h), float(scale), _ptr(weight.contiguous()), _ptr(x_out), _ptr(y),
+                                     x.numel() // d, d, float(eps), dtype_code(x.dtype), _stream(dev)),
+               "m3b_add_rmsnorm")
+    return x_out, y
 
 
 def selftest_umma(A, B, mode):

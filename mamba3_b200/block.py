@@ -35,7 +35,24 @@ class SwiGLU(nn.Module):
         self.w_up = nn.Linear(d_model, d_ff, bias=bias)
         self.w_down = nn.Linear(d_ff, d_model, bias=bias)
 
+    def _stacked(self):
+        """[w_gate; w_up] (and biases) as one weight, rebuilt whenever either changes."""
+        wg, wu = self.w_gate.weight, self.w_up.weight
+        key = (wg.data_ptr(), wg._version, wu.data_ptr(), wu._version, wg.dtype, wg.device)
+        if getattr(self, "_gu_key", None) != key:
+            self._gu_w = torch.cat([wg.detach(), wu.detach()], 0)
+            self._gu_b = (torch.cat([self.w_gate.bias.detach(), self.w_up.bias.detach()], 0)
+                          if self.w_gate.bias is not None else None)
+            self._gu_key = key
+        return self._gu_w, self._gu_b
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        d_ff = self.w_gate.out_features
+        if (ops.kernel_ok(x) and d_ff % 8 == 0
+                and not (torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()))):
+            # inference: the gate and up projections as one GEMM over the stacked weights
+            w, b = self._stacked()
+            return self.w_down(ops.swiglu_rows(F.linear(x, w, b)))
         g, u = self.w_gate(x), self.w_up(x)
         a = ops.swiglu_act(g, u) if ops.kernel_ok(g, u) else F.silu(g) * u
         return self.w_down(a)

@@ -538,6 +538,15 @@ __device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
+// Programmatic dependent launch: the primary grid lets the next grid on the stream (launched
+// with cudaLaunchAttributeProgrammaticStreamSerialization) start early; that grid waits, before
+// it reads anything the primary writes, until the primary has completed and its memory is
+// visible.  Both are no-ops for grids launched without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Barrier among `n` threads (multiple of 32) of the CTA on hardware barrier `id` (1..15).
 __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

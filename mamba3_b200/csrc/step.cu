@@ -398,6 +398,9 @@ __global__ void __launch_bounds__(256) step_prep_kernel(m3b_step_args a, float* 
   const m3b_layer_params& prm = a.prm;
   const int H = prm.H, P = prm.P, G = prm.G, pd = prm.param_dtype;
   const int lane = threadIdx.x & 31;
+  // the streaming kernel may start now: it loads the state (which this kernel does not touch)
+  // and waits for this grid's completion before it reads the operand blocks
+  pdl_launch_dependents();
   const int item = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (item >= nitems) return;
   const int b = item / H, h = item - b * H, hpg = H / G, g = h / hpg;
@@ -589,31 +592,42 @@ __global__ void __launch_bounds__(kStepThreads, COMPACT ? 3 : 1)
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
   };
-  // bulk copies of item `it` into slot `sl` (thread 0): state, operand block, previous token
-  auto issue = [&](int it, int sl) {
+  // bulk copies of item `it` into slot `sl` (thread 0): state, operand block, previous token.
+  // parts: 1 = the state and previous token (with the slot's expected byte count), 2 = the
+  // operand block and the group's B / C rows, 3 = both.
+  auto issue = [&](int it, int sl, int parts) {
     uint8_t* d = ssm + sl * SP::slot;
     uint64_t* bar = &bars[sl];
     const int64_t sbase = (int64_t)it * P * N;
-    mbar_arrive_expect_tx(bar, (COMPACT ? sbytes + pbytes + xbytes : 2 * sbytes) + (uint32_t)OB::bytes + bcbytes);
-    bulk(d, a.h + sbase, sbytes, bar);
-    const int ib = it / H, ig = (it - ib * H) / hpg;
-    bulk(d + SP::bc, wbc + ((int64_t)ib * prm.G + ig) * OB::bc_floats, bcbytes, bar);
-    if constexpr (COMPACT) {
-      bulk(d + SP::pb, a.prev_b + (int64_t)it * N * R, pbytes, bar);
-      bulk(d + SP::px, a.prev_x + (int64_t)it * P * R, xbytes, bar);
-    } else {
-      bulk(d + SP::st, a.prev_bx + sbase, sbytes, bar);
+    if (parts & 1) {
+      mbar_arrive_expect_tx(bar, (COMPACT ? sbytes + pbytes + xbytes : 2 * sbytes) + (uint32_t)OB::bytes + bcbytes);
+      bulk(d, a.h + sbase, sbytes, bar);
+      if constexpr (COMPACT) {
+        bulk(d + SP::pb, a.prev_b + (int64_t)it * N * R, pbytes, bar);
+        bulk(d + SP::px, a.prev_x + (int64_t)it * P * R, xbytes, bar);
+      } else {
+        bulk(d + SP::st, a.prev_bx + sbase, sbytes, bar);
+      }
     }
-    bulk(d + SP::ob, ws + (int64_t)it * OB::floats, (uint32_t)OB::bytes, bar);
+    if (parts & 2) {
+      const int ib = it / H, ig = (it - ib * H) / hpg;
+      bulk(d + SP::bc, wbc + ((int64_t)ib * prm.G + ig) * OB::bc_floats, bcbytes, bar);
+      bulk(d + SP::ob, ws + (int64_t)it * OB::floats, (uint32_t)OB::bytes, bar);
+    }
   };
   const int stride = (int)gridDim.x;
-  if (tid == 0 && (int)blockIdx.x < nitems) issue((int)blockIdx.x, 0);
+  // The first item's state and previous-token copies do not depend on the preparation kernel
+  // before this one (programmatic dependent launch): they start before the wait for it; the
+  // operand block and B / C rows it writes are copied after.
+  if (tid == 0 && (int)blockIdx.x < nitems) issue((int)blockIdx.x, 0, 1);
+  pdl_wait_primary();
+  if (tid == 0 && (int)blockIdx.x < nitems) issue((int)blockIdx.x, 0, 2);
   int k = 0;
   for (int item = (int)blockIdx.x; item < nitems; item += stride, ++k) {
     const int sl = k & 1;
     const bool pending = item + stride < nitems;
     // the next item streams into the other slot (released by the barrier ending the last item)
-    if (tid == 0 && pending) issue(item + stride, sl ^ 1);
+    if (tid == 0 && pending) issue(item + stride, sl ^ 1, 3);
     bool ok = mbar_wait(&bars[sl], (k >> 1) & 1, wait_ns);
     ok = __syncthreads_and(ok);
     if (!ok) {
@@ -823,7 +837,20 @@ static int launch_stream_t(const m3b_step_args* a, float* ws, cudaStream_t st) {
   if (rc != M3B_OK) return rc;
   const int cap = num_sms() * occ;
   const int grid = nitems < cap ? nitems : cap;
-  step_stream_kernel<TA, R, COMPACT><<<grid, kStepThreads, SP::bytes, st>>>(*a, ws, nitems, kWaitLimitNs);
+  // programmatic dependent launch: the streaming kernel starts while the preparation finishes
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = SP::bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const uint64_t lim = kWaitLimitNs;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, step_stream_kernel<TA, R, COMPACT>, *a, (const float*)ws, nitems, lim);
+  if (e != cudaSuccess) return fail(M3B_ERR_CUDA, "step (stream): %s", cudaGetErrorString(e));
   return check_launch("step (stream)");
 }
 

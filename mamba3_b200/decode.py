@@ -51,9 +51,20 @@ class GraphDecoder:
         d = ssm._dims()
         return (d["H"], d["P"], d["N"], d["R"], d["G"], d["trapezoidal"], d["complex_ssm"], d["norm_eps"])
 
-    def _layer_step(self, i, blk, x):
+    def _add_norm(self, x, h, scale, norm):
+        """(x + h * scale, norm of it): one kernel for 16-bit activations, else the two the eager
+        path runs (both store the same values)."""
+        if x.dtype in (torch.bfloat16, torch.float16) and x.shape[-1] % 8 == 0:
+            return ops.add_rmsnorm(x, h, scale, norm.weight, norm.eps)
+        x = _residual(x, h, scale)
+        return x, norm(x)
+
+    def _layer_step(self, i, blk, x, n):
+        """Block i on the residual stream x with n = its ssm_norm(x); returns the stream after the
+        block and the next norm (the next block's ssm_norm, or the LM's final norm) of it, each
+        residual add fused with the norm that follows it."""
         ssm = blk.ssm
-        proj = ssm.in_proj(blk.ssm_norm(x))
+        proj = ssm.in_proj(n)
         st = self.states[i]
         # one step workspace for every layer (the layers run one after another on one stream);
         # allocated by the first, uncaptured step
@@ -64,7 +75,11 @@ class GraphDecoder:
             self.step_ws = ops.step_ssm_(ssm._param_tensors(), self.dims[i], proj, st["h"], st["prev_BX"],
                                          st["angle"], self.ybuf[i], workspace=self.step_ws)
         h = ssm.out_proj(self.ybuf[i])
-        return blk._mlp_residual(_residual(x, h, blk.residual_scale))
+        nxt = self.layers[i + 1].ssm_norm if i + 1 < len(self.layers) else self.lm.norm
+        if blk.use_mlp:
+            x, n1 = self._add_norm(x, h, blk.residual_scale, blk.mlp_norm)
+            return self._add_norm(x, blk.mlp(n1), blk.residual_scale, nxt)
+        return self._add_norm(x, h, blk.residual_scale, nxt)
 
     def _sample(self, logits):
         from .block import _sample
@@ -75,9 +90,10 @@ class GraphDecoder:
     def _decode_body(self):
         """One token: self.tok -> layers -> next token in self.tok and in self.out[:, pos]."""
         x = self.lm.embedding(self.tok.squeeze(1))
+        n = self.layers[0].ssm_norm(x)
         for i, blk in enumerate(self.layers):
-            x = self._layer_step(i, blk, x)
-        logits = self.lm.lm_head(self.lm.norm(x))
+            x, n = self._layer_step(i, blk, x, n)
+        logits = self.lm.lm_head(n)
         nxt = self._sample(logits)
         self.tok.copy_(nxt)
         self.out.scatter_(1, self.pos.view(1, 1).expand(self.B, 1), nxt)

@@ -220,6 +220,27 @@ def _(g, u):
     return torch.empty_like(g)
 
 
+@torch.library.custom_op("mamba3_b200::swiglu_rows", mutates_args=())
+def swiglu_rows(gu: torch.Tensor) -> torch.Tensor:
+    return _lib.swiglu_rows(gu.contiguous())
+
+
+@swiglu_rows.register_fake
+def _(gu):
+    return gu.new_empty(*gu.shape[:-1], gu.shape[-1] // 2)
+
+
+@torch.library.custom_op("mamba3_b200::add_rmsnorm", mutates_args=())
+def add_rmsnorm(x: torch.Tensor, h: torch.Tensor, scale: float, weight: torch.Tensor,
+                eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    return _lib.add_rmsnorm(x.contiguous(), h.contiguous(), scale, weight.to(x.dtype), eps)
+
+
+@add_rmsnorm.register_fake
+def _(x, h, scale, weight, eps):
+    return torch.empty_like(x), torch.empty_like(x)
+
+
 @torch.library.custom_op("mamba3_b200::scaled_add", mutates_args=())
 def scaled_add(x: torch.Tensor, h: torch.Tensor, scale: float) -> torch.Tensor:
     return _lib.scaled_add(x.contiguous(), h.contiguous(), scale)

@@ -311,6 +311,28 @@ def test_swiglu_and_residual_kernels_match_torch(dtype, n):
         assert (res == ref2).float().mean().item() > 0.99
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows,d,f", [(256, 768, 2112), (3, 128, 384), (0, 768, 2112)])
+def test_fused_block_steps_equal_unfused(dtype, rows, d, f):
+    """The decoder's fused block steps give bit for bit what the separate kernels store:
+    m3b_add_rmsnorm == m3b_scaled_add then m3b_rmsnorm (both outputs), and m3b_swiglu_rows on one
+    [g | u] GEMM output == m3b_swiglu_act on its two halves."""
+    from mamba3_b200 import _lib
+
+    g = torch.Generator().manual_seed(rows + d)
+    x = torch.randn(rows, d, generator=g).to("cuda", dtype)
+    h = (torch.randn(rows, d, generator=g) * 4).to("cuda", dtype)
+    w = (1 + 0.1 * torch.randn(d, generator=g)).to("cuda", dtype)
+    x1, y1 = _lib.add_rmsnorm(x, h, 0.1443, w, 1e-5)
+    x2 = _lib.scaled_add(x, h, 0.1443)
+    y2 = _lib.rmsnorm(x2, w, 1e-5)
+    assert torch.equal(x1, x2) and torch.equal(y1, y2)
+    gu = (torch.randn(rows, 2 * f, generator=g) * 3).to("cuda", dtype)
+    a1 = _lib.swiglu_rows(gu)
+    a2 = _lib.swiglu_act(gu[:, :f].contiguous(), gu[:, f:].contiguous())
+    assert a1.shape == (rows, f) and torch.equal(a1, a2)
+
+
 @pytest.mark.parametrize("R,rows,dtype", [(1, 300, torch.float32), (2, 1000, torch.float32), (3, 129, torch.float32),
                                           (4, 257, torch.float32), (2, 1000, torch.bfloat16), (2, 0, torch.float32)])
 def test_gate_kernels_match_torch_autograd(R, rows, dtype):
