@@ -343,6 +343,10 @@ typedef struct m3b_ssd_bwd_args {
   float* dA;                 /* (H) */
   float* dD;                 /* (H) */
   float* dh_init;            /* (batch,H,P,N) or NULL */
+  /* 0: chunk-level products on tensor cores where they apply (bf16, N <= 128 and P <= 64 both
+   * multiples of 8, mimo_rank 1, 2 or 4, 16-byte aligned per-token tensors), else the token
+   * sweeps; 1: always the token sweeps (fp32 CUDA cores).  No counterpart in the reference. */
+  int32_t algo;
 } m3b_ssd_bwd_args;
 M3B_API size_t m3b_chunked_ssd_bwd_workspace(const m3b_ssd_bwd_args* a);
 M3B_API int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream);

@@ -98,7 +98,7 @@ class SsdBwdArgs(C.Structure):
                 ("ad_dtype", C.c_int32), ("h_init", C.c_void_p), ("dy", C.c_void_p), ("dh_final", C.c_void_p),
                 ("dx_g", C.c_void_p), ("dx_b", C.c_void_p), ("dB_g", C.c_void_p), ("dB_b", C.c_void_p),
                 ("dC", C.c_void_p), ("dx_raw", C.c_void_p), ("ddt", C.c_void_p), ("dA", C.c_void_p),
-                ("dD", C.c_void_p), ("dh_init", C.c_void_p)]
+                ("dD", C.c_void_p), ("dh_init", C.c_void_p), ("algo", C.c_int32)]
 
 
 class GateArgs(C.Structure):
@@ -394,11 +394,12 @@ def chunked_ssd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, y, h_init=None, h_final
     _after_launch(dev)
 
 
-def chunked_ssd_bwd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init=None, dh_final=None):
+def chunked_ssd_bwd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init=None, dh_final=None, algo=0):
     """Launch the chunked SSD backward.  Activations, dy contiguous and of one dtype (fp32 / bf16);
     dt fp32 / bf16 / fp16; A, D of one dtype; h_init, dh_final fp32 or None.  Returns a dict of
     gradients (x_g, x_b, B_g, B_b, C, x_raw in the activation dtype, dt in dt's dtype, A, D, h_init
-    fp32; None for absent inputs)."""
+    fp32; None for absent inputs).  algo 0: chunk-level products on tensor cores where they apply,
+    1: the token sweeps."""
     dev = _cuda(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init, dh_final)
     Bt, T, H, P, R = x_g.shape
     N = B_g.shape[3]
@@ -409,7 +410,8 @@ def chunked_ssd_bwd(x_g, x_b, B_g, B_b, Cm, dt, A, D, x_raw, dy, h_init=None, dh
     a = SsdBwdArgs(Bt, T, H, P, N, R, dtype_code(x_g.dtype), _ptr(x_g), _ptr(x_b), _ptr(B_g), _ptr(B_b), _ptr(Cm),
                    _ptr(x_raw), _ptr(dt), dtype_code(dt.dtype), _ptr(A), _ptr(D), dtype_code(A.dtype), _ptr(h_init),
                    _ptr(dy), _ptr(dh_final), _ptr(g["x_g"]), _ptr(g["x_b"]), _ptr(g["B_g"]), _ptr(g["B_b"]),
-                   _ptr(g["C"]), _ptr(g["x_raw"]), _ptr(g["dt"]), _ptr(g["A"]), _ptr(g["D"]), _ptr(g["h_init"]))
+                   _ptr(g["C"]), _ptr(g["x_raw"]), _ptr(g["dt"]), _ptr(g["A"]), _ptr(g["D"]), _ptr(g["h_init"]),
+                   int(algo))
     L = lib()
     need = L.m3b_chunked_ssd_bwd_workspace(C.byref(a))
     if need == 0:

@@ -52,4 +52,11 @@ size_t layer_fwd_workspace(const m3b_layer_fwd_args* a);
 // The least workspace layer_fwd accepts (it then runs whole sequences per CTA).
 size_t layer_fwd_workspace_min(const m3b_layer_fwd_args* a);
 
+// chunked_ssd backward on tensor cores (ssd_general.cu): applicable shapes, extra workspace, and
+// the run that writes every gradient but ddt / dA / dD plus the per-token partials fw / ew
+// ((batch H, T, 8) floats), m_T = <dh_final, h_final> and sum dy . x_raw per (batch, head).
+bool bwd_tc_ok(const m3b_ssd_bwd_args* a);
+size_t bwd_tc_workspace(const m3b_ssd_bwd_args* a);
+int bwd_tc_run(const m3b_ssd_bwd_args* a, void* ws, float* fw, float* ew, float* mT, float* dDf, cudaStream_t st);
+
 }  // namespace m3b

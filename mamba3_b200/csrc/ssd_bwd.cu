@@ -815,7 +815,8 @@ size_t bwd_smem(const m3b_ssd_bwd_args* a) {
 
 extern "C" size_t m3b_chunked_ssd_bwd_workspace(const m3b_ssd_bwd_args* a) {
   if (!a || m3b::bvalidate(a) != M3B_OK) return 0;
-  return m3b::bwd_layout(a).total;
+  const size_t base = m3b::bwd_layout(a).total;
+  return a->algo == 0 && m3b::bwd_tc_ok(a) ? base + m3b::bwd_tc_workspace(a) : base;
 }
 
 extern "C" int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* ws, size_t ws_bytes, void* stream) {
@@ -833,8 +834,10 @@ extern "C" int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* ws, size_t w
     return M3B_OK;
   }
   const BwdLayout w = bwd_layout(a);
-  if (!ws || ws_bytes < w.total)
-    return fail(M3B_ERR_WORKSPACE, "chunked_ssd_bwd: need %zu workspace bytes", w.total);
+  const bool tc = a->algo == 0 && bwd_tc_ok(a);
+  const size_t need = tc ? w.total + bwd_tc_workspace(a) : w.total;
+  if (!ws || ws_bytes < need) return fail(M3B_ERR_WORKSPACE, "chunked_ssd_bwd: need %zu workspace bytes", need);
+  if (a->algo != 0 && a->algo != 1) return fail(M3B_ERR_INVALID_ARG, "chunked_ssd_bwd: algo %d", a->algo);
   const bool tiled = a->P <= 64 && a->N <= 128 && (a->R == 1 || a->R == 2 || a->R == 4);
   const size_t smem = tiled ? 0 : bwd_smem(a);
   if (smem > 227 * 1024) return fail(M3B_ERR_UNSUPPORTED, "chunked_ssd_bwd: state too large for shared memory");
@@ -877,7 +880,12 @@ extern "C" int m3b_chunked_ssd_bwd(const m3b_ssd_bwd_args* a, void* ws, size_t w
   p.dDf_bh = reinterpret_cast<float*>(base + w.dDf);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned grid = (unsigned)(a->batch * a->H);
-  if (tiled) {
+  if (tc) {
+    // chunk-level products on tensor cores, then the same suffix pass on their per-token partials
+    if ((rc = bwd_tc_run(a, base + w.total, p.fw, p.ew, p.mT_bh, p.dDf_bh, st)) != M3B_OK) return rc;
+    ssd_bwd_finish_kernel<<<grid, kBwdThreads, 0, st>>>(p);
+    if ((rc = check_launch("chunked_ssd_bwd_finish")) != M3B_OK) return rc;
+  } else if (tiled) {
     const bool f32 = a->dtype == M3B_F32, beta = a->x_b != nullptr;
     switch (a->R * 2 + (beta ? 1 : 0)) {
       case 2: rc = f32 ? launch_tiled<float, 1, 1>(p, grid, st) : launch_tiled<__nv_bfloat16, 1, 1>(p, grid, st); break;

@@ -190,3 +190,36 @@ def test_chunked_ssd_backward_large_state_vs_oracle(P, N, R, beta):
             assert got[k] is None, k
         else:
             assert max_rel(to_np(got[k]), v) < 1e-4, k
+
+
+@pytest.mark.parametrize("R,beta,T", [(2, True, 1000), (1, False, 200), (4, True, 161), (2, False, 64)])
+def test_chunked_ssd_backward_tensor_cores_vs_token_sweeps(R, beta, T):
+    """The tensor-core backward (chunk-level products, algo 0) against the token-sweep kernel
+    (algo 1, fp32 CUDA cores, pinned to the oracle above) on the same bf16 inputs: every gradient
+    within the bf16 tolerance, and bitwise identical on a second launch (no atomics)."""
+    from mamba3_b200 import _lib
+
+    B, H, P, N = 2, 3, 64, 128
+    g = torch.Generator().manual_seed(7 * R + T)
+    r = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    x_g, x_b, x_raw, dy = r(B, T, H, P, R), r(B, T, H, P, R), r(B, T, H, P, R), r(B, T, H, P, R)
+    B_g, B_b, C = r(B, T, H, N, R) * 0.3, r(B, T, H, N, R) * 0.3, r(B, T, H, N, R) * 0.3
+    dt = torch.rand(B, T, H, generator=g) * 0.1 + 0.01
+    A = -torch.exp(r(H).clamp(-4, 0))
+    D = r(H)
+    h_init, dhf = r(B, H, P, N), r(B, H, P, N)
+    if not beta:
+        x_b = B_b = None
+    bf = lambda t: None if t is None else t.to(torch.bfloat16).cuda().contiguous()  # noqa: E731
+    cu = lambda t: None if t is None else t.cuda().contiguous()  # noqa: E731
+    args = [bf(x_g), bf(x_b), bf(B_g), bf(B_b), bf(C), cu(dt), cu(A), cu(D), bf(x_raw), bf(dy), cu(h_init), cu(dhf)]
+    tc = _lib.chunked_ssd_bwd(*args, algo=0)
+    again = _lib.chunked_ssd_bwd(*args, algo=0)
+    sweep = _lib.chunked_ssd_bwd(*args, algo=1)
+    for k in tc:
+        if tc[k] is None:
+            assert sweep[k] is None, k
+            continue
+        assert torch.equal(tc[k], again[k]), k
+        err = max_rel(to_np(tc[k]), to_np(sweep[k]))
+        assert err < 2e-2, (k, err)
