@@ -424,6 +424,10 @@ struct BwdTcParams {
   float* dDk;  // (B, K, H) per-chunk sums of dy . x_raw
 };
 
+// Gradient rows staged in shared memory: token s's W x R entries (the layout of the global
+// tensor) at row pitch W R + 8 elements (16-byte aligned rows, staggered banks).
+__host__ __device__ constexpr int bwd_pitch(int W, int R) { return W * R + 8; }
+
 template <int RP>
 struct BPlan {
   static constexpr int L = 128 / RP;
@@ -440,6 +444,9 @@ struct BPlan {
   static constexpr int taddr = bars + 32;
   static constexpr int bytes = taddr + 16 + 1024;
   static_assert(bytes <= 227 * 1024, "shared memory");
+  // staged gradient rows (bf16): dBt then dXt rows in the score-tile space, dC rows in tB / tX
+  static_assert(L * (bwd_pitch(kNS, RP) + bwd_pitch(kPP, RP)) * 2 <= 65536, "dBt / dXt staging");
+  static_assert(L * bwd_pitch(kNS, RP) * 2 <= tMg - tB, "dC staging");
 };
 
 // Tile rows (s RP + q) x columns w < Wpad of src (B, T, H, W, R) for the L tokens of chunk k
@@ -498,6 +505,22 @@ __device__ void bwd_state_tiles(uint8_t* hi, uint8_t* lo, const float* st, int P
     }
     sw128_store_chunk(hi, pp, c, kPP, make_uint4(wh[0], wh[1], wh[2], wh[3]));
     sw128_store_chunk(lo, pp, c, kPP, make_uint4(wl[0], wl[1], wl[2], wl[3]));
+  }
+}
+
+
+// Copies the staged rows of the chunk's live tokens to dst (B, T, H, W, R) with 16-byte vectors.
+template <typename TA>
+__device__ void bwd_copy_out(void* dst, const uint8_t* stage, const SsdParams& a, int W, int R, int L, int b, int k,
+                             int h) {
+  const int WR = W * R, nv = WR / 8, pitch = bwd_pitch(W, R);
+  for (int u = threadIdx.x; u < L * nv; u += kCT) {
+    const int s = u / nv, c = u % nv;
+    const int64_t tok = (int64_t)k * L + s;
+    if (tok >= a.T) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + ((int64_t)s * pitch + 8 * c) * sizeof(TA));
+    *reinterpret_cast<uint4*>(reinterpret_cast<TA*>(dst) + (((int64_t)b * a.T + tok) * a.H + h) * (int64_t)WR +
+                              8 * c) = v;
   }
 }
 
@@ -726,7 +749,9 @@ __global__ void __launch_bounds__(kCT, 1) bwd_out_kernel(BwdTcParams p) {
         float v1[32], v2[32];
         tmem_ld32(trow + 256 + 32 * ch, v1);
         tmem_ld32(trow + 320 + 32 * ch, v2);
-        TA* dst = reinterpret_cast<TA*>(half ? p.dx_b : p.dx_g) + (((int64_t)b * a.T + tok) * a.H + h) * (int64_t)a.P * R + qr;
+        // staged (s, p, j) rows: after the dBt rows in the free score-tile space
+        TA* dst = reinterpret_cast<TA*>(sm + PL::tMg + L * bwd_pitch(kNS, R) * (int)sizeof(TA)) +
+                  tr * bwd_pitch(a.P, R) + qr;
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
           const int p0 = 32 * ch + 8 * c8;
@@ -738,9 +763,8 @@ __global__ void __launch_bounds__(kCT, 1) bwd_out_kernel(BwdTcParams p) {
             const int i = 8 * c8 + 2 * e2;
             frs = fmaf(xv.x, v2[i], fmaf(xv.y, v2[i + 1], frs));
             if (live) {
-              if (p0 + 2 * e2 < a.P) io<TA>::st(dst + (int64_t)(p0 + 2 * e2) * R, dts * fmaf(ge, v2[i], v1[i]));
-              if (p0 + 2 * e2 + 1 < a.P)
-                io<TA>::st(dst + (int64_t)(p0 + 2 * e2 + 1) * R, dts * fmaf(ge, v2[i + 1], v1[i + 1]));
+              if (p0 + 2 * e2 < a.P) io<TA>::st(dst + (p0 + 2 * e2) * R, dts * fmaf(ge, v2[i], v1[i]));
+              if (p0 + 2 * e2 + 1 < a.P) io<TA>::st(dst + (p0 + 2 * e2 + 1) * R, dts * fmaf(ge, v2[i + 1], v1[i + 1]));
             }
           }
         }
@@ -749,7 +773,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_out_kernel(BwdTcParams p) {
       for (int o = 1; o < RP; o <<= 1) frs += __shfl_xor_sync(0xffffffffu, frs, o);
       if (qr == 0) fws[(2 + half * 2 + ch) * L + tr] = ge * frs;
       const float tail = ge * dts;
-      TA* dstB = reinterpret_cast<TA*>(half ? p.dB_b : p.dB_g) + (((int64_t)b * a.T + tok) * a.H + h) * (int64_t)a.N * R + qr;
+      TA* dstB = reinterpret_cast<TA*>(sm + PL::tMg) + tr * bwd_pitch(a.N, R) + qr;  // staged (s, n, j) rows
 #pragma unroll
       for (int c32 = 0; c32 < 2; ++c32) {
         const int n0 = 64 * ch + 32 * c32;
@@ -759,13 +783,19 @@ __global__ void __launch_bounds__(kCT, 1) bwd_out_kernel(BwdTcParams p) {
         if (live) {
 #pragma unroll
           for (int e = 0; e < 32; ++e)
-            if (n0 + e < a.N) io<TA>::st(dstB + (int64_t)(n0 + e) * R, fmaf(tail, v4[e], v3[e]));
+            if (n0 + e < a.N) io<TA>::st(dstB + (n0 + e) * R, fmaf(tail, v4[e], v3[e]));
         }
       }
     }
     tc_fence_before();
-    __syncthreads();  // TMEM columns 0-383 and the half's tiles are free again
+    __syncthreads();  // TMEM columns 0-383 and the half's tiles are free again; the rows are staged
     tc_fence_after();
+    if (ok) {
+      bwd_copy_out<TA>(half ? p.dB_b : p.dB_g, sm + PL::tMg, a, a.N, R, L, b, k, h);
+      bwd_copy_out<TA>(half ? p.dx_b : p.dx_g, sm + PL::tMg + L * bwd_pitch(kNS, R) * (int)sizeof(TA), a, a.P, R, L,
+                       b, k, h);
+    }
+    __syncthreads();  // the staging space is the next half's score tiles
   }
   // ---- dC = Wg Bt (both halves) + exp(cum_t) dy h_k, h_k split into the free score-tile space
   bwd_state_tiles(sm + PL::tH, sm + PL::tHlo,
@@ -788,7 +818,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_out_kernel(BwdTcParams p) {
     const bool live = tok < a.T && qr < R;
     const float ec = exp2f(cum2[tr]);
     float es = 0.f;  // <C_t, dy_t h_k> (inter-chunk part of e_t, before exp(cum_t))
-    TA* dst = reinterpret_cast<TA*>(p.dC) + (((int64_t)b * a.T + tok) * a.H + h) * (int64_t)a.N * R + qr;
+    TA* dst = reinterpret_cast<TA*>(sm + PL::tB) + tr * bwd_pitch(a.N, R) + qr;  // staged (t, n, q) rows
 #pragma unroll
     for (int c32 = 0; c32 < 2; ++c32) {
       const int n0 = 64 * ch + 32 * c32;
@@ -805,8 +835,8 @@ __global__ void __launch_bounds__(kCT, 1) bwd_out_kernel(BwdTcParams p) {
           const int i = 8 * c8 + 2 * e2;
           es = fmaf(cv.x, v6[i], fmaf(cv.y, v6[i + 1], es));
           if (live) {
-            if (n0 + i < a.N) io<TA>::st(dst + (int64_t)(n0 + i) * R, fmaf(ec, v6[i], v5[i]));
-            if (n0 + i + 1 < a.N) io<TA>::st(dst + (int64_t)(n0 + i + 1) * R, fmaf(ec, v6[i + 1], v5[i + 1]));
+            if (n0 + i < a.N) io<TA>::st(dst + (n0 + i) * R, fmaf(ec, v6[i], v5[i]));
+            if (n0 + i + 1 < a.N) io<TA>::st(dst + (n0 + i + 1) * R, fmaf(ec, v6[i + 1], v5[i + 1]));
           }
         }
       }
@@ -815,6 +845,8 @@ __global__ void __launch_bounds__(kCT, 1) bwd_out_kernel(BwdTcParams p) {
     for (int o = 1; o < RP; o <<= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
     if (qr == 0) ews[(4 + ch) * L + tr] = ec * es;
   }
+  __syncthreads();
+  if (ok) bwd_copy_out<TA>(p.dC, sm + PL::tB, a, a.N, R, L, b, k, h);
   // ---- dx_raw = D dy and this chunk's share of dD = sum dy . x_raw
   float dd = 0.f;
   {
