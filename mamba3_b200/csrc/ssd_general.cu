@@ -603,6 +603,28 @@ __global__ void __launch_bounds__(kCT, 1) bwd_out_kernel(BwdTcParams p) {
     fws[e] = 0.f;
     ews[e] = 0.f;
   }
+  // every token row this CTA reads (C, dy, both halves of Bt and Xt, x_raw) and the two states,
+  // requested into L2 up front: the tile loaders below then wait on L2, not on HBM
+  {
+    const int64_t PN = (int64_t)a.P * a.N;
+    const void* rows[7] = {a.C, p.dy, a.B_g, a.x_g, BETA ? a.B_b : nullptr, BETA ? a.x_b : nullptr, a.x_raw};
+    const int width[7] = {a.N, a.P, a.N, a.P, a.N, a.P, a.P};
+    for (int u = threadIdx.x; u < 7 * L; u += kCT) {
+      const int which = u / L, s = u % L;
+      const int64_t t = (int64_t)k * L + s;
+      if (rows[which] && t < a.T) {
+        const uint32_t bytes = (uint32_t)(width[which] * R * sizeof(TA));
+        prefetch_l2(reinterpret_cast<const TA*>(rows[which]) + (((int64_t)b * a.T + t) * a.H + h) * width[which] * R,
+                    bytes);
+      }
+    }
+    if (threadIdx.x < 2) {
+      const float* st = threadIdx.x == 0 ? reinterpret_cast<const float*>(p.gstate) +
+                                               (((int64_t)b * a.K + (a.K - 1 - k)) * a.H + h) * PN
+                                         : reinterpret_cast<const float*>(p.hstate) + (((int64_t)b * a.K + k) * a.H + h) * PN;
+      for (int64_t off = 0; off < PN; off += 4096) prefetch_l2(st + off, (uint32_t)((PN - off < 4096 ? PN - off : 4096) * 4));
+    }
+  }
   // operands shared by both halves: C, dy, Gx_k (split)
   bwd_rows<TA, R>(sm + PL::tC, a.C, a, a.N, kNS, b, k, h);
   bwd_rows<TA, R>(sm + PL::tDY, p.dy, a, a.P, kPP, b, k, h);
