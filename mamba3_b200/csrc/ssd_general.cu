@@ -174,6 +174,24 @@ __device__ void gen_x(const SsdParams& a, uint8_t* tile, const float* wgt, int b
   }
 }
 
+// Requests the chunk's token rows of up to four (B, T, H, W, R) tensors into L2 (one bulk
+// prefetch per token and tensor; null tensors are skipped), so that the tile loaders that follow
+// wait on L2 rather than on HBM.  W R elements of TA per row, 16-byte aligned rows.
+template <typename TA, int R>
+__device__ void prefetch_rows(const SsdParams& a, int b, int k, int h, int L, const void* t0, int w0, const void* t1,
+                              int w1, const void* t2, int w2, const void* t3, int w3) {
+  const void* src[4] = {t0, t1, t2, t3};
+  const int wid[4] = {w0, w1, w2, w3};
+  for (int u = threadIdx.x; u < 4 * L; u += kCT) {
+    const int which = u / L, s = u % L;
+    const int64_t t = (int64_t)k * L + s;
+    const uint32_t bytes = (uint32_t)(wid[which] * R * sizeof(TA));
+    // the bulk prefetch wants a 16-byte aligned address and size: other shapes go without it
+    if (src[which] && t < a.T && bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(src[which]) & 15) == 0)
+      prefetch_l2(reinterpret_cast<const TA*>(src[which]) + (((int64_t)b * a.T + t) * a.H + h) * wid[which] * R, bytes);
+  }
+}
+
 // REV (the backward's reverse chunk scan): the chunk's contribution to dL/dh at its start,
 // sum_t exp(cum_t) x_t^T B_t with x = dy, B = C (weights exp(cum_t), no dt), and the chunk's
 // decay, stored at chunk index K-1-k so that the forward scan kernel runs the reverse scan.
@@ -197,6 +215,8 @@ __global__ void __launch_bounds__(kCT, 1) gen_state_kernel(SsdParams a) {
     mbar_init(&bar[0], 1);
     fence_mbar_init();
   }
+  prefetch_rows<TA, R>(a, b, k, h, 128 / RP, a.B_g, a.N, BETA ? a.B_b : nullptr, a.N, a.x_g, a.P,
+                       BETA ? a.x_b : nullptr, a.P);
   gen_scalars<TA, R, BETA, true, SP>(a, sm, b, k, h);
   const float* cum2 = reinterpret_cast<const float*>(sm + PL::cum2);
   const float* dtv = reinterpret_cast<const float*>(sm + PL::dtv);
@@ -274,6 +294,8 @@ __global__ void __launch_bounds__(kCT, 1) gen_out_kernel(SsdParams a) {
     mbar_init(&bar[1], 1);
     fence_mbar_init();
   }
+  prefetch_rows<TA, R>(a, b, k, h, 128 / RP, a.C, a.N, a.B_g, a.N, BETA ? a.B_b : nullptr, a.N, a.x_g, a.P);
+  prefetch_rows<TA, R>(a, b, k, h, 128 / RP, BETA ? a.x_b : nullptr, a.P, a.x_raw, a.P, nullptr, 0, nullptr, 0);
   gen_scalars<TA, R, BETA>(a, sm, b, k, h);
   const float* cum2 = reinterpret_cast<const float*>(sm + PL::cum2);
   const float* dtv = reinterpret_cast<const float*>(sm + PL::dtv);
