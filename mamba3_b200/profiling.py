@@ -125,6 +125,8 @@ def kernel_workload(case: str, reps: int = 3) -> None:
              fused kernel at R = 4 (prep_kernel, ssd_fused_kernel per forward)
     chunked  chunked_ssd on pre-processed bf16 tensors (2, 4096) x 24 heads, P 64, N 128, R 2,
              trapezoid: gen_state_kernel, the scan, gen_out_kernel
+    chunked_bwd  its backward on the same tensors (tensor-core path): the chunk-state kernels, the
+             two scans, bwd_out_kernel, the sums and the suffix pass
     step     one layer's decode step at config-4 shapes (batch 256 x 24 heads, compact state):
              step_prep_kernel, step_stream_kernel
     fp32     config-0 layer forward (4, 1024, 768) fp32: prep, angle prefix, the tf32
@@ -157,6 +159,17 @@ def kernel_workload(case: str, reps: int = 3) -> None:
                     torch.rand(B, T, H, device="cuda", generator=g) * 0.1, -torch.rand(H, device="cuda", generator=g),
                     torch.randn(H, device="cuda", generator=g), r(B, T, H, P, R))
             run = lambda: chunked_ssd(*args, return_final_state=True)  # noqa: E731
+        elif case == "chunked_bwd":
+            from . import _lib
+
+            B, T, H, P, N, R = 2, 4096, 24, 64, 128, 2
+            r = lambda *sh: torch.randn(*sh, device="cuda", generator=g).to(torch.bfloat16)  # noqa: E731
+            f = lambda *sh: torch.randn(*sh, device="cuda", generator=g)  # noqa: E731
+            args = (r(B, T, H, P, R), r(B, T, H, P, R), r(B, T, H, N, R), r(B, T, H, N, R), r(B, T, H, N, R),
+                    torch.rand(B, T, H, device="cuda", generator=g) * 0.1, -torch.rand(H, device="cuda", generator=g),
+                    torch.randn(H, device="cuda", generator=g), r(B, T, H, P, R), r(B, T, H, P, R), f(B, H, P, N),
+                    f(B, H, P, N))
+            run = lambda: _lib.chunked_ssd_bwd(*args)  # noqa: E731
         elif case == "in_proj":
             m = KulaMamba(d_model=768, d_state=128, headdim=64, mimo_rank=2).cuda().to(torch.bfloat16).eval()
             x = torch.randn(16, 4096, 768, device="cuda", generator=g).to(torch.bfloat16)
@@ -200,7 +213,7 @@ if __name__ == "__main__":
     import argparse
 
     ap = argparse.ArgumentParser(description="profiling helpers")
-    ap.add_argument("what", choices=["train", "cfg3", "chunked", "step", "fp32", "in_proj", "decode"])
+    ap.add_argument("what", choices=["train", "cfg3", "chunked", "chunked_bwd", "step", "fp32", "in_proj", "decode"])
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seqlen", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=3)
