@@ -351,12 +351,16 @@ def run_scan(dev, world, rank, barrier):
     args = (r(Bb, T, Hh, P, R), r(Bb, T, Hh, P, R), r(Bb, T, Hh, N, R), r(Bb, T, Hh, N, R), r(Bb, T, Hh, N, R),
             torch.rand(Bb, T, Hh, device=dev, generator=g) * 0.1, -torch.rand(Hh, device=dev, generator=g) - 0.1,
             torch.randn(Hh, device=dev, generator=g), r(Bb, T, Hh, P, R), r(Bb, T, Hh, P, R))
-    ms_s = timed(lambda: _lib.chunked_ssd_bwd(*args), reps=3)
-    # fp32 multiply-adds per (token, head): h and G updates P N (RI + R), dC N R P, dX P RI N, dB N RI P
+    ms_s = timed(lambda: _lib.chunked_ssd_bwd(*args), reps=3)  # tensor-core path (algo 0)
+    ms_w = timed(lambda: _lib.chunked_ssd_bwd(*args, algo=1), reps=1)  # the token sweeps, for comparison
+    # token-recurrence multiply-adds per (token, head): h and G updates P N (RI + R), dC N R P,
+    # dX P RI N, dB N RI P -- a fixed count, so that both paths are measured on the same scale
     ri = 2 * R
     flops = 2.0 * P * N * (3 * ri + 2 * R) * Bb * T * Hh
     out["ssd_bwd"] = {"workload": f"chunked_ssd backward, bf16 ({Bb}, {T}) x {Hh} heads, P {P}, N {N}, R {R}",
-                      "ms": ms_s, "tokens_per_s": Bb * T / (ms_s / 1e3), "fp32_tflops": flops / (ms_s / 1e3) / 1e12}
+                      "ms": ms_s, "tokens_per_s": Bb * T / (ms_s / 1e3), "path": "tensor cores (chunk products)",
+                      "recurrence_tflops": flops / (ms_s / 1e3) / 1e12,
+                      "token_sweeps_ms": ms_w}
     return out
 
 

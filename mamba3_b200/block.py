@@ -170,11 +170,33 @@ class KulaMambaLM(nn.Module):
             if isinstance(m, KulaMamba):
                 m._init_weights(dt_min=0.001, dt_max=0.1)
 
+    def _forward_fused(self, x):
+        """Inference forward with the residual adds inside the stack fused into the norm that
+        follows each (ops.add_rmsnorm: the same stored values as the residual kernel then the norm
+        kernel); the final norm runs as its module, so hooks on it still see its output."""
+        n = self.layers[0].ssm_norm(x)
+        last = len(self.layers) - 1
+        for i, blk in enumerate(self.layers):
+            h = blk.ssm(n)
+            if blk.use_mlp:
+                x, n1 = ops.add_rmsnorm(x, h, blk.residual_scale, blk.mlp_norm.weight, blk.mlp_norm.eps)
+                h = blk.mlp(n1)
+            if i < last:
+                nxt = self.layers[i + 1].ssm_norm
+                x, n = ops.add_rmsnorm(x, h, blk.residual_scale, nxt.weight, nxt.eps)
+            else:
+                n = self.norm(_residual(x, h, blk.residual_scale))
+        return n
+
     def forward(self, input_ids, labels=None):
         x = self.embedding(input_ids)
-        for layer in self.layers:
-            x = layer(x)
-        logits = self.lm_head(self.norm(x))
+        if (ops.kernel_ok(x) and x.dtype in (torch.bfloat16, torch.float16) and x.shape[-1] % 8 == 0
+                and x.shape[-1] <= 2048 and not torch.is_grad_enabled()):
+            logits = self.lm_head(self._forward_fused(x))
+        else:
+            for layer in self.layers:
+                x = layer(x)
+            logits = self.lm_head(self.norm(x))
         result = {"logits": logits}
         if labels is not None:
             result["loss"] = F.cross_entropy(logits[:, :-1].reshape(-1, logits.size(-1)), labels[:, 1:].reshape(-1))
