@@ -580,7 +580,26 @@ def host_copy_gbs(dev, nbytes=1 << 28, reps=5):
         b.record()
         torch.cuda.synchronize()
         out[name] = nbytes * reps / (a.elapsed_time(b) / 1e3) / 1e9
-    del h, d
+    # both directions at once (as forward_host runs them): bytes moved each way per second
+    h2, d2 = torch.empty(nbytes, dtype=torch.uint8).pin_memory(), torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(cur)
+    s_in.wait_stream(cur)
+    s_out.wait_stream(cur)
+    for _ in range(reps):
+        with torch.cuda.stream(s_in):
+            d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            h2.copy_(d2, non_blocking=True)
+    cur.wait_stream(s_in)
+    cur.wait_stream(s_out)
+    b.record(cur)
+    torch.cuda.synchronize()
+    out["both_ways_gbs_each"] = nbytes * reps / (a.elapsed_time(b) / 1e3) / 1e9
+    del h, d, h2, d2
     return out
 
 
@@ -711,7 +730,7 @@ def run_ours(args):
         hc_alone = host_copy_gbs(dev) if rank == 0 else None
         barrier()
         hc = host_copy_gbs(dev)
-        hcv = torch.tensor([hc["h2d_gbs"], hc["d2h_gbs"]], device=dev)
+        hcv = torch.tensor([hc["h2d_gbs"], hc["d2h_gbs"], hc["both_ways_gbs_each"]], device=dev)
         if world > 1:
             dist.all_reduce(hcv, op=dist.ReduceOp.MIN)
 
@@ -775,10 +794,14 @@ def run_ours(args):
                     "ms_per_step": ms_e2e,
                     "api": f"KulaMamba.forward_host(pieces={args.e2e_pieces}, graph=True)",
                     "host_link": {"rank0_alone": hc_alone, "all_ranks_min_h2d_gbs": float(hcv[0]),
-                                  "all_ranks_min_d2h_gbs": float(hcv[1]), "numa_node_rank0": numa,
-                                  # copies in and out overlap (full-duplex link): the slower direction bounds a step
-                                  "bound_ms_per_step": max(x_host.numel() * 2 / (float(hcv[0]) * 1e9),
-                                                           y_host.numel() * 2 / (float(hcv[1]) * 1e9)) * 1e3}},
+                                  "all_ranks_min_d2h_gbs": float(hcv[1]),
+                                  "all_ranks_min_both_ways_gbs_each": float(hcv[2]), "numa_node_rank0": numa,
+                                  # copies in and out run at once: the link's rate in that mode bounds a step
+                                  "bound_ms_per_step": max(x_host.numel(), y_host.numel()) * 2 / (float(hcv[2]) * 1e9)
+                                  * 1e3,
+                                  "bound_ms_per_step_one_way_rates": max(x_host.numel() * 2 / (float(hcv[0]) * 1e9),
+                                                                         y_host.numel() * 2 / (float(hcv[1]) * 1e9))
+                                  * 1e3}},
             "clocks": clk.summary(),
         }
         if decode is not None:

@@ -28,14 +28,17 @@ struct SsdParams {
   int* err;
 };
 
-// ST: the state kernel's plan, which needs no C and no H tile (about 99 KB instead of 147 KB
-// at NC = 256, so two state CTAs share an SM)
+// The (s, q) columns of a chunk are taken one rank half at a time -- the gamma half (x_g, B_g)
+// and, with the trapezoid, the beta half (x_b, B_b) -- so every column tile is L RP = 128 wide
+// and the halves accumulate into the same TMEM result: 98 KB of shared memory for the output
+// kernel (two CTAs per SM) and 49 KB for the state kernel (three).
+// ST: the state kernel's plan, which needs no C and no H tile.
 // SP (state plan only): the weighted X^T operand is also kept as its bf16 remainder (a second
 // tile), so the chunk states are accurate to about 2^-17 (the backward's states).
 template <int RP, int RIP, bool ST = false, bool SP = false>
 struct GPlan {
   static constexpr int L = 128 / RP;
-  static constexpr int NC = L * RIP;                 // (s,q) columns: 128 or 256
+  static constexpr int NC = L * RP;                  // (s, q) columns of one rank half: 128
   static constexpr int tileC = 0;                    // 128 x 128 (not in the state plan)
   static constexpr int tileB = ST ? 0 : 32768;       // NC x 128
   static constexpr int tileX = tileB + NC * 256;     // 64 x NC
@@ -47,10 +50,10 @@ struct GPlan {
   static constexpr int bars = (wgt + L * 4 + 15) & ~15;
   static constexpr int taddr = bars + 32;
   static constexpr int bytes = taddr + 16 + 1024;
-  static constexpr int tcols = NC == 256 ? 512 : 256;
+  static constexpr int tcols = 256;
   static constexpr int colY = NC, colYi = NC + 64;
-  static_assert(NC == 128 || NC == 256, "column tile must be 128 or 256");
-  static_assert(bytes <= 227 * 1024, "shared memory");
+  static_assert(NC == 128, "one rank half is 128 columns");
+  static_assert(bytes <= 113 * 1024, "two CTAs per SM");
 };
 
 template <typename TA, int R, bool BETA, bool ST = false, bool SP = false>
@@ -131,12 +134,14 @@ __device__ void gen_rows(const SsdParams& a, uint8_t* tile, const void* src0, co
   }
 }
 
-// X^T tile: row p, column (s*RIP + q) = Xt[s,p,q] (* wgt[s] when WEIGHTED); with `lo`, also the
-// bf16 remainder of each entry (entry - bf16(entry)) in a second tile.
-template <typename TA, int R, int RIP, bool WEIGHTED>
-__device__ void gen_x(const SsdParams& a, uint8_t* tile, const float* wgt, int b, int k, int h, int L,
-                      uint8_t* lo = nullptr) {
-  const int NC = L * RIP;
+// X^T tile of one rank half: row p, column (s*RP + q) = src[s,p,q] (* wgt[s] when WEIGHTED),
+// q < R (zero for the padding ranks); with `lo`, also the bf16 remainder of each entry
+// (entry - bf16(entry)) in a second tile.
+template <typename TA, int R, bool WEIGHTED>
+__device__ void gen_x(const SsdParams& a, uint8_t* tile, const float* wgt, const void* src, int b, int k, int h,
+                      int L, uint8_t* lo = nullptr) {
+  constexpr int RP = rp_of(R);
+  const int NC = L * RP;
   const int ncc = NC / 8;
   for (int u = threadIdx.x; u < kPP * ncc; u += kCT) {
     const int pp = u % kPP, cc = u / kPP;
@@ -144,17 +149,12 @@ __device__ void gen_x(const SsdParams& a, uint8_t* tile, const float* wgt, int b
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int col = cc * 8 + e;
-      const int s = col / RIP, q = col % RIP;
+      const int s = col / RP, q = col % RP;
       const int64_t t = (int64_t)k * L + s;
       float val = 0.f;
-      if (pp < a.P && t < a.T && q < 2 * R) {
-        const void* src = q < R ? a.x_g : a.x_b;
-        if (src) {
-          const int r = q < R ? q : q - R;
-          val = io<TA>::ld(reinterpret_cast<const TA*>(src) +
-                           ((((int64_t)b * a.T + t) * a.H + h) * a.P + pp) * R + r);
-          if (WEIGHTED) val *= wgt[s];
-        }
+      if (pp < a.P && t < a.T && q < R && src) {
+        val = io<TA>::ld(reinterpret_cast<const TA*>(src) + ((((int64_t)b * a.T + t) * a.H + h) * a.P + pp) * R + q);
+        if (WEIGHTED) val *= wgt[s];
       }
       v[e] = val;
     }
@@ -197,7 +197,7 @@ __device__ void prefetch_rows(const SsdParams& a, int b, int k, int h, int L, co
 // decay, stored at chunk index K-1-k so that the forward scan kernel runs the reverse scan.
 // SP: the weighted X^T operand as a hi / lo pair (two MMA groups), for states accurate to fp32.
 template <typename TA, typename TS, int R, bool BETA, bool REV = false, bool SP = false>
-__global__ void __launch_bounds__(kCT, 1) gen_state_kernel(SsdParams a) {
+__global__ void __launch_bounds__(kCT, 3) gen_state_kernel(SsdParams a) {
   constexpr int RP = rp_of(R), RIP = rp_of(BETA ? 2 * R : R);
   using PL = GPlan<RP, RIP, true, SP>;
   constexpr int L = PL::L, NC = PL::NC;
@@ -225,31 +225,36 @@ __global__ void __launch_bounds__(kCT, 1) gen_state_kernel(SsdParams a) {
   const int ko = REV ? a.K - 1 - k : k;  // chunk index of the outputs
   if (threadIdx.x == 0) a.decay[((int64_t)b * a.K + ko) * a.H + h] = exp2f(cum2[L - 1]);
   __syncthreads();
-  gen_rows<TA, R, RIP>(a, sm + PL::tileB, a.B_g, BETA ? a.B_b : nullptr, b, k, h, L);
-  gen_x<TA, R, RIP, true>(a, sm + PL::tileX, wgt, b, k, h, L, SP ? sm + PL::tileXlo : nullptr);
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   const uint32_t tbase = *tslot;
-  if (threadIdx.x == 0) {
-    constexpr uint32_t idesc = idesc_bf16(128, kPP, true, false);
-#pragma unroll
-    for (int kk = 0; kk < NC / 16; ++kk)
-      umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, NC, kk * 16), kmajor_desc(sm + PL::tileX, kPP, kk * 16), idesc,
-                kk > 0 ? 1u : 0u);
-    if constexpr (SP) {
+  bool ok = true;
+  constexpr int NH = BETA ? 2 : 1;
+  for (int hb = 0; hb < NH && ok; ++hb) {  // rank halves, accumulated into one state
+    gen_rows<TA, R, RP>(a, sm + PL::tileB, hb ? a.B_b : a.B_g, nullptr, b, k, h, L);
+    gen_x<TA, R, true>(a, sm + PL::tileX, wgt, hb ? a.x_b : a.x_g, b, k, h, L, SP ? sm + PL::tileXlo : nullptr);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, kPP, true, false);
 #pragma unroll
       for (int kk = 0; kk < NC / 16; ++kk)
-        umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, NC, kk * 16), kmajor_desc(sm + PL::tileXlo, kPP, kk * 16), idesc,
-                  1u);
+        umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, NC, kk * 16), kmajor_desc(sm + PL::tileX, kPP, kk * 16), idesc,
+                  (hb > 0 || kk > 0) ? 1u : 0u);
+      if constexpr (SP) {
+#pragma unroll
+        for (int kk = 0; kk < NC / 16; ++kk)
+          umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, NC, kk * 16), kmajor_desc(sm + PL::tileXlo, kPP, kk * 16),
+                    idesc, 1u);
+      }
+      umma_commit(&bar[0]);
     }
-    umma_commit(&bar[0]);
+    // the half's tiles are read until its MMAs complete
+    ok = mbar_wait(&bar[0], hb & 1);
+    __syncwarp();
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
   }
-  bool ok = mbar_wait(&bar[0], 0);
-  __syncwarp();
-  ok = __syncthreads_and(ok);
-  tc_fence_after();
   if (ok) {
     const int lq = warp & 3, half = warp >> 2;
     const int n = 32 * lq + lane;
@@ -275,7 +280,7 @@ __global__ void __launch_bounds__(kCT, 1) gen_state_kernel(SsdParams a) {
 }
 
 template <typename TA, typename TS, int R, bool BETA>
-__global__ void __launch_bounds__(kCT, 1) gen_out_kernel(SsdParams a) {
+__global__ void __launch_bounds__(kCT, 2) gen_out_kernel(SsdParams a) {
   constexpr int RP = rp_of(R), RIP = rp_of(BETA ? 2 * R : R);
   using PL = GPlan<RP, RIP>;
   constexpr int L = PL::L, NC = PL::NC;
@@ -299,10 +304,8 @@ __global__ void __launch_bounds__(kCT, 1) gen_out_kernel(SsdParams a) {
   gen_scalars<TA, R, BETA>(a, sm, b, k, h);
   const float* cum2 = reinterpret_cast<const float*>(sm + PL::cum2);
   const float* dtv = reinterpret_cast<const float*>(sm + PL::dtv);
-  // C rows (t*RP + r): reuse the row producer with RIP = RP and no second source
+  // C rows (t*RP + r) and the H tile, shared by both rank halves
   gen_rows<TA, R, RP>(a, sm + PL::tileC, a.C, nullptr, b, k, h, L);
-  gen_rows<TA, R, RIP>(a, sm + PL::tileB, a.B_g, BETA ? a.B_b : nullptr, b, k, h, L);
-  gen_x<TA, R, RIP, false>(a, sm + PL::tileX, nullptr, b, k, h, L);
   {
     uint8_t* tH = sm + PL::tileH;
     const TS* hs = reinterpret_cast<const TS*>(a.hstate) + (((int64_t)b * a.K + k) * a.H + h) * (int64_t)a.P * a.N;
@@ -323,74 +326,83 @@ __global__ void __launch_bounds__(kCT, 1) gen_out_kernel(SsdParams a) {
       sw128_store_chunk(tH, pp, c, kPP, o);
     }
   }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   const uint32_t tbase = *tslot;
-  if (threadIdx.x == 0) {
-    constexpr uint32_t id_s = idesc_bf16(128, NC, false, false);
-    constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16(tbase, kmajor_desc(sm + PL::tileC, 128, kk * 16), kmajor_desc(sm + PL::tileB, NC, kk * 16), id_s,
-                kk > 0 ? 1u : 0u);
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16(tbase + PL::colYi, kmajor_desc(sm + PL::tileC, 128, kk * 16),
-                kmajor_desc(sm + PL::tileH, kPP, kk * 16), id_o, kk > 0 ? 1u : 0u);
-    umma_commit(&bar[0]);
-  }
-  bool ok = mbar_wait(&bar[0], 0);
-  __syncwarp();
-  ok = __syncthreads_and(ok);
-  tc_fence_after();
   const int lq = warp & 3, half = warp >> 2;
   const int m = 32 * lq + lane;
   const int t = m / RP, r = m % RP;
   const uint32_t trow = tbase + ((uint32_t)(32 * lq) << 16);
-  if (ok) {
-    uint8_t* tP = sm + PL::tileB;  // P = mask(S) overwrites the B tile (128 x NC, K-major)
-    const float ct = cum2[t];
+  bool ok = true;
+  constexpr int NH = BETA ? 2 : 1;
+  for (int hb = 0; hb < NH && ok; ++hb) {  // rank halves: S and P per half, Y accumulated
+    gen_rows<TA, R, RP>(a, sm + PL::tileB, hb ? a.B_b : a.B_g, nullptr, b, k, h, L);
+    gen_x<TA, R, false>(a, sm + PL::tileX, nullptr, hb ? a.x_b : a.x_g, b, k, h, L);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+      constexpr uint32_t id_s = idesc_bf16(128, NC, false, false);
+      constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
 #pragma unroll
-    for (int g2 = 0; g2 < NC / 64; ++g2) {
-      const int c0 = (NC / 2) * half + 32 * g2;
-      float v[32];
-      tmem_ld32(trow + c0, v);
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tbase, kmajor_desc(sm + PL::tileC, 128, kk * 16), kmajor_desc(sm + PL::tileB, NC, kk * 16), id_s,
+                  kk > 0 ? 1u : 0u);
+      if (hb == 0) {
 #pragma unroll
-      for (int j = 0; j < 32; j += RIP) {
-        const int s = (c0 + j) / RIP;
-        const float w = s <= t ? exp2f(ct - cum2[s]) * dtv[s] : 0.f;
-#pragma unroll
-        for (int q = 0; q < RIP; ++q) v[j + q] *= w;
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tbase + PL::colYi, kmajor_desc(sm + PL::tileC, 128, kk * 16),
+                    kmajor_desc(sm + PL::tileH, kPP, kk * 16), id_o, kk > 0 ? 1u : 0u);
       }
+      umma_commit(&bar[0]);
+    }
+    ok = mbar_wait(&bar[0], hb & 1);
+    __syncwarp();
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (ok) {
+      uint8_t* tP = sm + PL::tileB;  // P = mask(S) overwrites the B tile (128 x NC, K-major)
+      const float ct = cum2[t];
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint4 o;
-        o.x = pack_bf16x2(v[8 * cc + 0], v[8 * cc + 1]);
-        o.y = pack_bf16x2(v[8 * cc + 2], v[8 * cc + 3]);
-        o.z = pack_bf16x2(v[8 * cc + 4], v[8 * cc + 5]);
-        o.w = pack_bf16x2(v[8 * cc + 6], v[8 * cc + 7]);
-        sw128_store_chunk(tP, m, c0 / 8 + cc, 128, o);
+      for (int g2 = 0; g2 < NC / 64; ++g2) {
+        const int c0 = (NC / 2) * half + 32 * g2;
+        float v[32];
+        tmem_ld32(trow + c0, v);
+#pragma unroll
+        for (int j = 0; j < 32; j += RP) {
+          const int s = (c0 + j) / RP;
+          const float w = s <= t ? exp2f(ct - cum2[s]) * dtv[s] : 0.f;
+#pragma unroll
+          for (int q = 0; q < RP; ++q) v[j + q] *= w;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint4 o;
+          o.x = pack_bf16x2(v[8 * cc + 0], v[8 * cc + 1]);
+          o.y = pack_bf16x2(v[8 * cc + 2], v[8 * cc + 3]);
+          o.z = pack_bf16x2(v[8 * cc + 4], v[8 * cc + 5]);
+          o.w = pack_bf16x2(v[8 * cc + 6], v[8 * cc + 7]);
+          sw128_store_chunk(tP, m, c0 / 8 + cc, 128, o);
+        }
       }
     }
-  }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (ok && threadIdx.x == 0) {
-    constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (ok && threadIdx.x == 0) {
+      constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
 #pragma unroll
-    for (int kk = 0; kk < NC / 16; ++kk)
-      umma_bf16(tbase + PL::colY, kmajor_desc(sm + PL::tileB, 128, kk * 16), kmajor_desc(sm + PL::tileX, kPP, kk * 16),
-                id_o, kk > 0 ? 1u : 0u);
-    umma_commit(&bar[1]);
+      for (int kk = 0; kk < NC / 16; ++kk)
+        umma_bf16(tbase + PL::colY, kmajor_desc(sm + PL::tileB, 128, kk * 16),
+                  kmajor_desc(sm + PL::tileX, kPP, kk * 16), id_o, (hb > 0 || kk > 0) ? 1u : 0u);
+      umma_commit(&bar[1]);
+    }
+    // the half's B / P and X tiles are read until its MMAs complete
+    if (ok) ok = mbar_wait(&bar[1], hb & 1);
+    __syncwarp();
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
   }
-  if (ok) ok = mbar_wait(&bar[1], 0);
-  __syncwarp();
-  ok = __syncthreads_and(ok);
-  tc_fence_after();
   if (ok) {
     float Y[32], Yi[32];
     tmem_ld32(trow + PL::colY + 32 * half, Y);
