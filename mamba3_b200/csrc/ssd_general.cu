@@ -26,6 +26,7 @@ struct SsdParams {
   float* decay;
   void* y;
   int* err;
+  int xvec;  // x tensors take the vector loader (P % 8 == 0, 16-byte aligned): X tiles as (s, q) rows
 };
 
 // The (s, q) columns of a chunk are taken one rank half at a time -- the gamma half (x_g, B_g)
@@ -174,6 +175,52 @@ __device__ void gen_x(const SsdParams& a, uint8_t* tile, const float* wgt, const
   }
 }
 
+// The same X operand as rows (s RP + q) x columns p of one rank half (* wgt[s] when WEIGHTED),
+// loaded with 16-byte vectors along p (P % 8 == 0, 16-byte aligned tensors) and read by the MMA
+// as an MN-major operand (N = p); with `lo`, the bf16 remainder too.
+template <typename TA, int R, bool WEIGHTED>
+__device__ void gen_xrows(const SsdParams& a, uint8_t* tile, const float* wgt, const void* src, int b, int k, int h,
+                          int L, uint8_t* lo = nullptr) {
+  constexpr int RP = rp_of(R);
+  constexpr int NCH = kPP / 8;
+  for (int u = threadIdx.x; u < L * NCH; u += kCT) {
+    const int s = u / NCH, c = u % NCH;
+    const int64_t t = (int64_t)k * L + s;
+    const bool valid = src && t < a.T && c * 8 < a.P;
+    float v[8 * R];
+    if (valid) {
+      const int64_t off = (((int64_t)b * a.T + t) * a.H + h) * (int64_t)a.P * R + c * 8 * R;
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        float tmp[8];
+        load8<TA>(reinterpret_cast<const TA*>(src) + off + j * 8, tmp);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[j * 8 + e] = tmp[e];
+      }
+      if (WEIGHTED) {
+        const float w = wgt[s];
+#pragma unroll
+        for (int e = 0; e < 8 * R; ++e) v[e] *= w;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < RP; ++q) {
+      uint32_t wh[4] = {0u, 0u, 0u, 0u}, wl[4] = {0u, 0u, 0u, 0u};
+      if (valid && q < R) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x0 = v[(2 * e) * R + q], x1 = v[(2 * e + 1) * R + q];
+          wh[e] = pack_bf16x2(x0, x1);
+          const float2 hv = bf2_to_f2(wh[e]);
+          wl[e] = pack_bf16x2(x0 - hv.x, x1 - hv.y);
+        }
+      }
+      sw128_store_chunk(tile, s * RP + q, c, 128, make_uint4(wh[0], wh[1], wh[2], wh[3]));
+      if (lo) sw128_store_chunk(lo, s * RP + q, c, 128, make_uint4(wl[0], wl[1], wl[2], wl[3]));
+    }
+  }
+}
+
 // Requests the chunk's token rows of up to four (B, T, H, W, R) tensors into L2 (one bulk
 // prefetch per token and tensor; null tensors are skipped), so that the tile loaders that follow
 // wait on L2 rather than on HBM.  W R elements of TA per row, 16-byte aligned rows.
@@ -230,22 +277,28 @@ __global__ void __launch_bounds__(kCT, 3) gen_state_kernel(SsdParams a) {
   constexpr int NH = BETA ? 2 : 1;
   for (int hb = 0; hb < NH && ok; ++hb) {  // rank halves, accumulated into one state
     gen_rows<TA, R, RP>(a, sm + PL::tileB, hb ? a.B_b : a.B_g, nullptr, b, k, h, L);
-    gen_x<TA, R, true>(a, sm + PL::tileX, wgt, hb ? a.x_b : a.x_g, b, k, h, L, SP ? sm + PL::tileXlo : nullptr);
+    if (a.xvec)
+      gen_xrows<TA, R, true>(a, sm + PL::tileX, wgt, hb ? a.x_b : a.x_g, b, k, h, L, SP ? sm + PL::tileXlo : nullptr);
+    else
+      gen_x<TA, R, true>(a, sm + PL::tileX, wgt, hb ? a.x_b : a.x_g, b, k, h, L, SP ? sm + PL::tileXlo : nullptr);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (threadIdx.x == 0) {
-      constexpr uint32_t idesc = idesc_bf16(128, kPP, true, false);
+      // X read K-major (rows p) from gen_x, or MN-major (rows (s, q)) from gen_xrows
+      const uint32_t idesc = a.xvec ? idesc_bf16(128, kPP, true, true) : idesc_bf16(128, kPP, true, false);
+      auto xdesc = [&](const uint8_t* t, int kk) {
+        return a.xvec ? mnmajor_desc(t, NC, kk * 16) : kmajor_desc(t, kPP, kk * 16);
+      };
 #pragma unroll
       for (int kk = 0; kk < NC / 16; ++kk)
-        umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, NC, kk * 16), kmajor_desc(sm + PL::tileX, kPP, kk * 16), idesc,
+        umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, NC, kk * 16), xdesc(sm + PL::tileX, kk), idesc,
                   (hb > 0 || kk > 0) ? 1u : 0u);
       if constexpr (SP) {
 #pragma unroll
         for (int kk = 0; kk < NC / 16; ++kk)
-          umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, NC, kk * 16), kmajor_desc(sm + PL::tileXlo, kPP, kk * 16),
-                    idesc, 1u);
+          umma_bf16(tbase, mnmajor_desc(sm + PL::tileB, NC, kk * 16), xdesc(sm + PL::tileXlo, kk), idesc, 1u);
       }
       umma_commit(&bar[0]);
     }
@@ -335,7 +388,10 @@ __global__ void __launch_bounds__(kCT, 2) gen_out_kernel(SsdParams a) {
   constexpr int NH = BETA ? 2 : 1;
   for (int hb = 0; hb < NH && ok; ++hb) {  // rank halves: S and P per half, Y accumulated
     gen_rows<TA, R, RP>(a, sm + PL::tileB, hb ? a.B_b : a.B_g, nullptr, b, k, h, L);
-    gen_x<TA, R, false>(a, sm + PL::tileX, nullptr, hb ? a.x_b : a.x_g, b, k, h, L);
+    if (a.xvec)
+      gen_xrows<TA, R, false>(a, sm + PL::tileX, nullptr, hb ? a.x_b : a.x_g, b, k, h, L);
+    else
+      gen_x<TA, R, false>(a, sm + PL::tileX, nullptr, hb ? a.x_b : a.x_g, b, k, h, L);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -390,11 +446,12 @@ __global__ void __launch_bounds__(kCT, 2) gen_out_kernel(SsdParams a) {
     __syncthreads();
     tc_fence_after();
     if (ok && threadIdx.x == 0) {
-      constexpr uint32_t id_o = idesc_bf16(128, kPP, false, false);
+      const uint32_t id_o = a.xvec ? idesc_bf16(128, kPP, false, true) : idesc_bf16(128, kPP, false, false);
 #pragma unroll
       for (int kk = 0; kk < NC / 16; ++kk)
         umma_bf16(tbase + PL::colY, kmajor_desc(sm + PL::tileB, 128, kk * 16),
-                  kmajor_desc(sm + PL::tileX, kPP, kk * 16), id_o, (hb > 0 || kk > 0) ? 1u : 0u);
+                  a.xvec ? mnmajor_desc(sm + PL::tileX, NC, kk * 16) : kmajor_desc(sm + PL::tileX, kPP, kk * 16), id_o,
+                  (hb > 0 || kk > 0) ? 1u : 0u);
       umma_commit(&bar[1]);
     }
     // the half's B / P and X tiles are read until its MMAs complete
@@ -1101,6 +1158,7 @@ extern "C" int m3b_chunked_ssd(const m3b_ssd_args* a, void* ws, size_t ws_bytes,
   sp.decay = reinterpret_cast<float*>(base + w.decay);
   sp.y = a->y;
   sp.err = a->err;
+  sp.xvec = a->P % 8 == 0 && aligned16(a->x_g) && (!a->x_b || aligned16(a->x_b));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a->dtype == M3B_BF16) return dispatch_general<__nv_bfloat16, __nv_bfloat16>(sp, a, st);
   return dispatch_general<float, float>(sp, a, st);
@@ -1164,6 +1222,7 @@ int bwd_tc_t(const m3b_ssd_bwd_args* a, uint8_t* base, float* fw, float* ew, flo
   f.D = a->D;
   f.dt_dtype = a->dt_dtype;
   f.ad_dtype = a->ad_dtype;
+  f.xvec = 1;  // bwd_tc_ok: P % 8 == 0 and 16-byte aligned tensors (dy included)
   f.sstate = base + w.sstate;
   f.hstate = base + w.hstate;
   f.decay = reinterpret_cast<float*>(base + w.decay_f);
