@@ -27,6 +27,7 @@ struct SsdParams {
   void* y;
   int* err;
   int xvec;  // x tensors take the vector loader (P % 8 == 0, 16-byte aligned): X tiles as (s, q) rows
+  int yvec;  // y and x_raw are 16-byte aligned too: the output goes through a shared-memory stage
 };
 
 // The (s, q) columns of a chunk are taken one rank half at a time -- the gamma half (x_g, B_g)
@@ -54,6 +55,7 @@ struct GPlan {
   static constexpr int tcols = 256;
   static constexpr int colY = NC, colYi = NC + 64;
   static_assert(NC == 128, "one rank half is 128 columns");
+  static_assert(ST || L * (kPP * RP + 4) * 4 <= tileH - tileB, "gen_out's fp32 output stage fits the B / X tiles");
   static_assert(bytes <= 113 * 1024, "two CTAs per SM");
 };
 
@@ -465,7 +467,20 @@ __global__ void __launch_bounds__(kCT, 2) gen_out_kernel(SsdParams a) {
     tmem_ld32(trow + PL::colY + 32 * half, Y);
     tmem_ld32(trow + PL::colYi + 32 * half, Yi);
     const int64_t tok = (int64_t)k * L + t;
-    if (tok < a.T && r < R) {
+    if (a.yvec) {
+      // Y + e^cum Yi as fp32 rows (t, p R + r) in the free B / X tile space; D x_raw is added and y
+      // stored below with 16-byte vectors per token row
+      float* stage = reinterpret_cast<float*>(sm + PL::tileB);
+      const int pitch = a.P * R + 4;
+      const float ec = exp2f(cum2[t]);
+      if (r < R) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int pp = 32 * half + j;
+          if (pp < a.P) stage[t * pitch + pp * R + r] = fmaf(ec, Yi[j], Y[j]);
+        }
+      }
+    } else if (tok < a.T && r < R) {
       const float ec = exp2f(cum2[t]);
       const float Dh = ldf(a.D, h, a.ad_dtype);
       const int64_t base = (((int64_t)b * a.T + tok) * a.H + h) * (int64_t)a.P * R + r;
@@ -482,6 +497,25 @@ __global__ void __launch_bounds__(kCT, 2) gen_out_kernel(SsdParams a) {
   }
   tc_fence_before();
   __syncthreads();
+  if (ok && a.yvec) {
+    const float* stage = reinterpret_cast<const float*>(sm + PL::tileB);
+    const int PR = a.P * R, pitch = PR + 4, nv = PR / 8;
+    const float Dh = ldf(a.D, h, a.ad_dtype);
+    for (int u = threadIdx.x; u < L * nv; u += kCT) {
+      const int s = u / nv, c = u % nv;
+      const int64_t tok = (int64_t)k * L + s;
+      if (tok >= a.T) continue;
+      const int64_t off = (((int64_t)b * a.T + tok) * a.H + h) * (int64_t)PR + 8 * c;
+      float xv[8], o[8];
+      load8<TA>(reinterpret_cast<const TA*>(a.x_raw) + off, xv);
+      const float4 v0 = *reinterpret_cast<const float4*>(stage + s * pitch + 8 * c);
+      const float4 v1 = *reinterpret_cast<const float4*>(stage + s * pitch + 8 * c + 4);
+      const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = fmaf(Dh, xv[e], vv[e]);
+      store8<TA>(reinterpret_cast<TA*>(a.y) + off, o);
+    }
+  }
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tbase, PL::tcols);
@@ -1159,6 +1193,7 @@ extern "C" int m3b_chunked_ssd(const m3b_ssd_args* a, void* ws, size_t ws_bytes,
   sp.y = a->y;
   sp.err = a->err;
   sp.xvec = a->P % 8 == 0 && aligned16(a->x_g) && (!a->x_b || aligned16(a->x_b));
+  sp.yvec = sp.xvec && aligned16(a->x_raw) && aligned16(a->y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a->dtype == M3B_BF16) return dispatch_general<__nv_bfloat16, __nv_bfloat16>(sp, a, st);
   return dispatch_general<float, float>(sp, a, st);
