@@ -601,5 +601,13 @@ __device__ __forceinline__ float2 silu_fast2(float2 v) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(th.y) : "f"(hv.y));
   return fma2(hv, th, hv);
 }
+// silu(2a) * m for a pair, from a (the halved argument): a m (1 + tanh a)
+__device__ __forceinline__ float2 silu2a_mul2(float2 a, float2 m) {
+  float2 th;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th.x) : "f"(a.x));
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th.y) : "f"(a.y));
+  const float2 am = mul2(a, m);
+  return fma2(am, th, am);
+}
 
 }  // namespace m3b

@@ -138,6 +138,31 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, bool l
   return *abort_flag == 0;
 }
 
+// Every thread of a role waits on the mbarrier itself, with no role barrier after it, so each warp
+// goes on as soon as the phase completes.  A timeout is kept in the thread's own `timed_out`
+// (later waits are then skipped) and the role acts on it at its next barrier_or.
+__device__ __forceinline__ void own_wait(uint64_t* bar, uint32_t parity, bool& timed_out, int* err, uint64_t lim) {
+  if (!timed_out && !mbar_wait(bar, parity, lim)) {
+    timed_out = true;
+    record_error(err, M3B_ERR_TIMEOUT);
+  }
+}
+
+// Named barrier that also ORs one flag over its threads (bar.red.or): every thread gets the same
+// result, computed at the barrier itself.
+__device__ __forceinline__ bool barrier_or(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 // 2R consecutive activations (the (2i, 2i+1) x R block of a B or C row), kept packed in
 // registers between the load and its use so a whole batch of loads can be in flight.
 template <typename TA, int R>
@@ -324,6 +349,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   if (warp >= 8) {
     // =============================== producers ===============================
     volatile int* abort_flag = prod_abort;
+    bool ptmo = false;  // this thread's own bounded waits (own_wait) timed out
     const int ptid = tid - kEpiThreads;
     const int nh2 = N / 2;
     int nseg = 1;
@@ -425,9 +451,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         named_bar(kBarProd, kProdThreads);  // the sequence's parameters are read below
       }
       if (ptid == 0) M3B_TL(g, 0);
-      // the stage is free (and on the TMA path its raw rows have landed)
-      if (!role_wait(&bars[BAR_STAGE0 + s], (g >> 1) & 1, ptid == 0, kBarProd, kProdThreads, abort_flag, a.err, a.wait_ns))
-        break;
+      // the stage is free (and on the TMA path its raw rows have landed); every thread waits
+      // itself, and a timeout is acted on at the barrier after the token scalars
+      own_wait(&bars[BAR_STAGE0 + s], (g >> 1) & 1, ptmo, a.err, a.wait_ns);
       if (ptid == 0) M3B_TL(g, 1);
       uint8_t* st = sm + s * PL::kStage;
       const TokRaw cur = nxt;
@@ -506,7 +532,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
       }
       if (ptid == 0) M3B_TL(g, 6);
-      named_bar(kBarProd, kProdThreads);  // scalars written
+      if (barrier_or(kBarProd, kProdThreads, ptmo)) {  // scalars written (or a stage wait timed out)
+        *abort_flag = 1;
+        break;
+      }
       if (ptid == 0) M3B_TL(g, 2);
       if (ptid < 32) {
         constexpr int PER = L / 32;
@@ -747,6 +776,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   } else {
     // =============================== epilogue ===============================
     volatile int* abort_flag = epi_abort;
+    bool tmo = false;  // this thread's own bounded waits (own_wait) timed out
     const int lq = warp & 3, ch = warp >> 2;  // TMEM lane quadrant, column half
     const int m = 32 * lq + lane;             // TMEM lane = tile row (t, r)
     const int t = m / RP, r = m % RP;
@@ -866,7 +896,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       tmem_wait_st();
       // the gate parameters into shared memory (the previous sequence's last output is complete)
       if (tid < kPP * RP) {
-        emz[gq * kPP + gpp] = gmz;
+        emz[gq * kPP + gpp] = 0.5f * gmz;  // halved: the output takes silu(2a) with a = z mimo_z / 2
         emd[gq * kPP + gpp] = gmd;
         emx[gq * kPP + gpp] = gmx;
       }
@@ -896,6 +926,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         if (lead) st_release_gpu(a.ho_flag + 2 * c.seq + 1, c.part + 1);
       }
     };
+    // The blocks of P above the block diagonal (column block > this warp's lane quadrant) are zero
+    // in every chunk: stored once here, never rewritten.
+    if constexpr (!SO) {
+      uint32_t z16[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) z16[e] = 0u;
+#pragma unroll
+      for (int c32 = 0; c32 < 2; ++c32)
+        if (2 * ch + c32 > lq) tmem_st16_nowait(trow + kColP + 16 * (2 * ch + c32), z16);
+      tmem_wait_st();
+    }
     Raw8<TA> xn[XU];  // x of the next chunk
     ChunkPos pos = sc.first();
     if (G > 0) load_x(pos, xn);
@@ -953,16 +994,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
         }
         // S_g (producer) must be complete before the mask reads it; the state GEMMs of chunk g
-        // (issued at the end of the previous chunk) keep running meanwhile
-        if (lead && !*abort_flag) {
-          if (!mbar_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1, a.wait_ns)) {
-            *abort_flag = 1;
-            record_error(a.err, M3B_ERR_TIMEOUT);
-          }
-        }
-        __syncwarp();
-        named_bar(kBarEpi, kEpiThreads);
-        if (*abort_flag) break;
+        // (issued at the end of the previous chunk) keep running meanwhile.  Every thread waits
+        // itself (no role barrier); a timeout is acted on after the barrier that ends the mask.
+        own_wait(&bars[BAR_SDONE0 + s], (g >> 1) & 1, tmo, a.err, a.wait_ns);
         tc_fence_after();
         if (lead) M3B_TL(g, 8);
         // ---- mask.  The intra-chunk weight of (token t, source s <= t) is
@@ -989,11 +1023,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           for (int c32 = 0; c32 < 2; ++c32) {
             const int blk = 2 * ch + c32;
             const int c0 = 32 * blk;
+            if (blk > lq) continue;  // above the block diagonal: stays zero (stored once at kernel start)
             float v[32];
-            if (blk > lq) {
-#pragma unroll
-              for (int e = 0; e < 32; ++e) v[e] = 0.f;
-            } else {
+            {
               tmem_ld32(trow + cs0 + c0, v);
               if (lead && c32 == 0) M3B_TL(g, 13);
               if (sep) {
@@ -1032,7 +1064,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           xq[c8] = *reinterpret_cast<const uint4*>(st + PL::tX + sw128_offset(m, 32 * ch + c8 * 8, 128));
         tmem_wait_st();
         tc_fence_before();
-        named_bar(kBarEpi, kEpiThreads);
+        if (barrier_or(kBarEpi, kEpiThreads, tmo)) {  // a wait of this chunk timed out
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
         if (lead) {
           // Y_g = P' W (separable) or P X into Y (the previous chunk's output has read it); A = P
           // from TMEM, K = (s, q) in 8 columns per instruction
@@ -1046,21 +1082,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         // The state GEMMs of chunk g (Yi_g, the H update; committed to HDONE) and Y_g (YDONE) are
         // the last readers of stage s: once both have completed, the stage goes to the producers
-        // for chunk g + 2 (with its TMA copies) while this chunk's output is written.
-        if (lead && !*abort_flag) {
-          if (!mbar_wait(&bars[BAR_HDONE], g & 1, a.wait_ns) || !mbar_wait(&bars[BAR_YDONE], g & 1, a.wait_ns)) {
-            *abort_flag = 1;
-            record_error(a.err, M3B_ERR_TIMEOUT);
-          } else if (g + 2 < G) {
-            issue_stage(sc.ahead(pnext, 1), g + 2);
-          }
-        }
-        __syncwarp();
-        named_bar(kBarEpi, kEpiThreads);
-        if (*abort_flag) {
-          ok = false;
-          break;
-        }
+        // for chunk g + 2 (with its TMA copies) while this chunk's output is written.  Every thread
+        // waits itself; a timeout is acted on after the next role barrier (the state of chunk g+1).
+        own_wait(&bars[BAR_HDONE], g & 1, tmo, a.err, a.wait_ns);
+        own_wait(&bars[BAR_YDONE], g & 1, tmo, a.err, a.wait_ns);
+        if (lead && !tmo && g + 2 < G) issue_stage(sc.ahead(pnext, 1), g + 2);
         tc_fence_after();
         if (lead) M3B_TL(g, 10);
         // ---- output of chunk g: y = e_t Y + e^cum_t Yi + D x_r, gate, MIMO down
@@ -1093,8 +1119,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                 const float2 ys = fma2(et2, make_float2(__uint_as_float(yraw[i]), __uint_as_float(yraw[i + 1])),
                                        mul2(ec2, make_float2(__uint_as_float(yiraw[i]), __uint_as_float(yiraw[i + 1]))));
                 const float2 yv = fma2(D2, bf2_to_f2(xw[e2]), ys);
-                const float2 gz = silu_fast2(mul2(zr[c8].pair(2 * e2), mzp[e2]));
-                const float2 o = mul2(mul2(yv, gz), mdp[e2]);
+                // silu(z mz) md with a = z mz / 2: a md (1 + tanh a)
+                const float2 o = mul2(yv, silu2a_mul2(mul2(zr[c8].pair(2 * e2), mzp[e2]), mdp[e2]));
                 acc[i] = o.x;
                 acc[i + 1] = o.y;
               }
@@ -1149,9 +1175,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           if (!(ok = state_init(pnext, g + 1))) break;
         } else {
           const int s1 = (g + 1) & 1;
-          if (!(ok = role_wait(&bars[BAR_FULL0 + s1], ((g + 1) >> 1) & 1, lead, kBarEpi, kEpiThreads, abort_flag,
-                               a.err, a.wait_ns)))
-            break;
+          // every thread waits itself; a timeout is acted on after the barrier below
+          own_wait(&bars[BAR_FULL0 + s1], ((g + 1) >> 1) & 1, tmo, a.err, a.wait_ns);
           const float* scal1 = reinterpret_cast<const float*>(sm + PL::scal + s1 * PL::scalStride);
           const float d = exp2f(scal1[L - 1]);
           float v[32];
@@ -1172,7 +1197,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         build_xw(g + 1, xn);
         fence_async_smem();
         tc_fence_before();
-        named_bar(kBarEpi, kEpiThreads);
+        if (barrier_or(kBarEpi, kEpiThreads, tmo)) {  // a wait of this chunk timed out
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
         if (lead) {
           issue_state_mma(g + 1);
           M3B_TL(g, 12);
