@@ -69,6 +69,7 @@ struct FPlan {
   static constexpr int segt = omega + 128 * 8;                       // 256 floats
   static constexpr int nrm = segt + 256 * 4;                         // B/C norm weight, bias: 4 x N*R fp32
   static constexpr int mxs = nrm + 4 * kNS * RP * 4;                 // mimo_x (epilogue): kPP x RP fp32
+  static_assert(RP * 64 * 16 <= 4 * kNS * RP * 4, "packed bf16 norm pairs (TMA path) fit the norm region");
   static constexpr int seqp = mxs + kPP * RP * 4;                    // A, dt_bias of the producers' sequence
   static constexpr int epar = seqp + 16;                             // mimo_z, mimo_down (epilogue)
   static constexpr int bars = epar + 2 * kPP * RP * 4;               // 9 mbarriers
@@ -423,11 +424,34 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const TA* rowbase = proj + (int64_t)b * a.T * a.proj_stride;
       if (pos.kk == 0) {  // a new job: its sequence's parameters (every producer passed chunk g-1's last barrier)
         const int pd = p.param_dtype;
-        for (int e = ptid; e < NR; e += kProdThreads) {
-          nwB[e] = ldf(p.B_norm_w, e, pd);
-          nwC[e] = ldf(p.C_norm_w, e, pd);
-          nbB[e] = ldf(p.B_bias, (int64_t)grp * NR + e, pd);
-          nbC[e] = ldf(p.C_bias, (int64_t)grp * NR + e, pd);
+        if constexpr (TMA) {
+          // the norm weights / biases of pair ptid as the packed bf16 pairs the rotation multiplies
+          // with, converted once per job; quad q of pair i at 16-byte slot q * 64 + i
+          if (ptid < nh2) {
+            uint4* hq = reinterpret_cast<uint4*>(sm + PL::nrm) + ptid;
+            const int64_t gb = (int64_t)grp * NR;
+            auto pk = [&](const void* base, int64_t i) { return pack_bf16x2(ldf(base, i, pd), ldf(base, i + 1, pd)); };
+            if constexpr (R % 2 == 0) {
+#pragma unroll
+              for (int rp = 0; rp < R / 2; ++rp) {
+                const int i0 = 2 * ptid * R + 2 * rp, i1 = i0 + R;  // (n = 2i | 2i+1, ranks 2rp, 2rp+1)
+                hq[(2 * rp) * 64] = make_uint4(pk(p.B_norm_w, i0), pk(p.B_norm_w, i1), pk(p.B_bias, gb + i0),
+                                               pk(p.B_bias, gb + i1));
+                hq[(2 * rp + 1) * 64] = make_uint4(pk(p.C_norm_w, i0), pk(p.C_norm_w, i1), pk(p.C_bias, gb + i0),
+                                                   pk(p.C_bias, gb + i1));
+              }
+            } else {
+              const int i0 = 2 * ptid;  // (n = 2i, 2i+1) of the single rank
+              hq[0] = make_uint4(pk(p.B_norm_w, i0), pk(p.B_bias, gb + i0), pk(p.C_norm_w, i0), pk(p.C_bias, gb + i0));
+            }
+          }
+        } else {
+          for (int e = ptid; e < NR; e += kProdThreads) {
+            nwB[e] = ldf(p.B_norm_w, e, pd);
+            nwC[e] = ldf(p.C_norm_w, e, pd);
+            nbB[e] = ldf(p.B_bias, (int64_t)grp * NR + e, pd);
+            nbC[e] = ldf(p.C_bias, (int64_t)grp * NR + e, pd);
+          }
         }
         if (pos.part == 0) {
           if (ptid < nh2)
@@ -583,7 +607,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         // norm weight / bias of (n = 2i + e, r) as r-pairs (R even) or n-pairs (R = 1)
         float2 wB0[RP / 2 + 1], wB1[RP / 2 + 1], bB0[RP / 2 + 1], bB1[RP / 2 + 1];
         float2 wC0[RP / 2 + 1], wC1[RP / 2 + 1], bC0[RP / 2 + 1], bC1[RP / 2 + 1];
-        if constexpr (R % 2 == 0) {
+        if constexpr (TMA) {
+          // (packed bf16 pairs below)
+        } else if constexpr (R % 2 == 0) {
 #pragma unroll
           for (int rp = 0; rp < R / 2; ++rp) {
             const int i0 = 2 * pi * R + 2 * rp, i1 = i0 + R;
@@ -607,19 +633,27 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         __nv_bfloat162 hwB0[RP / 2 + 1], hwB1[RP / 2 + 1], hbB0[RP / 2 + 1], hbB1[RP / 2 + 1];
         __nv_bfloat162 hwC0[RP / 2 + 1], hwC1[RP / 2 + 1], hbC0[RP / 2 + 1], hbC1[RP / 2 + 1];
         if constexpr (TMA) {
-          const int nrp = R % 2 == 0 ? R / 2 : 1;
+          const uint4* hq = reinterpret_cast<const uint4*>(sm + PL::nrm) + pi;
+          auto h2 = [](uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); };
+          if constexpr (R % 2 == 0) {
 #pragma unroll
-          for (int rp = 0; rp < nrp; ++rp) {
-            hwB0[rp] = __floats2bfloat162_rn(wB0[rp].x, wB0[rp].y);
-            hbB0[rp] = __floats2bfloat162_rn(bB0[rp].x, bB0[rp].y);
-            hwC0[rp] = __floats2bfloat162_rn(wC0[rp].x, wC0[rp].y);
-            hbC0[rp] = __floats2bfloat162_rn(bC0[rp].x, bC0[rp].y);
-            if constexpr (R % 2 == 0) {
-              hwB1[rp] = __floats2bfloat162_rn(wB1[rp].x, wB1[rp].y);
-              hbB1[rp] = __floats2bfloat162_rn(bB1[rp].x, bB1[rp].y);
-              hwC1[rp] = __floats2bfloat162_rn(wC1[rp].x, wC1[rp].y);
-              hbC1[rp] = __floats2bfloat162_rn(bC1[rp].x, bC1[rp].y);
+            for (int rp = 0; rp < R / 2; ++rp) {
+              const uint4 qb = hq[(2 * rp) * 64], qc = hq[(2 * rp + 1) * 64];
+              hwB0[rp] = h2(qb.x);
+              hwB1[rp] = h2(qb.y);
+              hbB0[rp] = h2(qb.z);
+              hbB1[rp] = h2(qb.w);
+              hwC0[rp] = h2(qc.x);
+              hwC1[rp] = h2(qc.y);
+              hbC0[rp] = h2(qc.z);
+              hbC1[rp] = h2(qc.w);
             }
+          } else {
+            const uint4 q = hq[0];
+            hwB0[0] = h2(q.x);
+            hbB0[0] = h2(q.y);
+            hwC0[0] = h2(q.z);
+            hbC0[0] = h2(q.w);
           }
         }
         // raw (2i, 2i+1) x R blocks: registers, or shared memory (TMA path), where the whole warp
