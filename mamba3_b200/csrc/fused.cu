@@ -19,9 +19,11 @@
 //   epilogue:         mask(g), [stage s handed over], output(g), state(g+1): H'_{g+1} = H -> bf16
 //                     tile, H *= d_{g+1}, X and W tiles of chunk g+1
 // The algebra (weights W, w, the first-token beta term carried by H') is in chunk.cuh.
-// Every wait is bounded.  On a timeout a role's leader raises that role's own abort flag, which
-// the role reads after its named barrier, so all its threads leave the loop together; the other
-// role then times out on the barrier this role no longer arrives on, and leaves too.
+// Every wait is bounded.  In the chunk loops each thread waits on the GEMM / stage mbarriers
+// itself (own_wait) and keeps its own timeout flag; the role ORs the flags at its next named
+// barrier (barrier_or, bar.red.or), so all its threads leave the loop together.  Job starts wait
+// through the role's leader and a shared abort flag read after a named barrier (role_wait).  The
+// other role then times out on the mbarrier this role no longer completes, and leaves too.
 #include <cuda.h>
 
 #include <mutex>
