@@ -329,7 +329,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   // tile blocks 0 | 1; token j's half lands on the bytes of tile rows j*RP .. j*RP+RP-1) and of
   // theta (-> the W tile, built only after theta has been consumed), counted as transaction
   // bytes of the same phase.  The producers hand chunks 0 and 1 to themselves; the epilogue
-  // leader hands chunk g + 2 over once every epilogue thread has written the output of chunk g.
+  // leader hands chunk g + 2 over once the last GEMMs that read chunk g's stage (its state GEMMs
+  // and Y = P'W; in the state-only variant the state GEMM) have completed.
   auto issue_stage = [&](const ChunkPos& c, int gg) {
     uint64_t* bar = &bars[BAR_STAGE0 + (gg & 1)];
     if constexpr (TMA) {
