@@ -30,6 +30,19 @@ from . import _lib, ops
 from .ssd import chunked_ssd
 
 
+class SequenceLengthError(ValueError, AssertionError):
+    """An input with no tokens.  The reference asserts T > 0 with this message
+    (mamba3/mamba3.py:194), so callers that catch its AssertionError catch this too; it is also a
+    ValueError, as the other argument checks here are."""
+
+
+def _check_tokens(x):
+    if x.dim() != 3:
+        raise ValueError(f"expected (batch, seqlen, d_model), got {tuple(x.shape)}")
+    if x.shape[1] <= 0:
+        raise SequenceLengthError(f"Sequence length must be positive, got {x.shape[1]}")
+
+
 class RMSNorm(nn.Module):
     """RMSNorm with the reference's semantics (mamba3/mamba3.py:19-35).  On CUDA without
     gradients (inference, decode) it is one kernel (``mamba3_b200::rmsnorm``); when autograd
@@ -304,8 +317,7 @@ class KulaMamba(nn.Module):
                 and self.B_norm.eps == self.C_norm.eps and H * (N // 2) <= 2048 and floats * 4 <= 200 * 1024)
 
     def _ssd(self, x, dt_scale, return_state, state=None):
-        if x.dim() != 3 or x.shape[1] <= 0:
-            raise ValueError(f"expected (batch, seqlen>0, d_model), got {tuple(x.shape)}")
+        _check_tokens(x)
         proj, rms = self._project(x)
         st = state or {}
         if self._needs_grad(x):
@@ -337,8 +349,7 @@ class KulaMamba(nn.Module):
         if compact_state:
             if dt_scale is not None:
                 raise NotImplementedError("dt_scale with a compact state")
-            if x.dim() != 3 or x.shape[1] <= 0:
-                raise ValueError(f"expected (batch, seqlen>0, d_model), got {tuple(x.shape)}")
+            _check_tokens(x)
             y, st = ops.layer_state_compact(self.in_proj(x), self._param_tensors(), self._dims_tuple())
             return self.out_proj(y), st
         return self._ssd(x, dt_scale, True)

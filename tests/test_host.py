@@ -142,6 +142,20 @@ def test_cpu_tensors_raise_no_fallback():
         ssd_scan(torch.rand(1, 2, 1), torch.randn(1, 2, 1, 4))
 
 
+def test_empty_sequence_raises_like_the_reference():
+    """T = 0: the reference asserts T > 0 (mamba3/mamba3.py:194); the same message, an
+    AssertionError (and a ValueError), before anything touches a device."""
+    from mamba3_b200 import KulaMamba
+
+    m = KulaMamba(d_model=64, d_state=16, headdim=16, chunk_size=8)
+    x = torch.zeros(2, 0, 64)
+    for call in (lambda: m(x), lambda: m.prefill(x), lambda: m.prefill(x, compact_state=True)):
+        with pytest.raises(AssertionError, match="Sequence length must be positive, got 0"):
+            call()
+        with pytest.raises(ValueError):
+            call()
+
+
 def test_state_shapes_and_dtypes():
     from mamba3_b200 import KulaMamba
 
