@@ -30,10 +30,14 @@ from . import _lib, ops
 from .ssd import chunked_ssd
 
 
-class SequenceLengthError(ValueError, AssertionError):
-    """An input with no tokens.  The reference asserts T > 0 with this message
-    (mamba3/mamba3.py:194), so callers that catch its AssertionError catch this too; it is also a
-    ValueError, as the other argument checks here are."""
+class ArgumentAssertionError(ValueError, AssertionError):
+    """An argument the reference rejects with `assert` (mamba3/mamba3.py:77, 79, 85, 194): an
+    AssertionError there, so callers that catch that catch this too; also a ValueError, as the
+    other argument checks here are."""
+
+
+class SequenceLengthError(ArgumentAssertionError):
+    """An input with no tokens (the reference's message, mamba3/mamba3.py:194)."""
 
 
 def _check_tokens(x):
@@ -166,13 +170,13 @@ class KulaMamba(nn.Module):
         self.use_complex_ssm = use_complex_ssm
         self.d_inner = expand * d_model
         if self.d_inner % headdim != 0:
-            raise ValueError("expand * d_model must be a multiple of headdim")
+            raise ArgumentAssertionError("expand * d_model must be a multiple of headdim")
         if d_state % 2 != 0:
-            raise ValueError("d_state must be even (RoPE pairing)")
+            raise ArgumentAssertionError("d_state must be even (RoPE pairing)")
         self.nheads = self.d_inner // headdim
         self.ngroups = ngroups if ngroups is not None else 1
         if self.nheads % self.ngroups != 0:
-            raise ValueError("nheads must be a multiple of ngroups")
+            raise ArgumentAssertionError("nheads must be a multiple of ngroups")
         self.heads_per_group = self.nheads // self.ngroups
         H, P, N, R, G = self.nheads, headdim, d_state, self.mimo_rank, self.ngroups
 

@@ -156,6 +156,21 @@ def test_empty_sequence_raises_like_the_reference():
             call()
 
 
+@pytest.mark.parametrize("kw", [dict(d_model=60, headdim=16), dict(d_state=15), dict(ngroups=3)],
+                         ids=["headdim", "odd_d_state", "ngroups"])
+def test_constructor_rejects_what_the_reference_asserts(kw):
+    """The reference rejects these with `assert` (mamba3/mamba3.py:77, 79, 85): an AssertionError
+    here too (and a ValueError)."""
+    from mamba3_b200 import KulaMamba
+
+    args = dict(d_model=64, d_state=16, headdim=16, chunk_size=8)
+    args.update(kw)
+    with pytest.raises(AssertionError):
+        KulaMamba(**args)
+    with pytest.raises(ValueError):
+        KulaMamba(**args)
+
+
 def test_state_shapes_and_dtypes():
     from mamba3_b200 import KulaMamba
 
