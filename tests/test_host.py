@@ -190,3 +190,55 @@ def test_compact_state_shapes():
     assert set(st) == {"h", "angle", "prev_B", "prev_x"}
     assert st["prev_B"].shape == (2, 8, 16, 2) and st["prev_x"].shape == (2, 8, 16, 2)
     assert all(v.dtype == torch.float32 for v in st.values())
+
+
+# The reference's public signatures (parameter names and defaults, in order), as its sources
+# declare them; the drop-in API takes every one of them the same way and may only add keyword
+# parameters with defaults after them.
+REFERENCE_SIGNATURES = {
+    # mamba3/mamba3.py:50
+    "KulaMamba.__init__": [("d_model", None), ("d_state", 128), ("expand", 2), ("headdim", 64), ("ngroups", None),
+                           ("mimo_rank", 2), ("chunk_size", 64), ("bias", False), ("dt_min", 0.001),
+                           ("dt_max", 0.1), ("use_trapezoidal", True), ("use_complex_ssm", True)],
+    # mamba3/mamba3.py:260, 264, 267, 324
+    "KulaMamba.forward": [("x", None), ("dt_scale", None)],
+    "KulaMamba.prefill": [("x", None), ("dt_scale", None)],
+    "KulaMamba.step": [("hidden_states", None), ("ssm_state", None), ("dt_scale", None)],
+    "KulaMamba.allocate_inference_state": [("batch_size", None), ("dtype", None), ("device", None)],
+    # mamba3/block.py:31
+    "KulaMambaBlock.__init__": [("d_model", None), ("d_state", 128), ("expand", 2), ("headdim", 64),
+                                ("ngroups", None), ("mimo_rank", 2), ("chunk_size", 64), ("use_mlp", True),
+                                ("mlp_expand", 2.667), ("norm_eps", 1e-05), ("bias", False), ("residual_scale", 1.0),
+                                ("gradient_checkpointing", False), ("use_trapezoidal", True),
+                                ("use_complex_ssm", True)],
+    # mamba3/block.py:112, 178, 196
+    "KulaMambaLM.__init__": [("vocab_size", None), ("d_model", 768), ("n_layers", 12), ("d_state", 128),
+                             ("expand", 2), ("headdim", 64), ("ngroups", None), ("mimo_rank", 2), ("chunk_size", 64),
+                             ("use_mlp", True), ("tie_weights", True), ("norm_eps", 1e-05), ("bias", False),
+                             ("residual_scale", "depth"), ("gradient_checkpointing", False),
+                             ("use_trapezoidal", True), ("use_complex_ssm", True)],
+    "KulaMambaLM.forward": [("input_ids", None), ("labels", None)],
+    "KulaMambaLM.generate": [("input_ids", None), ("max_new_tokens", 100), ("temperature", 1.0), ("top_k", None)],
+    # mamba3/ssd.py:118, mamba3/scan.py:144
+    "chunked_ssd": [("x_g", None), ("x_b", None), ("B_g", None), ("B_b", None), ("C", None), ("dt", None),
+                    ("A", None), ("D", None), ("x_raw", None), ("chunk_size", 64), ("h_init", None),
+                    ("return_final_state", False)],
+    "ssd_scan": [("chunk_decay", None), ("h_chunk", None), ("h_init", None)],
+}
+
+
+@pytest.mark.parametrize("name", sorted(REFERENCE_SIGNATURES))
+def test_public_signatures_match_the_reference(name):
+    import inspect
+
+    import mamba3_b200
+
+    obj = mamba3_b200
+    for part in name.split("."):
+        obj = getattr(obj, part)
+    params = [p for p in inspect.signature(obj).parameters.values() if p.name != "self"]
+    want = REFERENCE_SIGNATURES[name]
+    got = [(p.name, None if p.default is inspect.Parameter.empty else p.default) for p in params[:len(want)]]
+    assert got == want
+    for p in params[len(want):]:  # extensions: keyword parameters with defaults only
+        assert p.default is not inspect.Parameter.empty, p.name
