@@ -36,6 +36,31 @@ def test_graph_decoder_matches_generate(dtype, compact):
     assert torch.equal(dec.generate(ids, temperature=0.0), ref)
 
 
+def test_graph_decoder_keeps_one_graph_per_sampling_rule():
+    """One decoder: greedy, then sampled (temperature 1, top-2), then greedy again.  The sampling
+    rule is part of the captured step, so the sampled call must replay a graph of its own: its
+    tokens are each step's top-2 candidates (top-3 of the teacher-forced forward, one rank of
+    slack for rounding), not all greedy; the greedy calls still equal generate's tokens."""
+    from mamba3_b200.decode import GraphDecoder
+
+    lm = _lm(torch.float32, seed=12)
+    g = torch.Generator().manual_seed(13)
+    ids = torch.randint(0, 1000, (3, 20), generator=g).cuda()
+    ref = lm.generate(ids, max_new_tokens=12, temperature=0.0)
+    dec = GraphDecoder(lm, batch_size=3, max_new_tokens=12)
+    assert torch.equal(dec.generate(ids, temperature=0.0), ref)
+    torch.manual_seed(14)
+    smp = dec.generate(ids, temperature=1.0, top_k=2)
+    assert smp.shape == ref.shape and torch.equal(smp[:, :20], ids)
+    assert not torch.equal(smp, ref)  # 36 draws between two close candidates: not all greedy
+    with torch.no_grad():
+        logits = lm(smp)["logits"][:, 19:31]
+    top3 = logits.topk(3, dim=-1).indices
+    assert (top3 == smp[:, 20:32].unsqueeze(-1)).any(-1).all()
+    assert torch.equal(dec.generate(ids, temperature=0.0), ref)
+    assert len(dec.graphs) == 2
+
+
 def test_step_logits_equal_parallel_forward():
     """Teacher-forced: logits of prefill + steps == logits of one forward over the sequence."""
     lm = _lm(torch.float32, seed=10)
