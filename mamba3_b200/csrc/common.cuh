@@ -593,15 +593,8 @@ __device__ __forceinline__ float silu_fast(float v) {
   return 0.5f * v * (1.f + th);
 }
 
-// silu of a pair: h (1 + tanh h) with h = v / 2, on packed fp32 pairs
-__device__ __forceinline__ float2 silu_fast2(float2 v) {
-  const float2 hv = mul2(v, make_float2(0.5f, 0.5f));
-  float2 th;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(th.x) : "f"(hv.x));
-  asm("tanh.approx.f32 %0, %1;" : "=f"(th.y) : "f"(hv.y));
-  return fma2(hv, th, hv);
-}
-// silu(2a) * m for a pair, from a (the halved argument): a m (1 + tanh a)
+// silu(2a) * m for a pair of packed fp32 values, from a (the halved argument): since
+// silu(v) = (v / 2) (1 + tanh(v / 2)), silu(2a) m = a m (1 + tanh a)
 __device__ __forceinline__ float2 silu2a_mul2(float2 a, float2 m) {
   float2 th;
   asm("tanh.approx.f32 %0, %1;" : "=f"(th.x) : "f"(a.x));
