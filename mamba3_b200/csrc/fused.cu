@@ -69,7 +69,8 @@ struct FPlan {
   static constexpr int scal = tileH + 16384;
   static constexpr int omega = scal + 2 * scalStride;                // 2 x 64 doubles (by chunk parity)
   static constexpr int segt = omega + 128 * 8;                       // 256 floats
-  static constexpr int nrm = segt + 256 * 4;                         // B/C norm weight, bias: 4 x N*R fp32
+  static constexpr int nrm = segt + 256 * 4;  // B/C norm weight, bias: 4 x N*R fp32 (register path);
+                                               // packed bf16 pairs, 16 B per (pair, rank pair) (TMA)
   static constexpr int mxs = nrm + 4 * kNS * RP * 4;                 // mimo_x (epilogue): kPP x RP fp32
   static_assert(RP * 64 * 16 <= 4 * kNS * RP * 4, "packed bf16 norm pairs (TMA path) fit the norm region");
   static constexpr int seqp = mxs + kPP * RP * 4;                    // A, dt_bias of the producers' sequence
